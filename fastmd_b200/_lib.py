@@ -1,0 +1,128 @@
+"""ctypes binding of libfastmd_b200.so (the C ABI declared in include/fastmd_b200.h).
+
+This is the only route from Python to the kernels. A missing or unloadable
+library raises ``FastMDLibraryError``: there is no CPU fallback anywhere in
+the package.
+"""
+from __future__ import annotations
+
+import ctypes
+from ctypes import POINTER, c_double, c_float, c_int32, c_int64, c_size_t, c_void_p
+from pathlib import Path
+
+import torch
+
+LIBRARY = Path(__file__).resolve().with_name("libfastmd_b200.so")
+
+
+class FastMDLibraryError(RuntimeError):
+    """libfastmd_b200.so is missing, failed to load, or a call returned an error status."""
+
+
+class FmdCatPart(ctypes.Structure):
+    _fields_ = [("src", c_void_p), ("index", c_void_p), ("ld", c_int64), ("n_src", c_int64),
+                ("width", c_int32), ("_pad", c_int32)]
+
+
+_P = c_void_p  # every device pointer and the stream travel as void*
+_I64, _I32 = c_int64, c_int32
+
+# name -> argument types (restype is int32 fmd_status unless listed in _RESTYPES)
+_SIGNATURES: dict[str, list] = {
+    "fmd_version": [],
+    "fmd_status_string": [_I32],
+    "fmd_last_error": [],
+    "fmd_gather_cat": [POINTER(FmdCatPart), _I32, _I64, _P, _I64, _P, _P],
+    "fmd_aligned_gather_cat3": [_P, _I64, _P, _I64, _I64, _P, _P, _I64, _I32, _P, _P, _P],
+    "fmd_gather_rows_bwd": [_P, _I64, _I32, _I32, _P, _P, _I64, _P, _I64, _I32, _P],
+    "fmd_copy_rows": [_P, _I64, _P, _I64, _I64, _I32, _P],
+    "fmd_csr_offsets_sorted": [_P, _I64, _I64, _P, _P],
+    "fmd_csr_build_workspace_bytes": [_I64, _I64, POINTER(c_size_t)],
+    "fmd_csr_build": [_P, _I64, _I64, _P, _P, _P, c_size_t, _P, _P],
+    "fmd_csr_segment_sum": [_P, _I64, _P, _I64, _P, _P, _I64, _I32, _I64, _P, _I64, _P],
+    "fmd_csr_segment_sum_bwd": [_P, _P, _I64, _P, _I64, _P, _I64, _I64, _I32, _I64, _P, _P, _P, _P],
+    "fmd_nhc_pre_force": [_P, _P, _P, _I64, _I32, _I32, _I32, _I32, _P, _P],
+    "fmd_nhc_post_force": [_P, _P, _P, _I64, _I32, _I32, _I32, _I32, _P, _P, _P, _P],
+}
+_RESTYPES = {"fmd_status_string": ctypes.c_char_p, "fmd_last_error": ctypes.c_char_p}
+
+_lib = None
+
+
+def declare(name: str, argtypes: list, restype=c_int32) -> None:
+    """Register the signature of an entry point (used by modules that add kernels)."""
+    _SIGNATURES[name] = argtypes
+    if restype is not c_int32:
+        _RESTYPES[name] = restype
+    if _lib is not None:
+        _bind(_lib, name)
+
+
+def _bind(lib, name: str) -> None:
+    fn = getattr(lib, name)
+    fn.argtypes = _SIGNATURES[name]
+    fn.restype = _RESTYPES.get(name, c_int32)
+
+
+def lib():
+    """The loaded library (loaded once per process)."""
+    global _lib
+    if _lib is None:
+        if not LIBRARY.exists():
+            raise FastMDLibraryError(
+                f"{LIBRARY} is not built: run `python -m fastmd_b200.build` (nvcc, sm_100a)")
+        try:
+            handle = ctypes.CDLL(str(LIBRARY))
+        except OSError as error:
+            raise FastMDLibraryError(f"cannot load {LIBRARY}: {error}") from error
+        for name in _SIGNATURES:
+            _bind(handle, name)
+        _lib = handle
+    return _lib
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        text = lib().fmd_status_string(status).decode()
+        detail = lib().fmd_last_error().decode() if status == 2 else ""
+        raise FastMDLibraryError(f"{what}: {text}" + (f" ({detail})" if detail else ""))
+
+
+def call(name: str, *args) -> None:
+    check(getattr(lib(), name)(*args), name)
+
+
+def ptr(tensor) -> int | None:
+    """The device address of ``tensor`` (None for None)."""
+    if tensor is None:
+        return None
+    return tensor.data_ptr()
+
+
+def stream(device=None) -> int:
+    """The handle of torch's current CUDA stream (kernels are launched on it)."""
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def require_cuda(*tensors) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise FastMDLibraryError("fastmd_b200 kernels run on CUDA tensors only (no CPU fallback)")
+
+
+_flags: dict[int, torch.Tensor] = {}
+
+
+def flags_word(device) -> torch.Tensor:
+    """The per-device int32 flags word the op kernels raise FMD_FLAG_* bits in."""
+    index = torch.device(device).index
+    index = torch.cuda.current_device() if index is None else index
+    word = _flags.get(index)
+    if word is None:
+        word = torch.zeros(1, dtype=torch.int32, device=f"cuda:{index}")
+        _flags[index] = word
+    return word
+
+
+__all__ = ["FastMDLibraryError", "FmdCatPart", "call", "check", "declare", "flags_word", "lib", "ptr",
+           "require_cuda", "stream", "c_double", "c_float"]

@@ -1,0 +1,289 @@
+// Nose-Hoover-chain NVT integrator (ASE 3.29 NoseHooverChainNVT step split
+// around the force call), fp64, one CTA per replica.
+//
+// The momenta of a replica stay in registers (EPT per thread) for the whole
+// half step; the thermostat scalars (eta, p_eta, Q) are thread-redundant
+// registers; the only cross-thread work is the block reduction of
+// sum(p^2/m), done 1 + 3*tloop times per half step with a fixed tree
+// (deterministic). This file is compiled with --fmad=false so every
+// elementwise operation rounds exactly as the NumPy expressions of ASE do;
+// exp is CUDA's double exp. The chain length is a template parameter so the
+// chain arrays are registers, not local memory.
+
+#include "common.cuh"
+
+namespace fmd {
+
+constexpr int kConstQ = 16;  // index of Q[0] in the constants table
+
+template <int THREADS>
+__device__ double block_sum(double v, double* smem) {
+    constexpr int kWarps = THREADS / 32;
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();  // previous readers of smem are done
+    if (lane == 0) smem[warp] = v;
+    __syncthreads();
+    double t = 0.0;
+    if (lane < kWarps) t = smem[lane];
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) t += __shfl_xor_sync(0xffffffffu, t, m);
+    return t;
+}
+
+template <int M>
+struct Chain {
+    double pe[M];
+    double eta[M];
+    double Q[M];
+};
+
+// ASE _integrate_p_eta_j for chain element J, ke2 = sum(p^2/m) of the current p
+template <int M>
+__device__ __forceinline__ void p_eta_j(Chain<M>& c, int J, double ke2, double kT, double ndof_kT,
+                                        double delta2, double neg_delta4) {
+    double pj = c.pe[J];
+    double s = 1.0;
+    if (J < M - 1) {
+        s = exp((neg_delta4 * c.pe[J + 1]) / c.Q[J + 1]);
+        pj = pj * s;
+    }
+    double g;
+    if (J == 0) g = ke2 - ndof_kT;
+    else g = (c.pe[J - 1] * c.pe[J - 1]) / c.Q[J - 1] - kT;
+    pj = pj + delta2 * g;
+    if (J < M - 1) pj = pj * s;
+    c.pe[J] = pj;
+}
+
+template <int EPT, int THREADS>
+__device__ __forceinline__ double ke2_sum(const double (&p)[EPT], const double (&m)[EPT],
+                                          const bool (&live)[EPT], double* smem) {
+    double acc = 0.0;
+#pragma unroll
+    for (int k = 0; k < EPT; ++k)
+        if (live[k]) acc += (p[k] * p[k]) / m[k];
+    return block_sum<THREADS>(acc, smem);
+}
+
+// ASE integrate_nhc(p, dt/2) with the Suzuki-Yoshida 4th order sub-steps
+template <int M, int EPT, int THREADS>
+__device__ void nhc_half(double (&p)[EPT], const double (&m)[EPT], const bool (&live)[EPT],
+                         Chain<M>& c, const double* __restrict__ consts, int tloop, double* smem) {
+    const double kT = consts[2];
+    const double ndof_kT = consts[3];
+    double ke2 = ke2_sum<EPT, THREADS>(p, m, live, smem);
+    for (int t = 0; t < tloop; ++t) {
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            const double delta = consts[4 + 4 * k];
+            const double delta2 = consts[5 + 4 * k];
+            const double neg_delta4 = consts[6 + 4 * k];
+            const double neg_delta = consts[7 + 4 * k];
+#pragma unroll
+            for (int jj = 0; jj < M; ++jj) p_eta_j<M>(c, M - 1 - jj, ke2, kT, ndof_kT, delta2, neg_delta4);
+#pragma unroll
+            for (int j = 0; j < M; ++j) c.eta[j] = c.eta[j] + (delta * c.pe[j]) / c.Q[j];
+            const double scale = exp((neg_delta * c.pe[0]) / c.Q[0]);
+#pragma unroll
+            for (int e = 0; e < EPT; ++e) p[e] = p[e] * scale;
+            ke2 = ke2_sum<EPT, THREADS>(p, m, live, smem);
+#pragma unroll
+            for (int j = 0; j < M; ++j) p_eta_j<M>(c, j, ke2, kT, ndof_kT, delta2, neg_delta4);
+        }
+    }
+}
+
+struct NhcArgs {
+    double* state;
+    const double* masses;
+    const double* consts;
+    int64_t n_atoms;
+    int32_t n_replicas;
+    int32_t tloop;
+    int32_t f32_kick;
+    float* positions32;       // pre: float32 copy of q (may be null)
+    const float* forces_f32;  // post
+    const double* forces_f64; // post
+    const double* energy;     // post (may be null)
+};
+
+template <int M>
+__device__ __forceinline__ void load_chain(Chain<M>& c, const NhcArgs& a, int64_t n3R, int r) {
+    const double* eta = a.state + 3 * n3R + int64_t(r) * M;
+    const double* pe = a.state + 3 * n3R + int64_t(a.n_replicas) * M + int64_t(r) * M;
+#pragma unroll
+    for (int j = 0; j < M; ++j) {
+        c.eta[j] = eta[j];
+        c.pe[j] = pe[j];
+        c.Q[j] = a.consts[kConstQ + j];
+    }
+}
+
+template <int M>
+__device__ __forceinline__ void store_chain(const Chain<M>& c, const NhcArgs& a, int64_t n3R, int r) {
+    if (threadIdx.x != 0) return;
+    double* eta = a.state + 3 * n3R + int64_t(r) * M;
+    double* pe = a.state + 3 * n3R + int64_t(a.n_replicas) * M + int64_t(r) * M;
+#pragma unroll
+    for (int j = 0; j < M; ++j) {
+        eta[j] = c.eta[j];
+        pe[j] = c.pe[j];
+    }
+}
+
+__device__ __forceinline__ double kick_of(double dt2, double f, int f32_kick) {
+    if (f32_kick) return double(__fmul_rn(float(dt2), float(f)));
+    return dt2 * f;
+}
+
+template <int M, int EPT, int THREADS>
+__global__ void __launch_bounds__(THREADS) nhc_pre_force_kernel(NhcArgs a) {
+    __shared__ double smem[32];
+    const int r = blockIdx.x;
+    const int64_t n3 = 3 * a.n_atoms;
+    const int64_t n3R = n3 * a.n_replicas;
+    double* q_ptr = a.state + int64_t(r) * n3;
+    double* p_ptr = a.state + n3R + int64_t(r) * n3;
+    const double* f_ptr = a.state + 2 * n3R + int64_t(r) * n3;
+    const double* m_ptr = a.masses + int64_t(r) * a.n_atoms;
+    double p[EPT], m[EPT];
+    bool live[EPT];
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) {
+        const int64_t i = threadIdx.x + int64_t(k) * THREADS;
+        live[k] = i < n3;
+        p[k] = live[k] ? p_ptr[i] : 0.0;
+        m[k] = live[k] ? m_ptr[i / 3] : 1.0;
+    }
+    Chain<M> c;
+    load_chain<M>(c, a, n3R, r);
+    // (1) p = integrate_nhc(p, dt/2)
+    nhc_half<M, EPT, THREADS>(p, m, live, c, a.consts, a.tloop, smem);
+    const double dt = a.consts[0];
+    const double dt2 = a.consts[1];
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) {
+        if (!live[k]) continue;
+        const int64_t i = threadIdx.x + int64_t(k) * THREADS;
+        // (2) p += dt/2 F(q_n), the cached forces
+        const double pk = p[k] + kick_of(dt2, f_ptr[i], a.f32_kick);
+        // (3) q += dt p / m
+        const double q = q_ptr[i] + (dt * pk) / m[k];
+        q_ptr[i] = q;
+        p_ptr[i] = pk;
+        if (a.positions32) a.positions32[int64_t(r) * n3 + i] = float(q);
+    }
+    store_chain<M>(c, a, n3R, r);
+}
+
+template <int M, int EPT, int THREADS>
+__global__ void __launch_bounds__(THREADS) nhc_post_force_kernel(NhcArgs a) {
+    __shared__ double smem[32];
+    const int r = blockIdx.x;
+    const int64_t n3 = 3 * a.n_atoms;
+    const int64_t n3R = n3 * a.n_replicas;
+    double* p_ptr = a.state + n3R + int64_t(r) * n3;
+    double* f_ptr = a.state + 2 * n3R + int64_t(r) * n3;
+    const double* m_ptr = a.masses + int64_t(r) * a.n_atoms;
+    const double dt2 = a.consts[1];
+    double p[EPT], m[EPT];
+    bool live[EPT];
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) {
+        const int64_t i = threadIdx.x + int64_t(k) * THREADS;
+        live[k] = i < n3;
+        m[k] = live[k] ? m_ptr[i / 3] : 1.0;
+        p[k] = 0.0;
+        if (live[k]) {
+            const int64_t g = int64_t(r) * n3 + i;
+            const double f = a.forces_f32 ? double(a.forces_f32[g]) : a.forces_f64[g];
+            // (4) p += dt/2 F(q_{n+1})
+            p[k] = p_ptr[i] + kick_of(dt2, f, a.f32_kick);
+            f_ptr[i] = f;  // cache F(q_{n+1}) for the next pre-force half
+        }
+    }
+    Chain<M> c;
+    load_chain<M>(c, a, n3R, r);
+    // (5) p = integrate_nhc(p, dt/2)
+    nhc_half<M, EPT, THREADS>(p, m, live, c, a.consts, a.tloop, smem);
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) {
+        const int64_t i = threadIdx.x + int64_t(k) * THREADS;
+        if (live[k]) p_ptr[i] = p[k];
+    }
+    store_chain<M>(c, a, n3R, r);
+    if (a.energy && threadIdx.x == 0) {
+        a.state[3 * n3R + 2 * int64_t(a.n_replicas) * M + r] = a.energy[r];
+    }
+}
+
+template <bool PRE, int M, int EPT, int THREADS>
+inline void launch_nhc(const NhcArgs& a, cudaStream_t s) {
+    if (PRE) nhc_pre_force_kernel<M, EPT, THREADS><<<a.n_replicas, THREADS, 0, s>>>(a);
+    else nhc_post_force_kernel<M, EPT, THREADS><<<a.n_replicas, THREADS, 0, s>>>(a);
+}
+
+// threads and elements per thread from 3n: the fewest threads (multiple of
+// 32, <= 1024) with at most EPT elements each
+template <bool PRE, int M>
+inline fmd_status dispatch_ept(const NhcArgs& a, cudaStream_t s) {
+    const int64_t n3 = 3 * a.n_atoms;
+    if (n3 <= 128) launch_nhc<PRE, M, 1, 128>(a, s);
+    else if (n3 <= 512) launch_nhc<PRE, M, 1, 512>(a, s);
+    else if (n3 <= 1024) launch_nhc<PRE, M, 1, 1024>(a, s);
+    else if (n3 <= 2048) launch_nhc<PRE, M, 2, 1024>(a, s);
+    else if (n3 <= 4096) launch_nhc<PRE, M, 4, 1024>(a, s);
+    else if (n3 <= 8192) launch_nhc<PRE, M, 8, 1024>(a, s);
+    else if (n3 <= 16384) launch_nhc<PRE, M, 16, 1024>(a, s);
+    else if (n3 <= 32768) launch_nhc<PRE, M, 32, 1024>(a, s);
+    else return FMD_ERR_UNSUPPORTED;
+    return check_launch();
+}
+
+template <bool PRE>
+inline fmd_status dispatch_chain(const NhcArgs& a, int tchain, cudaStream_t s) {
+    switch (tchain) {
+        case 1: return dispatch_ept<PRE, 1>(a, s);
+        case 2: return dispatch_ept<PRE, 2>(a, s);
+        case 3: return dispatch_ept<PRE, 3>(a, s);
+        case 4: return dispatch_ept<PRE, 4>(a, s);
+        case 5: return dispatch_ept<PRE, 5>(a, s);
+        case 6: return dispatch_ept<PRE, 6>(a, s);
+        case 7: return dispatch_ept<PRE, 7>(a, s);
+        case 8: return dispatch_ept<PRE, 8>(a, s);
+        default: return FMD_ERR_UNSUPPORTED;
+    }
+}
+
+}  // namespace fmd
+
+using namespace fmd;
+
+extern "C" {
+
+fmd_status fmd_nhc_pre_force(double* state, const double* masses, const double* consts,
+                             int64_t n_atoms, int32_t n_replicas, int32_t tchain, int32_t tloop,
+                             int32_t f32_kick, float* positions32, void* stream) {
+    if (state == nullptr || masses == nullptr || consts == nullptr || n_atoms < 1 || n_replicas < 1 ||
+        tloop < 1 || tchain < 1)
+        return FMD_ERR_INVALID_ARGUMENT;
+    NhcArgs a{state, masses, consts, n_atoms, n_replicas, tloop, f32_kick, positions32,
+              nullptr, nullptr, nullptr};
+    return dispatch_chain<true>(a, tchain, as_stream(stream));
+}
+
+fmd_status fmd_nhc_post_force(double* state, const double* masses, const double* consts,
+                              int64_t n_atoms, int32_t n_replicas, int32_t tchain, int32_t tloop,
+                              int32_t f32_kick, const float* forces_f32, const double* forces_f64,
+                              const double* energy, void* stream) {
+    if (state == nullptr || masses == nullptr || consts == nullptr || n_atoms < 1 || n_replicas < 1 ||
+        tloop < 1 || tchain < 1 || ((forces_f32 == nullptr) == (forces_f64 == nullptr)))
+        return FMD_ERR_INVALID_ARGUMENT;
+    NhcArgs a{state, masses, consts, n_atoms, n_replicas, tloop, f32_kick, nullptr,
+              forces_f32, forces_f64, energy};
+    return dispatch_chain<false>(a, tchain, as_stream(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,297 @@
+"""Generate the golden fixtures of tests/golden/*.npz from the reference's own code.
+
+Run in a container that holds the FastMD reference source tree (read-only):
+
+    python tests/golden/make_golden.py /path/to/fastmd-reference
+
+It imports the reference with two stand-in modules for packages absent here
+(``ase.units`` with ASE's CODATA-2014 unit definitions; nothing else of ASE is
+used) and runs, on CPU:
+
+* the reference's Triton kernels under ``TRITON_INTERPRET=1``:
+  ``_aligned_gather_cat3_fwd/_bwd`` and ``_aligned_gather_cat4_fwd/_bwd``
+  (fastmd/models/matris/op/triton_gather_cat.py:30/:59/:203/:236),
+  ``_csr_segsum_fwd`` and ``_csr_segsum_bwd_rows``
+  (fastmd/models/matris/op/triton_csr_segment_sum.py:71/:184), and the
+  fixed-capacity re-filter ``_count_neighbors_kernel`` /
+  ``_materialize_neighbors_kernel`` (fastmd/graph/fixed_capacity_builder.py:98/:189)
+  on candidate lists of a dense search, followed by the reference's
+  canonical sort key (fixed_capacity_builder.py:1978-1996);
+* the torch backend of ``GPUNoseHooverChainNVT`` (fastmd/execution/gpu_nhc.py:709,
+  ``backend="torch"``) with harmonic forces, and ``maxwell_boltzmann_momenta``
+  (gpu_nhc.py:199).
+
+The fixtures are small (a few hundred KB in total) and are the pins of the
+oracle and of the GPU parity tests; nothing at test time reads the reference.
+"""
+from __future__ import annotations
+
+import math
+import os
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+
+
+def _install_stubs() -> None:
+    ase = types.ModuleType("ase")
+    units = types.ModuleType("ase.units")
+    _e, _amu, _k = 1.6021766208e-19, 1.660539040e-27, 1.38064852e-23  # CODATA 2014
+    units.kB = _k / _e
+    units.second = 1e10 * math.sqrt(_e / _amu)
+    units.fs = 1e-15 * units.second
+    units.Pascal = (1 / _e) / 1e30
+    units.GPa = 1e9 * units.Pascal
+    ase.units = units
+    sys.modules["ase"] = ase
+    sys.modules["ase.units"] = units
+
+
+def gather_cat_cases(torch, gc):
+    out = {}
+    rng = np.random.default_rng(11)
+    for tag, (E, N, D) in {"small": (37, 11, 8), "wide": (53, 17, 128), "odd": (29, 7, 5)}.items():
+        A = rng.standard_normal((E, D)).astype(np.float32)
+        X = rng.standard_normal((N, D)).astype(np.float32)
+        ia = np.sort(rng.integers(0, N, E)).astype(np.int64)  # sorted (receiver-like)
+        ib = rng.integers(0, N, E).astype(np.int64)            # unsorted (sender-like)
+        G = rng.standard_normal((E, 3 * D)).astype(np.float32)
+        block = 1 << (D - 1).bit_length()
+        t = {k: torch.from_numpy(v) for k, v in dict(A=A, X=X, ia=ia, ib=ib, G=G).items()}
+        y = torch.empty(E, 3 * D)
+        gc._aligned_gather_cat3_fwd[(E,)](t["A"], t["X"], t["ia"], t["ib"], y, E, D=D, BLK=block,
+                                          S0_STRIDE=D, S1_STRIDE=D)
+        ga = torch.empty(E, D)
+        gx = torch.zeros(N, D)
+        gc._aligned_gather_cat3_bwd[(E,)](ga, gx, t["ia"], t["ib"], t["G"], E, D=D, BLK=block)
+        out.update({f"cat3_{tag}_{k}": v for k, v in dict(A=A, X=X, ia=ia, ib=ib, G=G).items()})
+        out[f"cat3_{tag}_out"] = y.numpy()
+        out[f"cat3_{tag}_grad_aligned"] = ga.numpy()
+        out[f"cat3_{tag}_grad_gathered"] = gx.numpy()
+    # cat4: [A | Xa[ia] | Xb[ib] | Xb[ic]]
+    E, Na, Nb, D = 41, 9, 13, 16
+    A = rng.standard_normal((E, D)).astype(np.float32)
+    Xa = rng.standard_normal((Na, D)).astype(np.float32)
+    Xb = rng.standard_normal((Nb, D)).astype(np.float32)
+    ia = rng.integers(0, Na, E).astype(np.int64)
+    ib = rng.integers(0, Nb, E).astype(np.int64)
+    ic = rng.integers(0, Nb, E).astype(np.int64)
+    G = rng.standard_normal((E, 4 * D)).astype(np.float32)
+    t = {k: torch.from_numpy(v) for k, v in dict(A=A, Xa=Xa, Xb=Xb, ia=ia, ib=ib, ic=ic, G=G).items()}
+    y = torch.empty(E, 4 * D)
+    gc._aligned_gather_cat4_fwd[(E,)](t["A"], t["Xa"], t["ia"], t["Xb"], t["ib"], t["ic"], y, E, D=D, BLK=D,
+                                      S0_STRIDE=D, S1_STRIDE=D, S2_STRIDE=D)
+    g0, g1, g2 = torch.empty(E, D), torch.zeros(Na, D), torch.zeros(Nb, D)
+    gc._aligned_gather_cat4_bwd[(E,)](g0, g1, g2, t["ia"], t["ib"], t["ic"], t["G"], E, D=D, BLK=D)
+    out.update({f"cat4_{k}": v for k, v in dict(A=A, Xa=Xa, Xb=Xb, ia=ia, ib=ib, ic=ic, G=G).items()})
+    out.update(cat4_out=y.numpy(), cat4_grad_aligned=g0.numpy(), cat4_grad_a=g1.numpy(), cat4_grad_b=g2.numpy())
+    return out
+
+
+def segment_sum_cases(torch, cs):
+    out = {}
+    rng = np.random.default_rng(12)
+    cases = {"identity": (200, 23, 32, True, False, -1), "perm_weighted": (301, 37, 20, False, True, -1),
+             "wide_skip": (150, 11, 128, True, True, 4), "narrow": (97, 13, 3, False, False, -1)}
+    for tag, (rows, S, D, identity, weighted, skip) in cases.items():
+        seg = rng.integers(0, S, rows).astype(np.int64)
+        if identity:
+            seg = np.sort(seg)
+        perm = np.argsort(seg, kind="stable").astype(np.int64)
+        off = np.searchsorted(seg[perm], np.arange(S + 1)).astype(np.int64)
+        V = rng.standard_normal((rows, D)).astype(np.float32)
+        W = rng.standard_normal((rows, D)).astype(np.float32)
+        G = rng.standard_normal((S, D)).astype(np.float32)
+        t = {k: torch.from_numpy(v) for k, v in dict(seg=seg, perm=perm, off=off, V=V, W=W, G=G).items()}
+        y = torch.empty(S, D)
+        bd = min(1 << (D - 1).bit_length(), 128)
+        cs._csr_segsum_fwd[(S, (D + bd - 1) // bd)](
+            t["V"], t["W"] if weighted else t["V"], t["off"] if identity else t["perm"], t["off"], y, S, skip,
+            D=D, VAL_S0=D, VAL_S1=1, W_S0=D, W_S1=1, BS=1, BR=16, BD=bd, IDENTITY_PERM=identity,
+            WEIGHTED=weighted, HAS_SKIP=skip >= 0, ACC_FP64=False)
+        gv, gw = torch.empty(rows, D), torch.empty(rows, D)
+        cs._csr_segsum_bwd_rows[((rows + 31) // 32, (D + bd - 1) // bd)](
+            t["G"], t["V"], t["W"] if weighted else t["V"], t["seg"], gv, gw, rows, skip, D=D, SEG_S0=1,
+            VAL_S0=D, VAL_S1=1, W_S0=D, W_S1=1, BM=32, BD=bd, WEIGHTED=weighted, NEED_GV=True,
+            NEED_GW=weighted, HAS_SKIP=skip >= 0)
+        out.update({f"segsum_{tag}_{k}": v for k, v in dict(seg=seg, perm=perm, off=off, V=V, W=W, G=G).items()})
+        out[f"segsum_{tag}_meta"] = np.array([S, int(identity), int(weighted), skip], dtype=np.int64)
+        out[f"segsum_{tag}_out"] = y.numpy()
+        out[f"segsum_{tag}_gvalue"] = gv.numpy()
+        if weighted:
+            out[f"segsum_{tag}_gweight"] = gw.numpy()
+    return out
+
+
+def nhc_cases(torch, gpu_nhc):
+    from ase import units
+
+    out = {}
+    rng = np.random.default_rng(13)
+    n = 10
+    masses = rng.uniform(1.0, 140.0, n)
+    q0 = rng.uniform(0.0, 8.0, (n, 3))
+    k_spring = 1.7
+
+    def harmonic(q, dtype):
+        f = -k_spring * (q - q0)
+        e = 0.5 * k_spring * float(np.sum((q - q0) ** 2))
+        return f.astype(dtype), e
+
+    cases = {"f64_m3_l1": (3, 1, np.float64), "f32_m3_l1": (3, 1, np.float32), "f64_m1_l1": (1, 1, np.float64),
+             "f64_m5_l2": (5, 2, np.float64)}
+    steps = 60
+    for tag, (tchain, tloop, fdtype) in cases.items():
+        momenta = gpu_nhc.maxwell_boltzmann_momenta(masses, 300.0, seed=0)
+        q_start = q0 + rng.normal(0.0, 0.1, (n, 3))
+        nhc = gpu_nhc.GPUNoseHooverChainNVT(
+            masses, q_start, momenta, temperature_K=300.0, timestep=1.0 * units.fs, tdamp=100.0 * units.fs,
+            tchain=tchain, tloop=tloop, device="cpu", backend="torch",
+            force_dtype=torch.float32 if fdtype == np.float32 else torch.float64)
+        f, e = harmonic(q_start, fdtype)
+        nhc.set_forces(torch.from_numpy(f), energy=torch.tensor([e], dtype=torch.float64))
+        flats = [nhc.state.flat.numpy().copy()]
+        for _ in range(steps):
+            q = nhc.step_pre_force().numpy().copy()
+            f, e = harmonic(q, fdtype)
+            nhc.step_post_force(torch.from_numpy(f), energy=torch.tensor([e], dtype=torch.float64))
+            flats.append(nhc.state.flat.numpy().copy())
+        out[f"nhc_{tag}_flat"] = np.array(flats)
+        out[f"nhc_{tag}_init"] = np.concatenate([masses, q_start.ravel(), momenta.ravel()])
+        out[f"nhc_{tag}_meta"] = np.array([n, tchain, tloop, int(fdtype == np.float32), steps], dtype=np.int64)
+    out["nhc_params"] = np.array([300.0, 1.0 * units.fs, 100.0 * units.fs, k_spring], dtype=np.float64)
+    out["nhc_q0"] = q0
+    # Maxwell-Boltzmann momenta of the 135-atom ABX3 masses at 500 K, seed 0
+    perov_masses = np.array([132.905, 118.71, 126.904, 126.904, 126.904] * 27)
+    out["mb_masses"] = perov_masses
+    out["mb_momenta_500K_seed0"] = gpu_nhc.maxwell_boltzmann_momenta(perov_masses, 500.0, seed=0)
+    return out
+
+
+def neighbor_cases(torch, fcb):
+    """The reference's fixed-capacity re-filter on dense candidate lists (wrapped positions)."""
+    out = {}
+    rng = np.random.default_rng(14)
+    systems = {
+        # cubic ABX3 3x3x3, a = 6.2, jittered: the 135-atom system of the benchmark configs
+        "perov": None,
+        # a triclinic cell with a short axis (images up to 2 away)
+        "tric": (np.array([[7.5, 0.0, 0.0], [1.9, 8.1, 0.0], [-1.2, 2.3, 9.4]], np.float32), 60),
+    }
+    for tag, spec in systems.items():
+        if spec is None:
+            frac_cell = np.array([[0, 0, 0], [.5, .5, .5], [.5, .5, 0], [.5, 0, .5], [0, .5, .5]])
+            grid = np.array([[i, j, k] for i in range(3) for j in range(3) for k in range(3)], float)
+            frac = (grid[:, None, :] + frac_cell[None, :, :]).reshape(-1, 3) / 3.0
+            cell = (np.eye(3) * 18.6).astype(np.float32)
+            pos = frac @ cell.astype(np.float64) + rng.normal(0, 0.05, frac.shape)
+        else:
+            cell, n = spec
+            pos = rng.uniform(0, 1, (n, 3)) @ cell.astype(np.float64) + rng.normal(0, 0.3, (n, 3))
+        pos32 = pos.astype(np.float32)
+        cell_t = torch.from_numpy(cell)
+        inv = torch.linalg.inv(cell_t)
+        p = torch.from_numpy(pos32)
+        frac_un = (p.unsqueeze(-1) * inv.unsqueeze(-3)).sum(dim=-2)
+        wraps = torch.floor(frac_un).to(torch.int32)
+        wrapped = ((frac_un - wraps.float()).unsqueeze(-1) * cell_t.unsqueeze(-3)).sum(dim=-2)
+        wrapped64 = wrapped.double().numpy()
+        cell64 = cell.astype(np.float64)
+        N = pos.shape[0]
+        # dense candidate lists at rc + skin (6 + 2), full list, every image in reach
+        rc, cand = 6.0, 8.0
+        heights = abs(np.linalg.det(cell64)) / np.array(
+            [np.linalg.norm(np.cross(cell64[(k + 1) % 3], cell64[(k + 2) % 3])) for k in range(3)])
+        reach = [int(np.ceil(cand / h)) + 1 for h in heights]
+        rows = [[] for _ in range(N)]
+        for ix in range(-reach[0], reach[0] + 1):
+            for iy in range(-reach[1], reach[1] + 1):
+                for iz in range(-reach[2], reach[2] + 1):
+                    shift = np.array([ix, iy, iz], float) @ cell64
+                    d = np.linalg.norm(wrapped64[None, :, :] + shift - wrapped64[:, None, :], axis=-1)
+                    for i, j in zip(*np.nonzero(d < cand)):
+                        if i != j or (ix, iy, iz) != (0, 0, 0):
+                            rows[i].append((j, ix, iy, iz))
+        bmax = max(len(r) for r in rows)
+        bmax = (bmax + 15) // 16 * 16
+        nm = np.full((N, bmax), N, np.int32)
+        ns = np.zeros((N, bmax, 3), np.int32)
+        nn = np.zeros(N, np.int32)
+        for i, r in enumerate(rows):
+            rng.shuffle(r)  # candidate order must not matter
+            nn[i] = len(r)
+            for k, (j, ix, iy, iz) in enumerate(r):
+                nm[i, k] = j
+                ns[i, k] = (ix, iy, iz)
+        t = dict(nm=torch.from_numpy(nm), ns=torch.from_numpy(ns), nn=torch.from_numpy(nn))
+        wrap_delta = torch.zeros(N, 3, dtype=torch.int32)
+        counts = torch.zeros(N, dtype=torch.int32)
+        iso = torch.zeros(1, dtype=torch.int32)
+        dummy_i = torch.zeros(1, dtype=torch.int32)
+        dummy_b = torch.zeros(1, dtype=torch.bool)
+        block = 1 << (bmax - 1).bit_length()
+        fcb._count_neighbors_kernel[(N,)](
+            wrapped, cell_t, t["nm"], t["ns"], t["nn"], wrap_delta, counts, counts, iso, dummy_i, N,
+            dummy_b, dummy_b, dummy_i, N=N, BMAX=bmax, BLOCK=block, EDGE_CUTOFF2=rc * rc, LINE_CUTOFF2=0.0,
+            HAS_SHORT=False)
+        offsets = torch.zeros(N + 1, dtype=torch.int64)
+        offsets[1:] = torch.cumsum(counts, 0)
+        E = int(offsets[-1])
+        center = torch.zeros(E, dtype=torch.int64)
+        neighbor = torch.zeros(E, dtype=torch.int64)
+        images = torch.zeros(E, 3, dtype=torch.int32)
+        dist = torch.zeros(E, dtype=torch.float32)
+        fcb._materialize_neighbors_kernel[(N,)](
+            wrapped, cell_t, t["nm"], t["ns"], t["nn"], wrap_delta, offsets, center, neighbor, images, dist,
+            counts, counts, N, dummy_b, dummy_b, dummy_i, N=N, BMAX=bmax, E_CAP=E, BLOCK=block,
+            EDGE_CUTOFF2=rc * rc, LINE_CUTOFF2=0.0, HAS_SHORT=False)
+        max_image = 12
+        radix = 2 * max_image + 1
+        key = ((center * N + neighbor) * radix**3 + (images[:, 0].long() + max_image) * radix * radix
+               + (images[:, 1].long() + max_image) * radix + images[:, 2].long() + max_image)
+        order = torch.argsort(key)
+        out[f"nbr_{tag}_cell"] = cell
+        out[f"nbr_{tag}_positions"] = pos32
+        out[f"nbr_{tag}_wrapped"] = wrapped.numpy()
+        out[f"nbr_{tag}_wraps"] = wraps.numpy()
+        out[f"nbr_{tag}_cand_matrix"] = nm
+        out[f"nbr_{tag}_cand_shifts"] = ns
+        out[f"nbr_{tag}_cand_count"] = nn
+        out[f"nbr_{tag}_counts"] = counts.numpy()
+        out[f"nbr_{tag}_edges"] = np.stack([center[order].numpy(), neighbor[order].numpy()], 1)
+        out[f"nbr_{tag}_images"] = images[order].numpy()
+        out[f"nbr_{tag}_dist"] = dist[order].numpy()
+        out[f"nbr_{tag}_cutoffs"] = np.array([rc, cand])
+    return out
+
+
+def main(reference: str) -> None:
+    os.environ["TRITON_INTERPRET"] = "1"
+    _install_stubs()
+    sys.path.insert(0, reference)
+    import torch
+
+    import fastmd.execution.gpu_nhc as gpu_nhc
+    import fastmd.graph.neighbor_list_backend as backend
+
+    # The re-filter kernels are defined only when the candidate backend (nvalchemiops, absent here)
+    # imports; they do not call it, so its import check is bypassed for this script.
+    backend.require = lambda: None
+    import fastmd.graph.fixed_capacity_builder as fcb
+    import fastmd.models.matris.op.triton_csr_segment_sum as cs
+    import fastmd.models.matris.op.triton_gather_cat as gc
+
+    np.savez_compressed(HERE / "gather_cat.npz", **gather_cat_cases(torch, gc))
+    np.savez_compressed(HERE / "segment_sum.npz", **segment_sum_cases(torch, cs))
+    np.savez_compressed(HERE / "nhc.npz", **nhc_cases(torch, gpu_nhc))
+    np.savez_compressed(HERE / "neighbors.npz", **neighbor_cases(torch, fcb))
+    for path in sorted(HERE.glob("*.npz")):
+        print(path.name, path.stat().st_size)
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

@@ -1,0 +1,73 @@
+"""The C ABI: the library loads, exports every entry point the headers declare, and rejects bad
+arguments with a status (CPU only: no call here reaches a kernel)."""
+import ctypes
+import re
+
+import pytest
+
+from conftest import ROOT
+
+
+def _declared():
+    names = []
+    for header in sorted((ROOT / "include").glob("*.h")):
+        names += re.findall(r"^FMD_API\s+[\w\s\*]+?\b(fmd_\w+)\s*\(", header.read_text(), flags=re.M)
+    return names
+
+
+def test_headers_declare_entry_points():
+    names = _declared()
+    assert len(names) >= 10
+    assert len(names) == len(set(names))
+
+
+def test_library_exports_every_declared_symbol():
+    from fastmd_b200 import _lib
+
+    lib = _lib.lib()
+    missing = [name for name in _declared() if not hasattr(lib, name)]
+    assert not missing, missing
+
+
+def test_python_binding_covers_every_symbol():
+    from fastmd_b200 import _lib
+
+    import fastmd_b200  # noqa: F401  (modules that register extra signatures)
+    missing = [name for name in _declared() if name not in _lib._SIGNATURES]
+    assert not missing, missing
+
+
+def test_status_strings_and_version():
+    from fastmd_b200 import _lib
+
+    lib = _lib.lib()
+    assert lib.fmd_version() >= 100
+    assert lib.fmd_status_string(0) == b"ok"
+    assert lib.fmd_status_string(1) == b"invalid argument"
+    assert lib.fmd_status_string(99) == b"unknown status"
+
+
+def test_invalid_arguments_are_rejected_before_any_launch():
+    from fastmd_b200 import _lib
+
+    lib = _lib.lib()
+    assert lib.fmd_gather_cat(None, 0, 0, None, 0, None, None) == 1
+    assert lib.fmd_copy_rows(None, 0, None, 0, 1, 1, None) == 1
+    assert lib.fmd_csr_segment_sum(None, 0, None, 0, None, None, 1, 1, -1, None, 0, None) == 1
+    assert lib.fmd_nhc_pre_force(None, None, None, 1, 1, 3, 1, 0, None, None) == 1
+    assert lib.fmd_nhc_post_force(ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16), 1, 1, 3, 1, 0,
+                                  None, None, None, None) == 1  # neither force dtype
+
+
+def test_no_cpu_fallback():
+    import torch
+
+    from fastmd_b200 import ops
+    from fastmd_b200._lib import FastMDLibraryError
+
+    x = torch.zeros(4, 8)
+    idx = torch.zeros(4, dtype=torch.int64)
+    with pytest.raises(FastMDLibraryError):
+        ops.aligned_gather_cat3(x, x, idx, idx)
+    with pytest.raises(FastMDLibraryError):
+        ops.csr_segment_sum(x, idx, 2)

@@ -1,0 +1,121 @@
+"""The fused Nose-Hoover-chain kernels against the reference's torch backend (golden) and the oracle."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(tag, cuda, replicas=1, graph=False):
+    from fastmd_b200.gpu_nhc import GPUNoseHooverChainNVT, ReplicaNoseHooverChainNVT
+
+    g = golden("nhc")
+    n, tchain, tloop, f32, steps = (int(v) for v in g[f"nhc_{tag}_meta"])
+    T, dt, tdamp, k = g["nhc_params"]
+    q0 = torch.from_numpy(g["nhc_q0"]).to(cuda)
+    init = g[f"nhc_{tag}_init"]
+    masses, q, p = init[:n], init[n:4 * n].reshape(n, 3), init[4 * n:].reshape(n, 3)
+    fdt = torch.float32 if f32 else torch.float64
+    kw = dict(temperature_K=T, timestep=dt, tdamp=tdamp, tchain=tchain, tloop=tloop, force_dtype=fdt,
+              device=cuda)
+    if replicas == 1:
+        nhc = GPUNoseHooverChainNVT(masses, q, p, **kw)
+    else:
+        nhc = ReplicaNoseHooverChainNVT(masses, np.tile(q, (replicas, 1)), np.tile(p, (replicas, 1)),
+                                        replicas=replicas, **kw)
+    q0r = q0.repeat(replicas, 1)
+
+    def forces(x):
+        d = x - q0r
+        e = (0.5 * k * (d * d).reshape(replicas, -1).sum(dim=1))
+        return (-k * d).to(fdt), e
+
+    f, e = forces(nhc.positions)
+    nhc.set_forces(f, e)
+    flats = [nhc.state.flat.clone()]
+    if graph:
+        static = {}
+        stream = torch.cuda.Stream()
+        stream.wait_stream(torch.cuda.current_stream())
+        g_ = torch.cuda.CUDAGraph()
+        snapshot = nhc.snapshot()
+        with torch.cuda.stream(stream):
+            for _ in range(2):  # warm-up
+                x = nhc.step_pre_force()
+                f, e = forces(x)
+                nhc.step_post_force(f, e)
+        torch.cuda.current_stream().wait_stream(stream)
+        nhc.load_snapshot(snapshot)
+        with torch.cuda.graph(g_):
+            x = nhc.step_pre_force()
+            f, e = forces(x)
+            nhc.step_post_force(f, e)
+        for _ in range(steps):
+            g_.replay()
+            flats.append(nhc.state.flat.clone())
+    else:
+        for _ in range(steps):
+            x = nhc.step_pre_force()
+            f, e = forces(x)
+            nhc.step_post_force(f, e)
+            flats.append(nhc.state.flat.clone())
+    return nhc, torch.stack(flats).cpu().numpy(), g[f"nhc_{tag}_flat"], n, tchain
+
+
+def _layout_single(flat, n, M, R, r):
+    """Replica r's [q|p|F|eta|p_eta|E] from the R-replica layout."""
+    n3 = 3 * n
+    q = flat[:, r * n3:(r + 1) * n3]
+    p = flat[:, R * n3 + r * n3:R * n3 + (r + 1) * n3]
+    f = flat[:, 2 * R * n3 + r * n3:2 * R * n3 + (r + 1) * n3]
+    base = 3 * R * n3
+    eta = flat[:, base + r * M:base + (r + 1) * M]
+    pe = flat[:, base + R * M + r * M:base + R * M + (r + 1) * M]
+    e = flat[:, base + 2 * R * M + r:base + 2 * R * M + r + 1]
+    return np.concatenate([q, p, f, eta, pe, e], axis=1)
+
+
+def _max_rel(a, b):
+    scale = np.maximum(np.abs(b).max(axis=0, keepdims=True), 1e-30)
+    return float(np.max(np.abs(a - b) / scale))
+
+
+@pytest.mark.parametrize("tag", ["f64_m3_l1", "f32_m3_l1", "f64_m1_l1", "f64_m5_l2"])
+def test_nhc_matches_reference_trajectory(cuda, tag):
+    _, mine, ref, n, M = _run(tag, cuda)
+    assert mine.shape == ref.shape
+    assert _max_rel(mine, ref) < 1e-12
+
+
+def test_replicas_bitwise_equal_single_system(cuda):
+    _, single, _, n, M = _run("f64_m3_l1", cuda)
+    _, rep, _, _, _ = _run("f64_m3_l1", cuda, replicas=4)
+    for r in range(4):
+        assert np.array_equal(_layout_single(rep, n, M, 4, r), single)
+
+
+def test_graph_replay_bitwise_equal_eager(cuda):
+    _, eager, _, _, _ = _run("f32_m3_l1", cuda)
+    _, replay, _, _, _ = _run("f32_m3_l1", cuda, graph=True)
+    assert np.array_equal(eager, replay)
+
+
+def test_backup_restore_and_observables(cuda):
+    nhc, _, _, n, M = _run("f64_m3_l1", cuda)
+    nhc.backup()
+    before = nhc.state.flat.clone()
+    nhc.step_pre_force()
+    nhc.restore()
+    assert torch.equal(before, nhc.state.flat)
+    ke = float(nhc.kinetic_energy())
+    p = nhc.momenta.cpu().numpy()
+    m = nhc.masses.cpu().numpy()
+    assert abs(ke - 0.5 * np.sum(p * p / m)) < 1e-12 * abs(ke)
+    assert np.isfinite(float(nhc.conserved_energy()))
+
+
+def test_positions32_follow_the_drift(cuda):
+    nhc, _, _, _, _ = _run("f64_m3_l1", cuda)
+    assert torch.equal(nhc.positions32, nhc.positions.float())
