@@ -41,6 +41,24 @@ _SIGNATURES: dict[str, list] = {
     "fmd_csr_build": [_P, _I64, _I64, _P, _P, _P, c_size_t, _P, _P],
     "fmd_csr_segment_sum": [_P, _I64, _P, _I64, _P, _P, _I64, _I32, _I64, _P, _I64, _P],
     "fmd_csr_segment_sum_bwd": [_P, _P, _I64, _P, _I64, _P, _I64, _I64, _I32, _I64, _P, _P, _P, _P],
+    "fmd_cell_list_workspace_bytes": [_P, c_float, _I64, _I32, POINTER(c_size_t)],
+    "fmd_candidates_build": [_P, _P, _I64, _I32, c_float, _I32, _P, _P, _P, _P, _P, _P, _P, c_size_t, _P, _P],
+    "fmd_refilter_workspace_bytes": [_I64, _I32, POINTER(c_size_t)],
+    "fmd_refilter_edges": [_P, _P, _I64, _I32, _P, _P, _P, _P, _P, _I32, c_float, c_float, _I64, _P, _I32, _P, _P,
+                           _P, _P, _P, _P, _P, _P, _P, _P, c_size_t, _P, _P],
+    "fmd_neighbor_list_workspace_bytes": [_P, c_float, _I64, _I32, POINTER(c_size_t)],
+    "fmd_neighbor_list": [_P, _P, _I64, c_float, _I32, _I64, _P, _P, _P, _P, _P, _P, _P, c_size_t, _P, _P],
+    "fmd_gemm_f32": [_P, _I64, _P, _I64, _P, _I64, _I32, _P, _P, _I64, _P, _I64, _I64, _I32, _I32, _I32, _I32, _P],
+    "fmd_mace_edge_geometry": [_P, _P, _P, _P, _I64, c_float, _I32, _I32, _P, _P, _P],
+    "fmd_mace_edge_geometry_bwd": [_P, _P, _P, c_float, _I32, _I32, _P, _P, _P, _P, _I64, _P, c_float, _I32, _P],
+    "fmd_mace_message": [_P, _I32, _P, _P, _P, _P, _P, _I64, _I32, c_float, _P, _P, _P],
+    "fmd_mace_message_bwd": [_P, _P, _P, _I32, _P, _P, _P, _P, _P, _P, _P, _I64, _I32, c_float, _P, _P, _I32, _P, _P,
+                             _P],
+    "fmd_mace_product": [_P, _P, _P, _P, _P, _I64, _I32, _P, _P, _P],
+    "fmd_mace_product_bwd": [_P, _P, _P, _P, _P, _P, _P, _I64, _I32, _P, _P, _P],
+    "fmd_element_linear": [_P, _I64, _I32, _P, _P, _I32, _I32, _I32, _P, _I32, _P],
+    "fmd_mace_node_energy": [_P, _I32, _I64, _P, _P, c_double, c_double, _I64, _I32, _P, _P, _P],
+    "fmd_mace_node_energy_bwd": [_P, c_double, _I64, _I32, _P, _P],
     "fmd_nhc_pre_force": [_P, _P, _P, _I64, _I32, _I32, _I32, _I32, _P, _P],
     "fmd_nhc_post_force": [_P, _P, _P, _I64, _I32, _I32, _I32, _I32, _P, _P, _P, _P],
 }

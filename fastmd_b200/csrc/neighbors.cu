@@ -1,0 +1,1101 @@
+// Neighbour lists of periodic systems: the cell-list candidate build and the
+// per-step exact re-filter of FastMD's fixed-capacity builder, and the
+// ragged (eager) neighbour list.
+//
+// Layout: R systems ("replicas") of n atoms each share one cell; atom a of
+// system r is global row r*n + a, and no pair crosses systems (the
+// disjoint-union graph of replica_batch.py).
+//
+// Candidate build (cell list):
+//   bin:     wrap every atom (the builder's float32 arithmetic), cell index
+//            from the fractional coordinates, atomic slot in the cell;
+//   scan:    cell starts (CUB exclusive scan over R*ncells counts);
+//   scatter: atoms grouped by cell, their wrapped positions as float4;
+//   query:   one CTA per home cell stages the atoms of the (2s+1)^3
+//            neighbouring (cell, image) pairs in shared memory, each warp
+//            tests one home atom against the staged atoms, compacts the hits
+//            with a warp ballot into a per-warp list, ranks the list by the
+//            canonical key (neighbour, image) and writes it out. The output
+//            order is therefore independent of the atomics of the bin pass.
+//
+// Re-filter (every MD step, inside the whole-step CUDA graph): two kernels,
+// one CTA per system. The count kernel wraps the positions (wrap delta
+// since the candidate refresh, skin test), and counts per atom the
+// candidates with dist2 < rc^2 evaluated in the reference's float32
+// operation order (fixed_capacity_builder.py:159-163; this file is compiled
+// without FMA contraction). The materialize kernel writes the edges with a
+// ballot compaction at the global offsets (candidates are sorted once per
+// refresh, so the edges come out in canonical order with no per-step sort),
+// the receiver CSR, the sender CSR (each run ascending), the padding rows
+// (far self-loops) and the status words.
+
+#include <cub/device/device_scan.cuh>
+
+#include "common.cuh"
+
+namespace fmd {
+
+// ------------------------------------------------------------------ geometry
+
+struct Cell9 {
+    float c[9];      // row-major lattice vectors
+    float inv[9];    // row-major float32 inverse
+};
+
+// small_matmul row: out[c] = (a0*m[0][c] + a1*m[1][c]) + a2*m[2][c] (geometry.py:7)
+__device__ __forceinline__ float3 row_times(float3 a, const float* m) {
+    return make_float3((a.x * m[0] + a.y * m[3]) + a.z * m[6], (a.x * m[1] + a.y * m[4]) + a.z * m[7],
+                       (a.x * m[2] + a.y * m[5]) + a.z * m[8]);
+}
+
+// build prologue (fixed_capacity_builder.py:2203-2208)
+__device__ __forceinline__ void wrap_atom(float3 p, const Cell9& cell, float3& wrapped, int3& wraps,
+                                          float3& frac) {
+    const float3 fu = row_times(p, cell.inv);
+    const float wx = floorf(fu.x), wy = floorf(fu.y), wz = floorf(fu.z);
+    wraps = make_int3(int(wx), int(wy), int(wz));
+    frac = make_float3(fu.x - wx, fu.y - wy, fu.z - wz);
+    wrapped = row_times(frac, cell.c);
+}
+
+// dist2 of a candidate in the re-filter's operation order (fixed_capacity_builder.py:159-163)
+__device__ __forceinline__ float refilter_dist2(float3 p, float3 q, float sx, float sy, float sz,
+                                                const float* c) {
+    const float dx = (((q.x - p.x) + sx * c[0]) + sy * c[3]) + sz * c[6];
+    const float dy = (((q.y - p.y) + sx * c[1]) + sy * c[4]) + sz * c[7];
+    const float dz = (((q.z - p.z) + sx * c[2]) + sy * c[5]) + sz * c[8];
+    return (dx * dx + dy * dy) + dz * dz;
+}
+
+// distance of the ragged path's re-filter (gpu_graph_builder.py:186-192):
+// diff = (q - p) + image @ cell (small_matmul), dist = |diff|
+__device__ __forceinline__ float ragged_dist(float3 p, float3 q, int3 s, const float* c) {
+    const float3 sh = row_times(make_float3(float(s.x), float(s.y), float(s.z)), c);
+    const float dx = (q.x - p.x) + sh.x, dy = (q.y - p.y) + sh.y, dz = (q.z - p.z) + sh.z;
+    return sqrtf((dx * dx + dy * dy) + dz * dz);
+}
+
+__device__ __forceinline__ float3 ld3(const float* p, int64_t i) {
+    return make_float3(p[3 * i], p[3 * i + 1], p[3 * i + 2]);
+}
+
+__device__ __forceinline__ int3 ld3i(const int32_t* p, int64_t i) {
+    return make_int3(p[3 * i], p[3 * i + 1], p[3 * i + 2]);
+}
+
+// canonical key of a candidate of one centre: neighbour, then the image
+// (each component offset by 512, 10 bits): unique per (neighbour, image)
+__device__ __forceinline__ uint64_t cand_key(int32_t nbr, int3 s) {
+    return (uint64_t(uint32_t(nbr)) << 30) | (uint64_t(uint32_t(s.x + 512) & 1023u) << 20) |
+           (uint64_t(uint32_t(s.y + 512) & 1023u) << 10) | uint64_t(uint32_t(s.z + 512) & 1023u);
+}
+
+__device__ __forceinline__ int floor_div(int a, int b) { return a >= 0 ? a / b : -((-a + b - 1) / b); }
+
+struct Grid {
+    int n[3];       // cells per axis
+    int s[3];       // search reach in cells per axis
+    int ncells;     // n0*n1*n2 (per system)
+};
+
+// --------------------------------------------------------------- cell list
+
+__global__ void cell_bin_kernel(const float* __restrict__ positions, int64_t n_atoms, int32_t n_systems,
+                                Cell9 cell, Grid grid, float4* __restrict__ wrapped_out,
+                                int32_t* __restrict__ atom_cell, int32_t* __restrict__ atom_slot,
+                                int32_t* __restrict__ cell_count, int32_t* flags) {
+    const int64_t total = n_atoms * n_systems;
+    for (int64_t a = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; a < total;
+         a += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t sys = a / n_atoms;
+        float3 w, f;
+        int3 wr;
+        wrap_atom(ld3(positions, a), cell, w, wr, f);
+        const bool finite = isfinite(w.x) && isfinite(w.y) && isfinite(w.z);
+        if (!finite) raise_flag(flags, FMD_FLAG_NONFINITE);
+        int cx = finite ? int(floorf(f.x * grid.n[0])) : 0;
+        int cy = finite ? int(floorf(f.y * grid.n[1])) : 0;
+        int cz = finite ? int(floorf(f.z * grid.n[2])) : 0;
+        cx = min(max(cx, 0), grid.n[0] - 1);
+        cy = min(max(cy, 0), grid.n[1] - 1);
+        cz = min(max(cz, 0), grid.n[2] - 1);
+        const int c = int(sys * grid.ncells) + (cx * grid.n[1] + cy) * grid.n[2] + cz;
+        atom_cell[a] = c;
+        atom_slot[a] = atomicAdd(cell_count + c, 1);
+        wrapped_out[a] = make_float4(w.x, w.y, w.z, 0.f);
+    }
+}
+
+__global__ void cell_scatter_kernel(int64_t total, const float4* __restrict__ wrapped,
+                                    const int32_t* __restrict__ atom_cell, const int32_t* __restrict__ atom_slot,
+                                    const int32_t* __restrict__ cell_start, int32_t* __restrict__ cell_atoms,
+                                    float4* __restrict__ cell_pos) {
+    for (int64_t a = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; a < total;
+         a += int64_t(gridDim.x) * blockDim.x) {
+        const int k = cell_start[atom_cell[a]] + atom_slot[a];
+        cell_atoms[k] = int32_t(a);
+        float4 p = wrapped[a];
+        cell_pos[k] = p;
+    }
+}
+
+constexpr int kQueryWarps = 8;
+constexpr int kStageCap = 1024;   // staged (atom, image) entries per chunk
+constexpr int kMaxOffsets = 1331; // (2s+1)^3 neighbour (cell, image) pairs, s <= 5
+constexpr int kMaxHome = 512;     // home atoms handled per pass over the neighbourhood
+
+struct QueryArgs {
+    const int32_t* cell_start;   // [R*ncells + 1]
+    const int32_t* cell_atoms;   // grouped by cell
+    const float4* cell_pos;      // wrapped positions grouped by cell
+    int64_t n_atoms;             // per system
+    int32_t n_systems;
+    Cell9 cell;
+    Grid grid;
+    float cutoff;                // candidate cutoff (dist2 < cutoff^2, FP32)
+    int32_t bmax;                // slots per atom in the output matrix
+    int32_t list_cap;            // per-warp sort buffer (shared memory), >= bmax
+    int32_t* nbr_out;            // [R*n, bmax] global neighbour rows
+    int32_t* shift_out;          // [R*n, bmax, 3]
+    int32_t* count_out;          // [R*n] true candidate count
+    int32_t* flags;
+};
+
+struct QuerySmem {
+    float4* pos;       // [kStageCap] staged positions, shifted by their image
+    int32_t* atom;     // [kStageCap]
+    int32_t* img;      // [kStageCap] packed image
+    int32_t* o_begin;  // [kMaxOffsets] first atom of the offset's cell
+    int32_t* o_pref;   // [kMaxOffsets + 1] exclusive prefix of the offsets' atom counts
+    int32_t* o_img;    // [kMaxOffsets]
+    float* o_shift;    // [kMaxOffsets * 3]
+    int32_t* hits;     // [kMaxHome]
+    uint64_t* list;    // [kQueryWarps * list_cap]
+};
+
+inline size_t query_smem(int list_cap) {
+    return sizeof(float4) * kStageCap + 2 * sizeof(int32_t) * kStageCap + sizeof(int32_t) * kMaxOffsets * 3 +
+           sizeof(int32_t) * (kMaxOffsets + 1) + sizeof(float) * kMaxOffsets * 3 + sizeof(int32_t) * kMaxHome +
+           sizeof(uint64_t) * size_t(kQueryWarps) * list_cap + 64;
+}
+
+__device__ QuerySmem carve_query_smem(unsigned char* raw, int list_cap) {
+    QuerySmem m;
+    m.pos = reinterpret_cast<float4*>(raw);
+    m.list = reinterpret_cast<uint64_t*>(m.pos + kStageCap);
+    m.atom = reinterpret_cast<int32_t*>(m.list + size_t(kQueryWarps) * list_cap);
+    m.img = m.atom + kStageCap;
+    m.o_begin = m.img + kStageCap;
+    m.o_pref = m.o_begin + kMaxOffsets;
+    m.o_img = m.o_pref + kMaxOffsets + 1;
+    m.hits = m.o_img + kMaxOffsets;
+    m.o_shift = reinterpret_cast<float*>(m.hits + kMaxHome);
+    return m;
+}
+
+__global__ void __launch_bounds__(kQueryWarps * 32) cell_query_kernel(QueryArgs q) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const QuerySmem m = carve_query_smem(smem_raw, q.list_cap);
+    __shared__ int s_scan[32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ncells = q.grid.ncells;
+    const int64_t total_cells = int64_t(ncells) * q.n_systems;
+    const float cut2 = q.cutoff * q.cutoff;
+    const int r0 = q.grid.s[0], r1 = q.grid.s[1], r2 = q.grid.s[2];
+    const int w1 = 2 * r1 + 1, w2 = 2 * r2 + 1;
+    const int n_off = (2 * r0 + 1) * w1 * w2;
+    const int zero_img = (512 << 20) | (512 << 10) | 512;
+    for (int64_t home = blockIdx.x; home < total_cells; home += gridDim.x) {
+        const int64_t sys = home / ncells;
+        const int32_t sys_base = int32_t(sys * q.n_atoms);
+        const int local = int(home - sys * ncells);
+        const int hx = local / (q.grid.n[1] * q.grid.n[2]);
+        const int hy = (local / q.grid.n[2]) % q.grid.n[1];
+        const int hz = local % q.grid.n[2];
+        const int h_begin = q.cell_start[home], h_end = q.cell_start[home + 1];
+        if (h_begin == h_end) continue;  // uniform per CTA
+        // the neighbourhood: (cell, image) per offset, atom counts, prefix
+        __syncthreads();
+        int running = 0;
+        for (int o0 = 0; o0 < n_off; o0 += blockDim.x) {
+            const int o = o0 + threadIdx.x;
+            int cnt = 0;
+            if (o < n_off) {
+                const int ox = o / (w1 * w2) - r0, oy = (o / w2) % w1 - r1, oz = o % w2 - r2;
+                const int gx = hx + ox, gy = hy + oy, gz = hz + oz;
+                const int ix = floor_div(gx, q.grid.n[0]), iy = floor_div(gy, q.grid.n[1]), iz = floor_div(gz, q.grid.n[2]);
+                const int cx = gx - ix * q.grid.n[0], cy = gy - iy * q.grid.n[1], cz = gz - iz * q.grid.n[2];
+                const int64_t c = sys * ncells + (cx * q.grid.n[1] + cy) * q.grid.n[2] + cz;
+                const int b = q.cell_start[c];
+                cnt = q.cell_start[c + 1] - b;
+                m.o_begin[o] = b;
+                m.o_img[o] = ((ix + 512) << 20) | ((iy + 512) << 10) | (iz + 512);
+                const float fx = float(ix), fy = float(iy), fz = float(iz);
+                m.o_shift[3 * o] = (fx * q.cell.c[0] + fy * q.cell.c[3]) + fz * q.cell.c[6];
+                m.o_shift[3 * o + 1] = (fx * q.cell.c[1] + fy * q.cell.c[4]) + fz * q.cell.c[7];
+                m.o_shift[3 * o + 2] = (fx * q.cell.c[2] + fy * q.cell.c[5]) + fz * q.cell.c[8];
+            }
+            // block exclusive scan of cnt
+            const int lane_s = threadIdx.x & 31, warp_s = threadIdx.x >> 5;
+            int x = cnt;
+            for (int d = 1; d < 32; d <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, x, d);
+                if (lane_s >= d) x += y;
+            }
+            __syncthreads();
+            if (lane_s == 31) s_scan[warp_s] = x;
+            __syncthreads();
+            int before = 0, chunk_total = 0;
+            for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+                if (w < warp_s) before += s_scan[w];
+                chunk_total += s_scan[w];
+            }
+            if (o < n_off) m.o_pref[o] = running + before + x - cnt;
+            running += chunk_total;
+            __syncthreads();
+        }
+        if (threadIdx.x == 0) m.o_pref[n_off] = running;
+        const int staged_total = running;
+        for (int hb = h_begin; hb < h_end; hb += kMaxHome) {
+            const int n_home = min(kMaxHome, h_end - hb);
+            for (int h = threadIdx.x; h < n_home; h += blockDim.x) m.hits[h] = 0;
+            for (int c0 = 0; c0 < staged_total; c0 += kStageCap) {
+                const int ns = min(kStageCap, staged_total - c0);
+                __syncthreads();
+                for (int t = threadIdx.x; t < ns; t += blockDim.x) {
+                    const int k = c0 + t;
+                    int lo = 0, hi = n_off;  // last offset with o_pref[o] <= k
+                    while (hi - lo > 1) {
+                        const int mid = (lo + hi) >> 1;
+                        if (m.o_pref[mid] <= k) lo = mid; else hi = mid;
+                    }
+                    const int src = m.o_begin[lo] + (k - m.o_pref[lo]);
+                    const float4 p = q.cell_pos[src];
+                    m.pos[t] = make_float4(p.x + m.o_shift[3 * lo], p.y + m.o_shift[3 * lo + 1],
+                                           p.z + m.o_shift[3 * lo + 2], 0.f);
+                    m.atom[t] = q.cell_atoms[src];
+                    m.img[t] = m.o_img[lo];
+                }
+                __syncthreads();
+                for (int h = warp; h < n_home; h += kQueryWarps) {
+                    const float4 hp = q.cell_pos[hb + h];
+                    const int32_t ha = q.cell_atoms[hb + h];
+                    const int64_t row = ha;
+                    int hits = m.hits[h];
+                    for (int base = 0; base < ns; base += 32) {
+                        const int k = base + lane;
+                        bool hit = false;
+                        int32_t atom = 0;
+                        int packed = 0;
+                        if (k < ns) {
+                            const float4 p = m.pos[k];
+                            const float dx = p.x - hp.x, dy = p.y - hp.y, dz = p.z - hp.z;
+                            const float d2 = (dx * dx + dy * dy) + dz * dz;
+                            atom = m.atom[k];
+                            packed = m.img[k];
+                            hit = d2 < cut2 && !(atom == ha && packed == zero_img);
+                        }
+                        const unsigned mask = __ballot_sync(0xffffffffu, hit);
+                        if (hit) {
+                            const int pos = hits + __popc(mask & ((1u << lane) - 1u));
+                            if (pos < q.bmax) {
+                                const int64_t slot = row * q.bmax + pos;
+                                q.nbr_out[slot] = atom;
+                                q.shift_out[3 * slot] = ((packed >> 20) & 1023) - 512;
+                                q.shift_out[3 * slot + 1] = ((packed >> 10) & 1023) - 512;
+                                q.shift_out[3 * slot + 2] = (packed & 1023) - 512;
+                            }
+                        }
+                        hits += __popc(mask);
+                    }
+                    if (lane == 0) m.hits[h] = hits;
+                }
+            }
+            __syncthreads();
+            // canonical order of every home row: rank sort by (neighbour, image)
+            uint64_t* list = m.list + size_t(warp) * q.list_cap;
+            for (int h = warp; h < n_home; h += kQueryWarps) {
+                const int32_t ha = q.cell_atoms[hb + h];
+                const int64_t row = ha;
+                const int hits = m.hits[h];
+                const int k_list = min(hits, q.bmax);
+                if (k_list > q.list_cap) {  // more than the sort buffer holds: reported, left unsorted
+                    if (lane == 0) {
+                        q.count_out[row] = hits;
+                        raise_flag(q.flags, FMD_FLAG_CANDIDATE_OVERFLOW);
+                    }
+                    continue;
+                }
+                for (int e = lane; e < k_list; e += 32) {
+                    const int64_t slot = row * q.bmax + e;
+                    const int3 s3 = make_int3(q.shift_out[3 * slot], q.shift_out[3 * slot + 1], q.shift_out[3 * slot + 2]);
+                    list[e] = cand_key(q.nbr_out[slot] - sys_base, s3);
+                }
+                __syncwarp();
+                for (int e = lane; e < k_list; e += 32) {
+                    const uint64_t key = list[e];
+                    int rank = 0;
+                    for (int f = 0; f < k_list; ++f) rank += list[f] < key ? 1 : 0;
+                    const int64_t slot = row * q.bmax + rank;
+                    q.nbr_out[slot] = sys_base + int32_t(key >> 30);
+                    q.shift_out[3 * slot] = int32_t((key >> 20) & 1023u) - 512;
+                    q.shift_out[3 * slot + 1] = int32_t((key >> 10) & 1023u) - 512;
+                    q.shift_out[3 * slot + 2] = int32_t(key & 1023u) - 512;
+                }
+                if (lane == 0) {
+                    q.count_out[row] = hits;
+                    if (hits > q.bmax) raise_flag(q.flags, FMD_FLAG_CANDIDATE_OVERFLOW);
+                }
+                __syncwarp();
+            }
+            __syncthreads();
+        }
+    }
+}
+
+// fill unused candidate slots (neighbour = R*n, shift 0) of every row
+__global__ void cand_fill_kernel(int64_t rows, int32_t bmax, int32_t fill, int32_t* __restrict__ nbr,
+                                 int32_t* __restrict__ shift, const int32_t* __restrict__ count) {
+    const int64_t total = rows * bmax;
+    for (int64_t t = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; t < total;
+         t += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t r = t / bmax;
+        const int k = int(t - r * bmax);
+        if (k >= count[r]) {
+            nbr[t] = fill;
+            shift[3 * t] = 0;
+            shift[3 * t + 1] = 0;
+            shift[3 * t + 2] = 0;
+        }
+    }
+}
+
+// reference snapshot of the refresh: positions, wraps; wrap delta reset
+__global__ void refresh_reference_kernel(const float* __restrict__ positions, int64_t total, Cell9 cell,
+                                         float* __restrict__ ref_pos, int32_t* __restrict__ ref_wraps,
+                                         int32_t* __restrict__ wrap_delta) {
+    for (int64_t a = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; a < total;
+         a += int64_t(gridDim.x) * blockDim.x) {
+        float3 p = ld3(positions, a), w, f;
+        int3 wr;
+        wrap_atom(p, cell, w, wr, f);
+        ref_pos[3 * a] = p.x;
+        ref_pos[3 * a + 1] = p.y;
+        ref_pos[3 * a + 2] = p.z;
+        ref_wraps[3 * a] = wr.x;
+        ref_wraps[3 * a + 1] = wr.y;
+        ref_wraps[3 * a + 2] = wr.z;
+        wrap_delta[3 * a] = 0;
+        wrap_delta[3 * a + 1] = 0;
+        wrap_delta[3 * a + 2] = 0;
+    }
+}
+
+// ------------------------------------------------------------ re-filter
+
+constexpr int kRefThreads = 512;
+constexpr int kRefWarps = kRefThreads / 32;
+
+struct RefilterArgs {
+    const float* positions;      // [R*n, 3] float32 (the integrator's float32 copy)
+    Cell9 cell;
+    const float* ref_pos;        // refresh snapshot
+    const int32_t* ref_wraps;
+    const int32_t* cand_nbr;     // [R*n, bmax] global rows
+    const int32_t* cand_shift;   // [R*n, bmax, 3]
+    const int32_t* cand_count;   // [R*n]
+    int64_t n_atoms;
+    int32_t n_systems;
+    int32_t bmax;
+    float cutoff2;               // rc^2 (float32)
+    float skin_limit;            // skin + 1e-6: an atom may move skin_limit / 2
+    int32_t minimum_image;       // a lattice jump of the caller's coordinates is no motion
+    int64_t e_cap;               // edge rows of the whole union
+    int32_t pad_image[3];        // far self-loop image
+    // outputs
+    float* wrapped;              // [R*n, 3]
+    int32_t* wrap_delta;         // [R*n, 3]
+    int32_t* counts;             // [R*n] edges per centre
+    int32_t* local_off;          // [R*n] exclusive offsets inside the system
+    int32_t* sys_total;          // [R]
+    float* max_disp;             // [R]
+    int32_t* edge_index;         // [e_cap, 2] (centre, neighbour), global rows
+    float* edge_image;           // [e_cap, 3]
+    int64_t* recv_off;           // [R*n + 1] receiver CSR (real edges)
+    int64_t* send_off;           // [R*n + 1] sender CSR offsets
+    int32_t* send_perm;          // [e_cap] edge ids grouped by sender (first n_edges used)
+    int64_t* n_edges;            // [1]
+    int32_t* flags;              // [1]: FMD_FLAG_* of this build
+};
+
+__device__ __forceinline__ int block_scan_exclusive(int v, int* smem, int& total) {
+    // blockDim <= 1024; warp scan + warp totals
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, m);
+        if (lane >= m) x += y;
+    }
+    __syncthreads();
+    if (lane == 31) smem[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        const int nw = blockDim.x >> 5;
+        int w = lane < nw ? smem[lane] : 0;
+#pragma unroll
+        for (int m = 1; m < 32; m <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, w, m);
+            if (lane >= m) w += y;
+        }
+        if (lane < nw) smem[lane] = w;  // inclusive warp prefix
+    }
+    __syncthreads();
+    const int before = warp > 0 ? smem[warp - 1] : 0;
+    total = smem[(blockDim.x >> 5) - 1];
+    __syncthreads();
+    return before + x - v;
+}
+
+// Count kernel: one CTA per system.
+__global__ void __launch_bounds__(kRefThreads) refilter_count_kernel(RefilterArgs a) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    float3* s_w = reinterpret_cast<float3*>(smem_raw);                    // wrapped [n]
+    int3* s_wd = reinterpret_cast<int3*>(s_w + a.n_atoms);                // wrap delta [n]
+    __shared__ int s_scan[32];
+    __shared__ float s_max[32];
+    const int64_t sys = blockIdx.x;
+    const int64_t base = sys * a.n_atoms;
+    const int n = int(a.n_atoms);
+    float my_max = 0.f;
+    bool nonfinite = false;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int64_t g = base + i;
+        float3 p = ld3(a.positions, g), w, f;
+        int3 wr;
+        wrap_atom(p, a.cell, w, wr, f);
+        const int3 rw = ld3i(a.ref_wraps, g);
+        int3 wd = make_int3(wr.x - rw.x, wr.y - rw.y, wr.z - rw.z);
+        const float3 r = ld3(a.ref_pos, g);
+        float dx = p.x - r.x, dy = p.y - r.y, dz = p.z - r.z;
+        if (a.minimum_image) {
+            // minimum-image displacement; the jump leaves the wrapped row (and the images) unchanged
+            // (fixed_capacity_builder.py:2229-2241)
+            const float3 fj = row_times(make_float3(dx, dy, dz), a.cell.inv);
+            const float jx = rintf(fj.x), jy = rintf(fj.y), jz = rintf(fj.z);
+            const float3 lj = row_times(make_float3(jx, jy, jz), a.cell.c);
+            dx -= lj.x;
+            dy -= lj.y;
+            dz -= lj.z;
+            wd = make_int3(wd.x - int(jx), wd.y - int(jy), wd.z - int(jz));
+        }
+        s_w[i] = w;
+        s_wd[i] = wd;
+        a.wrapped[3 * g] = w.x;
+        a.wrapped[3 * g + 1] = w.y;
+        a.wrapped[3 * g + 2] = w.z;
+        a.wrap_delta[3 * g] = wd.x;
+        a.wrap_delta[3 * g + 1] = wd.y;
+        a.wrap_delta[3 * g + 2] = wd.z;
+        const float d = sqrtf((dx * dx + dy * dy) + dz * dz);
+        if (!(d == d) || !isfinite(p.x) || !isfinite(p.y) || !isfinite(p.z)) nonfinite = true;
+        my_max = fmaxf(my_max, d);
+    }
+    // block max of the displacement (NaN-safe: nonfinite is flagged separately)
+    for (int m = 16; m > 0; m >>= 1) my_max = fmaxf(my_max, __shfl_xor_sync(0xffffffffu, my_max, m));
+    if ((threadIdx.x & 31) == 0) s_max[threadIdx.x >> 5] = my_max;
+    if (nonfinite) raise_flag(a.flags, FMD_FLAG_NONFINITE);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float m = 0.f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, s_max[w]);
+        a.max_disp[sys] = m;
+        if (!(m * 2.0f <= a.skin_limit)) raise_flag(a.flags, FMD_FLAG_SKIN);
+    }
+    // counts: one warp per centre
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = warp; i < n; i += kRefWarps) {
+        const int64_t g = base + i;
+        const int cnt = min(a.cand_count[g], a.bmax);
+        const float3 p = s_w[i];
+        const int3 wdi = s_wd[i];
+        int edges = 0;
+        for (int k0 = 0; k0 < cnt; k0 += 32) {
+            const int k = k0 + lane;
+            bool hit = false;
+            if (k < cnt) {
+                int64_t j = int64_t(a.cand_nbr[g * a.bmax + k]) - base;
+                j = j < 0 ? 0 : (j >= n ? n - 1 : j);
+                const int3 s = ld3i(a.cand_shift, g * a.bmax + k);
+                const int3 wdj = s_wd[j];
+                const float sx = float(s.x + wdj.x - wdi.x), sy = float(s.y + wdj.y - wdi.y),
+                            sz = float(s.z + wdj.z - wdi.z);
+                hit = refilter_dist2(p, s_w[j], sx, sy, sz, a.cell.c) < a.cutoff2;
+            }
+            edges += __popc(__ballot_sync(0xffffffffu, hit));
+        }
+        if (lane == 0) a.counts[g] = edges;
+    }
+    __syncthreads();
+    // per-system exclusive scan of the counts
+    int running = 0;
+    for (int i0 = 0; i0 < n; i0 += blockDim.x) {
+        const int i = i0 + threadIdx.x;
+        const int v = i < n ? a.counts[base + i] : 0;
+        int chunk_total;
+        const int ex = block_scan_exclusive(v, s_scan, chunk_total);
+        if (i < n) a.local_off[base + i] = running + ex;
+        running += chunk_total;
+    }
+    if (threadIdx.x == 0) a.sys_total[sys] = running;
+}
+
+// Materialize kernel: one CTA per system.
+__global__ void __launch_bounds__(kRefThreads) refilter_materialize_kernel(RefilterArgs a) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    float3* s_w = reinterpret_cast<float3*>(smem_raw);
+    int3* s_wd = reinterpret_cast<int3*>(s_w + a.n_atoms);
+    int32_t* s_cursor = reinterpret_cast<int32_t*>(s_wd + a.n_atoms);      // sender cursors [n]
+    int32_t* s_soff = s_cursor + a.n_atoms;                                // sender offsets [n + 1]
+    __shared__ int s_scan[32];
+    __shared__ long long s_base, s_grand;
+    const int64_t sys = blockIdx.x;
+    const int64_t base = sys * a.n_atoms;
+    const int n = int(a.n_atoms);
+    if (threadIdx.x == 0) {
+        long long b = 0, g = 0;
+        for (int r = 0; r < a.n_systems; ++r) {
+            const int t = a.sys_total[r];
+            if (r < sys) b += t;
+            g += t;
+        }
+        s_base = b;
+        s_grand = g;
+    }
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int64_t g = base + i;
+        s_w[i] = ld3(a.wrapped, g);
+        s_wd[i] = ld3i(a.wrap_delta, g);
+        s_cursor[i] = 0;
+    }
+    __syncthreads();
+    const int64_t sys_base = s_base;
+    const int64_t grand = s_grand;
+    const int64_t cap = a.e_cap;
+    // receiver CSR over the real edges (global), clipped to the capacity
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int64_t o = sys_base + a.local_off[base + i];
+        a.recv_off[base + i] = o < cap ? o : cap;
+    }
+    if (sys == a.n_systems - 1 && threadIdx.x == 0) {
+        a.recv_off[int64_t(a.n_systems) * a.n_atoms] = grand < cap ? grand : cap;
+        a.n_edges[0] = grand;
+        if (grand > cap) raise_flag(a.flags, FMD_FLAG_EDGE_OVERFLOW);
+    }
+    // edges: warp per centre, ballot compaction in candidate (= canonical) order
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = warp; i < n; i += kRefWarps) {
+        const int64_t g = base + i;
+        const int cnt = min(a.cand_count[g], a.bmax);
+        const float3 p = s_w[i];
+        const int3 wdi = s_wd[i];
+        int64_t out = sys_base + a.local_off[g];
+        for (int k0 = 0; k0 < cnt; k0 += 32) {
+            const int k = k0 + lane;
+            bool hit = false;
+            int j = 0;
+            int3 img = make_int3(0, 0, 0);
+            if (k < cnt) {
+                int64_t jj = int64_t(a.cand_nbr[g * a.bmax + k]) - base;
+                j = int(jj < 0 ? 0 : (jj >= n ? n - 1 : jj));
+                const int3 s = ld3i(a.cand_shift, g * a.bmax + k);
+                const int3 wdj = s_wd[j];
+                img = make_int3(s.x + wdj.x - wdi.x, s.y + wdj.y - wdi.y, s.z + wdj.z - wdi.z);
+                hit = refilter_dist2(p, s_w[j], float(img.x), float(img.y), float(img.z), a.cell.c) < a.cutoff2;
+            }
+            const unsigned mask = __ballot_sync(0xffffffffu, hit);
+            if (hit) {
+                const int64_t e = out + __popc(mask & ((1u << lane) - 1u));
+                if (e < cap) {
+                    a.edge_index[2 * e] = int32_t(g);
+                    a.edge_index[2 * e + 1] = int32_t(base + j);
+                    a.edge_image[3 * e] = float(img.x);
+                    a.edge_image[3 * e + 1] = float(img.y);
+                    a.edge_image[3 * e + 2] = float(img.z);
+                    atomicAdd(s_cursor + j, 1);  // sender count
+                }
+            }
+            out += __popc(mask);
+        }
+    }
+    __syncthreads();
+    // sender CSR of this system: counts -> exclusive scan -> fill -> sort runs
+    int running = 0;
+    for (int i0 = 0; i0 < n; i0 += blockDim.x) {
+        const int i = i0 + threadIdx.x;
+        const int v = i < n ? s_cursor[i] : 0;
+        int chunk_total;
+        const int ex = block_scan_exclusive(v, s_scan, chunk_total);
+        if (i < n) s_soff[i] = running + ex;
+        running += chunk_total;
+    }
+    if (threadIdx.x == 0) s_soff[n] = running;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int64_t o = sys_base + s_soff[i];
+        a.send_off[base + i] = o < cap ? o : cap;
+        s_cursor[i] = 0;
+    }
+    if (sys == a.n_systems - 1 && threadIdx.x == 0)
+        a.send_off[int64_t(a.n_systems) * a.n_atoms] = grand < cap ? grand : cap;
+    __syncthreads();
+    const int64_t sys_edges = a.sys_total[sys];
+    for (int64_t t = threadIdx.x; t < sys_edges; t += blockDim.x) {
+        const int64_t e = sys_base + t;
+        if (e >= cap) break;
+        const int j = int(int64_t(a.edge_index[2 * e + 1]) - base);
+        const int slot = atomicAdd(s_cursor + j, 1);
+        const int64_t dst = sys_base + s_soff[j] + slot;
+        if (dst < cap) a.send_perm[dst] = int32_t(e);
+    }
+    __syncthreads();
+    // each sender run ascending by edge id (rank sort, warp per sender)
+    for (int j = warp; j < n; j += kRefWarps) {
+        const int64_t b = sys_base + s_soff[j];
+        const int len = s_soff[j + 1] - s_soff[j];
+        if (len <= 1 || b + len > cap) continue;
+        int vals[8];
+        int nv = 0;
+        for (int k = lane; k < len && nv < 8; k += 32) vals[nv++] = a.send_perm[b + k];
+        __syncwarp();
+        int ranks[8];
+        for (int v = 0; v < nv; ++v) {
+            int r = 0;
+            for (int f = 0; f < len; ++f) r += a.send_perm[b + f] < vals[v] ? 1 : 0;
+            ranks[v] = r;
+        }
+        __syncwarp();
+        for (int v = 0; v < nv; ++v) a.send_perm[b + ranks[v]] = vals[v];
+        if (len > 256 && lane == 0) raise_flag(a.flags, FMD_FLAG_CANDIDATE_OVERFLOW);
+        __syncwarp();
+    }
+    // padding rows [grand, cap): far self-loops round robin over the union's atoms
+    const int64_t total_atoms = int64_t(a.n_systems) * a.n_atoms;
+    const int64_t first = grand < cap ? grand : cap;
+    for (int64_t e = first + int64_t(sys) * blockDim.x + threadIdx.x; e < cap;
+         e += int64_t(a.n_systems) * blockDim.x) {
+        const int32_t atom = int32_t((e - first) % total_atoms);
+        a.edge_index[2 * e] = atom;
+        a.edge_index[2 * e + 1] = atom;
+        a.edge_image[3 * e] = float(a.pad_image[0]);
+        a.edge_image[3 * e + 1] = float(a.pad_image[1]);
+        a.edge_image[3 * e + 2] = float(a.pad_image[2]);
+    }
+}
+
+// ------------------------------------------------------------- ragged list
+
+// edges per centre with the ragged path's predicate (|diff| < rc)
+__global__ void ragged_count_kernel(const float4* __restrict__ wrapped, int64_t rows, Cell9 cell,
+                                    const int32_t* __restrict__ nbr, const int32_t* __restrict__ shift,
+                                    const int32_t* __restrict__ count, int32_t bmax, float cutoff,
+                                    int64_t* __restrict__ counts_out) {
+    const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    for (int64_t i = warp_global; i < rows; i += nwarps) {
+        const int cnt = min(count[i], bmax);
+        const float4 p4 = wrapped[i];
+        const float3 p = make_float3(p4.x, p4.y, p4.z);
+        int edges = 0;
+        for (int k0 = 0; k0 < cnt; k0 += 32) {
+            const int k = k0 + lane;
+            bool hit = false;
+            if (k < cnt) {
+                const int32_t j = nbr[i * bmax + k];
+                const float4 q4 = wrapped[j];
+                hit = ragged_dist(p, make_float3(q4.x, q4.y, q4.z), ld3i(shift, i * bmax + k), cell.c) < cutoff;
+            }
+            edges += __popc(__ballot_sync(0xffffffffu, hit));
+        }
+        if (lane == 0) counts_out[i] = edges;
+    }
+}
+
+__global__ void ragged_write_kernel(const float4* __restrict__ wrapped, int64_t rows, Cell9 cell,
+                                    const int32_t* __restrict__ nbr, const int32_t* __restrict__ shift,
+                                    const int32_t* __restrict__ count, int32_t bmax, float cutoff,
+                                    const int64_t* __restrict__ offsets, int64_t e_cap,
+                                    int64_t* __restrict__ center, int64_t* __restrict__ neighbor,
+                                    int32_t* __restrict__ images, float* __restrict__ dist) {
+    const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    for (int64_t i = warp_global; i < rows; i += nwarps) {
+        const int cnt = min(count[i], bmax);
+        const float4 p4 = wrapped[i];
+        const float3 p = make_float3(p4.x, p4.y, p4.z);
+        int64_t out = offsets[i];
+        for (int k0 = 0; k0 < cnt; k0 += 32) {
+            const int k = k0 + lane;
+            bool hit = false;
+            float d = 0.f;
+            int32_t j = 0;
+            int3 s = make_int3(0, 0, 0);
+            if (k < cnt) {
+                j = nbr[i * bmax + k];
+                s = ld3i(shift, i * bmax + k);
+                const float4 q4 = wrapped[j];
+                d = ragged_dist(p, make_float3(q4.x, q4.y, q4.z), s, cell.c);
+                hit = d < cutoff;
+            }
+            const unsigned mask = __ballot_sync(0xffffffffu, hit);
+            if (hit) {
+                const int64_t e = out + __popc(mask & ((1u << lane) - 1u));
+                if (e < e_cap) {
+                    center[e] = i;
+                    neighbor[e] = j;
+                    images[3 * e] = s.x;
+                    images[3 * e + 1] = s.y;
+                    images[3 * e + 2] = s.z;
+                    dist[e] = d;
+                }
+            }
+            out += __popc(mask);
+        }
+    }
+}
+
+__global__ void copy_wrapped_kernel(const float4* __restrict__ src, int64_t n, float* __restrict__ dst) {
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+        const float4 v = src[i];
+        dst[3 * i] = v.x;
+        dst[3 * i + 1] = v.y;
+        dst[3 * i + 2] = v.z;
+    }
+}
+
+// ------------------------------------------------------------------ host
+
+inline size_t align_up(size_t x) { return (x + 255) & ~size_t(255); }
+
+inline bool make_grid(const float* cell_host, double cutoff, Grid& g) {
+    double c[9];
+    for (int k = 0; k < 9; ++k) c[k] = cell_host[k];
+    const double cross[3][3] = {
+        {c[4] * c[8] - c[5] * c[7], c[5] * c[6] - c[3] * c[8], c[3] * c[7] - c[4] * c[6]},
+        {c[7] * c[2] - c[8] * c[1], c[8] * c[0] - c[6] * c[2], c[6] * c[1] - c[7] * c[0]},
+        {c[1] * c[5] - c[2] * c[4], c[2] * c[3] - c[0] * c[5], c[0] * c[4] - c[1] * c[3]},
+    };
+    const double vol = fabs(c[0] * cross[0][0] + c[1] * cross[0][1] + c[2] * cross[0][2]);
+    if (!(vol > 0) || !(cutoff > 0)) return false;
+    int64_t total = 1;
+    for (int k = 0; k < 3; ++k) {
+        const double area = sqrt(cross[k][0] * cross[k][0] + cross[k][1] * cross[k][1] + cross[k][2] * cross[k][2]);
+        const double h = vol / area;  // perpendicular height along axis k
+        int n = int(floor(h / cutoff));
+        if (n < 1) n = 1;
+        if (n > 256) n = 256;
+        g.n[k] = n;
+        g.s[k] = int(ceil(cutoff * n / h * (1.0 + 1e-6)));
+        if (g.s[k] > 5) return false;  // (2s+1)^3 <= kMaxOffsets neighbour (cell, image) pairs
+        total *= n;
+    }
+    g.ncells = int(total);
+    return true;
+}
+
+inline bool make_cell(const float* cell_host, Cell9& cell) {
+    double c[9];
+    for (int k = 0; k < 9; ++k) c[k] = cell_host[k];
+    const double det = c[0] * (c[4] * c[8] - c[5] * c[7]) - c[1] * (c[3] * c[8] - c[5] * c[6]) +
+                       c[2] * (c[3] * c[7] - c[4] * c[6]);
+    if (!(fabs(det) > 0)) return false;
+    const double inv[9] = {
+        (c[4] * c[8] - c[5] * c[7]) / det, (c[2] * c[7] - c[1] * c[8]) / det, (c[1] * c[5] - c[2] * c[4]) / det,
+        (c[5] * c[6] - c[3] * c[8]) / det, (c[0] * c[8] - c[2] * c[6]) / det, (c[2] * c[3] - c[0] * c[5]) / det,
+        (c[3] * c[7] - c[4] * c[6]) / det, (c[1] * c[6] - c[0] * c[7]) / det, (c[0] * c[4] - c[1] * c[3]) / det,
+    };
+    for (int k = 0; k < 9; ++k) {
+        cell.c[k] = cell_host[k];
+        cell.inv[k] = float(inv[k]);
+    }
+    return true;
+}
+
+struct CellWorkspace {
+    float4* wrapped;
+    int32_t* atom_cell;
+    int32_t* atom_slot;
+    int32_t* cell_count;   // [R*ncells + 1]
+    int32_t* cell_start;   // [R*ncells + 1]
+    int32_t* cell_atoms;
+    float4* cell_pos;
+    void* scan_temp;
+    size_t scan_bytes;
+};
+
+inline size_t scan_temp_bytes(int64_t items) {
+    size_t bytes = 0;
+    cub::DeviceScan::ExclusiveSum(nullptr, bytes, (const int32_t*)nullptr, (int32_t*)nullptr, int(items));
+    return bytes;
+}
+
+inline size_t cell_workspace_bytes(int64_t atoms, int64_t cells) {
+    return align_up(sizeof(float4) * atoms) + 2 * align_up(sizeof(int32_t) * atoms) +
+           2 * align_up(sizeof(int32_t) * (cells + 1)) + align_up(sizeof(int32_t) * atoms) +
+           align_up(sizeof(float4) * atoms) + align_up(scan_temp_bytes(cells + 1));
+}
+
+inline CellWorkspace carve(void* ws, int64_t atoms, int64_t cells) {
+    CellWorkspace w{};
+    char* p = static_cast<char*>(ws);
+    w.wrapped = reinterpret_cast<float4*>(p); p += align_up(sizeof(float4) * atoms);
+    w.atom_cell = reinterpret_cast<int32_t*>(p); p += align_up(sizeof(int32_t) * atoms);
+    w.atom_slot = reinterpret_cast<int32_t*>(p); p += align_up(sizeof(int32_t) * atoms);
+    w.cell_count = reinterpret_cast<int32_t*>(p); p += align_up(sizeof(int32_t) * (cells + 1));
+    w.cell_start = reinterpret_cast<int32_t*>(p); p += align_up(sizeof(int32_t) * (cells + 1));
+    w.cell_atoms = reinterpret_cast<int32_t*>(p); p += align_up(sizeof(int32_t) * atoms);
+    w.cell_pos = reinterpret_cast<float4*>(p); p += align_up(sizeof(float4) * atoms);
+    w.scan_temp = p;
+    w.scan_bytes = scan_temp_bytes(cells + 1);
+    return w;
+}
+
+inline int list_cap_for(int32_t bmax) { return bmax < 32 ? 32 : (bmax > 1024 ? 1024 : bmax); }
+
+// bin + scan + scatter + query into a candidate matrix
+inline fmd_status run_cell_list(const float* positions, int64_t n_atoms, int32_t n_systems, const Cell9& cell,
+                                const Grid& grid, float cutoff, int32_t bmax, int32_t* nbr, int32_t* shift,
+                                int32_t* count, const CellWorkspace& w, int32_t* flags, cudaStream_t s) {
+    const int64_t atoms = n_atoms * n_systems;
+    const int64_t cells = int64_t(grid.ncells) * n_systems;
+    cudaError_t err = cudaMemsetAsync(w.cell_count, 0, sizeof(int32_t) * (cells + 1), s);
+    if (err != cudaSuccess) return record_cuda_error(err);
+    const int threads = 256;
+    cell_bin_kernel<<<grid_for(atoms, threads), threads, 0, s>>>(positions, n_atoms, n_systems, cell, grid,
+                                                                  w.wrapped, w.atom_cell, w.atom_slot,
+                                                                  w.cell_count, flags);
+    fmd_status st = check_launch();
+    if (st != FMD_OK) return st;
+    size_t bytes = w.scan_bytes;
+    err = cub::DeviceScan::ExclusiveSum(w.scan_temp, bytes, w.cell_count, w.cell_start, int(cells + 1), s);
+    if (err != cudaSuccess) return record_cuda_error(err);
+    cell_scatter_kernel<<<grid_for(atoms, threads), threads, 0, s>>>(atoms, w.wrapped, w.atom_cell, w.atom_slot,
+                                                                      w.cell_start, w.cell_atoms, w.cell_pos);
+    if ((st = check_launch()) != FMD_OK) return st;
+    QueryArgs q{};
+    q.cell_start = w.cell_start;
+    q.cell_atoms = w.cell_atoms;
+    q.cell_pos = w.cell_pos;
+    q.n_atoms = n_atoms;
+    q.n_systems = n_systems;
+    q.cell = cell;
+    q.grid = grid;
+    q.cutoff = cutoff;
+    q.bmax = bmax;
+    q.list_cap = list_cap_for(bmax);
+    q.nbr_out = nbr;
+    q.shift_out = shift;
+    q.count_out = count;
+    q.flags = flags;
+    const size_t smem = query_smem(q.list_cap);
+    if (smem > 227 * 1024) return FMD_ERR_UNSUPPORTED;
+    err = cudaFuncSetAttribute(cell_query_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (err != cudaSuccess) return record_cuda_error(err);
+    const int qgrid = int(cells < int64_t(kNumSMs) * 16 ? cells : int64_t(kNumSMs) * 16);
+    cell_query_kernel<<<qgrid, kQueryWarps * 32, smem, s>>>(q);
+    if ((st = check_launch()) != FMD_OK) return st;
+    cand_fill_kernel<<<grid_for(atoms * bmax, threads), threads, 0, s>>>(atoms, bmax, int32_t(atoms), nbr, shift,
+                                                                         count);
+    return check_launch();
+}
+
+}  // namespace fmd
+
+using namespace fmd;
+
+extern "C" {
+
+fmd_status fmd_cell_list_workspace_bytes(const float* cell_host, float cutoff, int64_t n_atoms,
+                                         int32_t n_systems, size_t* bytes) {
+    Grid g{};
+    if (cell_host == nullptr || bytes == nullptr || n_atoms < 1 || n_systems < 1 ||
+        !make_grid(cell_host, cutoff, g))
+        return FMD_ERR_INVALID_ARGUMENT;
+    *bytes = cell_workspace_bytes(n_atoms * n_systems, int64_t(g.ncells) * n_systems);
+    return FMD_OK;
+}
+
+fmd_status fmd_candidates_build(const float* positions, const float* cell_host, int64_t n_atoms,
+                                int32_t n_systems, float candidate_cutoff, int32_t bmax,
+                                int32_t* cand_nbr, int32_t* cand_shift, int32_t* cand_count,
+                                float* ref_positions, int32_t* ref_wraps, int32_t* wrap_delta,
+                                void* workspace, size_t workspace_bytes, int32_t* flags, void* stream) {
+    Cell9 cell{};
+    Grid grid{};
+    if (positions == nullptr || cand_nbr == nullptr || cand_shift == nullptr || cand_count == nullptr ||
+        n_atoms < 1 || n_systems < 1 || bmax < 1 || !make_cell(cell_host, cell) ||
+        !make_grid(cell_host, candidate_cutoff, grid) || int64_t(n_atoms) * n_systems >= (int64_t(1) << 31) ||
+        n_atoms >= (int64_t(1) << 33))
+        return FMD_ERR_INVALID_ARGUMENT;
+    const int64_t atoms = n_atoms * n_systems;
+    const int64_t cells = int64_t(grid.ncells) * n_systems;
+    if (workspace == nullptr || workspace_bytes < cell_workspace_bytes(atoms, cells)) return FMD_ERR_WORKSPACE;
+    cudaStream_t s = as_stream(stream);
+    const CellWorkspace w = carve(workspace, atoms, cells);
+    if (ref_positions != nullptr && ref_wraps != nullptr && wrap_delta != nullptr) {
+        refresh_reference_kernel<<<grid_for(atoms, 256), 256, 0, s>>>(positions, atoms, cell, ref_positions,
+                                                                       ref_wraps, wrap_delta);
+        fmd_status st = check_launch();
+        if (st != FMD_OK) return st;
+    }
+    return run_cell_list(positions, n_atoms, n_systems, cell, grid, candidate_cutoff, bmax, cand_nbr, cand_shift,
+                         cand_count, w, flags, s);
+}
+
+fmd_status fmd_refilter_workspace_bytes(int64_t n_atoms, int32_t n_systems, size_t* bytes) {
+    if (bytes == nullptr || n_atoms < 1 || n_systems < 1) return FMD_ERR_INVALID_ARGUMENT;
+    const int64_t atoms = n_atoms * n_systems;
+    *bytes = 2 * align_up(sizeof(int32_t) * atoms) + align_up(sizeof(int32_t) * n_systems);
+    return FMD_OK;
+}
+
+// largest system the single-CTA-per-system re-filter holds in shared memory
+static int64_t refilter_smem_bytes(int64_t n_atoms) {
+    return int64_t(sizeof(float3) + sizeof(int3) + 2 * sizeof(int32_t)) * n_atoms + 4;
+}
+
+fmd_status fmd_refilter_edges(const float* positions, const float* cell_host, int64_t n_atoms, int32_t n_systems,
+                              const float* ref_positions, const int32_t* ref_wraps, const int32_t* cand_nbr,
+                              const int32_t* cand_shift, const int32_t* cand_count, int32_t bmax, float cutoff,
+                              float skin, int64_t e_capacity, const int32_t* pad_image_host,
+                              int32_t minimum_image, float* wrapped, int32_t* wrap_delta, int32_t* edge_index, float* edge_image, int64_t* recv_off,
+                              int64_t* send_off, int32_t* send_perm, int64_t* n_edges, float* max_displacement,
+                              void* workspace, size_t workspace_bytes, int32_t* flags, void* stream) {
+    Cell9 cell{};
+    if (positions == nullptr || ref_positions == nullptr || ref_wraps == nullptr || cand_nbr == nullptr ||
+        cand_shift == nullptr || cand_count == nullptr || wrapped == nullptr || wrap_delta == nullptr ||
+        edge_index == nullptr || edge_image == nullptr || recv_off == nullptr || send_off == nullptr ||
+        send_perm == nullptr || n_edges == nullptr || max_displacement == nullptr || flags == nullptr ||
+        n_atoms < 1 || n_systems < 1 || bmax < 1 || e_capacity < 0 || !make_cell(cell_host, cell) ||
+        int64_t(n_atoms) * n_systems >= (int64_t(1) << 31) || e_capacity >= (int64_t(1) << 31))
+        return FMD_ERR_INVALID_ARGUMENT;
+    const int64_t smem = refilter_smem_bytes(n_atoms);
+    if (smem > 200 * 1024) return FMD_ERR_UNSUPPORTED;  // per-system atoms beyond shared memory
+    size_t need = 0;
+    fmd_refilter_workspace_bytes(n_atoms, n_systems, &need);
+    if (workspace == nullptr || workspace_bytes < need) return FMD_ERR_WORKSPACE;
+    const int64_t atoms = n_atoms * n_systems;
+    char* ws = static_cast<char*>(workspace);
+    RefilterArgs a{};
+    a.positions = positions;
+    a.cell = cell;
+    a.ref_pos = ref_positions;
+    a.ref_wraps = ref_wraps;
+    a.cand_nbr = cand_nbr;
+    a.cand_shift = cand_shift;
+    a.cand_count = cand_count;
+    a.n_atoms = n_atoms;
+    a.n_systems = n_systems;
+    a.bmax = bmax;
+    a.cutoff2 = cutoff * cutoff;
+    a.skin_limit = skin + 1.0e-6f;
+    a.minimum_image = minimum_image;
+    a.e_cap = e_capacity;
+    for (int k = 0; k < 3; ++k) a.pad_image[k] = pad_image_host ? pad_image_host[k] : 0;
+    a.wrapped = wrapped;
+    a.wrap_delta = wrap_delta;
+    a.counts = reinterpret_cast<int32_t*>(ws); ws += align_up(sizeof(int32_t) * atoms);
+    a.local_off = reinterpret_cast<int32_t*>(ws); ws += align_up(sizeof(int32_t) * atoms);
+    a.sys_total = reinterpret_cast<int32_t*>(ws);
+    a.max_disp = max_displacement;
+    a.edge_index = edge_index;
+    a.edge_image = edge_image;
+    a.recv_off = recv_off;
+    a.send_off = send_off;
+    a.send_perm = send_perm;
+    a.n_edges = n_edges;
+    a.flags = flags;
+    cudaStream_t s = as_stream(stream);
+    const size_t smem_count = (sizeof(float3) + sizeof(int3)) * size_t(n_atoms);
+    const size_t smem_mat = size_t(smem);
+    cudaError_t err = cudaFuncSetAttribute(refilter_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           int(smem_count));
+    if (err != cudaSuccess) return record_cuda_error(err);
+    err = cudaFuncSetAttribute(refilter_materialize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               int(smem_mat));
+    if (err != cudaSuccess) return record_cuda_error(err);
+    refilter_count_kernel<<<n_systems, kRefThreads, smem_count, s>>>(a);
+    fmd_status st = check_launch();
+    if (st != FMD_OK) return st;
+    refilter_materialize_kernel<<<n_systems, kRefThreads, smem_mat, s>>>(a);
+    return check_launch();
+}
+
+static size_t ragged_scan_bytes(int64_t n_atoms) {
+    size_t cub_bytes = 0;
+    cub::DeviceScan::ExclusiveSum(nullptr, cub_bytes, (const int64_t*)nullptr, (int64_t*)nullptr, int(n_atoms + 1));
+    return cub_bytes;
+}
+
+fmd_status fmd_neighbor_list_workspace_bytes(const float* cell_host, float cutoff, int64_t n_atoms,
+                                             int32_t bmax, size_t* bytes) {
+    Grid g{};
+    if (cell_host == nullptr || bytes == nullptr || n_atoms < 1 || bmax < 1 ||
+        !make_grid(cell_host, cutoff + 1e-6f, g))
+        return FMD_ERR_INVALID_ARGUMENT;
+    *bytes = cell_workspace_bytes(n_atoms, g.ncells) + align_up(sizeof(int32_t) * size_t(n_atoms) * bmax) +
+             align_up(sizeof(int32_t) * size_t(n_atoms) * bmax * 3) + align_up(sizeof(int32_t) * n_atoms) +
+             align_up(sizeof(int64_t) * (n_atoms + 1)) + align_up(ragged_scan_bytes(n_atoms));
+    return FMD_OK;
+}
+
+fmd_status fmd_neighbor_list(const float* positions, const float* cell_host, int64_t n_atoms, float cutoff,
+                             int32_t bmax, int64_t e_capacity, float* wrapped, int64_t* center, int64_t* neighbor,
+                             int32_t* images, float* dist, int64_t* offsets, void* workspace,
+                             size_t workspace_bytes, int32_t* flags, void* stream) {
+    Cell9 cell{};
+    Grid grid{};
+    const float cand_cut = cutoff + 1e-6f;  // candidates at rc + 1e-6 (gpu_graph_builder.py:161)
+    if (positions == nullptr || center == nullptr || neighbor == nullptr || images == nullptr ||
+        dist == nullptr || offsets == nullptr || n_atoms < 1 || bmax < 1 || e_capacity < 0 ||
+        !make_cell(cell_host, cell) || !make_grid(cell_host, cand_cut, grid) || n_atoms >= (int64_t(1) << 31))
+        return FMD_ERR_INVALID_ARGUMENT;
+    size_t need = 0;
+    if (fmd_neighbor_list_workspace_bytes(cell_host, cutoff, n_atoms, bmax, &need) != FMD_OK)
+        return FMD_ERR_INVALID_ARGUMENT;
+    if (workspace == nullptr || workspace_bytes < need) return FMD_ERR_WORKSPACE;
+    cudaStream_t s = as_stream(stream);
+    char* p = static_cast<char*>(workspace);
+    const CellWorkspace w = carve(p, n_atoms, grid.ncells);
+    p += cell_workspace_bytes(n_atoms, grid.ncells);
+    int32_t* nbr = reinterpret_cast<int32_t*>(p); p += align_up(sizeof(int32_t) * size_t(n_atoms) * bmax);
+    int32_t* shift = reinterpret_cast<int32_t*>(p); p += align_up(sizeof(int32_t) * size_t(n_atoms) * bmax * 3);
+    int32_t* count = reinterpret_cast<int32_t*>(p); p += align_up(sizeof(int32_t) * n_atoms);
+    int64_t* counts64 = reinterpret_cast<int64_t*>(p); p += align_up(sizeof(int64_t) * (n_atoms + 1));
+    void* cub_temp = p;
+    size_t cub_bytes = ragged_scan_bytes(n_atoms);
+    fmd_status st = run_cell_list(positions, n_atoms, 1, cell, grid, cand_cut, bmax, nbr, shift, count, w,
+                                  flags, s);
+    if (st != FMD_OK) return st;
+    const int threads = 256;
+    ragged_count_kernel<<<grid_for(n_atoms * 32, threads), threads, 0, s>>>(w.wrapped, n_atoms, cell, nbr, shift,
+                                                                            count, bmax, cutoff, counts64);
+    if ((st = check_launch()) != FMD_OK) return st;
+    cudaError_t err = cudaMemsetAsync(counts64 + n_atoms, 0, sizeof(int64_t), s);
+    if (err != cudaSuccess) return record_cuda_error(err);
+    err = cub::DeviceScan::ExclusiveSum(cub_temp, cub_bytes, counts64, offsets, int(n_atoms + 1), s);
+    if (err != cudaSuccess) return record_cuda_error(err);
+    ragged_write_kernel<<<grid_for(n_atoms * 32, threads), threads, 0, s>>>(
+        w.wrapped, n_atoms, cell, nbr, shift, count, bmax, cutoff, offsets, e_capacity, center, neighbor, images,
+        dist);
+    if ((st = check_launch()) != FMD_OK) return st;
+    if (wrapped != nullptr) {
+        copy_wrapped_kernel<<<grid_for(n_atoms, threads), threads, 0, s>>>(w.wrapped, n_atoms, wrapped);
+        if ((st = check_launch()) != FMD_OK) return st;
+    }
+    return FMD_OK;
+}
+
+}  // extern "C"

@@ -147,6 +147,171 @@ FMD_API fmd_status fmd_csr_segment_sum_bwd(const float* gout, const float* value
                                    int64_t skip_segment, float* gvalue, float* gweight,
                                    int32_t* flags, void* stream);
 
+/* ------------------------------------------------- neighbour lists (A1-A3) */
+
+/* R systems of n atoms share one cell (`cell_host`: 9 floats, row-major
+ * lattice vectors, HOST memory); row r*n + a is atom a of system r and no
+ * pair crosses systems (the disjoint-union graph of
+ * fastmd/execution/replica_batch.py:126). Positions are float32 [R*n, 3]. */
+
+/* Workspace of fmd_candidates_build for this cell, cutoff and size. */
+FMD_API fmd_status fmd_cell_list_workspace_bytes(const float* cell_host, float cutoff, int64_t n_atoms,
+                                                 int32_t n_systems, size_t* bytes);
+
+/* Skin candidate list (full, both directions) within `candidate_cutoff` of
+ * the wrapped positions, by a cell list: cand_nbr [R*n, bmax] (global rows,
+ * unused slots = R*n), cand_shift [R*n, bmax, 3] integer images,
+ * cand_count [R*n] (the true count; > bmax raises
+ * FMD_FLAG_CANDIDATE_OVERFLOW). Each row is in canonical (neighbour, image)
+ * order. When ref_positions/ref_wraps/wrap_delta are given, the refresh
+ * snapshot is taken too (positions, their wraps; wrap delta zeroed).
+ * Replaces FixedCapacityGraphBuilder.refresh_candidates
+ * (fastmd/graph/fixed_capacity_builder.py:1675, :1519) over nvalchemiops'
+ * batch_build_cell_list / batch_query_cell_list (neighbor_list_backend.py:134-154). */
+FMD_API fmd_status fmd_candidates_build(const float* positions, const float* cell_host, int64_t n_atoms,
+                                        int32_t n_systems, float candidate_cutoff, int32_t bmax,
+                                        int32_t* cand_nbr, int32_t* cand_shift, int32_t* cand_count,
+                                        float* ref_positions, int32_t* ref_wraps, int32_t* wrap_delta,
+                                        void* workspace, size_t workspace_bytes, int32_t* flags, void* stream);
+
+/* Workspace of fmd_refilter_edges. */
+FMD_API fmd_status fmd_refilter_workspace_bytes(int64_t n_atoms, int32_t n_systems, size_t* bytes);
+
+/* Per-step exact edges from the candidates (capture-safe, 2 kernels, one CTA
+ * per system): wraps the positions (wrapped [R*n,3], wrap_delta since the
+ * refresh), tests the skin (max_displacement [R]; 2*max > skin + 1e-6 raises
+ * FMD_FLAG_SKIN), keeps the candidates with float32
+ * dist2 = dx*dx+dy*dy+dz*dz < cutoff^2 in the reference's operation order,
+ * and writes edge_index [e_capacity, 2] int32 (centre, neighbour),
+ * edge_image [e_capacity, 3] float32 in canonical order (no sort), rows past
+ * the real edges padded with far self-loops (pad_image_host, 3 ints, HOST),
+ * minimum_image = 1: a lattice jump of the caller's coordinates since the
+ * refresh is no motion (the skin test takes the minimum-image displacement),
+ * n_edges [1] int64 (> e_capacity raises FMD_FLAG_EDGE_OVERFLOW), the
+ * receiver CSR recv_off [R*n + 1] and the sender CSR send_off [R*n + 1] /
+ * send_perm [e_capacity] (edge ids, each run ascending). Replaces
+ * FixedCapacityGraphBuilder.build(rebuild_candidates=False)
+ * (fixed_capacity_builder.py:2181: _count_neighbors_kernel :98,
+ * _materialize_neighbors_kernel :189, _pad_self_loops_kernel :324,
+ * _sort_edges :1968). At most 8192 atoms per system. */
+FMD_API fmd_status fmd_refilter_edges(const float* positions, const float* cell_host, int64_t n_atoms,
+                                      int32_t n_systems, const float* ref_positions, const int32_t* ref_wraps,
+                                      const int32_t* cand_nbr, const int32_t* cand_shift,
+                                      const int32_t* cand_count, int32_t bmax, float cutoff, float skin,
+                                      int64_t e_capacity, const int32_t* pad_image_host,
+                                      int32_t minimum_image, float* wrapped,
+                                      int32_t* wrap_delta, int32_t* edge_index, float* edge_image,
+                                      int64_t* recv_off, int64_t* send_off, int32_t* send_perm, int64_t* n_edges,
+                                      float* max_displacement, void* workspace, size_t workspace_bytes,
+                                      int32_t* flags, void* stream);
+
+/* Workspace of fmd_neighbor_list. */
+FMD_API fmd_status fmd_neighbor_list_workspace_bytes(const float* cell_host, float cutoff, int64_t n_atoms,
+                                                     int32_t bmax, size_t* bytes);
+
+/* Ragged full neighbour list of one system (eager path): candidates at
+ * cutoff + 1e-6 by the cell list, kept when |(q - p) + image @ cell| < cutoff
+ * (float32), rows in canonical (centre, neighbour, image) order: center,
+ * neighbor int64 [e_capacity], images int32 [e_capacity, 3], dist float32,
+ * offsets int64 [n + 1] (edges per centre; offsets[n] = edge count, rows past
+ * e_capacity are not written). wrapped (optional) receives the wrapped
+ * positions. More than bmax candidates of an atom raises
+ * FMD_FLAG_CANDIDATE_OVERFLOW (grow bmax and rerun). Replaces
+ * neighbor_list_nvidia (fastmd/graph/gpu_graph_builder.py:108). */
+FMD_API fmd_status fmd_neighbor_list(const float* positions, const float* cell_host, int64_t n_atoms,
+                                     float cutoff, int32_t bmax, int64_t e_capacity, float* wrapped,
+                                     int64_t* center, int64_t* neighbor, int32_t* images, float* dist,
+                                     int64_t* offsets, void* workspace, size_t workspace_bytes,
+                                     int32_t* flags, void* stream);
+
+/* ------------------------------------------- dense layers (D2), IEEE FP32 */
+
+/* y[m, n] (=|+=) act(a'[m, :] . op(w) + bias) on the CUDA cores, IEEE FP32,
+ * one sequential FMA chain over k per output (deterministic).
+ * op(w) = w^T for w [n, k] (trans_w = 1, the nn.Linear layout), w for w [k, n];
+ * a' = a, or a * silu'(a_pre) when a_pre is given (the SiLU backward of the
+ * previous layer fused into the operand load); act 0 = identity, 1 = SiLU
+ * (y_pre, when given, receives the pre-activation). The TF32-off parity
+ * path of the wide projections of fastmd/engine/kernels/triton_wide_gemm.py:482
+ * (linear) and :534 (matmul), where the reference runs cuBLAS FP32. */
+FMD_API fmd_status fmd_gemm_f32(const float* a, int64_t lda, const float* a_pre, int64_t lda_pre,
+                                const float* w, int64_t ldw, int32_t trans_w, const float* bias, float* y,
+                                int64_t ldy, float* y_pre, int64_t ldy_pre, int64_t m, int32_t n, int32_t k,
+                                int32_t act, int32_t accumulate, void* stream);
+
+/* ------------------------- MACE-architecture message passing (D1, D3, E2) */
+
+/* The message-passing backbone of the MACE-architecture potential behind
+ * fastmd/models/mace.py:356 (MACEAdapter.node_energy, upstream mace-torch
+ * 0.3.16 ScaleShiftMACE): channels C (multiple of 32), hidden irreps
+ * C x 0e + C x 1o, spherical harmonics l <= 1, correlation 3. Scalars are
+ * [N, C], vectors [N, 3, C]; edges follow fmd_refilter_edges (edge_index,
+ * edge_image, receiver CSR recv_off, sender CSR send_off/send_perm). */
+
+/* Per edge e = (centre i <- neighbour j): r = pos[j] - pos[i] + image @ cell,
+ * d = |r|; ysh [E, 4] = (sqrt(3) r/d, d) (16-byte aligned), phi [E, n_basis]
+ * = sqrt(2/r_max) sin(n pi d / r_max) / d * f_cut(d / r_max) with the
+ * polynomial cutoff of exponent poly_p (exactly 0 at d >= r_max). `cell` is
+ * a DEVICE [3, 3] float32. The radial basis of the reference
+ * (fastmd/models/matris/basis_function.py:139 BesselExpansion) in MACE's form. */
+FMD_API fmd_status fmd_mace_edge_geometry(const float* positions, const float* cell, const int32_t* edge_index,
+                                          const float* edge_image, int64_t n_edges, float r_max, int32_t n_basis,
+                                          int32_t poly_p, float* ysh, float* phi, void* stream);
+
+/* Backward of the edge geometry to the positions (the force chain, dE/dr):
+ * grad_positions[a] (=|+=) scale * (sum over edges sent by a of g_r(e) - sum
+ * over edges received by a of g_r(e)), through both CSRs (no atomics);
+ * scale = -1 gives the forces. */
+FMD_API fmd_status fmd_mace_edge_geometry_bwd(const float* ysh, const float* grad_y, const float* grad_phi,
+                                              float r_max, int32_t n_basis, int32_t poly_p,
+                                              const int32_t* edge_index, const int64_t* recv_off,
+                                              const int64_t* send_off, const int32_t* send_perm, int64_t n_atoms,
+                                              float* grad_positions, float scale, int32_t accumulate,
+                                              void* stream);
+
+/* Fused gather -> channel-wise tensor-product message -> receiver segment sum:
+ * A0[i] = inv_avg * sum_e (R0 s_t[j] + R3 (v_t[j].Y)/sqrt3),
+ * A1[i] = inv_avg * sum_e (R1 s_t[j] Y + R2 v_t[j]) over the receiver run of i
+ * (n_paths 2: layer without vector input, R [E, 2C]; 4: R [E, 4C]). */
+FMD_API fmd_status fmd_mace_message(const float* R, int32_t n_paths, const float* s_t, const float* v_t,
+                                    const float* ysh, const int32_t* edge_index, const int64_t* recv_off,
+                                    int64_t n_atoms, int32_t channels, float inv_avg, float* A0, float* A1,
+                                    void* stream);
+
+/* Backward of fmd_mace_message: dR [E, P*C], dY [E, 3] (=|+= by accumulate_dy;
+ * per receiver run) and ds_t [N, C], dv_t [N, 3, C] (per sender run), deterministic. */
+FMD_API fmd_status fmd_mace_message_bwd(const float* dA0, const float* dA1, const float* R, int32_t n_paths,
+                                        const float* s_t, const float* v_t, const float* ysh,
+                                        const int32_t* edge_index, const int64_t* recv_off,
+                                        const int64_t* send_off, const int32_t* send_perm, int64_t n_atoms,
+                                        int32_t channels, float inv_avg, float* dR, float* dY,
+                                        int32_t accumulate_dy, float* ds_t, float* dv_t, void* stream);
+
+/* Symmetric contraction, correlation 3, l <= 1, element weights W0 [Z, 5, C]
+ * (and W1 [Z, 4, C] for the vector output, NULL on the last layer). */
+FMD_API fmd_status fmd_mace_product(const float* A0, const float* A1, const int32_t* elem, const float* W0,
+                                    const float* W1, int64_t n_atoms, int32_t channels, float* B0, float* B1,
+                                    void* stream);
+FMD_API fmd_status fmd_mace_product_bwd(const float* dB0, const float* dB1, const float* A0, const float* A1,
+                                        const int32_t* elem, const float* W0, const float* W1, int64_t n_atoms,
+                                        int32_t channels, float* dA0, float* dA1, void* stream);
+
+/* Element-dependent linear map (MACE's skip connection): y[r] (=|+=) x[r] @ W[z]
+ * with z = elem[r / rows_per_atom], W [Z, c_in, c_out] (transpose: x @ W[z]^T). */
+FMD_API fmd_status fmd_element_linear(const float* x, int64_t rows, int32_t rows_per_atom, const int32_t* elem,
+                                      const float* W, int32_t c_in, int32_t c_out, int32_t transpose, float* y,
+                                      int32_t accumulate, void* stream);
+
+/* Node energies E_i = e0[elem_i] + scale * sum_t e_terms[t, i] + shift (fp64) and
+ * the fp64 total of each of n_systems systems of n_atoms atoms (block tree). */
+FMD_API fmd_status fmd_mace_node_energy(const float* e_terms, int32_t n_terms, int64_t ld_terms,
+                                        const int32_t* elem, const double* e0, double scale, double shift,
+                                        int64_t n_atoms, int32_t n_systems, double* node_energy, double* total,
+                                        void* stream);
+/* d_term[i] = scale * d_total[system of i] (the energy terms' gradient). */
+FMD_API fmd_status fmd_mace_node_energy_bwd(const double* d_total, double scale, int64_t n_atoms,
+                                            int32_t n_systems, float* d_term, void* stream);
+
 /* -------------------------------------- Nose-Hoover chain integrator (F1/F3) */
 
 /* Flat fp64 state of R replicas of n atoms each and chain length M:

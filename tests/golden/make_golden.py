@@ -17,6 +17,8 @@ used) and runs, on CPU:
   ``_materialize_neighbors_kernel`` (fastmd/graph/fixed_capacity_builder.py:98/:189)
   on candidate lists of a dense search, followed by the reference's
   canonical sort key (fixed_capacity_builder.py:1978-1996);
+* the radial basis ``BesselExpansion`` + ``PolynomialEnvelope``
+  (fastmd/models/matris/basis_function.py:139, :31) at the MACE and MatRIS settings;
 * the torch backend of ``GPUNoseHooverChainNVT`` (fastmd/execution/gpu_nhc.py:709,
   ``backend="torch"``) with harmonic forces, and ``maxwell_boltzmann_momenta``
   (gpu_nhc.py:199).
@@ -269,6 +271,20 @@ def neighbor_cases(torch, fcb):
     return out
 
 
+def radial_cases(torch):
+    """The reference's radial basis (fastmd/models/matris/basis_function.py:139 BesselExpansion with the
+    PolynomialEnvelope of :31) at the MACE setting (8 functions, rc 6, p 5) and MatRIS's (7, 6, 8)."""
+    from fastmd.models.matris.basis_function import BesselExpansion
+
+    d = torch.linspace(0.35, 6.4, 977, dtype=torch.float32)
+    out = {"radial_d": d.numpy()}
+    for tag, (n, rc, p) in {"mace": (8, 6.0, 5), "matris": (7, 6.0, 8)}.items():
+        module = BesselExpansion(num_radial=n, cutoff=rc, envelope_exponent=p)
+        out[f"radial_{tag}"] = module(d).detach().numpy()
+        out[f"radial_{tag}_params"] = np.array([n, rc, p], dtype=np.float64)
+    return out
+
+
 def main(reference: str) -> None:
     os.environ["TRITON_INTERPRET"] = "1"
     _install_stubs()
@@ -289,6 +305,7 @@ def main(reference: str) -> None:
     np.savez_compressed(HERE / "segment_sum.npz", **segment_sum_cases(torch, cs))
     np.savez_compressed(HERE / "nhc.npz", **nhc_cases(torch, gpu_nhc))
     np.savez_compressed(HERE / "neighbors.npz", **neighbor_cases(torch, fcb))
+    np.savez_compressed(HERE / "radial.npz", **radial_cases(torch))
     for path in sorted(HERE.glob("*.npz")):
         print(path.name, path.stat().st_size)
 

@@ -1,0 +1,146 @@
+"""The MACE-architecture potential on the GPU kernels against the FP64 oracle (parity unpinned for
+the model itself: its oracle restates the published equations; the radial basis is pinned to the
+reference's BesselExpansion)."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+from oracle import mace as omace
+from oracle import neighbors as onb
+
+pytestmark = pytest.mark.gpu
+
+# the tolerance of the benchmark contract: per-step energies and forces within 1e-5 relative (fp32)
+REL = 1e-5
+
+
+def _system(seed=0):
+    from fastmd_b200.structures import perovskite
+
+    return perovskite(seed=seed)
+
+
+def _graph(pos, cell, numbers, cuda, replicas=1, u_capacity=4096):
+    from fastmd_b200.graph import FixedCapacityGraphBuilder
+
+    b = FixedCapacityGraphBuilder(cell=torch.tensor(cell, dtype=torch.float32), atomic_numbers=torch.tensor(numbers),
+                                  u_capacity=u_capacity * replicas, atom_graph_cutoff=6.0, candidate_cutoff=8.0,
+                                  device=cuda, replicas=replicas)
+    batch, status = b.build(torch.from_numpy(np.asarray(pos, np.float32)).to(cuda))
+    assert int(status.flags.item()) == 0
+    return b, batch
+
+
+def _oracle(model, batch, numbers, replicas=1):
+    n = int(batch.n_edges.item())
+    edges = batch.edge_index[:n].cpu().numpy()
+    images = batch.edge_image[:n].cpu().numpy().round()
+    return omace.energy_forces(model.weights_host, model.config, batch.positions.cpu().numpy().astype(np.float64),
+                               batch.cell.cpu().numpy(), np.tile(numbers, replicas), edges, images,
+                               n_systems=replicas)
+
+
+@pytest.mark.parametrize("tag", ["mace", "matris"])
+def test_radial_basis_kernel_matches_reference_module(cuda, tag):
+    from fastmd_b200._lib import call, ptr, stream
+
+    g = golden("radial")
+    n, rc, p = g[f"radial_{tag}_params"]
+    d = g["radial_d"]
+    E = d.size
+    pos = np.zeros((E + 1, 3), np.float32)
+    pos[1:, 0] = d
+    edge_index = np.stack([np.zeros(E), np.arange(1, E + 1)], 1).astype(np.int32)
+    t = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(cuda)  # noqa: E731
+    # every device buffer stays referenced until the kernel has run
+    cell, pos_t, edges_t, images_t = (t(np.eye(3, dtype=np.float32) * 50.0), t(pos), t(edge_index),
+                                      t(np.zeros((E, 3), np.float32)))
+    ysh = torch.empty(E, 4, device=cuda)
+    phi = torch.empty(E, int(n), device=cuda)
+    call("fmd_mace_edge_geometry", ptr(pos_t), ptr(cell), ptr(edges_t), ptr(images_t), E, float(rc), int(n), int(p),
+         ptr(ysh), ptr(phi), stream(cuda))
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(phi.cpu().numpy(), g[f"radial_{tag}"], rtol=2e-5, atol=2e-6)
+    assert torch.equal(ysh[:, 3].cpu(), torch.from_numpy(d))
+
+
+def _close(mine, ref, rel=REL):
+    scale = max(float(np.abs(ref).max()), 1e-12)
+    err = float(np.abs(np.asarray(mine, np.float64) - ref).max())
+    assert err <= rel * scale, (err, scale)
+
+
+def test_energy_forces_match_fp64_oracle(cuda):
+    from fastmd_b200.mace import MACEModel
+
+    pos, cell, numbers, _ = _system(0)
+    model = MACEModel(device=cuda)
+    _, batch = _graph(pos, cell, numbers, cuda)
+    energy, forces = model.energy_forces(batch)
+    E, F, node = _oracle(model, batch, numbers)
+    _close(energy.cpu().numpy(), E, 1e-7)
+    _close(model.buffers(batch.positions.shape[0], batch.edge_index.shape[0]).t["node_energy"].cpu().numpy(), node,
+           1e-6)
+    _close(forces.cpu().numpy(), F)
+    assert float(np.abs(F).max()) > 0.05  # the forces are not trivially small
+
+
+def test_energy_derivative_autograd_route_equals_explicit_backward(cuda):
+    from fastmd_b200.energy_derivative import EnergyDerivative
+    from fastmd_b200.mace import MACEModel
+
+    pos, cell, numbers, _ = _system(1)
+    model = MACEModel(device=cuda)
+    _, batch = _graph(pos, cell, numbers, cuda)
+    energy, forces = model.energy_forces(batch)
+    energy, forces = energy.clone(), forces.clone()
+    out = EnergyDerivative(model)(batch, batch, task="ef", n_real=batch.positions.shape[0])
+    assert torch.equal(out["e"], energy)
+    assert torch.equal(out["f"][0], forces)
+
+
+def test_small_channel_model_matches_oracle_and_is_deterministic(cuda):
+    from fastmd_b200.mace import MACEConfig, MACEModel
+
+    pos, cell, numbers, _ = _system(2)
+    model = MACEModel(MACEConfig(channels=32, num_interactions=3), device=cuda, seed=3)
+    _, batch = _graph(pos, cell, numbers, cuda)
+    e1, f1 = (x.clone() for x in model.energy_forces(batch))
+    e2, f2 = model.energy_forces(batch)
+    assert torch.equal(e1, e2) and torch.equal(f1, f2)
+    E, F, _ = _oracle(model, batch, numbers)
+    _close(e1.cpu().numpy(), E, 1e-7)
+    _close(f1.cpu().numpy(), F)
+
+
+def test_replica_union_energies_equal_single_systems(cuda):
+    from fastmd_b200.mace import MACEModel
+
+    R = 3
+    systems = [_system(seed) for seed in range(R)]
+    cell, numbers = systems[0][1], systems[0][2]
+    model = MACEModel(device=cuda)
+    _, batch = _graph(np.concatenate([s[0] for s in systems]), cell, numbers, cuda, replicas=R)
+    energy, forces = model.energy_forces(batch, n_systems=R)
+    energy, forces = energy.clone(), forces.clone()
+    N = numbers.size
+    for r, s in enumerate(systems):
+        _, single = _graph(s[0], cell, numbers, cuda)
+        e, f = model.energy_forces(single)
+        assert torch.equal(energy[r:r + 1], e)
+        assert torch.equal(forces[r * N:(r + 1) * N], f)
+
+
+def test_forces_sum_to_zero_and_translation_invariance(cuda):
+    from fastmd_b200.mace import MACEModel
+
+    pos, cell, numbers, _ = _system(4)
+    model = MACEModel(device=cuda)
+    _, batch = _graph(pos, cell, numbers, cuda)
+    e0, f0 = (x.clone() for x in model.energy_forces(batch))
+    assert float(f0.double().sum(0).abs().max()) < 1e-4
+    _, moved = _graph(pos + np.array([0.37, -1.1, 2.3]), cell, numbers, cuda)
+    e1, f1 = model.energy_forces(moved)
+    assert abs(float(e1 - e0)) < 1e-9 * abs(float(e0)) + 2e-4
+    _close(f1.cpu().numpy(), f0.cpu().numpy().astype(np.float64), 1e-4)

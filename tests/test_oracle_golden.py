@@ -113,3 +113,24 @@ def test_refilter_equals_dense_fp64_search_up_to_ties(tag):
     theirs = {key for key, d in dense.items() if d < rc}
     for key in mine ^ theirs:
         assert abs(dense[key] - rc) < 1e-5, key
+
+
+@pytest.mark.parametrize("tag", ["mace", "matris"])
+def test_radial_basis_oracle_matches_reference_module(tag):
+    import torch
+
+    from oracle import mace as omace
+
+    g = golden("radial")
+    n, rc, p = g[f"radial_{tag}_params"]
+    d = torch.as_tensor(g["radial_d"], dtype=torch.float64)
+    mine = omace.bessel_envelope(d, float(rc), int(n), float(p)).numpy()
+    np.testing.assert_allclose(mine, g[f"radial_{tag}"], rtol=2e-5, atol=2e-6)
+
+
+def test_neighbor_oracle_candidates_cover_the_dense_search():
+    g = golden("neighbors")
+    wrapped, cell = g["nbr_perov_wrapped"], g["nbr_perov_cell"]
+    nm, ns, nn = onb.candidates(wrapped, cell, 8.0)
+    assert int(nn.sum()) == int(g["nbr_perov_cand_count"].sum())
+    assert onb.estimate_max_neighbors(8.0, 0.35, 2.0) == 1504
