@@ -1,0 +1,358 @@
+"""Benchmark of the per-step MD hot path (BASELINE configs 1 and 4) -- prints ONE JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: the 135-atom ABX3 perovskite (3x3x3, a = 6.2 A, jitter N(0, 0.05 A),
+seed = replica index), Maxwell-Boltzmann momenta at 500 K, NVT Nose-Hoover
+chain (tchain 3, tloop 1, tdamp 25 fs, dt 0.25 fs), the MACE-architecture
+potential (128 channels, l <= 1, correlation 3, 2 interactions, 8 Bessel,
+r_max 6 A, 89 elements; random weights, seed 1; IEEE FP32), whole-step
+CUDA-graph mode. One MD step = NHC half -> exact neighbour re-filter ->
+model energy and forces -> NHC half. ``--replicas R`` runs R independent
+135-atom replicas per GPU as one disjoint-union graph (config 4 uses 64).
+
+Under torchrun (N > 1) every rank integrates its own replicas (seeds
+rank*R .. rank*R+R-1), no collective on the step path; the per-replica
+(E_pot, T) are all-gathered over NCCL once per window (the thermo log).
+
+``--impl reference``: the CPU restatement of the same path (oracle/md.py:
+dense neighbour search, FP64 model with autograd forces, NHC) timed on the
+host cores -- the reference's own CPU path cannot run here (mace-torch is
+not installed), so its restatement stands in.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "ms/MD-step at 135 atoms (1 B200); atom-steps/s per box at 1/2/4/8 B200"
+UNIT = "atom-steps/s"
+TEMPERATURE = 500.0
+
+
+def _args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=2000)
+    p.add_argument("--warmup", type=int, default=100)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--replicas", type=int, default=1, help="135-atom replicas per GPU")
+    p.add_argument("--steps-per-launch", type=int, default=10)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def _config(args, world):
+    return {"workload": "config1: 135-atom CsSnI3 3x3x3, MACE-arch 128ch L1 corr3 2 layers, NVT-NHC whole_step"
+                        + (f", {args.replicas} replicas per GPU (config 4 sharding)" if args.replicas > 1 else ""),
+            "atoms_per_replica": 135, "replicas_per_gpu": args.replicas, "replicas_total": args.replicas * world,
+            "dt_fs": 0.25, "temperature_K": TEMPERATURE, "tchain": 3, "tdamp_fs": 25.0,
+            "steps_per_launch": args.steps_per_launch, "parallelism": f"replicas x{world} (no step-path collective)",
+            "l2": "flushed (256 MB write) before every timed window; windows timed by CUDA events"}
+
+
+def _system(seed):
+    from fastmd_b200.structures import perovskite
+
+    return perovskite(seed=seed)
+
+
+def _reference(args):
+    """The CPU oracle path, rank 0 only, all host threads."""
+    import torch
+
+    from fastmd_b200.gpu_nhc import maxwell_boltzmann_momenta
+    from fastmd_b200.mace import MACEConfig, init_weights
+    from fastmd_b200 import units
+    from oracle.md import OracleMD
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return None
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cfg = MACEConfig()
+    weights = init_weights(cfg, 1)
+    pos, cell, numbers, masses = _system(0)
+    md = OracleMD(weights, cfg, pos, cell, numbers, masses, maxwell_boltzmann_momenta(masses, TEMPERATURE, 0),
+                  temperature_K=TEMPERATURE, timestep=0.25 * units.fs, tdamp=25 * units.fs)
+    for _ in range(max(args.warmup // 50, 1)):
+        md.step()
+    steps = max(min(args.steps // 20, 60), 3)  # a bounded sample of the workload (~0.2 s per CPU step)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        md.step()
+    elapsed = time.perf_counter() - t0
+    ms = 1e3 * elapsed / steps
+    value = 135 * steps / elapsed
+    return {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+            "steps": steps, "warmup": max(args.warmup // 50, 1), "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": _config(argparse.Namespace(**{**vars(args), "replicas": 1}), 1),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"{steps} MD steps of one 135-atom replica (oracle/md.py, FP64 torch on "
+                                       f"{threads} threads)"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+class _Clocks:
+    """nvidia-smi samples of this GPU during the timed region."""
+
+    def __init__(self, index: int):
+        self.proc = None
+        self.path = ROOT / "gpurun_out" / f"clocks_{index}.csv"
+        try:
+            self.path.parent.mkdir(exist_ok=True)
+            self.out = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={index}", "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,"
+                 "clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.out, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        self.out.close()
+        sm, smax, reasons = [], [], set()
+        names = ["active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names[1:], parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), float(data["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def _ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from fastmd_b200 import _lib, units
+    from fastmd_b200.mace import MACEModel
+    from fastmd_b200.whole_step import GPUResidentMolecularDynamics
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    R = args.replicas
+    systems = [_system(rank * R + r) for r in range(R)]
+    cell, numbers, masses = systems[0][1], systems[0][2], systems[0][3]
+    positions = np.concatenate([s[0] for s in systems])
+    model = MACEModel(device=device, seed=1)
+    S = math.gcd(args.steps, args.steps_per_launch) or 1
+    md = GPUResidentMolecularDynamics(model, positions=positions, cell=cell, atomic_numbers=numbers, masses=masses,
+                                      temperature_K=TEMPERATURE, timestep=0.25 * units.fs, tdamp=25 * units.fs,
+                                      replicas=R, steps_per_launch=S, device=device)
+    runner = md.runner
+    # kernels of one window (counted on an eager window; the graph replays the same launches)
+    snapshot = md.integrator.snapshot()
+    _lib.count_launches(True)
+    runner._window_body()
+    counted = _lib.count_launches(False)
+    md.integrator.load_snapshot(snapshot)
+    launches_per_window = sum(n * _lib.KERNELS_PER_CALL.get(name, 1) for name, n in counted.items())
+    thermo = torch.zeros(R, 2, dtype=torch.float64, device=device)
+    gathered = torch.zeros(world * R, 2, dtype=torch.float64, device=device)
+
+    def thermo_log():
+        if world > 1:
+            thermo[:, 0].copy_(md.integrator.state.energy)
+            thermo[:, 1].copy_(md.integrator.temperature().reshape(-1))
+            dist.all_gather_into_tensor(gathered, thermo)
+
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+    for _ in range(max(1, -(-args.warmup // S))):
+        runner.launch()
+        runner.settle()
+        thermo_log()
+    windows = args.steps // S
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(windows)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(windows)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = _Clocks(local)
+    t0 = time.perf_counter()
+    for w in range(windows):
+        flush.zero_()
+        starts[w].record()
+        runner.launch()
+        ends[w].record()
+        runner.settle()
+        thermo_log()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    device_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    total = torch.tensor([device_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(total, op=dist.ReduceOp.MAX)
+    device_ms = float(total[0])
+    ms_per_step = device_ms / (windows * S)
+    atoms = 135 * R * world
+    value = atoms * 1e3 / ms_per_step
+
+    # e2e: host state in, host state out, every window through the public API
+    pin = lambda t: torch.empty(t.shape, dtype=t.dtype).pin_memory()  # noqa: E731
+    integ = md.integrator
+    host_q, host_p = pin(integ.state.q), pin(integ.state.p)
+    host_q.copy_(integ.state.q)
+    host_p.copy_(integ.state.p)
+    out = {"positions": pin(integ.state.q), "momenta": pin(integ.state.p), "forces": pin(integ.state.f),
+           "energy": pin(integ.state.energy)}
+    e2e_windows = max(1, min(windows, 200))
+    md.step_host(host_q, host_p, out)
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    for _ in range(e2e_windows):
+        md.step_host(out["positions"], out["momenta"], out)
+    e2e_s = time.perf_counter() - t1
+    e2e_ms_step = 1e3 * e2e_s / (e2e_windows * S)
+    e2e_t = torch.tensor([e2e_ms_step], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    e2e_value = atoms * 1e3 / float(e2e_t[0])
+    h2d = (host_q.numel() + host_p.numel()) * 8 / S
+    d2h = sum(t.numel() * t.element_size() for t in out.values()) / S
+
+    roofline = _roofline(md, device) if rank == 0 else None
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = _cpu_baseline()
+    thermo_now = md.thermodynamics() if rank == 0 else None
+    if world > 1:
+        dist.barrier()
+        del runner
+        md.runner.graph = None
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+    return {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": windows * S,
+            "warmup": max(1, -(-args.warmup // S)) * S, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32 (NHC state f64)", "data": "synthetic",
+            "config": _config(args, world), "wall_s_timed": wall,
+            "e2e": {"value": e2e_value, "unit": UNIT, "ms_per_step": float(e2e_t[0]), "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "path": "GPUResidentMolecularDynamics.step_host: pinned host "
+                    "positions+momenta in, positions/momenta/forces/energy out, per window of "
+                    f"{S} steps"},
+            "gpu_launches": launches_per_window * windows, "launches_per_step": launches_per_window / S,
+            "roofline": roofline, "cpu_baseline": cpu, "clocks": clk,
+            "fallbacks": md.runner.fallbacks, "candidate_refreshes": md.runner.refreshes,
+            "final_temperature_K": float(thermo_now["temperature"][0]),
+            "final_conserved_eV": float(thermo_now["conserved_energy"][0])}
+
+
+def _roofline(md, device):
+    """The dominant kernel of the step (the radial-MLP output GEMM of layer 2, [E, 64] x [64, 512]),
+    timed alone with CUDA events on its stream, against the HBM roofline of its algorithmic bytes."""
+    import torch
+
+    from fastmd_b200.mace import _gemm
+
+    model = md.model
+    buf = next(iter(model._buffers.values()))
+    b, w = buf.t, model.w
+    E = buf.n_edges
+    a, wt, y = b["1.h3"], w["1.radial.3"], b["1.R"]
+    n, k = wt.shape
+    s = torch.cuda.current_stream(device)
+    for _ in range(20):
+        _gemm(a, wt, y, s=s.cuda_stream)
+    reps = 200
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(s)
+    for _ in range(reps):
+        _gemm(a, wt, y, s=s.cuda_stream)
+    end.record(s)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / reps
+    hbm, tf, kind = _peaks()
+    flops = 2.0 * E * n * k
+    bytes_ = 4.0 * (E * k + n * k + E * n)
+    achieved_gbs = bytes_ / (ms * 1e-3) / 1e9
+    return {"kernel": "sgemm_kernel (layer-2 radial MLP output, fmd_gemm_f32)", "bound": "hbm",
+            "achieved": achieved_gbs, "peak": hbm, "unit": "GB/s", "frac": achieved_gbs / hbm,
+            "peak_source": f"{kind} (MEASURED_PEAKS.json hbm_gbs)" if kind == "measured" else "fallback",
+            "traffic": None, "algorithmic_bytes_per_launch": bytes_, "flops_per_launch": flops,
+            "avg_launch_us": ms * 1e3, "achieved_tflops_fp32": flops / (ms * 1e-3) / 1e12,
+            "note": "latency-bound at 135 atoms: the step is ~50 tiny kernels; see profiles/"}
+
+
+def _cpu_baseline():
+    """The oracle MD on the host cores, a bounded sample (~10-20 s)."""
+    import torch
+
+    from fastmd_b200.gpu_nhc import maxwell_boltzmann_momenta
+    from fastmd_b200.mace import MACEConfig, init_weights
+    from fastmd_b200 import units
+    from oracle.md import OracleMD
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cfg = MACEConfig()
+    pos, cell, numbers, masses = _system(0)
+    md = OracleMD(init_weights(cfg, 1), cfg, pos, cell, numbers, masses,
+                  maxwell_boltzmann_momenta(masses, TEMPERATURE, 0), temperature_K=TEMPERATURE,
+                  timestep=0.25 * units.fs, tdamp=25 * units.fs)
+    md.step()
+    steps, t0 = 0, time.perf_counter()
+    while steps < 3 or (time.perf_counter() - t0 < 10.0 and steps < 200):
+        md.step()
+        steps += 1
+    elapsed = time.perf_counter() - t0
+    return {"value": 135 * steps / elapsed, "unit": UNIT, "cores": threads, "kind": "port",
+            "ms_per_step": 1e3 * elapsed / steps,
+            "sample": f"{steps} MD steps of one 135-atom replica (oracle/md.py: dense neighbour search, FP64 "
+                      f"MACE-arch forces with autograd, NHC) on {threads} threads"}
+
+
+def main():
+    args = _args()
+    result = _reference(args) if args.impl == "reference" else _ours(args)
+    if result is not None:
+        print(json.dumps(result), flush=True)
+
+
+if __name__ == "__main__":
+    main()

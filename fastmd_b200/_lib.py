@@ -106,7 +106,24 @@ def check(status: int, what: str) -> None:
         raise FastMDLibraryError(f"{what}: {text}" + (f" ({detail})" if detail else ""))
 
 
+# kernels each entry point launches (for the launch count of a step); the default is one
+KERNELS_PER_CALL = {"fmd_refilter_edges": 2, "fmd_mace_message_bwd": 2}
+_counting: dict | None = None
+
+
+def count_launches(enabled: bool = True) -> dict | None:
+    """Start (or stop and return) counting entry-point calls made through ``call``."""
+    global _counting
+    if enabled:
+        _counting = {}
+        return None
+    counted, _counting = _counting, None
+    return counted
+
+
 def call(name: str, *args) -> None:
+    if _counting is not None:
+        _counting[name] = _counting.get(name, 0) + 1
     check(getattr(lib(), name)(*args), name)
 
 

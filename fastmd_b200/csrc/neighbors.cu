@@ -779,6 +779,19 @@ __global__ void copy_wrapped_kernel(const float4* __restrict__ src, int64_t n, f
 
 inline size_t align_up(size_t x) { return (x + 255) & ~size_t(255); }
 
+// Largest dynamic shared memory granted so far per kernel (per process; one device per process).
+// The attribute is raised only when a launch needs more, so a launch inside a CUDA-graph capture
+// that was preceded by an eager launch of the same size makes no attribute call.
+static size_t g_query_smem = 48 * 1024, g_count_smem = 48 * 1024, g_mat_smem = 48 * 1024;
+
+inline fmd_status allow_smem(const void* kernel, size_t bytes, size_t& granted) {
+    if (bytes <= granted) return FMD_OK;
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+    if (err != cudaSuccess) return record_cuda_error(err);
+    granted = bytes;
+    return FMD_OK;
+}
+
 inline bool make_grid(const float* cell_host, double cutoff, Grid& g) {
     double c[9];
     for (int k = 0; k < 9; ++k) c[k] = cell_host[k];
@@ -901,8 +914,7 @@ inline fmd_status run_cell_list(const float* positions, int64_t n_atoms, int32_t
     q.flags = flags;
     const size_t smem = query_smem(q.list_cap);
     if (smem > 227 * 1024) return FMD_ERR_UNSUPPORTED;
-    err = cudaFuncSetAttribute(cell_query_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    if (err != cudaSuccess) return record_cuda_error(err);
+    if ((st = allow_smem(reinterpret_cast<const void*>(cell_query_kernel), smem, g_query_smem)) != FMD_OK) return st;
     const int qgrid = int(cells < int64_t(kNumSMs) * 16 ? cells : int64_t(kNumSMs) * 16);
     cell_query_kernel<<<qgrid, kQueryWarps * 32, smem, s>>>(q);
     if ((st = check_launch()) != FMD_OK) return st;
@@ -1020,12 +1032,10 @@ fmd_status fmd_refilter_edges(const float* positions, const float* cell_host, in
     cudaStream_t s = as_stream(stream);
     const size_t smem_count = (sizeof(float3) + sizeof(int3)) * size_t(n_atoms);
     const size_t smem_mat = size_t(smem);
-    cudaError_t err = cudaFuncSetAttribute(refilter_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           int(smem_count));
-    if (err != cudaSuccess) return record_cuda_error(err);
-    err = cudaFuncSetAttribute(refilter_materialize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               int(smem_mat));
-    if (err != cudaSuccess) return record_cuda_error(err);
+    fmd_status st0 = allow_smem(reinterpret_cast<const void*>(refilter_count_kernel), smem_count, g_count_smem);
+    if (st0 != FMD_OK) return st0;
+    st0 = allow_smem(reinterpret_cast<const void*>(refilter_materialize_kernel), smem_mat, g_mat_smem);
+    if (st0 != FMD_OK) return st0;
     refilter_count_kernel<<<n_systems, kRefThreads, smem_count, s>>>(a);
     fmd_status st = check_launch();
     if (st != FMD_OK) return st;

@@ -1,0 +1,207 @@
+"""Whole-step CUDA-graph MD (fastmd/execution/whole_step_cuda_graph.py:56) and its driver.
+
+``WholeStepGraphRunner`` captures a window of ``steps_per_launch`` MD steps
+as ONE CUDA graph: integrator pre-force half -> exact neighbour re-filter ->
+model energy and forces -> integrator post-force half, per step, all on
+libfastmd_b200 kernels, with the builder's FMD_FLAG_* bits ORed into one
+window word. The window is a transaction (whole_step_cuda_graph.py:326-386):
+the integrator state is backed up at its start, and ``settle`` reads the
+window word once; an invalid window (skin exceeded, candidate or edge
+overflow, non-finite state) is rolled back, the candidates are refreshed at
+the restored positions, and the window is replayed. A proactive refresh runs
+when the last step moved an atom more than ``proactive_refresh_fraction`` of
+the skin (whole_step_cuda_graph.py:579-584).
+
+``GPUResidentMolecularDynamics`` (fastmd/interfaces/gpu_md.py:98) wires a
+model, a builder and the Nose-Hoover chain together: ``run(steps)``,
+``thermodynamics()`` and the host-buffer step ``step_host``.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+from torch import Tensor
+
+from fastmd_b200.graph import FLAG_CANDIDATE_OVERFLOW, FLAG_EDGE_OVERFLOW, FLAG_NONFINITE, FLAG_SKIN
+from fastmd_b200.graph import FixedCapacityGraphBuilder
+from fastmd_b200.gpu_nhc import GPUNoseHooverChainNVT, ReplicaNoseHooverChainNVT, maxwell_boltzmann_momenta
+from fastmd_b200.mace import MACEModel
+from fastmd_b200 import units
+
+
+class FixedCapacityOverflow(RuntimeError):
+    """The real graph no longer fits the builder's capacity (whole_step_cuda_graph.py:38)."""
+
+
+class WholeStepGraphRunner:
+    def __init__(self, *, model: MACEModel, builder: FixedCapacityGraphBuilder, integrator, steps_per_launch: int = 1,
+                 warmup: int = 3, proactive_refresh_fraction: float = 0.25) -> None:
+        if steps_per_launch <= 0:
+            raise ValueError("steps_per_launch must be positive")
+        self.model, self.builder, self.integrator = model, builder, integrator
+        self.steps_per_launch = int(steps_per_launch)
+        self.warmup = int(warmup)
+        self.proactive_refresh_fraction = float(proactive_refresh_fraction)
+        self.replicas = builder.replicas
+        self.device = builder.device
+        self.window_flags = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.fallbacks = 0
+        self.refreshes = 0
+        self.graph: torch.cuda.CUDAGraph | None = None
+        # initial state: candidates at the current positions, F(q0) and E(q0) cached in the integrator
+        builder.refresh_candidates(integrator.positions32)
+        self.refreshes += 1
+        batch, _ = builder.build(integrator.positions32, rebuild_candidates=False)
+        self.model.prepare(batch)
+        energy, forces = model.energy_forces(batch, n_systems=self.replicas)
+        integrator.set_forces(forces, energy)
+        flags = int(builder.flags.item())
+        if flags & FLAG_EDGE_OVERFLOW:
+            raise FixedCapacityOverflow(f"{int(batch.n_edges.item())} edges exceed the capacity "
+                                        f"{builder.e_capacity}")
+        if flags & (FLAG_CANDIDATE_OVERFLOW | FLAG_NONFINITE):
+            raise RuntimeError(f"invalid initial graph (flags {flags})")
+        self._capture()
+
+    # --------------------------------------------------------------- window
+    def _window_body(self) -> None:
+        integ, builder, model = self.integrator, self.builder, self.model
+        integ.backup()
+        self.window_flags.copy_(builder.refresh_flags)
+        for _ in range(self.steps_per_launch):
+            integ.step_pre_force()
+            batch, _ = builder.build(integ.positions32, rebuild_candidates=False, flags=self.window_flags)
+            energy, forces = model.energy_forces(batch, n_systems=self.replicas)
+            integ.step_post_force(forces, energy)
+
+    def _capture(self) -> None:
+        snapshot = self.integrator.snapshot()
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            for _ in range(self.warmup):
+                self._window_body()
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        self.integrator.load_snapshot(snapshot)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self._window_body()
+        self.integrator.load_snapshot(snapshot)
+        self.graph = graph
+
+    def launch(self) -> None:
+        """Replay one window (no host synchronisation)."""
+        self.graph.replay()
+
+    def settle(self) -> int:
+        """Read the window word (one host sync); roll back and redo an invalid window; refresh the
+        candidates proactively. Returns the flags of the committed window."""
+        flags = int(self.window_flags.item())
+        if flags & (FLAG_SKIN | FLAG_CANDIDATE_OVERFLOW | FLAG_NONFINITE | FLAG_EDGE_OVERFLOW):
+            flags = self._fallback(flags)
+        elif self.proactive_refresh_fraction > 0:
+            moved = float(self.builder.max_displacement.max())
+            if moved >= self.proactive_refresh_fraction * self.builder.skin:
+                self.builder.refresh_candidates(self.integrator.positions32)
+                self.refreshes += 1
+        return flags
+
+    def _fallback(self, flags: int) -> int:
+        self.fallbacks += 1
+        self.integrator.restore()
+        if flags & FLAG_EDGE_OVERFLOW:
+            raise FixedCapacityOverflow("the window's graph exceeded the edge capacity (grow u_capacity)")
+        if flags & FLAG_NONFINITE:
+            raise FloatingPointError("non-finite positions in the window")
+        self.builder.refresh_candidates(self.integrator.positions32)
+        self.refreshes += 1
+        self.graph.replay()
+        again = int(self.window_flags.item())
+        if again & (FLAG_SKIN | FLAG_CANDIDATE_OVERFLOW | FLAG_EDGE_OVERFLOW | FLAG_NONFINITE):
+            raise RuntimeError(f"window invalid after a candidate refresh (flags {again})")
+        return again
+
+    def run(self, steps: int) -> None:
+        """``steps`` MD steps (a multiple of steps_per_launch), one settle per window."""
+        if steps % self.steps_per_launch:
+            raise ValueError("steps must be a multiple of steps_per_launch")
+        for _ in range(steps // self.steps_per_launch):
+            self.launch()
+            self.settle()
+
+
+class GPUResidentMolecularDynamics:
+    """NVT Nose-Hoover-chain MD of ``replicas`` copies of one periodic system with the
+    MACE-architecture potential, in whole-step CUDA-graph mode (gpu_md.py:98, replica_md.py:224).
+
+    ``positions`` [R*n, 3] (or [n, 3] for one replica), Angstrom; ``momenta`` likewise
+    (default Maxwell-Boltzmann at ``temperature_K`` with seed 0 per replica)."""
+
+    def __init__(self, model: MACEModel, *, positions, cell, atomic_numbers, masses, temperature_K: float,
+                 timestep: float, tdamp: float, tchain: int = 3, tloop: int = 1, momenta=None, replicas: int = 1,
+                 skin: float = 2.0, u_capacity: int | None = None, steps_per_launch: int = 10,
+                 device="cuda") -> None:
+        self.device = torch.device(device)
+        self.replicas = int(replicas)
+        n = len(atomic_numbers)
+        positions = np.asarray(positions, np.float64).reshape(self.replicas * n, 3)
+        if momenta is None:
+            momenta = np.concatenate([maxwell_boltzmann_momenta(masses, temperature_K, seed=r)
+                                      for r in range(self.replicas)])
+        cutoff = model.config.r_max
+        if u_capacity is None:
+            # MACE's capacity tiers (mace.py:70, CapacityStep(32, 32, 1.02)) from the initial pair count
+            pairs = self._initial_pairs(positions[:n], cell, cutoff)
+            u_capacity = int(math.ceil(max(pairs * 1.02, pairs + 32) / 32.0)) * 32 * self.replicas
+        self.builder = FixedCapacityGraphBuilder(
+            cell=torch.as_tensor(np.asarray(cell), dtype=torch.float32), atomic_numbers=torch.as_tensor(atomic_numbers),
+            u_capacity=u_capacity, atom_graph_cutoff=cutoff, candidate_cutoff=cutoff + skin, device=self.device,
+            replicas=self.replicas)
+        kw = dict(temperature_K=temperature_K, timestep=timestep, tdamp=tdamp, tchain=tchain, tloop=tloop,
+                  force_dtype=torch.float32, device=self.device)
+        if self.replicas == 1:
+            self.integrator = GPUNoseHooverChainNVT(masses, positions, momenta, **kw)
+        else:
+            self.integrator = ReplicaNoseHooverChainNVT(masses, positions, momenta, replicas=self.replicas, **kw)
+        self.model = model
+        self.runner = WholeStepGraphRunner(model=model, builder=self.builder, integrator=self.integrator,
+                                           steps_per_launch=steps_per_launch)
+        self.n_atoms = n
+        self.steps_done = 0
+
+    @staticmethod
+    def _initial_pairs(positions, cell, cutoff) -> int:
+        from fastmd_b200.graph import neighbor_list
+
+        pos = torch.as_tensor(positions, dtype=torch.float32).cuda()
+        center, _, _, _ = neighbor_list(pos, torch.as_tensor(np.asarray(cell), dtype=torch.float32), cutoff)
+        return int(center.shape[0] + 1) // 2
+
+    def run(self, steps: int) -> None:
+        self.runner.run(steps)
+        self.steps_done += steps
+
+    def thermodynamics(self) -> dict:
+        """Per-replica potential, kinetic and conserved energy (eV) and temperature (K)."""
+        integ = self.integrator
+        return {"potential_energy": integ.state.energy.cpu().numpy().copy(),
+                "kinetic_energy": np.atleast_1d(integ.kinetic_energy().cpu().numpy()).copy(),
+                "temperature": np.atleast_1d(integ.temperature().cpu().numpy()).copy(),
+                "conserved_energy": np.atleast_1d(integ.conserved_energy().cpu().numpy()).copy()}
+
+    def step_host(self, positions: Tensor, momenta: Tensor, out: dict) -> None:
+        """One window from HOST state: upload positions and momenta (pinned), replay, settle, and
+        download positions, momenta, forces and energies into the pinned ``out`` buffers."""
+        integ = self.integrator
+        integ.state.q.copy_(positions, non_blocking=True)
+        integ.state.p.copy_(momenta, non_blocking=True)
+        integ.positions32.copy_(integ.state.q)
+        self.runner.launch()
+        self.runner.settle()
+        out["positions"].copy_(integ.state.q, non_blocking=True)
+        out["momenta"].copy_(integ.state.p, non_blocking=True)
+        out["forces"].copy_(integ.state.f, non_blocking=True)
+        out["energy"].copy_(integ.state.energy, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
