@@ -10,14 +10,17 @@ T = 500.0
 
 def _md(cuda, *, seeds=(0,), skin=2.0, steps_per_launch=5, channels=128):
     from fastmd_b200 import units
+    from fastmd_b200.gpu_nhc import maxwell_boltzmann_momenta
     from fastmd_b200.mace import MACEConfig, MACEModel
     from fastmd_b200.structures import perovskite
     from fastmd_b200.whole_step import GPUResidentMolecularDynamics
 
     systems = [perovskite(seed=s) for s in seeds]
     _, cell, numbers, masses = systems[0]
+    momenta = np.concatenate([maxwell_boltzmann_momenta(masses, T, seed=s) for s in seeds])
     model = MACEModel(MACEConfig(channels=channels), device=cuda, seed=1)
-    return GPUResidentMolecularDynamics(model, positions=np.concatenate([s[0] for s in systems]), cell=cell,
+    return GPUResidentMolecularDynamics(model, positions=np.concatenate([s[0] for s in systems]), momenta=momenta,
+                                        cell=cell,
                                         atomic_numbers=numbers, masses=masses, temperature_K=T,
                                         timestep=0.25 * units.fs, tdamp=25 * units.fs, replicas=len(seeds),
                                         skin=skin, steps_per_launch=steps_per_launch, device=cuda)
