@@ -252,23 +252,29 @@ class _NoseHooverChain:
     def velocities(self) -> Tensor:
         return self.state.p / self.masses
 
-    def kinetic_energy(self) -> Tensor:
-        """0.5 vdot(p, p/m) per replica (fp64)."""
+    def _kinetic(self) -> Tensor:
         p = self._per_replica(self.state.p)
         m = self.masses.reshape(self.replicas, self.n_atoms, 1)
         return 0.5 * (p * (p / m)).sum(dim=(1, 2))
 
-    def temperature(self) -> Tensor:
-        return 2 * self.kinetic_energy() / (3 * self.n_atoms * units.kB)
-
-    def thermostat_energy(self) -> Tensor:
+    def _thermostat(self) -> Tensor:
         st = self.state
         return (self.ndof_kT * st.eta[:, 0] + self.kT * st.eta[:, 1:].sum(dim=1)
                 + (0.5 * (st.p_eta * st.p_eta) / self.Q).sum(dim=1))
 
+    def kinetic_energy(self) -> Tensor:
+        """0.5 vdot(p, p/m) per replica (fp64)."""
+        return self._kinetic()
+
+    def temperature(self) -> Tensor:
+        return 2 * self._kinetic() / (3 * self.n_atoms * units.kB)
+
+    def thermostat_energy(self) -> Tensor:
+        return self._thermostat()
+
     def conserved_energy(self, potential_energy=None) -> Tensor:
         epot = self.state.energy if potential_energy is None else potential_energy
-        return epot + self.kinetic_energy() + self.thermostat_energy()
+        return epot + self._kinetic() + self._thermostat()
 
     # ------------------------------------------------------------- transactions
     def backup(self) -> None:
@@ -310,17 +316,17 @@ class GPUNoseHooverChainNVT(_NoseHooverChain):
         return self.state.p_eta[0]
 
     def kinetic_energy(self) -> Tensor:
-        return super().kinetic_energy()[0]
+        return self._kinetic()[0]
 
     def temperature(self) -> Tensor:
-        return super().temperature()[0]
+        return 2 * self._kinetic()[0] / (3 * self.n_atoms * units.kB)
 
     def thermostat_energy(self) -> Tensor:
-        return super().thermostat_energy()[0]
+        return self._thermostat()[0]
 
     def conserved_energy(self, potential_energy=None) -> Tensor:
         epot = self.state.energy[0] if potential_energy is None else potential_energy
-        return epot + self.kinetic_energy() + self.thermostat_energy()
+        return epot + self._kinetic()[0] + self._thermostat()[0]
 
     def state_dict(self) -> dict:
         return {"eta": self.eta.cpu().numpy().copy(), "p_eta": self.p_eta.cpu().numpy().copy(),

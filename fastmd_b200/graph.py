@@ -244,6 +244,15 @@ class FixedCapacityGraphBuilder:
         )
         self._candidate_initialized = False
 
+    def resized(self, u_capacity: int) -> "FixedCapacityGraphBuilder":
+        """A builder of the same system with another pair capacity (new buffers; the candidates
+        are refreshed by the caller)."""
+        return FixedCapacityGraphBuilder(
+            cell=self.cell, atomic_numbers=self.batch.species[:self.n_atoms], u_capacity=u_capacity,
+            atom_graph_cutoff=self.atom_graph_cutoff, device=self.device, candidate_cutoff=self.candidate_cutoff,
+            padding=self.padding, replicas=self.replicas, max_neighbors=self.buffer_max,
+            minimum_image=self.minimum_image)
+
     # ------------------------------------------------------------------ inputs
     def _positions(self, positions: Tensor) -> Tensor:
         if positions.shape != (self.n_real, 3):

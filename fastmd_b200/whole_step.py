@@ -25,6 +25,7 @@ import torch
 from torch import Tensor
 
 from fastmd_b200.graph import FLAG_CANDIDATE_OVERFLOW, FLAG_EDGE_OVERFLOW, FLAG_NONFINITE, FLAG_SKIN
+_INVALID = FLAG_SKIN | FLAG_CANDIDATE_OVERFLOW | FLAG_NONFINITE | FLAG_EDGE_OVERFLOW
 from fastmd_b200.graph import FixedCapacityGraphBuilder
 from fastmd_b200.gpu_nhc import GPUNoseHooverChainNVT, ReplicaNoseHooverChainNVT, maxwell_boltzmann_momenta
 from fastmd_b200.mace import MACEModel
@@ -49,6 +50,9 @@ class WholeStepGraphRunner:
         self.window_flags = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.fallbacks = 0
         self.refreshes = 0
+        self.eager_steps = 0
+        self.capacity_growths = 0
+        self.on_resize = None
         self.graph: torch.cuda.CUDAGraph | None = None
         # initial state: candidates at the current positions, F(q0) and E(q0) cached in the integrator
         builder.refresh_candidates(integrator.positions32)
@@ -97,10 +101,10 @@ class WholeStepGraphRunner:
 
     def settle(self) -> int:
         """Read the window word (one host sync); roll back and redo an invalid window; refresh the
-        candidates proactively. Returns the flags of the committed window."""
+        candidates proactively. Returns the flags of the window as first replayed."""
         flags = int(self.window_flags.item())
-        if flags & (FLAG_SKIN | FLAG_CANDIDATE_OVERFLOW | FLAG_NONFINITE | FLAG_EDGE_OVERFLOW):
-            flags = self._fallback(flags)
+        if flags & _INVALID:
+            self._fallback(flags)
         elif self.proactive_refresh_fraction > 0:
             moved = float(self.builder.max_displacement.max())
             if moved >= self.proactive_refresh_fraction * self.builder.skin:
@@ -108,20 +112,67 @@ class WholeStepGraphRunner:
                 self.refreshes += 1
         return flags
 
-    def _fallback(self, flags: int) -> int:
+    def _fallback(self, flags: int) -> None:
+        """Roll the window back and redo it (whole_step_cuda_graph.py:477): with more edge capacity
+        (a new builder and a recapture) after an overflow; else with candidates refreshed at the
+        restored positions; and when even those cannot cover the window, as eager steps that each
+        refresh the candidates first. The edges are exact in every route, so the trajectory is the
+        same."""
         self.fallbacks += 1
         self.integrator.restore()
-        if flags & FLAG_EDGE_OVERFLOW:
-            raise FixedCapacityOverflow("the window's graph exceeded the edge capacity (grow u_capacity)")
         if flags & FLAG_NONFINITE:
             raise FloatingPointError("non-finite positions in the window")
+        if flags & FLAG_EDGE_OVERFLOW:
+            self._grow()
         self.builder.refresh_candidates(self.integrator.positions32)
         self.refreshes += 1
         self.graph.replay()
         again = int(self.window_flags.item())
-        if again & (FLAG_SKIN | FLAG_CANDIDATE_OVERFLOW | FLAG_EDGE_OVERFLOW | FLAG_NONFINITE):
-            raise RuntimeError(f"window invalid after a candidate refresh (flags {again})")
-        return again
+        if not again & _INVALID:
+            return
+        self.integrator.restore()
+        if again & FLAG_EDGE_OVERFLOW:
+            self._grow()
+            self.builder.refresh_candidates(self.integrator.positions32)
+            self.graph.replay()
+            if not int(self.window_flags.item()) & _INVALID:
+                return
+            self.integrator.restore()
+        self._eager_window()
+
+    def _eager_window(self) -> None:
+        integ, builder, model = self.integrator, self.builder, self.model
+        for _ in range(self.steps_per_launch):
+            integ.step_pre_force()
+            batch, status = builder.build(integ.positions32, rebuild_candidates=True)
+            flags = int(status.flags.item())
+            if flags & FLAG_EDGE_OVERFLOW:
+                self._grow()
+                batch, status = self.builder.build(integ.positions32, rebuild_candidates=True)
+                builder = self.builder
+                flags = int(status.flags.item())
+            if flags & _INVALID:
+                raise RuntimeError(f"invalid graph in an eager step (flags {flags})")
+            energy, forces = model.energy_forces(batch, n_systems=self.replicas)
+            integ.step_post_force(forces, energy)
+        self.eager_steps += self.steps_per_launch
+
+    def _grow(self) -> None:
+        """A larger edge capacity (the needed edges + 10 %, pairs rounded to 32) and a recapture."""
+        old = self.builder
+        needed = int(old.batch.n_edges.item())
+        u = int(math.ceil(max(needed * 1.1 / 2, old.u_capacity + 32 * old.replicas) / 32.0)) * 32
+        self.builder = old.resized(u)
+        self.graph = None
+        self.model.prepare(self.builder.batch)
+        self.builder.refresh_candidates(self.integrator.positions32)
+        batch, _ = self.builder.build(self.integrator.positions32, rebuild_candidates=False)
+        self.model.energy_forces(batch, n_systems=self.replicas)  # buffers of the new size, eagerly
+        self.integrator.restore()
+        self._capture()
+        self.capacity_growths += 1
+        if self.on_resize is not None:
+            self.on_resize(self.builder)
 
     def run(self, steps: int) -> None:
         """``steps`` MD steps (a multiple of steps_per_launch), one settle per window."""
@@ -154,7 +205,7 @@ class GPUResidentMolecularDynamics:
         if u_capacity is None:
             # MACE's capacity tiers (mace.py:70, CapacityStep(32, 32, 1.02)) from the initial pair count
             pairs = self._initial_pairs(positions[:n], cell, cutoff)
-            u_capacity = int(math.ceil(max(pairs * 1.02, pairs + 32) / 32.0)) * 32 * self.replicas
+            u_capacity = int(math.ceil(max(pairs * 1.08, pairs + 32) / 32.0)) * 32 * self.replicas
         self.builder = FixedCapacityGraphBuilder(
             cell=torch.as_tensor(np.asarray(cell), dtype=torch.float32), atomic_numbers=torch.as_tensor(atomic_numbers),
             u_capacity=u_capacity, atom_graph_cutoff=cutoff, candidate_cutoff=cutoff + skin, device=self.device,
@@ -168,8 +219,12 @@ class GPUResidentMolecularDynamics:
         self.model = model
         self.runner = WholeStepGraphRunner(model=model, builder=self.builder, integrator=self.integrator,
                                            steps_per_launch=steps_per_launch)
+        self.runner.on_resize = self._resized
         self.n_atoms = n
         self.steps_done = 0
+
+    def _resized(self, builder) -> None:
+        self.builder = builder
 
     @staticmethod
     def _initial_pairs(positions, cell, cutoff) -> int:
