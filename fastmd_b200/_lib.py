@@ -46,6 +46,8 @@ _SIGNATURES: dict[str, list] = {
     "fmd_refilter_workspace_bytes": [_I64, _I32, POINTER(c_size_t)],
     "fmd_refilter_edges": [_P, _P, _I64, _I32, _P, _P, _P, _P, _P, _I32, c_float, c_float, _I64, _P, _I32, _P, _P,
                            _P, _P, _P, _P, _P, _P, _P, _P, c_size_t, _P, _P],
+    "fmd_refilter_edges_noalloc": [_P, _P, _I64, _I32, _P, _P, _P, _P, _P, _I32, c_float, c_float, _I64, _P, _I32,
+                                   _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P],
     "fmd_neighbor_list_workspace_bytes": [_P, c_float, _I64, _I32, POINTER(c_size_t)],
     "fmd_neighbor_list": [_P, _P, _I64, c_float, _I32, _I64, _P, _P, _P, _P, _P, _P, _P, c_size_t, _P, _P],
     "fmd_gemm_f32": [_P, _I64, _P, _I64, _P, _I64, _I32, _P, _P, _I64, _P, _I64, _I64, _I32, _I32, _I32, _I32, _P],

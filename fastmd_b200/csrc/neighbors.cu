@@ -31,6 +31,8 @@
 
 #include <cub/device/device_scan.cuh>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace fmd {
@@ -1043,6 +1045,52 @@ fmd_status fmd_refilter_edges(const float* positions, const float* cell_host, in
     return check_launch();
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free re-filter. Some callers cannot allocate device memory at
+// all: a C or Fortran MD host that links this library but has no CUDA
+// allocator or memory pool of its own to hand out a workspace, or a caller
+// running inside another framework whose memory manager owns every byte of
+// the device. For them the re-filter's scratch (per-atom edge counts and
+// offsets, per-system totals) lives in this file-scope device array instead
+// of a caller workspace. It is 1 MiB, held by every GPU that loads the
+// library until the process exits, and serves up to 126,976 atoms in total
+// (n_atoms * n_systems, with up to 4,096 systems); larger calls are refused
+// with FMD_ERR_WORKSPACE before anything is launched.
+// ---------------------------------------------------------------------------
+
+constexpr size_t kNoAllocScratchBytes = size_t(1) << 20;
+constexpr int64_t kNoAllocMaxAtoms = 126976;   // n_atoms * n_systems
+constexpr int32_t kNoAllocMaxSystems = 4096;
+constexpr int kNoAllocMaxDevices = 64;
+// the largest admitted call fits the array: 2 x 507,904 B of counts/offsets + 16,384 B of totals
+static_assert(2 * ((4 * kNoAllocMaxAtoms + 255) / 256 * 256) + (4 * kNoAllocMaxSystems + 255) / 256 * 256 <=
+                  int64_t(kNoAllocScratchBytes),
+              "the allocation-free re-filter limits must fit its static scratch");
+
+static __device__ __align__(256) unsigned char g_refilter_scratch[kNoAllocScratchBytes];
+
+// Host code must not pass g_refilter_scratch itself to a kernel: on the host
+// that name is only a stand-in for the device symbol. The device address is
+// looked up once per device (with that device current) and cached.
+static void* g_refilter_scratch_ptr[kNoAllocMaxDevices] = {};
+static std::mutex g_refilter_scratch_mutex;
+
+static fmd_status refilter_scratch_address(void** out) {
+    int device = 0;
+    cudaError_t err = cudaGetDevice(&device);
+    if (err != cudaSuccess) return record_cuda_error(err);
+    if (device < 0 || device >= kNoAllocMaxDevices) return FMD_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lock(g_refilter_scratch_mutex);
+    if (g_refilter_scratch_ptr[device] == nullptr) {
+        void* address = nullptr;
+        err = cudaGetSymbolAddress(&address, g_refilter_scratch);
+        if (err != cudaSuccess) return record_cuda_error(err);
+        g_refilter_scratch_ptr[device] = address;
+    }
+    *out = g_refilter_scratch_ptr[device];
+    return FMD_OK;
+}
+
 static size_t ragged_scan_bytes(int64_t n_atoms) {
     size_t cub_bytes = 0;
     cub::DeviceScan::ExclusiveSum(nullptr, cub_bytes, (const int64_t*)nullptr, (int64_t*)nullptr, int(n_atoms + 1));
@@ -1106,6 +1154,30 @@ fmd_status fmd_neighbor_list(const float* positions, const float* cell_host, int
         if ((st = check_launch()) != FMD_OK) return st;
     }
     return FMD_OK;
+}
+
+fmd_status fmd_refilter_edges_noalloc(const float* positions, const float* cell_host, int64_t n_atoms,
+                                      int32_t n_systems, const float* ref_positions, const int32_t* ref_wraps,
+                                      const int32_t* cand_nbr, const int32_t* cand_shift,
+                                      const int32_t* cand_count, int32_t bmax, float cutoff, float skin,
+                                      int64_t e_capacity, const int32_t* pad_image_host, int32_t minimum_image,
+                                      float* wrapped, int32_t* wrap_delta, int32_t* edge_index, float* edge_image,
+                                      int64_t* recv_off, int64_t* send_off, int32_t* send_perm, int64_t* n_edges,
+                                      float* max_displacement, int32_t* flags, void* stream) {
+    if (n_atoms < 1 || n_systems < 1) return FMD_ERR_INVALID_ARGUMENT;
+    if (n_systems > kNoAllocMaxSystems || n_atoms > kNoAllocMaxAtoms / n_systems) return FMD_ERR_WORKSPACE;
+    size_t need = 0;
+    fmd_status st = fmd_refilter_workspace_bytes(n_atoms, n_systems, &need);
+    if (st != FMD_OK) return st;
+    if (need > kNoAllocScratchBytes) return FMD_ERR_WORKSPACE;  // beyond the static scratch
+    void* scratch = nullptr;
+    if ((st = refilter_scratch_address(&scratch)) != FMD_OK) return st;
+    // Every field of the scratch is written before it is read within the call, so the previous
+    // call's contents need no clearing.
+    return fmd_refilter_edges(positions, cell_host, n_atoms, n_systems, ref_positions, ref_wraps, cand_nbr,
+                              cand_shift, cand_count, bmax, cutoff, skin, e_capacity, pad_image_host, minimum_image,
+                              wrapped, wrap_delta, edge_index, edge_image, recv_off, send_off, send_perm, n_edges,
+                              max_displacement, scratch, kNoAllocScratchBytes, flags, stream);
 }
 
 }  // extern "C"

@@ -205,6 +205,30 @@ FMD_API fmd_status fmd_refilter_edges(const float* positions, const float* cell_
                                       float* max_displacement, void* workspace, size_t workspace_bytes,
                                       int32_t* flags, void* stream);
 
+/* fmd_refilter_edges for callers that cannot allocate device memory (no
+ * counterpart in the reference): a C or Fortran MD host that links this
+ * library without a CUDA allocator or memory pool of its own, or a caller
+ * inside another framework whose memory manager owns the device. The same
+ * arguments and results as fmd_refilter_edges, without the workspace: the
+ * scratch is a static 1 MiB device array held by every GPU that loads the
+ * library until exit, enough for n_atoms * n_systems <= 126,976 atoms (up to
+ * 4,096 systems); larger calls return FMD_ERR_WORKSPACE and launch nothing.
+ * The first call on a device looks the array's device address up (once per
+ * device, with that device current): make that first call before any stream
+ * capture. All calls share the array, so calls that overlap on the GPU (two
+ * streams, two host threads) race; serialise them. Nothing in it needs to
+ * start at zero (every field is written before it is read). Allocates nothing. */
+FMD_API fmd_status fmd_refilter_edges_noalloc(const float* positions, const float* cell_host, int64_t n_atoms,
+                                              int32_t n_systems, const float* ref_positions,
+                                              const int32_t* ref_wraps, const int32_t* cand_nbr,
+                                              const int32_t* cand_shift, const int32_t* cand_count, int32_t bmax,
+                                              float cutoff, float skin, int64_t e_capacity,
+                                              const int32_t* pad_image_host, int32_t minimum_image, float* wrapped,
+                                              int32_t* wrap_delta, int32_t* edge_index, float* edge_image,
+                                              int64_t* recv_off, int64_t* send_off, int32_t* send_perm,
+                                              int64_t* n_edges, float* max_displacement, int32_t* flags,
+                                              void* stream);
+
 /* Workspace of fmd_neighbor_list. */
 FMD_API fmd_status fmd_neighbor_list_workspace_bytes(const float* cell_host, float cutoff, int64_t n_atoms,
                                                      int32_t bmax, size_t* bytes);
