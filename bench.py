@@ -189,7 +189,9 @@ def _ours(args):
     runner._window_body()
     counted = _lib.count_launches(False)
     md.integrator.load_snapshot(snapshot)
-    launches_per_window = sum(n * _lib.KERNELS_PER_CALL.get(name, 1) for name, n in counted.items())
+    launches_per_window = sum(n * (_lib.fused_step_kernels(model.config.num_interactions)
+                                   if name == "fmd_mace_fused_step" else _lib.KERNELS_PER_CALL.get(name, 1))
+                              for name, n in counted.items())
     thermo = torch.zeros(R, 2, dtype=torch.float64, device=device)
     gathered = torch.zeros(world * R, 2, dtype=torch.float64, device=device)
 
@@ -256,7 +258,12 @@ def _ours(args):
     h2d = (host_q.numel() + host_p.numel()) * 8 / S
     d2h = sum(t.numel() * t.element_size() for t in out.values()) / S
 
-    roofline = _roofline(md, device) if rank == 0 else None
+    roofline = None
+    if rank == 0:
+        try:
+            roofline = _roofline(md, device)
+        except Exception as error:  # noqa: BLE001 - the line still reports the measured step
+            roofline = {"error": f"{type(error).__name__}: {error}"}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = _cpu_baseline()

@@ -1,0 +1,9 @@
+"""fastmd_b200: FastMD's per-step MD hot path on hand-written sm_100a kernels (libfastmd_b200.so).
+
+Surfaces mirroring the reference: ``ops`` (fastmd.ops), ``graph`` (fastmd.graph builders),
+``energy_derivative`` (fastmd.engine), ``gpu_nhc`` and ``whole_step`` (fastmd.execution /
+fastmd.interfaces), ``mace`` (the MACE-architecture energy tap).
+"""
+from fastmd_b200 import _lib, energy_derivative, gpu_nhc, graph, mace, ops, units, whole_step  # noqa: F401
+
+__all__ = ["energy_derivative", "gpu_nhc", "graph", "mace", "ops", "units", "whole_step"]

@@ -109,7 +109,13 @@ def check(status: int, what: str) -> None:
 
 
 # kernels each entry point launches (for the launch count of a step); the default is one
-KERNELS_PER_CALL = {"fmd_refilter_edges": 2, "fmd_mace_message_bwd": 2}
+KERNELS_PER_CALL = {"fmd_refilter_edges": 2, "fmd_refilter_edges_noalloc": 2, "fmd_mace_message_bwd": 2}
+
+
+def fused_step_kernels(n_layers: int) -> int:
+    """Launches of one fmd_mace_fused_step: edge_fwd, L messages, L-1 node_fwd, node_last,
+    L-1 (msg_bwd_edge + sender_node), msg_bwd_edge(0), edge_bwd, forces."""
+    return 1 + n_layers + (n_layers - 1) + 1 + 2 * (n_layers - 1) + 1 + 1 + 1
 _counting: dict | None = None
 
 
@@ -161,5 +167,8 @@ def flags_word(device) -> torch.Tensor:
     return word
 
 
+c_int32_t, c_int64_t = c_int32, c_int64
+c_void_p_t = c_void_p
+
 __all__ = ["FastMDLibraryError", "FmdCatPart", "call", "check", "declare", "flags_word", "lib", "ptr",
-           "require_cuda", "stream", "c_double", "c_float"]
+           "require_cuda", "stream", "c_double", "c_float", "c_int32", "c_int64", "c_void_p", "ctypes"]

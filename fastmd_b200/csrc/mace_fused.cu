@@ -1,0 +1,1022 @@
+// The MACE-architecture step in a few fused kernels (the whole-step path).
+//
+// A 135-atom step is latency-bound: the unfused model launches ~60 small
+// kernels. Here one step of an L-layer model is
+//   edge_fwd        geometry + radial basis + the radial MLP of every layer
+//                   (32-edge tiles, hidden activations in shared memory)
+//   message(l)      gather -> tensor-product message -> receiver segment sum
+//                   (one CTA per receiver, warps over its edges, fixed-order
+//                   combine: deterministic, no atomics)
+//   node_fwd(l)     per group of same-element atoms: channel mixing, the
+//                   symmetric contraction, the output mixing, the skip
+//                   connection, the readout and the next layer's up-mixing
+//   node_last       the last layer's node update, its readout, the node
+//                   energies, and the start of the backward (to dA)
+//   msg_bwd_edge(l) per receiver run: dR and dY (warp per edge)
+//   sender_node(l)  per sender run: the gathered rows' gradient, the
+//                   up-mixing backward and the previous layer's node backward
+//   edge_bwd        the radial MLP backward (recomputed forward) of every
+//                   layer and the geometry backward: dE/dr_e per edge
+//   forces          F_a = sum over received edges - sum over sent edges of
+//                   dE/dr_e (both CSRs), the per-system energy sums
+// Weights are frozen; the host prepares transposed copies once so every
+// channel-mixing loop reads weights coalesced (thread = output channel).
+
+#include "common.cuh"
+
+namespace fmd {
+
+constexpr int kMaxLayers = 4;
+constexpr int kH = 64;        // radial MLP width
+constexpr int kTE = 32;       // edges per tile of the forward edge kernel
+constexpr int kMaxPC = 512;   // P*C of a layer's radial output (C <= 128)
+constexpr int kTB = 16;       // edges per tile of the backward edge kernel (its activations fit 48 KB)
+constexpr int kG = 4;         // atoms per group of the node kernels
+constexpr float kS3 = 1.7320508075688772f;
+constexpr float kIS3 = 0.5773502691896258f;
+
+struct FusedWeights {
+    // radial MLP per layer: transposed [in][out] for the forward, original [out][in] for the backward
+    const float* w1t[kMaxLayers];
+    const float* w2t[kMaxLayers];
+    const float* w3t[kMaxLayers];
+    const float* w4t[kMaxLayers];
+    const float* w1[kMaxLayers];
+    const float* w2[kMaxLayers];
+    const float* w3[kMaxLayers];
+    const float* w4[kMaxLayers];
+    // channel mixing: original [out][in] and transposed [in][out]
+    const float* lin0[kMaxLayers];
+    const float* lin1[kMaxLayers];
+    const float* lin0t[kMaxLayers];
+    const float* lin1t[kMaxLayers];
+    const float* out0[kMaxLayers];
+    const float* out1[kMaxLayers];
+    const float* out0t[kMaxLayers];
+    const float* out1t[kMaxLayers];
+    const float* up0[kMaxLayers];
+    const float* up1[kMaxLayers];
+    const float* up0t[kMaxLayers];
+    const float* up1t[kMaxLayers];
+    const float* prod0[kMaxLayers];   // [Z][5][C]
+    const float* prod1[kMaxLayers];   // [Z][4][C]
+    const float* skip0[kMaxLayers];   // [Z][in][out]
+    const float* skip1[kMaxLayers];
+    const float* skip0t[kMaxLayers];  // [Z][out][in]
+    const float* skip1t[kMaxLayers];
+    const float* s_t0;                // [Z][C]: layer 0's up-mixing of the embedding
+    const float* r0;                  // [C] readout of layer 0
+    const float* ra;                  // [RH][C]
+    const float* rb;                  // [RH]
+    const double* e0;                 // [Z]
+    double scale, shift;
+    int n_layers, n_basis, poly_p, readout_hidden;
+    float r_max, inv_avg;
+};
+
+// per-layer activations
+struct FusedState {
+    float* R[kMaxLayers];       // [E][P*C]
+    float* dR[kMaxLayers];
+    float* s_t[kMaxLayers];     // [N][C] (layer 0: unused, the table)
+    float* v_t[kMaxLayers];     // [N][3][C]
+    float* A0[kMaxLayers];      // [N][C] aggregated messages
+    float* A1[kMaxLayers];      // [N][3][C]
+    float* A0l[kMaxLayers];     // after the channel mixing
+    float* A1l[kMaxLayers];
+    float* s_out[kMaxLayers];   // layer outputs
+    float* v_out[kMaxLayers];
+    float* dA0[kMaxLayers];
+    float* dA1[kMaxLayers];
+    float* ds_skip[kMaxLayers]; // gradient of layer l's input from its skip connection
+    float* dv_skip[kMaxLayers];
+    float4* ysh;                // [E] (sqrt3 u, d)
+    float* dY;                  // [E][3]
+    float* g_r;                 // [E][3] dE/dr_e
+    float* e_term0;             // [N]
+    double* node_energy;        // [N]
+    const int32_t* elem;        // [N]
+    const int32_t* groups;      // [n_groups][kG] atom ids (-1 padding), same element per group
+    int64_t n_groups;
+};
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+__device__ __forceinline__ float silu_g(float x) {
+    const float s = 1.0f / (1.0f + expf(-x));
+    return s * (1.0f + x * (1.0f - s));
+}
+
+__device__ __forceinline__ void cutoff_poly(float d, float r_max, int pp, float& f, float& df) {
+    const float x = d / r_max;
+    if (!(x < 1.0f)) {
+        f = 0.f;
+        df = 0.f;
+        return;
+    }
+    const float p = float(pp);
+    const float a = (p + 1.f) * (p + 2.f) * 0.5f, b = p * (p + 2.f), c = p * (p + 1.f) * 0.5f;
+    const float xpm1 = powf(x, p - 1.f);
+    const float xp = xpm1 * x;
+    f = 1.f - a * xp + b * xp * x - c * xp * x * x;
+    df = (-a * p * xpm1 + b * (p + 1.f) * xp - c * (p + 2.f) * xp * x) / r_max;
+}
+
+// ---------------------------------------------------------------- edge forward
+
+struct EdgeArgs {
+    const float* pos;
+    const float* cell;
+    const int32_t* edge_index;
+    const float* edge_image;
+    int64_t n_edges;
+    int C;
+};
+
+struct EdgeFwdSmem {
+    float phi[kTE][17];
+    float h[2][kTE][kH + 1];
+    float w1[16][kH];          // W1^T [basis][hidden]
+    float w2[kH][kH + 1];      // W2^T [in][out], rows padded (conflict-free either way)
+    float w3[kH][kH + 1];
+};
+
+// stage one layer's radial weights W1^T, W2^T, W3^T in shared memory (coalesced, all threads)
+__device__ __forceinline__ void stage_radial(float (*w1)[kH], float (*w2)[kH + 1], float (*w3)[kH + 1],
+                                             const FusedWeights& w, int L, int nthreads) {
+    for (int idx = threadIdx.x; idx < w.n_basis * kH; idx += nthreads) w1[idx / kH][idx % kH] = w.w1t[L][idx];
+    for (int idx = threadIdx.x; idx < kH * kH; idx += nthreads) {
+        w2[idx / kH][idx % kH] = w.w2t[L][idx];
+        w3[idx / kH][idx % kH] = w.w3t[L][idx];
+    }
+}
+
+// geometry, radial features and the radial MLP of every layer for one 32-edge tile; the hidden
+// layers read their weights from shared memory, the output layer streams W4^T from L2
+__global__ void __launch_bounds__(256) edge_fwd_kernel(EdgeArgs a, FusedWeights w, FusedState st) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    EdgeFwdSmem& m = *reinterpret_cast<EdgeFwdSmem*>(smem_raw);
+    const int t = threadIdx.x;
+    const float pref = sqrtf(2.0f / w.r_max);
+    const int64_t n_tiles = (a.n_edges + kTE - 1) / kTE;
+    for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+        const int64_t e0 = tile * kTE;
+        __syncthreads();
+        if (t < kTE) {
+            const int64_t e = e0 + t;
+            float d = 0.f;
+            if (e < a.n_edges) {
+                const int64_t i = a.edge_index[2 * e], j = a.edge_index[2 * e + 1];
+                const float ix = a.edge_image[3 * e], iy = a.edge_image[3 * e + 1], iz = a.edge_image[3 * e + 2];
+                const float* c = a.cell;
+                const float rx = (a.pos[3 * j] - a.pos[3 * i]) + ((ix * c[0] + iy * c[3]) + iz * c[6]);
+                const float ry = (a.pos[3 * j + 1] - a.pos[3 * i + 1]) + ((ix * c[1] + iy * c[4]) + iz * c[7]);
+                const float rz = (a.pos[3 * j + 2] - a.pos[3 * i + 2]) + ((ix * c[2] + iy * c[5]) + iz * c[8]);
+                d = sqrtf((rx * rx + ry * ry) + rz * rz);
+                const float inv = d > 0.f ? 1.0f / d : 0.f;
+                st.ysh[e] = make_float4(kS3 * rx * inv, kS3 * ry * inv, kS3 * rz * inv, d);
+            }
+            float f, df;
+            cutoff_poly(d, w.r_max, w.poly_p, f, df);
+            const float inv = d > 0.f ? 1.0f / d : 0.f;
+            for (int n = 0; n < w.n_basis; ++n) {
+                const float k = float(n + 1) * 3.14159265358979323846f / w.r_max;
+                m.phi[t][n] = d > 0.f ? pref * sinf(k * d) * inv * f : 0.f;
+            }
+        }
+        for (int L = 0; L < w.n_layers; ++L) {
+            const int PC = (L == 0 ? 2 : 4) * a.C;
+            __syncthreads();
+            stage_radial(m.w1, m.w2, m.w3, w, L, 256);
+            __syncthreads();
+            for (int idx = t; idx < kTE * kH; idx += 256) {
+                const int e = idx / kH, k = idx % kH;
+                float acc = 0.f;
+                for (int n = 0; n < w.n_basis; ++n) acc = fmaf(m.phi[e][n], m.w1[n][k], acc);
+                m.h[0][e][k] = silu_f(acc);
+            }
+            __syncthreads();
+            for (int idx = t; idx < kTE * kH; idx += 256) {
+                const int e = idx / kH, k = idx % kH;
+                float acc = 0.f;
+#pragma unroll 16
+                for (int c = 0; c < kH; ++c) acc = fmaf(m.h[0][e][c], m.w2[c][k], acc);
+                m.h[1][e][k] = silu_f(acc);
+            }
+            __syncthreads();
+            for (int idx = t; idx < kTE * kH; idx += 256) {
+                const int e = idx / kH, k = idx % kH;
+                float acc = 0.f;
+#pragma unroll 16
+                for (int c = 0; c < kH; ++c) acc = fmaf(m.h[1][e][c], m.w3[c][k], acc);
+                m.h[0][e][k] = silu_f(acc);
+            }
+            __syncthreads();
+            for (int n = t; n < PC; n += 256) {
+                float acc[kTE];
+#pragma unroll
+                for (int e = 0; e < kTE; ++e) acc[e] = 0.f;
+#pragma unroll 16
+                for (int c = 0; c < kH; ++c) {
+                    const float wv = w.w4t[L][c * PC + n];
+#pragma unroll
+                    for (int e = 0; e < kTE; ++e) acc[e] = fmaf(m.h[0][e][c], wv, acc[e]);
+                }
+#pragma unroll
+                for (int e = 0; e < kTE; ++e)
+                    if (e0 + e < a.n_edges) st.R[L][(e0 + e) * PC + n] = acc[e];
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------ messages
+
+struct GraphArgs {
+    const int32_t* edge_index;
+    const int64_t* recv_off;
+    const int64_t* send_off;
+    const int32_t* send_perm;
+    int64_t n_atoms;
+};
+
+// A(l) of every receiver; warps over the receiver's edges, fixed-order combine of the 4 warp partials
+template <int C, int P>
+__global__ void __launch_bounds__(128) message_fused_kernel(GraphArgs g, FusedWeights w, FusedState st, int L) {
+    constexpr int CPL = C / 32;
+    __shared__ float s_part[4][4][C];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float* R = st.R[L];
+    const float* v_t = st.v_t[L];
+    for (int64_t i = blockIdx.x; i < g.n_atoms; i += gridDim.x) {
+        float a0[CPL], ax[CPL], ay[CPL], az[CPL];
+#pragma unroll
+        for (int q = 0; q < CPL; ++q) a0[q] = ax[q] = ay[q] = az[q] = 0.f;
+        const int64_t beg = g.recv_off[i], end = g.recv_off[i + 1];
+        for (int64_t e = beg + warp; e < end; e += 4) {
+            const int64_t j = g.edge_index[2 * e + 1];
+            const float4 y = st.ysh[e];
+            const float* Re = R + e * (P * C);
+            const float* srow = (L == 0) ? w.s_t0 + int64_t(st.elem[j]) * C : st.s_t[L] + j * C;
+#pragma unroll
+            for (int q = 0; q < CPL; ++q) {
+                const int k = lane * CPL + q;
+                const float s = srow[k];
+                a0[q] = fmaf(Re[k], s, a0[q]);
+                const float m1 = Re[C + k] * s;
+                ax[q] = fmaf(m1, y.x, ax[q]);
+                ay[q] = fmaf(m1, y.y, ay[q]);
+                az[q] = fmaf(m1, y.z, az[q]);
+                if constexpr (P == 4) {
+                    const float vx = v_t[j * 3 * C + k], vy = v_t[j * 3 * C + C + k], vz = v_t[j * 3 * C + 2 * C + k];
+                    const float r2 = Re[2 * C + k], r3 = Re[3 * C + k];
+                    ax[q] = fmaf(r2, vx, ax[q]);
+                    ay[q] = fmaf(r2, vy, ay[q]);
+                    az[q] = fmaf(r2, vz, az[q]);
+                    a0[q] = fmaf(r3 * kIS3, (vx * y.x + vy * y.y) + vz * y.z, a0[q]);
+                }
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < CPL; ++q) {
+            const int k = lane * CPL + q;
+            s_part[warp][0][k] = a0[q];
+            s_part[warp][1][k] = ax[q];
+            s_part[warp][2][k] = ay[q];
+            s_part[warp][3][k] = az[q];
+        }
+        __syncthreads();
+        for (int idx = threadIdx.x; idx < 4 * C; idx += 128) {
+            const int comp = idx / C, k = idx % C;
+            const float v = ((s_part[0][comp][k] + s_part[1][comp][k]) + (s_part[2][comp][k] + s_part[3][comp][k])) *
+                            w.inv_avg;
+            if (comp == 0) st.A0[L][i * C + k] = v;
+            else st.A1[L][i * 3 * C + (comp - 1) * C + k] = v;
+        }
+        __syncthreads();
+    }
+}
+
+// ------------------------------------------------------------ node kernels
+//
+// A CTA of 4*C threads owns a group of kG = 4 same-element atoms. Channel
+// mixings [rows x C] . [C x C] split the reduction over c into 4 quarters
+// (thread (k, q) = output channel k, quarter q): each thread issues its 32
+// weight loads at once, so a matrix costs one L2 round trip; the quarters
+// are combined in a fixed order in shared memory. Elementwise phases use
+// thread (k, g) = channel k of atom g.
+
+constexpr int kGV = kG * 3;
+constexpr int kQ = 4;  // reduction quarters (== kG: the same threads serve both layouts)
+
+template <int C>
+struct NodeSmem {
+    float s[kG][C];             // scalar rows of the group
+    float v[kGV][C];            // vector rows (atom-major, component-minor)
+    float t[kG][C];
+    float tv[kGV][C];
+    float red[kQ][kG + kGV][C]; // quarter partials
+    float ra[32][C];            // readout weights (node_last)
+    float pre[kG][32];
+    float sc[kG][32];           // per-atom scalar reduction scratch
+};
+
+// outs[r][k] = sum_c xs[r][c] W0[c*C + k] (r < NS) and outv[r][k] = sum_c xv[r][c] W1[c*C + k]
+// (r < NV); out may alias x. All 4*C threads call it; it ends with a barrier.
+template <int C, int NS, int NV>
+__device__ __forceinline__ void mix_rows(const float (*xs)[C], const float* __restrict__ W0, const float (*xv)[C],
+                                         const float* __restrict__ W1, float (*outs)[C], float (*outv)[C],
+                                         float (*red)[kG + kGV][C]) {
+    constexpr int CQ = C / kQ;
+    const int k = threadIdx.x % C, q = threadIdx.x / C;
+    float acc[NS + NV];
+#pragma unroll
+    for (int r = 0; r < NS + NV; ++r) acc[r] = 0.f;
+#pragma unroll
+    for (int cc = 0; cc < CQ; ++cc) {
+        const int c = q * CQ + cc;
+        if constexpr (NS > 0) {
+            const float w0 = W0[c * C + k];
+#pragma unroll
+            for (int r = 0; r < NS; ++r) acc[r] = fmaf(xs[r][c], w0, acc[r]);
+        }
+        if constexpr (NV > 0) {
+            const float w1 = W1[c * C + k];
+#pragma unroll
+            for (int r = 0; r < NV; ++r) acc[NS + r] = fmaf(xv[r][c], w1, acc[NS + r]);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < NS + NV; ++r) red[q][r][k] = acc[r];
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < (NS + NV) * C; idx += kQ * C) {
+        const int r = idx / C, kk = idx % C;
+        const float y = (red[0][r][kk] + red[1][r][kk]) + (red[2][r][kk] + red[3][r][kk]);
+        if (r < NS) outs[r][kk] = y;
+        else outv[r - NS][kk] = y;
+    }
+    __syncthreads();
+}
+
+// sum over the C channels of atom g (threads g*C .. g*C+C-1), result returned to every thread of atom g
+template <int C>
+__device__ __forceinline__ float atom_sum(float x, float (*sc)[32]) {
+    const int g = threadIdx.x / C, k = threadIdx.x % C;
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) x += __shfl_xor_sync(0xffffffffu, x, d);
+    if ((k & 31) == 0) sc[g][k >> 5] = x;
+    __syncthreads();
+    float y = 0.f;
+    for (int wv = 0; wv < C / 32; ++wv) y += sc[g][wv];
+    __syncthreads();
+    return y;
+}
+
+__device__ __forceinline__ void group_atoms(const FusedState& st, int64_t grp, int (&atoms)[kG]) {
+#pragma unroll
+    for (int g = 0; g < kG; ++g) atoms[g] = st.groups[grp * kG + g];
+}
+
+// forward node update of a non-last layer L
+template <int C>
+__global__ void __launch_bounds__(kQ * C) node_fwd_kernel(FusedWeights w, FusedState st, int L) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    NodeSmem<C>& m = *reinterpret_cast<NodeSmem<C>*>(smem_raw);
+    const int k = threadIdx.x % C, g = threadIdx.x / C;
+    for (int64_t grp = blockIdx.x; grp < st.n_groups; grp += gridDim.x) {
+        int atoms[kG];
+        group_atoms(st, grp, atoms);
+        const int64_t z = st.elem[atoms[0]];
+        const int my = atoms[g];
+        const int64_t i = my < 0 ? atoms[0] : my;
+        __syncthreads();
+        m.s[g][k] = st.A0[L][i * C + k];
+#pragma unroll
+        for (int c = 0; c < 3; ++c) m.v[g * 3 + c][k] = st.A1[L][i * 3 * C + c * C + k];
+        if (L > 0) {
+            m.t[g][k] = st.s_out[L - 1][i * C + k];
+#pragma unroll
+            for (int c = 0; c < 3; ++c) m.tv[g * 3 + c][k] = st.v_out[L - 1][i * 3 * C + c * C + k];
+        }
+        __syncthreads();
+        mix_rows<C, kG, kGV>(m.s, w.lin0t[L], m.v, w.lin1t[L], m.s, m.v, m.red);
+        if (L > 0) mix_rows<C, kG, kGV>(m.t, w.skip0[L] + z * C * C, m.tv, w.skip1[L] + z * C * C, m.t, m.tv, m.red);
+        // symmetric contraction (thread (k, g))
+        const float aa = m.s[g][k];
+        const float vx = m.v[g * 3][k], vy = m.v[g * 3 + 1][k], vz = m.v[g * 3 + 2][k];
+        if (my >= 0) {
+            st.A0l[L][my * int64_t(C) + k] = aa;
+            st.A1l[L][my * int64_t(3 * C) + k] = vx;
+            st.A1l[L][my * int64_t(3 * C) + C + k] = vy;
+            st.A1l[L][my * int64_t(3 * C) + 2 * C + k] = vz;
+        }
+        const float* p0 = w.prod0[L] + z * 5 * C + k;
+        const float* p1 = w.prod1[L] + z * 4 * C + k;
+        const float q = (vx * vx + vy * vy) + vz * vz;
+        const float b0 = (((p0[0] * aa + p0[C] * aa * aa) + p0[2 * C] * q) + p0[3 * C] * aa * aa * aa) + p0[4 * C] * aa * q;
+        const float cc = ((p1[0] + p1[C] * aa) + p1[2 * C] * aa * aa) + p1[3 * C] * q;
+        __syncthreads();
+        m.s[g][k] = b0;
+        m.v[g * 3][k] = cc * vx;
+        m.v[g * 3 + 1][k] = cc * vy;
+        m.v[g * 3 + 2][k] = cc * vz;
+        __syncthreads();
+        mix_rows<C, kG, kGV>(m.s, w.out0t[L], m.v, w.out1t[L], m.s, m.v, m.red);
+        float so = m.s[g][k];
+        float vo[3] = {m.v[g * 3][k], m.v[g * 3 + 1][k], m.v[g * 3 + 2][k]};
+        if (L > 0) {
+            so += m.t[g][k];
+#pragma unroll
+            for (int c = 0; c < 3; ++c) vo[c] += m.tv[g * 3 + c][k];
+        }
+        if (my >= 0) {
+            st.s_out[L][my * int64_t(C) + k] = so;
+#pragma unroll
+            for (int c = 0; c < 3; ++c) st.v_out[L][my * int64_t(3 * C) + c * C + k] = vo[c];
+        }
+        if (L == 0) {  // readout of layer 0: e_term0 = s . r0
+            const float e = atom_sum<C>(so * w.r0[k], m.sc);
+            if (k == 0 && my >= 0) st.e_term0[my] = e;
+        }
+        __syncthreads();
+        m.s[g][k] = so;
+#pragma unroll
+        for (int c = 0; c < 3; ++c) m.v[g * 3 + c][k] = vo[c];
+        __syncthreads();
+        // the next layer's up-mixing
+        mix_rows<C, kG, kGV>(m.s, w.up0t[L + 1], m.v, w.up1t[L + 1], m.s, m.v, m.red);
+        if (my >= 0) {
+            st.s_t[L + 1][my * int64_t(C) + k] = m.s[g][k];
+#pragma unroll
+            for (int c = 0; c < 3; ++c) st.v_t[L + 1][my * int64_t(3 * C) + c * C + k] = m.v[g * 3 + c][k];
+        }
+    }
+}
+
+// the last layer: node update, readout, node energies, and the backward to dA(L)
+template <int C>
+__global__ void __launch_bounds__(kQ * C) node_last_kernel(FusedWeights w, FusedState st, int L) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    NodeSmem<C>& m = *reinterpret_cast<NodeSmem<C>*>(smem_raw);
+    const int k = threadIdx.x % C, g = threadIdx.x / C;
+    const int RH = w.readout_hidden;
+    for (int idx = threadIdx.x; idx < RH * C; idx += kQ * C) m.ra[idx / C][idx % C] = w.ra[idx];
+    for (int64_t grp = blockIdx.x; grp < st.n_groups; grp += gridDim.x) {
+        int atoms[kG];
+        group_atoms(st, grp, atoms);
+        const int64_t z = st.elem[atoms[0]];
+        const int my = atoms[g];
+        const int64_t i = my < 0 ? atoms[0] : my;
+        __syncthreads();
+        m.s[g][k] = st.A0[L][i * C + k];
+#pragma unroll
+        for (int c = 0; c < 3; ++c) m.v[g * 3 + c][k] = st.A1[L][i * 3 * C + c * C + k];
+        m.t[g][k] = L > 0 ? st.s_out[L - 1][i * C + k] : 0.f;
+        __syncthreads();
+        mix_rows<C, kG, kGV>(m.s, w.lin0t[L], m.v, w.lin1t[L], m.s, m.v, m.red);
+        if (L > 0) mix_rows<C, kG, 0>(m.t, w.skip0[L] + z * C * C, nullptr, nullptr, m.t, nullptr, m.red);
+        const float aa = m.s[g][k];
+        const float vx = m.v[g * 3][k], vy = m.v[g * 3 + 1][k], vz = m.v[g * 3 + 2][k];
+        const float q = (vx * vx + vy * vy) + vz * vz;
+        const float* p0 = w.prod0[L] + z * 5 * C + k;
+        const float b0 = (((p0[0] * aa + p0[C] * aa * aa) + p0[2 * C] * q) + p0[3 * C] * aa * aa * aa) + p0[4 * C] * aa * q;
+        __syncthreads();
+        m.s[g][k] = b0;
+        __syncthreads();
+        mix_rows<C, kG, 0>(m.s, w.out0t[L], nullptr, nullptr, m.s, nullptr, m.red);
+        const float so = m.s[g][k] + (L > 0 ? m.t[g][k] : 0.f);
+        float e0_term = 0.f;
+        if (L == 0) e0_term = atom_sum<C>(so * w.r0[k], m.sc);  // a one-layer model: readout 0 as well
+        __syncthreads();
+        m.s[g][k] = so;
+        __syncthreads();
+        // readout MLP: pre_j = s . ra_j
+        for (int idx = threadIdx.x; idx < kG * RH; idx += kQ * C) {
+            const int gg = idx / RH, j = idx % RH;
+            float acc = 0.f;
+            for (int c = 0; c < C; ++c) acc = fmaf(m.s[gg][c], m.ra[j][c], acc);
+            m.pre[gg][j] = acc;
+        }
+        __syncthreads();
+        if (k == 0 && my >= 0) {
+            float e1 = 0.f;
+            for (int j = 0; j < RH; ++j) e1 = fmaf(w.rb[j], silu_f(m.pre[g][j]), e1);
+            const float et = L > 0 ? st.e_term0[my] : e0_term;
+            st.node_energy[my] = w.e0[z] + w.scale * (double(et) + double(e1)) + w.shift;
+        }
+        // ---- backward: ds = scale * sum_j rb[j] silu'(pre_j) ra[j] (+ scale * r0 for a one-layer model)
+        const float sc = float(w.scale);
+        float acc = 0.f;
+        for (int j = 0; j < RH; ++j) acc = fmaf(w.rb[j] * silu_g(m.pre[g][j]), m.ra[j][k], acc);
+        float ds = sc * acc;
+        if (L == 0) ds = fmaf(sc, w.r0[k], ds);
+        __syncthreads();
+        m.t[g][k] = ds;
+        __syncthreads();
+        if (L > 0) {
+            mix_rows<C, kG, 0>(m.t, w.skip0t[L] + z * C * C, nullptr, nullptr, m.v, nullptr, m.red);
+            if (my >= 0) st.ds_skip[L][my * int64_t(C) + k] = m.v[g][k];
+        }
+        mix_rows<C, kG, 0>(m.t, w.out0[L], nullptr, nullptr, m.t, nullptr, m.red);
+        const float db0 = m.t[g][k];
+        const float gq = db0 * (p0[2 * C] + p0[4 * C] * aa);
+        const float da = db0 * (((p0[0] + 2.f * p0[C] * aa) + 3.f * p0[3 * C] * aa * aa) + p0[4 * C] * q);
+        __syncthreads();
+        m.s[g][k] = da;
+        m.v[g * 3][k] = 2.f * gq * vx;
+        m.v[g * 3 + 1][k] = 2.f * gq * vy;
+        m.v[g * 3 + 2][k] = 2.f * gq * vz;
+        __syncthreads();
+        mix_rows<C, kG, kGV>(m.s, w.lin0[L], m.v, w.lin1[L], m.s, m.v, m.red);
+        if (my >= 0) {
+            st.dA0[L][my * int64_t(C) + k] = m.s[g][k];
+#pragma unroll
+            for (int c = 0; c < 3; ++c) st.dA1[L][my * int64_t(3 * C) + c * C + k] = m.v[g * 3 + c][k];
+        }
+    }
+}
+
+// per receiver run: dR(l) and dY (warp per edge, lane channels; dY accumulated over layers)
+template <int C, int P>
+__global__ void __launch_bounds__(128) msg_bwd_edge_kernel(GraphArgs g, FusedWeights w, FusedState st, int L,
+                                                           int accumulate_dy) {
+    constexpr int CPL = C / 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float* R = st.R[L];
+    float* dR = st.dR[L];
+    for (int64_t i = blockIdx.x; i < g.n_atoms; i += gridDim.x) {
+        float g0[CPL], gx[CPL], gy[CPL], gz[CPL];
+#pragma unroll
+        for (int q = 0; q < CPL; ++q) {
+            const int k = lane * CPL + q;
+            g0[q] = st.dA0[L][i * C + k] * w.inv_avg;
+            gx[q] = st.dA1[L][i * 3 * C + k] * w.inv_avg;
+            gy[q] = st.dA1[L][i * 3 * C + C + k] * w.inv_avg;
+            gz[q] = st.dA1[L][i * 3 * C + 2 * C + k] * w.inv_avg;
+        }
+        const int64_t beg = g.recv_off[i], end = g.recv_off[i + 1];
+        for (int64_t e = beg + warp; e < end; e += 4) {
+            const int64_t j = g.edge_index[2 * e + 1];
+            const float4 y = st.ysh[e];
+            const float* Re = R + e * (P * C);
+            float* dRe = dR + e * (P * C);
+            const float* srow = (L == 0) ? w.s_t0 + int64_t(st.elem[j]) * C : st.s_t[L] + j * C;
+            float px = 0.f, py = 0.f, pz = 0.f;
+#pragma unroll
+            for (int q = 0; q < CPL; ++q) {
+                const int k = lane * CPL + q;
+                const float s = srow[k];
+                const float gdy = (gx[q] * y.x + gy[q] * y.y) + gz[q] * y.z;
+                dRe[k] = g0[q] * s;
+                dRe[C + k] = s * gdy;
+                const float c1 = Re[C + k] * s;
+                px = fmaf(c1, gx[q], px);
+                py = fmaf(c1, gy[q], py);
+                pz = fmaf(c1, gz[q], pz);
+                if constexpr (P == 4) {
+                    const float* vrow = st.v_t[L] + j * 3 * C;
+                    const float vx = vrow[k], vy = vrow[C + k], vz = vrow[2 * C + k];
+                    dRe[2 * C + k] = (gx[q] * vx + gy[q] * vy) + gz[q] * vz;
+                    dRe[3 * C + k] = g0[q] * ((vx * y.x + vy * y.y) + vz * y.z) * kIS3;
+                    const float c3 = Re[3 * C + k] * g0[q] * kIS3;
+                    px = fmaf(c3, vx, px);
+                    py = fmaf(c3, vy, py);
+                    pz = fmaf(c3, vz, pz);
+                }
+            }
+#pragma unroll
+            for (int d = 16; d > 0; d >>= 1) {
+                px += __shfl_xor_sync(0xffffffffu, px, d);
+                py += __shfl_xor_sync(0xffffffffu, py, d);
+                pz += __shfl_xor_sync(0xffffffffu, pz, d);
+            }
+            if (lane == 0) {
+                float* out = st.dY + 3 * e;
+                if (accumulate_dy) {
+                    out[0] += px;
+                    out[1] += py;
+                    out[2] += pz;
+                } else {
+                    out[0] = px;
+                    out[1] = py;
+                    out[2] = pz;
+                }
+            }
+        }
+    }
+}
+
+// per sender: the gathered rows' gradient of layer L (ds_t, dv_t), the up-mixing backward into
+// layer L-1's outputs, and layer L-1's node backward (to dA(L-1)). One atom group per CTA; the
+// C threads of atom g reduce its sender run (warps over edges).
+template <int C>
+__global__ void __launch_bounds__(kQ * C) sender_node_kernel(GraphArgs gr, FusedWeights w, FusedState st, int L) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    NodeSmem<C>& m = *reinterpret_cast<NodeSmem<C>*>(smem_raw);
+    constexpr int CPL = C / 32, NW = C / 32;  // warps per atom
+    const int k = threadIdx.x % C, g = threadIdx.x / C;
+    const int lane = threadIdx.x & 31, wa = k >> 5;  // warp index within the atom
+    const int P = 4;
+    const float* R = st.R[L];
+    const int Lp = L - 1;
+    for (int64_t grp = blockIdx.x; grp < st.n_groups; grp += gridDim.x) {
+        int atoms[kG];
+        group_atoms(st, grp, atoms);
+        const int64_t z = st.elem[atoms[0]];
+        const int my = atoms[g];
+        const int64_t j = my < 0 ? atoms[0] : my;
+        float ds[CPL], dx[CPL], dy[CPL], dz[CPL];
+#pragma unroll
+        for (int qq = 0; qq < CPL; ++qq) ds[qq] = dx[qq] = dy[qq] = dz[qq] = 0.f;
+        for (int64_t t = gr.send_off[j] + wa; t < gr.send_off[j + 1]; t += NW) {
+            const int64_t e = gr.send_perm[t];
+            const int64_t i = gr.edge_index[2 * e];
+            const float4 y = st.ysh[e];
+            const float* Re = R + e * (P * C);
+#pragma unroll
+            for (int qq = 0; qq < CPL; ++qq) {
+                const int kk = lane * CPL + qq;
+                const float g0 = st.dA0[L][i * C + kk] * w.inv_avg;
+                const float gx = st.dA1[L][i * 3 * C + kk] * w.inv_avg;
+                const float gy = st.dA1[L][i * 3 * C + C + kk] * w.inv_avg;
+                const float gz = st.dA1[L][i * 3 * C + 2 * C + kk] * w.inv_avg;
+                ds[qq] = fmaf(Re[kk], g0, ds[qq]);
+                ds[qq] = fmaf(Re[C + kk], (gx * y.x + gy * y.y) + gz * y.z, ds[qq]);
+                const float r2 = Re[2 * C + kk], r3 = Re[3 * C + kk] * g0 * kIS3;
+                dx[qq] = fmaf(r2, gx, fmaf(r3, y.x, dx[qq]));
+                dy[qq] = fmaf(r2, gy, fmaf(r3, y.y, dy[qq]));
+                dz[qq] = fmaf(r2, gz, fmaf(r3, y.z, dz[qq]));
+            }
+        }
+        __syncthreads();
+        // warp partials of atom g -> red[g-th quarter block] (reuse red as [warp][4][C] per atom)
+#pragma unroll
+        for (int qq = 0; qq < CPL; ++qq) {
+            const int kk = lane * CPL + qq;
+            m.red[g][wa * 4 + 0][kk] = ds[qq];
+            m.red[g][wa * 4 + 1][kk] = dx[qq];
+            m.red[g][wa * 4 + 2][kk] = dy[qq];
+            m.red[g][wa * 4 + 3][kk] = dz[qq];
+        }
+        __syncthreads();
+        {
+            float sum[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int wv = 0; wv < NW; ++wv)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) sum[c] += m.red[g][wv * 4 + c][k];
+            m.s[g][k] = sum[0];
+#pragma unroll
+            for (int c = 0; c < 3; ++c) m.v[g * 3 + c][k] = sum[1 + c];
+        }
+        __syncthreads();
+        // up-mixing backward into layer Lp's outputs, plus the skip and readout parts
+        mix_rows<C, kG, kGV>(m.s, w.up0[L], m.v, w.up1[L], m.s, m.v, m.red);
+        float dsi = m.s[g][k];
+        float dvi[3] = {m.v[g * 3][k], m.v[g * 3 + 1][k], m.v[g * 3 + 2][k]};
+        if (st.ds_skip[L]) dsi += st.ds_skip[L][j * C + k];
+        if (st.dv_skip[L])
+#pragma unroll
+            for (int c = 0; c < 3; ++c) dvi[c] += st.dv_skip[L][j * 3 * C + c * C + k];
+        if (Lp == 0) dsi = fmaf(float(w.scale), w.r0[k], dsi);  // layer 0 feeds the linear readout
+        __syncthreads();
+        m.t[g][k] = dsi;
+#pragma unroll
+        for (int c = 0; c < 3; ++c) m.tv[g * 3 + c][k] = dvi[c];
+        __syncthreads();
+        // layer Lp: out-mixing backward (into s/v) and skip backward (t/tv in place)
+        mix_rows<C, kG, kGV>(m.t, w.out0[Lp], m.tv, w.out1[Lp], m.s, m.v, m.red);
+        if (Lp > 0) {
+            mix_rows<C, kG, kGV>(m.t, w.skip0t[Lp] + z * C * C, m.tv, w.skip1t[Lp] + z * C * C, m.t, m.tv, m.red);
+            if (my >= 0) {
+                st.ds_skip[Lp][my * int64_t(C) + k] = m.t[g][k];
+#pragma unroll
+                for (int c = 0; c < 3; ++c) st.dv_skip[Lp][my * int64_t(3 * C) + c * C + k] = m.tv[g * 3 + c][k];
+            }
+        }
+        // product backward
+        const float* p0 = w.prod0[Lp] + z * 5 * C + k;
+        const float* p1 = w.prod1[Lp] + z * 4 * C + k;
+        const float aa = st.A0l[Lp][j * C + k];
+        const float vx = st.A1l[Lp][j * 3 * C + k], vy = st.A1l[Lp][j * 3 * C + C + k],
+                    vz = st.A1l[Lp][j * 3 * C + 2 * C + k];
+        const float q = (vx * vx + vy * vy) + vz * vz;
+        const float db0 = m.s[g][k];
+        const float bx = m.v[g * 3][k], by = m.v[g * 3 + 1][k], bz = m.v[g * 3 + 2][k];
+        float ga = db0 * (((p0[0] + 2.f * p0[C] * aa) + 3.f * p0[3 * C] * aa * aa) + p0[4 * C] * q);
+        float gq = db0 * (p0[2 * C] + p0[4 * C] * aa);
+        const float cc = ((p1[0] + p1[C] * aa) + p1[2 * C] * aa * aa) + p1[3 * C] * q;
+        const float bv = (bx * vx + by * vy) + bz * vz;
+        ga += bv * (p1[C] + 2.f * p1[2 * C] * aa);
+        gq += bv * p1[3 * C];
+        __syncthreads();
+        m.s[g][k] = ga;
+        m.v[g * 3][k] = cc * bx + 2.f * gq * vx;
+        m.v[g * 3 + 1][k] = cc * by + 2.f * gq * vy;
+        m.v[g * 3 + 2][k] = cc * bz + 2.f * gq * vz;
+        __syncthreads();
+        mix_rows<C, kG, kGV>(m.s, w.lin0[Lp], m.v, w.lin1[Lp], m.s, m.v, m.red);
+        if (my >= 0) {
+            st.dA0[Lp][my * int64_t(C) + k] = m.s[g][k];
+#pragma unroll
+            for (int c = 0; c < 3; ++c) st.dA1[Lp][my * int64_t(3 * C) + c * C + k] = m.v[g * 3 + c][k];
+        }
+    }
+}
+
+// ---------------------------------------------------------------- edge backward
+
+struct EdgeBwdSmem {
+    float phi[kTB][17];
+    float dphi[kTB][17];
+    float h[2][kTB][kH + 1];    // h1, h2 (post-activation)
+    float p[3][kTB][kH + 1];    // pre-activations
+    float g[2][kTB][kH + 1];    // gradient ping-pong
+    float w1[16][kH];
+    float w2[kH][kH + 1];
+    float w3[kH][kH + 1];
+    float dR[kTB][kMaxPC];      // the tile's dR rows
+    float red[4][kTB][kH];      // quarter partials of dR . W4
+};
+
+// the radial MLP backward of every layer (the forward recomputed from the distances) and the
+// geometry backward: g_r [E][3] = dE/dr_e. dR . W4 splits its reduction over 4 thread quarters.
+__global__ void __launch_bounds__(256) edge_bwd_kernel(EdgeArgs a, FusedWeights w, FusedState st) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    EdgeBwdSmem& m = *reinterpret_cast<EdgeBwdSmem*>(smem_raw);
+    const int t = threadIdx.x;
+    const float pref = sqrtf(2.0f / w.r_max);
+    const int64_t n_tiles = (a.n_edges + kTB - 1) / kTB;
+    for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+        const int64_t e0 = tile * kTB;
+        const int ne = int(a.n_edges - e0 < kTB ? a.n_edges - e0 : kTB);
+        __syncthreads();
+        if (t < kTB) {
+            const int64_t e = e0 + t;
+            const float d = t < ne ? st.ysh[e].w : 0.f;
+            float f, df;
+            cutoff_poly(d, w.r_max, w.poly_p, f, df);
+            const float inv = d > 0.f ? 1.0f / d : 0.f;
+            for (int n = 0; n < w.n_basis; ++n) {
+                const float k = float(n + 1) * 3.14159265358979323846f / w.r_max;
+                m.phi[t][n] = d > 0.f ? pref * sinf(k * d) * inv * f : 0.f;
+                m.dphi[t][n] = 0.f;
+            }
+        }
+        for (int L = 0; L < w.n_layers; ++L) {
+            const int PC = (L == 0 ? 2 : 4) * a.C;
+            __syncthreads();
+            stage_radial(m.w1, m.w2, m.w3, w, L, 256);
+            // the tile's dR rows, coalesced
+            const float* dR = st.dR[L];
+            for (int idx = t; idx < kTB * PC; idx += 256) {
+                const int e = idx / PC, n = idx % PC;
+                m.dR[e][n] = e < ne ? dR[(e0 + e) * PC + n] : 0.f;
+            }
+            __syncthreads();
+            // forward recompute
+            for (int idx = t; idx < kTB * kH; idx += 256) {
+                const int e = idx / kH, k = idx % kH;
+                float acc = 0.f;
+                for (int n = 0; n < w.n_basis; ++n) acc = fmaf(m.phi[e][n], m.w1[n][k], acc);
+                m.p[0][e][k] = acc;
+                m.h[0][e][k] = silu_f(acc);
+            }
+            __syncthreads();
+            for (int idx = t; idx < kTB * kH; idx += 256) {
+                const int e = idx / kH, k = idx % kH;
+                float acc = 0.f;
+#pragma unroll 16
+                for (int c = 0; c < kH; ++c) acc = fmaf(m.h[0][e][c], m.w2[c][k], acc);
+                m.p[1][e][k] = acc;
+                m.h[1][e][k] = silu_f(acc);
+            }
+            __syncthreads();
+            for (int idx = t; idx < kTB * kH; idx += 256) {
+                const int e = idx / kH, k = idx % kH;
+                float acc = 0.f;
+#pragma unroll 16
+                for (int c = 0; c < kH; ++c) acc = fmaf(m.h[1][e][c], m.w3[c][k], acc);
+                m.p[2][e][k] = acc;
+            }
+            // dh3 = dR . W4 (W4 [P*C][64]): thread (k, quarter)
+            {
+                const int k = t % kH, qt = t / kH;
+                const int nq = PC / 4;
+                float acc[kTB];
+#pragma unroll
+                for (int e = 0; e < kTB; ++e) acc[e] = 0.f;
+                const float* W4 = w.w4[L];
+#pragma unroll 16
+                for (int nn = 0; nn < nq; ++nn) {
+                    const int n = qt * nq + nn;
+                    const float wv = W4[n * kH + k];
+#pragma unroll
+                    for (int e = 0; e < kTB; ++e) acc[e] = fmaf(m.dR[e][n], wv, acc[e]);
+                }
+#pragma unroll
+                for (int e = 0; e < kTB; ++e) m.red[qt][e][k] = acc[e];
+            }
+            __syncthreads();
+            for (int idx = t; idx < kTB * kH; idx += 256) {
+                const int e = idx / kH, k = idx % kH;
+                const float gsum = (m.red[0][e][k] + m.red[1][e][k]) + (m.red[2][e][k] + m.red[3][e][k]);
+                m.g[0][e][k] = gsum * silu_g(m.p[2][e][k]);
+            }
+            __syncthreads();
+            // dh2 = g3 . W3 (W3[c][k] = W3^T[k][c], the staged rows)
+            for (int idx = t; idx < kTB * kH; idx += 256) {
+                const int e = idx / kH, k = idx % kH;
+                float acc = 0.f;
+#pragma unroll 16
+                for (int c = 0; c < kH; ++c) acc = fmaf(m.g[0][e][c], m.w3[k][c], acc);
+                m.g[1][e][k] = acc * silu_g(m.p[1][e][k]);
+            }
+            __syncthreads();
+            for (int idx = t; idx < kTB * kH; idx += 256) {
+                const int e = idx / kH, k = idx % kH;
+                float acc = 0.f;
+#pragma unroll 16
+                for (int c = 0; c < kH; ++c) acc = fmaf(m.g[1][e][c], m.w2[k][c], acc);
+                m.g[0][e][k] = acc * silu_g(m.p[0][e][k]);
+            }
+            __syncthreads();
+            // dphi += g1 . W1 (W1[c][n] = W1^T[n][c])
+            for (int idx = t; idx < kTB * w.n_basis; idx += 256) {
+                const int e = idx / w.n_basis, n = idx % w.n_basis;
+                float acc = 0.f;
+#pragma unroll 16
+                for (int c = 0; c < kH; ++c) acc = fmaf(m.g[0][e][c], m.w1[n][c], acc);
+                m.dphi[e][n] += acc;
+            }
+        }
+        __syncthreads();
+        // geometry backward of each edge
+        if (t < ne) {
+            const int64_t e = e0 + t;
+            const float4 y = st.ysh[e];
+            const float d = y.w;
+            float gx = 0.f, gy = 0.f, gz = 0.f;
+            if (d > 0.f) {
+                const float inv = 1.0f / d;
+                const float ux = y.x * kIS3, uy = y.y * kIS3, uz = y.z * kIS3;
+                const float* gyv = st.dY + 3 * e;
+                const float gu = (gyv[0] * ux + gyv[1] * uy) + gyv[2] * uz;
+                gx = kS3 * (gyv[0] - gu * ux) * inv;
+                gy = kS3 * (gyv[1] - gu * uy) * inv;
+                gz = kS3 * (gyv[2] - gu * uz) * inv;
+                float f, df;
+                cutoff_poly(d, w.r_max, w.poly_p, f, df);
+                float gd = 0.f;
+                for (int n = 0; n < w.n_basis; ++n) {
+                    const float k = float(n + 1) * 3.14159265358979323846f / w.r_max;
+                    float sn, cs;
+                    sincosf(k * d, &sn, &cs);
+                    const float b = pref * sn * inv;
+                    const float db = pref * (k * cs * d - sn) * inv * inv;
+                    gd += m.dphi[t][n] * (db * f + b * df);
+                }
+                gx += gd * ux;
+                gy += gd * uy;
+                gz += gd * uz;
+            }
+            st.g_r[3 * e] = gx;
+            st.g_r[3 * e + 1] = gy;
+            st.g_r[3 * e + 2] = gz;
+        }
+    }
+}
+
+// forces F_a = sum over received edges of g_r - sum over sent edges of g_r, and the energies
+__global__ void forces_kernel(GraphArgs g, const float* __restrict__ g_r, const double* __restrict__ node_energy,
+                              int64_t atoms_per_system, float* __restrict__ forces, double* __restrict__ total) {
+    __shared__ double s_part[32];
+    const int64_t sys = blockIdx.x;
+    double acc_e = 0.0;
+    for (int64_t t = threadIdx.x; t < atoms_per_system * 3; t += blockDim.x) {
+        const int64_t a = sys * atoms_per_system + t / 3;
+        const int c = int(t % 3);
+        float f = 0.f;
+        for (int64_t e = g.recv_off[a]; e < g.recv_off[a + 1]; ++e) f += g_r[3 * e + c];
+        for (int64_t s = g.send_off[a]; s < g.send_off[a + 1]; ++s) f -= g_r[3 * int64_t(g.send_perm[s]) + c];
+        forces[3 * a + c] = f;
+        if (c == 0) acc_e += node_energy[a];
+    }
+    for (int d = 16; d > 0; d >>= 1) acc_e += __shfl_xor_sync(0xffffffffu, acc_e, d);
+    if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = acc_e;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double s = 0.0;
+        for (int wv = 0; wv < (int)(blockDim.x >> 5); ++wv) s += s_part[wv];
+        total[sys] = s;
+    }
+}
+
+// dynamic shared memory granted per kernel (raised once, before any capture of the same size)
+static size_t g_granted[8] = {};
+
+inline fmd_status grant(const void* kernel, size_t bytes, int slot) {
+    if (bytes <= 48 * 1024 || bytes <= g_granted[slot]) return FMD_OK;
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+    if (err != cudaSuccess) return record_cuda_error(err);
+    g_granted[slot] = bytes;
+    return FMD_OK;
+}
+
+template <int C>
+fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeights& w, const FusedState& st,
+                       int64_t atoms_per_system, int32_t n_systems, float* forces, double* total, cudaStream_t s) {
+    const int64_t n_tiles = (ea.n_edges + kTE - 1) / kTE;
+    const int edge_grid = int(n_tiles < int64_t(kNumSMs) * 8 ? n_tiles : int64_t(kNumSMs) * 8);
+    const int atom_grid = int(ga.n_atoms < int64_t(kNumSMs) * 16 ? ga.n_atoms : int64_t(kNumSMs) * 16);
+    const int group_grid = int(st.n_groups < int64_t(kNumSMs) * 16 ? st.n_groups : int64_t(kNumSMs) * 16);
+    const int64_t b_tiles = (ea.n_edges + kTB - 1) / kTB;
+    const int bwd_grid = int(b_tiles < int64_t(kNumSMs) * 8 ? b_tiles : int64_t(kNumSMs) * 8);
+    const size_t node_smem = sizeof(NodeSmem<C>);
+    const int slot = C == 32 ? 0 : (C == 64 ? 1 : 2);
+    fmd_status stt;
+    if ((stt = grant((const void*)edge_fwd_kernel, sizeof(EdgeFwdSmem), 3)) != FMD_OK) return stt;
+    if ((stt = grant((const void*)edge_bwd_kernel, sizeof(EdgeBwdSmem), 4)) != FMD_OK) return stt;
+    if ((stt = grant((const void*)node_fwd_kernel<C>, node_smem, slot)) != FMD_OK) return stt;
+    // the three node kernels share one NodeSmem size: grant each (slot bookkeeping per kernel family)
+    {
+        static size_t last_granted[3] = {};
+        if (node_smem > 48 * 1024 && node_smem > last_granted[slot]) {
+            cudaError_t err = cudaFuncSetAttribute((const void*)node_last_kernel<C>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, int(node_smem));
+            if (err == cudaSuccess)
+                err = cudaFuncSetAttribute((const void*)sender_node_kernel<C>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, int(node_smem));
+            if (err != cudaSuccess) return record_cuda_error(err);
+            last_granted[slot] = node_smem;
+        }
+    }
+    const int L = w.n_layers;
+    if (n_tiles > 0) edge_fwd_kernel<<<edge_grid, 256, sizeof(EdgeFwdSmem), s>>>(ea, w, st);
+    for (int l = 0; l < L; ++l) {
+        if (l == 0) message_fused_kernel<C, 2><<<atom_grid, 128, 0, s>>>(ga, w, st, l);
+        else message_fused_kernel<C, 4><<<atom_grid, 128, 0, s>>>(ga, w, st, l);
+        if (l < L - 1) node_fwd_kernel<C><<<group_grid, kQ * C, node_smem, s>>>(w, st, l);
+    }
+    node_last_kernel<C><<<group_grid, kQ * C, node_smem, s>>>(w, st, L - 1);
+    for (int l = L - 1; l >= 1; --l) {
+        msg_bwd_edge_kernel<C, 4><<<atom_grid, 128, 0, s>>>(ga, w, st, l, l != L - 1);
+        sender_node_kernel<C><<<group_grid, kQ * C, node_smem, s>>>(ga, w, st, l);
+    }
+    msg_bwd_edge_kernel<C, 2><<<atom_grid, 128, 0, s>>>(ga, w, st, 0, L != 1);
+    if (b_tiles > 0) edge_bwd_kernel<<<bwd_grid, 256, sizeof(EdgeBwdSmem), s>>>(ea, w, st);
+    forces_kernel<<<n_systems, 256, 0, s>>>(ga, st.g_r, st.node_energy, atoms_per_system, forces, total);
+    return check_launch();
+}
+
+}  // namespace fmd
+
+using namespace fmd;
+
+extern "C" {
+
+fmd_status fmd_mace_fused_step(const fmd_mace_fused_weights* weights, const fmd_mace_fused_state* state,
+                               const float* positions, const float* cell, const int32_t* edge_index,
+                               const float* edge_image, int64_t n_edges, const int64_t* recv_off,
+                               const int64_t* send_off, const int32_t* send_perm, int64_t atoms_per_system,
+                               int32_t n_systems, int32_t channels, float* forces, double* energy, void* stream) {
+    if (weights == nullptr || state == nullptr || positions == nullptr || cell == nullptr || edge_index == nullptr ||
+        edge_image == nullptr || recv_off == nullptr || send_off == nullptr || send_perm == nullptr ||
+        forces == nullptr || energy == nullptr || n_edges < 0 || atoms_per_system < 1 || n_systems < 1)
+        return FMD_ERR_INVALID_ARGUMENT;
+    FusedWeights w{};
+    FusedState st{};
+    const fmd_mace_fused_weights& h = *weights;
+    if (h.n_layers < 1 || h.n_layers > kMaxLayers || h.n_basis < 1 || h.n_basis > 16 || h.readout_hidden < 1 ||
+        h.readout_hidden > 32 || h.radial_hidden != kH)
+        return FMD_ERR_UNSUPPORTED;
+    for (int l = 0; l < h.n_layers; ++l) {
+        w.w1t[l] = h.radial_w1t[l]; w.w2t[l] = h.radial_w2t[l]; w.w3t[l] = h.radial_w3t[l]; w.w4t[l] = h.radial_w4t[l];
+        w.w1[l] = h.radial_w1[l]; w.w2[l] = h.radial_w2[l]; w.w3[l] = h.radial_w3[l]; w.w4[l] = h.radial_w4[l];
+        w.lin0[l] = h.lin0[l]; w.lin1[l] = h.lin1[l]; w.lin0t[l] = h.lin0t[l]; w.lin1t[l] = h.lin1t[l];
+        w.out0[l] = h.out0[l]; w.out1[l] = h.out1[l]; w.out0t[l] = h.out0t[l]; w.out1t[l] = h.out1t[l];
+        w.up0[l] = h.up0[l]; w.up1[l] = h.up1[l]; w.up0t[l] = h.up0t[l]; w.up1t[l] = h.up1t[l];
+        w.prod0[l] = h.prod0[l]; w.prod1[l] = h.prod1[l];
+        w.skip0[l] = h.skip0[l]; w.skip1[l] = h.skip1[l]; w.skip0t[l] = h.skip0t[l]; w.skip1t[l] = h.skip1t[l];
+        st.R[l] = state->R[l]; st.dR[l] = state->dR[l]; st.s_t[l] = state->s_t[l]; st.v_t[l] = state->v_t[l];
+        st.A0[l] = state->A0[l]; st.A1[l] = state->A1[l]; st.A0l[l] = state->A0l[l]; st.A1l[l] = state->A1l[l];
+        st.s_out[l] = state->s_out[l]; st.v_out[l] = state->v_out[l]; st.dA0[l] = state->dA0[l];
+        st.dA1[l] = state->dA1[l]; st.ds_skip[l] = state->ds_skip[l]; st.dv_skip[l] = state->dv_skip[l];
+    }
+    w.s_t0 = h.s_t0; w.r0 = h.r0; w.ra = h.ra; w.rb = h.rb; w.e0 = h.e0;
+    w.scale = h.scale; w.shift = h.shift; w.n_layers = h.n_layers; w.n_basis = h.n_basis; w.poly_p = h.poly_p;
+    w.readout_hidden = h.readout_hidden; w.r_max = h.r_max; w.inv_avg = h.inv_avg;
+    st.ysh = reinterpret_cast<float4*>(state->ysh); st.dY = state->dY; st.g_r = state->g_r;
+    st.e_term0 = state->e_term0; st.node_energy = state->node_energy; st.elem = state->elem;
+    st.groups = state->groups; st.n_groups = state->n_groups;
+    if (!aligned16(state->ysh)) return FMD_ERR_INVALID_ARGUMENT;
+    const EdgeArgs ea{positions, cell, edge_index, edge_image, n_edges, channels};
+    const GraphArgs ga{edge_index, recv_off, send_off, send_perm, atoms_per_system * n_systems};
+    cudaStream_t s = as_stream(stream);
+    switch (channels) {
+        case 32: return launch_step<32>(ea, ga, w, st, atoms_per_system, n_systems, forces, energy, s);
+        case 64: return launch_step<64>(ea, ga, w, st, atoms_per_system, n_systems, forces, energy, s);
+        case 128: return launch_step<128>(ea, ga, w, st, atoms_per_system, n_systems, forces, energy, s);
+        default: return FMD_ERR_UNSUPPORTED;
+    }
+}
+
+}  // extern "C"

@@ -279,7 +279,8 @@ class MACEModel:
             P = c.paths(L)
             p = f"{L}."
             if L == 0:  # first readout: e0 = r0 . s
-                _gemm(d_term.view(N, 1), w["readout.0"], b[p + "ds"], trans_w=False, accumulate=not last, s=s)
+                # layer 0's output also feeds the linear readout (ds already holds its other uses)
+                _gemm(d_term.view(N, 1), w["readout.0"], b[p + "ds"], trans_w=False, accumulate=True, s=s)
             # out-linears
             _gemm(b[p + "ds"], w[p + "out0"], b[p + "dB0"], trans_w=False, s=s)
             if not last:
@@ -371,3 +372,174 @@ class _NodeEnergy(torch.autograd.Function):
         dpos = torch.empty(buf.n_atoms, 3, dtype=torch.float32, device=d_term.device)
         model.backward(ctx.batch, buf, d_term, out=dpos)
         return dpos.to(ctx.pos_dtype), None, None, None
+
+
+# --------------------------------------------------------------------------- fused step
+
+_L = 4  # FMD_MACE_MAX_LAYERS
+_FP = ctypes_fp = None
+
+
+def _struct_types():
+    import ctypes
+
+    P = ctypes.c_void_p
+    arr = P * _L
+
+    class FusedWeights(ctypes.Structure):
+        _fields_ = [(name, arr) for name in (
+            "radial_w1t", "radial_w2t", "radial_w3t", "radial_w4t", "radial_w1", "radial_w2", "radial_w3",
+            "radial_w4", "lin0", "lin1", "lin0t", "lin1t", "out0", "out1", "out0t", "out1t", "up0", "up1", "up0t",
+            "up1t", "prod0", "prod1", "skip0", "skip1", "skip0t", "skip1t")] + [
+            ("s_t0", P), ("r0", P), ("ra", P), ("rb", P), ("e0", P), ("scale", ctypes.c_double),
+            ("shift", ctypes.c_double), ("n_layers", ctypes.c_int32), ("n_basis", ctypes.c_int32),
+            ("poly_p", ctypes.c_int32), ("readout_hidden", ctypes.c_int32), ("radial_hidden", ctypes.c_int32),
+            ("r_max", ctypes.c_float), ("inv_avg", ctypes.c_float), ("_pad", ctypes.c_int32)]
+
+    class FusedState(ctypes.Structure):
+        _fields_ = [(name, arr) for name in (
+            "R", "dR", "s_t", "v_t", "A0", "A1", "A0l", "A1l", "s_out", "v_out", "dA0", "dA1", "ds_skip",
+            "dv_skip")] + [
+            ("ysh", P), ("dY", P), ("g_r", P), ("e_term0", P), ("node_energy", P), ("elem", P), ("groups", P),
+            ("n_groups", ctypes.c_int64)]
+
+    return FusedWeights, FusedState
+
+
+_FusedWeights, _FusedState = _struct_types()
+_lib.declare("fmd_mace_fused_step", [_lib.ctypes.POINTER(_FusedWeights), _lib.ctypes.POINTER(_FusedState),
+                                     *([_lib.c_void_p] * 4), _lib.c_int64, *([_lib.c_void_p] * 3), _lib.c_int64,
+                                     _lib.c_int32, _lib.c_int32, _lib.c_void_p, _lib.c_void_p, _lib.c_void_p])
+
+
+def _fused_weights(model: "MACEModel"):
+    """Device copies of the weights in the layouts the fused kernels read (built once)."""
+    c, w, dev = model.config, model.w, model.device
+    keep: dict[str, Tensor] = {}
+
+    def t(x):
+        return x.t().contiguous()
+
+    fw = _FusedWeights()
+    for L in range(c.num_interactions):
+        p = f"{L}."
+        for k in range(4):
+            keep[f"{p}w{k + 1}t"] = t(w[f"{p}radial.{k}"])
+            keep[f"{p}w{k + 1}"] = w[f"{p}radial.{k}"].contiguous()
+        for name in ("lin0", "lin1", "out0", "out1", "up0", "up1"):
+            if p + name in w:
+                keep[p + name] = w[p + name].contiguous()
+                keep[p + name + "t"] = t(w[p + name])
+        for name in ("skip0", "skip1"):
+            if p + name in w:
+                keep[p + name] = w[p + name].contiguous()
+                keep[p + name + "t"] = w[p + name].transpose(1, 2).contiguous()
+        for name in ("prod0", "prod1"):
+            if p + name in w:
+                keep[p + name] = w[p + name].contiguous()
+    # layer 0's up-mixing of the embedding, per element, with the GEMM of the unfused path
+    table = torch.empty(c.num_elements, c.channels, dtype=torch.float32, device=dev)
+    _gemm(w["embedding"], w["0.up0"], table, s=stream(dev))
+    keep["s_t0"] = table
+    keep["r0"] = w["readout.0"].reshape(-1).contiguous()
+    keep["ra"] = w["readout.1a"].contiguous()
+    keep["rb"] = w["readout.1b"].reshape(-1).contiguous()
+    keep["e0"] = w["e0"].contiguous()
+
+    def q(name):
+        return ptr(keep[name]) if name in keep else None
+
+    for L in range(c.num_interactions):
+        p = f"{L}."
+        for k in range(4):
+            getattr(fw, f"radial_w{k + 1}t")[L] = q(f"{p}w{k + 1}t")
+            getattr(fw, f"radial_w{k + 1}")[L] = q(f"{p}w{k + 1}")
+        for name in ("lin0", "lin1", "out0", "out1", "up0", "up1", "skip0", "skip1"):
+            getattr(fw, name)[L] = q(p + name)
+            getattr(fw, name + "t")[L] = q(p + name + "t")
+        fw.prod0[L] = q(p + "prod0")
+        fw.prod1[L] = q(p + "prod1")
+    fw.s_t0, fw.r0, fw.ra, fw.rb, fw.e0 = q("s_t0"), q("r0"), q("ra"), q("rb"), q("e0")
+    fw.scale, fw.shift = float(c.scale), float(c.shift)
+    fw.n_layers, fw.n_basis, fw.poly_p = c.num_interactions, c.num_bessel, c.poly_p
+    fw.readout_hidden, fw.radial_hidden = c.readout_hidden, c.radial_hidden[0]
+    fw.r_max, fw.inv_avg = float(c.r_max), float(1.0 / c.avg_num_neighbors)
+    if len(set(c.radial_hidden)) != 1 or c.radial_hidden[0] != 64:
+        raise ValueError("the fused step implements radial MLP widths (64, 64, 64)")
+    return fw, keep
+
+
+def element_groups(elements: np.ndarray, size: int = 4) -> np.ndarray:
+    """Atoms grouped by element, ``size`` per group (-1 padding): the node kernels' work units."""
+    groups = []
+    for z in np.unique(elements):
+        atoms = np.nonzero(elements == z)[0]
+        for start in range(0, atoms.size, size):
+            chunk = atoms[start:start + size]
+            groups.append(np.concatenate([chunk, np.full(size - chunk.size, -1)]))
+    return np.asarray(groups, dtype=np.int32).reshape(-1, size)
+
+
+class _FusedBuffers:
+    def __init__(self, model: "MACEModel", n_atoms: int, n_edges: int, elem: Tensor):
+        c, dev = model.config, model.device
+        C, N, E = c.channels, n_atoms, n_edges
+        z = lambda *s, dtype=torch.float32: torch.zeros(*s, dtype=dtype, device=dev)  # noqa: E731
+        self.t: dict[str, Tensor] = {}
+        st = _FusedState()
+        last = c.num_interactions - 1
+        for L in range(c.num_interactions):
+            P = c.paths(L)
+            for name, shape in (("R", (E, P * C)), ("dR", (E, P * C)), ("s_t", (N, C)), ("v_t", (N, 3, C)),
+                                ("A0", (N, C)), ("A1", (N, 3, C)), ("A0l", (N, C)), ("A1l", (N, 3, C)),
+                                ("s_out", (N, C)), ("v_out", (N, 3, C)), ("dA0", (N, C)), ("dA1", (N, 3, C))):
+                self.t[f"{L}.{name}"] = z(*shape)
+                getattr(st, name)[L] = ptr(self.t[f"{L}.{name}"])
+            if L > 0:
+                self.t[f"{L}.ds_skip"] = z(N, C)
+                st.ds_skip[L] = ptr(self.t[f"{L}.ds_skip"])
+                if L < last:
+                    self.t[f"{L}.dv_skip"] = z(N, 3, C)
+                    st.dv_skip[L] = ptr(self.t[f"{L}.dv_skip"])
+        for name, shape, dtype in (("ysh", (E, 4), torch.float32), ("dY", (E, 3), torch.float32),
+                                   ("g_r", (E, 3), torch.float32), ("e_term0", (N,), torch.float32),
+                                   ("node_energy", (N,), torch.float64), ("forces", (N, 3), torch.float32)):
+            self.t[name] = z(*shape, dtype=dtype)
+        groups = torch.from_numpy(element_groups(elem.cpu().numpy())).to(dev)
+        self.t["groups"] = groups
+        self.t["elem"] = elem
+        st.ysh, st.dY, st.g_r = ptr(self.t["ysh"]), ptr(self.t["dY"]), ptr(self.t["g_r"])
+        st.e_term0, st.node_energy = ptr(self.t["e_term0"]), ptr(self.t["node_energy"])
+        st.elem, st.groups, st.n_groups = ptr(elem), ptr(groups), int(groups.shape[0])
+        self.state = st
+        self.energy: dict[int, Tensor] = {}
+
+
+def _energy_forces_fused(self: "MACEModel", batch, n_systems: int = 1):
+    """(per-system fp64 energies [R], forces [N, 3] float32) of ``batch`` in the fused kernels
+    (``fmd_mace_fused_step``); the same mathematics as ``energy_forces``."""
+    if getattr(batch, "element", None) is None:
+        self.prepare(batch)
+    N, E = batch.positions.shape[0], batch.edge_index.shape[0]
+    if getattr(self, "_fused_w", None) is None:
+        self._fused_w = _fused_weights(self)
+        self._fused_bufs = {}
+    key = (N, E, ptr(batch.element))
+    buf = self._fused_bufs.get(key)
+    if buf is None:
+        buf = _FusedBuffers(self, N, E, batch.element)
+        self._fused_bufs[key] = buf
+    if n_systems not in buf.energy:
+        buf.energy[n_systems] = torch.zeros(n_systems, dtype=torch.float64, device=self.device)
+    energy, forces = buf.energy[n_systems], buf.t["forces"]
+    fw, _ = self._fused_w
+    import ctypes as _ct
+
+    call("fmd_mace_fused_step", _ct.byref(fw), _ct.byref(buf.state), ptr(batch.positions), ptr(batch.cell),
+         ptr(batch.edge_index), ptr(batch.edge_image), E, ptr(batch.recv_off), ptr(batch.send_off),
+         ptr(batch.send_perm), N // n_systems, n_systems, self.config.channels, ptr(forces), ptr(energy),
+         stream(self.device))
+    return energy, forces
+
+
+MACEModel.energy_forces_fused = _energy_forces_fused

@@ -38,10 +38,12 @@ class FixedCapacityOverflow(RuntimeError):
 
 class WholeStepGraphRunner:
     def __init__(self, *, model: MACEModel, builder: FixedCapacityGraphBuilder, integrator, steps_per_launch: int = 1,
-                 warmup: int = 3, proactive_refresh_fraction: float = 0.25) -> None:
+                 warmup: int = 3, proactive_refresh_fraction: float = 0.25, fused: bool = True) -> None:
         if steps_per_launch <= 0:
             raise ValueError("steps_per_launch must be positive")
         self.model, self.builder, self.integrator = model, builder, integrator
+        # the model evaluation of a step: the fused kernels (default) or the building blocks
+        self._evaluate = model.energy_forces_fused if fused else model.energy_forces
         self.steps_per_launch = int(steps_per_launch)
         self.warmup = int(warmup)
         self.proactive_refresh_fraction = float(proactive_refresh_fraction)
@@ -59,7 +61,7 @@ class WholeStepGraphRunner:
         self.refreshes += 1
         batch, _ = builder.build(integrator.positions32, rebuild_candidates=False)
         self.model.prepare(batch)
-        energy, forces = model.energy_forces(batch, n_systems=self.replicas)
+        energy, forces = self._evaluate(batch, n_systems=self.replicas)
         integrator.set_forces(forces, energy)
         flags = int(builder.flags.item())
         if flags & FLAG_EDGE_OVERFLOW:
@@ -77,7 +79,7 @@ class WholeStepGraphRunner:
         for _ in range(self.steps_per_launch):
             integ.step_pre_force()
             batch, _ = builder.build(integ.positions32, rebuild_candidates=False, flags=self.window_flags)
-            energy, forces = model.energy_forces(batch, n_systems=self.replicas)
+            energy, forces = self._evaluate(batch, n_systems=self.replicas)
             integ.step_post_force(forces, energy)
 
     def _capture(self) -> None:
@@ -153,7 +155,7 @@ class WholeStepGraphRunner:
                 flags = int(status.flags.item())
             if flags & _INVALID:
                 raise RuntimeError(f"invalid graph in an eager step (flags {flags})")
-            energy, forces = model.energy_forces(batch, n_systems=self.replicas)
+            energy, forces = self._evaluate(batch, n_systems=self.replicas)
             integ.step_post_force(forces, energy)
         self.eager_steps += self.steps_per_launch
 
@@ -167,7 +169,7 @@ class WholeStepGraphRunner:
         self.model.prepare(self.builder.batch)
         self.builder.refresh_candidates(self.integrator.positions32)
         batch, _ = self.builder.build(self.integrator.positions32, rebuild_candidates=False)
-        self.model.energy_forces(batch, n_systems=self.replicas)  # buffers of the new size, eagerly
+        self._evaluate(batch, n_systems=self.replicas)  # buffers of the new size, eagerly
         self.integrator.restore()
         self._capture()
         self.capacity_growths += 1
@@ -193,7 +195,7 @@ class GPUResidentMolecularDynamics:
     def __init__(self, model: MACEModel, *, positions, cell, atomic_numbers, masses, temperature_K: float,
                  timestep: float, tdamp: float, tchain: int = 3, tloop: int = 1, momenta=None, replicas: int = 1,
                  skin: float = 2.0, u_capacity: int | None = None, steps_per_launch: int = 10,
-                 device="cuda") -> None:
+                 fused: bool = True, device="cuda") -> None:
         self.device = torch.device(device)
         self.replicas = int(replicas)
         n = len(atomic_numbers)
@@ -218,7 +220,7 @@ class GPUResidentMolecularDynamics:
             self.integrator = ReplicaNoseHooverChainNVT(masses, positions, momenta, replicas=self.replicas, **kw)
         self.model = model
         self.runner = WholeStepGraphRunner(model=model, builder=self.builder, integrator=self.integrator,
-                                           steps_per_launch=steps_per_launch)
+                                           steps_per_launch=steps_per_launch, fused=fused)
         self.runner.on_resize = self._resized
         self.n_atoms = n
         self.steps_done = 0

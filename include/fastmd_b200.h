@@ -336,6 +336,106 @@ FMD_API fmd_status fmd_mace_node_energy(const float* e_terms, int32_t n_terms, i
 FMD_API fmd_status fmd_mace_node_energy_bwd(const double* d_total, double scale, int64_t n_atoms,
                                             int32_t n_systems, float* d_term, void* stream);
 
+/* The whole MACE-architecture energy and force evaluation of one step in ~10
+ * fused kernels (the whole-step path; same mathematics as the fmd_mace_*
+ * building blocks above). Weights are device pointers prepared once: the
+ * radial MLP (per layer, hidden width 64) as [in][out] ("t") and [out][in]
+ * copies, the channel mixings lin/out/up as [out][in] and [in][out] ("t"),
+ * the symmetric-contraction weights prod0 [Z][5][C] / prod1 [Z][4][C], the
+ * element skip matrices skip [Z][in][out] and skipt [Z][out][in], the
+ * up-mixed element embedding s_t0 [Z][C], the readouts r0 [C], ra [RH][C],
+ * rb [RH] and e0 [Z] (fp64). Pointers of absent pieces (layer 0's up and
+ * skip, the last layer's vector output) are NULL. */
+#define FMD_MACE_MAX_LAYERS 4
+typedef struct fmd_mace_fused_weights {
+    const float* radial_w1t[FMD_MACE_MAX_LAYERS];
+    const float* radial_w2t[FMD_MACE_MAX_LAYERS];
+    const float* radial_w3t[FMD_MACE_MAX_LAYERS];
+    const float* radial_w4t[FMD_MACE_MAX_LAYERS];
+    const float* radial_w1[FMD_MACE_MAX_LAYERS];
+    const float* radial_w2[FMD_MACE_MAX_LAYERS];
+    const float* radial_w3[FMD_MACE_MAX_LAYERS];
+    const float* radial_w4[FMD_MACE_MAX_LAYERS];
+    const float* lin0[FMD_MACE_MAX_LAYERS];
+    const float* lin1[FMD_MACE_MAX_LAYERS];
+    const float* lin0t[FMD_MACE_MAX_LAYERS];
+    const float* lin1t[FMD_MACE_MAX_LAYERS];
+    const float* out0[FMD_MACE_MAX_LAYERS];
+    const float* out1[FMD_MACE_MAX_LAYERS];
+    const float* out0t[FMD_MACE_MAX_LAYERS];
+    const float* out1t[FMD_MACE_MAX_LAYERS];
+    const float* up0[FMD_MACE_MAX_LAYERS];
+    const float* up1[FMD_MACE_MAX_LAYERS];
+    const float* up0t[FMD_MACE_MAX_LAYERS];
+    const float* up1t[FMD_MACE_MAX_LAYERS];
+    const float* prod0[FMD_MACE_MAX_LAYERS];
+    const float* prod1[FMD_MACE_MAX_LAYERS];
+    const float* skip0[FMD_MACE_MAX_LAYERS];
+    const float* skip1[FMD_MACE_MAX_LAYERS];
+    const float* skip0t[FMD_MACE_MAX_LAYERS];
+    const float* skip1t[FMD_MACE_MAX_LAYERS];
+    const float* s_t0;
+    const float* r0;
+    const float* ra;
+    const float* rb;
+    const double* e0;
+    double scale;
+    double shift;
+    int32_t n_layers;
+    int32_t n_basis;
+    int32_t poly_p;
+    int32_t readout_hidden;
+    int32_t radial_hidden;
+    float r_max;
+    float inv_avg;
+    int32_t _pad;
+} fmd_mace_fused_weights;
+
+/* Persistent activations of the fused step (caller-owned device buffers,
+ * sized for N atoms and E edge rows): per layer R/dR [E][P*C] (P = 2 for
+ * layer 0, else 4), s_t [N][C], v_t/A1/A1l/v_out/dA1/dv_skip [N][3][C],
+ * A0/A0l/s_out/dA0/ds_skip [N][C]; ysh [E][4] (16-byte aligned), dY and g_r
+ * [E][3], e_term0 [N], node_energy [N] (fp64), elem [N] (element rows) and
+ * groups [n_groups][4] (atom ids of the same element, -1 padding). */
+typedef struct fmd_mace_fused_state {
+    float* R[FMD_MACE_MAX_LAYERS];
+    float* dR[FMD_MACE_MAX_LAYERS];
+    float* s_t[FMD_MACE_MAX_LAYERS];
+    float* v_t[FMD_MACE_MAX_LAYERS];
+    float* A0[FMD_MACE_MAX_LAYERS];
+    float* A1[FMD_MACE_MAX_LAYERS];
+    float* A0l[FMD_MACE_MAX_LAYERS];
+    float* A1l[FMD_MACE_MAX_LAYERS];
+    float* s_out[FMD_MACE_MAX_LAYERS];
+    float* v_out[FMD_MACE_MAX_LAYERS];
+    float* dA0[FMD_MACE_MAX_LAYERS];
+    float* dA1[FMD_MACE_MAX_LAYERS];
+    float* ds_skip[FMD_MACE_MAX_LAYERS];
+    float* dv_skip[FMD_MACE_MAX_LAYERS];
+    float* ysh;
+    float* dY;
+    float* g_r;
+    float* e_term0;
+    double* node_energy;
+    const int32_t* elem;
+    const int32_t* groups;
+    int64_t n_groups;
+} fmd_mace_fused_state;
+
+/* Energies and forces of one step: geometry, radial MLPs, messages, node
+ * updates, the explicit backward and the force assembly
+ * F_a = sum_{received e} dE/dr_e - sum_{sent e} dE/dr_e over both CSRs.
+ * forces [N][3] float32, energy [n_systems] fp64 (deterministic sums).
+ * channels 32, 64 or 128. Replaces the energy-tap evaluation of the
+ * whole-step runner (whole_step_cuda_graph.py:256 _evaluate with
+ * fastmd/engine/energy_derivative.py:110 over mace.py:356). */
+FMD_API fmd_status fmd_mace_fused_step(const fmd_mace_fused_weights* weights, const fmd_mace_fused_state* state,
+                                       const float* positions, const float* cell, const int32_t* edge_index,
+                                       const float* edge_image, int64_t n_edges, const int64_t* recv_off,
+                                       const int64_t* send_off, const int32_t* send_perm, int64_t atoms_per_system,
+                                       int32_t n_systems, int32_t channels, float* forces, double* energy,
+                                       void* stream);
+
 /* -------------------------------------- Nose-Hoover chain integrator (F1/F3) */
 
 /* Flat fp64 state of R replicas of n atoms each and chain length M:

@@ -144,3 +144,37 @@ def test_forces_sum_to_zero_and_translation_invariance(cuda):
     e1, f1 = model.energy_forces(moved)
     assert abs(float(e1 - e0)) < 1e-9 * abs(float(e0)) + 2e-4
     _close(f1.cpu().numpy(), f0.cpu().numpy().astype(np.float64), 1e-4)
+
+
+@pytest.mark.parametrize("channels,layers,seed", [(128, 2, 0), (32, 3, 2), (64, 1, 3)])
+def test_fused_step_matches_fp64_oracle(cuda, channels, layers, seed):
+    from fastmd_b200.mace import MACEConfig, MACEModel
+
+    pos, cell, numbers, _ = _system(seed)
+    model = MACEModel(MACEConfig(channels=channels, num_interactions=layers), device=cuda, seed=seed + 1)
+    _, batch = _graph(pos, cell, numbers, cuda)
+    energy, forces = model.energy_forces_fused(batch)
+    E, F, _ = _oracle(model, batch, numbers)
+    _close(energy.cpu().numpy(), E, 1e-7)
+    _close(forces.cpu().numpy(), F)
+    e2, f2 = model.energy_forces_fused(batch)
+    assert torch.equal(e2, energy) and torch.equal(f2, forces)  # deterministic
+    eu, fu = model.energy_forces(batch)
+    _close(fu.cpu().numpy(), forces.cpu().numpy().astype(np.float64))
+
+
+def test_fused_replica_union_equals_single_systems(cuda):
+    from fastmd_b200.mace import MACEModel
+
+    R = 3
+    systems = [_system(seed) for seed in range(R)]
+    cell, numbers = systems[0][1], systems[0][2]
+    model = MACEModel(device=cuda)
+    _, batch = _graph(np.concatenate([s[0] for s in systems]), cell, numbers, cuda, replicas=R)
+    energy, forces = (x.clone() for x in model.energy_forces_fused(batch, n_systems=R))
+    N = numbers.size
+    for r, s in enumerate(systems):
+        _, single = _graph(s[0], cell, numbers, cuda)
+        e, f = model.energy_forces_fused(single)
+        assert torch.equal(energy[r:r + 1], e)
+        assert torch.equal(forces[r * N:(r + 1) * N], f)
