@@ -28,9 +28,9 @@ namespace fmd {
 
 constexpr int kMaxLayers = 4;
 constexpr int kH = 64;        // radial MLP width
-constexpr int kTE = 32;       // edges per tile of the forward edge kernel
+constexpr int kTF = 16;       // edges per tile of the forward edge kernel
 constexpr int kMaxPC = 512;   // P*C of a layer's radial output (C <= 128)
-constexpr int kTB = 16;       // edges per tile of the backward edge kernel (its activations fit 48 KB)
+constexpr int kTB = 16;       // edges per tile of the backward edge kernel
 constexpr int kG = 4;         // atoms per group of the node kernels
 constexpr float kS3 = 1.7320508075688772f;
 constexpr float kIS3 = 0.5773502691896258f;
@@ -128,43 +128,113 @@ struct EdgeArgs {
     const float* cell;
     const int32_t* edge_index;
     const float* edge_image;
-    int64_t n_edges;
+    int64_t n_edges;           // rows of the edge arrays
+    const int64_t* n_real;     // device count of the real rows (padding rows are skipped), or null
     int C;
 };
 
+constexpr int kHS = kH + 4;   // row stride of activation tiles (16-byte rows, broadcast float4 reads)
+constexpr int kWS = kH + 1;   // row stride of staged weights (conflict-free row and column walks)
+
 struct EdgeFwdSmem {
-    float phi[kTE][17];
-    float h[2][kTE][kH + 1];
+    float phi[kTF][16];
+    float h[2][kTF][kHS];
     float w1[16][kH];          // W1^T [basis][hidden]
-    float w2[kH][kH + 1];      // W2^T [in][out], rows padded (conflict-free either way)
-    float w3[kH][kH + 1];
+    float w2[kH][kWS];         // W2^T [in][out]
+    float w3[kH][kWS];
 };
 
-// stage one layer's radial weights W1^T, W2^T, W3^T in shared memory (coalesced, all threads)
-__device__ __forceinline__ void stage_radial(float (*w1)[kH], float (*w2)[kH + 1], float (*w3)[kH + 1],
-                                             const FusedWeights& w, int L, int nthreads) {
-    for (int idx = threadIdx.x; idx < w.n_basis * kH; idx += nthreads) w1[idx / kH][idx % kH] = w.w1t[L][idx];
-    for (int idx = threadIdx.x; idx < kH * kH; idx += nthreads) {
-        w2[idx / kH][idx % kH] = w.w2t[L][idx];
-        w3[idx / kH][idx % kH] = w.w3t[L][idx];
+// stage one layer's radial weights W1^T, W2^T, W3^T in shared memory (float4 loads, unrolled)
+__device__ __forceinline__ void stage_radial(float (*w1)[kH], float (*w2)[kWS], float (*w3)[kWS],
+                                             const FusedWeights& w, int L) {
+    const float4* g2 = reinterpret_cast<const float4*>(w.w2t[L]);
+    const float4* g3 = reinterpret_cast<const float4*>(w.w3t[L]);
+#pragma unroll
+    for (int r = 0; r < kH * kH / 4 / 256; ++r) {
+        const int idx = threadIdx.x + 256 * r;  // float4 index
+        const float4 a = g2[idx], b = g3[idx];
+        const int row = (idx * 4) / kH, col = (idx * 4) % kH;
+        w2[row][col] = a.x; w2[row][col + 1] = a.y; w2[row][col + 2] = a.z; w2[row][col + 3] = a.w;
+        w3[row][col] = b.x; w3[row][col + 1] = b.y; w3[row][col + 2] = b.z; w3[row][col + 3] = b.w;
+    }
+    for (int idx = threadIdx.x; idx < w.n_basis * kH; idx += 256) w1[idx / kH][idx % kH] = w.w1t[L][idx];
+}
+
+// out[e][k] = act(sum_c in[e][c] W[c][k]) for the tile (thread k = t % 64, 4 edge groups)
+template <int TE, bool ACT>
+__device__ __forceinline__ void hidden_layer(const float (*in)[kHS], const float (*W)[kWS], float (*out)[kHS],
+                                             float (*pre)[kHS]) {
+    constexpr int EPG = TE / 4;
+    const int k = threadIdx.x % kH, eg = threadIdx.x / kH;
+    float acc[EPG];
+#pragma unroll
+    for (int m = 0; m < EPG; ++m) acc[m] = 0.f;
+#pragma unroll 4
+    for (int c = 0; c < kH; c += 4) {
+        const float w0 = W[c][k], w1 = W[c + 1][k], w2 = W[c + 2][k], w3 = W[c + 3][k];
+#pragma unroll
+        for (int m = 0; m < EPG; ++m) {
+            const float4 x = *reinterpret_cast<const float4*>(&in[eg * EPG + m][c]);
+            acc[m] = fmaf(x.x, w0, acc[m]);
+            acc[m] = fmaf(x.y, w1, acc[m]);
+            acc[m] = fmaf(x.z, w2, acc[m]);
+            acc[m] = fmaf(x.w, w3, acc[m]);
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < EPG; ++m) {
+        if (pre) pre[eg * EPG + m][k] = acc[m];
+        out[eg * EPG + m][k] = ACT ? silu_f(acc[m]) : acc[m];
     }
 }
 
-// geometry, radial features and the radial MLP of every layer for one 32-edge tile; the hidden
-// layers read their weights from shared memory, the output layer streams W4^T from L2
+__device__ __forceinline__ int64_t real_edges(const EdgeArgs& a) {
+    const int64_t n = a.n_real ? *a.n_real : a.n_edges;
+    return n < a.n_edges ? n : a.n_edges;
+}
+
+// R[e][n] = sum_c h3[e][c] W4^T[c][n] for one tile, PC columns (thread columns t, t+256, ...)
+template <int PC>
+__device__ __forceinline__ void radial_out(const float (*h)[kHS], const float* __restrict__ w4t, float* __restrict__ R,
+                                           int64_t e0, int ne) {
+#pragma unroll
+    for (int n = threadIdx.x; n < PC; n += 256) {
+        float acc[kTF];
+#pragma unroll
+        for (int e = 0; e < kTF; ++e) acc[e] = 0.f;
+#pragma unroll 4
+        for (int c = 0; c < kH; c += 4) {
+            const float w0 = w4t[(c + 0) * PC + n], w1 = w4t[(c + 1) * PC + n];
+            const float w2 = w4t[(c + 2) * PC + n], w3 = w4t[(c + 3) * PC + n];
+#pragma unroll
+            for (int e = 0; e < kTF; ++e) {
+                const float4 x = *reinterpret_cast<const float4*>(&h[e][c]);
+                acc[e] = fmaf(x.x, w0, fmaf(x.y, w1, fmaf(x.z, w2, fmaf(x.w, w3, acc[e]))));
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < kTF; ++e)
+            if (e < ne) R[(e0 + e) * PC + n] = acc[e];
+    }
+}
+
+// geometry, radial features and the radial MLP of every layer for one 16-edge tile
+template <int C>
 __global__ void __launch_bounds__(256) edge_fwd_kernel(EdgeArgs a, FusedWeights w, FusedState st) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     EdgeFwdSmem& m = *reinterpret_cast<EdgeFwdSmem*>(smem_raw);
     const int t = threadIdx.x;
     const float pref = sqrtf(2.0f / w.r_max);
-    const int64_t n_tiles = (a.n_edges + kTE - 1) / kTE;
+    const int64_t n_edges = real_edges(a);
+    const int64_t n_tiles = (n_edges + kTF - 1) / kTF;
     for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-        const int64_t e0 = tile * kTE;
+        const int64_t e0 = tile * kTF;
+        const int ne = int(n_edges - e0 < kTF ? n_edges - e0 : kTF);
         __syncthreads();
-        if (t < kTE) {
+        if (t < kTF) {
             const int64_t e = e0 + t;
             float d = 0.f;
-            if (e < a.n_edges) {
+            if (t < ne) {
                 const int64_t i = a.edge_index[2 * e], j = a.edge_index[2 * e + 1];
                 const float ix = a.edge_image[3 * e], iy = a.edge_image[3 * e + 1], iz = a.edge_image[3 * e + 2];
                 const float* c = a.cell;
@@ -184,47 +254,22 @@ __global__ void __launch_bounds__(256) edge_fwd_kernel(EdgeArgs a, FusedWeights 
             }
         }
         for (int L = 0; L < w.n_layers; ++L) {
-            const int PC = (L == 0 ? 2 : 4) * a.C;
             __syncthreads();
-            stage_radial(m.w1, m.w2, m.w3, w, L, 256);
+            stage_radial(m.w1, m.w2, m.w3, w, L);
             __syncthreads();
-            for (int idx = t; idx < kTE * kH; idx += 256) {
+            for (int idx = t; idx < kTF * kH; idx += 256) {
                 const int e = idx / kH, k = idx % kH;
                 float acc = 0.f;
                 for (int n = 0; n < w.n_basis; ++n) acc = fmaf(m.phi[e][n], m.w1[n][k], acc);
                 m.h[0][e][k] = silu_f(acc);
             }
             __syncthreads();
-            for (int idx = t; idx < kTE * kH; idx += 256) {
-                const int e = idx / kH, k = idx % kH;
-                float acc = 0.f;
-#pragma unroll 16
-                for (int c = 0; c < kH; ++c) acc = fmaf(m.h[0][e][c], m.w2[c][k], acc);
-                m.h[1][e][k] = silu_f(acc);
-            }
+            hidden_layer<kTF, true>(m.h[0], m.w2, m.h[1], nullptr);
             __syncthreads();
-            for (int idx = t; idx < kTE * kH; idx += 256) {
-                const int e = idx / kH, k = idx % kH;
-                float acc = 0.f;
-#pragma unroll 16
-                for (int c = 0; c < kH; ++c) acc = fmaf(m.h[1][e][c], m.w3[c][k], acc);
-                m.h[0][e][k] = silu_f(acc);
-            }
+            hidden_layer<kTF, true>(m.h[1], m.w3, m.h[0], nullptr);
             __syncthreads();
-            for (int n = t; n < PC; n += 256) {
-                float acc[kTE];
-#pragma unroll
-                for (int e = 0; e < kTE; ++e) acc[e] = 0.f;
-#pragma unroll 16
-                for (int c = 0; c < kH; ++c) {
-                    const float wv = w.w4t[L][c * PC + n];
-#pragma unroll
-                    for (int e = 0; e < kTE; ++e) acc[e] = fmaf(m.h[0][e][c], wv, acc[e]);
-                }
-#pragma unroll
-                for (int e = 0; e < kTE; ++e)
-                    if (e0 + e < a.n_edges) st.R[L][(e0 + e) * PC + n] = acc[e];
-            }
+            if (L == 0) radial_out<2 * C>(m.h[0], w.w4t[L], st.R[L], e0, ne);
+            else radial_out<4 * C>(m.h[0], w.w4t[L], st.R[L], e0, ne);
         }
     }
 }
@@ -725,33 +770,93 @@ __global__ void __launch_bounds__(kQ * C) sender_node_kernel(GraphArgs gr, Fused
 // ---------------------------------------------------------------- edge backward
 
 struct EdgeBwdSmem {
-    float phi[kTB][17];
-    float dphi[kTB][17];
-    float h[2][kTB][kH + 1];    // h1, h2 (post-activation)
-    float p[3][kTB][kH + 1];    // pre-activations
-    float g[2][kTB][kH + 1];    // gradient ping-pong
+    float phi[kTB][16];
+    float dphi[kTB][16];
+    float h[2][kTB][kHS];       // h1, h2 (post-activation)
+    float p[3][kTB][kHS];       // pre-activations
+    float g[2][kTB][kHS];       // gradient ping-pong
     float w1[16][kH];
-    float w2[kH][kH + 1];
-    float w3[kH][kH + 1];
+    float w2[kH][kWS];
+    float w3[kH][kWS];
     float dR[kTB][kMaxPC];      // the tile's dR rows
     float red[4][kTB][kH];      // quarter partials of dR . W4
 };
 
+// dh3[e][k] = sum_n dR[e][n] W4[n][k]: thread (k, quarter of n), float4 broadcast reads of dR
+template <int PC>
+__device__ __forceinline__ void radial_out_bwd(const float (*dR)[kMaxPC], const float* __restrict__ W4,
+                                               float (*red)[kTB][kH]) {
+    constexpr int NQ = PC / 4;
+    const int k = threadIdx.x % kH, qt = threadIdx.x / kH;
+    float acc[kTB];
+#pragma unroll
+    for (int e = 0; e < kTB; ++e) acc[e] = 0.f;
+#pragma unroll 4
+    for (int nn = 0; nn < NQ; nn += 4) {
+        const int n = qt * NQ + nn;
+        const float w0 = W4[(n + 0) * kH + k], w1 = W4[(n + 1) * kH + k];
+        const float w2 = W4[(n + 2) * kH + k], w3 = W4[(n + 3) * kH + k];
+#pragma unroll
+        for (int e = 0; e < kTB; ++e) {
+            const float4 x = *reinterpret_cast<const float4*>(&dR[e][n]);
+            acc[e] = fmaf(x.x, w0, fmaf(x.y, w1, fmaf(x.z, w2, fmaf(x.w, w3, acc[e]))));
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < kTB; ++e) red[qt][e][k] = acc[e];
+}
+
+// stage the tile's dR rows (float4, unrolled)
+template <int PC>
+__device__ __forceinline__ void stage_dr(float (*dst)[kMaxPC], const float* __restrict__ dR, int64_t e0, int ne) {
+    constexpr int V = kTB * PC / 4 / 256;  // float4 per thread
+#pragma unroll
+    for (int r = 0; r < V; ++r) {
+        const int idx = threadIdx.x + 256 * r;
+        const int e = (idx * 4) / PC, n = (idx * 4) % PC;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (e < ne) v = reinterpret_cast<const float4*>(dR + (e0 + e) * PC)[n / 4];
+        *reinterpret_cast<float4*>(&dst[e][n]) = v;
+    }
+}
+
+// out[e][k] = (sum_c g[e][c] W[k][c]) * silu'(pre[e][k]) (the transpose walk of a staged W^T)
+__device__ __forceinline__ void hidden_bwd(const float (*g)[kHS], const float (*W)[kWS], const float (*pre)[kHS],
+                                           float (*out)[kHS]) {
+    constexpr int EPG = kTB / 4;
+    const int k = threadIdx.x % kH, eg = threadIdx.x / kH;
+    float acc[EPG];
+#pragma unroll
+    for (int m = 0; m < EPG; ++m) acc[m] = 0.f;
+#pragma unroll 4
+    for (int c = 0; c < kH; c += 4) {
+        const float w0 = W[k][c], w1 = W[k][c + 1], w2 = W[k][c + 2], w3 = W[k][c + 3];
+#pragma unroll
+        for (int m = 0; m < EPG; ++m) {
+            const float4 x = *reinterpret_cast<const float4*>(&g[eg * EPG + m][c]);
+            acc[m] = fmaf(x.x, w0, fmaf(x.y, w1, fmaf(x.z, w2, fmaf(x.w, w3, acc[m]))));
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < EPG; ++m) out[eg * EPG + m][k] = acc[m] * silu_g(pre[eg * EPG + m][k]);
+}
+
 // the radial MLP backward of every layer (the forward recomputed from the distances) and the
-// geometry backward: g_r [E][3] = dE/dr_e. dR . W4 splits its reduction over 4 thread quarters.
+// geometry backward: g_r [E][3] = dE/dr_e
+template <int C>
 __global__ void __launch_bounds__(256) edge_bwd_kernel(EdgeArgs a, FusedWeights w, FusedState st) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     EdgeBwdSmem& m = *reinterpret_cast<EdgeBwdSmem*>(smem_raw);
     const int t = threadIdx.x;
     const float pref = sqrtf(2.0f / w.r_max);
-    const int64_t n_tiles = (a.n_edges + kTB - 1) / kTB;
+    const int64_t n_edges = real_edges(a);
+    const int64_t n_tiles = (n_edges + kTB - 1) / kTB;
     for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
         const int64_t e0 = tile * kTB;
-        const int ne = int(a.n_edges - e0 < kTB ? a.n_edges - e0 : kTB);
+        const int ne = int(n_edges - e0 < kTB ? n_edges - e0 : kTB);
         __syncthreads();
         if (t < kTB) {
-            const int64_t e = e0 + t;
-            const float d = t < ne ? st.ysh[e].w : 0.f;
+            const float d = t < ne ? st.ysh[e0 + t].w : 0.f;
             float f, df;
             cutoff_poly(d, w.r_max, w.poly_p, f, df);
             const float inv = d > 0.f ? 1.0f / d : 0.f;
@@ -762,15 +867,10 @@ __global__ void __launch_bounds__(256) edge_bwd_kernel(EdgeArgs a, FusedWeights 
             }
         }
         for (int L = 0; L < w.n_layers; ++L) {
-            const int PC = (L == 0 ? 2 : 4) * a.C;
             __syncthreads();
-            stage_radial(m.w1, m.w2, m.w3, w, L, 256);
-            // the tile's dR rows, coalesced
-            const float* dR = st.dR[L];
-            for (int idx = t; idx < kTB * PC; idx += 256) {
-                const int e = idx / PC, n = idx % PC;
-                m.dR[e][n] = e < ne ? dR[(e0 + e) * PC + n] : 0.f;
-            }
+            stage_radial(m.w1, m.w2, m.w3, w, L);
+            if (L == 0) stage_dr<2 * C>(m.dR, st.dR[L], e0, ne);
+            else stage_dr<4 * C>(m.dR, st.dR[L], e0, ne);
             __syncthreads();
             // forward recompute
             for (int idx = t; idx < kTB * kH; idx += 256) {
@@ -781,40 +881,11 @@ __global__ void __launch_bounds__(256) edge_bwd_kernel(EdgeArgs a, FusedWeights 
                 m.h[0][e][k] = silu_f(acc);
             }
             __syncthreads();
-            for (int idx = t; idx < kTB * kH; idx += 256) {
-                const int e = idx / kH, k = idx % kH;
-                float acc = 0.f;
-#pragma unroll 16
-                for (int c = 0; c < kH; ++c) acc = fmaf(m.h[0][e][c], m.w2[c][k], acc);
-                m.p[1][e][k] = acc;
-                m.h[1][e][k] = silu_f(acc);
-            }
+            hidden_layer<kTB, true>(m.h[0], m.w2, m.h[1], m.p[1]);
             __syncthreads();
-            for (int idx = t; idx < kTB * kH; idx += 256) {
-                const int e = idx / kH, k = idx % kH;
-                float acc = 0.f;
-#pragma unroll 16
-                for (int c = 0; c < kH; ++c) acc = fmaf(m.h[1][e][c], m.w3[c][k], acc);
-                m.p[2][e][k] = acc;
-            }
-            // dh3 = dR . W4 (W4 [P*C][64]): thread (k, quarter)
-            {
-                const int k = t % kH, qt = t / kH;
-                const int nq = PC / 4;
-                float acc[kTB];
-#pragma unroll
-                for (int e = 0; e < kTB; ++e) acc[e] = 0.f;
-                const float* W4 = w.w4[L];
-#pragma unroll 16
-                for (int nn = 0; nn < nq; ++nn) {
-                    const int n = qt * nq + nn;
-                    const float wv = W4[n * kH + k];
-#pragma unroll
-                    for (int e = 0; e < kTB; ++e) acc[e] = fmaf(m.dR[e][n], wv, acc[e]);
-                }
-#pragma unroll
-                for (int e = 0; e < kTB; ++e) m.red[qt][e][k] = acc[e];
-            }
+            hidden_layer<kTB, false>(m.h[1], m.w3, m.g[1], m.p[2]);  // only the pre-activation is kept
+            if (L == 0) radial_out_bwd<2 * C>(m.dR, w.w4[L], m.red);
+            else radial_out_bwd<4 * C>(m.dR, w.w4[L], m.red);
             __syncthreads();
             for (int idx = t; idx < kTB * kH; idx += 256) {
                 const int e = idx / kH, k = idx % kH;
@@ -822,22 +893,9 @@ __global__ void __launch_bounds__(256) edge_bwd_kernel(EdgeArgs a, FusedWeights 
                 m.g[0][e][k] = gsum * silu_g(m.p[2][e][k]);
             }
             __syncthreads();
-            // dh2 = g3 . W3 (W3[c][k] = W3^T[k][c], the staged rows)
-            for (int idx = t; idx < kTB * kH; idx += 256) {
-                const int e = idx / kH, k = idx % kH;
-                float acc = 0.f;
-#pragma unroll 16
-                for (int c = 0; c < kH; ++c) acc = fmaf(m.g[0][e][c], m.w3[k][c], acc);
-                m.g[1][e][k] = acc * silu_g(m.p[1][e][k]);
-            }
+            hidden_bwd(m.g[0], m.w3, m.p[1], m.g[1]);
             __syncthreads();
-            for (int idx = t; idx < kTB * kH; idx += 256) {
-                const int e = idx / kH, k = idx % kH;
-                float acc = 0.f;
-#pragma unroll 16
-                for (int c = 0; c < kH; ++c) acc = fmaf(m.g[1][e][c], m.w2[k][c], acc);
-                m.g[0][e][k] = acc * silu_g(m.p[0][e][k]);
-            }
+            hidden_bwd(m.g[1], m.w2, m.p[0], m.g[0]);
             __syncthreads();
             // dphi += g1 . W1 (W1[c][n] = W1^T[n][c])
             for (int idx = t; idx < kTB * w.n_basis; idx += 256) {
@@ -849,7 +907,6 @@ __global__ void __launch_bounds__(256) edge_bwd_kernel(EdgeArgs a, FusedWeights 
             }
         }
         __syncthreads();
-        // geometry backward of each edge
         if (t < ne) {
             const int64_t e = e0 + t;
             const float4 y = st.ysh[e];
@@ -911,7 +968,7 @@ __global__ void forces_kernel(GraphArgs g, const float* __restrict__ g_r, const 
 }
 
 // dynamic shared memory granted per kernel (raised once, before any capture of the same size)
-static size_t g_granted[8] = {};
+static size_t g_granted[16] = {};
 
 inline fmd_status grant(const void* kernel, size_t bytes, int slot) {
     if (bytes <= 48 * 1024 || bytes <= g_granted[slot]) return FMD_OK;
@@ -924,7 +981,7 @@ inline fmd_status grant(const void* kernel, size_t bytes, int slot) {
 template <int C>
 fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeights& w, const FusedState& st,
                        int64_t atoms_per_system, int32_t n_systems, float* forces, double* total, cudaStream_t s) {
-    const int64_t n_tiles = (ea.n_edges + kTE - 1) / kTE;
+    const int64_t n_tiles = (ea.n_edges + kTF - 1) / kTF;
     const int edge_grid = int(n_tiles < int64_t(kNumSMs) * 8 ? n_tiles : int64_t(kNumSMs) * 8);
     const int atom_grid = int(ga.n_atoms < int64_t(kNumSMs) * 16 ? ga.n_atoms : int64_t(kNumSMs) * 16);
     const int group_grid = int(st.n_groups < int64_t(kNumSMs) * 16 ? st.n_groups : int64_t(kNumSMs) * 16);
@@ -933,8 +990,8 @@ fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeigh
     const size_t node_smem = sizeof(NodeSmem<C>);
     const int slot = C == 32 ? 0 : (C == 64 ? 1 : 2);
     fmd_status stt;
-    if ((stt = grant((const void*)edge_fwd_kernel, sizeof(EdgeFwdSmem), 3)) != FMD_OK) return stt;
-    if ((stt = grant((const void*)edge_bwd_kernel, sizeof(EdgeBwdSmem), 4)) != FMD_OK) return stt;
+    if ((stt = grant((const void*)edge_fwd_kernel<C>, sizeof(EdgeFwdSmem), 3 + 2 * slot)) != FMD_OK) return stt;
+    if ((stt = grant((const void*)edge_bwd_kernel<C>, sizeof(EdgeBwdSmem), 4 + 2 * slot)) != FMD_OK) return stt;
     if ((stt = grant((const void*)node_fwd_kernel<C>, node_smem, slot)) != FMD_OK) return stt;
     // the three node kernels share one NodeSmem size: grant each (slot bookkeeping per kernel family)
     {
@@ -950,7 +1007,7 @@ fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeigh
         }
     }
     const int L = w.n_layers;
-    if (n_tiles > 0) edge_fwd_kernel<<<edge_grid, 256, sizeof(EdgeFwdSmem), s>>>(ea, w, st);
+    if (n_tiles > 0) edge_fwd_kernel<C><<<edge_grid, 256, sizeof(EdgeFwdSmem), s>>>(ea, w, st);
     for (int l = 0; l < L; ++l) {
         if (l == 0) message_fused_kernel<C, 2><<<atom_grid, 128, 0, s>>>(ga, w, st, l);
         else message_fused_kernel<C, 4><<<atom_grid, 128, 0, s>>>(ga, w, st, l);
@@ -962,7 +1019,7 @@ fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeigh
         sender_node_kernel<C><<<group_grid, kQ * C, node_smem, s>>>(ga, w, st, l);
     }
     msg_bwd_edge_kernel<C, 2><<<atom_grid, 128, 0, s>>>(ga, w, st, 0, L != 1);
-    if (b_tiles > 0) edge_bwd_kernel<<<bwd_grid, 256, sizeof(EdgeBwdSmem), s>>>(ea, w, st);
+    if (b_tiles > 0) edge_bwd_kernel<C><<<bwd_grid, 256, sizeof(EdgeBwdSmem), s>>>(ea, w, st);
     forces_kernel<<<n_systems, 256, 0, s>>>(ga, st.g_r, st.node_energy, atoms_per_system, forces, total);
     return check_launch();
 }
@@ -975,7 +1032,8 @@ extern "C" {
 
 fmd_status fmd_mace_fused_step(const fmd_mace_fused_weights* weights, const fmd_mace_fused_state* state,
                                const float* positions, const float* cell, const int32_t* edge_index,
-                               const float* edge_image, int64_t n_edges, const int64_t* recv_off,
+                               const float* edge_image, int64_t n_edges, const int64_t* n_real_edges,
+                               const int64_t* recv_off,
                                const int64_t* send_off, const int32_t* send_perm, int64_t atoms_per_system,
                                int32_t n_systems, int32_t channels, float* forces, double* energy, void* stream) {
     if (weights == nullptr || state == nullptr || positions == nullptr || cell == nullptr || edge_index == nullptr ||
@@ -1008,7 +1066,7 @@ fmd_status fmd_mace_fused_step(const fmd_mace_fused_weights* weights, const fmd_
     st.e_term0 = state->e_term0; st.node_energy = state->node_energy; st.elem = state->elem;
     st.groups = state->groups; st.n_groups = state->n_groups;
     if (!aligned16(state->ysh)) return FMD_ERR_INVALID_ARGUMENT;
-    const EdgeArgs ea{positions, cell, edge_index, edge_image, n_edges, channels};
+    const EdgeArgs ea{positions, cell, edge_index, edge_image, n_edges, n_real_edges, channels};
     const GraphArgs ga{edge_index, recv_off, send_off, send_perm, atoms_per_system * n_systems};
     cudaStream_t s = as_stream(stream);
     switch (channels) {

@@ -408,7 +408,7 @@ def _struct_types():
 
 _FusedWeights, _FusedState = _struct_types()
 _lib.declare("fmd_mace_fused_step", [_lib.ctypes.POINTER(_FusedWeights), _lib.ctypes.POINTER(_FusedState),
-                                     *([_lib.c_void_p] * 4), _lib.c_int64, *([_lib.c_void_p] * 3), _lib.c_int64,
+                                     *([_lib.c_void_p] * 4), _lib.c_int64, *([_lib.c_void_p] * 4), _lib.c_int64,
                                      _lib.c_int32, _lib.c_int32, _lib.c_void_p, _lib.c_void_p, _lib.c_void_p])
 
 
@@ -536,7 +536,7 @@ def _energy_forces_fused(self: "MACEModel", batch, n_systems: int = 1):
     import ctypes as _ct
 
     call("fmd_mace_fused_step", _ct.byref(fw), _ct.byref(buf.state), ptr(batch.positions), ptr(batch.cell),
-         ptr(batch.edge_index), ptr(batch.edge_image), E, ptr(batch.recv_off), ptr(batch.send_off),
+         ptr(batch.edge_index), ptr(batch.edge_image), E, ptr(batch.n_edges), ptr(batch.recv_off), ptr(batch.send_off),
          ptr(batch.send_perm), N // n_systems, n_systems, self.config.channels, ptr(forces), ptr(energy),
          stream(self.device))
     return energy, forces

@@ -426,12 +426,15 @@ typedef struct fmd_mace_fused_state {
  * updates, the explicit backward and the force assembly
  * F_a = sum_{received e} dE/dr_e - sum_{sent e} dE/dr_e over both CSRs.
  * forces [N][3] float32, energy [n_systems] fp64 (deterministic sums).
+ * n_real_edges (device int64, may be NULL): the count of real rows; the
+ * padding rows after it are skipped by the edge kernels.
  * channels 32, 64 or 128. Replaces the energy-tap evaluation of the
  * whole-step runner (whole_step_cuda_graph.py:256 _evaluate with
  * fastmd/engine/energy_derivative.py:110 over mace.py:356). */
 FMD_API fmd_status fmd_mace_fused_step(const fmd_mace_fused_weights* weights, const fmd_mace_fused_state* state,
                                        const float* positions, const float* cell, const int32_t* edge_index,
-                                       const float* edge_image, int64_t n_edges, const int64_t* recv_off,
+                                       const float* edge_image, int64_t n_edges, const int64_t* n_real_edges,
+                                       const int64_t* recv_off,
                                        const int64_t* send_off, const int32_t* send_perm, int64_t atoms_per_system,
                                        int32_t n_systems, int32_t channels, float* forces, double* energy,
                                        void* stream);
