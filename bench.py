@@ -51,6 +51,7 @@ def _args():
     p.add_argument("--replicas", type=int, default=1, help="135-atom replicas per GPU")
     p.add_argument("--steps-per-launch", type=int, default=10)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-ops", action="store_true", help="skip the config-2 op microbenchmark")
     return p.parse_args()
 
 
@@ -267,6 +268,12 @@ def _ours(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = _cpu_baseline()
+    ops = None
+    if rank == 0 and world == 1 and not args.no_ops:
+        try:
+            ops = _ops_c2(device)
+        except Exception as error:  # noqa: BLE001 - the line still reports the measured step
+            ops = {"error": f"{type(error).__name__}: {error}"}
     thermo_now = md.thermodynamics() if rank == 0 else None
     if world > 1:
         dist.barrier()
@@ -284,46 +291,173 @@ def _ours(args):
                     "positions+momenta in, positions/momenta/forces/energy out, per window of "
                     f"{S} steps"},
             "gpu_launches": launches_per_window * windows, "launches_per_step": launches_per_window / S,
-            "roofline": roofline, "cpu_baseline": cpu, "clocks": clk,
+            "roofline": roofline, "cpu_baseline": cpu, "clocks": clk, "ops_config2": ops,
             "fallbacks": md.runner.fallbacks, "candidate_refreshes": md.runner.refreshes,
             "final_temperature_K": float(thermo_now["temperature"][0]),
             "final_conserved_eV": float(thermo_now["conserved_energy"][0])}
 
 
-def _roofline(md, device):
-    """The dominant kernel of the step (the radial-MLP output GEMM of layer 2, [E, 64] x [64, 512]),
-    timed alone with CUDA events on its stream, against the HBM roofline of its algorithmic bytes."""
+STAGES = {0: ("edge_fwd_kernel", 1), 1: ("message_fused_kernel (per layer)", 2), 2: ("node_fwd_kernel", 1),
+          3: ("node_last_kernel", 1), 4: ("msg_bwd_edge_kernel (per layer)", 2), 5: ("sender_node_kernel", 1),
+          6: ("edge_bwd_kernel", 1), 7: ("forces_kernel", 1)}
+
+
+def _time_stage(md, device, bit, reps=200):
     import torch
 
-    from fastmd_b200.mace import _gemm
-
-    model = md.model
-    buf = next(iter(model._buffers.values()))
-    b, w = buf.t, model.w
-    E = buf.n_edges
-    a, wt, y = b["1.h3"], w["1.radial.3"], b["1.R"]
-    n, k = wt.shape
+    model, batch = md.model, md.builder.batch
     s = torch.cuda.current_stream(device)
-    for _ in range(20):
-        _gemm(a, wt, y, s=s.cuda_stream)
-    reps = 200
+    for _ in range(10):
+        model.energy_forces_fused(batch, n_systems=md.replicas, stages=1 << bit)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(s)
     for _ in range(reps):
-        _gemm(a, wt, y, s=s.cuda_stream)
+        model.energy_forces_fused(batch, n_systems=md.replicas, stages=1 << bit)
     end.record(s)
     torch.cuda.synchronize()
-    ms = start.elapsed_time(end) / reps
-    hbm, tf, kind = _peaks()
-    flops = 2.0 * E * n * k
-    bytes_ = 4.0 * (E * k + n * k + E * n)
-    achieved_gbs = bytes_ / (ms * 1e-3) / 1e9
-    return {"kernel": "sgemm_kernel (layer-2 radial MLP output, fmd_gemm_f32)", "bound": "hbm",
-            "achieved": achieved_gbs, "peak": hbm, "unit": "GB/s", "frac": achieved_gbs / hbm,
-            "peak_source": f"{kind} (MEASURED_PEAKS.json hbm_gbs)" if kind == "measured" else "fallback",
-            "traffic": None, "algorithmic_bytes_per_launch": bytes_, "flops_per_launch": flops,
-            "avg_launch_us": ms * 1e3, "achieved_tflops_fp32": flops / (ms * 1e-3) / 1e12,
-            "note": "latency-bound at 135 atoms: the step is ~50 tiny kernels; see profiles/"}
+    return start.elapsed_time(end) / reps * 1e3  # us per launch group
+
+
+def _roofline(md, device):
+    """Every fused stage timed alone (CUDA events, 200 back-to-back launches on the step's stream,
+    after the timed run); the roofline of the dominant single-kernel stage against the measured HBM
+    copy bandwidth (algorithmic bytes: the stage's compulsory reads and writes)."""
+    hbm, _, kind = _peaks()
+    stages = {STAGES[bit][0]: round(_time_stage(md, device, bit), 3) for bit in STAGES}
+    single = {bit: stages[STAGES[bit][0]] for bit in STAGES if STAGES[bit][1] == 1}
+    bit = max(single, key=single.get)
+    us = single[bit]
+    c = md.model.config
+    N = md.builder.n_real
+    E = int(md.builder.batch.n_edges.item())
+    pc = sum(c.paths(L) * c.channels for L in range(c.num_interactions))
+    weights = 4 * sum(c.num_bessel * 64 + 2 * 64 * 64 + 64 * c.paths(L) * c.channels
+                      for L in range(c.num_interactions))
+    # per-stage algorithmic bytes / flops (one launch over the step's real edges)
+    algo = {0: (E * (8 + 12 + 16 + 4 * pc) + N * 12 + weights,
+                2.0 * E * sum(c.num_bessel * 64 + 2 * 64 * 64 + 64 * c.paths(L) * c.channels
+                              for L in range(c.num_interactions))),
+            6: (E * (16 + 12 + 12 + 4 * pc) + weights,
+                2.0 * E * sum(2 * (c.num_bessel * 64 + 2 * 64 * 64) + 64 * c.paths(L) * c.channels
+                              for L in range(c.num_interactions)))}
+    bytes_, flops = algo.get(bit, (None, None))
+    traffic = None
+    tpath = ROOT / "profiles" / "traffic.json"
+    if tpath.exists():
+        traffic = json.loads(tpath.read_text()).get(STAGES[bit][0])
+    out = {"kernel": STAGES[bit][0], "bound": "hbm", "unit": "GB/s", "peak": hbm,
+           "peak_source": f"{kind} (MEASURED_PEAKS.json hbm_gbs)" if kind == "measured" else "fallback 6650 GB/s",
+           "avg_launch_us": us, "stages_us": stages, "traffic": traffic,
+           "note": "135 atoms / 2,054 edges: every stage is latency-bound (see profiles/)"}
+    if bytes_ is not None:
+        achieved = bytes_ / (us * 1e-6) / 1e9
+        out.update({"achieved": achieved, "frac": achieved / hbm, "algorithmic_bytes_per_launch": bytes_,
+                    "flops_per_launch": flops, "achieved_tflops_fp32": flops / (us * 1e-6) / 1e12})
+    return out
+
+
+def _ops_c2(device):
+    """BASELINE config 2, the op microbenchmark: 100,000 atoms uniform at 0.06 / A^3 (seed 2), rc 6 A,
+    node features N(0,1) of width 128; each stage timed alone with CUDA events (inputs larger than
+    L2; median of 5 after 2 warm-ups) against the measured HBM bandwidth (or the FP32 rate of the
+    IEEE GEMM)."""
+    import ctypes
+
+    import torch
+
+    from fastmd_b200 import _lib
+    from fastmd_b200._lib import call, ptr
+    from fastmd_b200.graph import _host_cell, estimate_max_neighbors
+    from fastmd_b200.mace import _gemm
+    from fastmd_b200.structures import random_box
+
+    hbm, _, kind = _peaks()
+    s = torch.cuda.current_stream(device)
+    sp = s.cuda_stream
+
+    def timed(fn, reps=5):
+        for _ in range(2):
+            fn()
+        times = []
+        for _ in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(s)
+            fn()
+            b.record(s)
+            torch.cuda.synchronize()
+            times.append(a.elapsed_time(b))
+        return statistics.median(times)
+
+    n = 100_000
+    pos_np, cell_np, _ = random_box(n, density=0.06, seed=2)
+    pos = torch.from_numpy(pos_np).float().to(device)
+    cell_host, cell_ptr = _host_cell(torch.from_numpy(cell_np).float())
+    bmax = estimate_max_neighbors(6.0, atomic_density=0.06, safety_factor=2.0)
+    e_cap = n * 64
+    nbytes = ctypes.c_size_t(0)
+    call("fmd_neighbor_list_workspace_bytes", cell_ptr, 6.0, n, bmax, ctypes.byref(nbytes))
+    ws = torch.empty(int(nbytes.value), dtype=torch.uint8, device=device)
+    center = torch.empty(e_cap, dtype=torch.int64, device=device)
+    neighbor = torch.empty(e_cap, dtype=torch.int64, device=device)
+    images = torch.empty(e_cap, 3, dtype=torch.int32, device=device)
+    dist = torch.empty(e_cap, dtype=torch.float32, device=device)
+    offsets = torch.empty(n + 1, dtype=torch.int64, device=device)
+    wrapped = torch.empty(n, 3, dtype=torch.float32, device=device)
+    flags = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def nlist():
+        call("fmd_neighbor_list", ptr(pos), cell_ptr, n, 6.0, bmax, e_cap, ptr(wrapped), ptr(center), ptr(neighbor),
+             ptr(images), ptr(dist), ptr(offsets), ptr(ws), ws.numel(), ptr(flags), sp)
+
+    t_nl = timed(nlist)
+    E = int(offsets[n].item())
+    if int(flags.item()) or E > e_cap:
+        return {"error": f"neighbour list flags {int(flags.item())}, {E} edges"}
+    D = 128
+    g = torch.Generator(device=device).manual_seed(2)
+    X = torch.randn(n, D, device=device, generator=g)
+    rbf = torch.randn(E, 8, device=device, generator=g)
+    cat = torch.empty(E, 2 * D + 8, device=device)
+    parts = (_lib.FmdCatPart * 3)()
+    for k, (src, idx, width, rows) in enumerate(((X, neighbor, D, n), (X, center, D, n), (rbf, None, 8, E))):
+        parts[k].src, parts[k].index, parts[k].ld, parts[k].n_src, parts[k].width = ptr(src), ptr(idx), width, rows, width
+
+    def gather():
+        call("fmd_gather_cat", parts, 3, E, ptr(cat), 2 * D + 8, ptr(flags), sp)
+
+    t_gc = timed(gather)
+    W0 = torch.randn(256, 2 * D + 8, device=device, generator=g) / 16.0
+    W1 = torch.randn(256, 256, device=device, generator=g) / 16.0
+    h = torch.empty(E, 256, device=device)
+    y = torch.empty(E, 256, device=device)
+
+    def mlp():
+        _gemm(cat, W0, h, act=1, s=sp)
+        _gemm(h, W1, y, s=sp)
+
+    t_mlp = timed(mlp, reps=3)
+    seg = torch.empty(n, 256, device=device)
+
+    def segsum():
+        call("fmd_csr_segment_sum", ptr(y), 256, None, 0, None, ptr(offsets), n, 256, -1, ptr(seg), 256, sp)
+
+    t_ss = timed(segsum)
+    b_nl = E * (8 + 8 + 12 + 4) + n * (12 + 16)
+    b_gc = E * (2 * D + 8) * 4 + 2 * E * 8 + E * 8 * 4 + n * D * 4
+    b_ss = E * 256 * 4 + (n + 1) * 8 + n * 256 * 4
+    f_mlp = 2.0 * E * ((2 * D + 8) * 256 + 256 * 256)
+
+    def hb(bytes_, ms):
+        gbs = bytes_ / (ms * 1e-3) / 1e9
+        return {"ms": round(ms, 4), "algorithmic_bytes": bytes_, "achieved_GBs": round(gbs, 1),
+                "frac_of_hbm": round(gbs / hbm, 3)}
+
+    return {"workload": "config2: 100,000 atoms, 0.06/A^3, rc 6 A, seed 2", "edges": E,
+            "edges_per_atom": round(E / n, 2), "hbm_peak_GBs": hbm, "peak_source": kind,
+            "neighbor_list": hb(b_nl, t_nl), "gather_cat_264": hb(b_gc, t_gc),
+            "edge_mlp_264_256_256_ieee_fp32": {"ms": round(t_mlp, 3), "flops": f_mlp,
+                                               "achieved_TFLOPs": round(f_mlp / (t_mlp * 1e-3) / 1e12, 2)},
+            "segment_sum_256": hb(b_ss, t_ss)}
 
 
 def _cpu_baseline():

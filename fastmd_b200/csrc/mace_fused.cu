@@ -980,7 +980,9 @@ inline fmd_status grant(const void* kernel, size_t bytes, int slot) {
 
 template <int C>
 fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeights& w, const FusedState& st,
-                       int64_t atoms_per_system, int32_t n_systems, float* forces, double* total, cudaStream_t s) {
+                       int64_t atoms_per_system, int32_t n_systems, float* forces, double* total, int32_t stages,
+                       cudaStream_t s) {
+    const auto on = [stages](int bit) { return (stages >> bit) & 1; };
     const int64_t n_tiles = (ea.n_edges + kTF - 1) / kTF;
     const int edge_grid = int(n_tiles < int64_t(kNumSMs) * 8 ? n_tiles : int64_t(kNumSMs) * 8);
     const int atom_grid = int(ga.n_atoms < int64_t(kNumSMs) * 16 ? ga.n_atoms : int64_t(kNumSMs) * 16);
@@ -1007,20 +1009,22 @@ fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeigh
         }
     }
     const int L = w.n_layers;
-    if (n_tiles > 0) edge_fwd_kernel<C><<<edge_grid, 256, sizeof(EdgeFwdSmem), s>>>(ea, w, st);
+    if (n_tiles > 0 && on(0)) edge_fwd_kernel<C><<<edge_grid, 256, sizeof(EdgeFwdSmem), s>>>(ea, w, st);
     for (int l = 0; l < L; ++l) {
-        if (l == 0) message_fused_kernel<C, 2><<<atom_grid, 128, 0, s>>>(ga, w, st, l);
-        else message_fused_kernel<C, 4><<<atom_grid, 128, 0, s>>>(ga, w, st, l);
-        if (l < L - 1) node_fwd_kernel<C><<<group_grid, kQ * C, node_smem, s>>>(w, st, l);
+        if (on(1)) {
+            if (l == 0) message_fused_kernel<C, 2><<<atom_grid, 128, 0, s>>>(ga, w, st, l);
+            else message_fused_kernel<C, 4><<<atom_grid, 128, 0, s>>>(ga, w, st, l);
+        }
+        if (l < L - 1 && on(2)) node_fwd_kernel<C><<<group_grid, kQ * C, node_smem, s>>>(w, st, l);
     }
-    node_last_kernel<C><<<group_grid, kQ * C, node_smem, s>>>(w, st, L - 1);
+    if (on(3)) node_last_kernel<C><<<group_grid, kQ * C, node_smem, s>>>(w, st, L - 1);
     for (int l = L - 1; l >= 1; --l) {
-        msg_bwd_edge_kernel<C, 4><<<atom_grid, 128, 0, s>>>(ga, w, st, l, l != L - 1);
-        sender_node_kernel<C><<<group_grid, kQ * C, node_smem, s>>>(ga, w, st, l);
+        if (on(4)) msg_bwd_edge_kernel<C, 4><<<atom_grid, 128, 0, s>>>(ga, w, st, l, l != L - 1);
+        if (on(5)) sender_node_kernel<C><<<group_grid, kQ * C, node_smem, s>>>(ga, w, st, l);
     }
-    msg_bwd_edge_kernel<C, 2><<<atom_grid, 128, 0, s>>>(ga, w, st, 0, L != 1);
-    if (b_tiles > 0) edge_bwd_kernel<C><<<bwd_grid, 256, sizeof(EdgeBwdSmem), s>>>(ea, w, st);
-    forces_kernel<<<n_systems, 256, 0, s>>>(ga, st.g_r, st.node_energy, atoms_per_system, forces, total);
+    if (on(4)) msg_bwd_edge_kernel<C, 2><<<atom_grid, 128, 0, s>>>(ga, w, st, 0, L != 1);
+    if (b_tiles > 0 && on(6)) edge_bwd_kernel<C><<<bwd_grid, 256, sizeof(EdgeBwdSmem), s>>>(ea, w, st);
+    if (on(7)) forces_kernel<<<n_systems, 256, 0, s>>>(ga, st.g_r, st.node_energy, atoms_per_system, forces, total);
     return check_launch();
 }
 
@@ -1035,7 +1039,8 @@ fmd_status fmd_mace_fused_step(const fmd_mace_fused_weights* weights, const fmd_
                                const float* edge_image, int64_t n_edges, const int64_t* n_real_edges,
                                const int64_t* recv_off,
                                const int64_t* send_off, const int32_t* send_perm, int64_t atoms_per_system,
-                               int32_t n_systems, int32_t channels, float* forces, double* energy, void* stream) {
+                               int32_t n_systems, int32_t channels, float* forces, double* energy, int32_t stages,
+                               void* stream) {
     if (weights == nullptr || state == nullptr || positions == nullptr || cell == nullptr || edge_index == nullptr ||
         edge_image == nullptr || recv_off == nullptr || send_off == nullptr || send_perm == nullptr ||
         forces == nullptr || energy == nullptr || n_edges < 0 || atoms_per_system < 1 || n_systems < 1)
@@ -1070,9 +1075,9 @@ fmd_status fmd_mace_fused_step(const fmd_mace_fused_weights* weights, const fmd_
     const GraphArgs ga{edge_index, recv_off, send_off, send_perm, atoms_per_system * n_systems};
     cudaStream_t s = as_stream(stream);
     switch (channels) {
-        case 32: return launch_step<32>(ea, ga, w, st, atoms_per_system, n_systems, forces, energy, s);
-        case 64: return launch_step<64>(ea, ga, w, st, atoms_per_system, n_systems, forces, energy, s);
-        case 128: return launch_step<128>(ea, ga, w, st, atoms_per_system, n_systems, forces, energy, s);
+        case 32: return launch_step<32>(ea, ga, w, st, atoms_per_system, n_systems, forces, energy, stages, s);
+        case 64: return launch_step<64>(ea, ga, w, st, atoms_per_system, n_systems, forces, energy, stages, s);
+        case 128: return launch_step<128>(ea, ga, w, st, atoms_per_system, n_systems, forces, energy, stages, s);
         default: return FMD_ERR_UNSUPPORTED;
     }
 }

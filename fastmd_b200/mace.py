@@ -409,7 +409,8 @@ def _struct_types():
 _FusedWeights, _FusedState = _struct_types()
 _lib.declare("fmd_mace_fused_step", [_lib.ctypes.POINTER(_FusedWeights), _lib.ctypes.POINTER(_FusedState),
                                      *([_lib.c_void_p] * 4), _lib.c_int64, *([_lib.c_void_p] * 4), _lib.c_int64,
-                                     _lib.c_int32, _lib.c_int32, _lib.c_void_p, _lib.c_void_p, _lib.c_void_p])
+                                     _lib.c_int32, _lib.c_int32, _lib.c_void_p, _lib.c_void_p, _lib.c_int32,
+                                     _lib.c_void_p])
 
 
 def _fused_weights(model: "MACEModel"):
@@ -515,7 +516,7 @@ class _FusedBuffers:
         self.energy: dict[int, Tensor] = {}
 
 
-def _energy_forces_fused(self: "MACEModel", batch, n_systems: int = 1):
+def _energy_forces_fused(self: "MACEModel", batch, n_systems: int = 1, stages: int = -1):
     """(per-system fp64 energies [R], forces [N, 3] float32) of ``batch`` in the fused kernels
     (``fmd_mace_fused_step``); the same mathematics as ``energy_forces``."""
     if getattr(batch, "element", None) is None:
@@ -538,7 +539,7 @@ def _energy_forces_fused(self: "MACEModel", batch, n_systems: int = 1):
     call("fmd_mace_fused_step", _ct.byref(fw), _ct.byref(buf.state), ptr(batch.positions), ptr(batch.cell),
          ptr(batch.edge_index), ptr(batch.edge_image), E, ptr(batch.n_edges), ptr(batch.recv_off), ptr(batch.send_off),
          ptr(batch.send_perm), N // n_systems, n_systems, self.config.channels, ptr(forces), ptr(energy),
-         stream(self.device))
+         int(stages), stream(self.device))
     return energy, forces
 
 

@@ -427,7 +427,11 @@ typedef struct fmd_mace_fused_state {
  * F_a = sum_{received e} dE/dr_e - sum_{sent e} dE/dr_e over both CSRs.
  * forces [N][3] float32, energy [n_systems] fp64 (deterministic sums).
  * n_real_edges (device int64, may be NULL): the count of real rows; the
- * padding rows after it are skipped by the edge kernels.
+ * padding rows after it are skipped by the edge kernels. stages: -1 for the
+ * whole step, else a bit mask of the kernels to launch (bit 0 edge forward,
+ * 1 messages, 2 node forward, 3 last node update, 4 per-edge message
+ * backward, 5 sender/node backward, 6 edge backward, 7 forces) -- a stage
+ * launched alone reads what earlier stages left in `state` (for timing).
  * channels 32, 64 or 128. Replaces the energy-tap evaluation of the
  * whole-step runner (whole_step_cuda_graph.py:256 _evaluate with
  * fastmd/engine/energy_derivative.py:110 over mace.py:356). */
@@ -437,7 +441,7 @@ FMD_API fmd_status fmd_mace_fused_step(const fmd_mace_fused_weights* weights, co
                                        const int64_t* recv_off,
                                        const int64_t* send_off, const int32_t* send_perm, int64_t atoms_per_system,
                                        int32_t n_systems, int32_t channels, float* forces, double* energy,
-                                       void* stream);
+                                       int32_t stages, void* stream);
 
 /* -------------------------------------- Nose-Hoover chain integrator (F1/F3) */
 
