@@ -120,7 +120,7 @@ class _Clocks:
                 ["nvidia-smi", f"--id={index}", "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,"
                  "clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
                  "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "200"],
+                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=self.out, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
@@ -174,14 +174,19 @@ def _ours(args):
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    from fastmd_b200.gpu_nhc import maxwell_boltzmann_momenta
+    from fastmd_b200.replicas import ThermoLog, replica_seeds
+
     R = args.replicas
-    systems = [_system(rank * R + r) for r in range(R)]
+    seeds = replica_seeds(rank, world, R)  # replica i: jitter and momentum seed i (config 4)
+    systems = [_system(seed) for seed in seeds]
     cell, numbers, masses = systems[0][1], systems[0][2], systems[0][3]
     positions = np.concatenate([s[0] for s in systems])
+    momenta = np.concatenate([maxwell_boltzmann_momenta(masses, TEMPERATURE, seed=seed) for seed in seeds])
     model = MACEModel(device=device, seed=1)
     S = math.gcd(args.steps, args.steps_per_launch) or 1
-    md = GPUResidentMolecularDynamics(model, positions=positions, cell=cell, atomic_numbers=numbers, masses=masses,
-                                      temperature_K=TEMPERATURE, timestep=0.25 * units.fs, tdamp=25 * units.fs,
+    md = GPUResidentMolecularDynamics(model, positions=positions, momenta=momenta, cell=cell, atomic_numbers=numbers,
+                                      masses=masses, temperature_K=TEMPERATURE, timestep=0.25 * units.fs, tdamp=25 * units.fs,
                                       replicas=R, steps_per_launch=S, device=device)
     runner = md.runner
     # kernels of one window (counted on an eager window; the graph replays the same launches)
@@ -193,14 +198,11 @@ def _ours(args):
     launches_per_window = sum(n * (_lib.fused_step_kernels(model.config.num_interactions)
                                    if name == "fmd_mace_fused_step" else _lib.KERNELS_PER_CALL.get(name, 1))
                               for name, n in counted.items())
-    thermo = torch.zeros(R, 2, dtype=torch.float64, device=device)
-    gathered = torch.zeros(world * R, 2, dtype=torch.float64, device=device)
+    log = ThermoLog(R, device)
 
-    def thermo_log():
+    def thermo_log():  # the per-replica (E_pot, T) of every rank, once per window (NCCL over NVLink)
         if world > 1:
-            thermo[:, 0].copy_(md.integrator.state.energy)
-            thermo[:, 1].copy_(md.integrator.temperature().reshape(-1))
-            dist.all_gather_into_tensor(gathered, thermo)
+            log.gather(md.integrator.state.energy, md.integrator.temperature())
 
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
     for _ in range(max(1, -(-args.warmup // S))):
