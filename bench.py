@@ -373,7 +373,9 @@ def _ops_c2(device):
     from fastmd_b200.mace import _gemm
     from fastmd_b200.structures import random_box
 
-    hbm, _, kind = _peaks()
+    hbm, bf16, kind = _peaks()
+    # kind::tf32 issues at half the bf16 rate; 3xTF32 makes three TF32 products per FP32 product
+    tf32_peak, tf32_kind = bf16 / 2.0, f"half of the {kind} bf16 dense figure"
     s = torch.cuda.current_stream(device)
     sp = s.cuda_stream
 
@@ -438,6 +440,17 @@ def _ops_c2(device):
         _gemm(h, W1, y, s=sp)
 
     t_mlp = timed(mlp, reps=3)
+    from fastmd_b200 import wide_gemm
+
+    def mlp_tc():
+        wide_gemm.linear_into(h, cat, W0, b0, act=1)
+        wide_gemm.linear_into(y, h, W1, b1)
+
+    b0 = torch.zeros(256, device=device)
+    b1 = torch.zeros(256, device=device)
+    wide_gemm._split(W0, False), wide_gemm._split(W1, False)  # once per weight version, outside the timing
+    t_tc = timed(mlp_tc, reps=5)
+    t_l1 = timed(lambda: wide_gemm.linear_into(h, cat, W0, b0, act=1), reps=5)
     seg = torch.empty(n, 256, device=device)
 
     def segsum():
@@ -459,7 +472,18 @@ def _ops_c2(device):
             "neighbor_list": hb(b_nl, t_nl), "gather_cat_264": hb(b_gc, t_gc),
             "edge_mlp_264_256_256_ieee_fp32": {"ms": round(t_mlp, 3), "flops": f_mlp,
                                                "achieved_TFLOPs": round(f_mlp / (t_mlp * 1e-3) / 1e12, 2)},
+            "edge_mlp_264_256_256_tf32x3_tcgen05": _tc_line(f_mlp, t_tc, E, tf32_peak, tf32_kind),
+            "edge_linear_264_256_silu_tf32x3_tcgen05": _tc_line(2.0 * E * 264 * 256, t_l1, E, tf32_peak, tf32_kind),
             "segment_sum_256": hb(b_ss, t_ss)}
+
+
+def _tc_line(flops, ms, rows, tf32_peak, kind):
+    """A 3xTF32 GEMM line: FP32-equivalent TFLOP/s, the TF32 tensor rate it implies (3 products per FP32
+    product) and its fraction of the TF32 dense peak."""
+    fp32_tflops = flops / (ms * 1e-3) / 1e12
+    return {"ms": round(ms, 3), "rows": rows, "flops": flops, "achieved_TFLOPs_fp32_equivalent": round(fp32_tflops, 2),
+            "tf32_tensor_TFLOPs": round(3 * fp32_tflops, 1), "tf32_peak_TFLOPs": round(tf32_peak, 1),
+            "frac_of_tf32_peak": round(3 * fp32_tflops / tf32_peak, 3), "peak_source": kind}
 
 
 def _cpu_baseline():

@@ -4,6 +4,6 @@ Surfaces mirroring the reference: ``ops`` (fastmd.ops), ``graph`` (fastmd.graph 
 ``energy_derivative`` (fastmd.engine), ``gpu_nhc`` and ``whole_step`` (fastmd.execution /
 fastmd.interfaces), ``mace`` (the MACE-architecture energy tap).
 """
-from fastmd_b200 import _lib, energy_derivative, gpu_nhc, graph, mace, ops, units, whole_step  # noqa: F401
+from fastmd_b200 import _lib, energy_derivative, gpu_nhc, graph, mace, ops, units, whole_step, wide_gemm  # noqa: F401
 
 __all__ = ["energy_derivative", "gpu_nhc", "graph", "mace", "ops", "units", "whole_step"]

@@ -15,6 +15,9 @@ constexpr int kNumSMs = 148;
 // Records the CUDA error text for fmd_last_error() (thread local).
 fmd_status record_cuda_error(cudaError_t err);
 
+// Records `text (code)` for fmd_last_error() and returns `status`.
+fmd_status record_error_text(fmd_status status, const char* text, long long code);
+
 inline fmd_status check_launch() {
     cudaError_t err = cudaGetLastError();
     return err == cudaSuccess ? FMD_OK : record_cuda_error(err);

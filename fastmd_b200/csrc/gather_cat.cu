@@ -27,6 +27,11 @@ fmd_status record_cuda_error(cudaError_t err) {
     return FMD_ERR_CUDA;
 }
 
+fmd_status record_error_text(fmd_status status, const char* text, long long code) {
+    snprintf(g_last_error, sizeof(g_last_error), "%s (%lld)", text, code);
+    return status;
+}
+
 constexpr int kMaxParts = 4;
 constexpr int kCatThreads = 256;
 constexpr int kCatRowsPerCta = 32;

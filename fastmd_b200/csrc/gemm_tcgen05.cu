@@ -1,0 +1,645 @@
+// Wide-row FP32 GEMM on the Blackwell tensor cores: tcgen05.mma kind::tf32
+// with TMA-fed shared-memory operands and TMEM accumulators, at FP32 accuracy
+// (3xTF32). The frozen-weight projections of
+// fastmd/engine/kernels/triton_wide_gemm.py (linear :482, matmul :534).
+//
+//   y[m, n] (=|+=) act( sum_chunks(x[m, :k] . w^T) + bias + c )   w [n, k]
+//
+// 3xTF32: v = v_hi + v_lo with v_hi = rna_tf32(v), v_lo = v - v_hi, and
+// x . w ~ x_lo w_hi + x_hi w_lo + x_hi w_hi (the x_lo w_lo term is below FP32
+// rounding; the small cross terms go first). The weight is split once per
+// weight version (fmd_tf32_split); x is split in shared memory as it arrives.
+// The tensor-core accumulator does not round its additions to nearest, so
+// every 64-wide K chunk accumulates in its own TMEM buffer and the chunk sums
+// are added in FP32 registers (round to nearest): the error stays flat in K
+// (triton_wide_gemm.py:6-13 and _tile :83). A row's result depends on its own
+// inputs only, not on m, its tile or the grid.
+//
+// One persistent CTA per SM (512 threads) walks 128 x 128 output tiles, N
+// fastest (the column tiles of a row block run together and share x in L2):
+//   warp 0      TMA producer: x, w_hi, w_lo tiles [128 rows x 32 k] per K
+//               stage into a 3-stage ring, 128-byte swizzle, zero fill past m,
+//               n and k
+//   warp 1      TMEM owner (512 columns = 4 chunk accumulators of 128
+//               columns) and MMA issuer (one thread): per stage 4 K-steps of 8,
+//               three products each, M = 128, N = 128 (or the tile's width)
+//   warps 4-7   split x in place into x_hi and x_lo (elementwise on the
+//               swizzled bytes, so the layout is untouched)
+//   warps 8-15  epilogue: TMEM -> registers, chunk sums, bias, residual,
+//               SiLU, stores; warp w reads TMEM lanes 32 (w % 4) .. +31 (its
+//               32 rows) and columns 64 ((w - 8) / 4) .. +63
+// Every mbarrier wait is bounded (about a second): on expiry the CTA raises
+// FMD_FLAG_WAIT_TIMEOUT, waits (bounded) for its copies and MMAs in flight,
+// frees its TMEM and returns. No cluster launch and no multicast.
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace fmd {
+namespace {
+
+constexpr int kBM = 128, kBN = 128, kBK = 32, kChunkK = 64;
+constexpr int kStages = 3, kAccBufs = 4;
+constexpr int kThreads = 512;
+constexpr int kSplitThreads = 128, kEpiThreads = 256;
+constexpr uint32_t kTileBytes = kBM * kBK * 4;    // 16 KB, one operand tile of one stage
+constexpr uint32_t kStageBytes = 4 * kTileBytes;  // x_hi (TMA target), x_lo, w_hi, w_lo
+constexpr uint32_t kTmemCols = kAccBufs * kBN;    // 512
+constexpr unsigned long long kWaitNs = 1000000000ull;
+
+struct Ctrl {
+    uint64_t full[kStages];   // TMA bytes landed (1 arrival + tx)
+    uint64_t split[kStages];  // x split into hi/lo (kSplitThreads arrivals)
+    uint64_t empty[kStages];  // MMAs of the stage done (tcgen05.commit)
+    uint64_t acc_full[kAccBufs];   // chunk accumulator complete (tcgen05.commit)
+    uint64_t acc_empty[kAccBufs];  // chunk accumulator read out (kEpiThreads arrivals)
+    uint64_t drain;           // MMAs in flight on abort
+    uint32_t tmem_base;
+    int32_t abort;
+};
+
+constexpr size_t kSmemBytes = size_t(kStages) * kStageBytes + sizeof(Ctrl) + 1024;  // + 1024-B alignment slack
+
+struct WideArgs {
+    const float* bias;  // [n] or null
+    const float* c;     // [m, ldc] residual or null
+    int64_t ldc;
+    float* y;
+    int64_t ldy;
+    int32_t* flags;
+    int64_t m;
+    int32_t n, k;
+    int32_t act, accumulate;
+    int32_t vec_c, vec_y;  // 16-byte row access valid
+};
+
+// ------------------------------------------------------------- PTX wrappers
+
+__device__ __forceinline__ uint32_t su32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(su32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+                     su32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Waits for the phase of `parity` to complete. Gives up after kWaitNs, or
+// as soon as another role of the CTA has given up (abort != 0, unless
+// `ignore_abort`); returns false then and sets the CTA's abort word.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int32_t* abort,
+                                          bool ignore_abort = false) {
+    const uint32_t a = su32(bar);
+    if (mbar_try_wait(a, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    while (true) {
+        if (mbar_try_wait(a, parity)) return true;
+        if (!ignore_abort && *abort) return false;
+        if (global_ns() - t0 > kWaitNs) {
+            *abort = 1;
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(su32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(su32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// 16 consecutive TMEM columns of this thread's lane (shape 32x32b, x16),
+// with the wait in the same statement so no use can move above it.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ float rna_tf32(float v) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+    return __uint_as_float(r);
+}
+
+// Shared-memory matrix descriptor of a K-major operand tile in the 128-byte
+// swizzle: rows of 128 B (32 fp32), 8-row groups 1024 B apart (SBO), the
+// leading offset unused (1), descriptor version 1, base offset 0 (tiles are
+// 1024-B aligned), layout type 2 = SWIZZLE_128B. A K-step of 8 tf32 inside
+// the swizzle atom advances the start address by 32 B (+2 in the field).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    return uint64_t((saddr & 0x3FFFFu) >> 4) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) |
+           (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+
+// Instruction descriptor of kind::tf32: FP32 accumulator, A and B TF32,
+// both K-major, no negation, N >> 3 at bit 17, M >> 4 at bit 24.
+__device__ __forceinline__ uint32_t tf32_idesc(int m, int n) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
+}
+
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
+
+// ------------------------------------------------------------------ kernel
+
+__global__ void __launch_bounds__(kThreads, 1)
+    wide_gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_wh,
+                            const __grid_constant__ CUtensorMap tmap_wl, WideArgs g) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* ring = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                           ~uintptr_t(1023));
+    Ctrl& ctl = *reinterpret_cast<Ctrl*>(ring + kStages * kStageBytes);
+    volatile int32_t* abort = &ctl.abort;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m_tiles = int((g.m + kBM - 1) / kBM);
+    const int n_tiles = (g.n + kBN - 1) / kBN;
+    const int tiles = m_tiles * n_tiles;
+    const int k_stages = (g.k + kBK - 1) / kBK;
+    const int chunks = (g.k + kChunkK - 1) / kChunkK;
+    constexpr int kStagesPerChunk = kChunkK / kBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&ctl.full[s], 1);
+            mbar_init(&ctl.split[s], kSplitThreads);
+            mbar_init(&ctl.empty[s], 1);
+        }
+        for (int b = 0; b < kAccBufs; ++b) {
+            mbar_init(&ctl.acc_full[b], 1);
+            mbar_init(&ctl.acc_empty[b], kEpiThreads);
+        }
+        mbar_init(&ctl.drain, 1);
+        ctl.abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&ctl.tmem_base)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = ctl.tmem_base;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------------------------------------------- producer
+            uint32_t armed = 0, armed_ph = 0;  // bit s: stage s has been loaded / in the phase of bit s
+            int s = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+                const int m0 = (t / n_tiles) * kBM, n0 = (t % n_tiles) * kBN;
+                for (int ks = 0; ks < k_stages; ++ks) {
+                    if (!mbar_wait(&ctl.empty[s], ph ^ 1u, abort)) {
+                        ok = false;
+                        break;
+                    }
+                    unsigned char* st = ring + s * kStageBytes;
+                    mbar_expect_tx(&ctl.full[s], 3 * kTileBytes);
+                    tma_load_2d(st, &tmap_x, &ctl.full[s], ks * kBK, m0);
+                    tma_load_2d(st + 2 * kTileBytes, &tmap_wh, &ctl.full[s], ks * kBK, n0);
+                    tma_load_2d(st + 3 * kTileBytes, &tmap_wl, &ctl.full[s], ks * kBK, n0);
+                    armed |= 1u << s;
+                    armed_ph = (armed_ph & ~(1u << s)) | (ph << s);
+                    if (++s == kStages) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                }
+            }
+            if (!ok) {  // let the copies in flight land before the CTA exits
+                for (int i = 0; i < kStages; ++i)
+                    if ((armed >> i) & 1u) mbar_wait(&ctl.full[i], (armed_ph >> i) & 1u, abort, true);
+            } else {  // tail: the last stages' release arrivals land before the CTA exits
+                for (int i = 0; i < kStages && mbar_wait(&ctl.empty[s], ph ^ 1u, abort); ++i) {
+                    if (++s == kStages) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ------------------------------------------------- MMA issuer
+            const uint32_t ring_addr = su32(ring);
+            int s = 0, cb = 0;
+            uint32_t ph = 0, cph = 0;
+            bool ok = true, issued = false;
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+                const int n0 = (t % n_tiles) * kBN;
+                const int nw = min(kBN, g.n - n0);
+                const uint32_t idesc = tf32_idesc(kBM, (nw + 15) & ~15);
+                int ks = 0;
+                for (int ch = 0; ch < chunks && ok; ++ch) {
+                    if (!mbar_wait(&ctl.acc_empty[cb], cph ^ 1u, abort)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d = tmem + uint32_t(cb * kBN);
+                    const int ks_end = min(ks + kStagesPerChunk, k_stages);
+                    uint32_t acc = 0;
+                    for (; ks < ks_end; ++ks) {
+                        if (!mbar_wait(&ctl.full[s], ph, abort) || !mbar_wait(&ctl.split[s], ph, abort)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t base = ring_addr + uint32_t(s) * kStageBytes;
+                        const uint64_t xh = sw128_desc(base), xl = sw128_desc(base + kTileBytes);
+                        const uint64_t wh = sw128_desc(base + 2 * kTileBytes), wl = sw128_desc(base + 3 * kTileBytes);
+#pragma unroll
+                        for (int kk = 0; kk < kBK / 8; ++kk) {
+                            tc_mma_tf32(d, xl + 2 * kk, wh + 2 * kk, idesc, acc);
+                            acc = 1;
+                        }
+#pragma unroll
+                        for (int kk = 0; kk < kBK / 8; ++kk) tc_mma_tf32(d, xh + 2 * kk, wl + 2 * kk, idesc, 1);
+#pragma unroll
+                        for (int kk = 0; kk < kBK / 8; ++kk) tc_mma_tf32(d, xh + 2 * kk, wh + 2 * kk, idesc, 1);
+                        issued = true;
+                        tc_commit(&ctl.empty[s]);  // frees the stage once these MMAs are done
+                        if (++s == kStages) {
+                            s = 0;
+                            ph ^= 1u;
+                        }
+                    }
+                    if (!ok) break;
+                    tc_commit(&ctl.acc_full[cb]);
+                    if (++cb == kAccBufs) {
+                        cb = 0;
+                        cph ^= 1u;
+                    }
+                }
+            }
+            if (!ok && issued) {  // the MMAs in flight finish before TMEM is freed
+                tc_commit(&ctl.drain);
+                mbar_wait(&ctl.drain, 0, abort, true);
+            }
+        }
+    } else if (warp >= 4 && warp < 8) {
+        // ------------------------------------------------------- x splitter
+        const int tid = threadIdx.x - 4 * 32;
+        int s = 0;
+        uint32_t ph = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+            for (int ks = 0; ks < k_stages; ++ks) {
+                if (!mbar_wait(&ctl.full[s], ph, abort)) {
+                    ok = false;
+                    break;
+                }
+                float4* xh = reinterpret_cast<float4*>(ring + s * kStageBytes);
+                float4* xl = xh + kTileBytes / 16;
+#pragma unroll 4
+                for (int i = tid; i < int(kTileBytes / 16); i += kSplitThreads) {
+                    const float4 v = xh[i];
+                    float4 h;
+                    h.x = rna_tf32(v.x);
+                    h.y = rna_tf32(v.y);
+                    h.z = rna_tf32(v.z);
+                    h.w = rna_tf32(v.w);
+                    xh[i] = h;
+                    xl[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+                }
+                // generic-proxy writes -> visible to the tensor core (async proxy)
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_arrive(&ctl.split[s]);
+                if (++s == kStages) {
+                    s = 0;
+                    ph ^= 1u;
+                }
+            }
+        }
+    } else if (warp >= 8) {
+        // --------------------------------------------------------- epilogue
+        const int q = warp & 3, half = (warp - 8) >> 2;
+        int cb = 0;
+        uint32_t cph = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+            const int64_t row = int64_t(t / n_tiles) * kBM + q * 32 + lane;
+            const int col0 = (t % n_tiles) * kBN + half * 64;
+            float acc[64];  // zeros + chunk sums, as the reference starts from a zero accumulator
+#pragma unroll
+            for (int j = 0; j < 64; ++j) acc[j] = 0.0f;
+            bool ok = true;
+            for (int ch = 0; ch < chunks; ++ch) {
+                const bool got = mbar_wait(&ctl.acc_full[cb], cph, abort);
+                if (!__all_sync(0xffffffffu, got)) {  // warp-uniform: tcgen05.ld is .sync.aligned
+                    *abort = 1;
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t ta = tmem + (uint32_t(q * 32) << 16) + uint32_t(cb * kBN + half * 64);
+#pragma unroll
+                for (int part = 0; part < 4; ++part) {
+                    float v[16];
+                    tmem_ld16(ta + uint32_t(part * 16), v);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) acc[part * 16 + j] += v[j];
+                }
+                tc_fence_before();
+                mbar_arrive(&ctl.acc_empty[cb]);
+                if (++cb == kAccBufs) {
+                    cb = 0;
+                    cph ^= 1u;
+                }
+            }
+            if (!ok) break;
+            if (row < g.m) {
+                float* yr = g.y + row * g.ldy;
+                const float* cr = g.c != nullptr ? g.c + row * g.ldc : nullptr;
+#pragma unroll
+                for (int j = 0; j < 64; j += 4) {
+                    const int col = col0 + j;
+                    if (col >= g.n) break;
+                    float o[4] = {acc[j], acc[j + 1], acc[j + 2], acc[j + 3]};
+                    const bool full4 = col + 4 <= g.n;
+                    if (g.bias != nullptr) {
+#pragma unroll
+                        for (int u = 0; u < 4; ++u)
+                            if (full4 || col + u < g.n) o[u] += __ldg(g.bias + col + u);
+                    }
+                    if (cr != nullptr) {
+                        if (full4 && g.vec_c) {
+                            const float4 cv = ldg4(cr + col);
+                            o[0] += cv.x;
+                            o[1] += cv.y;
+                            o[2] += cv.z;
+                            o[3] += cv.w;
+                        } else {
+#pragma unroll
+                            for (int u = 0; u < 4; ++u)
+                                if (col + u < g.n) o[u] += __ldg(cr + col + u);
+                        }
+                    }
+                    if (g.act == 1) {
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) o[u] = silu(o[u]);
+                    }
+                    if (full4 && g.vec_y) {
+                        float4* p = reinterpret_cast<float4*>(yr + col);
+                        float4 w = make_float4(o[0], o[1], o[2], o[3]);
+                        if (g.accumulate) w = f4_add(*p, w);
+                        *p = w;
+                    } else {
+#pragma unroll
+                        for (int u = 0; u < 4; ++u)
+                            if (col + u < g.n) yr[col + u] = g.accumulate ? yr[col + u] + o[u] : o[u];
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
+                     : "memory");
+    }
+    if (threadIdx.x == 0 && ctl.abort) raise_flag(g.flags, FMD_FLAG_WAIT_TIMEOUT);
+}
+
+// hi = rna_tf32(w), lo = w - hi, row-major [rows, cols] or, with transpose,
+// [cols, rows] (the K-major operand of dX = dY . w), output row stride ldo.
+__global__ void tf32_split_kernel(const float* __restrict__ w, int64_t rows, int64_t cols, int64_t ldw,
+                                  int transpose, float* __restrict__ hi, float* __restrict__ lo, int64_t ldo) {
+    const int64_t total = rows * cols;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total;
+         i += int64_t(gridDim.x) * blockDim.x) {
+        int64_t r, c, o;
+        if (transpose) {  // output row c, column r
+            c = i / rows;
+            r = i - c * rows;
+            o = c * ldo + r;
+        } else {
+            r = i / cols;
+            c = i - r * cols;
+            o = r * ldo + c;
+        }
+        const float v = w[r * ldw + c];
+        const float h = rna_tf32(v);
+        hi[o] = h;
+        lo[o] = v - h;
+    }
+}
+
+// ------------------------------------------------------------------- host
+
+using EncodeTiled = PFN_cuTensorMapEncodeTiled_v12000;
+using CtxGetCurrent = PFN_cuCtxGetCurrent_v4000;
+
+struct DriverCalls {
+    EncodeTiled encode = nullptr;
+    CtxGetCurrent ctx_get_current = nullptr;
+};
+
+// Driver entry points through the runtime (no link against libcuda).
+const DriverCalls& driver_calls() {
+    static DriverCalls calls;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            calls.encode = reinterpret_cast<EncodeTiled>(p);
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            calls.ctx_get_current = reinterpret_cast<CtxGetCurrent>(p);
+    });
+    return calls;
+}
+
+// [rows, cols] fp32 with row stride ld (elements), box [128 rows x 32 cols],
+// 128-byte swizzle, zero fill outside.
+CUresult encode_operand(EncodeTiled enc, CUtensorMap* map, const float* base, int64_t rows, int64_t cols,
+                        int64_t ld) {
+    const cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+    const cuuint64_t strides[1] = {cuuint64_t(ld) * sizeof(float)};
+    const cuuint32_t box[2] = {cuuint32_t(kBK), cuuint32_t(kBM)};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+struct DeviceInfo {
+    bool ready = false;
+    bool sm100 = false;
+    int sms = 0;
+};
+
+// Per-device facts and the one-time shared-memory opt-in (a function
+// attribute, set outside any stream capture on the first call).
+fmd_status device_info(DeviceInfo* out) {
+    static std::mutex mu;
+    static DeviceInfo info[64];
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return record_cuda_error(err);
+    if (dev < 0 || dev >= 64) return FMD_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lock(mu);
+    DeviceInfo& d = info[dev];
+    if (!d.ready) {
+        int major = 0, sms = 0;
+        if ((err = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess ||
+            (err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+            return record_cuda_error(err);
+        d.sm100 = major == 10;
+        d.sms = sms;
+        if (d.sm100) {
+            err = cudaFuncSetAttribute(wide_gemm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(kSmemBytes));
+            if (err != cudaSuccess) return record_cuda_error(err);
+        }
+        d.ready = true;
+    }
+    *out = d;
+    return FMD_OK;
+}
+
+}  // namespace
+}  // namespace fmd
+
+using namespace fmd;
+
+extern "C" {
+
+fmd_status fmd_tf32_split(const float* w, int64_t rows, int64_t cols, int64_t ldw, int32_t transpose, float* hi,
+                          float* lo, int64_t ldo, void* stream) {
+    if (rows < 0 || cols < 0 || (rows > 0 && cols > 0 && (w == nullptr || hi == nullptr || lo == nullptr)) ||
+        ldw < cols || ldo < (transpose ? rows : cols))
+        return FMD_ERR_INVALID_ARGUMENT;
+    if (rows == 0 || cols == 0) return FMD_OK;
+    tf32_split_kernel<<<grid_for(rows * cols, 256), 256, 0, as_stream(stream)>>>(w, rows, cols, ldw,
+                                                                                 transpose != 0, hi, lo, ldo);
+    return check_launch();
+}
+
+fmd_status fmd_gemm_tf32x3(const float* x, int64_t ldx, const float* w_hi, const float* w_lo, int64_t ldw,
+                           const float* bias, const float* c, int64_t ldc, float* y, int64_t ldy, int64_t m,
+                           int32_t n, int32_t k, int32_t act, int32_t accumulate, int32_t* flags, void* stream) {
+    if (m < 0 || n < 1 || k < 1 || m > (int64_t(1) << 31) - kBM || x == nullptr || w_hi == nullptr ||
+        w_lo == nullptr || y == nullptr || ldx < k || ldw < k || ldy < n || (c != nullptr && ldc < n) ||
+        (act != 0 && act != 1))
+        return FMD_ERR_INVALID_ARGUMENT;
+    // TMA: 16-byte aligned bases and row strides
+    if (!aligned16(x) || !aligned16(w_hi) || !aligned16(w_lo) || (ldx & 3) || (ldw & 3))
+        return FMD_ERR_UNSUPPORTED;
+    const int64_t tiles = ((m + kBM - 1) / kBM) * ((n + kBN - 1) / kBN);
+    if (tiles > INT32_MAX) return FMD_ERR_UNSUPPORTED;
+    DeviceInfo dev;
+    fmd_status st = device_info(&dev);
+    if (st != FMD_OK) return st;
+    if (!dev.sm100) return FMD_ERR_UNSUPPORTED;
+    if (m == 0) return FMD_OK;
+    const DriverCalls& drv = driver_calls();
+    if (drv.encode == nullptr || drv.ctx_get_current == nullptr)
+        return record_error_text(FMD_ERR_CUDA, "driver entry point cuTensorMapEncodeTiled unavailable", 0);
+    // The tensor-map encoder is a driver call: a host thread on which the runtime has not yet made the
+    // primary context current (a fresh autograd worker, say) gets it bound first.
+    CUcontext current = nullptr;
+    if (drv.ctx_get_current(&current) != CUDA_SUCCESS || current == nullptr) {
+        int dev_index = 0;
+        cudaError_t err = cudaGetDevice(&dev_index);
+        if (err == cudaSuccess) err = cudaSetDevice(dev_index);
+        if (err != cudaSuccess) return record_cuda_error(err);
+    }
+    CUtensorMap tx, twh, twl;
+    CUresult r = encode_operand(drv.encode, &tx, x, m, k, ldx);
+    if (r == CUDA_SUCCESS) r = encode_operand(drv.encode, &twh, w_hi, n, k, ldw);
+    if (r == CUDA_SUCCESS) r = encode_operand(drv.encode, &twl, w_lo, n, k, ldw);
+    if (r != CUDA_SUCCESS) return record_error_text(FMD_ERR_CUDA, "cuTensorMapEncodeTiled failed, CUresult", r);
+    WideArgs g;
+    g.bias = bias;
+    g.c = c;
+    g.ldc = ldc;
+    g.y = y;
+    g.ldy = ldy;
+    g.flags = flags;
+    g.m = m;
+    g.n = n;
+    g.k = k;
+    g.act = act;
+    g.accumulate = accumulate != 0;
+    g.vec_c = c != nullptr && aligned16(c) && (ldc & 3) == 0;
+    g.vec_y = aligned16(y) && (ldy & 3) == 0;
+    const int grid = int(tiles < dev.sms ? tiles : dev.sms);
+    wide_gemm_tf32x3_kernel<<<grid, kThreads, kSmemBytes, as_stream(stream)>>>(tx, twh, twl, g);
+    return check_launch();
+}
+
+}  // extern "C"

@@ -52,6 +52,7 @@ typedef int32_t fmd_status;
 #define FMD_FLAG_SKIN 8             /* an atom moved more than half the skin */
 #define FMD_FLAG_NONFINITE 16       /* a non-finite position or momentum */
 #define FMD_FLAG_CELL_RANGE 32      /* a fractional coordinate outside the cell grid */
+#define FMD_FLAG_WAIT_TIMEOUT 64    /* a bounded in-kernel wait gave up (about 1 s); outputs invalid */
 
 /* ---------------------------------------------------------------- library */
 
@@ -262,6 +263,31 @@ FMD_API fmd_status fmd_gemm_f32(const float* a, int64_t lda, const float* a_pre,
                                 const float* w, int64_t ldw, int32_t trans_w, const float* bias, float* y,
                                 int64_t ldy, float* y_pre, int64_t ldy_pre, int64_t m, int32_t n, int32_t k,
                                 int32_t act, int32_t accumulate, void* stream);
+
+/* ------------------------------------ dense layers (D2), tcgen05 3xTF32 */
+
+/* hi = rna_tf32(w), lo = w - hi for w [rows, cols] (row stride ldw), written
+ * [rows, cols], or [cols, rows] with transpose = 1 (the K-major operand of
+ * dX = dY . w), with row stride ldo (a multiple of 4 for fmd_gemm_tf32x3).
+ * Once per weight version: the weight split of
+ * fastmd/engine/kernels/triton_wide_gemm.py:132 (_split_kernel). */
+FMD_API fmd_status fmd_tf32_split(const float* w, int64_t rows, int64_t cols, int64_t ldw, int32_t transpose,
+                                  float* hi, float* lo, int64_t ldo, void* stream);
+
+/* y[m, n] (=|+=) act(x[m, :k] . w^T + bias + c) on the tcgen05 tensor cores
+ * at FP32 accuracy (3xTF32: x_lo w_hi + x_hi w_lo + x_hi w_hi, a fresh TMEM
+ * accumulator per 64-wide K chunk, the chunks summed in FP32), for w [n, k]
+ * given as its fmd_tf32_split pair (w_hi, w_lo, row stride ldw). bias [n]
+ * and the residual c [m, ldc] are optional; act 0 = identity, 1 = SiLU.
+ * x, w_hi, w_lo 16-byte aligned with ldx, ldw multiples of 4 (TMA), else
+ * FMD_ERR_UNSUPPORTED (as on a non-sm_100 device). A bounded in-kernel wait
+ * that expires raises FMD_FLAG_WAIT_TIMEOUT in flags (may be null).
+ * Replaces _wide_gemm_persistent / _wide_gemm_tiles behind linear and matmul
+ * (fastmd/engine/kernels/triton_wide_gemm.py:105, :120, :482, :534). */
+FMD_API fmd_status fmd_gemm_tf32x3(const float* x, int64_t ldx, const float* w_hi, const float* w_lo, int64_t ldw,
+                                   const float* bias, const float* c, int64_t ldc, float* y, int64_t ldy, int64_t m,
+                                   int32_t n, int32_t k, int32_t act, int32_t accumulate, int32_t* flags,
+                                   void* stream);
 
 /* ------------------------- MACE-architecture message passing (D1, D3, E2) */
 

@@ -57,6 +57,14 @@ def test_invalid_arguments_are_rejected_before_any_launch():
     assert lib.fmd_nhc_pre_force(None, None, None, 1, 1, 3, 1, 0, None, None) == 1
     assert lib.fmd_nhc_post_force(ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16), 1, 1, 3, 1, 0,
                                   None, None, None, None) == 1  # neither force dtype
+    p16 = ctypes.c_void_p(1 << 20)
+    assert lib.fmd_gemm_tf32x3(None, 8, p16, p16, 8, None, None, 0, p16, 8, 1, 8, 8, 0, 0, None, None) == 1
+    assert lib.fmd_gemm_tf32x3(p16, 8, p16, p16, 8, None, None, 0, p16, 8, 1, 8, 8, 2, 0, None, None) == 1  # act
+    # TMA operands: unaligned base or a row stride that is not a multiple of 16 bytes -> unsupported
+    assert lib.fmd_gemm_tf32x3(ctypes.c_void_p((1 << 20) + 4), 8, p16, p16, 8, None, None, 0, p16, 8, 1, 8, 8, 0, 0,
+                               None, None) == 3
+    assert lib.fmd_gemm_tf32x3(p16, 9, p16, p16, 8, None, None, 0, p16, 8, 1, 8, 8, 0, 0, None, None) == 3
+    assert lib.fmd_tf32_split(None, 2, 2, 2, 0, None, None, 2, None) == 1
 
 
 def test_no_cpu_fallback():
@@ -71,3 +79,7 @@ def test_no_cpu_fallback():
         ops.aligned_gather_cat3(x, x, idx, idx)
     with pytest.raises(FastMDLibraryError):
         ops.csr_segment_sum(x, idx, 2)
+    from fastmd_b200 import wide_gemm
+
+    with pytest.raises(FastMDLibraryError):
+        wide_gemm.linear(x, torch.zeros(16, 8))
