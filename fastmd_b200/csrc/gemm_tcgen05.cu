@@ -18,22 +18,29 @@
 // One persistent CTA per SM (512 threads) walks 128 x 128 output tiles, N
 // fastest (the column tiles of a row block run together and share x in L2):
 //   warp 0      TMA producer: x, w_hi, w_lo tiles [128 rows x 32 k] per K
-//               stage into a 3-stage ring, 128-byte swizzle, zero fill past m,
-//               n and k
-//   warp 1      TMEM owner (512 columns = 4 chunk accumulators of 128
-//               columns) and MMA issuer (one thread): per stage 4 K-steps of 8,
-//               three products each, M = 128, N = 128 (or the tile's width)
-//   warps 4-7   split x in place into x_hi and x_lo (elementwise on the
-//               swizzled bytes, so the layout is untouched)
+//               stage into a 4-stage shared-memory ring, 128-byte swizzle,
+//               zero fill past m, n and k
+//   warp 1      TMEM owner and MMA issuer (one thread): per stage 4 K-steps
+//               of 8, three products each, M = 128, N = 128 (or the tile's
+//               width); A (x_hi / x_lo) from TMEM, B (w) from shared memory
+//   warps 4-7   splitter: row r of the x tile (one thread per row, reading
+//               the swizzled tile) -> x_hi, x_lo in registers -> TMEM lane r
+//               (tcgen05.st), double-buffered A operand
 //   warps 8-15  epilogue: TMEM -> registers, chunk sums, bias, residual,
 //               SiLU, stores; warp w reads TMEM lanes 32 (w % 4) .. +31 (its
 //               32 rows) and columns 64 ((w - 8) / 4) .. +63
+// TMEM (512 columns): 3 chunk accumulators of 128 columns, then 2 A buffers
+// of 64 columns (x_hi k 0..31, x_lo k 0..31). Keeping A out of shared memory
+// halves the tensor core's shared-memory reads (B only), which at M = N = 128
+// in FP32 would otherwise use the whole shared-memory bandwidth.
 // Every mbarrier wait is bounded (about a second): on expiry the CTA raises
 // FMD_FLAG_WAIT_TIMEOUT, waits (bounded) for its copies and MMAs in flight,
 // frees its TMEM and returns. No cluster launch and no multicast.
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
+
+#include <string.h>
 
 #include <mutex>
 
@@ -43,26 +50,36 @@ namespace fmd {
 namespace {
 
 constexpr int kBM = 128, kBN = 128, kBK = 32, kChunkK = 64;
-constexpr int kStages = 3, kAccBufs = 4;
+constexpr int kStages = 4, kAccBufs = 3, kABufs = 2;
 constexpr int kThreads = 512;
 constexpr int kSplitThreads = 128, kEpiThreads = 256;
 constexpr uint32_t kTileBytes = kBM * kBK * 4;    // 16 KB, one operand tile of one stage
-constexpr uint32_t kStageBytes = 4 * kTileBytes;  // x_hi (TMA target), x_lo, w_hi, w_lo
-constexpr uint32_t kTmemCols = kAccBufs * kBN;    // 512
+constexpr uint32_t kStageBytes = 3 * kTileBytes;  // x (raw), w_hi, w_lo
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kAccCols = kBN;                // one chunk accumulator: 128 lanes x 128 fp32
+constexpr uint32_t kACols = 2 * kBK;              // one A buffer: x_hi then x_lo, 32 columns each
+constexpr uint32_t kABase = kAccBufs * kAccCols;  // 384
+static_assert(kABase + kABufs * kACols <= kTmemCols, "TMEM budget");
 constexpr unsigned long long kWaitNs = 1000000000ull;
 
 struct Ctrl {
-    uint64_t full[kStages];   // TMA bytes landed (1 arrival + tx)
-    uint64_t split[kStages];  // x split into hi/lo (kSplitThreads arrivals)
-    uint64_t empty[kStages];  // MMAs of the stage done (tcgen05.commit)
+    uint64_t full[kStages];        // TMA bytes landed (1 arrival + tx)
+    uint64_t empty[kStages];       // MMAs of the stage done (tcgen05.commit)
+    uint64_t a_full[kABufs];       // x_hi/x_lo of a stage in TMEM (kSplitThreads arrivals)
+    uint64_t a_empty[kABufs];      // MMAs reading that A buffer done (tcgen05.commit)
     uint64_t acc_full[kAccBufs];   // chunk accumulator complete (tcgen05.commit)
     uint64_t acc_empty[kAccBufs];  // chunk accumulator read out (kEpiThreads arrivals)
-    uint64_t drain;           // MMAs in flight on abort
+    uint64_t drain;                // MMAs in flight on abort
     uint32_t tmem_base;
     int32_t abort;
 };
 
-constexpr size_t kSmemBytes = size_t(kStages) * kStageBytes + sizeof(Ctrl) + 1024;  // + 1024-B alignment slack
+// Output staging: one 32 x 32 fp32 box (4 KB, 128-byte swizzle) per epilogue warp, stored by TMA.
+constexpr uint32_t kEpiBoxBytes = 32 * 32 * 4;
+constexpr uint32_t kEpiBytes = (kEpiThreads / 32) * kEpiBoxBytes;
+constexpr size_t kSmemBytes =
+    size_t(kStages) * kStageBytes + kEpiBytes + sizeof(Ctrl) + 1024;  // + 1024-B alignment slack
+static_assert(kSmemBytes <= 232448, "shared memory per block");
 
 struct WideArgs {
     const float* bias;  // [n] or null
@@ -75,6 +92,7 @@ struct WideArgs {
     int32_t n, k;
     int32_t act, accumulate;
     int32_t vec_c, vec_y;  // 16-byte row access valid
+    int32_t tma_y;         // y stored through tmap_y (else direct stores)
 };
 
 // ------------------------------------------------------------- PTX wrappers
@@ -142,6 +160,21 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
         : "memory");
 }
 
+// Tile store shared -> global (bulk group); the box outside the tensor is not written.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(su32(src))
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+__device__ __forceinline__ void bulk_wait_read_all() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ void tc_fence_before() {
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -155,12 +188,35 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
                  : "memory");
 }
 
-__device__ __forceinline__ void tc_mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                            uint32_t accumulate) {
+// D (=|+)= A . B^T with A [128 x 8] tf32 in TMEM (lane m, columns k) and B
+// from a shared-memory descriptor.
+__device__ __forceinline__ void tc_mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                               uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// 32 consecutive TMEM columns of this thread's lane (shape 32x32b, x32),
+// then the wait for the stores to land.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};\n\t"
+        "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+        "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+        "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+        "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+        "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+        "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+        "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+        "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
         : "memory");
 }
 
@@ -202,17 +258,80 @@ __device__ __forceinline__ uint32_t tf32_idesc(int m, int n) {
     return (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
 }
 
-__device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
+// SiLU as the reference's fused Triton epilogues evaluate it, x * sigmoid(x) with the hardware exp2
+// and an approximate divide (a few ulp; 0 for large negative x, x for large positive x).
+__device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 // ------------------------------------------------------------------ kernel
 
+__device__ __forceinline__ void advance(int& slot, uint32_t& phase, int slots) {
+    if (++slot == slots) {
+        slot = 0;
+        phase ^= 1u;
+    }
+}
+
+// o[j] = act(acc[j] + bias[col] + c[row, col]) (+ y[row, col] when accumulating) for the 32 columns
+// col0 .. col0 + 31 of this thread's row; nothing is read outside [0, m) x [0, n).
+__device__ __forceinline__ void finish_values(const WideArgs& g, int64_t row, int col0, const float* acc,
+                                              float (&o)[32]) {
+    const bool row_ok = row < g.m;
+    const float* cr = (g.c != nullptr && row_ok) ? g.c + row * g.ldc : nullptr;
+    const float* yr = (g.accumulate && row_ok) ? g.y + row * g.ldy : nullptr;
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+        const int col = col0 + j;
+        const bool full4 = col + 4 <= g.n;
+        float t[4] = {acc[j], acc[j + 1], acc[j + 2], acc[j + 3]};
+        if (g.bias != nullptr) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (col + u < g.n) t[u] += __ldg(g.bias + col + u);
+        }
+        if (cr != nullptr) {
+            if (full4 && g.vec_c) {
+                const float4 cv = ldg4(cr + col);
+                t[0] += cv.x;
+                t[1] += cv.y;
+                t[2] += cv.z;
+                t[3] += cv.w;
+            } else {
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    if (col + u < g.n) t[u] += __ldg(cr + col + u);
+            }
+        }
+        if (g.act == 1) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) t[u] = silu(t[u]);
+        }
+        if (yr != nullptr) {  // y (=|+=): the previous y, read before this thread's store
+            if (full4 && g.vec_y) {
+                const float4 yv = *reinterpret_cast<const float4*>(yr + col);
+                t[0] += yv.x;
+                t[1] += yv.y;
+                t[2] += yv.z;
+                t[3] += yv.w;
+            } else {
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    if (col + u < g.n) t[u] += yr[col + u];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) o[j + u] = t[u];
+    }
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     wide_gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_wh,
-                            const __grid_constant__ CUtensorMap tmap_wl, WideArgs g) {
+                            const __grid_constant__ CUtensorMap tmap_wl, const __grid_constant__ CUtensorMap tmap_y,
+                            WideArgs g) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char* ring = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                            ~uintptr_t(1023));
-    Ctrl& ctl = *reinterpret_cast<Ctrl*>(ring + kStages * kStageBytes);
+    unsigned char* epi_smem = ring + kStages * kStageBytes;
+    Ctrl& ctl = *reinterpret_cast<Ctrl*>(epi_smem + kEpiBytes);
     volatile int32_t* abort = &ctl.abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m_tiles = int((g.m + kBM - 1) / kBM);
@@ -225,8 +344,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&ctl.full[s], 1);
-            mbar_init(&ctl.split[s], kSplitThreads);
             mbar_init(&ctl.empty[s], 1);
+        }
+        for (int b = 0; b < kABufs; ++b) {
+            mbar_init(&ctl.a_full[b], kSplitThreads);
+            mbar_init(&ctl.a_empty[b], 1);
         }
         for (int b = 0; b < kAccBufs; ++b) {
             mbar_init(&ctl.acc_full[b], 1);
@@ -262,36 +384,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     unsigned char* st = ring + s * kStageBytes;
-                    mbar_expect_tx(&ctl.full[s], 3 * kTileBytes);
+                    mbar_expect_tx(&ctl.full[s], kStageBytes);
                     tma_load_2d(st, &tmap_x, &ctl.full[s], ks * kBK, m0);
-                    tma_load_2d(st + 2 * kTileBytes, &tmap_wh, &ctl.full[s], ks * kBK, n0);
-                    tma_load_2d(st + 3 * kTileBytes, &tmap_wl, &ctl.full[s], ks * kBK, n0);
+                    tma_load_2d(st + kTileBytes, &tmap_wh, &ctl.full[s], ks * kBK, n0);
+                    tma_load_2d(st + 2 * kTileBytes, &tmap_wl, &ctl.full[s], ks * kBK, n0);
                     armed |= 1u << s;
                     armed_ph = (armed_ph & ~(1u << s)) | (ph << s);
-                    if (++s == kStages) {
-                        s = 0;
-                        ph ^= 1u;
-                    }
+                    advance(s, ph, kStages);
                 }
             }
             if (!ok) {  // let the copies in flight land before the CTA exits
                 for (int i = 0; i < kStages; ++i)
                     if ((armed >> i) & 1u) mbar_wait(&ctl.full[i], (armed_ph >> i) & 1u, abort, true);
             } else {  // tail: the last stages' release arrivals land before the CTA exits
-                for (int i = 0; i < kStages && mbar_wait(&ctl.empty[s], ph ^ 1u, abort); ++i) {
-                    if (++s == kStages) {
-                        s = 0;
-                        ph ^= 1u;
-                    }
-                }
+                for (int i = 0; i < kStages && mbar_wait(&ctl.empty[s], ph ^ 1u, abort); ++i) advance(s, ph, kStages);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             // ------------------------------------------------- MMA issuer
             const uint32_t ring_addr = su32(ring);
-            int s = 0, cb = 0;
-            uint32_t ph = 0, cph = 0;
+            int s = 0, sa = 0, cb = 0;
+            uint32_t ph = 0, aph = 0, cph = 0;
             bool ok = true, issued = false;
             for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
                 const int n0 = (t % n_tiles) * kBN;
@@ -304,40 +418,37 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t d = tmem + uint32_t(cb * kBN);
+                    const uint32_t d = tmem + uint32_t(cb) * kAccCols;
                     const int ks_end = min(ks + kStagesPerChunk, k_stages);
                     uint32_t acc = 0;
                     for (; ks < ks_end; ++ks) {
-                        if (!mbar_wait(&ctl.full[s], ph, abort) || !mbar_wait(&ctl.split[s], ph, abort)) {
+                        if (!mbar_wait(&ctl.full[s], ph, abort) || !mbar_wait(&ctl.a_full[sa], aph, abort)) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
                         const uint32_t base = ring_addr + uint32_t(s) * kStageBytes;
-                        const uint64_t xh = sw128_desc(base), xl = sw128_desc(base + kTileBytes);
-                        const uint64_t wh = sw128_desc(base + 2 * kTileBytes), wl = sw128_desc(base + 3 * kTileBytes);
+                        const uint64_t wh = sw128_desc(base + kTileBytes), wl = sw128_desc(base + 2 * kTileBytes);
+                        const uint32_t xh = tmem + kABase + uint32_t(sa) * kACols, xl = xh + kBK;
+                        // the small cross terms first: x_lo w_hi, x_hi w_lo, then x_hi w_hi
 #pragma unroll
                         for (int kk = 0; kk < kBK / 8; ++kk) {
-                            tc_mma_tf32(d, xl + 2 * kk, wh + 2 * kk, idesc, acc);
+                            tc_mma_tf32_ts(d, xl + 8 * kk, wh + 2 * kk, idesc, acc);
                             acc = 1;
                         }
 #pragma unroll
-                        for (int kk = 0; kk < kBK / 8; ++kk) tc_mma_tf32(d, xh + 2 * kk, wl + 2 * kk, idesc, 1);
+                        for (int kk = 0; kk < kBK / 8; ++kk) tc_mma_tf32_ts(d, xh + 8 * kk, wl + 2 * kk, idesc, 1);
 #pragma unroll
-                        for (int kk = 0; kk < kBK / 8; ++kk) tc_mma_tf32(d, xh + 2 * kk, wh + 2 * kk, idesc, 1);
+                        for (int kk = 0; kk < kBK / 8; ++kk) tc_mma_tf32_ts(d, xh + 8 * kk, wh + 2 * kk, idesc, 1);
                         issued = true;
-                        tc_commit(&ctl.empty[s]);  // frees the stage once these MMAs are done
-                        if (++s == kStages) {
-                            s = 0;
-                            ph ^= 1u;
-                        }
+                        tc_commit(&ctl.empty[s]);     // the stage's shared memory is free once these are done
+                        tc_commit(&ctl.a_empty[sa]);  // and so is its A buffer
+                        advance(s, ph, kStages);
+                        advance(sa, aph, kABufs);
                     }
                     if (!ok) break;
                     tc_commit(&ctl.acc_full[cb]);
-                    if (++cb == kAccBufs) {
-                        cb = 0;
-                        cph ^= 1u;
-                    }
+                    advance(cb, cph, kAccBufs);
                 }
             }
             if (!ok && issued) {  // the MMAs in flight finish before TMEM is freed
@@ -347,36 +458,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp >= 4 && warp < 8) {
         // ------------------------------------------------------- x splitter
-        const int tid = threadIdx.x - 4 * 32;
-        int s = 0;
-        uint32_t ph = 0;
+        // thread = row r of the tile = TMEM lane r; the row's 32 floats sit in
+        // 8 16-byte chunks, chunk c at position c ^ (r % 8) (128-byte swizzle)
+        const int q = warp & 3, r = q * 32 + lane;
+        const uint32_t lane_addr = uint32_t(q * 32) << 16;
+        int s = 0, sa = 0;
+        uint32_t ph = 0, aph = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
             for (int ks = 0; ks < k_stages; ++ks) {
-                if (!mbar_wait(&ctl.full[s], ph, abort)) {
+                const bool got = mbar_wait(&ctl.full[s], ph, abort) && mbar_wait(&ctl.a_empty[sa], aph ^ 1u, abort);
+                if (!__all_sync(0xffffffffu, got)) {  // warp-uniform: tcgen05.st is .sync.aligned
+                    *abort = 1;
                     ok = false;
                     break;
                 }
-                float4* xh = reinterpret_cast<float4*>(ring + s * kStageBytes);
-                float4* xl = xh + kTileBytes / 16;
-#pragma unroll 4
-                for (int i = tid; i < int(kTileBytes / 16); i += kSplitThreads) {
-                    const float4 v = xh[i];
-                    float4 h;
-                    h.x = rna_tf32(v.x);
-                    h.y = rna_tf32(v.y);
-                    h.z = rna_tf32(v.z);
-                    h.w = rna_tf32(v.w);
-                    xh[i] = h;
-                    xl[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+                const float4* row = reinterpret_cast<const float4*>(ring + s * kStageBytes + r * 128);
+                float v[32], h[32];
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const float4 f = row[c ^ (r & 7)];
+                    v[4 * c] = f.x;
+                    v[4 * c + 1] = f.y;
+                    v[4 * c + 2] = f.z;
+                    v[4 * c + 3] = f.w;
                 }
-                // generic-proxy writes -> visible to the tensor core (async proxy)
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                mbar_arrive(&ctl.split[s]);
-                if (++s == kStages) {
-                    s = 0;
-                    ph ^= 1u;
-                }
+#pragma unroll
+                for (int j = 0; j < 32; ++j) h[j] = rna_tf32(v[j]);
+                tc_fence_after();
+                const uint32_t ta = tmem + lane_addr + kABase + uint32_t(sa) * kACols;
+                tmem_st32(ta, h);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] -= h[j];
+                tmem_st32(ta + kBK, v);
+                tc_fence_before();
+                mbar_arrive(&ctl.a_full[sa]);
+                advance(s, ph, kStages);
+                advance(sa, aph, kABufs);
             }
         }
     } else if (warp >= 8) {
@@ -399,7 +517,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t ta = tmem + (uint32_t(q * 32) << 16) + uint32_t(cb * kBN + half * 64);
+                const uint32_t ta = tmem + (uint32_t(q * 32) << 16) + uint32_t(cb) * kAccCols + uint32_t(half * 64);
 #pragma unroll
                 for (int part = 0; part < 4; ++part) {
                     float v[16];
@@ -409,56 +527,50 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tc_fence_before();
                 mbar_arrive(&ctl.acc_empty[cb]);
-                if (++cb == kAccBufs) {
-                    cb = 0;
-                    cph ^= 1u;
-                }
+                advance(cb, cph, kAccBufs);
             }
             if (!ok) break;
-            if (row < g.m) {
+            if (g.tma_y) {
+                // stage each 32 x 32 piece in this warp's box (row = lane, 128-byte swizzle) and let
+                // TMA store it: whole lines to L2 instead of 16-byte pieces of 32 rows
+                float* box = reinterpret_cast<float*>(epi_smem + (warp - 8) * kEpiBoxBytes);
+                const int row0 = int(row - lane);
+#pragma unroll
+                for (int piece = 0; piece < 2; ++piece) {
+                    float o[32];
+                    finish_values(g, row, col0 + piece * 32, acc + piece * 32, o);
+                    if (lane == 0) bulk_wait_read_all();  // the previous store has read the box
+                    __syncwarp();
+                    float4* b4 = reinterpret_cast<float4*>(box + lane * 32);
+#pragma unroll
+                    for (int c = 0; c < 8; ++c)
+                        b4[c ^ (lane & 7)] = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0 && row0 < g.m && col0 + piece * 32 < g.n)  // boxes with no element in y skipped
+                        tma_store_2d(&tmap_y, box, col0 + piece * 32, row0);
+                }
+            } else if (row < g.m) {
                 float* yr = g.y + row * g.ldy;
-                const float* cr = g.c != nullptr ? g.c + row * g.ldc : nullptr;
 #pragma unroll
-                for (int j = 0; j < 64; j += 4) {
-                    const int col = col0 + j;
-                    if (col >= g.n) break;
-                    float o[4] = {acc[j], acc[j + 1], acc[j + 2], acc[j + 3]};
-                    const bool full4 = col + 4 <= g.n;
-                    if (g.bias != nullptr) {
+                for (int piece = 0; piece < 2; ++piece) {
+                    float o[32];
+                    finish_values(g, row, col0 + piece * 32, acc + piece * 32, o);
 #pragma unroll
-                        for (int u = 0; u < 4; ++u)
-                            if (full4 || col + u < g.n) o[u] += __ldg(g.bias + col + u);
-                    }
-                    if (cr != nullptr) {
-                        if (full4 && g.vec_c) {
-                            const float4 cv = ldg4(cr + col);
-                            o[0] += cv.x;
-                            o[1] += cv.y;
-                            o[2] += cv.z;
-                            o[3] += cv.w;
+                    for (int j = 0; j < 32; j += 4) {
+                        const int col = col0 + piece * 32 + j;
+                        if (col + 4 <= g.n && g.vec_y) {
+                            *reinterpret_cast<float4*>(yr + col) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
                         } else {
 #pragma unroll
                             for (int u = 0; u < 4; ++u)
-                                if (col + u < g.n) o[u] += __ldg(cr + col + u);
+                                if (col + u < g.n) yr[col + u] = o[j + u];
                         }
-                    }
-                    if (g.act == 1) {
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) o[u] = silu(o[u]);
-                    }
-                    if (full4 && g.vec_y) {
-                        float4* p = reinterpret_cast<float4*>(yr + col);
-                        float4 w = make_float4(o[0], o[1], o[2], o[3]);
-                        if (g.accumulate) w = f4_add(*p, w);
-                        *p = w;
-                    } else {
-#pragma unroll
-                        for (int u = 0; u < 4; ++u)
-                            if (col + u < g.n) yr[col + u] = g.accumulate ? yr[col + u] + o[u] : o[u];
                     }
                 }
             }
         }
+        if (g.tma_y && lane == 0) bulk_wait_all();  // stores complete before the CTA exits
     }
 
     tc_fence_before();
@@ -526,10 +638,10 @@ const DriverCalls& driver_calls() {
 // [rows, cols] fp32 with row stride ld (elements), box [128 rows x 32 cols],
 // 128-byte swizzle, zero fill outside.
 CUresult encode_operand(EncodeTiled enc, CUtensorMap* map, const float* base, int64_t rows, int64_t cols,
-                        int64_t ld) {
+                        int64_t ld, uint32_t box_rows = kBM) {
     const cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
     const cuuint64_t strides[1] = {cuuint64_t(ld) * sizeof(float)};
-    const cuuint32_t box[2] = {cuuint32_t(kBK), cuuint32_t(kBM)};
+    const cuuint32_t box[2] = {cuuint32_t(kBK), box_rows};
     const cuuint32_t estr[2] = {1, 1};
     return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -623,6 +735,11 @@ fmd_status fmd_gemm_tf32x3(const float* x, int64_t ldx, const float* w_hi, const
     if (r == CUDA_SUCCESS) r = encode_operand(drv.encode, &twh, w_hi, n, k, ldw);
     if (r == CUDA_SUCCESS) r = encode_operand(drv.encode, &twl, w_lo, n, k, ldw);
     if (r != CUDA_SUCCESS) return record_error_text(FMD_ERR_CUDA, "cuTensorMapEncodeTiled failed, CUresult", r);
+    // y through TMA stores (32 x 32 boxes) when its base and row stride allow it
+    CUtensorMap ty;
+    memset(&ty, 0, sizeof(ty));
+    const bool tma_y = aligned16(y) && (ldy & 3) == 0 &&
+                       encode_operand(drv.encode, &ty, y, m, n, ldy, 32) == CUDA_SUCCESS;
     WideArgs g;
     g.bias = bias;
     g.c = c;
@@ -637,8 +754,9 @@ fmd_status fmd_gemm_tf32x3(const float* x, int64_t ldx, const float* w_hi, const
     g.accumulate = accumulate != 0;
     g.vec_c = c != nullptr && aligned16(c) && (ldc & 3) == 0;
     g.vec_y = aligned16(y) && (ldy & 3) == 0;
+    g.tma_y = tma_y;
     const int grid = int(tiles < dev.sms ? tiles : dev.sms);
-    wide_gemm_tf32x3_kernel<<<grid, kThreads, kSmemBytes, as_stream(stream)>>>(tx, twh, twl, g);
+    wide_gemm_tf32x3_kernel<<<grid, kThreads, kSmemBytes, as_stream(stream)>>>(tx, twh, twl, ty, g);
     return check_launch();
 }
 

@@ -88,6 +88,10 @@ def test_residual_silu_accumulate_and_ieee():
     ref = torch.nn.functional.silu(torch.from_numpy(ow.gemm_3xtf32(x.numpy(), w.numpy(), b.numpy()))) + c.double()
     scale = 1.1 * torch.from_numpy(ow.error_scale(x.numpy(), w.numpy(), b.numpy())) + ref.abs()
     assert ((y2.cpu().double() - ref).abs() / scale).max() < TOL
+    # an output row stride the TMA cannot take (257 floats): the direct-store epilogue
+    out = torch.empty(m, n + 1, device="cuda")[:, :n]
+    wide_gemm.linear_into(out, xd, wd, bd)
+    _check(out, x, w, b)
     # the IEEE parity path through the same surface
     yi = wide_gemm.linear(xd, wd, bd, precision="ieee")
     _check(yi, x, w, b, tol=2e-6)
