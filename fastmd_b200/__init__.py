@@ -4,6 +4,7 @@ Surfaces mirroring the reference: ``ops`` (fastmd.ops), ``graph`` (fastmd.graph 
 ``energy_derivative`` (fastmd.engine), ``gpu_nhc`` and ``whole_step`` (fastmd.execution /
 fastmd.interfaces), ``mace`` (the MACE-architecture energy tap).
 """
-from fastmd_b200 import _lib, energy_derivative, gpu_nhc, graph, mace, ops, units, whole_step, wide_gemm  # noqa: F401
+from fastmd_b200 import (  # noqa: F401
+    _lib, energy_derivative, gpu_nhc, graph, mace, ops, segment_attention, units, whole_step, wide_gemm)
 
 __all__ = ["energy_derivative", "gpu_nhc", "graph", "mace", "ops", "units", "whole_step"]

@@ -24,10 +24,12 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
           "--expt-relaxed-constexpr", "-I", str(INCLUDE), "-I", str(CSRC)]
 # Per-file flags: the integrator rounds every operation as NumPy does (no FMA contraction); the
-# neighbour predicates follow the reference's FP32 operation order (no contraction either).
+# neighbour predicates and the segment-attention recurrences follow the reference's FP32 operation
+# order (no contraction either).
 EXTRA = {
     "nhc.cu": ["--fmad=false"],
     "neighbors.cu": ["--fmad=false"],
+    "segment_attention.cu": ["--fmad=false"],
 }
 
 

@@ -264,6 +264,50 @@ FMD_API fmd_status fmd_gemm_f32(const float* a, int64_t lda, const float* a_pre,
                                 int64_t ldy, float* y_pre, int64_t ldy_pre, int64_t m, int32_t n, int32_t k,
                                 int32_t act, int32_t accumulate, void* stream);
 
+/* ------------------------------------------- segment attention (C2) */
+
+/* out[s, :] = sum over the rows i of segment s of softmax(logits[i, :] over
+ * the segment, per column) * value[i, :], over a CSR (off [S+1] int64; perm
+ * [off[S]] int64 row ids, or null for the identity CSR row = j). The online
+ * recurrence of the reference in FP32, per segment in CSR order. out, lse,
+ * seg_max, seg_denom are [S, dim] contiguous; lse (m + log denom, -inf for an
+ * empty or skipped segment), seg_max and seg_denom (the paired backward's
+ * statistics) are optional. skip_segment (or -1) runs no rows: out 0.
+ * Row ids outside [0, rows) raise FMD_FLAG_INDEX_RANGE and are skipped.
+ * Replaces _csr_segment_attention_fwd and, called once per side,
+ * _paired_csr_segment_attention_fwd
+ * (fastmd/models/matris/op/triton_segment_attention.py:62, :210). */
+FMD_API fmd_status fmd_segment_attention(const float* logits, int64_t ldl, const float* value, int64_t ldv,
+                                         const int64_t* perm, const int64_t* off, int64_t rows, int64_t num_segment,
+                                         int32_t dim, int64_t skip_segment, float* out, float* lse, float* seg_max,
+                                         float* seg_denom, int32_t* flags, void* stream);
+
+/* Backward of fmd_segment_attention: per segment the statistics again, then
+ * per row alpha = e^(l - m) / denom, grad_value = alpha g, grad_logits =
+ * alpha g (v - out) (+ alpha glse when glse is given). Rows of no visited
+ * segment (the skipped one, rows outside a partial CSR) are not written.
+ * Replaces _csr_segment_attention_bwd (triton_segment_attention.py:128). */
+FMD_API fmd_status fmd_segment_attention_bwd(const float* logits, int64_t ldl, const float* value, int64_t ldv,
+                                             const float* out, const float* gout, const float* glse,
+                                             const int64_t* perm, const int64_t* off, int64_t rows,
+                                             int64_t num_segment, int32_t dim, int64_t skip_segment,
+                                             float* grad_logits, int64_t ldgl, float* grad_value, int64_t ldgv,
+                                             int32_t* flags, void* stream);
+
+/* Row backward of the paired attention (two segmentations of the same rows
+ * sharing value): statistics [S, dim] of both sides from
+ * fmd_segment_attention, per-row segment ids segment_a / segment_b. A row's
+ * side in skip_segment contributes exactly 0. grad_value [rows, dim]
+ * contiguous. Replaces _paired_segment_attention_bwd_rows
+ * (triton_segment_attention.py:319). */
+FMD_API fmd_status fmd_paired_segment_attention_bwd_rows(
+    const float* logits_a, int64_t ldla, const float* logits_b, int64_t ldlb, const float* value, int64_t ldv,
+    const float* gout_a, const float* gout_b, const float* out_a, const float* out_b, const float* max_a,
+    const float* denom_a, const float* max_b, const float* denom_b, const int64_t* segment_a,
+    const int64_t* segment_b, const float* glse_a, const float* glse_b, int64_t rows, int64_t num_segment,
+    int32_t dim, int64_t skip_segment, float* grad_logits_a, int64_t ldga, float* grad_logits_b, int64_t ldgb,
+    float* grad_value, int32_t* flags, void* stream);
+
 /* ------------------------------------ dense layers (D2), tcgen05 3xTF32 */
 
 /* hi = rna_tf32(w), lo = w - hi for w [rows, cols] (row stride ldw), written

@@ -12,7 +12,10 @@ used) and runs, on CPU:
   ``_aligned_gather_cat3_fwd/_bwd`` and ``_aligned_gather_cat4_fwd/_bwd``
   (fastmd/models/matris/op/triton_gather_cat.py:30/:59/:203/:236),
   ``_csr_segsum_fwd`` and ``_csr_segsum_bwd_rows``
-  (fastmd/models/matris/op/triton_csr_segment_sum.py:71/:184), and the
+  (fastmd/models/matris/op/triton_csr_segment_sum.py:71/:184), the segment
+  attention kernels ``_csr_segment_attention_fwd/_bwd``, ``_paired_csr_segment_attention_fwd``
+  and ``_paired_segment_attention_bwd_rows``
+  (fastmd/models/matris/op/triton_segment_attention.py:62/:128/:210/:319), and the
   fixed-capacity re-filter ``_count_neighbors_kernel`` /
   ``_materialize_neighbors_kernel`` (fastmd/graph/fixed_capacity_builder.py:98/:189)
   on candidate lists of a dense search, followed by the reference's
@@ -126,6 +129,85 @@ def segment_sum_cases(torch, cs):
         out[f"segsum_{tag}_gvalue"] = gv.numpy()
         if weighted:
             out[f"segsum_{tag}_gweight"] = gw.numpy()
+    return out
+
+
+def segment_attention_cases(torch, sa):
+    """``_csr_segment_attention_fwd/_bwd`` and the paired forward / row backward
+    (fastmd/models/matris/op/triton_segment_attention.py:62/:128/:210/:319)."""
+    out = {}
+    rng = np.random.default_rng(13)
+    # rows, segments, width, identity CSR, skip segment, lse
+    cases = {"perm_lse": (120, 17, 32, False, -1, True), "identity_skip": (90, 12, 128, True, 11, False),
+             "odd_lse_skip": (77, 9, 5, False, 3, True), "wide_empty": (64, 40, 64, False, -1, True)}
+    for tag, (rows, S, D, identity, skip, lse) in cases.items():
+        seg = rng.integers(0, S, rows).astype(np.int64)
+        if tag == "wide_empty":
+            seg = rng.choice(np.arange(0, S, 3), rows).astype(np.int64)  # two thirds of the segments empty
+        if identity:
+            seg = np.sort(seg)
+        perm = np.argsort(seg, kind="stable").astype(np.int64)
+        off = np.searchsorted(seg[perm], np.arange(S + 1)).astype(np.int64)
+        L = (3.0 * rng.standard_normal((rows, D))).astype(np.float32)
+        V = rng.standard_normal((rows, D)).astype(np.float32)
+        G = rng.standard_normal((S, D)).astype(np.float32)
+        GL = rng.standard_normal((S, D)).astype(np.float32)
+        t = {k: torch.from_numpy(v) for k, v in dict(seg=seg, perm=perm, off=off, L=L, V=V, G=G, GL=GL).items()}
+        blk = 1 << (D - 1).bit_length()
+        y = torch.empty(S, D)
+        ls = torch.empty(S, D) if lse else None
+        sa._csr_segment_attention_fwd[(S,)](
+            t["L"], t["V"], t["seg"] if identity else t["perm"], t["off"], y, ls, skip, D=D, LOG_S0=D, LOG_S1=1,
+            VAL_S0=D, VAL_S1=1, BLK=blk, IDENTITY_PERM=identity, HAS_SKIP=skip >= 0, STORE_LSE=lse)
+        gl = torch.zeros(rows, D)
+        gv = torch.zeros(rows, D)
+        sa._csr_segment_attention_bwd[(S,)](
+            t["L"], t["V"], y, t["G"], t["seg"] if identity else t["perm"], t["off"], gl, gv,
+            t["GL"] if lse else None, skip, D=D, LOG_S0=D, LOG_S1=1, VAL_S0=D, VAL_S1=1, GL_S0=D, BLK=blk,
+            IDENTITY_PERM=identity, HAS_SKIP=skip >= 0, HAS_GLSE=lse)
+        out.update({f"sa_{tag}_{k}": v for k, v in dict(seg=seg, perm=perm, off=off, L=L, V=V, G=G).items()})
+        if lse:
+            out[f"sa_{tag}_GL"] = GL
+            out[f"sa_{tag}_lse"] = ls.numpy()
+        out[f"sa_{tag}_meta"] = np.array([S, int(identity), skip, int(lse)], dtype=np.int64)
+        out[f"sa_{tag}_out"] = y.numpy()
+        out[f"sa_{tag}_glogits"] = gl.numpy()
+        out[f"sa_{tag}_gvalue"] = gv.numpy()
+    # paired: two CSRs over the same rows sharing the values
+    for tag, (rows, S, D, skip, lse) in {"pair": (110, 14, 32, -1, True), "pair_skip": (96, 10, 20, 9, False)}.items():
+        sa_, sb_ = rng.integers(0, S, rows).astype(np.int64), rng.integers(0, S, rows).astype(np.int64)
+        pa, pb = np.argsort(sa_, kind="stable").astype(np.int64), np.argsort(sb_, kind="stable").astype(np.int64)
+        oa = np.searchsorted(sa_[pa], np.arange(S + 1)).astype(np.int64)
+        ob = np.searchsorted(sb_[pb], np.arange(S + 1)).astype(np.int64)
+        La = (2.0 * rng.standard_normal((rows, D))).astype(np.float32)
+        Lb = (2.0 * rng.standard_normal((rows, D))).astype(np.float32)
+        V = rng.standard_normal((rows, D)).astype(np.float32)
+        Ga, Gb = rng.standard_normal((S, D)).astype(np.float32), rng.standard_normal((S, D)).astype(np.float32)
+        GLa, GLb = rng.standard_normal((S, D)).astype(np.float32), rng.standard_normal((S, D)).astype(np.float32)
+        arrays = dict(sa=sa_, sb=sb_, pa=pa, pb=pb, oa=oa, ob=ob, La=La, Lb=Lb, V=V, Ga=Ga, Gb=Gb, GLa=GLa, GLb=GLb)
+        t = {k: torch.from_numpy(v) for k, v in arrays.items()}
+        blk = 1 << (D - 1).bit_length()
+        res = {k: torch.empty(S, D) for k in ("out_a", "out_b", "max_a", "denom_a", "max_b", "denom_b")}
+        lse_a, lse_b = (torch.empty(S, D), torch.empty(S, D)) if lse else (None, None)
+        sa._paired_csr_segment_attention_fwd[(S,)](
+            t["La"], t["Lb"], t["V"], t["pa"], t["oa"], t["pb"], t["ob"], res["out_a"], res["out_b"], res["max_a"],
+            res["denom_a"], res["max_b"], res["denom_b"], lse_a, lse_b, skip, D=D, LOGA_S0=D, LOGA_S1=1,
+            LOGB_S0=D, LOGB_S1=1, VAL_S0=D, VAL_S1=1, BLK=blk, IDENTITY_A=False, IDENTITY_B=False,
+            HAS_SKIP=skip >= 0, STORE_LSE=lse)
+        gla, glb, gv = torch.empty(rows, D), torch.empty(rows, D), torch.empty(rows, D)
+        bd = min(blk, 128)
+        sa._paired_segment_attention_bwd_rows[((rows + 7) // 8, (D + bd - 1) // bd)](
+            t["La"], t["Lb"], t["V"], t["Ga"], t["Gb"], res["out_a"], res["out_b"], res["max_a"], res["denom_a"],
+            res["max_b"], res["denom_b"], t["sa"], t["sb"], gla, glb, gv, t["GLa"] if lse else None,
+            t["GLb"] if lse else None, rows, skip, D=D, LOGA_S0=D, LOGA_S1=1, LOGB_S0=D, LOGB_S1=1, VAL_S0=D,
+            VAL_S1=1, GLA_S0=D, GLB_S0=D, BM=8, BD=bd, HAS_SKIP=skip >= 0, HAS_GLSE=lse)
+        out.update({f"psa_{tag}_{k}": v for k, v in arrays.items()})
+        out[f"psa_{tag}_meta"] = np.array([S, skip, int(lse)], dtype=np.int64)
+        out.update({f"psa_{tag}_{k}": v.numpy() for k, v in res.items()})
+        if lse:
+            out[f"psa_{tag}_lse_a"], out[f"psa_{tag}_lse_b"] = lse_a.numpy(), lse_b.numpy()
+        out[f"psa_{tag}_glogits_a"], out[f"psa_{tag}_glogits_b"] = gla.numpy(), glb.numpy()
+        out[f"psa_{tag}_gvalue"] = gv.numpy()
     return out
 
 
@@ -300,12 +382,14 @@ def main(reference: str) -> None:
     import fastmd.graph.fixed_capacity_builder as fcb
     import fastmd.models.matris.op.triton_csr_segment_sum as cs
     import fastmd.models.matris.op.triton_gather_cat as gc
+    import fastmd.models.matris.op.triton_segment_attention as sa
 
     np.savez_compressed(HERE / "gather_cat.npz", **gather_cat_cases(torch, gc))
     np.savez_compressed(HERE / "segment_sum.npz", **segment_sum_cases(torch, cs))
     np.savez_compressed(HERE / "nhc.npz", **nhc_cases(torch, gpu_nhc))
     np.savez_compressed(HERE / "neighbors.npz", **neighbor_cases(torch, fcb))
     np.savez_compressed(HERE / "radial.npz", **radial_cases(torch))
+    np.savez_compressed(HERE / "segment_attention.npz", **segment_attention_cases(torch, sa))
     for path in sorted(HERE.glob("*.npz")):
         print(path.name, path.stat().st_size)
 
