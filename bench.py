@@ -457,6 +457,13 @@ def _ops_c2(device):
         call("fmd_csr_segment_sum", ptr(y), 256, None, 0, None, ptr(offsets), n, 256, -1, ptr(seg), 256, sp)
 
     t_ss = timed(segsum)
+    # segment attention (MatRIS receiver softmax-weighted sum) on the same receiver CSR, width 128
+    from fastmd_b200.segment_attention import segment_attention
+
+    logits = torch.randn(E, D, device=device, generator=g)
+    vals = torch.randn(E, D, device=device, generator=g)
+    t_sa = timed(lambda: segment_attention(logits, vals, center, n, off=offsets, identity_perm=True))
+    b_sa = 2 * E * D * 4 + (n + 1) * 8 + n * D * 4
     b_nl = E * (8 + 8 + 12 + 4) + n * (12 + 16)
     b_gc = E * (2 * D + 8) * 4 + 2 * E * 8 + E * 8 * 4 + n * D * 4
     b_ss = E * 256 * 4 + (n + 1) * 8 + n * 256 * 4
@@ -474,7 +481,7 @@ def _ops_c2(device):
                                                "achieved_TFLOPs": round(f_mlp / (t_mlp * 1e-3) / 1e12, 2)},
             "edge_mlp_264_256_256_tf32x3_tcgen05": _tc_line(f_mlp, t_tc, E, tf32_peak, tf32_kind),
             "edge_linear_264_256_silu_tf32x3_tcgen05": _tc_line(2.0 * E * 264 * 256, t_l1, E, tf32_peak, tf32_kind),
-            "segment_sum_256": hb(b_ss, t_ss)}
+            "segment_sum_256": hb(b_ss, t_ss), "segment_attention_128": hb(b_sa, t_sa)}
 
 
 def _tc_line(flops, ms, rows, tf32_peak, kind):

@@ -60,6 +60,7 @@ _SIGNATURES: dict[str, list] = {
     "fmd_gemm_tf32x3": [_P, _I64, _P, _P, _I64, _P, _P, _I64, _P, _I64, _I64, _I32, _I32, _I32, _I32, _P, _P],
     "fmd_mace_edge_geometry": [_P, _P, _P, _P, _I64, c_float, _I32, _I32, _P, _P, _P],
     "fmd_mace_edge_geometry_bwd": [_P, _P, _P, c_float, _I32, _I32, _P, _P, _P, _P, _I64, _P, c_float, _I32, _P],
+    "fmd_mace_edge_virial": [_P, _P, _P, c_float, _I32, _I32, _P, _I64, _P, _P, c_float, _P, _P, _I32, _P],
     "fmd_mace_message": [_P, _I32, _P, _P, _P, _P, _P, _I64, _I32, c_float, _P, _P, _P],
     "fmd_mace_message_bwd": [_P, _P, _P, _I32, _P, _P, _P, _P, _P, _P, _P, _I64, _I32, c_float, _P, _P, _I32, _P, _P,
                              _P],
@@ -116,7 +117,8 @@ def check(status: int, what: str) -> None:
 
 
 # kernels each entry point launches (for the launch count of a step); the default is one
-KERNELS_PER_CALL = {"fmd_refilter_edges": 2, "fmd_refilter_edges_noalloc": 2, "fmd_mace_message_bwd": 2}
+KERNELS_PER_CALL = {"fmd_refilter_edges": 2, "fmd_refilter_edges_noalloc": 2, "fmd_mace_message_bwd": 2,
+                    "fmd_mace_edge_virial": 2}
 
 
 def fused_step_kernels(n_layers: int) -> int:

@@ -104,6 +104,63 @@ __device__ __forceinline__ float3 edge_grad_r(const float4 y, const float* gy, c
     return gr;
 }
 
+// Cell gradient and virial of the edge geometry: per edge g = d(loss)/d(r_e),
+// image_grad[a][b] = sum_e image_e[a] g_b (d(loss)/d(cell), r_e = pos_j - pos_i
+// + image_e . cell) and virial[a][b] = sum_e r_e[a] g_b. Deterministic: a fixed
+// grid, each thread a fixed stride of edges summed in double, the CTA partials
+// reduced in a fixed order by a second single-CTA pass.
+constexpr int kVirialBlocks = 296, kVirialThreads = 256;
+static_assert(FMD_EDGE_VIRIAL_WORKSPACE_DOUBLES >= kVirialBlocks * 18, "virial workspace");
+
+__global__ void __launch_bounds__(kVirialThreads) edge_virial_partial_kernel(
+    const float4* __restrict__ ysh, const float* __restrict__ gy, const float* __restrict__ gphi, Geo g,
+    const float* __restrict__ edge_image, int64_t n_edges, const int64_t* __restrict__ n_real,
+    double* __restrict__ partial) {
+    __shared__ double red[kVirialThreads / 32][18];
+    const int64_t n = n_real != nullptr ? min(*n_real, n_edges) : n_edges;
+    double acc[18];
+#pragma unroll
+    for (int i = 0; i < 18; ++i) acc[i] = 0.0;
+    for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < n; e += int64_t(gridDim.x) * blockDim.x) {
+        const float4 y = ysh[e];
+        const float3 gr = edge_grad_r(y, gy + 3 * e, gphi + e * g.n_basis, g);
+        const float gv[3] = {gr.x, gr.y, gr.z};
+        const float r[3] = {y.x * y.w * kInvSqrt3, y.y * y.w * kInvSqrt3, y.z * y.w * kInvSqrt3};
+        const float im[3] = {edge_image[3 * e], edge_image[3 * e + 1], edge_image[3 * e + 2]};
+#pragma unroll
+        for (int a = 0; a < 3; ++a)
+#pragma unroll
+            for (int b = 0; b < 3; ++b) {
+                acc[3 * a + b] += double(im[a]) * double(gv[b]);
+                acc[9 + 3 * a + b] += double(r[a]) * double(gv[b]);
+            }
+    }
+#pragma unroll
+    for (int i = 0; i < 18; ++i) {
+        double v = acc[i];
+        for (int d = 16; d > 0; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5][i] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x < 18) {
+        double v = 0.0;
+        for (int w = 0; w < kVirialThreads / 32; ++w) v += red[w][threadIdx.x];
+        partial[blockIdx.x * 18 + threadIdx.x] = v;
+    }
+}
+
+__global__ void edge_virial_final_kernel(const double* __restrict__ partial, int blocks, float scale,
+                                         float* __restrict__ image_grad, float* __restrict__ virial, int accumulate) {
+    const int i = threadIdx.x;
+    if (i >= 18) return;
+    double v = 0.0;
+    for (int b = 0; b < blocks; ++b) v += partial[b * 18 + i];
+    float* out = i < 9 ? image_grad : virial;
+    if (out == nullptr) return;
+    const float x = float(v) * scale;
+    out[i % 9] = accumulate ? out[i % 9] + x : x;
+}
+
 // dpos[a] = sum over edges sending from a of g_r - sum over edges received by a of g_r
 __global__ void edge_geometry_bwd_kernel(const float4* __restrict__ ysh, const float* __restrict__ gy,
                                          const float* __restrict__ gphi, Geo g, const int32_t* __restrict__ edge_index,
@@ -428,6 +485,21 @@ fmd_status fmd_mace_edge_geometry_bwd(const float* ysh, const float* grad_y, con
     edge_geometry_bwd_kernel<<<grid_for(n_atoms, 128), 128, 0, as_stream(stream)>>>(
         reinterpret_cast<const float4*>(ysh), grad_y, grad_phi, g, edge_index, recv_off, send_off, send_perm,
         n_atoms, grad_positions, scale, accumulate);
+    return check_launch();
+}
+
+fmd_status fmd_mace_edge_virial(const float* ysh, const float* grad_y, const float* grad_phi, float r_max,
+                                int32_t n_basis, int32_t poly_p, const float* edge_image, int64_t n_edges,
+                                const int64_t* n_real_edges, double* workspace, float scale, float* image_grad,
+                                float* virial, int32_t accumulate, void* stream) {
+    const Geo g{r_max, n_basis, poly_p};
+    if (ysh == nullptr || grad_y == nullptr || grad_phi == nullptr || edge_image == nullptr || workspace == nullptr ||
+        n_edges < 0 || !geo_ok(g) || !aligned16(ysh) || (image_grad == nullptr && virial == nullptr))
+        return FMD_ERR_INVALID_ARGUMENT;
+    cudaStream_t st = as_stream(stream);
+    edge_virial_partial_kernel<<<kVirialBlocks, kVirialThreads, 0, st>>>(
+        reinterpret_cast<const float4*>(ysh), grad_y, grad_phi, g, edge_image, n_edges, n_real_edges, workspace);
+    edge_virial_final_kernel<<<1, 32, 0, st>>>(workspace, kVirialBlocks, scale, image_grad, virial, accumulate);
     return check_launch();
 }
 

@@ -33,15 +33,25 @@ class EnergyDerivative:
         return energy
 
     def __call__(self, batch, inputs, *, task: str = "ef", n_real: int | None = None) -> dict:
-        if "s" in task:
-            raise NotImplementedError("stress (the strain leaf) is not part of this build's energy taps")
+        stress = "s" in task
         with torch.enable_grad():
             leaf = batch.positions.detach().requires_grad_(True)
-            energies = self.adapter.node_energy(inputs, leaf, batch.cell)
+            positions, cell = leaf, batch.cell
+            leaves = (leaf,)
+            if stress:  # x' = x (1 + eps), cell' = cell (1 + eps), eps symmetric
+                strain = torch.zeros((3, 3), dtype=leaf.dtype, device=leaf.device, requires_grad=True)
+                symmetric = 0.5 * (strain + strain.transpose(0, 1))
+                positions = leaf + _times(leaf, symmetric)
+                cell = cell + _times(cell, symmetric)
+                leaves = (leaf, strain)
+            energies = self.adapter.node_energy(inputs, positions, cell)
             rows = energies.shape[0] if n_real is None else n_real
             energy = energies[:rows].to(torch.float64).sum()
-            (grad,) = torch.autograd.grad(energy, (leaf,))
-        return {"e": energy.detach().reshape(1), "f": [-grad]}
+            grads = torch.autograd.grad(energy, leaves)
+        out = {"e": energy.detach().reshape(1), "f": [-grads[0]]}
+        if stress:
+            out["s"] = [grads[1] / cell_volume(batch.cell)]
+        return out
 
 
 def engine_derivative(adapter) -> EnergyDerivative:

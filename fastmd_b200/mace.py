@@ -319,6 +319,20 @@ class MACEModel:
              ptr(out), float(sign), 0, s)
         return out
 
+    def cell_grad(self, batch, buf: _Buffers) -> Tensor:
+        """d(loss)/d(cell) [3, 3] = sum_e image_e^T g_e after ``backward`` (its edge gradients)."""
+        c = self.config
+        b = buf.t
+        if "virial_ws" not in b:
+            b["virial_ws"] = torch.empty(5328, dtype=torch.float64, device=self.device)  # FMD_EDGE_VIRIAL_WORKSPACE_DOUBLES
+        out = torch.empty(3, 3, dtype=torch.float32, device=self.device)
+        n_real = getattr(batch, "n_edges", None)
+        call("fmd_mace_edge_virial", ptr(b["ysh"]), ptr(b["gY"]), ptr(b["gphi"]), c.r_max, c.num_bessel, c.poly_p,
+             ptr(batch.edge_image), batch.edge_index.shape[0],
+             ptr(n_real) if isinstance(n_real, Tensor) and n_real.is_cuda else None, ptr(b["virial_ws"]), 1.0,
+             ptr(out), None, 0, stream(self.device))
+        return out
+
     # ------------------------------------------------------------ entry points
     def prepare(self, batch):
         """Attach the element rows of the batch's atomic numbers (host check, once per system;
@@ -347,7 +361,7 @@ class MACEModel:
         return total, forces
 
     def node_energy(self, inputs, positions: Tensor, cell: Tensor) -> Tensor:
-        """Energy tap: per-atom fp64 energies, differentiable with respect to ``positions``."""
+        """Energy tap: per-atom fp64 energies, differentiable with respect to ``positions`` and ``cell``."""
         return _NodeEnergy.apply(positions, cell, self, inputs)
 
 
@@ -361,7 +375,7 @@ class _NodeEnergy(torch.autograd.Function):
         model.forward(batch, positions=pos, cell=cell.detach().float().contiguous(), buf=buf)
         model.energies(batch, buf, 1)
         ctx.model, ctx.batch, ctx.buf = model, batch, buf
-        ctx.pos_dtype = positions.dtype
+        ctx.pos_dtype, ctx.cell_dtype = positions.dtype, cell.dtype
         return buf.t["node_energy"].clone()
 
     @staticmethod
@@ -371,7 +385,10 @@ class _NodeEnergy(torch.autograd.Function):
         torch.mul(grad_node.to(torch.float32), float(model.config.scale), out=d_term)
         dpos = torch.empty(buf.n_atoms, 3, dtype=torch.float32, device=d_term.device)
         model.backward(ctx.batch, buf, d_term, out=dpos)
-        return dpos.to(ctx.pos_dtype), None, None, None
+        dcell = None
+        if ctx.needs_input_grad[1]:  # the strain leaf of a stress: d(loss)/d(cell) over the edge images
+            dcell = model.cell_grad(ctx.batch, buf).to(ctx.cell_dtype)
+        return dpos.to(ctx.pos_dtype), dcell, None, None
 
 
 # --------------------------------------------------------------------------- fused step

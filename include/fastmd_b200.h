@@ -363,6 +363,21 @@ FMD_API fmd_status fmd_mace_edge_geometry_bwd(const float* ysh, const float* gra
                                               float* grad_positions, float scale, int32_t accumulate,
                                               void* stream);
 
+/* The strain / cell derivative of the edge geometry for the stress (E1, E2):
+ * with g_e = d(loss)/d(r_e) from the same gradients as
+ * fmd_mace_edge_geometry_bwd, image_grad [3, 3] = scale * sum_e image_e^T g_e
+ * (d(loss)/d(cell)) and virial [3, 3] = scale * sum_e r_e^T g_e (either may be
+ * null; device float32, accumulated into when accumulate = 1). Edges from
+ * *n_real_edges on (device int64, or all when null) are padding and skipped.
+ * workspace: FMD_EDGE_VIRIAL_WORKSPACE_DOUBLES doubles of device scratch.
+ * Deterministic (fixed grid, fixed reduction order). The cell leaf of the
+ * reference's strain derivative (fastmd/engine/energy_derivative.py:110-132). */
+#define FMD_EDGE_VIRIAL_WORKSPACE_DOUBLES 5328
+FMD_API fmd_status fmd_mace_edge_virial(const float* ysh, const float* grad_y, const float* grad_phi, float r_max,
+                                        int32_t n_basis, int32_t poly_p, const float* edge_image, int64_t n_edges,
+                                        const int64_t* n_real_edges, double* workspace, float scale,
+                                        float* image_grad, float* virial, int32_t accumulate, void* stream);
+
 /* Fused gather -> channel-wise tensor-product message -> receiver segment sum:
  * A0[i] = inv_avg * sum_e (R0 s_t[j] + R3 (v_t[j].Y)/sqrt3),
  * A1[i] = inv_avg * sum_e (R1 s_t[j] Y + R2 v_t[j]) over the receiver run of i

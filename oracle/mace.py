@@ -40,11 +40,14 @@ def silu(x):
 
 
 def energy_forces(weights: dict, config, positions, cell, atomic_numbers, edges, images, *, n_systems=1,
-                  dtype=torch.float64):
-    """(per-system energies [R], forces [N, 3], node energies [N]) in float64.
+                  dtype=torch.float64, stress=False):
+    """(per-system energies [R], forces [N, 3], node energies [N]) in float64, and the stress [3, 3]
+    (eV/A^3) after them with ``stress``.
 
     ``edges`` [E, 2] (centre i, neighbour j), ``images`` [E, 3] integer images: the edge vector
-    is x_j + image @ cell - x_i, messages flow j -> i."""
+    is x_j + image @ cell - x_i, messages flow j -> i. The stress is the reference's strain leaf
+    (fastmd/engine/energy_derivative.py:110-132): x' = x + x eps, cell' = cell + cell eps with a
+    symmetric eps, s = dE/d(eps) / |det cell|."""
     W = {k: torch.as_tensor(np.asarray(v), dtype=dtype if v.dtype != np.float64 else torch.float64)
          for k, v in weights.items()}
     C = config.channels
@@ -55,7 +58,10 @@ def energy_forces(weights: dict, config, positions, cell, atomic_numbers, edges,
     images = torch.as_tensor(np.asarray(images, np.float64), dtype=dtype)
     N = pos.shape[0]
     i, j = edges[:, 0], edges[:, 1]
-    r = pos[j] + images @ cell - pos[i]
+    strain = torch.zeros(3, 3, dtype=dtype, requires_grad=True)
+    sym = 0.5 * (strain + strain.T)
+    pos_s, cell_s = (pos + pos @ sym, cell + cell @ sym) if stress else (pos, cell)
+    r = pos_s[j] + images @ cell_s - pos_s[i]
     d = torch.linalg.vector_norm(r, dim=1)
     Y = math.sqrt(3.0) * r / d[:, None]
     phi = bessel_envelope(d, config.r_max, config.num_bessel, config.poly_p)
@@ -104,5 +110,10 @@ def energy_forces(weights: dict, config, positions, cell, atomic_numbers, edges,
     e0 = torch.as_tensor(np.asarray(weights["e0"], np.float64))
     node = e0[z] + config.scale * sum(t.to(torch.float64) for t in terms) + config.shift
     totals = node.reshape(n_systems, -1).sum(dim=1)
-    (grad,) = torch.autograd.grad(totals.sum(), pos)
-    return totals.detach().numpy(), (-grad).detach().numpy(), node.detach().numpy()
+    if not stress:
+        (grad,) = torch.autograd.grad(totals.sum(), pos)
+        return totals.detach().numpy(), (-grad).detach().numpy(), node.detach().numpy()
+    grad, gstrain = torch.autograd.grad(totals.sum(), (pos, strain))
+    volume = abs(float(torch.linalg.det(cell)))
+    return (totals.detach().numpy(), (-grad).detach().numpy(), node.detach().numpy(),
+            (gstrain / volume).detach().numpy())

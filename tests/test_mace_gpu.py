@@ -100,6 +100,28 @@ def test_energy_derivative_autograd_route_equals_explicit_backward(cuda):
     assert torch.equal(out["f"][0], forces)
 
 
+def test_stress_strain_leaf_matches_fp64_oracle(cuda):
+    """EnergyDerivative(task="efs"): the reference's strain leaf through the model's cell gradient
+    (fmd_mace_edge_virial) against the FP64 oracle's own strain leaf."""
+    from fastmd_b200.energy_derivative import EnergyDerivative
+    from fastmd_b200.mace import MACEModel
+
+    pos, cell, numbers, _ = _system(2)
+    model = MACEModel(device=cuda)
+    _, batch = _graph(pos, cell, numbers, cuda)
+    out = EnergyDerivative(model)(batch, batch, task="efs", n_real=batch.positions.shape[0])
+    n = int(batch.n_edges.item())
+    E, F, _, S = omace.energy_forces(model.weights_host, model.config, batch.positions.cpu().numpy().astype(np.float64),
+                                     batch.cell.cpu().numpy(), numbers, batch.edge_index[:n].cpu().numpy(),
+                                     batch.edge_image[:n].cpu().numpy().round(), stress=True)
+    _close(out["e"].cpu().numpy(), E, 1e-7)
+    _close(out["f"][0].cpu().numpy(), F)
+    s = out["s"][0].cpu().numpy()
+    assert s.shape == (3, 3) and np.allclose(s, s.T, atol=1e-6 * np.abs(S).max())
+    _close(s, S, 1e-4)
+    assert float(np.abs(S).max()) > 1e-4  # not trivially zero
+
+
 def test_small_channel_model_matches_oracle_and_is_deterministic(cuda):
     from fastmd_b200.mace import MACEConfig, MACEModel
 
