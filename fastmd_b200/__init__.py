@@ -5,6 +5,8 @@ Surfaces mirroring the reference: ``ops`` (fastmd.ops), ``graph`` (fastmd.graph 
 fastmd.interfaces), ``mace`` (the MACE-architecture energy tap).
 """
 from fastmd_b200 import (  # noqa: F401
-    _lib, energy_derivative, gpu_nhc, graph, mace, ops, segment_attention, units, whole_step, wide_gemm)
+    _lib, decomposed_indexed_cat_silu_linear, energy_derivative, gpu_nhc, graph, mace, ops, segment_attention, units,
+    whole_step, wide_gemm)
 
-__all__ = ["energy_derivative", "gpu_nhc", "graph", "mace", "ops", "units", "whole_step"]
+__all__ = ["decomposed_indexed_cat_silu_linear", "energy_derivative", "gpu_nhc", "graph", "mace", "ops",
+           "segment_attention", "units", "whole_step", "wide_gemm"]

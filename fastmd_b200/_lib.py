@@ -51,6 +51,8 @@ _SIGNATURES: dict[str, list] = {
     "fmd_neighbor_list_workspace_bytes": [_P, c_float, _I64, _I32, POINTER(c_size_t)],
     "fmd_neighbor_list": [_P, _P, _I64, c_float, _I32, _I64, _P, _P, _P, _P, _P, _P, _P, c_size_t, _P, _P],
     "fmd_gemm_f32": [_P, _I64, _P, _I64, _P, _I64, _I32, _P, _P, _I64, _P, _I64, _I64, _I32, _I32, _I32, _I32, _P],
+    "fmd_gather_add_silu": [_P, _I64, POINTER(FmdCatPart), _I32, _P, _I64, _I32, _P, _P, _P, _P, _P],
+    "fmd_silu_pair_bwd": [_P, _P, _P, _I64, _I32, _P, _I64, _P],
     "fmd_segment_attention": [_P, _I64, _P, _I64, _P, _P, _I64, _I64, _I32, _I64, _P, _P, _P, _P, _P, _P],
     "fmd_segment_attention_bwd": [_P, _I64, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I32, _I64, _P, _I64, _P,
                                   _I64, _P, _P],

@@ -30,6 +30,7 @@ EXTRA = {
     "nhc.cu": ["--fmad=false"],
     "neighbors.cu": ["--fmad=false"],
     "segment_attention.cu": ["--fmad=false"],
+    "gather_add_silu.cu": ["--fmad=false"],
 }
 
 

@@ -264,6 +264,30 @@ FMD_API fmd_status fmd_gemm_f32(const float* a, int64_t lda, const float* a_pre,
                                 int64_t ldy, float* y_pre, int64_t ldy_pre, int64_t m, int32_t n, int32_t k,
                                 int32_t act, int32_t accumulate, void* stream);
 
+/* -------------------------- decomposed indexed-concat SiLU epilogue (B2) */
+
+/* preact[r] = p0[r] + gathered[0].src[index_0[r]] + ... + bias (the FP32
+ * additions in that order), core_act = silu(preact[:, :h]), gate_act =
+ * silu(preact[:, h:]) with silu(x) = x / (1 + e^-x) evaluated as
+ * x * (1 / (1 + e^-x)). p0 [rows, 2h] (row stride ldp0); up to 3 gathered
+ * projections [n_src, 2h] (fmd_cat_part: src, index [rows] int64, ld, n_src;
+ * width unused); bias [2h] or null; preact [rows, 2h], core_act and
+ * gate_act [rows, h] contiguous. Index values outside [0, n_src) add
+ * nothing and raise FMD_FLAG_INDEX_RANGE. Replaces
+ * _cat3_gather_add_silu_fwd / _cat4_gather_add_silu_fwd
+ * (fastmd/engine/kernels/decomposed_indexed_cat_silu_linear.py:97, :156). */
+FMD_API fmd_status fmd_gather_add_silu(const float* p0, int64_t ldp0, const fmd_cat_part* gathered,
+                                       int32_t n_gathered, const float* bias, int64_t rows, int32_t h,
+                                       float* preact, float* core_act, float* gate_act, int32_t* flags,
+                                       void* stream);
+
+/* grad_pre[r] = [g_core s (1 + x (1 - s)) | g_gate s (1 + x (1 - s))] with x
+ * the halves of preact and s = sigmoid(x): the per-row part of
+ * _cat3_gather_add_silu_bwd / _cat4_gather_add_silu_bwd (:234, :383); the
+ * gathered parts' gradients are its CSR row sums (fmd_gather_rows_bwd). */
+FMD_API fmd_status fmd_silu_pair_bwd(const float* grad_core, const float* grad_gate, const float* preact,
+                                     int64_t rows, int32_t h, float* grad_pre, int64_t ldgp, void* stream);
+
 /* ------------------------------------------- segment attention (C2) */
 
 /* out[s, :] = sum over the rows i of segment s of softmax(logits[i, :] over

@@ -15,7 +15,9 @@ used) and runs, on CPU:
   (fastmd/models/matris/op/triton_csr_segment_sum.py:71/:184), the segment
   attention kernels ``_csr_segment_attention_fwd/_bwd``, ``_paired_csr_segment_attention_fwd``
   and ``_paired_segment_attention_bwd_rows``
-  (fastmd/models/matris/op/triton_segment_attention.py:62/:128/:210/:319), and the
+  (fastmd/models/matris/op/triton_segment_attention.py:62/:128/:210/:319), the
+  decomposed indexed-concat SiLU epilogues ``_cat3/_cat4_gather_add_silu_fwd/_bwd``
+  (fastmd/engine/kernels/decomposed_indexed_cat_silu_linear.py:97/:156/:234/:383), and the
   fixed-capacity re-filter ``_count_neighbors_kernel`` /
   ``_materialize_neighbors_kernel`` (fastmd/graph/fixed_capacity_builder.py:98/:189)
   on candidate lists of a dense search, followed by the reference's
@@ -211,6 +213,54 @@ def segment_attention_cases(torch, sa):
     return out
 
 
+def gather_add_silu_cases(torch, di):
+    """The decomposed indexed-concat epilogues ``_cat3_gather_add_silu_fwd/_bwd`` and
+    ``_cat4_gather_add_silu_fwd/_bwd`` (fastmd/engine/kernels/decomposed_indexed_cat_silu_linear.py:97,
+    :156, :234, :383): preact = p0 + p1[ia] + p2[ib] (+ p3[ic]) + bias, SiLU of its core / gate halves,
+    and the backward's SiLU derivative with its scatter into the gathered projections."""
+    out = {}
+    rng = np.random.default_rng(14)
+    for tag, (M, NS, H, cat4, sorted_a, bias) in {"cat3": (57, 13, 16, False, False, True),
+                                                  "cat3_sorted_odd": (45, 9, 12, False, True, False),
+                                                  "cat4": (38, 11, 8, True, False, True)}.items():
+        N = 2 * H
+        blk = 1 << (H - 1).bit_length()
+        ia = rng.integers(0, NS, M).astype(np.int64)
+        if sorted_a:
+            ia = np.sort(ia)
+        ib = rng.integers(0, NS, M).astype(np.int64)
+        ic = rng.integers(0, NS, M).astype(np.int64)
+        arr = dict(p0=rng.standard_normal((M, N)), p1=rng.standard_normal((NS, N)), p2=rng.standard_normal((NS, N)),
+                   p3=rng.standard_normal((NS, N)), b=rng.standard_normal(N), gc=rng.standard_normal((M, H)),
+                   gg=rng.standard_normal((M, H)))
+        arr = {k: (2.0 * v).astype(np.float32) for k, v in arr.items()}
+        arr.update(ia=ia, ib=ib, ic=ic)
+        t = {k: torch.from_numpy(v) for k, v in arr.items()}
+        pre, ca, ga = torch.empty(M, N), torch.empty(M, H), torch.empty(M, H)
+        gp = [torch.zeros(M, N)] + [torch.zeros(NS, N) for _ in range(3)]
+        bias_t = t["b"] if bias else None
+        if cat4:
+            di._cat4_gather_add_silu_fwd[((M + 7) // 8,)](
+                t["p0"], t["p1"], t["p2"], t["p3"], t["ia"], t["ib"], t["ic"], bias_t, pre, ca, ga, SIA=1, SIB=1,
+                SIC=1, SP0=N, M=M, H=H, N=N, BM=8, BLK=blk, HAS_BIAS=bias)
+            di._cat4_gather_add_silu_bwd[((M + 7) // 8,)](
+                t["gc"], t["gg"], pre, t["ia"], t["ib"], t["ic"], gp[0], gp[1], gp[2], gp[3], SIA=1, SIB=1, SIC=1,
+                M=M, H=H, N=N, BM=8, BLK=blk, SORTED_A=sorted_a)
+        else:
+            di._cat3_gather_add_silu_fwd[((M + 7) // 8,)](
+                t["p0"], t["p1"], t["p2"], t["ia"], t["ib"], bias_t, pre, ca, ga, SIA=1, SIB=1, SP0=N, M=M, H=H,
+                N=N, BM=8, BLK=blk, HAS_BIAS=bias)
+            di._cat3_gather_add_silu_bwd[((M + 7) // 8,)](
+                t["gc"], t["gg"], pre, t["ia"], t["ib"], gp[0], gp[1], gp[2], SIA=1, SIB=1, M=M, H=H, N=N, BM=8,
+                BLK=blk, SORTED_A=sorted_a)
+        out.update({f"gas_{tag}_{k}": v for k, v in arr.items()})
+        out[f"gas_{tag}_meta"] = np.array([M, NS, H, int(cat4), int(sorted_a), int(bias)], dtype=np.int64)
+        out[f"gas_{tag}_preact"], out[f"gas_{tag}_core"], out[f"gas_{tag}_gate"] = pre.numpy(), ca.numpy(), ga.numpy()
+        for k in range(4 if cat4 else 3):
+            out[f"gas_{tag}_gp{k}"] = gp[k].numpy()
+    return out
+
+
 def nhc_cases(torch, gpu_nhc):
     from ase import units
 
@@ -383,6 +433,7 @@ def main(reference: str) -> None:
     import fastmd.models.matris.op.triton_csr_segment_sum as cs
     import fastmd.models.matris.op.triton_gather_cat as gc
     import fastmd.models.matris.op.triton_segment_attention as sa
+    import fastmd.engine.kernels.decomposed_indexed_cat_silu_linear as di
 
     np.savez_compressed(HERE / "gather_cat.npz", **gather_cat_cases(torch, gc))
     np.savez_compressed(HERE / "segment_sum.npz", **segment_sum_cases(torch, cs))
@@ -390,6 +441,7 @@ def main(reference: str) -> None:
     np.savez_compressed(HERE / "neighbors.npz", **neighbor_cases(torch, fcb))
     np.savez_compressed(HERE / "radial.npz", **radial_cases(torch))
     np.savez_compressed(HERE / "segment_attention.npz", **segment_attention_cases(torch, sa))
+    np.savez_compressed(HERE / "gather_add_silu.npz", **gather_add_silu_cases(torch, di))
     for path in sorted(HERE.glob("*.npz")):
         print(path.name, path.stat().st_size)
 
