@@ -1,12 +1,14 @@
 """fastmd_b200: FastMD's per-step MD hot path on hand-written sm_100a kernels (libfastmd_b200.so).
 
-Surfaces mirroring the reference: ``ops`` (fastmd.ops), ``graph`` (fastmd.graph builders),
-``energy_derivative`` (fastmd.engine), ``gpu_nhc`` and ``whole_step`` (fastmd.execution /
-fastmd.interfaces), ``mace`` (the MACE-architecture energy tap).
+Surfaces mirroring the reference: ``ops`` (fastmd.ops), ``graph`` and ``line_graph`` (fastmd.graph
+builders, the MatRIS bond pairs and triplets), ``wide_gemm`` and ``decomposed_indexed_cat_silu_linear``
+(fastmd.engine.kernels), ``segment_attention`` (the MatRIS receiver attention), ``energy_derivative``
+(fastmd.engine), ``gpu_nhc`` and ``whole_step`` (fastmd.execution / fastmd.interfaces), ``mace`` (the
+MACE-architecture energy tap).
 """
 from fastmd_b200 import (  # noqa: F401
-    _lib, decomposed_indexed_cat_silu_linear, energy_derivative, gpu_nhc, graph, mace, ops, segment_attention, units,
-    whole_step, wide_gemm)
+    _lib, decomposed_indexed_cat_silu_linear, energy_derivative, gpu_nhc, graph, line_graph, mace, ops,
+    segment_attention, units, whole_step, wide_gemm)
 
-__all__ = ["decomposed_indexed_cat_silu_linear", "energy_derivative", "gpu_nhc", "graph", "mace", "ops",
+__all__ = ["decomposed_indexed_cat_silu_linear", "energy_derivative", "gpu_nhc", "graph", "line_graph", "mace", "ops",
            "segment_attention", "units", "whole_step", "wide_gemm"]

@@ -53,6 +53,7 @@ typedef int32_t fmd_status;
 #define FMD_FLAG_NONFINITE 16       /* a non-finite position or momentum */
 #define FMD_FLAG_CELL_RANGE 32      /* a fractional coordinate outside the cell grid */
 #define FMD_FLAG_WAIT_TIMEOUT 64    /* a bounded in-kernel wait gave up (about 1 s); outputs invalid */
+#define FMD_FLAG_TRIPLET_OVERFLOW 128 /* more line-graph triplets than the triplet capacity */
 
 /* ---------------------------------------------------------------- library */
 
@@ -263,6 +264,37 @@ FMD_API fmd_status fmd_gemm_f32(const float* a, int64_t lda, const float* a_pre,
                                 const float* w, int64_t ldw, int32_t trans_w, const float* bias, float* y,
                                 int64_t ldy, float* y_pre, int64_t ldy_pre, int64_t m, int32_t n, int32_t k,
                                 int32_t act, int32_t accumulate, void* stream);
+
+/* ------------------------------- MatRIS bond pairs and line graph (A5) */
+
+/* Reverse-edge pairing of directed edges (center, neighbor [E] int64, images
+ * [E, 3] int32 within +-10): pair(e) = the edge whose forward key
+ * (c N + n) 21^3 + code(image) equals e's reverse key (n N + c) 21^3 +
+ * code(-image), located by lower bound among the sorted forward keys
+ * (clamped to the last edge; presorted = 1 when the edges are in key order);
+ * directed2undirected[e] = rank of min(e, pair(e)) among the distinct minima,
+ * undirected2directed[u] = smallest edge of u (entries past *n_undirected set
+ * to E), *n_undirected (device int64). Replaces _build_d2u
+ * (fastmd/graph/gpu_graph_builder.py:217). */
+FMD_API fmd_status fmd_reverse_pairs_workspace_bytes(int64_t n_edges, size_t* bytes);
+FMD_API fmd_status fmd_reverse_pairs(const int64_t* center, const int64_t* neighbor, const int32_t* images,
+                                     int64_t n_edges, int64_t n_atoms, int32_t presorted, void* workspace,
+                                     size_t workspace_bytes, int32_t* directed2undirected,
+                                     int32_t* undirected2directed, int64_t* n_undirected, int32_t* flags,
+                                     void* stream);
+
+/* Ordered bond pairs around each atom: the short edges (dist < cutoff),
+ * stably grouped by centre (already grouped when presorted = 1), give an atom
+ * with k of them the k (k - 1) rows [atom, u(first), first, u(second), second]
+ * (int32 [t_capacity, 5]) in the order first = l / (k - 1), second =
+ * l % (k - 1) skipping first. *n_triplets (device int64) receives the count;
+ * rows past t_capacity are not written and raise FMD_FLAG_TRIPLET_OVERFLOW.
+ * Replaces _build_line_graph (fastmd/graph/gpu_graph_builder.py:511). */
+FMD_API fmd_status fmd_line_graph_workspace_bytes(int64_t n_edges, int64_t n_atoms, size_t* bytes);
+FMD_API fmd_status fmd_line_graph(const int64_t* center, const float* dist, const int32_t* directed2undirected,
+                                  int64_t n_edges, int64_t n_atoms, float cutoff, int32_t presorted,
+                                  int64_t t_capacity, void* workspace, size_t workspace_bytes, int32_t* triplets,
+                                  int64_t* n_triplets, int32_t* flags, void* stream);
 
 /* -------------------------- decomposed indexed-concat SiLU epilogue (B2) */
 

@@ -17,7 +17,9 @@ used) and runs, on CPU:
   and ``_paired_segment_attention_bwd_rows``
   (fastmd/models/matris/op/triton_segment_attention.py:62/:128/:210/:319), the
   decomposed indexed-concat SiLU epilogues ``_cat3/_cat4_gather_add_silu_fwd/_bwd``
-  (fastmd/engine/kernels/decomposed_indexed_cat_silu_linear.py:97/:156/:234/:383), and the
+  (fastmd/engine/kernels/decomposed_indexed_cat_silu_linear.py:97/:156/:234/:383), the
+  MatRIS reverse-edge pairing and ordered triplets ``_build_d2u`` / ``_build_line_graph``
+  (fastmd/graph/gpu_graph_builder.py:217/:511, their torch path on CPU), and the
   fixed-capacity re-filter ``_count_neighbors_kernel`` /
   ``_materialize_neighbors_kernel`` (fastmd/graph/fixed_capacity_builder.py:98/:189)
   on candidate lists of a dense search, followed by the reference's
@@ -261,6 +263,49 @@ def gather_add_silu_cases(torch, di):
     return out
 
 
+def pairs_line_graph_cases(torch, ggb):
+    """MatRIS reverse-edge pairing ``_build_d2u`` and the ordered triplets ``_build_line_graph``
+    (fastmd/graph/gpu_graph_builder.py:217, :511) on dense FP64 neighbour lists of a perovskite
+    (canonically sorted edges), a small triclinic cell with many images (edges shuffled) and a
+    sparse box with isolated atoms."""
+    sys.path.insert(0, str(HERE.parents[1]))
+    from oracle.neighbors import dense_pairs
+
+    out = {}
+    rng = np.random.default_rng(15)
+    a = 6.2
+    basis = np.array([[0, 0, 0], [.5, .5, .5], [.5, .5, 0], [.5, 0, .5], [0, .5, .5]])
+    grid = np.array([[i, j, k] for i in range(3) for j in range(3) for k in range(3)], float)
+    perov = ((grid[:, None] + basis[None]).reshape(-1, 3) * a + rng.normal(0, 0.05, (135, 3)), np.eye(3) * 3 * a)
+    tric_cell = np.array([[4.0, 0.0, 0.0], [1.1, 3.8, 0.0], [0.7, 0.9, 4.2]])
+    tric = (rng.uniform(0, 1, (6, 3)) @ tric_cell, tric_cell)
+    sparse = (np.concatenate([rng.uniform(0, 3, (4, 3)), rng.uniform(10, 20, (5, 3))]), np.eye(3) * 30.0)
+    for tag, ((pos, cell), rc, line_cut, presorted) in {"perov": (perov, 6.0, 4.5, True),
+                                                        "triclinic": (tric, 5.0, 3.2, False),
+                                                        "sparse": (sparse, 4.0, 2.5, False)}.items():
+        pairs = dense_pairs(pos, cell, rc)
+        keys = sorted(pairs)
+        center = np.array([k[0] for k in keys], np.int64)
+        neighbor = np.array([k[1] for k in keys], np.int64)
+        images = np.array([k[2:] for k in keys], np.int32).reshape(-1, 3)
+        dist = np.array([pairs[k] for k in keys], np.float32)
+        if not presorted:
+            order = rng.permutation(len(keys))
+            center, neighbor, images, dist = center[order], neighbor[order], images[order], dist[order]
+        n = pos.shape[0]
+        d2u, u2d = ggb._build_d2u(torch.from_numpy(center), torch.from_numpy(neighbor),
+                                  torch.from_numpy(images.astype(np.int64)), n, presorted=presorted)
+        lg = ggb._build_line_graph(torch.from_numpy(center), d2u, torch.from_numpy(dist), n, line_cut,
+                                   presorted=presorted)
+        out.update({f"plg_{tag}_{k}": v for k, v in dict(center=center, neighbor=neighbor, images=images,
+                                                             dist=dist).items()})
+        out[f"plg_{tag}_meta"] = np.array([n, int(presorted)], dtype=np.int64)
+        out[f"plg_{tag}_cutoff"] = np.array([line_cut], dtype=np.float32)
+        out[f"plg_{tag}_d2u"], out[f"plg_{tag}_u2d"] = d2u.numpy(), u2d.numpy()
+        out[f"plg_{tag}_triplets"] = lg.numpy()
+    return out
+
+
 def nhc_cases(torch, gpu_nhc):
     from ase import units
 
@@ -434,6 +479,7 @@ def main(reference: str) -> None:
     import fastmd.models.matris.op.triton_gather_cat as gc
     import fastmd.models.matris.op.triton_segment_attention as sa
     import fastmd.engine.kernels.decomposed_indexed_cat_silu_linear as di
+    import fastmd.graph.gpu_graph_builder as ggb
 
     np.savez_compressed(HERE / "gather_cat.npz", **gather_cat_cases(torch, gc))
     np.savez_compressed(HERE / "segment_sum.npz", **segment_sum_cases(torch, cs))
@@ -442,6 +488,7 @@ def main(reference: str) -> None:
     np.savez_compressed(HERE / "radial.npz", **radial_cases(torch))
     np.savez_compressed(HERE / "segment_attention.npz", **segment_attention_cases(torch, sa))
     np.savez_compressed(HERE / "gather_add_silu.npz", **gather_add_silu_cases(torch, di))
+    np.savez_compressed(HERE / "line_graph.npz", **pairs_line_graph_cases(torch, ggb))
     for path in sorted(HERE.glob("*.npz")):
         print(path.name, path.stat().st_size)
 
