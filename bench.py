@@ -52,6 +52,9 @@ def _args():
     p.add_argument("--steps-per-launch", type=int, default=10)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-ops", action="store_true", help="skip the config-2 op microbenchmark")
+    p.add_argument("--op", choices=["wide_gemm"], default=None,
+                   help="time one op alone (the profiling entry of profiles/): prints its own JSON line")
+    p.add_argument("--rows", type=int, default=300_000, help="rows of --op")
     return p.parse_args()
 
 
@@ -304,26 +307,38 @@ STAGES = {0: ("edge_fwd_kernel", 1), 1: ("message_fused_kernel (per layer)", 2),
           6: ("edge_bwd_kernel", 1), 7: ("forces_kernel", 1)}
 
 
-def _time_stage(md, device, bit, reps=200):
+def _time_stage(md, device, bit, per_graph=20, replays=10):
+    """GPU time of one launch group of fused stage ``bit``: ``per_graph`` launches captured in a CUDA
+    graph (no host launch cost between them), replayed ``replays`` times between CUDA events."""
     import torch
 
     model, batch = md.model, md.builder.batch
-    s = torch.cuda.current_stream(device)
-    for _ in range(10):
-        model.energy_forces_fused(batch, n_systems=md.replicas, stages=1 << bit)
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record(s)
-    for _ in range(reps):
-        model.energy_forces_fused(batch, n_systems=md.replicas, stages=1 << bit)
-    end.record(s)
-    torch.cuda.synchronize()
-    return start.elapsed_time(end) / reps * 1e3  # us per launch group
+    s = torch.cuda.Stream(device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            model.energy_forces_fused(batch, n_systems=md.replicas, stages=1 << bit)
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        for _ in range(per_graph):
+            model.energy_forces_fused(batch, n_systems=md.replicas, stages=1 << bit)
+    with torch.cuda.stream(s):
+        graph.replay()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(s)
+        for _ in range(replays):
+            graph.replay()
+        end.record(s)
+    torch.cuda.synchronize(device)
+    del graph
+    return start.elapsed_time(end) / (replays * per_graph) * 1e3  # us per launch group
 
 
 def _roofline(md, device):
-    """Every fused stage timed alone (CUDA events, 200 back-to-back launches on the step's stream,
-    after the timed run); the roofline of the dominant single-kernel stage against the measured HBM
-    copy bandwidth (algorithmic bytes: the stage's compulsory reads and writes)."""
+    """Every fused stage timed alone (CUDA events around replays of a CUDA graph of 20 launches of the
+    stage, after the timed run); the roofline of the dominant single-kernel stage against the measured
+    HBM copy bandwidth (algorithmic bytes: the stage's compulsory reads and writes)."""
     hbm, _, kind = _peaks()
     stages = {STAGES[bit][0]: round(_time_stage(md, device, bit), 3) for bit in STAGES}
     single = {bit: stages[STAGES[bit][0]] for bit in STAGES if STAGES[bit][1] == 1}
@@ -374,8 +389,9 @@ def _ops_c2(device):
     from fastmd_b200.structures import random_box
 
     hbm, bf16, kind = _peaks()
-    # kind::tf32 issues at half the bf16 rate; 3xTF32 makes three TF32 products per FP32 product
-    tf32_peak, tf32_kind = bf16 / 2.0, f"half of the {kind} bf16 dense figure"
+    # the tensor pipe's own kind::tf32 rate, measured here (fmd_tf32_mma_rate: back-to-back MMAs, no data
+    # movement); 3xTF32 makes three TF32 products per FP32 product
+    tf32_peak, tf32_kind = _tf32_rate(device), "measured this run (fmd_tf32_mma_rate, tcgen05 issue rate)"
     s = torch.cuda.current_stream(device)
     sp = s.cuda_stream
 
@@ -484,6 +500,24 @@ def _ops_c2(device):
             "segment_sum_256": hb(b_ss, t_ss), "segment_attention_128": hb(b_sa, t_sa)}
 
 
+def _tf32_rate(device, iters=20000):
+    """TF/s of back-to-back tcgen05 kind::tf32 MMAs (M = N = 128, K = 8) on every SM."""
+    import torch
+
+    from fastmd_b200._lib import call, ptr
+
+    flags = torch.zeros(1, dtype=torch.int32, device=device)
+    s = torch.cuda.current_stream(device)
+    call("fmd_tf32_mma_rate", 1000, ptr(flags), s.cuda_stream)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(s)
+    call("fmd_tf32_mma_rate", iters, ptr(flags), s.cuda_stream)
+    end.record(s)
+    torch.cuda.synchronize(device)
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    return sms * iters * 2.0 * 128 * 128 * 8 / (start.elapsed_time(end) * 1e-3) / 1e12
+
+
 def _tc_line(flops, ms, rows, tf32_peak, kind):
     """A 3xTF32 GEMM line: FP32-equivalent TFLOP/s, the TF32 tensor rate it implies (3 products per FP32
     product) and its fraction of the TF32 dense peak."""
@@ -521,8 +555,42 @@ def _cpu_baseline():
                       f"MACE-arch forces with autograd, NHC) on {threads} threads"}
 
 
+def _op(args):
+    """One op alone on cuda:0, the profiling entry: ``--op wide_gemm`` runs the config-2 first edge
+    layer (264 -> 256, bias, SiLU, 3xTF32 on tcgen05) over ``--rows`` rows, 3 warm-up launches then
+    10 timed ones (CUDA events; the input is larger than L2 from 120,000 rows on)."""
+    import torch
+
+    from fastmd_b200 import wide_gemm
+
+    dev = torch.device("cuda", 0)
+    m, n, k = args.rows, 256, 264
+    g = torch.Generator(device=dev).manual_seed(5)
+    x = torch.randn(m, k, device=dev, generator=g)
+    w = torch.randn(n, k, device=dev, generator=g) / 16
+    b = torch.randn(n, device=dev, generator=g)
+    y = torch.empty(m, n, device=dev)
+    wide_gemm._split(w, False)
+    for _ in range(3):
+        wide_gemm.linear_into(y, x, w, b, act=1)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(10):
+        wide_gemm.linear_into(y, x, w, b, act=1)
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / 10
+    flops = 2.0 * m * n * k
+    return {"op": "wide_gemm_tf32x3", "rows": m, "k": k, "n": n, "ms": round(ms, 4),
+            "tflops_fp32_equivalent": round(flops / ms / 1e9, 1), "tf32_tensor_tflops": round(3 * flops / ms / 1e9, 1)}
+
+
 def main():
     args = _args()
+    if args.op is not None:
+        print(json.dumps(_op(args)), flush=True)
+        return
     result = _reference(args) if args.impl == "reference" else _ours(args)
     if result is not None:
         print(json.dumps(result), flush=True)

@@ -24,7 +24,8 @@
 //               of 8, three products each, M = 128, N = 128 (or the tile's
 //               width); A (x_hi / x_lo) from TMEM, B (w) from shared memory
 //   warps 4-7   splitter: row r of the x tile (one thread per row, reading
-//               the swizzled tile) -> x_hi, x_lo in registers -> TMEM lane r
+//               the swizzled tile) -> x_hi, x_lo in registers (computed while
+//               the A buffer's previous MMAs still run) -> TMEM lane r
 //               (tcgen05.st), double-buffered A operand
 //   warps 8-15  epilogue: TMEM -> registers, chunk sums, bias, residual,
 //               SiLU, stores; warp w reads TMEM lanes 32 (w % 4) .. +31 (its
@@ -199,13 +200,12 @@ __device__ __forceinline__ void tc_mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem,
         : "memory");
 }
 
-// 32 consecutive TMEM columns of this thread's lane (shape 32x32b, x32),
-// then the wait for the stores to land.
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+// 32 consecutive TMEM columns of this thread's lane (shape 32x32b, x32); with
+// `wait`, then the wait for this thread's TMEM stores to land.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32], bool wait) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};\n\t"
-        "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
         "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
         "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
         "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
@@ -218,6 +218,23 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
         "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
         "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
         : "memory");
+    if (wait) asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// 16 consecutive TMEM columns of this thread's lane (shape 32x32b, x16) from
+// v[0..15]; with `wait`, then the wait for this thread's TMEM stores.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v, bool wait) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16};" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+        "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+        "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+        "r"(__float_as_uint(v[15]))
+        : "memory");
+    if (wait) asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // 16 consecutive TMEM columns of this thread's lane (shape 32x32b, x16),
@@ -467,30 +484,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
             for (int ks = 0; ks < k_stages; ++ks) {
-                const bool got = mbar_wait(&ctl.full[s], ph, abort) && mbar_wait(&ctl.a_empty[sa], aph ^ 1u, abort);
+                // the split is computed while the A buffer's previous MMAs may still run; only the
+                // TMEM stores wait for them
+                bool got = mbar_wait(&ctl.full[s], ph, abort);
+                float h[32], v[32];
+                if (got) {
+                    const float4* row = reinterpret_cast<const float4*>(ring + s * kStageBytes + r * 128);
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const float4 f = row[c ^ (r & 7)];
+                        v[4 * c] = f.x;
+                        v[4 * c + 1] = f.y;
+                        v[4 * c + 2] = f.z;
+                        v[4 * c + 3] = f.w;
+                    }
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        h[j] = rna_tf32(v[j]);
+                        v[j] -= h[j];
+                    }
+                    got = mbar_wait(&ctl.a_empty[sa], aph ^ 1u, abort);
+                }
                 if (!__all_sync(0xffffffffu, got)) {  // warp-uniform: tcgen05.st is .sync.aligned
                     *abort = 1;
                     ok = false;
                     break;
                 }
-                const float4* row = reinterpret_cast<const float4*>(ring + s * kStageBytes + r * 128);
-                float v[32], h[32];
-#pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const float4 f = row[c ^ (r & 7)];
-                    v[4 * c] = f.x;
-                    v[4 * c + 1] = f.y;
-                    v[4 * c + 2] = f.z;
-                    v[4 * c + 3] = f.w;
-                }
-#pragma unroll
-                for (int j = 0; j < 32; ++j) h[j] = rna_tf32(v[j]);
                 tc_fence_after();
                 const uint32_t ta = tmem + lane_addr + kABase + uint32_t(sa) * kACols;
-                tmem_st32(ta, h);
-#pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] -= h[j];
-                tmem_st32(ta + kBK, v);
+                tmem_st32(ta, h, false);
+                tmem_st32(ta + kBK, v, true);
                 tc_fence_before();
                 mbar_arrive(&ctl.a_full[sa]);
                 advance(s, ph, kStages);
@@ -608,6 +631,56 @@ __global__ void tf32_split_kernel(const float* __restrict__ w, int64_t rows, int
     }
 }
 
+// The tensor pipe's own kind::tf32 rate: one CTA per SM, one thread issuing
+// `iters` back-to-back M = 128, N = 128, K = 8 MMAs (A from TMEM, B from
+// shared memory, zero operands) with no data movement; the roofline
+// denominator of the wide GEMM (2 * 128 * 128 * 8 flops per MMA).
+__global__ void __launch_bounds__(128, 1) tf32_mma_rate_kernel(int iters, int32_t* flags) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* b = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                        ~uintptr_t(1023));
+    __shared__ uint64_t bar;
+    __shared__ uint32_t slot;
+    __shared__ int32_t abort_word;
+    for (int i = threadIdx.x; i < int(kTileBytes / 4); i += blockDim.x) reinterpret_cast<float*>(b)[i] = 0.f;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_word = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (threadIdx.x < 32) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(su32(&slot))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = slot;
+    {  // A operand columns [128, 136) of every lane: zeros
+        float z[16] = {};
+        tmem_st16(tmem + (uint32_t((threadIdx.x >> 5) * 32) << 16) + 128u, z, true);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (threadIdx.x == 0) {
+        const uint64_t bd = sw128_desc(su32(b));
+        const uint32_t id = tf32_idesc(128, 128);
+        for (int i = 0; i < iters; ++i) tc_mma_tf32_ts(tmem, tmem + 128u, bd, id, i > 0);
+        tc_commit(&bar);
+        if (!mbar_wait(&bar, 0, &abort_word)) raise_flag(flags, FMD_FLAG_WAIT_TIMEOUT);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem) : "memory");
+    }
+}
+
 // ------------------------------------------------------------------- host
 
 using EncodeTiled = PFN_cuTensorMapEncodeTiled_v12000;
@@ -698,6 +771,17 @@ fmd_status fmd_tf32_split(const float* w, int64_t rows, int64_t cols, int64_t ld
     if (rows == 0 || cols == 0) return FMD_OK;
     tf32_split_kernel<<<grid_for(rows * cols, 256), 256, 0, as_stream(stream)>>>(w, rows, cols, ldw,
                                                                                  transpose != 0, hi, lo, ldo);
+    return check_launch();
+}
+
+fmd_status fmd_tf32_mma_rate(int32_t iters, int32_t* flags, void* stream) {
+    if (iters < 1) return FMD_ERR_INVALID_ARGUMENT;
+    DeviceInfo dev;
+    fmd_status st = device_info(&dev);
+    if (st != FMD_OK) return st;
+    if (!dev.sm100) return FMD_ERR_UNSUPPORTED;
+    const int smem = int(kTileBytes) + 1024;
+    tf32_mma_rate_kernel<<<dev.sms, 128, smem, as_stream(stream)>>>(iters, flags);
     return check_launch();
 }
 

@@ -320,6 +320,12 @@ FMD_API fmd_status fmd_gather_add_silu(const float* p0, int64_t ldp0, const fmd_
 FMD_API fmd_status fmd_silu_pair_bwd(const float* grad_core, const float* grad_gate, const float* preact,
                                      int64_t rows, int32_t h, float* grad_pre, int64_t ldgp, void* stream);
 
+/* The roofline denominator of fmd_gemm_tf32x3: one CTA per SM issuing `iters`
+ * back-to-back tcgen05 kind::tf32 MMAs (M = 128, N = 128, K = 8, 262,144
+ * flops each) with no data movement; time the launch with events on `stream`.
+ * No counterpart in the reference (a measurement entry). */
+FMD_API fmd_status fmd_tf32_mma_rate(int32_t iters, int32_t* flags, void* stream);
+
 /* ------------------------------------------- segment attention (C2) */
 
 /* out[s, :] = sum over the rows i of segment s of softmax(logits[i, :] over
