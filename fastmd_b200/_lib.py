@@ -51,6 +51,10 @@ _SIGNATURES: dict[str, list] = {
     "fmd_neighbor_list_workspace_bytes": [_P, c_float, _I64, _I32, POINTER(c_size_t)],
     "fmd_neighbor_list": [_P, _P, _I64, c_float, _I32, _I64, _P, _P, _P, _P, _P, _P, _P, c_size_t, _P, _P],
     "fmd_gemm_f32": [_P, _I64, _P, _I64, _P, _I64, _I32, _P, _P, _I64, _P, _I64, _I64, _I32, _I32, _I32, _I32, _P],
+    "fmd_gated_ln": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I32, c_float, c_float, _P, _P, _P, _P, _P, _P],
+    "fmd_gated_ln_bwd": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I32, _P, _P, _P, _P],
+    "fmd_column_sum_workspace_bytes": [_I64, _I32, POINTER(c_size_t)],
+    "fmd_column_sum": [_P, _I64, _I32, _I64, _P, c_size_t, _P, _P],
     "fmd_reverse_pairs_workspace_bytes": [_I64, POINTER(c_size_t)],
     "fmd_reverse_pairs": [_P, _P, _P, _I64, _I64, _I32, _P, c_size_t, _P, _P, _P, _P, _P],
     "fmd_line_graph_workspace_bytes": [_I64, _I64, POINTER(c_size_t)],
@@ -125,7 +129,7 @@ def check(status: int, what: str) -> None:
 
 # kernels each entry point launches (for the launch count of a step); the default is one
 KERNELS_PER_CALL = {"fmd_refilter_edges": 2, "fmd_refilter_edges_noalloc": 2, "fmd_mace_message_bwd": 2,
-                    "fmd_mace_edge_virial": 2, "fmd_reverse_pairs": 5, "fmd_line_graph": 6}
+                    "fmd_mace_edge_virial": 2, "fmd_reverse_pairs": 5, "fmd_line_graph": 6, "fmd_column_sum": 2}
 
 
 def fused_step_kernels(n_layers: int) -> int:

@@ -31,6 +31,7 @@ EXTRA = {
     "neighbors.cu": ["--fmad=false"],
     "segment_attention.cu": ["--fmad=false"],
     "gather_add_silu.cu": ["--fmad=false"],
+    "gated_ln.cu": ["--fmad=false"],
 }
 
 

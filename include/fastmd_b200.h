@@ -326,6 +326,39 @@ FMD_API fmd_status fmd_silu_pair_bwd(const float* grad_core, const float* grad_g
  * No counterpart in the reference (a measurement entry). */
 FMD_API fmd_status fmd_tf32_mma_rate(int32_t iters, int32_t* flags, void* stream);
 
+/* ------------------------------------------ MatRIS gated-LN epilogue */
+
+/* out = silu(LN(core_x + core_lb)) * sigmoid(LN(gate_x + gate_lb))
+ * (+ residual * res_weight) per row of width dim (<= 256), LN(x) =
+ * (x - mean) rstd w + b with rstd = 1 / sqrt(var + eps); the per-row mean /
+ * rstd of both halves are written for the backward. core_lb / gate_lb (both
+ * or neither) are the preceding linears' biases; residual / res_weight (both
+ * or neither). All [rows, dim] arrays contiguous. Replaces _gated_ln_fwd /
+ * _gated_ln_fwd_2d (fastmd/models/matris/op/triton_gated_ln.py:57, :205). */
+FMD_API fmd_status fmd_gated_ln(const float* core_x, const float* gate_x, const float* core_lb, const float* gate_lb,
+                                const float* core_w, const float* core_b, const float* gate_w, const float* gate_b,
+                                const float* residual, const float* res_weight, int64_t rows, int32_t dim,
+                                float eps_core, float eps_gate, float* out, float* core_mean, float* core_rstd,
+                                float* gate_mean, float* gate_rstd, void* stream);
+
+/* Backward of fmd_gated_ln from its saved mean / rstd: grad_core_x,
+ * grad_gate_x [rows, dim] and, when grad_residual is given,
+ * grad_residual = grad_out * res_weight. Replaces _gated_ln_bwd /
+ * _gated_ln_bwd_2d (triton_gated_ln.py:127, :280). */
+FMD_API fmd_status fmd_gated_ln_bwd(const float* core_x, const float* gate_x, const float* core_lb,
+                                    const float* gate_lb, const float* core_w, const float* core_b,
+                                    const float* gate_w, const float* gate_b, const float* res_weight,
+                                    const float* grad_out, const float* core_mean, const float* core_rstd,
+                                    const float* gate_mean, const float* gate_rstd, int64_t rows, int32_t dim,
+                                    float* grad_core_x, float* grad_gate_x, float* grad_residual, void* stream);
+
+/* out[c] = sum over rows of x[r, c] (row stride ld), in a fixed order (128-row
+ * partials, then their sum): the gradients of the folded linear biases
+ * (triton_gated_ln.py:369 _linear_bias_grads). */
+FMD_API fmd_status fmd_column_sum_workspace_bytes(int64_t rows, int32_t cols, size_t* bytes);
+FMD_API fmd_status fmd_column_sum(const float* x, int64_t rows, int32_t cols, int64_t ld, void* workspace,
+                                  size_t workspace_bytes, float* out, void* stream);
+
 /* ------------------------------------------- segment attention (C2) */
 
 /* out[s, :] = sum over the rows i of segment s of softmax(logits[i, :] over

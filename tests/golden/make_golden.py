@@ -19,7 +19,9 @@ used) and runs, on CPU:
   decomposed indexed-concat SiLU epilogues ``_cat3/_cat4_gather_add_silu_fwd/_bwd``
   (fastmd/engine/kernels/decomposed_indexed_cat_silu_linear.py:97/:156/:234/:383), the
   MatRIS reverse-edge pairing and ordered triplets ``_build_d2u`` / ``_build_line_graph``
-  (fastmd/graph/gpu_graph_builder.py:217/:511, their torch path on CPU), and the
+  (fastmd/graph/gpu_graph_builder.py:217/:511, their torch path on CPU), the
+  gated-LN epilogue ``_gated_ln_fwd_2d`` / ``_gated_ln_bwd_2d``
+  (fastmd/models/matris/op/triton_gated_ln.py:205/:280), and the
   fixed-capacity re-filter ``_count_neighbors_kernel`` /
   ``_materialize_neighbors_kernel`` (fastmd/graph/fixed_capacity_builder.py:98/:189)
   on candidate lists of a dense search, followed by the reference's
@@ -306,6 +308,46 @@ def pairs_line_graph_cases(torch, ggb):
     return out
 
 
+def gated_ln_cases(torch, gl):
+    """The fused GatedMLP epilogue ``silu(LN(core)) * sigmoid(LN(gate)) (+ res_weight * residual)``:
+    the reference's default 2-D tile kernels ``_gated_ln_fwd_2d`` / ``_gated_ln_bwd_2d``
+    (fastmd/models/matris/op/triton_gated_ln.py:205, :280), tiles from its ``_tile_2d``."""
+    out = {}
+    rng = np.random.default_rng(16)
+    for tag, (rows, D, residual, bias) in {"w128_res_bias": (37, 128, True, True), "w32": (45, 32, False, False),
+                                           "w24_bias": (29, 24, False, True), "w128_res": (20, 128, True, False)}.items():
+        blk = 1 << (D - 1).bit_length()
+        arr = dict(cx=2 * rng.standard_normal((rows, D)) + 0.5, gx=rng.standard_normal((rows, D)),
+                   cw=1 + 0.3 * rng.standard_normal(D), cb=0.2 * rng.standard_normal(D),
+                   gw=1 + 0.3 * rng.standard_normal(D), gb=0.2 * rng.standard_normal(D),
+                   clb=0.5 * rng.standard_normal(D), glb=0.5 * rng.standard_normal(D),
+                   res=rng.standard_normal((rows, D)), rw=rng.standard_normal(D), g=rng.standard_normal((rows, D)))
+        arr = {k: v.astype(np.float32) for k, v in arr.items()}
+        t = {k: torch.from_numpy(v) for k, v in arr.items()}
+        y = torch.empty(rows, D)
+        stats = [torch.empty(rows) for _ in range(4)]
+        bm, _ = gl._tile_2d(blk, False)
+        gl._gated_ln_fwd_2d[((rows + bm - 1) // bm,)](
+            t["cx"], t["gx"], t["clb"] if bias else t["cw"], t["glb"] if bias else t["cw"], t["cw"], t["cb"], t["gw"],
+            t["gb"], t["res"] if residual else t["cx"], t["rw"] if residual else t["cw"], y, *stats, rows, D=D, BLK=blk,
+            BM=bm, EPS_CORE=1e-5, EPS_GATE=1e-5, HAS_RESIDUAL=residual, HAS_BIAS=bias)
+        gc, gg, gr = torch.empty(rows, D), torch.empty(rows, D), torch.empty(rows, D)
+        bmb, _ = gl._tile_2d(blk, True)
+        gl._gated_ln_bwd_2d[((rows + bmb - 1) // bmb,)](
+            t["cx"], t["gx"], t["clb"] if bias else t["cw"], t["glb"] if bias else t["cw"], t["cw"], t["cb"], t["gw"],
+            t["gb"], t["rw"] if residual else t["cw"], t["g"], *stats, gc, gg, gr if residual else gc, rows, D=D,
+            BLK=blk, BM=bmb, HAS_RESIDUAL=residual, HAS_BIAS=bias)
+        out.update({f"gln_{tag}_{k}": v for k, v in arr.items()})
+        out[f"gln_{tag}_meta"] = np.array([rows, D, int(residual), int(bias)], dtype=np.int64)
+        out[f"gln_{tag}_out"] = y.numpy()
+        for k, v in zip(("cmean", "crstd", "gmean", "grstd"), stats):
+            out[f"gln_{tag}_{k}"] = v.numpy()
+        out[f"gln_{tag}_gcore"], out[f"gln_{tag}_ggate"] = gc.numpy(), gg.numpy()
+        if residual:
+            out[f"gln_{tag}_gres"] = gr.numpy()
+    return out
+
+
 def nhc_cases(torch, gpu_nhc):
     from ase import units
 
@@ -480,6 +522,7 @@ def main(reference: str) -> None:
     import fastmd.models.matris.op.triton_segment_attention as sa
     import fastmd.engine.kernels.decomposed_indexed_cat_silu_linear as di
     import fastmd.graph.gpu_graph_builder as ggb
+    import fastmd.models.matris.op.triton_gated_ln as gl
 
     np.savez_compressed(HERE / "gather_cat.npz", **gather_cat_cases(torch, gc))
     np.savez_compressed(HERE / "segment_sum.npz", **segment_sum_cases(torch, cs))
@@ -489,6 +532,7 @@ def main(reference: str) -> None:
     np.savez_compressed(HERE / "segment_attention.npz", **segment_attention_cases(torch, sa))
     np.savez_compressed(HERE / "gather_add_silu.npz", **gather_add_silu_cases(torch, di))
     np.savez_compressed(HERE / "line_graph.npz", **pairs_line_graph_cases(torch, ggb))
+    np.savez_compressed(HERE / "gated_ln.npz", **gated_ln_cases(torch, gl))
     for path in sorted(HERE.glob("*.npz")):
         print(path.name, path.stat().st_size)
 
