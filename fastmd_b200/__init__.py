@@ -2,14 +2,14 @@
 
 Surfaces mirroring the reference: ``ops`` (fastmd.ops), ``graph`` and ``line_graph`` (fastmd.graph
 builders, the MatRIS bond pairs and triplets), ``wide_gemm`` and ``decomposed_indexed_cat_silu_linear``
-(fastmd.engine.kernels), ``segment_attention`` and ``gated_ln`` (the MatRIS receiver attention and
-GatedMLP epilogue), ``energy_derivative``
+(fastmd.engine.kernels), ``segment_attention``, ``gated_ln`` and ``pair_aggregate`` (the MatRIS receiver
+attention, GatedMLP epilogue and directed-pair aggregation), ``energy_derivative``
 (fastmd.engine), ``gpu_nhc`` and ``whole_step`` (fastmd.execution / fastmd.interfaces), ``mace`` (the
 MACE-architecture energy tap).
 """
 from fastmd_b200 import (  # noqa: F401
     _lib, decomposed_indexed_cat_silu_linear, energy_derivative, gated_ln, gpu_nhc, graph, line_graph, mace, ops,
-    segment_attention, units, whole_step, wide_gemm)
+    pair_aggregate, segment_attention, units, whole_step, wide_gemm)
 
 __all__ = ["decomposed_indexed_cat_silu_linear", "energy_derivative", "gated_ln", "gpu_nhc", "graph", "line_graph",
-           "mace", "ops", "segment_attention", "units", "whole_step", "wide_gemm"]
+           "mace", "ops", "pair_aggregate", "segment_attention", "units", "whole_step", "wide_gemm"]

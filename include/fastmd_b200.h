@@ -359,6 +359,27 @@ FMD_API fmd_status fmd_column_sum_workspace_bytes(int64_t rows, int32_t cols, si
 FMD_API fmd_status fmd_column_sum(const float* x, int64_t rows, int32_t cols, int64_t ld, void* workspace,
                                   size_t workspace_bytes, float* out, void* stream);
 
+/* ------------------------------- MatRIS directed-pair aggregation */
+
+#define FMD_PAIR_AVERAGE 0
+#define FMD_PAIR_AVERAGE_BWD 1
+#define FMD_PAIR_EXPAND 2
+#define FMD_PAIR_EXPAND_BWD 3
+
+/* The directed-edge <-> undirected-pair maps of the MatRIS atom graph over
+ * pair_index [n_pairs, 2] int64 (a bijection onto the 2U directed rows):
+ *   FMD_PAIR_AVERAGE      out[u] = (in[p0] + in[p1]) * 0.5   in [2U, dim], out [U, dim]
+ *   FMD_PAIR_AVERAGE_BWD  out[p0] = out[p1] = in[u] * 0.5    in [U, dim],  out [2U, dim]
+ *   FMD_PAIR_EXPAND       out[p0] = out[p1] = in[u]          in [U, dim],  out [2U, dim]
+ *   FMD_PAIR_EXPAND_BWD   out[u] = in[p0] + in[p1]           in [2U, dim], out [U, dim]
+ * `in` has row stride ldi (>= dim), `out` is contiguous. Index values outside
+ * [0, 2U) raise FMD_FLAG_INDEX_RANGE (a gathered row reads as zero, a
+ * scattered row is skipped). Replaces _directed_pair_average_fwd / _bwd and
+ * _undirected_pair_expand_fwd / _bwd
+ * (fastmd/models/matris/op/triton_directed_pair_aggregate.py:61, :83, :105, :127). */
+FMD_API fmd_status fmd_pair_aggregate(int32_t op, const float* in, int64_t ldi, const int64_t* pair_index,
+                                      int64_t n_pairs, int32_t dim, float* out, int32_t* flags, void* stream);
+
 /* ------------------------------------------- segment attention (C2) */
 
 /* out[s, :] = sum over the rows i of segment s of softmax(logits[i, :] over

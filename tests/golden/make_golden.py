@@ -21,7 +21,9 @@ used) and runs, on CPU:
   MatRIS reverse-edge pairing and ordered triplets ``_build_d2u`` / ``_build_line_graph``
   (fastmd/graph/gpu_graph_builder.py:217/:511, their torch path on CPU), the
   gated-LN epilogue ``_gated_ln_fwd_2d`` / ``_gated_ln_bwd_2d``
-  (fastmd/models/matris/op/triton_gated_ln.py:205/:280), and the
+  (fastmd/models/matris/op/triton_gated_ln.py:205/:280), the directed-pair average and
+  undirected-pair expansion ``_directed_pair_average_fwd/_bwd`` / ``_undirected_pair_expand_fwd/_bwd``
+  (fastmd/models/matris/op/triton_directed_pair_aggregate.py:61/:83/:105/:127), and the
   fixed-capacity re-filter ``_count_neighbors_kernel`` /
   ``_materialize_neighbors_kernel`` (fastmd/graph/fixed_capacity_builder.py:98/:189)
   on candidate lists of a dense search, followed by the reference's
@@ -348,6 +350,37 @@ def gated_ln_cases(torch, gl):
     return out
 
 
+def pair_aggregate_cases(torch, pa):
+    """Directed-edge <-> undirected-pair aggregation: the reference's ``_directed_pair_average_fwd/_bwd``
+    and ``_undirected_pair_expand_fwd/_bwd`` (fastmd/models/matris/op/triton_directed_pair_aggregate.py:61,
+    :83, :105, :127) on a shuffled pair bijection, launched as its wrappers launch them (BM 8,
+    BD = next_pow2(min(128, D)), grid (cdiv(U, BM), cdiv(D, 128))); the inputs are column views of a
+    wider buffer (row stride ``S0``) where the case says so."""
+    out = {}
+    rng = np.random.default_rng(17)
+    for tag, (U, D, stride) in {"d32": (23, 32, 32), "d128_strided": (24, 128, 192), "d5": (9, 5, 5)}.items():
+        seg = np.repeat(np.arange(U), 2)[rng.permutation(2 * U)]
+        pair = np.argsort(seg, kind="stable").reshape(U, 2).astype(np.int64)
+        base = rng.standard_normal((2 * U, stride)).astype(np.float32)
+        gavg = rng.standard_normal((U, D)).astype(np.float32)
+        und = rng.standard_normal((U, stride)).astype(np.float32)
+        gexp = rng.standard_normal((2 * U, D)).astype(np.float32)
+        bd = min(1 << (D - 1).bit_length(), 128)
+        grid = ((U + 7) // 8, (D + 127) // 128)
+        t_pair = torch.from_numpy(pair)
+        avg, gdata = torch.empty(U, D), torch.empty(2 * U, D)
+        exp, gund = torch.empty(2 * U, D), torch.empty(U, D)
+        pa._directed_pair_average_fwd[grid](torch.from_numpy(base), t_pair, avg, U, D=D, S0=stride, BM=8, BD=bd)
+        pa._directed_pair_average_bwd[grid](torch.from_numpy(gavg), t_pair, gdata, U, D=D, BM=8, BD=bd)
+        pa._undirected_pair_expand_fwd[grid](torch.from_numpy(und), t_pair, exp, U, D=D, S0=stride, BM=8, BD=bd)
+        pa._undirected_pair_expand_bwd[grid](torch.from_numpy(gexp), t_pair, gund, U, D=D, BM=8, BD=bd)
+        out.update({f"pa_{tag}_base": base, f"pa_{tag}_pair": pair, f"pa_{tag}_gavg": gavg, f"pa_{tag}_und": und,
+                    f"pa_{tag}_gexp": gexp, f"pa_{tag}_meta": np.array([U, D, stride], dtype=np.int64),
+                    f"pa_{tag}_avg": avg.numpy(), f"pa_{tag}_gdata": gdata.numpy(), f"pa_{tag}_exp": exp.numpy(),
+                    f"pa_{tag}_gund": gund.numpy()})
+    return out
+
+
 def nhc_cases(torch, gpu_nhc):
     from ase import units
 
@@ -523,6 +556,7 @@ def main(reference: str) -> None:
     import fastmd.engine.kernels.decomposed_indexed_cat_silu_linear as di
     import fastmd.graph.gpu_graph_builder as ggb
     import fastmd.models.matris.op.triton_gated_ln as gl
+    import fastmd.models.matris.op.triton_directed_pair_aggregate as pa
 
     np.savez_compressed(HERE / "gather_cat.npz", **gather_cat_cases(torch, gc))
     np.savez_compressed(HERE / "segment_sum.npz", **segment_sum_cases(torch, cs))
@@ -533,6 +567,7 @@ def main(reference: str) -> None:
     np.savez_compressed(HERE / "gather_add_silu.npz", **gather_add_silu_cases(torch, di))
     np.savez_compressed(HERE / "line_graph.npz", **pairs_line_graph_cases(torch, ggb))
     np.savez_compressed(HERE / "gated_ln.npz", **gated_ln_cases(torch, gl))
+    np.savez_compressed(HERE / "pair_aggregate.npz", **pair_aggregate_cases(torch, pa))
     for path in sorted(HERE.glob("*.npz")):
         print(path.name, path.stat().st_size)
 

@@ -65,6 +65,9 @@ def test_invalid_arguments_are_rejected_before_any_launch():
                                None, None) == 3
     assert lib.fmd_gemm_tf32x3(p16, 9, p16, p16, 8, None, None, 0, p16, 8, 1, 8, 8, 0, 0, None, None) == 3
     assert lib.fmd_tf32_split(None, 2, 2, 2, 0, None, None, 2, None) == 1
+    assert lib.fmd_pair_aggregate(4, p16, 8, p16, 1, 8, p16, None, None) == 1  # no such op
+    assert lib.fmd_pair_aggregate(0, p16, 4, p16, 1, 8, p16, None, None) == 1  # row stride below the width
+    assert lib.fmd_pair_aggregate(0, None, 8, None, 0, 8, None, None, None) == 0  # no pairs: nothing to do
 
 
 def test_no_cpu_fallback():
