@@ -3,7 +3,12 @@
 // (3xTF32). The frozen-weight projections of
 // fastmd/engine/kernels/triton_wide_gemm.py (linear :482, matmul :534).
 //
-//   y[m, n] (=|+=) act( sum_chunks(x[m, :k] . w^T) + bias + c )   w [n, k]
+//   y[m, n] (=|+=) act( sum_chunks(in(x)[m, :k] . w^T) + bias + c )   w [n, k]
+//
+// act: SiLU or none; or the SiLU-derivative gate of a backward,
+// y = (sum + bias) * silu'(c) with c the pre-activation (then not added).
+// in(x): x, or silu(x) applied to the operand as it is split (the next layer
+// of an MLP reading the previous layer's pre-activation).
 //
 // 3xTF32: v = v_hi + v_lo with v_hi = rna_tf32(v), v_lo = v - v_hi, and
 // x . w ~ x_lo w_hi + x_hi w_lo + x_hi w_hi (the x_lo w_lo term is below FP32
@@ -91,8 +96,9 @@ struct WideArgs {
     int32_t* flags;
     int64_t m;
     int32_t n, k;
-    int32_t act, accumulate;
-    int32_t vec_c, vec_y;  // 16-byte row access valid
+    int32_t act, accumulate;  // act: 0 none, 1 SiLU, 2 times silu'(c)
+    int32_t in_silu;          // SiLU on the x operand before the split
+    int32_t vec_c, vec_y;     // 16-byte row access valid
     int32_t tma_y;         // y stored through tmap_y (else direct stores)
 };
 
@@ -279,6 +285,12 @@ __device__ __forceinline__ uint32_t tf32_idesc(int m, int n) {
 // and an approximate divide (a few ulp; 0 for large negative x, x for large positive x).
 __device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
+// d silu / dx = s (1 + x (1 - s)), s = sigmoid(x), with the same hardware exp2 and divide.
+__device__ __forceinline__ float silu_grad(float x) {
+    const float s = __fdividef(1.0f, 1.0f + __expf(-x));
+    return s * (1.0f + x * (1.0f - s));
+}
+
 // ------------------------------------------------------------------ kernel
 
 __device__ __forceinline__ void advance(int& slot, uint32_t& phase, int slots) {
@@ -289,54 +301,63 @@ __device__ __forceinline__ void advance(int& slot, uint32_t& phase, int slots) {
 }
 
 // o[j] = act(acc[j] + bias[col] + c[row, col]) (+ y[row, col] when accumulating) for the 32 columns
-// col0 .. col0 + 31 of this thread's row; nothing is read outside [0, m) x [0, n).
+// col0 .. col0 + 31 of this thread's row, or (act 2) o[j] = (acc[j] + bias[col]) * silu'(c[row, col]);
+// nothing is read outside [0, m) x [0, n). Written as a few whole-row passes, each a straight run of
+// predicated loads and arithmetic behind one uniform test: per-element tests inside one unrolled loop
+// cost the epilogue warps an instruction fetch at every skipped block.
 __device__ __forceinline__ void finish_values(const WideArgs& g, int64_t row, int col0, const float* acc,
                                               float (&o)[32]) {
     const bool row_ok = row < g.m;
-    const float* cr = (g.c != nullptr && row_ok) ? g.c + row * g.ldc : nullptr;
-    const float* yr = (g.accumulate && row_ok) ? g.y + row * g.ldy : nullptr;
+    const bool full = col0 + 32 <= g.n;
 #pragma unroll
-    for (int j = 0; j < 32; j += 4) {
-        const int col = col0 + j;
-        const bool full4 = col + 4 <= g.n;
-        float t[4] = {acc[j], acc[j + 1], acc[j + 2], acc[j + 3]};
-        if (g.bias != nullptr) {
+    for (int j = 0; j < 32; ++j) o[j] = acc[j];
+    if (g.bias != nullptr) {
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
-                if (col + u < g.n) t[u] += __ldg(g.bias + col + u);
-        }
-        if (cr != nullptr) {
-            if (full4 && g.vec_c) {
-                const float4 cv = ldg4(cr + col);
-                t[0] += cv.x;
-                t[1] += cv.y;
-                t[2] += cv.z;
-                t[3] += cv.w;
-            } else {
+        for (int j = 0; j < 32; ++j) o[j] += (col0 + j < g.n) ? __ldg(g.bias + col0 + j) : 0.0f;
+    }
+    if (g.c != nullptr && row_ok) {
+        const float* cr = g.c + row * g.ldc + col0;
+        float cv[32];
+        if (full && g.vec_c) {
 #pragma unroll
-                for (int u = 0; u < 4; ++u)
-                    if (col + u < g.n) t[u] += __ldg(cr + col + u);
+            for (int j = 0; j < 32; j += 4) {
+                const float4 c4 = ldg4(cr + j);
+                cv[j] = c4.x;
+                cv[j + 1] = c4.y;
+                cv[j + 2] = c4.z;
+                cv[j + 3] = c4.w;
             }
-        }
-        if (g.act == 1) {
+        } else {
 #pragma unroll
-            for (int u = 0; u < 4; ++u) t[u] = silu(t[u]);
+            for (int j = 0; j < 32; ++j) cv[j] = (col0 + j < g.n) ? __ldg(cr + j) : 0.0f;
         }
-        if (yr != nullptr) {  // y (=|+=): the previous y, read before this thread's store
-            if (full4 && g.vec_y) {
-                const float4 yv = *reinterpret_cast<const float4*>(yr + col);
-                t[0] += yv.x;
-                t[1] += yv.y;
-                t[2] += yv.z;
-                t[3] += yv.w;
-            } else {
+        if (g.act == 2) {
 #pragma unroll
-                for (int u = 0; u < 4; ++u)
-                    if (col + u < g.n) t[u] += yr[col + u];
+            for (int j = 0; j < 32; ++j) o[j] *= silu_grad(cv[j]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) o[j] += cv[j];
+        }
+    }
+    if (g.act == 1) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) o[j] = silu(o[j]);
+    }
+    if (g.accumulate && row_ok) {  // y (=|+=): the previous y, read before this thread's store
+        const float* yr = g.y + row * g.ldy + col0;
+        if (full && g.vec_y) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+                const float4 yv = *reinterpret_cast<const float4*>(yr + j);
+                o[j] += yv.x;
+                o[j + 1] += yv.y;
+                o[j + 2] += yv.z;
+                o[j + 3] += yv.w;
             }
-        }
+        } else {
 #pragma unroll
-        for (int u = 0; u < 4; ++u) o[j + u] = t[u];
+            for (int j = 0; j < 32; ++j) o[j] += (col0 + j < g.n) ? yr[j] : 0.0f;
+        }
     }
 }
 
@@ -497,6 +518,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         v[4 * c + 1] = f.y;
                         v[4 * c + 2] = f.z;
                         v[4 * c + 3] = f.w;
+                    }
+                    if (g.in_silu) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] = silu(v[j]);
                     }
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
@@ -790,7 +815,8 @@ fmd_status fmd_gemm_tf32x3(const float* x, int64_t ldx, const float* w_hi, const
                            int32_t n, int32_t k, int32_t act, int32_t accumulate, int32_t* flags, void* stream) {
     if (m < 0 || n < 1 || k < 1 || m > (int64_t(1) << 31) - kBM || x == nullptr || w_hi == nullptr ||
         w_lo == nullptr || y == nullptr || ldx < k || ldw < k || ldy < n || (c != nullptr && ldc < n) ||
-        (act != 0 && act != 1))
+        (act & ~(FMD_ACT_MASK | FMD_ACT_INPUT_SILU)) || (act & FMD_ACT_MASK) > FMD_ACT_SILU_GRAD ||
+        ((act & FMD_ACT_MASK) == FMD_ACT_SILU_GRAD && c == nullptr))
         return FMD_ERR_INVALID_ARGUMENT;
     // TMA: 16-byte aligned bases and row strides
     if (!aligned16(x) || !aligned16(w_hi) || !aligned16(w_lo) || (ldx & 3) || (ldw & 3))
@@ -834,7 +860,8 @@ fmd_status fmd_gemm_tf32x3(const float* x, int64_t ldx, const float* w_hi, const
     g.m = m;
     g.n = n;
     g.k = k;
-    g.act = act;
+    g.act = act & FMD_ACT_MASK;
+    g.in_silu = (act & FMD_ACT_INPUT_SILU) != 0;
     g.accumulate = accumulate != 0;
     g.vec_c = c != nullptr && aligned16(c) && (ldc & 3) == 0;
     g.vec_y = aligned16(y) && (ldy & 3) == 0;

@@ -19,6 +19,11 @@
 //                   layer and the geometry backward: dE/dr_e per edge
 //   forces          F_a = sum over received edges - sum over sent edges of
 //                   dE/dr_e (both CSRs), the per-system energy sums
+// From the tensor-core threshold on (the large replica unions), edge_fwd and
+// edge_bwd are replaced by a geometry kernel, the radial MLPs as chained
+// tcgen05 3xTF32 GEMMs on the pre-activations (fmd_gemm_tf32x3 with the SiLU
+// on its input operand, and the SiLU-derivative gate in the backward), and a
+// geometry backward kernel.
 // Weights are frozen; the host prepares transposed copies once so every
 // channel-mixing loop reads weights coalesced (thread = output channel).
 
@@ -72,6 +77,12 @@ struct FusedWeights {
     double scale, shift;
     int n_layers, n_basis, poly_p, readout_hidden;
     float r_max, inv_avg;
+    // tensor-core radial MLP: TF32 splits of W2, W3, W4 as [out][in] and as [in][out]
+    const float* tc_hi[3][kMaxLayers];
+    const float* tc_lo[3][kMaxLayers];
+    const float* tc_t_hi[3][kMaxLayers];
+    const float* tc_t_lo[3][kMaxLayers];
+    int64_t tc_min_edges;             // 0: never
 };
 
 // per-layer activations
@@ -98,6 +109,8 @@ struct FusedState {
     const int32_t* elem;        // [N]
     const int32_t* groups;      // [n_groups][kG] atom ids (-1 padding), same element per group
     int64_t n_groups;
+    float* pre[3][kMaxLayers];  // [E][kH] radial pre-activations p1..p3 (tensor-core path; gradients in place)
+    int32_t* flags;
 };
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
@@ -841,6 +854,42 @@ __device__ __forceinline__ void hidden_bwd(const float (*g)[kHS], const float (*
     for (int m = 0; m < EPG; ++m) out[eg * EPG + m][k] = acc[m] * silu_g(pre[eg * EPG + m][k]);
 }
 
+// g_r[e] = dE/dr_e from the spherical-harmonic gradient dY[e] and the radial-feature gradient dphi
+// (the geometry backward of one edge)
+__device__ __forceinline__ void geometry_grad(const FusedWeights& w, const FusedState& st, int64_t e,
+                                              const float* dphi) {
+    const float pref = sqrtf(2.0f / w.r_max);
+    const float4 y = st.ysh[e];
+    const float d = y.w;
+    float gx = 0.f, gy = 0.f, gz = 0.f;
+    if (d > 0.f) {
+        const float inv = 1.0f / d;
+        const float ux = y.x * kIS3, uy = y.y * kIS3, uz = y.z * kIS3;
+        const float* gyv = st.dY + 3 * e;
+        const float gu = (gyv[0] * ux + gyv[1] * uy) + gyv[2] * uz;
+        gx = kS3 * (gyv[0] - gu * ux) * inv;
+        gy = kS3 * (gyv[1] - gu * uy) * inv;
+        gz = kS3 * (gyv[2] - gu * uz) * inv;
+        float f, df;
+        cutoff_poly(d, w.r_max, w.poly_p, f, df);
+        float gd = 0.f;
+        for (int n = 0; n < w.n_basis; ++n) {
+            const float k = float(n + 1) * 3.14159265358979323846f / w.r_max;
+            float sn, cs;
+            sincosf(k * d, &sn, &cs);
+            const float b = pref * sn * inv;
+            const float db = pref * (k * cs * d - sn) * inv * inv;
+            gd += dphi[n] * (db * f + b * df);
+        }
+        gx += gd * ux;
+        gy += gd * uy;
+        gz += gd * uz;
+    }
+    st.g_r[3 * e] = gx;
+    st.g_r[3 * e + 1] = gy;
+    st.g_r[3 * e + 2] = gz;
+}
+
 // the radial MLP backward of every layer (the forward recomputed from the distances) and the
 // geometry backward: g_r [E][3] = dE/dr_e
 template <int C>
@@ -907,39 +956,144 @@ __global__ void __launch_bounds__(256) edge_bwd_kernel(EdgeArgs a, FusedWeights 
             }
         }
         __syncthreads();
-        if (t < ne) {
+        if (t < ne) geometry_grad(w, st, e0 + t, m.dphi[t]);
+    }
+}
+
+// ------------------------------------------------ tensor-core radial MLP path
+
+constexpr int kTG = 16;  // edges per tile of the geometry kernels
+
+// geometry, radial features and the first radial layer's pre-activation p1 = phi W1^T of every layer
+// for every edge row (padding rows after the real count: p1 = 0, so the GEMM chain yields R = 0 there)
+__global__ void __launch_bounds__(256) edge_geom_tc_kernel(EdgeArgs a, FusedWeights w, FusedState st) {
+    __shared__ float phi[kTG][16];
+    __shared__ float w1t[kMaxLayers][16][kH];
+    const int t = threadIdx.x;
+    const float pref = sqrtf(2.0f / w.r_max);
+    const int64_t n_real = real_edges(a);
+    for (int L = 0; L < w.n_layers; ++L)
+        for (int idx = t; idx < w.n_basis * kH; idx += 256) w1t[L][idx / kH][idx % kH] = w.w1t[L][idx];
+    const int64_t n_tiles = (a.n_edges + kTG - 1) / kTG;
+    for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+        const int64_t e0 = tile * kTG;
+        const int ne = int(a.n_edges - e0 < kTG ? a.n_edges - e0 : kTG);
+        __syncthreads();
+        if (t < kTG) {
             const int64_t e = e0 + t;
-            const float4 y = st.ysh[e];
-            const float d = y.w;
-            float gx = 0.f, gy = 0.f, gz = 0.f;
-            if (d > 0.f) {
-                const float inv = 1.0f / d;
-                const float ux = y.x * kIS3, uy = y.y * kIS3, uz = y.z * kIS3;
-                const float* gyv = st.dY + 3 * e;
-                const float gu = (gyv[0] * ux + gyv[1] * uy) + gyv[2] * uz;
-                gx = kS3 * (gyv[0] - gu * ux) * inv;
-                gy = kS3 * (gyv[1] - gu * uy) * inv;
-                gz = kS3 * (gyv[2] - gu * uz) * inv;
-                float f, df;
-                cutoff_poly(d, w.r_max, w.poly_p, f, df);
-                float gd = 0.f;
-                for (int n = 0; n < w.n_basis; ++n) {
-                    const float k = float(n + 1) * 3.14159265358979323846f / w.r_max;
-                    float sn, cs;
-                    sincosf(k * d, &sn, &cs);
-                    const float b = pref * sn * inv;
-                    const float db = pref * (k * cs * d - sn) * inv * inv;
-                    gd += m.dphi[t][n] * (db * f + b * df);
-                }
-                gx += gd * ux;
-                gy += gd * uy;
-                gz += gd * uz;
+            float d = 0.f;
+            if (e < n_real) {
+                const int64_t i = a.edge_index[2 * e], j = a.edge_index[2 * e + 1];
+                const float ix = a.edge_image[3 * e], iy = a.edge_image[3 * e + 1], iz = a.edge_image[3 * e + 2];
+                const float* c = a.cell;
+                const float rx = (a.pos[3 * j] - a.pos[3 * i]) + ((ix * c[0] + iy * c[3]) + iz * c[6]);
+                const float ry = (a.pos[3 * j + 1] - a.pos[3 * i + 1]) + ((ix * c[1] + iy * c[4]) + iz * c[7]);
+                const float rz = (a.pos[3 * j + 2] - a.pos[3 * i + 2]) + ((ix * c[2] + iy * c[5]) + iz * c[8]);
+                d = sqrtf((rx * rx + ry * ry) + rz * rz);
+                const float inv = d > 0.f ? 1.0f / d : 0.f;
+                st.ysh[e] = make_float4(kS3 * rx * inv, kS3 * ry * inv, kS3 * rz * inv, d);
             }
-            st.g_r[3 * e] = gx;
-            st.g_r[3 * e + 1] = gy;
-            st.g_r[3 * e + 2] = gz;
+            float f, df;
+            cutoff_poly(d, w.r_max, w.poly_p, f, df);
+            const float inv = d > 0.f ? 1.0f / d : 0.f;
+            for (int n = 0; n < w.n_basis; ++n) {
+                const float k = float(n + 1) * 3.14159265358979323846f / w.r_max;
+                phi[t][n] = d > 0.f ? pref * sinf(k * d) * inv * f : 0.f;
+            }
+        }
+        __syncthreads();
+        for (int L = 0; L < w.n_layers; ++L) {
+            float* p1 = st.pre[0][L];
+            for (int idx = t; idx < ne * kH; idx += 256) {
+                const int e = idx / kH, k = idx % kH;
+                float acc = 0.f;
+                for (int n = 0; n < w.n_basis; ++n) acc = fmaf(phi[e][n], w1t[L][n][k], acc);
+                p1[(e0 + e) * kH + k] = acc;
+            }
         }
     }
+}
+
+// dphi = sum over layers of g1 W1 (g1 = dE/dp1, left in the p1 buffer by the GEMM chain), then the
+// geometry backward of every real edge
+__global__ void __launch_bounds__(256) edge_geom_bwd_tc_kernel(EdgeArgs a, FusedWeights w, FusedState st) {
+    __shared__ float w1[kMaxLayers][kH][17];  // W1 [hidden][basis] (padded rows)
+    __shared__ float g[kTG][kH + 1];
+    __shared__ float dphi[kTG][16];
+    const int t = threadIdx.x;
+    const int nb = w.n_basis;
+    for (int L = 0; L < w.n_layers; ++L)
+        for (int idx = t; idx < kH * nb; idx += 256) w1[L][idx / nb][idx % nb] = w.w1[L][idx];
+    const int64_t n_edges = real_edges(a);
+    const int64_t n_tiles = (n_edges + kTG - 1) / kTG;
+    for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+        const int64_t e0 = tile * kTG;
+        const int ne = int(n_edges - e0 < kTG ? n_edges - e0 : kTG);
+        __syncthreads();
+        if (t < kTG * 16) dphi[t / 16][t % 16] = 0.f;
+        for (int L = 0; L < w.n_layers; ++L) {
+            const float* g1 = st.pre[0][L];
+            __syncthreads();
+            for (int idx = t; idx < ne * kH; idx += 256) g[idx / kH][idx % kH] = g1[(e0 + idx / kH) * kH + idx % kH];
+            __syncthreads();
+            if (t < ne * nb) {
+                const int e = t / nb, n = t % nb;
+                float acc = 0.f;
+#pragma unroll 16
+                for (int c = 0; c < kH; ++c) acc = fmaf(g[e][c], w1[L][c][n], acc);
+                dphi[e][n] += acc;
+            }
+        }
+        __syncthreads();
+        if (t < ne) geometry_grad(w, st, e0 + t, dphi[t]);
+    }
+}
+
+// the radial MLPs of every layer as GEMMs on the tensor cores:
+//   p2 = silu(p1) W2^T, p3 = silu(p2) W3^T, R = silu(p3) W4^T
+fmd_status radial_tc_forward(const FusedWeights& w, const FusedState& st, int64_t E, int C, cudaStream_t s) {
+    for (int L = 0; L < w.n_layers; ++L) {
+        const int PC = (L == 0 ? 2 : 4) * C;
+        const int act = FMD_ACT_NONE | FMD_ACT_INPUT_SILU;
+        fmd_status r = fmd_gemm_tf32x3(st.pre[0][L], kH, w.tc_hi[0][L], w.tc_lo[0][L], kH, nullptr, nullptr, 0,
+                                       st.pre[1][L], kH, E, kH, kH, act, 0, st.flags, s);
+        if (r == FMD_OK)
+            r = fmd_gemm_tf32x3(st.pre[1][L], kH, w.tc_hi[1][L], w.tc_lo[1][L], kH, nullptr, nullptr, 0,
+                                st.pre[2][L], kH, E, kH, kH, act, 0, st.flags, s);
+        if (r == FMD_OK)
+            r = fmd_gemm_tf32x3(st.pre[2][L], kH, w.tc_hi[2][L], w.tc_lo[2][L], kH, nullptr, nullptr, 0, st.R[L],
+                                PC, E, PC, kH, act, 0, st.flags, s);
+        if (r != FMD_OK) return r;
+    }
+    return FMD_OK;
+}
+
+// their backward, each gradient written over its pre-activation:
+//   g3 = (dR W4) silu'(p3), g2 = (g3 W3) silu'(p2), g1 = (g2 W2) silu'(p1)
+fmd_status radial_tc_backward(const FusedWeights& w, const FusedState& st, int64_t E, int C, cudaStream_t s) {
+    for (int L = 0; L < w.n_layers; ++L) {
+        const int PC = (L == 0 ? 2 : 4) * C;
+        fmd_status r = fmd_gemm_tf32x3(st.dR[L], PC, w.tc_t_hi[2][L], w.tc_t_lo[2][L], PC, nullptr, st.pre[2][L],
+                                       kH, st.pre[2][L], kH, E, kH, PC, FMD_ACT_SILU_GRAD, 0, st.flags, s);
+        if (r == FMD_OK)
+            r = fmd_gemm_tf32x3(st.pre[2][L], kH, w.tc_t_hi[1][L], w.tc_t_lo[1][L], kH, nullptr, st.pre[1][L], kH,
+                                st.pre[1][L], kH, E, kH, kH, FMD_ACT_SILU_GRAD, 0, st.flags, s);
+        if (r == FMD_OK)
+            r = fmd_gemm_tf32x3(st.pre[1][L], kH, w.tc_t_hi[0][L], w.tc_t_lo[0][L], kH, nullptr, st.pre[0][L], kH,
+                                st.pre[0][L], kH, E, kH, kH, FMD_ACT_SILU_GRAD, 0, st.flags, s);
+        if (r != FMD_OK) return r;
+    }
+    return FMD_OK;
+}
+
+// every pointer of the tensor-core path present, and the step large enough
+bool use_radial_tc(const FusedWeights& w, const FusedState& st, int64_t n_edges) {
+    if (w.tc_min_edges <= 0 || n_edges < w.tc_min_edges) return false;
+    for (int L = 0; L < w.n_layers; ++L)
+        for (int k = 0; k < 3; ++k)
+            if (!w.tc_hi[k][L] || !w.tc_lo[k][L] || !w.tc_t_hi[k][L] || !w.tc_t_lo[k][L] || !st.pre[k][L])
+                return false;
+    return true;
 }
 
 // forces F_a = sum over received edges of g_r - sum over sent edges of g_r, and the energies
@@ -1009,7 +1163,16 @@ fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeigh
         }
     }
     const int L = w.n_layers;
-    if (n_tiles > 0 && on(0)) edge_fwd_kernel<C><<<edge_grid, 256, sizeof(EdgeFwdSmem), s>>>(ea, w, st);
+    const bool tc = use_radial_tc(w, st, ea.n_edges);
+    const int geom_grid = int((ea.n_edges + kTG - 1) / kTG < int64_t(kNumSMs) * 8 ? (ea.n_edges + kTG - 1) / kTG
+                                                                                  : int64_t(kNumSMs) * 8);
+    if (tc && n_tiles > 0 && on(0)) {
+        edge_geom_tc_kernel<<<geom_grid, 256, 0, s>>>(ea, w, st);
+        if ((stt = check_launch()) != FMD_OK) return stt;
+        if ((stt = radial_tc_forward(w, st, ea.n_edges, C, s)) != FMD_OK) return stt;
+    } else if (n_tiles > 0 && on(0)) {
+        edge_fwd_kernel<C><<<edge_grid, 256, sizeof(EdgeFwdSmem), s>>>(ea, w, st);
+    }
     for (int l = 0; l < L; ++l) {
         if (on(1)) {
             if (l == 0) message_fused_kernel<C, 2><<<atom_grid, 128, 0, s>>>(ga, w, st, l);
@@ -1023,7 +1186,13 @@ fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeigh
         if (on(5)) sender_node_kernel<C><<<group_grid, kQ * C, node_smem, s>>>(ga, w, st, l);
     }
     if (on(4)) msg_bwd_edge_kernel<C, 2><<<atom_grid, 128, 0, s>>>(ga, w, st, 0, L != 1);
-    if (b_tiles > 0 && on(6)) edge_bwd_kernel<C><<<bwd_grid, 256, sizeof(EdgeBwdSmem), s>>>(ea, w, st);
+    if (tc && b_tiles > 0 && on(6)) {
+        if ((stt = check_launch()) != FMD_OK) return stt;
+        if ((stt = radial_tc_backward(w, st, ea.n_edges, C, s)) != FMD_OK) return stt;
+        edge_geom_bwd_tc_kernel<<<geom_grid, 256, 0, s>>>(ea, w, st);
+    } else if (b_tiles > 0 && on(6)) {
+        edge_bwd_kernel<C><<<bwd_grid, 256, sizeof(EdgeBwdSmem), s>>>(ea, w, st);
+    }
     if (on(7)) forces_kernel<<<n_systems, 256, 0, s>>>(ga, st.g_r, st.node_energy, atoms_per_system, forces, total);
     return check_launch();
 }
@@ -1067,6 +1236,14 @@ fmd_status fmd_mace_fused_step(const fmd_mace_fused_weights* weights, const fmd_
     w.s_t0 = h.s_t0; w.r0 = h.r0; w.ra = h.ra; w.rb = h.rb; w.e0 = h.e0;
     w.scale = h.scale; w.shift = h.shift; w.n_layers = h.n_layers; w.n_basis = h.n_basis; w.poly_p = h.poly_p;
     w.readout_hidden = h.readout_hidden; w.r_max = h.r_max; w.inv_avg = h.inv_avg;
+    w.tc_min_edges = h.radial_tc_min_edges;
+    for (int k = 0; k < 3; ++k)
+        for (int l = 0; l < h.n_layers; ++l) {
+            w.tc_hi[k][l] = h.radial_tc_hi[k][l]; w.tc_lo[k][l] = h.radial_tc_lo[k][l];
+            w.tc_t_hi[k][l] = h.radial_tc_t_hi[k][l]; w.tc_t_lo[k][l] = h.radial_tc_t_lo[k][l];
+            st.pre[k][l] = state->radial_pre[k][l];
+        }
+    st.flags = state->flags;
     st.ysh = reinterpret_cast<float4*>(state->ysh); st.dY = state->dY; st.g_r = state->g_r;
     st.e_term0 = state->e_term0; st.node_energy = state->node_energy; st.elem = state->elem;
     st.groups = state->groups; st.n_groups = state->n_groups;

@@ -37,6 +37,9 @@ from fastmd_b200 import _lib
 from fastmd_b200._lib import call, ptr, stream
 
 ELEMENTS = 89  # one-hot over Z = 1..89 (the benchmark's "89 element embeddings")
+RADIAL_PRECISIONS = ("auto", "tf32x3", "ieee")
+# the captured-mode row threshold of the reference's 3xTF32 wide GEMMs (fastmd/config.py:153)
+RADIAL_TC_MIN_EDGES = 65536
 
 
 @dataclass(frozen=True)
@@ -136,8 +139,13 @@ class MACEModel:
     name = "mace"
 
     def __init__(self, config: MACEConfig | None = None, weights: dict | None = None, *, seed: int = 1,
-                 device="cuda") -> None:
+                 device="cuda", radial_precision: str = "auto") -> None:
         self.config = config or MACEConfig()
+        if radial_precision not in RADIAL_PRECISIONS:
+            raise ValueError(f"radial_precision must be one of {RADIAL_PRECISIONS}")
+        # the fused step's radial MLPs: tcgen05 3xTF32 GEMMs from this many edge rows on, else the
+        # IEEE FP32 edge kernels ("auto": the reference's 65,536-row wide-GEMM threshold)
+        self.radial_tc_min_edges = {"auto": RADIAL_TC_MIN_EDGES, "tf32x3": 1, "ieee": 0}[radial_precision]
         if self.config.l_max != 1 or self.config.correlation != 3:
             raise ValueError("this build implements l_max = 1 and correlation = 3")
         if self.config.channels % 32 != 0:
@@ -411,14 +419,16 @@ def _struct_types():
             ("s_t0", P), ("r0", P), ("ra", P), ("rb", P), ("e0", P), ("scale", ctypes.c_double),
             ("shift", ctypes.c_double), ("n_layers", ctypes.c_int32), ("n_basis", ctypes.c_int32),
             ("poly_p", ctypes.c_int32), ("readout_hidden", ctypes.c_int32), ("radial_hidden", ctypes.c_int32),
-            ("r_max", ctypes.c_float), ("inv_avg", ctypes.c_float), ("_pad", ctypes.c_int32)]
+            ("r_max", ctypes.c_float), ("inv_avg", ctypes.c_float), ("_pad", ctypes.c_int32)] + [
+            (name, arr * 3) for name in ("radial_tc_hi", "radial_tc_lo", "radial_tc_t_hi", "radial_tc_t_lo")] + [
+            ("radial_tc_min_edges", ctypes.c_int64)]
 
     class FusedState(ctypes.Structure):
         _fields_ = [(name, arr) for name in (
             "R", "dR", "s_t", "v_t", "A0", "A1", "A0l", "A1l", "s_out", "v_out", "dA0", "dA1", "ds_skip",
             "dv_skip")] + [
             ("ysh", P), ("dY", P), ("g_r", P), ("e_term0", P), ("node_energy", P), ("elem", P), ("groups", P),
-            ("n_groups", ctypes.c_int64)]
+            ("n_groups", ctypes.c_int64), ("radial_pre", arr * 3), ("flags", P)]
 
     return FusedWeights, FusedState
 
@@ -484,6 +494,23 @@ def _fused_weights(model: "MACEModel"):
     fw.r_max, fw.inv_avg = float(c.r_max), float(1.0 / c.avg_num_neighbors)
     if len(set(c.radial_hidden)) != 1 or c.radial_hidden[0] != 64:
         raise ValueError("the fused step implements radial MLP widths (64, 64, 64)")
+    fw.radial_tc_min_edges = int(model.radial_tc_min_edges)
+    if model.radial_tc_min_edges > 0:
+        # TF32 hi/lo pairs of W2..W4 as [out][in] (forward) and [in][out] (backward), K-major for TMA
+        s = stream(dev)
+        for L in range(c.num_interactions):
+            for k in range(3):
+                wk = w[f"{L}.radial.{k + 1}"].contiguous()
+                for transposed, hi_name, lo_name in ((0, "radial_tc_hi", "radial_tc_lo"),
+                                                     (1, "radial_tc_t_hi", "radial_tc_t_lo")):
+                    rows, cols = wk.shape
+                    shape = (cols, rows) if transposed else (rows, cols)
+                    hi = torch.empty(shape, dtype=torch.float32, device=dev)
+                    lo = torch.empty(shape, dtype=torch.float32, device=dev)
+                    call("fmd_tf32_split", ptr(wk), rows, cols, cols, transposed, ptr(hi), ptr(lo), shape[1], s)
+                    keep[f"{L}.{hi_name}{k}"], keep[f"{L}.{lo_name}{k}"] = hi, lo
+                    getattr(fw, hi_name)[k][L] = ptr(hi)
+                    getattr(fw, lo_name)[k][L] = ptr(lo)
     return fw, keep
 
 
@@ -529,6 +556,13 @@ class _FusedBuffers:
         st.ysh, st.dY, st.g_r = ptr(self.t["ysh"]), ptr(self.t["dY"]), ptr(self.t["g_r"])
         st.e_term0, st.node_energy = ptr(self.t["e_term0"]), ptr(self.t["node_energy"])
         st.elem, st.groups, st.n_groups = ptr(elem), ptr(groups), int(groups.shape[0])
+        if 0 < model.radial_tc_min_edges <= E:  # the radial pre-activations of the tensor-core path
+            for L in range(c.num_interactions):
+                for k in range(3):
+                    self.t[f"{L}.pre{k}"] = z(E, c.radial_hidden[0])
+                    st.radial_pre[k][L] = ptr(self.t[f"{L}.pre{k}"])
+        st.flags = ptr(_lib.flags_word(dev))
+        self.tensor_core_radial = 0 < model.radial_tc_min_edges <= E
         self.state = st
         self.energy: dict[int, Tensor] = {}
 

@@ -434,11 +434,20 @@ FMD_API fmd_status fmd_paired_segment_attention_bwd_rows(
 FMD_API fmd_status fmd_tf32_split(const float* w, int64_t rows, int64_t cols, int64_t ldw, int32_t transpose,
                                   float* hi, float* lo, int64_t ldo, void* stream);
 
+#define FMD_ACT_NONE 0
+#define FMD_ACT_SILU 1        /* y = silu(sum + bias + c) */
+#define FMD_ACT_SILU_GRAD 2   /* y = (sum + bias) * silu'(c): c is a pre-activation, not added */
+#define FMD_ACT_MASK 15
+#define FMD_ACT_INPUT_SILU 16 /* or-ed in: the x operand enters as silu(x) */
+
 /* y[m, n] (=|+=) act(x[m, :k] . w^T + bias + c) on the tcgen05 tensor cores
  * at FP32 accuracy (3xTF32: x_lo w_hi + x_hi w_lo + x_hi w_hi, a fresh TMEM
  * accumulator per 64-wide K chunk, the chunks summed in FP32), for w [n, k]
  * given as its fmd_tf32_split pair (w_hi, w_lo, row stride ldw). bias [n]
- * and the residual c [m, ldc] are optional; act 0 = identity, 1 = SiLU.
+ * and the residual c [m, ldc] are optional; act is one of FMD_ACT_NONE,
+ * FMD_ACT_SILU, FMD_ACT_SILU_GRAD (c required), optionally or-ed with
+ * FMD_ACT_INPUT_SILU (the layers of an MLP chained on pre-activations, and
+ * their backward). y may alias c (each element is read before it is written).
  * x, w_hi, w_lo 16-byte aligned with ldx, ldw multiples of 4 (TMA), else
  * FMD_ERR_UNSUPPORTED (as on a non-sm_100 device). A bounded in-kernel wait
  * that expires raises FMD_FLAG_WAIT_TIMEOUT in flags (may be null).
@@ -546,7 +555,16 @@ FMD_API fmd_status fmd_mace_node_energy_bwd(const double* d_total, double scale,
  * element skip matrices skip [Z][in][out] and skipt [Z][out][in], the
  * up-mixed element embedding s_t0 [Z][C], the readouts r0 [C], ra [RH][C],
  * rb [RH] and e0 [Z] (fp64). Pointers of absent pieces (layer 0's up and
- * skip, the last layer's vector output) are NULL. */
+ * skip, the last layer's vector output) are NULL.
+ * Tensor-core radial MLPs: with radial_tc_min_edges > 0, the TF32 splits
+ * (fmd_tf32_split) of W2, W3, W4 as [out][in] (radial_tc_hi/lo[0..2]) and as
+ * [in][out] (radial_tc_t_hi/lo[0..2]) given, and the state's radial_pre
+ * buffers given, a step of at least radial_tc_min_edges edge rows runs the
+ * radial MLPs and their backward as chained fmd_gemm_tf32x3 GEMMs on the
+ * pre-activations p1..p3 (3xTF32, FP32 accuracy) instead of the SIMT edge
+ * kernels (IEEE FP32). The reference's own wide-GEMM rule takes the 3xTF32
+ * path from 65,536 rows in a capture (fastmd/config.py:153,
+ * fastmd/engine/kernels/triton_wide_gemm.py:339 _decide). */
 #define FMD_MACE_MAX_LAYERS 4
 typedef struct fmd_mace_fused_weights {
     const float* radial_w1t[FMD_MACE_MAX_LAYERS];
@@ -590,6 +608,11 @@ typedef struct fmd_mace_fused_weights {
     float r_max;
     float inv_avg;
     int32_t _pad;
+    const float* radial_tc_hi[3][FMD_MACE_MAX_LAYERS];
+    const float* radial_tc_lo[3][FMD_MACE_MAX_LAYERS];
+    const float* radial_tc_t_hi[3][FMD_MACE_MAX_LAYERS];
+    const float* radial_tc_t_lo[3][FMD_MACE_MAX_LAYERS];
+    int64_t radial_tc_min_edges;
 } fmd_mace_fused_weights;
 
 /* Persistent activations of the fused step (caller-owned device buffers,
@@ -597,7 +620,10 @@ typedef struct fmd_mace_fused_weights {
  * layer 0, else 4), s_t [N][C], v_t/A1/A1l/v_out/dA1/dv_skip [N][3][C],
  * A0/A0l/s_out/dA0/ds_skip [N][C]; ysh [E][4] (16-byte aligned), dY and g_r
  * [E][3], e_term0 [N], node_energy [N] (fp64), elem [N] (element rows) and
- * groups [n_groups][4] (atom ids of the same element, -1 padding). */
+ * groups [n_groups][4] (atom ids of the same element, -1 padding);
+ * radial_pre[k][L] [E][64] the radial pre-activations p1..p3 of the
+ * tensor-core path (NULL when it is not used) and flags (may be NULL) for
+ * FMD_FLAG_WAIT_TIMEOUT of its GEMMs. */
 typedef struct fmd_mace_fused_state {
     float* R[FMD_MACE_MAX_LAYERS];
     float* dR[FMD_MACE_MAX_LAYERS];
@@ -621,6 +647,8 @@ typedef struct fmd_mace_fused_state {
     const int32_t* elem;
     const int32_t* groups;
     int64_t n_groups;
+    float* radial_pre[3][FMD_MACE_MAX_LAYERS];
+    int32_t* flags;
 } fmd_mace_fused_state;
 
 /* Energies and forces of one step: geometry, radial MLPs, messages, node

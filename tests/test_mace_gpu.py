@@ -200,3 +200,53 @@ def test_fused_replica_union_equals_single_systems(cuda):
         e, f = model.energy_forces_fused(single)
         assert torch.equal(energy[r:r + 1], e)
         assert torch.equal(forces[r * N:(r + 1) * N], f)
+
+
+def test_fused_tensor_core_radial_matches_oracle(cuda):
+    """The radial MLPs and their backward as the tcgen05 3xTF32 GEMM chain (forced on the 135-atom
+    graph) against the FP64 oracle and the IEEE edge kernels, to the benchmark's 1e-5."""
+    from fastmd_b200.mace import MACEModel
+    from fastmd_b200.ops import read_flags
+
+    pos, cell, numbers, _ = _system(0)
+    _, batch = _graph(pos, cell, numbers, cuda)
+    read_flags(cuda)
+    tc = MACEModel(device=cuda, radial_precision="tf32x3")
+    energy, forces = (x.clone() for x in tc.energy_forces_fused(batch))
+    assert next(iter(tc._fused_bufs.values())).tensor_core_radial
+    E, F, _ = _oracle(tc, batch, numbers)
+    _close(energy.cpu().numpy(), E)
+    _close(forces.cpu().numpy(), F)
+    ieee = MACEModel(device=cuda, radial_precision="ieee")
+    ei, fi = ieee.energy_forces_fused(batch)
+    assert not next(iter(ieee._fused_bufs.values())).tensor_core_radial
+    _close(forces.cpu().numpy(), fi.cpu().numpy().astype(np.float64))
+    e2, f2 = tc.energy_forces_fused(batch)
+    assert torch.equal(e2, energy) and torch.equal(f2, forces)  # deterministic
+    assert read_flags(cuda) == 0
+
+
+def test_fused_tensor_core_radial_on_a_large_union(cuda):
+    """32 replicas (about 70k edge rows, above the 65,536-row threshold): the default precision takes
+    the tensor-core radial path; per-replica energies and forces match the IEEE path and, for replica 0,
+    the FP64 oracle of the single system."""
+    from fastmd_b200.mace import MACEModel
+
+    R = 32
+    systems = [_system(seed) for seed in range(R)]
+    cell, numbers = systems[0][1], systems[0][2]
+    N = numbers.size
+    _, batch = _graph(np.concatenate([s[0] for s in systems]), cell, numbers, cuda, replicas=R, u_capacity=1100)
+    assert batch.edge_index.shape[0] >= 65536
+    auto = MACEModel(device=cuda)
+    energy, forces = (x.clone() for x in auto.energy_forces_fused(batch, n_systems=R))
+    assert next(iter(auto._fused_bufs.values())).tensor_core_radial
+    ieee = MACEModel(device=cuda, radial_precision="ieee")
+    ei, fi = ieee.energy_forces_fused(batch, n_systems=R)
+    for r in range(R):
+        _close(energy[r].cpu().numpy(), ei[r].cpu().numpy())
+        _close(forces[r * N:(r + 1) * N].cpu().numpy(), fi[r * N:(r + 1) * N].cpu().numpy().astype(np.float64))
+    _, single = _graph(systems[0][0], cell, numbers, cuda)
+    E, F, _ = _oracle(auto, single, numbers)
+    _close(energy[0].cpu().numpy(), E)
+    _close(forces[:N].cpu().numpy(), F)
