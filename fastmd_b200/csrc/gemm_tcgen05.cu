@@ -56,6 +56,7 @@ namespace fmd {
 namespace {
 
 constexpr int kBM = 128, kBN = 128, kBK = 32, kChunkK = 64;
+static_assert(kBK == 32, "the stage MMA issue is written for 4 K-steps of 8");
 constexpr int kStages = 4, kAccBufs = 3, kABufs = 2;
 constexpr int kThreads = 512;
 constexpr int kSplitThreads = 128, kEpiThreads = 256;
@@ -203,6 +204,23 @@ __device__ __forceinline__ void tc_mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem,
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
         "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// The four K-steps of one product of a 32-wide K stage with every operand precomputed, so the issuing
+// thread spends one instruction per MMA (back to back the tensor pipe takes an M = N = 128 MMA about
+// every 64 cycles; per-MMA address or predicate arithmetic in a single issuing thread is slower than
+// that). A from TMEM (columns a .. a + 31), B from the shared-memory descriptor b; ACC0: whether the
+// first MMA adds to D (0 at the start of a chunk).
+template <int ACC0>
+__device__ __forceinline__ void tc_mma_k32_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc) {
+    asm volatile(
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %3, %9, %10;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%2], %4, %9, 1;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%5], %6, %9, 1;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%7], %8, %9, 1;\n\t" ::"r"(d),
+        "r"(a), "r"(a + 8), "l"(b), "l"(b + 2), "r"(a + 16), "l"(b + 4), "r"(a + 24), "l"(b + 6), "r"(idesc),
+        "n"(ACC0)
         : "memory");
 }
 
@@ -469,15 +487,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint64_t wh = sw128_desc(base + kTileBytes), wl = sw128_desc(base + 2 * kTileBytes);
                         const uint32_t xh = tmem + kABase + uint32_t(sa) * kACols, xl = xh + kBK;
                         // the small cross terms first: x_lo w_hi, x_hi w_lo, then x_hi w_hi
-#pragma unroll
-                        for (int kk = 0; kk < kBK / 8; ++kk) {
-                            tc_mma_tf32_ts(d, xl + 8 * kk, wh + 2 * kk, idesc, acc);
-                            acc = 1;
-                        }
-#pragma unroll
-                        for (int kk = 0; kk < kBK / 8; ++kk) tc_mma_tf32_ts(d, xh + 8 * kk, wl + 2 * kk, idesc, 1);
-#pragma unroll
-                        for (int kk = 0; kk < kBK / 8; ++kk) tc_mma_tf32_ts(d, xh + 8 * kk, wh + 2 * kk, idesc, 1);
+                        if (acc)
+                            tc_mma_k32_ts<1>(d, xl, wh, idesc);
+                        else
+                            tc_mma_k32_ts<0>(d, xl, wh, idesc);
+                        acc = 1;
+                        tc_mma_k32_ts<1>(d, xh, wl, idesc);
+                        tc_mma_k32_ts<1>(d, xh, wh, idesc);
                         issued = true;
                         tc_commit(&ctl.empty[s]);     // the stage's shared memory is free once these are done
                         tc_commit(&ctl.a_empty[sa]);  // and so is its A buffer

@@ -822,10 +822,11 @@ __device__ __forceinline__ void radial_out_bwd(const float (*dR)[kMaxPC], const 
 // stage the tile's dR rows (float4, unrolled)
 template <int PC>
 __device__ __forceinline__ void stage_dr(float (*dst)[kMaxPC], const float* __restrict__ dR, int64_t e0, int ne) {
-    constexpr int V = kTB * PC / 4 / 256;  // float4 per thread
+    constexpr int V = (kTB * PC / 4 + 255) / 256;  // float4 per thread (the last round partial)
 #pragma unroll
     for (int r = 0; r < V; ++r) {
         const int idx = threadIdx.x + 256 * r;
+        if (idx >= kTB * PC / 4) break;
         const int e = (idx * 4) / PC, n = (idx * 4) % PC;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (e < ne) v = reinterpret_cast<const float4*>(dR + (e0 + e) * PC)[n / 4];
