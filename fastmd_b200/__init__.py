@@ -4,12 +4,12 @@ Surfaces mirroring the reference: ``ops`` (fastmd.ops), ``graph`` and ``line_gra
 builders, the MatRIS bond pairs and triplets), ``wide_gemm`` and ``decomposed_indexed_cat_silu_linear``
 (fastmd.engine.kernels), ``segment_attention``, ``gated_ln`` and ``pair_aggregate`` (the MatRIS receiver
 attention, GatedMLP epilogue and directed-pair aggregation), ``energy_derivative``
-(fastmd.engine), ``gpu_nhc`` and ``whole_step`` (fastmd.execution / fastmd.interfaces), ``mace`` (the
+(fastmd.engine), ``gpu_nhc``, ``whole_step`` and ``model_graph`` (fastmd.execution / fastmd.interfaces), ``mace`` (the
 MACE-architecture energy tap).
 """
 from fastmd_b200 import (  # noqa: F401
-    _lib, decomposed_indexed_cat_silu_linear, energy_derivative, gated_ln, gpu_nhc, graph, line_graph, mace, ops,
-    pair_aggregate, segment_attention, units, whole_step, wide_gemm)
+    _lib, decomposed_indexed_cat_silu_linear, energy_derivative, gated_ln, gpu_nhc, graph, line_graph, mace,
+    model_graph, ops, pair_aggregate, segment_attention, units, whole_step, wide_gemm)
 
 __all__ = ["decomposed_indexed_cat_silu_linear", "energy_derivative", "gated_ln", "gpu_nhc", "graph", "line_graph",
-           "mace", "ops", "pair_aggregate", "segment_attention", "units", "whole_step", "wide_gemm"]
+           "mace", "model_graph", "ops", "pair_aggregate", "segment_attention", "units", "whole_step", "wide_gemm"]
