@@ -273,6 +273,12 @@ def _ours(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = _cpu_baseline()
+    modes = None
+    if rank == 0 and world == 1 and R == 1 and not args.no_ops:
+        try:
+            modes = _execution_modes(md, model, systems[0], momenta, device)
+        except Exception as error:  # noqa: BLE001 - the line still reports the measured step
+            modes = {"error": f"{type(error).__name__}: {error}"}
     ops = None
     if rank == 0 and world == 1 and not args.no_ops:
         try:
@@ -297,9 +303,40 @@ def _ours(args):
                     f"{S} steps"},
             "gpu_launches": launches_per_window * windows, "launches_per_step": launches_per_window / S,
             "roofline": roofline, "cpu_baseline": cpu, "clocks": clk, "ops_config2": ops,
+            "execution_modes": modes,
             "fallbacks": md.runner.fallbacks, "candidate_refreshes": md.runner.refreshes,
             "final_temperature_K": float(thermo_now["temperature"][0]),
             "final_conserved_eV": float(thermo_now["conserved_energy"][0])}
+
+
+def _execution_modes(md_ws, model, system, momenta, device, steps=200, warmup=20):
+    """ms per MD step of config 1 in the reference's three execution modes (gpu_md.py:104) through the
+    same driver: whole_step (the headline, from the timed windows above: here again over ``steps``),
+    model_graph (a ragged build per step, the model replayed from its bucket's graph) and eager.
+    Host wall clock over ``steps`` steps after ``warmup`` (the two per-step modes synchronise on the
+    host every step, for the ragged build's edge count)."""
+    import torch
+
+    from fastmd_b200 import units
+    from fastmd_b200.whole_step import GPUResidentMolecularDynamics
+
+    pos, cell, numbers, masses = system
+    out = {}
+    for execution in ("whole_step", "model_graph", "eager"):
+        md = md_ws if execution == "whole_step" else GPUResidentMolecularDynamics(
+            model, positions=pos, momenta=momenta, cell=cell, atomic_numbers=numbers, masses=masses,
+            temperature_K=TEMPERATURE, timestep=0.25 * units.fs, tdamp=25 * units.fs, execution=execution,
+            device=device)
+        n = steps - steps % md_ws.runner.steps_per_launch if execution == "whole_step" else steps
+        w = warmup - warmup % md_ws.runner.steps_per_launch if execution == "whole_step" else warmup
+        md.run(max(w, md_ws.runner.steps_per_launch if execution == "whole_step" else 1))
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        md.run(n)
+        torch.cuda.synchronize()
+        out[execution] = round(1e3 * (time.perf_counter() - t0) / n, 4)
+    out["unit"] = "ms/MD-step (host wall clock, 135 atoms)"
+    return out
 
 
 STAGES = {0: ("edge_fwd_kernel", 1), 1: ("message_fused_kernel (per layer)", 2), 2: ("node_fwd_kernel", 1),

@@ -562,7 +562,7 @@ class _FusedBuffers:
                     self.t[f"{L}.pre{k}"] = z(E, c.radial_hidden[0])
                     st.radial_pre[k][L] = ptr(self.t[f"{L}.pre{k}"])
         st.flags = ptr(_lib.flags_word(dev))
-        self.tensor_core_radial = 0 < model.radial_tc_min_edges <= E
+        self.tensor_core_radial = False  # whether the last step took the tensor-core radial path
         self.state = st
         self.energy: dict[int, Tensor] = {}
 
@@ -576,11 +576,15 @@ def _energy_forces_fused(self: "MACEModel", batch, n_systems: int = 1, stages: i
     if getattr(self, "_fused_w", None) is None:
         self._fused_w = _fused_weights(self)
         self._fused_bufs = {}
-    key = (N, E, ptr(batch.element))
+    # buffers per (atoms, edge rows rounded up to 256): a ragged build whose edge count drifts
+    # reuses them (the kernels touch the first E rows only)
+    cap = -(-max(E, 1) // 256) * 256
+    key = (N, cap, ptr(batch.element))
     buf = self._fused_bufs.get(key)
     if buf is None:
-        buf = _FusedBuffers(self, N, E, batch.element)
+        buf = _FusedBuffers(self, N, cap, batch.element)
         self._fused_bufs[key] = buf
+    buf.tensor_core_radial = 0 < self.radial_tc_min_edges <= E
     if n_systems not in buf.energy:
         buf.energy[n_systems] = torch.zeros(n_systems, dtype=torch.float64, device=self.device)
     energy, forces = buf.energy[n_systems], buf.t["forces"]

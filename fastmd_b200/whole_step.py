@@ -14,7 +14,11 @@ the skin (whole_step_cuda_graph.py:579-584).
 
 ``GPUResidentMolecularDynamics`` (fastmd/interfaces/gpu_md.py:98) wires a
 model, a builder and the Nose-Hoover chain together: ``run(steps)``,
-``thermodynamics()`` and the host-buffer step ``step_host``.
+``thermodynamics()`` and the host-buffer step ``step_host``, in the
+reference's three execution modes (gpu_md.py:104): ``whole_step`` (above),
+``model_graph`` (per step: the integrator halves and a ragged neighbour build
+eagerly, the model's energy and forces by replay of its capacity bucket's CUDA
+graph, fastmd_b200/model_graph.py) and ``eager`` (nothing captured).
 """
 from __future__ import annotations
 
@@ -26,10 +30,13 @@ from torch import Tensor
 
 from fastmd_b200.graph import FLAG_CANDIDATE_OVERFLOW, FLAG_EDGE_OVERFLOW, FLAG_NONFINITE, FLAG_SKIN
 _INVALID = FLAG_SKIN | FLAG_CANDIDATE_OVERFLOW | FLAG_NONFINITE | FLAG_EDGE_OVERFLOW
-from fastmd_b200.graph import FixedCapacityGraphBuilder
+from fastmd_b200.graph import FixedCapacityGraphBuilder, TensorGraphBuilder
 from fastmd_b200.gpu_nhc import GPUNoseHooverChainNVT, ReplicaNoseHooverChainNVT, maxwell_boltzmann_momenta
 from fastmd_b200.mace import MACEModel
+from fastmd_b200.model_graph import BucketedGraphRunner
 from fastmd_b200 import units
+
+EXECUTIONS = ("whole_step", "model_graph", "eager")
 
 
 class FixedCapacityOverflow(RuntimeError):
@@ -187,15 +194,22 @@ class WholeStepGraphRunner:
 
 class GPUResidentMolecularDynamics:
     """NVT Nose-Hoover-chain MD of ``replicas`` copies of one periodic system with the
-    MACE-architecture potential, in whole-step CUDA-graph mode (gpu_md.py:98, replica_md.py:224).
+    MACE-architecture potential (gpu_md.py:98, replica_md.py:224).
 
     ``positions`` [R*n, 3] (or [n, 3] for one replica), Angstrom; ``momenta`` likewise
-    (default Maxwell-Boltzmann at ``temperature_K`` with seed 0 per replica)."""
+    (default Maxwell-Boltzmann at ``temperature_K`` with seed 0 per replica). ``execution``:
+    ``"whole_step"`` (windows of ``steps_per_launch`` steps as one CUDA graph), ``"model_graph"``
+    or ``"eager"`` (one system; a ragged build per step)."""
 
     def __init__(self, model: MACEModel, *, positions, cell, atomic_numbers, masses, temperature_K: float,
                  timestep: float, tdamp: float, tchain: int = 3, tloop: int = 1, momenta=None, replicas: int = 1,
                  skin: float = 2.0, u_capacity: int | None = None, steps_per_launch: int = 10,
-                 fused: bool = True, device="cuda") -> None:
+                 fused: bool = True, execution: str = "whole_step", device="cuda") -> None:
+        if execution not in EXECUTIONS:
+            raise ValueError(f"execution must be one of {EXECUTIONS}")
+        if execution != "whole_step" and int(replicas) != 1:
+            raise ValueError(f"execution={execution!r} runs one system; replica ensembles run whole_step")
+        self.execution = execution
         self.device = torch.device(device)
         self.replicas = int(replicas)
         n = len(atomic_numbers)
@@ -219,11 +233,37 @@ class GPUResidentMolecularDynamics:
         else:
             self.integrator = ReplicaNoseHooverChainNVT(masses, positions, momenta, replicas=self.replicas, **kw)
         self.model = model
-        self.runner = WholeStepGraphRunner(model=model, builder=self.builder, integrator=self.integrator,
-                                           steps_per_launch=steps_per_launch, fused=fused)
-        self.runner.on_resize = self._resized
         self.n_atoms = n
         self.steps_done = 0
+        if execution == "whole_step":
+            self.runner = WholeStepGraphRunner(model=model, builder=self.builder, integrator=self.integrator,
+                                               steps_per_launch=steps_per_launch, fused=fused)
+            self.runner.on_resize = self._resized
+            return
+        # model_graph / eager: a ragged build per step (gpu_graph_builder.py:935), F(q0) first
+        self.ragged = TensorGraphBuilder(cell=torch.as_tensor(np.asarray(cell), dtype=torch.float32),
+                                         atomic_numbers=torch.as_tensor(atomic_numbers), atom_graph_cutoff=cutoff,
+                                         device=self.device)
+        self._element = None
+        self.runner = BucketedGraphRunner(model) if execution == "model_graph" else None
+        energy, forces = self._evaluate(self.ragged.build(self.integrator.positions32))
+        self.integrator.set_forces(forces, energy)
+
+    def _evaluate(self, batch):
+        """Energies and forces of a ragged build: replay of its bucket, or the fused kernels eagerly."""
+        if self.runner is not None:
+            return self.runner.run(batch)
+        if self._element is None:  # element rows once (a host conversion), reused every step
+            self.model.prepare(batch)
+            self._element = (batch.element, batch.element64)
+        batch.element, batch.element64 = self._element
+        return self.model.energy_forces_fused(batch)
+
+    def _step(self) -> None:
+        integ = self.integrator
+        integ.step_pre_force()
+        energy, forces = self._evaluate(self.ragged.build(integ.positions32))
+        integ.step_post_force(forces, energy)
 
     def _resized(self, builder) -> None:
         self.builder = builder
@@ -237,7 +277,11 @@ class GPUResidentMolecularDynamics:
         return int(center.shape[0] + 1) // 2
 
     def run(self, steps: int) -> None:
-        self.runner.run(steps)
+        if self.execution == "whole_step":
+            self.runner.run(steps)
+        else:
+            for _ in range(steps):
+                self._step()
         self.steps_done += steps
 
     def thermodynamics(self) -> dict:
@@ -251,6 +295,8 @@ class GPUResidentMolecularDynamics:
     def step_host(self, positions: Tensor, momenta: Tensor, out: dict) -> None:
         """One window from HOST state: upload positions and momenta (pinned), replay, settle, and
         download positions, momenta, forces and energies into the pinned ``out`` buffers."""
+        if self.execution != "whole_step":
+            raise RuntimeError("step_host replays whole-step windows (execution='whole_step')")
         integ = self.integrator
         integ.state.q.copy_(positions, non_blocking=True)
         integ.state.p.copy_(momenta, non_blocking=True)
