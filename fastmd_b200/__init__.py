@@ -4,12 +4,13 @@ Surfaces mirroring the reference: ``ops`` (fastmd.ops), ``graph`` and ``line_gra
 builders, the MatRIS bond pairs and triplets), ``wide_gemm`` and ``decomposed_indexed_cat_silu_linear``
 (fastmd.engine.kernels), ``segment_attention``, ``gated_ln`` and ``pair_aggregate`` (the MatRIS receiver
 attention, GatedMLP epilogue and directed-pair aggregation), ``energy_derivative``
-(fastmd.engine), ``gpu_nhc``, ``whole_step`` and ``model_graph`` (fastmd.execution / fastmd.interfaces), ``mace`` (the
-MACE-architecture energy tap).
+(fastmd.engine), ``gpu_nhc``, ``whole_step``, ``model_graph`` and ``md_protocol`` (fastmd.execution /
+fastmd.interfaces: the execution modes, restart files and extxyz frames), ``mace`` (the MACE-architecture
+energy tap).
 """
 from fastmd_b200 import (  # noqa: F401
     _lib, decomposed_indexed_cat_silu_linear, energy_derivative, gated_ln, gpu_nhc, graph, line_graph, mace,
-    model_graph, ops, pair_aggregate, segment_attention, units, whole_step, wide_gemm)
+    md_protocol, model_graph, ops, pair_aggregate, segment_attention, units, whole_step, wide_gemm)
 
 __all__ = ["decomposed_indexed_cat_silu_linear", "energy_derivative", "gated_ln", "gpu_nhc", "graph", "line_graph",
-           "mace", "model_graph", "ops", "pair_aggregate", "segment_attention", "units", "whole_step", "wide_gemm"]
+           "mace", "md_protocol", "model_graph", "ops", "pair_aggregate", "segment_attention", "units", "whole_step", "wide_gemm"]

@@ -32,7 +32,8 @@ from fastmd_b200.graph import FLAG_CANDIDATE_OVERFLOW, FLAG_EDGE_OVERFLOW, FLAG_
 _INVALID = FLAG_SKIN | FLAG_CANDIDATE_OVERFLOW | FLAG_NONFINITE | FLAG_EDGE_OVERFLOW
 from fastmd_b200.graph import FixedCapacityGraphBuilder, TensorGraphBuilder
 from fastmd_b200.gpu_nhc import GPUNoseHooverChainNVT, ReplicaNoseHooverChainNVT, maxwell_boltzmann_momenta
-from fastmd_b200.mace import MACEModel
+from fastmd_b200.mace import MACEModel, element_index
+from fastmd_b200.md_protocol import ExtxyzTrajectory, RestartData
 from fastmd_b200.model_graph import BucketedGraphRunner
 from fastmd_b200 import units
 
@@ -235,6 +236,8 @@ class GPUResidentMolecularDynamics:
         self.model = model
         self.n_atoms = n
         self.steps_done = 0
+        self.numbers = np.asarray(atomic_numbers, np.int64).reshape(-1)
+        self.cell = np.asarray(cell, np.float64).reshape(3, 3)
         if execution == "whole_step":
             self.runner = WholeStepGraphRunner(model=model, builder=self.builder, integrator=self.integrator,
                                                steps_per_launch=steps_per_launch, fused=fused)
@@ -283,6 +286,53 @@ class GPUResidentMolecularDynamics:
             for _ in range(steps):
                 self._step()
         self.steps_done += steps
+
+    # ------------------------------------------------------------ restart files and frames
+    def restart_data(self, parameters: dict | None = None, offsets: dict | None = None) -> RestartData:
+        """The current state as a restart file's contents (md_protocol.py:123): one system, rows in ID
+        order, the cached forces and energy of the state, the chain, ``engine`` "native"."""
+        if self.replicas != 1:
+            raise ValueError("a restart file holds one system")
+        integ = self.integrator
+        e0 = np.asarray(self.model.weights_host["e0"], np.float64)[element_index(self.numbers)]
+        params = {"ensemble": "nvt_nhc", "tchain": integ.tchain, "tloop": integ.tloop, "timestep": integ.dt,
+                  "tdamp": integ.tdamp, "execution": self.execution, **(parameters or {})}
+        return RestartData(
+            ids=np.arange(self.n_atoms, dtype=np.int64), numbers=self.numbers.copy(),
+            masses=integ.masses.cpu().numpy().astype(np.float64), positions=integ.state.q.cpu().numpy().copy(),
+            momenta=integ.state.p.cpu().numpy().copy(), forces=integ.state.f.cpu().numpy().astype(np.float32),
+            energy=integ.state.energy.cpu().numpy().copy(), reference_energy=np.array([e0.sum()]),
+            cell=self.cell.copy(), pbc=np.ones(3, bool), step=int(self.steps_done), parameters=params,
+            temperature_K=float(integ.temperature_K), nhc_state=integ.state_dict(), offsets=dict(offsets or {}),
+            engine="native")
+
+    def load_restart(self, data: RestartData) -> None:
+        """Continue from a restart file's state: positions, momenta, the cached forces and energy (not
+        re-evaluated), the chain and the step count; the candidates are rebuilt at the positions."""
+        if self.replicas != 1 or len(data.numbers) != self.n_atoms or not np.array_equal(
+                np.asarray(data.numbers)[np.argsort(data.ids)], self.numbers):
+            raise ValueError("the restart file holds another system")
+        order = np.argsort(np.asarray(data.ids))
+        integ = self.integrator
+        integ.set_state(positions=np.asarray(data.positions, np.float64)[order],
+                        momenta=np.asarray(data.momenta, np.float64)[order],
+                        forces=np.asarray(data.forces, np.float64)[order],
+                        potential_energy=np.asarray(data.energy, np.float64).reshape(-1))
+        if data.nhc_state is not None:
+            integ.load_state_dict(data.nhc_state)
+        self.steps_done = int(data.step)
+        if self.execution == "whole_step":
+            self.builder.refresh_candidates(integ.positions32)
+
+    def write_frame(self, trajectory: ExtxyzTrajectory, info: dict | None = None) -> None:
+        """The current state as one extxyz frame (velocities = momenta / masses, the cached forces)."""
+        if self.replicas != 1:
+            raise ValueError("a frame holds one system")
+        integ = self.integrator
+        p, m = integ.state.p.cpu().numpy(), integ.masses.cpu().numpy()
+        trajectory.write(numbers=self.numbers, positions=integ.state.q.cpu().numpy(), cell=self.cell,
+                         pbc=np.ones(3, bool), velocities=p / m[:, None], forces=integ.state.f.cpu().numpy(),
+                         energy=float(integ.state.energy[0]), info={"step": self.steps_done, **(info or {})})
 
     def thermodynamics(self) -> dict:
         """Per-replica potential, kinetic and conserved energy (eV) and temperature (K)."""

@@ -102,3 +102,30 @@ def test_execution_modes_give_one_trajectory(cuda):
     assert runs["model_graph"].runner.stats()["captures"] >= 1
     with pytest.raises(RuntimeError):
         runs["eager"].step_host(None, None, {})
+
+
+@pytest.mark.parametrize("execution", ["whole_step", "model_graph"])
+def test_restart_continues_the_trajectory_bitwise(cuda, tmp_path, execution):
+    """10 steps, a restart file, 10 more steps; a fresh driver loaded from the file runs the same 10 steps
+    to the same state bit for bit (the cached forces are not re-evaluated); frames read back."""
+    from fastmd_b200.md_protocol import ExtxyzTrajectory, read_extxyz, read_restart, write_restart
+
+    a = _md(cuda, execution=execution)
+    a.run(10)
+    write_restart(tmp_path / "r.npz", a.restart_data(parameters={"note": "test"}))
+    traj = ExtxyzTrajectory(tmp_path / "t.extxyz")
+    a.write_frame(traj)
+    a.run(10)
+    a.write_frame(traj)
+    traj.close()
+    data = read_restart(tmp_path / "r.npz")
+    assert data.step == 10 and data.engine == "native" and data.parameters["note"] == "test"
+    b = _md(cuda, execution=execution, seeds=(5,))  # another start, overwritten by the file
+    b.load_restart(data)
+    b.run(10)
+    assert b.steps_done == 20
+    assert torch.equal(a.integrator.state.flat, b.integrator.state.flat)
+    frames = read_extxyz(tmp_path / "t.extxyz")
+    assert [f["step"] for f in frames] == [10, 20]
+    q = a.integrator.state.q.cpu().numpy()
+    assert np.abs(frames[1]["positions"] - q).max() < 1e-7
