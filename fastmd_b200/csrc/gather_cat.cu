@@ -77,24 +77,31 @@ __global__ void __launch_bounds__(kCatThreads) gather_cat_kernel(CatParams p) {
             s_index[part][r] = idx;
         }
         __syncthreads();
-        const int total = rows_here * p.row_vecs;
-        for (int t = threadIdx.x; t < total; t += blockDim.x) {
-            const int r = t / p.row_vecs;
-            const int v = t - r * p.row_vecs;
+        // the flat vector walk t = r * row_vecs + v, stepped without a division per vector
+        const int step_r = kCatThreads / p.row_vecs, step_v = kCatThreads - step_r * p.row_vecs;
+        int r = threadIdx.x / p.row_vecs, v = threadIdx.x - r * p.row_vecs;
+        for (; r < rows_here; r += step_r, v += step_v) {
+            if (v >= p.row_vecs) {
+                v -= p.row_vecs;
+                ++r;
+                if (r >= rows_here) break;
+            }
             int part = 0;
 #pragma unroll
             for (int k = 1; k < kMaxParts; ++k) part += (k < p.n_parts && v >= p.start[k]) ? 1 : 0;
             const int col = (v - p.start[part]) * VEC;
             const int64_t src_row = s_index[part][r];
             float* dst = p.out + (row0 + r) * p.ldo + int64_t(v) * VEC;
+            // the output is written once and not read back here: evict-first stores keep the
+            // gathered node tables in L2
             if constexpr (VEC == 4) {
                 float4 val = f4_zero();
                 if (src_row >= 0) val = ldg4(p.src[part] + src_row * p.ld[part] + col);
-                st4(dst, val);
+                __stcs(reinterpret_cast<float4*>(dst), val);
             } else {
                 float val = 0.f;
                 if (src_row >= 0) val = __ldg(p.src[part] + src_row * p.ld[part] + col);
-                *dst = val;
+                __stcs(dst, val);
             }
         }
     }
