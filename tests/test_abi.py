@@ -59,7 +59,9 @@ def test_invalid_arguments_are_rejected_before_any_launch():
                                   None, None, None, None) == 1  # neither force dtype
     p16 = ctypes.c_void_p(1 << 20)
     assert lib.fmd_gemm_tf32x3(None, 8, p16, p16, 8, None, None, 0, p16, 8, 1, 8, 8, 0, 0, None, None) == 1
-    assert lib.fmd_gemm_tf32x3(p16, 8, p16, p16, 8, None, None, 0, p16, 8, 1, 8, 8, 2, 0, None, None) == 1  # act
+    assert lib.fmd_gemm_tf32x3(p16, 8, p16, p16, 8, None, None, 0, p16, 8, 1, 8, 8, 2, 0, None, None) == 1  # gate: c
+    assert lib.fmd_gemm_tf32x3(p16, 8, p16, p16, 8, None, None, 0, p16, 8, 1, 8, 8, 3, 0, None, None) == 1  # act
+    assert lib.fmd_gemm_tf32x3(p16, 8, p16, p16, 8, None, None, 0, p16, 8, 1, 8, 8, 32, 0, None, None) == 1
     # TMA operands: unaligned base or a row stride that is not a multiple of 16 bytes -> unsupported
     assert lib.fmd_gemm_tf32x3(ctypes.c_void_p((1 << 20) + 4), 8, p16, p16, 8, None, None, 0, p16, 8, 1, 8, 8, 0, 0,
                                None, None) == 3

@@ -152,3 +152,45 @@ def test_large_rows_sampled():
     base = torch.randn(1000, k + 1, device="cuda", generator=g)
     view = base[:, 1:]
     _check(wide_gemm.linear(view, wd, bd), view.cpu().contiguous(), wd.cpu(), bd.cpu())
+
+
+@pytest.mark.parametrize("m,n,k", [(1000, 64, 64), (333, 256, 264), (77, 5, 3)])
+def test_input_silu_and_silu_grad_modes(m, n, k):
+    """FMD_ACT_INPUT_SILU (the operand enters as silu(x)) and FMD_ACT_SILU_GRAD (y = (x w^T + b) silu'(c),
+    in place over c) against the oracle: the layers of an MLP chained on pre-activations and their
+    backward. silu and silu' run on the hardware exp2 / divide: a few ulp of the operand or the gate."""
+    from fastmd_b200 import _lib, wide_gemm
+    from fastmd_b200._lib import call, ptr
+
+    x, w, b = _data(m, n, k, seed=m + 3 * n + k)
+    ldx = (k + 3) // 4 * 4  # TMA: a row stride of whole 16-byte units
+    xd = torch.zeros(m, ldx, device="cuda")
+    xd[:, :k] = x.cuda()
+    wd, bd = w.cuda(), b.cuda()
+    sp = wide_gemm._split(wd, False)
+    ldw = sp.hi.stride(0)
+    s = _lib.stream()
+    # input SiLU, SiLU output as well: y = silu(silu(x) w^T + b)
+    y = torch.empty(m, n, device="cuda")
+    call("fmd_gemm_tf32x3", ptr(xd), ldx, ptr(sp.hi), ptr(sp.lo), ldw, ptr(bd), None, 0, ptr(y), n, m, n, k, 1 | 16,
+         0, None, s)
+    sx = torch.nn.functional.silu(x.double()).float()
+    _check(y, sx, w, b, act=1, tol=2e-5)
+    # silu' gate, in place over the pre-activation c
+    c = torch.randn(m, n, generator=torch.Generator().manual_seed(99)) * 3
+    cd = c.cuda()
+    call("fmd_gemm_tf32x3", ptr(xd), ldx, ptr(sp.hi), ptr(sp.lo), ldw, ptr(bd), ptr(cd), n, ptr(cd), n, m, n, k, 2,
+         0, None, s)
+    torch.cuda.synchronize()
+    sig = torch.sigmoid(c.double())
+    gate = (sig * (1 + c.double() * (1 - sig))).numpy()
+    acc = ow.gemm_3xtf32(x.numpy(), w.numpy(), b.numpy())
+    # the product's error scaled by the gate, plus the gate's own absolute error (hardware exp2 and
+    # divide: s to a few ulp, then 1 - s and c (1 - s) for |c| <= 12: below 1e-5)
+    bound = TOL * ow.error_scale(x.numpy(), w.numpy(), b.numpy()) * np.abs(gate) + 1e-5 * np.abs(acc) + 1e-12
+    err = np.abs(cd.cpu().double().numpy() - acc * gate) / bound
+    assert err.max() < 1.0, err.max()
+    # mode 2 without c is an argument error
+    lib = _lib.lib()
+    assert lib.fmd_gemm_tf32x3(ptr(xd), ldx, ptr(sp.hi), ptr(sp.lo), ldw, None, None, 0, ptr(y), n, m, n, k, 2, 0,
+                               None, s) == 1
