@@ -143,7 +143,6 @@ __global__ void cell_scatter_kernel(int64_t total, const float4* __restrict__ wr
 
 constexpr int kQueryWarps = 8;
 constexpr int kStageCap = 1024;   // staged (atom, image) entries per chunk
-constexpr int kMaxOffsets = 1331; // (2s+1)^3 neighbour (cell, image) pairs, s <= 5
 constexpr int kMaxHome = 512;     // home atoms handled per pass over the neighbourhood
 
 struct QueryArgs {
@@ -157,6 +156,7 @@ struct QueryArgs {
     float cutoff;                // candidate cutoff (dist2 < cutoff^2, FP32)
     int32_t bmax;                // slots per atom in the output matrix
     int32_t list_cap;            // per-warp sort buffer (shared memory), >= bmax
+    int32_t off_cap;             // (cell, image) offsets the shared memory holds: (2s0+1)(2s1+1)(2s2+1)
     int32_t* nbr_out;            // [R*n, bmax] global neighbour rows
     int32_t* shift_out;          // [R*n, bmax, 3]
     int32_t* count_out;          // [R*n] true candidate count
@@ -167,37 +167,39 @@ struct QuerySmem {
     float4* pos;       // [kStageCap] staged positions, shifted by their image
     int32_t* atom;     // [kStageCap]
     int32_t* img;      // [kStageCap] packed image
-    int32_t* o_begin;  // [kMaxOffsets] first atom of the offset's cell
-    int32_t* o_pref;   // [kMaxOffsets + 1] exclusive prefix of the offsets' atom counts
-    int32_t* o_img;    // [kMaxOffsets]
-    float* o_shift;    // [kMaxOffsets * 3]
+    int32_t* o_begin;  // [off_cap] first atom of the offset's cell
+    int32_t* o_pref;   // [off_cap + 1] exclusive prefix of the offsets' atom counts
+    int32_t* o_img;    // [off_cap]
+    float* o_shift;    // [off_cap * 3]
     int32_t* hits;     // [kMaxHome]
     uint64_t* list;    // [kQueryWarps * list_cap]
 };
 
-inline size_t query_smem(int list_cap) {
-    return sizeof(float4) * kStageCap + 2 * sizeof(int32_t) * kStageCap + sizeof(int32_t) * kMaxOffsets * 3 +
-           sizeof(int32_t) * (kMaxOffsets + 1) + sizeof(float) * kMaxOffsets * 3 + sizeof(int32_t) * kMaxHome +
+// Shared memory of a query CTA for off_cap offsets (sized to the grid's search reach, not to the
+// largest one: the 27 offsets of a reach of one cell leave room for twice the resident CTAs).
+inline size_t query_smem(int list_cap, int off_cap) {
+    return sizeof(float4) * kStageCap + 2 * sizeof(int32_t) * kStageCap + sizeof(int32_t) * off_cap * 3 +
+           sizeof(int32_t) * (off_cap + 1) + sizeof(float) * off_cap * 3 + sizeof(int32_t) * kMaxHome +
            sizeof(uint64_t) * size_t(kQueryWarps) * list_cap + 64;
 }
 
-__device__ QuerySmem carve_query_smem(unsigned char* raw, int list_cap) {
+__device__ QuerySmem carve_query_smem(unsigned char* raw, int list_cap, int off_cap) {
     QuerySmem m;
     m.pos = reinterpret_cast<float4*>(raw);
     m.list = reinterpret_cast<uint64_t*>(m.pos + kStageCap);
     m.atom = reinterpret_cast<int32_t*>(m.list + size_t(kQueryWarps) * list_cap);
     m.img = m.atom + kStageCap;
     m.o_begin = m.img + kStageCap;
-    m.o_pref = m.o_begin + kMaxOffsets;
-    m.o_img = m.o_pref + kMaxOffsets + 1;
-    m.hits = m.o_img + kMaxOffsets;
+    m.o_pref = m.o_begin + off_cap;
+    m.o_img = m.o_pref + off_cap + 1;
+    m.hits = m.o_img + off_cap;
     m.o_shift = reinterpret_cast<float*>(m.hits + kMaxHome);
     return m;
 }
 
 __global__ void __launch_bounds__(kQueryWarps * 32) cell_query_kernel(QueryArgs q) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    const QuerySmem m = carve_query_smem(smem_raw, q.list_cap);
+    const QuerySmem m = carve_query_smem(smem_raw, q.list_cap, q.off_cap);
     __shared__ int s_scan[32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ncells = q.grid.ncells;
@@ -258,6 +260,71 @@ __global__ void __launch_bounds__(kQueryWarps * 32) cell_query_kernel(QueryArgs 
         }
         if (threadIdx.x == 0) m.o_pref[n_off] = running;
         const int staged_total = running;
+        // One staging pass holds the whole neighbourhood (the common case): each warp collects a home
+        // atom's hit keys in its shared-memory list, ranks them there and writes each slot once.
+        if (staged_total <= kStageCap && q.bmax <= q.list_cap) {
+            const int ns = staged_total;
+            __syncthreads();
+            for (int t = threadIdx.x; t < ns; t += blockDim.x) {
+                int lo = 0, hi = n_off;  // last offset with o_pref[o] <= t
+                while (hi - lo > 1) {
+                    const int mid = (lo + hi) >> 1;
+                    if (m.o_pref[mid] <= t) lo = mid; else hi = mid;
+                }
+                const int src = m.o_begin[lo] + (t - m.o_pref[lo]);
+                const float4 p = q.cell_pos[src];
+                m.pos[t] = make_float4(p.x + m.o_shift[3 * lo], p.y + m.o_shift[3 * lo + 1],
+                                       p.z + m.o_shift[3 * lo + 2], 0.f);
+                m.atom[t] = q.cell_atoms[src];
+                m.img[t] = m.o_img[lo];
+            }
+            __syncthreads();
+            uint64_t* list = m.list + size_t(warp) * q.list_cap;
+            for (int h = warp; h < h_end - h_begin; h += kQueryWarps) {
+                const float4 hp = q.cell_pos[h_begin + h];
+                const int32_t ha = q.cell_atoms[h_begin + h];
+                const int64_t row = ha;
+                int hits = 0;
+                for (int base = 0; base < ns; base += 32) {
+                    const int k = base + lane;
+                    bool hit = false;
+                    int32_t atom = 0;
+                    int packed = 0;
+                    if (k < ns) {
+                        const float4 p = m.pos[k];
+                        const float dx = p.x - hp.x, dy = p.y - hp.y, dz = p.z - hp.z;
+                        const float d2 = (dx * dx + dy * dy) + dz * dz;
+                        atom = m.atom[k];
+                        packed = m.img[k];
+                        hit = d2 < cut2 && !(atom == ha && packed == zero_img);
+                    }
+                    const unsigned mask = __ballot_sync(0xffffffffu, hit);
+                    if (hit) {  // the first bmax hits in discovery order, as the two-pass path keeps them
+                        const int pos = hits + __popc(mask & ((1u << lane) - 1u));
+                        if (pos < q.bmax) list[pos] = (uint64_t(uint32_t(atom - sys_base)) << 30) | uint32_t(packed);
+                    }
+                    hits += __popc(mask);
+                }
+                __syncwarp();
+                const int k_list = min(hits, q.bmax);
+                for (int e = lane; e < k_list; e += 32) {
+                    const uint64_t key = list[e];
+                    int rank = 0;
+                    for (int f = 0; f < k_list; ++f) rank += list[f] < key ? 1 : 0;
+                    const int64_t slot = row * q.bmax + rank;
+                    q.nbr_out[slot] = sys_base + int32_t(key >> 30);
+                    q.shift_out[3 * slot] = int32_t((key >> 20) & 1023u) - 512;
+                    q.shift_out[3 * slot + 1] = int32_t((key >> 10) & 1023u) - 512;
+                    q.shift_out[3 * slot + 2] = int32_t(key & 1023u) - 512;
+                }
+                if (lane == 0) {
+                    q.count_out[row] = hits;
+                    if (hits > q.bmax) raise_flag(q.flags, FMD_FLAG_CANDIDATE_OVERFLOW);
+                }
+                __syncwarp();
+            }
+            continue;
+        }
         for (int hb = h_begin; hb < h_end; hb += kMaxHome) {
             const int n_home = min(kMaxHome, h_end - hb);
             for (int h = threadIdx.x; h < n_home; h += blockDim.x) m.hits[h] = 0;
@@ -813,7 +880,7 @@ inline bool make_grid(const float* cell_host, double cutoff, Grid& g) {
         if (n > 256) n = 256;
         g.n[k] = n;
         g.s[k] = int(ceil(cutoff * n / h * (1.0 + 1e-6)));
-        if (g.s[k] > 5) return false;  // (2s+1)^3 <= kMaxOffsets neighbour (cell, image) pairs
+        if (g.s[k] > 5) return false;  // at most (2 * 5 + 1)^3 neighbour (cell, image) pairs
         total *= n;
     }
     g.ncells = int(total);
@@ -882,7 +949,8 @@ inline int list_cap_for(int32_t bmax) { return bmax < 32 ? 32 : (bmax > 1024 ? 1
 // bin + scan + scatter + query into a candidate matrix
 inline fmd_status run_cell_list(const float* positions, int64_t n_atoms, int32_t n_systems, const Cell9& cell,
                                 const Grid& grid, float cutoff, int32_t bmax, int32_t* nbr, int32_t* shift,
-                                int32_t* count, const CellWorkspace& w, int32_t* flags, cudaStream_t s) {
+                                int32_t* count, const CellWorkspace& w, int32_t* flags, cudaStream_t s,
+                                bool fill_unused = true) {
     const int64_t atoms = n_atoms * n_systems;
     const int64_t cells = int64_t(grid.ncells) * n_systems;
     cudaError_t err = cudaMemsetAsync(w.cell_count, 0, sizeof(int32_t) * (cells + 1), s);
@@ -910,16 +978,18 @@ inline fmd_status run_cell_list(const float* positions, int64_t n_atoms, int32_t
     q.cutoff = cutoff;
     q.bmax = bmax;
     q.list_cap = list_cap_for(bmax);
+    q.off_cap = (2 * grid.s[0] + 1) * (2 * grid.s[1] + 1) * (2 * grid.s[2] + 1);
     q.nbr_out = nbr;
     q.shift_out = shift;
     q.count_out = count;
     q.flags = flags;
-    const size_t smem = query_smem(q.list_cap);
+    const size_t smem = query_smem(q.list_cap, q.off_cap);
     if (smem > 227 * 1024) return FMD_ERR_UNSUPPORTED;
     if ((st = allow_smem(reinterpret_cast<const void*>(cell_query_kernel), smem, g_query_smem)) != FMD_OK) return st;
     const int qgrid = int(cells < int64_t(kNumSMs) * 16 ? cells : int64_t(kNumSMs) * 16);
     cell_query_kernel<<<qgrid, kQueryWarps * 32, smem, s>>>(q);
     if ((st = check_launch()) != FMD_OK) return st;
+    if (!fill_unused) return FMD_OK;  // a consumer that reads only the first count slots of a row
     cand_fill_kernel<<<grid_for(atoms * bmax, threads), threads, 0, s>>>(atoms, bmax, int32_t(atoms), nbr, shift,
                                                                          count);
     return check_launch();
@@ -1134,8 +1204,9 @@ fmd_status fmd_neighbor_list(const float* positions, const float* cell_host, int
     int64_t* counts64 = reinterpret_cast<int64_t*>(p); p += align_up(sizeof(int64_t) * (n_atoms + 1));
     void* cub_temp = p;
     size_t cub_bytes = ragged_scan_bytes(n_atoms);
+    // the ragged kernels read only the first count slots of a candidate row: no fill of the rest
     fmd_status st = run_cell_list(positions, n_atoms, 1, cell, grid, cand_cut, bmax, nbr, shift, count, w,
-                                  flags, s);
+                                  flags, s, false);
     if (st != FMD_OK) return st;
     const int threads = 256;
     ragged_count_kernel<<<grid_for(n_atoms * 32, threads), threads, 0, s>>>(w.wrapped, n_atoms, cell, nbr, shift,
