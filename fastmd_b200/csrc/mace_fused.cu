@@ -1211,9 +1211,11 @@ fmd_status fmd_mace_fused_step(const fmd_mace_fused_weights* weights, const fmd_
                                const int64_t* send_off, const int32_t* send_perm, int64_t atoms_per_system,
                                int32_t n_systems, int32_t channels, float* forces, double* energy, int32_t stages,
                                void* stream) {
-    if (weights == nullptr || state == nullptr || positions == nullptr || cell == nullptr || edge_index == nullptr ||
-        edge_image == nullptr || recv_off == nullptr || send_off == nullptr || send_perm == nullptr ||
-        forces == nullptr || energy == nullptr || n_edges < 0 || atoms_per_system < 1 || n_systems < 1)
+    // the edge arrays may be NULL (empty tensors) when there are no edge rows: nothing reads them then
+    if (weights == nullptr || state == nullptr || positions == nullptr || cell == nullptr ||
+        (n_edges > 0 && (edge_index == nullptr || edge_image == nullptr || send_perm == nullptr)) ||
+        recv_off == nullptr || send_off == nullptr || forces == nullptr || energy == nullptr || n_edges < 0 ||
+        atoms_per_system < 1 || n_systems < 1)
         return FMD_ERR_INVALID_ARGUMENT;
     FusedWeights w{};
     FusedState st{};

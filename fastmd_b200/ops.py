@@ -203,8 +203,11 @@ class _CsrSegmentSum(Function):
         ldw = 0
         if weight is not None:
             weight, ldw = _rows_view(weight)
-        out = torch.empty((num_segment, dim), device=value.device, dtype=value.dtype)
-        if num_segment > 0 and dim > 0:
+        if n_rows == 0:  # no rows: every segment sums to zero (nothing to read, nothing to launch)
+            out = torch.zeros((num_segment, dim), device=value.device, dtype=value.dtype)
+        else:
+            out = torch.empty((num_segment, dim), device=value.device, dtype=value.dtype)
+        if n_rows > 0 and num_segment > 0 and dim > 0:
             call("fmd_csr_segment_sum", ptr(value), ldv, ptr(weight), ldw,
                  None if identity_perm else ptr(perm), ptr(off), num_segment, dim, skip_segment, ptr(out),
                  dim, stream(value.device))

@@ -655,6 +655,7 @@ typedef struct fmd_mace_fused_state {
  * updates, the explicit backward and the force assembly
  * F_a = sum_{received e} dE/dr_e - sum_{sent e} dE/dr_e over both CSRs.
  * forces [N][3] float32, energy [n_systems] fp64 (deterministic sums).
+ * edge_index / edge_image / send_perm may be NULL when n_edges is 0.
  * n_real_edges (device int64, may be NULL): the count of real rows; the
  * padding rows after it are skipped by the edge kernels. stages: -1 for the
  * whole step, else a bit mask of the kernels to launch (bit 0 edge forward,
