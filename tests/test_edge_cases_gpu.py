@@ -62,3 +62,30 @@ def test_segment_sum_with_no_rows_and_empty_segments(cuda):
     out = csr_segment_sum(v, seg, 6)
     assert torch.count_nonzero(out[1]) == 0 and torch.count_nonzero(out[2]) == 0 and torch.count_nonzero(out[5]) == 0
     torch.testing.assert_close(out[3], v[2:5].sum(0), rtol=1e-6, atol=1e-6)
+
+
+def test_zero_row_inputs_of_the_op_surface(cuda):
+    """Every op of the surface takes inputs without rows (an empty graph's edges, a system without bonds)
+    and returns the reference's empty results: zeros / -inf lse for the segments, empty rows elsewhere."""
+    from fastmd_b200 import gated_ln, line_graph, segment_attention, wide_gemm
+    from fastmd_b200.decomposed_indexed_cat_silu_linear import decomposed_indexed_cat3_silu_linear
+
+    D = 16
+    z = torch.zeros(0, D, device=cuda)
+    seg = torch.zeros(0, dtype=torch.int64, device=cuda)
+    out, lse = segment_attention.segment_attention(z, z, seg, 4, return_lse=True)
+    assert out.shape == (4, D) and torch.count_nonzero(out) == 0 and torch.isneginf(lse).all()
+    pa = segment_attention.paired_segment_attention(z, z, z, seg, seg, 3)
+    assert all(t.shape == (3, D) and torch.count_nonzero(t) == 0 for t in pa[:2])
+    w = torch.ones(D, device=cuda)
+    assert gated_ln.fused_gated_ln(z, z, w, w * 0, w, w * 0).shape == (0, D)
+    W = torch.randn(32, D, device=cuda)
+    assert wide_gemm.linear(z, W).shape == (0, 32)
+    gathered = torch.randn(5, D, device=cuda)
+    ws = tuple(torch.randn(8, D, device=cuda) for _ in range(3))
+    core, gate = decomposed_indexed_cat3_silu_linear(z, gathered, seg, seg, ws)
+    assert core.shape == (0, 4) and gate.shape == (0, 4)
+    d2u, u2d = line_graph.build_d2u(seg, seg, torch.zeros(0, 3, dtype=torch.int32, device=cuda), 5)
+    assert d2u.shape == (0,) and u2d.shape == (0,)
+    trip = line_graph.build_line_graph(seg, d2u, torch.zeros(0, device=cuda), 5, 4.5)
+    assert trip.shape == (0, 5)
