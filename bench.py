@@ -52,9 +52,10 @@ def _args():
     p.add_argument("--steps-per-launch", type=int, default=10)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-ops", action="store_true", help="skip the config-2 op microbenchmark")
-    p.add_argument("--op", choices=["wide_gemm"], default=None,
+    p.add_argument("--op", choices=["wide_gemm", "hbm_ops"], default=None,
                    help="time one op alone (the profiling entry of profiles/): prints its own JSON line")
-    p.add_argument("--rows", type=int, default=300_000, help="rows of --op")
+    p.add_argument("--rows", type=int, default=300_000, help="rows of --op wide_gemm")
+    p.add_argument("--atoms", type=int, default=25_000, help="atoms of --op hbm_ops (config 2's box density)")
     return p.parse_args()
 
 
@@ -592,10 +593,57 @@ def _cpu_baseline():
                       f"MACE-arch forces with autograd, NHC) on {threads} threads"}
 
 
+def _op_hbm(args):
+    """``--op hbm_ops``: config 2's HBM-bound ops on a box of ``--atoms`` atoms at its density (rc 6 A):
+    gather-cat (neighbour 128 | centre 128 | basis 8), the CSR segment sum of [E x 256] and the segment
+    attention of [E x 128], 3 warm-up calls then 5 timed (CUDA events each)."""
+    import torch
+
+    from fastmd_b200.graph import neighbor_list
+    from fastmd_b200.ops import csr_segment_sum, gather_cat, segment_csr
+    from fastmd_b200.segment_attention import segment_attention
+    from fastmd_b200.structures import random_box
+
+    dev = torch.device("cuda", 0)
+    n = args.atoms
+    pos_np, cell_np, _ = random_box(n, density=0.06, seed=2)
+    center, neighbor, _, _ = neighbor_list(torch.from_numpy(pos_np).float().to(dev), torch.from_numpy(cell_np).float(),
+                                           6.0)
+    E = int(center.shape[0])
+    g = torch.Generator(device=dev).manual_seed(0)
+    h = torch.randn(n, 128, device=dev, generator=g)
+    rbf = torch.randn(E, 8, device=dev, generator=g)
+    v = torch.randn(E, 256, device=dev, generator=g)
+    logits = torch.randn(E, 128, device=dev, generator=g)
+    val = torch.randn(E, 128, device=dev, generator=g)
+    perm, off = segment_csr(center, n)
+    ops = {"gather_cat_264": lambda: gather_cat([(h, neighbor), (h, center), (rbf, None)]),
+           "segment_sum_256": lambda: csr_segment_sum(v, center, n, perm, off),
+           "segment_attention_128": lambda: segment_attention(logits, val, center, n, perm, off)}
+    out = {"op": "hbm_ops", "atoms": n, "edges": E}
+    for name, fn in ops.items():
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(5):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            times.append(a.elapsed_time(b))
+        out[name + "_ms"] = round(statistics.median(times), 4)
+    return out
+
+
 def _op(args):
     """One op alone on cuda:0, the profiling entry: ``--op wide_gemm`` runs the config-2 first edge
     layer (264 -> 256, bias, SiLU, 3xTF32 on tcgen05) over ``--rows`` rows, 3 warm-up launches then
-    10 timed ones (CUDA events; the input is larger than L2 from 120,000 rows on)."""
+    10 timed ones (CUDA events; the input is larger than L2 from 120,000 rows on); ``--op hbm_ops``
+    the HBM-bound ops (``_op_hbm``)."""
+    if args.op == "hbm_ops":
+        return _op_hbm(args)
     import torch
 
     from fastmd_b200 import wide_gemm
