@@ -33,9 +33,13 @@
 
 #include <mutex>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace fmd {
+
+namespace cg = cooperative_groups;
 
 // ------------------------------------------------------------------ geometry
 
@@ -526,19 +530,42 @@ __device__ __forceinline__ int block_scan_exclusive(int v, int* smem, int& total
     return before + x - v;
 }
 
-// Count kernel: one CTA per system.
-__global__ void __launch_bounds__(kRefThreads) refilter_count_kernel(RefilterArgs a) {
+// Both re-filter kernels run a thread-block cluster of kRefCluster CTAs per system (grid n_systems *
+// kRefCluster): CTA `rank` of a system owns the centre slice [rank * per, rank * per + per); the
+// per-system steps (the displacement maximum, the offsets of the count scan, the sender CSR) go
+// through cluster barriers (release / acquire at cluster scope) and the distributed shared memory of
+// the cluster. A 135-atom system so spreads over 8 SMs instead of one. Every CTA of a cluster takes
+// every barrier (no early exit), and the last barrier keeps each CTA's shared memory alive while the
+// others may still read it.
+constexpr int kRefCluster = 8;
+
+__device__ __forceinline__ void slice_of(int n, int rank, int& lo, int& hi) {
+    const int per = (n + kRefCluster - 1) / kRefCluster;
+    lo = min(n, rank * per);
+    hi = min(n, lo + per);
+}
+
+// Count kernel: wrap, displacement and skin test, edges per centre, per-system offsets.
+__global__ void __cluster_dims__(kRefCluster, 1, 1) __launch_bounds__(kRefThreads)
+    refilter_count_kernel(RefilterArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    float3* s_w = reinterpret_cast<float3*>(smem_raw);                    // wrapped [n]
+    float3* s_w = reinterpret_cast<float3*>(smem_raw);                    // wrapped [n] (the whole system)
     int3* s_wd = reinterpret_cast<int3*>(s_w + a.n_atoms);                // wrap delta [n]
     __shared__ int s_scan[32];
     __shared__ float s_max[32];
-    const int64_t sys = blockIdx.x;
+    __shared__ float s_cmax;   // this CTA's largest displacement (read by rank 0)
+    __shared__ int s_total;    // this CTA's edge count (read by the higher ranks)
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = int(cluster.block_rank());
+    const int64_t sys = blockIdx.x / kRefCluster;
     const int64_t base = sys * a.n_atoms;
     const int n = int(a.n_atoms);
+    int lo, hi;
+    slice_of(n, rank, lo, hi);
+    // wrap this CTA's slice
     float my_max = 0.f;
     bool nonfinite = false;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
         const int64_t g = base + i;
         float3 p = ld3(a.positions, g), w, f;
         int3 wr;
@@ -558,8 +585,6 @@ __global__ void __launch_bounds__(kRefThreads) refilter_count_kernel(RefilterArg
             dz -= lj.z;
             wd = make_int3(wd.x - int(jx), wd.y - int(jy), wd.z - int(jz));
         }
-        s_w[i] = w;
-        s_wd[i] = wd;
         a.wrapped[3 * g] = w.x;
         a.wrapped[3 * g + 1] = w.y;
         a.wrapped[3 * g + 2] = w.z;
@@ -570,7 +595,7 @@ __global__ void __launch_bounds__(kRefThreads) refilter_count_kernel(RefilterArg
         if (!(d == d) || !isfinite(p.x) || !isfinite(p.y) || !isfinite(p.z)) nonfinite = true;
         my_max = fmaxf(my_max, d);
     }
-    // block max of the displacement (NaN-safe: nonfinite is flagged separately)
+    // CTA max of the displacement (NaN-safe: nonfinite is flagged separately)
     for (int m = 16; m > 0; m >>= 1) my_max = fmaxf(my_max, __shfl_xor_sync(0xffffffffu, my_max, m));
     if ((threadIdx.x & 31) == 0) s_max[threadIdx.x >> 5] = my_max;
     if (nonfinite) raise_flag(a.flags, FMD_FLAG_NONFINITE);
@@ -578,12 +603,25 @@ __global__ void __launch_bounds__(kRefThreads) refilter_count_kernel(RefilterArg
     if (threadIdx.x == 0) {
         float m = 0.f;
         for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, s_max[w]);
+        s_cmax = m;
+    }
+    cluster.sync();  // every slice wrapped: the whole system's rows are visible
+    if (rank == 0 && threadIdx.x == 0) {
+        float m = 0.f;
+        for (int r = 0; r < kRefCluster; ++r) m = fmaxf(m, *cluster.map_shared_rank(&s_cmax, r));
         a.max_disp[sys] = m;
         if (!(m * 2.0f <= a.skin_limit)) raise_flag(a.flags, FMD_FLAG_SKIN);
     }
-    // counts: one warp per centre
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {  // the system's rows, written by the whole cluster
+        const int64_t g = base + i;
+        s_w[i] = make_float3(__ldcg(a.wrapped + 3 * g), __ldcg(a.wrapped + 3 * g + 1), __ldcg(a.wrapped + 3 * g + 2));
+        s_wd[i] = make_int3(__ldcg(a.wrap_delta + 3 * g), __ldcg(a.wrap_delta + 3 * g + 1),
+                            __ldcg(a.wrap_delta + 3 * g + 2));
+    }
+    __syncthreads();
+    // counts: one warp per centre of the slice
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int i = warp; i < n; i += kRefWarps) {
+    for (int i = lo + warp; i < hi; i += kRefWarps) {
         const int64_t g = base + i;
         const int cnt = min(a.cand_count[g], a.bmax);
         const float3 p = s_w[i];
@@ -606,31 +644,45 @@ __global__ void __launch_bounds__(kRefThreads) refilter_count_kernel(RefilterArg
         if (lane == 0) a.counts[g] = edges;
     }
     __syncthreads();
-    // per-system exclusive scan of the counts
+    // exclusive scan of the slice's counts (offsets inside the slice for now)
     int running = 0;
-    for (int i0 = 0; i0 < n; i0 += blockDim.x) {
+    for (int i0 = lo; i0 < hi; i0 += blockDim.x) {
         const int i = i0 + threadIdx.x;
-        const int v = i < n ? a.counts[base + i] : 0;
+        const int v = i < hi ? a.counts[base + i] : 0;
         int chunk_total;
         const int ex = block_scan_exclusive(v, s_scan, chunk_total);
-        if (i < n) a.local_off[base + i] = running + ex;
+        if (i < hi) a.local_off[base + i] = running + ex;
         running += chunk_total;
     }
-    if (threadIdx.x == 0) a.sys_total[sys] = running;
+    if (threadIdx.x == 0) s_total = running;
+    cluster.sync();  // every slice's total is known
+    int prefix = 0;  // edges of the lower ranks' slices
+    for (int r = 0; r < rank; ++r) prefix += *cluster.map_shared_rank(&s_total, r);
+    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) a.local_off[base + i] += prefix;
+    if (rank == kRefCluster - 1 && threadIdx.x == 0) a.sys_total[sys] = prefix + running;
+    cluster.sync();  // no CTA leaves while another may read its shared memory
 }
 
-// Materialize kernel: one CTA per system.
-__global__ void __launch_bounds__(kRefThreads) refilter_materialize_kernel(RefilterArgs a) {
+// Materialize kernel: the edges in canonical order, both CSRs, the padding rows.
+__global__ void __cluster_dims__(kRefCluster, 1, 1) __launch_bounds__(kRefThreads)
+    refilter_materialize_kernel(RefilterArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     float3* s_w = reinterpret_cast<float3*>(smem_raw);
     int3* s_wd = reinterpret_cast<int3*>(s_w + a.n_atoms);
-    int32_t* s_cursor = reinterpret_cast<int32_t*>(s_wd + a.n_atoms);      // sender cursors [n]
+    int32_t* s_cursor = reinterpret_cast<int32_t*>(s_wd + a.n_atoms);      // sender counts, then cursors [n]
     int32_t* s_soff = s_cursor + a.n_atoms;                                // sender offsets [n + 1]
     __shared__ int s_scan[32];
     __shared__ long long s_base, s_grand;
-    const int64_t sys = blockIdx.x;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = int(cluster.block_rank());
+    const int64_t sys = blockIdx.x / kRefCluster;
     const int64_t base = sys * a.n_atoms;
     const int n = int(a.n_atoms);
+    int lo, hi;
+    slice_of(n, rank, lo, hi);
+    // the sender arrays of the system live in rank 0's shared memory
+    int32_t* cursor0 = cluster.map_shared_rank(s_cursor, 0);
+    const int32_t* soff0 = cluster.map_shared_rank(s_soff, 0);
     if (threadIdx.x == 0) {
         long long b = 0, g = 0;
         for (int r = 0; r < a.n_systems; ++r) {
@@ -645,25 +697,25 @@ __global__ void __launch_bounds__(kRefThreads) refilter_materialize_kernel(Refil
         const int64_t g = base + i;
         s_w[i] = ld3(a.wrapped, g);
         s_wd[i] = ld3i(a.wrap_delta, g);
-        s_cursor[i] = 0;
+        if (rank == 0) s_cursor[i] = 0;
     }
-    __syncthreads();
+    cluster.sync();  // rank 0's sender counts are zero before any CTA adds to them
     const int64_t sys_base = s_base;
     const int64_t grand = s_grand;
     const int64_t cap = a.e_cap;
     // receiver CSR over the real edges (global), clipped to the capacity
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
         const int64_t o = sys_base + a.local_off[base + i];
         a.recv_off[base + i] = o < cap ? o : cap;
     }
-    if (sys == a.n_systems - 1 && threadIdx.x == 0) {
+    if (sys == a.n_systems - 1 && rank == 0 && threadIdx.x == 0) {
         a.recv_off[int64_t(a.n_systems) * a.n_atoms] = grand < cap ? grand : cap;
         a.n_edges[0] = grand;
         if (grand > cap) raise_flag(a.flags, FMD_FLAG_EDGE_OVERFLOW);
     }
-    // edges: warp per centre, ballot compaction in candidate (= canonical) order
+    // edges of the slice's centres: warp per centre, ballot compaction in candidate (= canonical) order
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int i = warp; i < n; i += kRefWarps) {
+    for (int i = lo + warp; i < hi; i += kRefWarps) {
         const int64_t g = base + i;
         const int cnt = min(a.cand_count[g], a.bmax);
         const float3 p = s_w[i];
@@ -691,56 +743,58 @@ __global__ void __launch_bounds__(kRefThreads) refilter_materialize_kernel(Refil
                     a.edge_image[3 * e] = float(img.x);
                     a.edge_image[3 * e + 1] = float(img.y);
                     a.edge_image[3 * e + 2] = float(img.z);
-                    atomicAdd(s_cursor + j, 1);  // sender count
+                    atomicAdd(cursor0 + j, 1);  // sender count
                 }
             }
             out += __popc(mask);
         }
     }
-    __syncthreads();
-    // sender CSR of this system: counts -> exclusive scan -> fill -> sort runs
-    int running = 0;
-    for (int i0 = 0; i0 < n; i0 += blockDim.x) {
-        const int i = i0 + threadIdx.x;
-        const int v = i < n ? s_cursor[i] : 0;
-        int chunk_total;
-        const int ex = block_scan_exclusive(v, s_scan, chunk_total);
-        if (i < n) s_soff[i] = running + ex;
-        running += chunk_total;
+    cluster.sync();  // every edge written, every sender counted
+    // sender CSR offsets of the system: counts -> exclusive scan in rank 0
+    if (rank == 0) {
+        int running = 0;
+        for (int i0 = 0; i0 < n; i0 += blockDim.x) {
+            const int i = i0 + threadIdx.x;
+            const int v = i < n ? s_cursor[i] : 0;
+            int chunk_total;
+            const int ex = block_scan_exclusive(v, s_scan, chunk_total);
+            if (i < n) s_soff[i] = running + ex;
+            running += chunk_total;
+        }
+        if (threadIdx.x == 0) s_soff[n] = running;
+        __syncthreads();
+        for (int i = threadIdx.x; i < n; i += blockDim.x) s_cursor[i] = 0;
     }
-    if (threadIdx.x == 0) s_soff[n] = running;
-    __syncthreads();
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const int64_t o = sys_base + s_soff[i];
+    cluster.sync();  // offsets known, cursors zero
+    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+        const int64_t o = sys_base + soff0[i];
         a.send_off[base + i] = o < cap ? o : cap;
-        s_cursor[i] = 0;
     }
-    if (sys == a.n_systems - 1 && threadIdx.x == 0)
+    if (sys == a.n_systems - 1 && rank == 0 && threadIdx.x == 0)
         a.send_off[int64_t(a.n_systems) * a.n_atoms] = grand < cap ? grand : cap;
-    __syncthreads();
     const int64_t sys_edges = a.sys_total[sys];
-    for (int64_t t = threadIdx.x; t < sys_edges; t += blockDim.x) {
+    for (int64_t t = int64_t(rank) * blockDim.x + threadIdx.x; t < sys_edges; t += int64_t(kRefCluster) * blockDim.x) {
         const int64_t e = sys_base + t;
         if (e >= cap) break;
-        const int j = int(int64_t(a.edge_index[2 * e + 1]) - base);
-        const int slot = atomicAdd(s_cursor + j, 1);
-        const int64_t dst = sys_base + s_soff[j] + slot;
+        const int j = int(int64_t(__ldcg(a.edge_index + 2 * e + 1)) - base);
+        const int slot = atomicAdd(cursor0 + j, 1);
+        const int64_t dst = sys_base + soff0[j] + slot;
         if (dst < cap) a.send_perm[dst] = int32_t(e);
     }
-    __syncthreads();
-    // each sender run ascending by edge id (rank sort, warp per sender)
-    for (int j = warp; j < n; j += kRefWarps) {
-        const int64_t b = sys_base + s_soff[j];
-        const int len = s_soff[j + 1] - s_soff[j];
+    cluster.sync();  // every sender run filled
+    // each sender run of the slice ascending by edge id (rank sort, warp per sender)
+    for (int j = lo + warp; j < hi; j += kRefWarps) {
+        const int64_t b = sys_base + soff0[j];
+        const int len = soff0[j + 1] - soff0[j];
         if (len <= 1 || b + len > cap) continue;
         int vals[8];
         int nv = 0;
-        for (int k = lane; k < len && nv < 8; k += 32) vals[nv++] = a.send_perm[b + k];
+        for (int k = lane; k < len && nv < 8; k += 32) vals[nv++] = __ldcg(a.send_perm + b + k);
         __syncwarp();
         int ranks[8];
         for (int v = 0; v < nv; ++v) {
             int r = 0;
-            for (int f = 0; f < len; ++f) r += a.send_perm[b + f] < vals[v] ? 1 : 0;
+            for (int f = 0; f < len; ++f) r += __ldcg(a.send_perm + b + f) < vals[v] ? 1 : 0;
             ranks[v] = r;
         }
         __syncwarp();
@@ -751,8 +805,8 @@ __global__ void __launch_bounds__(kRefThreads) refilter_materialize_kernel(Refil
     // padding rows [grand, cap): far self-loops round robin over the union's atoms
     const int64_t total_atoms = int64_t(a.n_systems) * a.n_atoms;
     const int64_t first = grand < cap ? grand : cap;
-    for (int64_t e = first + int64_t(sys) * blockDim.x + threadIdx.x; e < cap;
-         e += int64_t(a.n_systems) * blockDim.x) {
+    for (int64_t e = first + int64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < cap;
+         e += int64_t(gridDim.x) * blockDim.x) {
         const int32_t atom = int32_t((e - first) % total_atoms);
         a.edge_index[2 * e] = atom;
         a.edge_index[2 * e + 1] = atom;
@@ -760,6 +814,7 @@ __global__ void __launch_bounds__(kRefThreads) refilter_materialize_kernel(Refil
         a.edge_image[3 * e + 1] = float(a.pad_image[1]);
         a.edge_image[3 * e + 2] = float(a.pad_image[2]);
     }
+    cluster.sync();  // rank 0's sender arrays stay alive until every CTA is done with them
 }
 
 // ------------------------------------------------------------- ragged list
@@ -1045,7 +1100,7 @@ fmd_status fmd_refilter_workspace_bytes(int64_t n_atoms, int32_t n_systems, size
     return FMD_OK;
 }
 
-// largest system the single-CTA-per-system re-filter holds in shared memory
+// largest system the re-filter holds in shared memory (every CTA of a system's cluster stages it)
 static int64_t refilter_smem_bytes(int64_t n_atoms) {
     return int64_t(sizeof(float3) + sizeof(int3) + 2 * sizeof(int32_t)) * n_atoms + 4;
 }
@@ -1104,14 +1159,15 @@ fmd_status fmd_refilter_edges(const float* positions, const float* cell_host, in
     cudaStream_t s = as_stream(stream);
     const size_t smem_count = (sizeof(float3) + sizeof(int3)) * size_t(n_atoms);
     const size_t smem_mat = size_t(smem);
+    const int grid = n_systems * kRefCluster;  // a cluster of kRefCluster CTAs per system
     fmd_status st0 = allow_smem(reinterpret_cast<const void*>(refilter_count_kernel), smem_count, g_count_smem);
     if (st0 != FMD_OK) return st0;
     st0 = allow_smem(reinterpret_cast<const void*>(refilter_materialize_kernel), smem_mat, g_mat_smem);
     if (st0 != FMD_OK) return st0;
-    refilter_count_kernel<<<n_systems, kRefThreads, smem_count, s>>>(a);
+    refilter_count_kernel<<<grid, kRefThreads, smem_count, s>>>(a);
     fmd_status st = check_launch();
     if (st != FMD_OK) return st;
-    refilter_materialize_kernel<<<n_systems, kRefThreads, smem_mat, s>>>(a);
+    refilter_materialize_kernel<<<grid, kRefThreads, smem_mat, s>>>(a);
     return check_launch();
 }
 
