@@ -19,7 +19,8 @@
 //            order is therefore independent of the atomics of the bin pass.
 //
 // Re-filter (every MD step, inside the whole-step CUDA graph): two kernels,
-// one CTA per system. The count kernel wraps the positions (wrap delta
+// a thread-block cluster of 8 CTAs per system, each CTA a slice of the
+// centres. The count kernel wraps the positions (wrap delta
 // since the candidate refresh, skin test), and counts per atom the
 // candidates with dist2 < rc^2 evaluated in the reference's float32
 // operation order (fixed_capacity_builder.py:159-163; this file is compiled
