@@ -595,12 +595,14 @@ def _cpu_baseline():
 
 def _op_hbm(args):
     """``--op hbm_ops``: config 2's HBM-bound ops on a box of ``--atoms`` atoms at its density (rc 6 A):
-    gather-cat (neighbour 128 | centre 128 | basis 8), the CSR segment sum of [E x 256] and the segment
-    attention of [E x 128], 3 warm-up calls then 5 timed (CUDA events each)."""
+    gather-cat (neighbour 128 | centre 128 | basis 8), the CSR segment sum of [E x 256], the segment
+    attention of [E x 128] and the residual add of [E x 128] (12 bytes per element: its GB/s is
+    reported), 3 warm-up calls then 5 timed (CUDA events each)."""
     import torch
 
     from fastmd_b200.graph import neighbor_list
     from fastmd_b200.ops import csr_segment_sum, gather_cat, segment_csr
+    from fastmd_b200.residual_add import residual_add
     from fastmd_b200.segment_attention import segment_attention
     from fastmd_b200.structures import random_box
 
@@ -616,10 +618,12 @@ def _op_hbm(args):
     v = torch.randn(E, 256, device=dev, generator=g)
     logits = torch.randn(E, 128, device=dev, generator=g)
     val = torch.randn(E, 128, device=dev, generator=g)
+    res_w = torch.randn(128, device=dev, generator=g)
     perm, off = segment_csr(center, n)
     ops = {"gather_cat_264": lambda: gather_cat([(h, neighbor), (h, center), (rbf, None)]),
            "segment_sum_256": lambda: csr_segment_sum(v, center, n, perm, off),
-           "segment_attention_128": lambda: segment_attention(logits, val, center, n, perm, off)}
+           "segment_attention_128": lambda: segment_attention(logits, val, center, n, perm, off),
+           "residual_add_128": lambda: residual_add(logits, val, res_w)}
     out = {"op": "hbm_ops", "atoms": n, "edges": E}
     for name, fn in ops.items():
         for _ in range(3):
@@ -634,6 +638,7 @@ def _op_hbm(args):
             torch.cuda.synchronize()
             times.append(a.elapsed_time(b))
         out[name + "_ms"] = round(statistics.median(times), 4)
+    out["residual_add_128_gbs"] = round(12 * E * 128 / out["residual_add_128_ms"] / 1e6, 1)
     return out
 
 

@@ -56,6 +56,7 @@ _SIGNATURES: dict[str, list] = {
     "fmd_column_sum_workspace_bytes": [_I64, _I32, POINTER(c_size_t)],
     "fmd_column_sum": [_P, _I64, _I32, _I64, _P, c_size_t, _P, _P],
     "fmd_pair_aggregate": [_I32, _P, _I64, _P, _I64, _I32, _P, _P, _P],
+    "fmd_residual_add": [_I32, _P, _I64, _P, _I64, _P, _I64, _I32, _P, _I64, _P],
     "fmd_reverse_pairs_workspace_bytes": [_I64, POINTER(c_size_t)],
     "fmd_reverse_pairs": [_P, _P, _P, _I64, _I64, _I32, _P, c_size_t, _P, _P, _P, _P, _P],
     "fmd_line_graph_workspace_bytes": [_I64, _I64, POINTER(c_size_t)],

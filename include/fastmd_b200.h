@@ -380,6 +380,21 @@ FMD_API fmd_status fmd_column_sum(const float* x, int64_t rows, int32_t cols, in
 FMD_API fmd_status fmd_pair_aggregate(int32_t op, const float* in, int64_t ldi, const int64_t* pair_index,
                                       int64_t n_pairs, int32_t dim, float* out, int32_t* flags, void* stream);
 
+/* ----------------------------------- MatRIS residual add (frozen weight) */
+
+#define FMD_RESIDUAL_ADD 0
+#define FMD_RESIDUAL_ADD_BWD 1
+
+/* FMD_RESIDUAL_ADD      out[r, c] = delta[r, c] + residual[r, c] * weight[c]
+ * FMD_RESIDUAL_ADD_BWD  out[r, c] = residual[r, c] * weight[c]   (residual = the
+ *                       output gradient; delta unused and may be NULL)
+ * over rows x dim, each matrix with its own row stride (>= dim); the product is
+ * rounded before the addition. Replaces _residual_add_fwd / _residual_add_bwd
+ * (fastmd/models/matris/op/triton_residual_add.py:40, :64). */
+FMD_API fmd_status fmd_residual_add(int32_t op, const float* delta, int64_t ldd, const float* residual, int64_t ldr,
+                                    const float* weight, int64_t rows, int32_t dim, float* out, int64_t ldo,
+                                    void* stream);
+
 /* ------------------------------------------- segment attention (C2) */
 
 /* out[s, :] = sum over the rows i of segment s of softmax(logits[i, :] over

@@ -2,7 +2,7 @@
 
 Run in a container that holds the FastMD reference source tree (read-only):
 
-    python tests/golden/make_golden.py /path/to/fastmd-reference
+    python tests/golden/make_golden.py /path/to/fastmd-reference [fixture ...]
 
 It imports the reference with two stand-in modules for packages absent here
 (``ase.units`` with ASE's CODATA-2014 unit definitions; nothing else of ASE is
@@ -23,7 +23,9 @@ used) and runs, on CPU:
   gated-LN epilogue ``_gated_ln_fwd_2d`` / ``_gated_ln_bwd_2d``
   (fastmd/models/matris/op/triton_gated_ln.py:205/:280), the directed-pair average and
   undirected-pair expansion ``_directed_pair_average_fwd/_bwd`` / ``_undirected_pair_expand_fwd/_bwd``
-  (fastmd/models/matris/op/triton_directed_pair_aggregate.py:61/:83/:105/:127), and the
+  (fastmd/models/matris/op/triton_directed_pair_aggregate.py:61/:83/:105/:127), the
+  residual add ``_residual_add_fwd`` / ``_residual_add_bwd``
+  (fastmd/models/matris/op/triton_residual_add.py:40/:64), and the
   fixed-capacity re-filter ``_count_neighbors_kernel`` /
   ``_materialize_neighbors_kernel`` (fastmd/graph/fixed_capacity_builder.py:98/:189)
   on candidate lists of a dense search, followed by the reference's
@@ -381,6 +383,33 @@ def pair_aggregate_cases(torch, pa):
     return out
 
 
+def residual_add_cases(torch, ra):
+    """The MatRIS residual add with a frozen weight: the reference's ``_residual_add_fwd`` /
+    ``_residual_add_bwd`` (fastmd/models/matris/op/triton_residual_add.py:40, :64) launched as its
+    wrapper launches them (BD = next_pow2(min(128, D)), BM 8, grid (cdiv(N, BM), cdiv(D, BD))); delta,
+    residual and out are column views of wider buffers (row strides ``sd``, ``sr``, ``so``) where the
+    case says so; out is contiguous, as the wrapper's ``empty_like`` of a row-strided view is."""
+    out = {}
+    rng = np.random.default_rng(23)
+    for tag, (n, d, sd, sr) in {"d128": (37, 128, 128, 128), "d64_strided": (20, 64, 96, 80),
+                                "d5": (9, 5, 5, 5)}.items():
+        delta = rng.standard_normal((n, sd)).astype(np.float32)
+        residual = rng.standard_normal((n, sr)).astype(np.float32)
+        weight = rng.standard_normal(d).astype(np.float32)
+        gout = rng.standard_normal((n, d)).astype(np.float32)
+        bd = min(1 << (d - 1).bit_length(), 128)
+        grid = ((n + 7) // 8, (d + bd - 1) // bd)
+        res = torch.empty(n, d)
+        ra._residual_add_fwd[grid](torch.from_numpy(delta), torch.from_numpy(residual), torch.from_numpy(weight),
+                                   res, n, d, sd, sr, d, 8, bd)
+        gres = torch.empty(n, d)
+        ra._residual_add_bwd[grid](torch.from_numpy(gout), torch.from_numpy(weight), gres, N=n, D=d, BM=8, BD=bd)
+        out.update({f"ra_{tag}_delta": delta, f"ra_{tag}_residual": residual, f"ra_{tag}_weight": weight,
+                    f"ra_{tag}_gout": gout, f"ra_{tag}_meta": np.array([n, d, sd, sr], dtype=np.int64),
+                    f"ra_{tag}_out": res.numpy(), f"ra_{tag}_gres": gres.numpy()})
+    return out
+
+
 def nhc_cases(torch, gpu_nhc):
     from ase import units
 
@@ -537,7 +566,7 @@ def radial_cases(torch):
     return out
 
 
-def main(reference: str) -> None:
+def main(reference: str, only: list[str]) -> None:
     os.environ["TRITON_INTERPRET"] = "1"
     _install_stubs()
     sys.path.insert(0, reference)
@@ -557,20 +586,28 @@ def main(reference: str) -> None:
     import fastmd.graph.gpu_graph_builder as ggb
     import fastmd.models.matris.op.triton_gated_ln as gl
     import fastmd.models.matris.op.triton_directed_pair_aggregate as pa
+    import fastmd.models.matris.op.triton_residual_add as ra
 
-    np.savez_compressed(HERE / "gather_cat.npz", **gather_cat_cases(torch, gc))
-    np.savez_compressed(HERE / "segment_sum.npz", **segment_sum_cases(torch, cs))
-    np.savez_compressed(HERE / "nhc.npz", **nhc_cases(torch, gpu_nhc))
-    np.savez_compressed(HERE / "neighbors.npz", **neighbor_cases(torch, fcb))
-    np.savez_compressed(HERE / "radial.npz", **radial_cases(torch))
-    np.savez_compressed(HERE / "segment_attention.npz", **segment_attention_cases(torch, sa))
-    np.savez_compressed(HERE / "gather_add_silu.npz", **gather_add_silu_cases(torch, di))
-    np.savez_compressed(HERE / "line_graph.npz", **pairs_line_graph_cases(torch, ggb))
-    np.savez_compressed(HERE / "gated_ln.npz", **gated_ln_cases(torch, gl))
-    np.savez_compressed(HERE / "pair_aggregate.npz", **pair_aggregate_cases(torch, pa))
+    fixtures = {
+        "gather_cat": lambda: gather_cat_cases(torch, gc),
+        "segment_sum": lambda: segment_sum_cases(torch, cs),
+        "nhc": lambda: nhc_cases(torch, gpu_nhc),
+        "neighbors": lambda: neighbor_cases(torch, fcb),
+        "radial": lambda: radial_cases(torch),
+        "segment_attention": lambda: segment_attention_cases(torch, sa),
+        "gather_add_silu": lambda: gather_add_silu_cases(torch, di),
+        "line_graph": lambda: pairs_line_graph_cases(torch, ggb),
+        "gated_ln": lambda: gated_ln_cases(torch, gl),
+        "pair_aggregate": lambda: pair_aggregate_cases(torch, pa),
+        "residual_add": lambda: residual_add_cases(torch, ra),
+    }
+    for name, make in fixtures.items():
+        if not only or name in only:
+            np.savez_compressed(HERE / f"{name}.npz", **make())
     for path in sorted(HERE.glob("*.npz")):
         print(path.name, path.stat().st_size)
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    # make_golden.py [reference-root] [fixture ...]: every fixture unless some are named
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference", sys.argv[2:])

@@ -70,6 +70,10 @@ def test_invalid_arguments_are_rejected_before_any_launch():
     assert lib.fmd_pair_aggregate(4, p16, 8, p16, 1, 8, p16, None, None) == 1  # no such op
     assert lib.fmd_pair_aggregate(0, p16, 4, p16, 1, 8, p16, None, None) == 1  # row stride below the width
     assert lib.fmd_pair_aggregate(0, None, 8, None, 0, 8, None, None, None) == 0  # no pairs: nothing to do
+    assert lib.fmd_residual_add(2, p16, 8, p16, 8, p16, 1, 8, p16, 8, None) == 1  # no such op
+    assert lib.fmd_residual_add(0, p16, 4, p16, 8, p16, 1, 8, p16, 8, None) == 1  # delta stride below the width
+    assert lib.fmd_residual_add(0, None, 8, p16, 8, p16, 1, 8, p16, 8, None) == 1  # forward needs delta
+    assert lib.fmd_residual_add(1, None, 0, None, 8, None, 0, 8, None, 8, None) == 0  # no rows: nothing to do
 
 
 def test_no_cpu_fallback():
