@@ -32,6 +32,7 @@ EXTRA = {
     "segment_attention.cu": ["--fmad=false"],
     "gather_add_silu.cu": ["--fmad=false"],
     "gated_ln.cu": ["--fmad=false"],
+    "bond_graph.cu": ["--fmad=false"],
 }
 
 

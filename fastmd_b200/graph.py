@@ -1,12 +1,15 @@
 """Neighbour-list builders (the ``fastmd.graph`` surface) on libfastmd_b200 kernels.
 
 * ``FixedCapacityGraphBuilder`` -- the capture-safe builder of
-  fastmd/graph/fixed_capacity_builder.py:1030 in its edges-only mode (the
-  MACE / energy-tap topology, ``line_graph_cutoff=None``): a skin candidate
-  list refreshed rarely (``refresh_candidates``, :1675) and an exact per-step
-  re-filter into persistent padded buffers (``build``, :2181), published as a
-  ``GraphBatch``. R replicas of one system form a disjoint union
-  (``replicas=R``; replica_batch.py:126).
+  fastmd/graph/fixed_capacity_builder.py:1030: a skin candidate list refreshed
+  rarely (``refresh_candidates``, :1675) and an exact per-step re-filter into
+  persistent padded buffers (``build``, :2181), published as a ``GraphBatch``.
+  Edges only (the MACE / energy-tap topology, ``line_graph_cutoff=None``), or
+  with the MatRIS bond graph (``line_graph_cutoff`` and ``t_capacity``): the
+  undirected pairs and the triplets of short edges at fixed capacities, padded
+  with sink atoms (``n_dummy`` sink rows) or far self-loops, on the all-padding
+  topology after an overflow (``fmd_bond_graph``). R replicas of one system
+  form a disjoint union (``replicas=R``; replica_batch.py:126).
 * ``TensorGraphBuilder`` / ``neighbor_list`` -- the ragged eager path
   (gpu_graph_builder.py:935 / :108).
 
@@ -34,7 +37,10 @@ FLAG_EDGE_OVERFLOW = 2
 FLAG_CANDIDATE_OVERFLOW = 4
 FLAG_SKIN = 8
 FLAG_NONFINITE = 16
-_INVALID = FLAG_EDGE_OVERFLOW | FLAG_CANDIDATE_OVERFLOW | FLAG_SKIN | FLAG_NONFINITE
+FLAG_TRIPLET_OVERFLOW = 128
+FLAG_INVALID_PAIRS = 256
+_INVALID = (FLAG_EDGE_OVERFLOW | FLAG_CANDIDATE_OVERFLOW | FLAG_SKIN | FLAG_NONFINITE | FLAG_TRIPLET_OVERFLOW
+            | FLAG_INVALID_PAIRS)
 
 
 class NeighborOverflowError(RuntimeError):
@@ -76,6 +82,9 @@ class GraphBatch:
     replicas: int = 1
     element: Tensor | None = None    # model element rows (set by a model's prepare)
     element64: Tensor | None = None
+    directed2undirected: Tensor | None = None  # [E_cap] int32 (a builder with a line graph)
+    undirected2directed: Tensor | None = None  # [U_cap] int32
+    line_graph: Tensor | None = None           # [T_cap, 5] int32 [atom, u1, e1, u2, e2]
 
     @property
     def edge_dst(self) -> Tensor:
@@ -91,12 +100,13 @@ class FixedCapacityGraphStatus:
     derived from the build's FMD_FLAG_* word when read."""
 
     def __init__(self, flags: Tensor, n_edges: Tensor, max_displacement: Tensor, recv_off: Tensor,
-                 n_real: int) -> None:
+                 n_real: int, n_triplets: Tensor | None = None) -> None:
         self.flags = flags
         self.edge_count = n_edges
         self.max_displacement = max_displacement
         self._recv_off = recv_off
         self._n_real = n_real
+        self._n_triplets = n_triplets
 
     @property
     def overflow(self) -> Tensor:
@@ -112,7 +122,7 @@ class FixedCapacityGraphStatus:
 
     @property
     def invalid_pairs(self) -> Tensor:
-        return torch.zeros(1, dtype=torch.bool, device=self.flags.device)
+        return (self.flags & FLAG_INVALID_PAIRS) != 0
 
     @property
     def undirected_count(self) -> Tensor:
@@ -120,7 +130,10 @@ class FixedCapacityGraphStatus:
 
     @property
     def triplet_count(self) -> Tensor:
-        return torch.zeros(1, dtype=torch.int64, device=self.flags.device)
+        """Triplets of the stored rows (after an edge overflow: of the rows that fit)."""
+        if self._n_triplets is None:
+            return torch.zeros(1, dtype=torch.int64, device=self.flags.device)
+        return self._n_triplets
 
     @property
     def isolated_atom_count(self) -> Tensor:
@@ -129,9 +142,14 @@ class FixedCapacityGraphStatus:
 
 
 def fixed_capacity_exceeded(status: FixedCapacityGraphStatus, builder) -> Tensor:
-    """Device predicate: the real graph does not fit the builder (edges-only: more edges than
-    the edge capacity, fixed_capacity_builder.py:796)."""
-    return (status.edge_count[0] > builder.e_capacity) | ((status.flags[0] & FLAG_EDGE_OVERFLOW) != 0)
+    """Device predicate: the real graph does not fit the builder (fixed_capacity_builder.py:796).
+    Edges only: more edges than the edge capacity. With a line graph the padded triplets need a
+    padded pair, so an edge count equal to the capacity overflows too, as do more triplets than
+    the triplet capacity and invalid pairs."""
+    if getattr(builder, "edges_only", True):
+        return (status.edge_count[0] > builder.e_capacity) | ((status.flags[0] & FLAG_EDGE_OVERFLOW) != 0)
+    return ((status.edge_count[0] >= builder.e_capacity) | (status.triplet_count[0] > builder.t_capacity)
+            | status.invalid_pairs[0])
 
 
 def estimate_max_neighbors(cutoff: float, atomic_density: float = 0.35, safety_factor: float = 5.0) -> int:
@@ -163,12 +181,16 @@ def _host_cell(cell: Tensor):
 
 
 class FixedCapacityGraphBuilder:
-    """Capture-safe edges-only graph builder with static shapes (fixed_capacity_builder.py:1030).
+    """Capture-safe graph builder with static shapes (fixed_capacity_builder.py:1030).
 
     ``u_capacity`` undirected pairs (``e_capacity = 2 u_capacity`` directed rows) over the whole
     union of ``replicas`` copies of the system. ``candidate_cutoff`` (default ``cutoff + 1e-6``)
     sets the skin: a step stays exact while no atom moved more than half the skin since the
-    last ``refresh_candidates``.
+    last ``refresh_candidates``. With ``line_graph_cutoff`` (at most the atom cutoff) and
+    ``t_capacity`` the build also publishes the MatRIS bond graph (``directed2undirected``,
+    ``undirected2directed``, ``line_graph`` on the batch); its padding is ``sink_atoms`` (the
+    default then: ``n_dummy`` sink rows after the real atoms, positions at the origin, species 1)
+    or ``far_self_loops``.
     """
 
     def __init__(self, *, cell: Tensor, atomic_numbers: Tensor, u_capacity: int, t_capacity: int = 0,
@@ -176,19 +198,26 @@ class FixedCapacityGraphBuilder:
                  n_dummy: int = 0, device="cuda", candidate_cutoff: float | None = None,
                  padding: PaddingRule | None = None, replicas: int = 1, max_neighbors: int | None = None,
                  minimum_image: bool = False, **unused) -> None:
-        if line_graph_cutoff is not None or t_capacity != 0:
-            raise ValueError("this build implements the edges-only builder (line_graph_cutoff=None, t_capacity=0)")
+        self.edges_only = line_graph_cutoff is None
         if pbc is not None and not bool(torch.as_tensor(pbc).all()):
             raise ValueError("this build implements fully periodic cells")
-        padding = PaddingRule("far_self_loops") if padding is None else padding
-        if padding.kind != "far_self_loops":
-            raise ValueError("edges-only builds pad with far self-loops here")
-        if int(u_capacity) <= 0:
-            raise ValueError("an edges-only builder needs u_capacity > 0 and t_capacity == 0")
+        if self.edges_only:
+            padding = PaddingRule("far_self_loops") if padding is None else padding
+            if padding.kind != "far_self_loops":
+                raise ValueError("edges-only builds pad with far self-loops here")
+            if int(u_capacity) <= 0 or t_capacity != 0:
+                raise ValueError("an edges-only builder needs u_capacity > 0 and t_capacity == 0")
+        else:
+            padding = PaddingRule("sink_atoms") if padding is None else padding
+            if int(u_capacity) <= 0 or int(t_capacity) <= 0 or (padding.kind == "sink_atoms" and int(n_dummy) <= 0):
+                raise ValueError("capacities and n_dummy must be positive")
+            if float(line_graph_cutoff) > float(atom_graph_cutoff):
+                raise ValueError("line graph cutoff must not exceed atom graph cutoff")
+            if padding.kind not in ("sink_atoms", "far_self_loops"):
+                raise ValueError("a builder with a line graph pads with sink atoms or far self-loops")
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise _lib.FastMDLibraryError("the graph builders run on CUDA devices only")
-        self.edges_only = True
         self.minimum_image = bool(minimum_image)
         self.padding = padding
         self.cell = cell.detach().to(device=self.device, dtype=torch.float32).reshape(3, 3).contiguous()
@@ -199,16 +228,17 @@ class FixedCapacityGraphBuilder:
         self.n_real = self.n_atoms * self.replicas
         self.u_capacity = int(u_capacity)
         self.e_capacity = 2 * self.u_capacity
-        self.t_capacity = 0
+        self.t_capacity = 0 if self.edges_only else int(t_capacity)
+        self.n_dummy = int(n_dummy) if padding.kind == "sink_atoms" else 0
         self.atom_graph_cutoff = float(atom_graph_cutoff)
-        self.line_graph_cutoff = None
+        self.line_graph_cutoff = None if self.edges_only else float(line_graph_cutoff)
         self.candidate_cutoff = float(candidate_cutoff or (self.atom_graph_cutoff + 1.0e-6))
         self.skin = self.candidate_cutoff - self.atom_graph_cutoff
         self.buffer_max = int(max_neighbors or estimate_max_neighbors(self.candidate_cutoff, safety_factor=2.0))
         image, length = self_loop_image(self.cell, self.atom_graph_cutoff, padding.min_length)
         self.pad_image = image
         self.pad_length = length
-        self._pad_image_host = (ctypes.c_int32 * 3)(*image)
+        self._pad_image_host = (ctypes.c_int32 * 3)(*image)  # sink padding: the bond graph rewrites the loops
         N, B, E, dev = self.n_real, self.buffer_max, self.e_capacity, self.device
         i32 = dict(dtype=torch.int32, device=dev)
         self.cand_nbr = torch.full((N, B), N, **i32)
@@ -227,10 +257,11 @@ class FixedCapacityGraphBuilder:
         call("fmd_refilter_workspace_bytes", self.n_atoms, self.replicas, ctypes.byref(nbytes))
         self._refilter_ws = torch.empty(max(int(nbytes.value), 1), dtype=torch.uint8, device=dev)
         self.positions32 = torch.zeros(N, 3, dtype=torch.float32, device=dev)
+        rows = N + self.n_dummy  # sink rows after the real atoms (at the origin, species 1)
         self.batch = GraphBatch(
-            positions=torch.zeros(N, 3, dtype=torch.float32, device=dev),
+            positions=torch.zeros(rows, 3, dtype=torch.float32, device=dev),
             cell=self.cell,
-            species=species.repeat(self.replicas),
+            species=torch.cat([species.repeat(self.replicas), torch.ones(self.n_dummy, **i32)]),
             n_real=N,
             edge_index=torch.zeros(E, 2, **i32),
             edge_image=torch.zeros(E, 3, dtype=torch.float32, device=dev),
@@ -242,14 +273,26 @@ class FixedCapacityGraphBuilder:
             send_perm=torch.zeros(E, **i32),
             replicas=self.replicas,
         )
+        self.n_triplets = None
+        if not self.edges_only:
+            U, T = self.u_capacity, self.t_capacity
+            self.batch.directed2undirected = torch.zeros(E, **i32)
+            self.batch.undirected2directed = torch.zeros(U, **i32)
+            self.batch.line_graph = torch.zeros((T, 5), **i32)
+            self.n_triplets = torch.zeros(1, dtype=torch.int64, device=dev)
+            call("fmd_bond_graph_workspace_bytes", N, E, ctypes.byref(nbytes))
+            self._bond_ws = torch.empty(max(int(nbytes.value), 1), dtype=torch.uint8, device=dev)
+            self._bond_pad_image = (ctypes.c_int32 * 3)(*image)
         self._candidate_initialized = False
 
-    def resized(self, u_capacity: int) -> "FixedCapacityGraphBuilder":
-        """A builder of the same system with another pair capacity (new buffers; the candidates
+    def resized(self, u_capacity: int, t_capacity: int | None = None) -> "FixedCapacityGraphBuilder":
+        """A builder of the same system with other capacities (new buffers; the candidates
         are refreshed by the caller)."""
         return FixedCapacityGraphBuilder(
             cell=self.cell, atomic_numbers=self.batch.species[:self.n_atoms], u_capacity=u_capacity,
-            atom_graph_cutoff=self.atom_graph_cutoff, device=self.device, candidate_cutoff=self.candidate_cutoff,
+            t_capacity=self.t_capacity if t_capacity is None else t_capacity,
+            atom_graph_cutoff=self.atom_graph_cutoff, line_graph_cutoff=self.line_graph_cutoff,
+            n_dummy=self.n_dummy, device=self.device, candidate_cutoff=self.candidate_cutoff,
             padding=self.padding, replicas=self.replicas, max_neighbors=self.buffer_max,
             minimum_image=self.minimum_image)
 
@@ -305,8 +348,15 @@ class FixedCapacityGraphBuilder:
              ptr(self.batch.edge_image), ptr(self.batch.recv_off), ptr(self.batch.send_off),
              ptr(self.batch.send_perm), ptr(self.batch.n_edges), ptr(self.max_displacement), ptr(self._refilter_ws),
              self._refilter_ws.numel(), ptr(flags), stream(self.device))
+        if not self.edges_only:
+            b = self.batch
+            call("fmd_bond_graph", ptr(b.positions), self._cell_ptr, self.n_real, ptr(b.edge_index), ptr(b.edge_image),
+                 ptr(b.n_edges), self.u_capacity, self.t_capacity, self.line_graph_cutoff,
+                 0 if self.padding.kind == "sink_atoms" else 1, self.n_dummy, self._bond_pad_image, ptr(self._bond_ws),
+                 self._bond_ws.numel(), ptr(b.directed2undirected), ptr(b.undirected2directed), ptr(b.line_graph),
+                 ptr(self.n_triplets), ptr(flags), stream(self.device))
         status = FixedCapacityGraphStatus(flags, self.batch.n_edges, self.max_displacement, self.batch.recv_off,
-                                          self.n_real)
+                                          self.n_real, self.n_triplets)
         return self.batch, status
 
 

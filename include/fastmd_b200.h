@@ -54,6 +54,7 @@ typedef int32_t fmd_status;
 #define FMD_FLAG_CELL_RANGE 32      /* a fractional coordinate outside the cell grid */
 #define FMD_FLAG_WAIT_TIMEOUT 64    /* a bounded in-kernel wait gave up (about 1 s); outputs invalid */
 #define FMD_FLAG_TRIPLET_OVERFLOW 128 /* more line-graph triplets than the triplet capacity */
+#define FMD_FLAG_INVALID_PAIRS 256  /* a real edge without its reverse, or an odd edge count */
 
 /* ---------------------------------------------------------------- library */
 
@@ -295,6 +296,41 @@ FMD_API fmd_status fmd_line_graph(const int64_t* center, const float* dist, cons
                                   int64_t n_edges, int64_t n_atoms, float cutoff, int32_t presorted,
                                   int64_t t_capacity, void* workspace, size_t workspace_bytes, int32_t* triplets,
                                   int64_t* n_triplets, int32_t* flags, void* stream);
+
+/* The fixed-capacity MatRIS bond graph of a fixed-capacity build, capture-safe
+ * (no count leaves the device). Input: edge_index [2 u_capacity, 2] int32 and
+ * edge_image [2 u_capacity, 3] (integer images as float) whose first
+ * min(*n_edges, 2 u_capacity) rows are the real edges in canonical (centre,
+ * neighbour, image) order (what fmd_refilter_edges writes), the wrapped
+ * positions [n_atoms, 3] they were computed from and the row-major host cell.
+ * Output, bit-identical to the reference builder:
+ *   the padded rows rewritten by the padding rule (FMD_PAD_SINK_ATOMS: both
+ *   rows of padded pair p on sink n_atoms + p n_dummy / n_pad_u, image
+ *   (3, 3, 3); FMD_PAD_FAR_SELF_LOOPS: the loops +pad_image / -pad_image of
+ *   atom p mod n_atoms);
+ *   directed2undirected [2 u_capacity], undirected2directed [u_capacity];
+ *   line_graph [t_capacity, 5] int32 rows [atom, u1, e1, u2, e2] over the
+ *   short edges (dist2 < line_cutoff^2 in the re-filter's FP32 order), then
+ *   padded triplets on padded pairs;
+ *   *n_triplets the triplet count (of the stored rows);
+ *   flags: FMD_FLAG_INVALID_PAIRS, FMD_FLAG_EDGE_OVERFLOW when the edges leave
+ *   no padded pair (>= 2 u_capacity), FMD_FLAG_TRIPLET_OVERFLOW.
+ * On an overflow (those, or a flags word already holding FMD_FLAG_SKIN,
+ * _CANDIDATE_OVERFLOW or _NONFINITE) every row, pair and triplet is the
+ * all-padding topology instead. Replaces _materialize_pairs,
+ * _materialize_line_graph / _line_graph_kernel, _pad_edges_kernel,
+ * _pad_loop_pairs_kernel and the overflow topology
+ * (fastmd/graph/fixed_capacity_builder.py:2001, :2101, :681, :292, :397,
+ * :1474, :2163). */
+#define FMD_PAD_SINK_ATOMS 0
+#define FMD_PAD_FAR_SELF_LOOPS 1
+FMD_API fmd_status fmd_bond_graph_workspace_bytes(int64_t n_atoms, int64_t e_capacity, size_t* bytes);
+FMD_API fmd_status fmd_bond_graph(const float* positions, const float* cell, int64_t n_atoms, int32_t* edge_index,
+                                  float* edge_image, const int64_t* n_edges, int64_t u_capacity, int64_t t_capacity,
+                                  float line_cutoff, int32_t padding, int64_t n_dummy, const int32_t* pad_image,
+                                  void* workspace, size_t workspace_bytes, int32_t* directed2undirected,
+                                  int32_t* undirected2directed, int32_t* line_graph, int64_t* n_triplets,
+                                  int32_t* flags, void* stream);
 
 /* -------------------------- decomposed indexed-concat SiLU epilogue (B2) */
 

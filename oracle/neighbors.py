@@ -53,14 +53,17 @@ def wrap(positions, cell, inv_cell=None):
     return small_matmul(frac, cell), wraps, frac
 
 
-def refilter(wrapped, cell, cand_matrix, cand_shifts, cand_count, cutoff, wrap_delta=None):
-    """Edges of a candidate list in candidate order: (center, neighbor, image int32 [E,3], dist f32)."""
+def refilter(wrapped, cell, cand_matrix, cand_shifts, cand_count, cutoff, wrap_delta=None, line_cutoff=None):
+    """Edges of a candidate list in candidate order: (center, neighbor, image int32 [E,3], dist f32), and
+    with ``line_cutoff`` the short flags ``dist2 < line_cutoff**2`` of the same float32 ``dist2``
+    (``_materialize_neighbors_kernel``'s ``short_valid``, fixed_capacity_builder.py:264)."""
     wrapped = np.asarray(wrapped, f32)
     cell = np.asarray(cell, f32)
     n, bmax = cand_matrix.shape
     wd = np.zeros((n, 3), np.int32) if wrap_delta is None else np.asarray(wrap_delta, np.int32)
     cut2 = f32(cutoff * cutoff)
-    centers, neighbors, images, dists = [], [], [], []
+    centers, neighbors, images, dists, shorts = [], [], [], [], []
+    line2 = None if line_cutoff is None else f32(line_cutoff * line_cutoff)
     for atom in range(n):
         cnt = int(cand_count[atom])
         nb = np.minimum(cand_matrix[atom, :cnt].astype(np.int64), n - 1)
@@ -81,8 +84,11 @@ def refilter(wrapped, cell, cand_matrix, cand_shifts, cand_count, cutoff, wrap_d
         neighbors.append(nb[keep])
         images.append(s[keep])
         dists.append(np.sqrt(dist2[keep]).astype(f32))
-    return (np.concatenate(centers), np.concatenate(neighbors), np.concatenate(images).reshape(-1, 3),
-            np.concatenate(dists))
+        if line2 is not None:
+            shorts.append(dist2[keep] < line2)
+    out = (np.concatenate(centers), np.concatenate(neighbors), np.concatenate(images).reshape(-1, 3),
+           np.concatenate(dists))
+    return out if line2 is None else (*out, np.concatenate(shorts))
 
 
 def ragged_filter(wrapped, cell, center, neighbor, images, cutoff):

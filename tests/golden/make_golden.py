@@ -552,6 +552,137 @@ def neighbor_cases(torch, fcb):
     return out
 
 
+def bond_graph_cases(torch, fcb):
+    """The reference's fixed-capacity MatRIS bond graph (a builder with a line graph): the re-filter with
+    short flags (``_count_neighbors_kernel`` / ``_materialize_neighbors_kernel`` with ``LINE_CUTOFF2``,
+    fixed_capacity_builder.py:98/:189), the padding rows (``_pad_edges_kernel`` :292, sink atoms;
+    ``_pad_loop_pairs_kernel`` :397, far self-loops), then the builder's own ``_materialize_pairs`` (:2001),
+    ``_materialize_line_graph`` (:2101, with ``_line_graph_kernel`` :681) and
+    ``_substitute_overflow_topology`` (:2163) over the overflow topology of ``_allocate_overflow_topology``
+    (:1474), run as unbound methods on a stand-in holding the builder's buffers. Candidates: the dense
+    list within rc + 2 of the wrapped positions. Cases: both paddings with room, a triplet overflow
+    (t_capacity one short) and an edge overflow (e_capacity equal to the edge count: no padding pair)."""
+    from types import SimpleNamespace
+
+    from fastmd.graph.fixed_capacity_builder import PaddingRule, self_loop_padding
+
+    out = {}
+    rng = np.random.default_rng(31)
+    frac_cell = np.array([[0, 0, 0], [.5, .5, .5], [.5, .5, 0], [.5, 0, .5], [0, .5, .5]])
+    grid = np.array([[i, j, k] for i in range(3) for j in range(3) for k in range(3)], float)
+    perov_cell = (np.eye(3) * 18.6).astype(np.float32)
+    perov = ((grid[:, None, :] + frac_cell[None, :, :]).reshape(-1, 3) / 3.0) @ perov_cell.astype(np.float64)
+    perov = (perov + rng.normal(0, 0.05, perov.shape)).astype(np.float32)
+    tric_cell = np.array([[7.5, 0.0, 0.0], [1.9, 8.1, 0.0], [-1.2, 2.3, 9.4]], np.float32)
+    tric = (rng.uniform(0, 1, (40, 3)) @ tric_cell.astype(np.float64) + rng.normal(0, 0.3, (40, 3))).astype(np.float32)
+    # (positions, cell, padding, n_dummy, extra undirected pairs, extra triplets)
+    cases = {"perov_sink": (perov, perov_cell, "sink_atoms", 64, 37, 123),
+             "perov_loop": (perov, perov_cell, "far_self_loops", 0, 20, 64),
+             "perov_sink_tover": (perov, perov_cell, "sink_atoms", 16, 5, -1),
+             "perov_loop_eover": (perov, perov_cell, "far_self_loops", 0, 0, 50),
+             "tric_sink": (tric, tric_cell, "sink_atoms", 8, 11, 9)}
+    rc, lrc, cand = 6.0, 4.5, 8.0
+    for tag, (pos32, cell, padding, n_dummy, extra_u, extra_t) in cases.items():
+        cell_t = torch.from_numpy(cell)
+        inv = torch.linalg.inv(cell_t.double()).float()
+        p = torch.from_numpy(pos32)
+        frac_un = (p.unsqueeze(-1) * inv.unsqueeze(-3)).sum(dim=-2)
+        wraps = torch.floor(frac_un).to(torch.int32)
+        wrapped = ((frac_un - wraps.float()).unsqueeze(-1) * cell_t.unsqueeze(-3)).sum(dim=-2)
+        wrapped64, cell64, N = wrapped.double().numpy(), cell.astype(np.float64), pos32.shape[0]
+        heights = abs(np.linalg.det(cell64)) / np.array(
+            [np.linalg.norm(np.cross(cell64[(k + 1) % 3], cell64[(k + 2) % 3])) for k in range(3)])
+        reach = [int(np.ceil(cand / h)) + 1 for h in heights]
+        rows = [[] for _ in range(N)]
+        for ix in range(-reach[0], reach[0] + 1):
+            for iy in range(-reach[1], reach[1] + 1):
+                for iz in range(-reach[2], reach[2] + 1):
+                    shift = np.array([ix, iy, iz], float) @ cell64
+                    d = np.linalg.norm(wrapped64[None, :, :] + shift - wrapped64[:, None, :], axis=-1)
+                    for i, j in zip(*np.nonzero(d < cand)):
+                        if i != j or (ix, iy, iz) != (0, 0, 0):
+                            rows[i].append((j, ix, iy, iz))
+        bmax = (max(len(r) for r in rows) + 15) // 16 * 16
+        nm = np.full((N, bmax), N, np.int32)
+        ns = np.zeros((N, bmax, 3), np.int32)
+        nn = np.zeros(N, np.int32)
+        for i, r in enumerate(rows):
+            rng.shuffle(r)
+            nn[i] = len(r)
+            for k, (j, ix, iy, iz) in enumerate(r):
+                nm[i, k], ns[i, k] = j, (ix, iy, iz)
+        nm_t, ns_t, nn_t = torch.from_numpy(nm), torch.from_numpy(ns), torch.from_numpy(nn)
+        wrap_delta = torch.zeros(N, 3, dtype=torch.int32)
+        dummy_i, dummy_b = torch.zeros(1, dtype=torch.int32), torch.zeros(1, dtype=torch.bool)
+        block = 1 << (bmax - 1).bit_length()
+        edge_counts = torch.zeros(N, dtype=torch.int64)
+        short_counts = torch.zeros(N, dtype=torch.int64)
+        iso = torch.zeros(1, dtype=torch.int32)
+        fcb._count_neighbors_kernel[(N,)](
+            wrapped, cell_t, nm_t, ns_t, nn_t, wrap_delta, edge_counts, short_counts, iso, dummy_i, N, dummy_b,
+            dummy_b, dummy_i, N=N, BMAX=bmax, BLOCK=block, EDGE_CUTOFF2=rc * rc, LINE_CUTOFF2=lrc * lrc)
+        total = int(edge_counts.sum())
+        u_cap = total // 2 + extra_u
+        e_cap = 2 * u_cap
+        t_real = int((short_counts * (short_counts - 1)).sum())
+        t_cap = t_real + extra_t
+        b = SimpleNamespace(n_real=N, n_dummy=n_dummy, u_capacity=u_cap, e_capacity=e_cap, t_capacity=t_cap,
+                            buffer_max=bmax, device=torch.device("cpu"), sort_key_dtype=torch.int64,
+                            sort_key_max_image=10, ghosts=None, _ghost_edges=0)
+        b.edge_ids = torch.arange(e_cap, dtype=torch.int64)
+        b.u_ids = torch.arange(u_cap, dtype=torch.int64)
+        b.triplet_ids = torch.arange(t_cap, dtype=torch.int64)
+        b._pad_loop = (None if padding == "sink_atoms"
+                       else self_loop_padding(PaddingRule("far_self_loops"), cell_t, rc))
+        b.edge_counts, b.short_counts = edge_counts, short_counts
+        b.edge_offsets = torch.zeros(N + 1, dtype=torch.int64)
+        b.edge_offsets[1:] = torch.cumsum(edge_counts, 0)
+        b.short_offsets = torch.zeros(N + 1, dtype=torch.int64)
+        b.pair_offsets = torch.zeros(N + 1, dtype=torch.int64)
+        b.short_edge_matrix = torch.zeros((N, bmax), dtype=torch.int32)
+        b.center = torch.zeros(e_cap, dtype=torch.int32)
+        b.neighbor = torch.zeros(e_cap, dtype=torch.int32)
+        b.images = torch.zeros((e_cap, 3), dtype=torch.int32)
+        b.distances = torch.zeros(e_cap, dtype=torch.float32)
+        b.short_flags = torch.zeros(e_cap, dtype=torch.bool)
+        b.directed2undirected = torch.zeros(e_cap, dtype=torch.int32)
+        b.undirected2directed = torch.zeros(u_cap, dtype=torch.int32)
+        b.line_graph = torch.zeros((t_cap, 5), dtype=torch.int32)
+        b._u2d_scatter = torch.empty(u_cap + e_cap, dtype=torch.int64)
+        b._short_scatter = torch.empty(N * bmax + e_cap, dtype=torch.int64)
+        b._overflow = torch.zeros(1, dtype=torch.bool)
+        b._invalid_pairs = torch.zeros(1, dtype=torch.bool)
+        b._candidate_valid = torch.ones(1, dtype=torch.bool)
+        fcb._materialize_neighbors_kernel[(N,)](
+            wrapped, cell_t, nm_t, ns_t, nn_t, wrap_delta, b.edge_offsets, b.center, b.neighbor, b.images,
+            b.distances, b.short_flags, b.short_edge_matrix, N, dummy_b, dummy_b, dummy_i, N=N, BMAX=bmax,
+            E_CAP=e_cap, BLOCK=block, EDGE_CUTOFF2=rc * rc, LINE_CUTOFF2=lrc * lrc)
+        grid = ((e_cap + 255) // 256,)
+        if b._pad_loop is None:
+            fcb._pad_edges_kernel[grid](b.edge_offsets[-1:], b.center, b.neighbor, b.images, b.distances,
+                                        b.short_flags, N=N, N_DUMMY=n_dummy, E_CAP=e_cap, BLOCK=256)
+        else:
+            image, length, _ = b._pad_loop
+            fcb._pad_loop_pairs_kernel[grid](b.edge_offsets[-1:], b.center, b.neighbor, b.images, b.distances,
+                                             b.short_flags, *image, length, N=N, E_CAP=e_cap, BLOCK=256)
+        cls = fcb.FixedCapacityGraphBuilder
+        cls._allocate_overflow_topology(b)
+        cls._materialize_pairs(b)
+        cls._materialize_line_graph(b)
+        cls._substitute_overflow_topology(b)
+        out.update({f"bg_{tag}_positions": pos32, f"bg_{tag}_cell": cell,
+                    f"bg_{tag}_meta": np.array([N, n_dummy, u_cap, t_cap, total, t_real,
+                                                int(padding == "sink_atoms")], dtype=np.int64),
+                    f"bg_{tag}_cutoffs": np.array([rc, lrc, cand]),
+                    f"bg_{tag}_pad_image": np.array(b._pad_loop[0] if b._pad_loop else (0, 0, 0), np.int32),
+                    f"bg_{tag}_center": b.center.numpy(), f"bg_{tag}_neighbor": b.neighbor.numpy(),
+                    f"bg_{tag}_images": b.images.numpy(), f"bg_{tag}_d2u": b.directed2undirected.numpy(),
+                    f"bg_{tag}_u2d": b.undirected2directed.numpy(), f"bg_{tag}_line_graph": b.line_graph.numpy(),
+                    f"bg_{tag}_short_flags": b.short_flags.numpy(),
+                    f"bg_{tag}_flags": np.array([bool(b._overflow), bool(b._invalid_pairs)], dtype=np.int64)})
+    return out
+
+
 def radial_cases(torch):
     """The reference's radial basis (fastmd/models/matris/basis_function.py:139 BesselExpansion with the
     PolynomialEnvelope of :31) at the MACE setting (8 functions, rc 6, p 5) and MatRIS's (7, 6, 8)."""
@@ -600,6 +731,7 @@ def main(reference: str, only: list[str]) -> None:
         "gated_ln": lambda: gated_ln_cases(torch, gl),
         "pair_aggregate": lambda: pair_aggregate_cases(torch, pa),
         "residual_add": lambda: residual_add_cases(torch, ra),
+        "bond_graph": lambda: bond_graph_cases(torch, fcb),
     }
     for name, make in fixtures.items():
         if not only or name in only:

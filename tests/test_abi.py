@@ -71,6 +71,25 @@ def test_invalid_arguments_are_rejected_before_any_launch():
     assert lib.fmd_pair_aggregate(0, p16, 4, p16, 1, 8, p16, None, None) == 1  # row stride below the width
     assert lib.fmd_pair_aggregate(0, None, 8, None, 0, 8, None, None, None) == 0  # no pairs: nothing to do
     assert lib.fmd_residual_add(2, p16, 8, p16, 8, p16, 1, 8, p16, 8, None) == 1  # no such op
+    nb = ctypes.c_size_t(0)
+    assert lib.fmd_bond_graph_workspace_bytes(0, 2100, ctypes.byref(nb)) == 1
+    cell = (ctypes.c_float * 9)(*[10, 0, 0, 0, 10, 0, 0, 0, 10])
+    image = (ctypes.c_int32 * 3)(1, 0, 0)
+    args = [p16, cell, 8, p16, p16, p16, 16, 32, ctypes.c_float(4.5), 0, 4, None, p16, 1 << 20, p16, p16, p16, p16,
+            p16, None]
+    bad = list(args)
+    bad[9] = 2  # no such padding rule
+    assert lib.fmd_bond_graph(*bad) == 1
+    bad = list(args)
+    bad[10] = 0  # sink padding needs sink atoms
+    assert lib.fmd_bond_graph(*bad) == 1
+    bad = list(args)
+    bad[9], bad[11] = 1, None  # far self-loops need the loop image
+    assert lib.fmd_bond_graph(*bad) == 1
+    bad = list(args)
+    bad[8] = ctypes.c_float(-1.0)  # negative line cutoff
+    assert lib.fmd_bond_graph(*bad) == 1
+    del image
     assert lib.fmd_residual_add(0, p16, 4, p16, 8, p16, 1, 8, p16, 8, None) == 1  # delta stride below the width
     assert lib.fmd_residual_add(0, None, 8, p16, 8, p16, 1, 8, p16, 8, None) == 1  # forward needs delta
     assert lib.fmd_residual_add(1, None, 0, None, 8, None, 0, 8, None, 8, None) == 0  # no rows: nothing to do
