@@ -52,7 +52,7 @@ def _args():
     p.add_argument("--steps-per-launch", type=int, default=10)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-ops", action="store_true", help="skip the config-2 op microbenchmark")
-    p.add_argument("--op", choices=["wide_gemm", "hbm_ops"], default=None,
+    p.add_argument("--op", choices=["wide_gemm", "hbm_ops", "bond_graph"], default=None,
                    help="time one op alone (the profiling entry of profiles/): prints its own JSON line")
     p.add_argument("--rows", type=int, default=300_000, help="rows of --op wide_gemm")
     p.add_argument("--atoms", type=int, default=25_000, help="atoms of --op hbm_ops (config 2's box density)")
@@ -642,6 +642,58 @@ def _op_hbm(args):
     return out
 
 
+def _op_bond_graph(args):
+    """``--op bond_graph``: the per-step fixed-capacity MatRIS build (re-filter of reused candidates, then
+    the bond graph: pairs and triplets at rc 6 / 4.5 A, sink padding) of ``--replicas`` 135-atom systems
+    (config 0's perovskite), against the edges-only re-filter of the same positions. Each build is
+    captured in a CUDA graph (as a whole step runs it); 3 warm-up replays, then 20 timed (CUDA events
+    around each replay)."""
+    import numpy as np
+    import torch
+
+    from fastmd_b200.graph import FixedCapacityGraphBuilder, PaddingRule
+    from fastmd_b200.structures import perovskite
+
+    dev = torch.device("cuda", 0)
+    R = max(args.replicas, 1)
+    pos = np.concatenate([perovskite(seed=s)[0] for s in range(R)]).astype(np.float32)
+    cell = torch.tensor(perovskite(seed=0)[1], dtype=torch.float32)
+    numbers = torch.tensor(perovskite(seed=0)[2])
+    common = dict(cell=cell, atomic_numbers=numbers, u_capacity=1100 * R, atom_graph_cutoff=6.0, candidate_cutoff=8.0,
+                  device=dev, replicas=R)
+    builders = {"refilter": FixedCapacityGraphBuilder(**common),
+                "refilter_bond_graph": FixedCapacityGraphBuilder(**common, line_graph_cutoff=4.5, t_capacity=19_000 * R,
+                                                                 padding=PaddingRule("sink_atoms"), n_dummy=64)}
+    x = torch.from_numpy(pos).to(dev)
+    out = {"op": "bond_graph", "replicas": R, "atoms": int(pos.shape[0])}
+    for name, b in builders.items():
+        b.refresh_candidates(x)
+        b.build(x, rebuild_candidates=False)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            b.build(x, rebuild_candidates=False)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(20):
+            a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            graph.replay()
+            e.record()
+            torch.cuda.synchronize()
+            times.append(a.elapsed_time(e))
+        graph.reset()
+        out[name + "_us"] = round(1e3 * statistics.median(times), 1)
+        if name == "refilter_bond_graph":
+            out["edges"] = int(b.batch.n_edges.item())
+            out["triplets"] = int(b.n_triplets.item())
+            out["flags"] = int(b.flags.item())
+    out["bond_graph_us"] = round(out["refilter_bond_graph_us"] - out["refilter_us"], 1)
+    return out
+
+
 def _op(args):
     """One op alone on cuda:0, the profiling entry: ``--op wide_gemm`` runs the config-2 first edge
     layer (264 -> 256, bias, SiLU, 3xTF32 on tcgen05) over ``--rows`` rows, 3 warm-up launches then
@@ -649,6 +701,8 @@ def _op(args):
     the HBM-bound ops (``_op_hbm``)."""
     if args.op == "hbm_ops":
         return _op_hbm(args)
+    if args.op == "bond_graph":
+        return _op_bond_graph(args)
     import torch
 
     from fastmd_b200 import wide_gemm
