@@ -197,7 +197,8 @@ class FixedCapacityGraphBuilder:
                  pbc: Tensor | None = None, atom_graph_cutoff: float = 6.0, line_graph_cutoff: float | None = None,
                  n_dummy: int = 0, device="cuda", candidate_cutoff: float | None = None,
                  padding: PaddingRule | None = None, replicas: int = 1, max_neighbors: int | None = None,
-                 minimum_image: bool = False, **unused) -> None:
+                 minimum_image: bool = False, candidates_from: "FixedCapacityGraphBuilder | None" = None,
+                 **unused) -> None:
         self.edges_only = line_graph_cutoff is None
         if pbc is not None and not bool(torch.as_tensor(pbc).all()):
             raise ValueError("this build implements fully periodic cells")
@@ -284,6 +285,25 @@ class FixedCapacityGraphBuilder:
             self._bond_ws = torch.empty(max(int(nbytes.value), 1), dtype=torch.uint8, device=dev)
             self._bond_pad_image = (ctypes.c_int32 * 3)(*image)
         self._candidate_initialized = False
+        self._candidate_owner = self
+        if candidates_from is not None:
+            self._share_candidates(candidates_from)
+
+    # the candidate state a ``candidates_from`` builder reads from its owner (fixed_capacity_builder.py:666)
+    _CANDIDATE_STATE = ("cand_nbr", "cand_shift", "cand_count", "reference_positions", "reference_wraps",
+                        "wrap_delta", "refresh_flags")
+
+    def _share_candidates(self, owner: "FixedCapacityGraphBuilder") -> None:
+        """Read ``owner``'s candidate list (its refreshes are this builder's): same atoms, cell,
+        candidate cutoff and slot count required."""
+        owner = owner._candidate_owner
+        if (owner.n_real != self.n_real or owner.buffer_max != self.buffer_max
+                or owner.candidate_cutoff != self.candidate_cutoff or not torch.equal(owner.cell, self.cell)
+                or owner.replicas != self.replicas or owner.minimum_image != self.minimum_image):
+            raise ValueError("candidates_from: the owner builds another system, cutoff or slot count")
+        for name in self._CANDIDATE_STATE:
+            setattr(self, name, getattr(owner, name))
+        self._candidate_owner = owner
 
     def resized(self, u_capacity: int, t_capacity: int | None = None) -> "FixedCapacityGraphBuilder":
         """A builder of the same system with other capacities (new buffers; the candidates
@@ -316,7 +336,7 @@ class FixedCapacityGraphBuilder:
              self.buffer_max, ptr(self.cand_nbr), ptr(self.cand_shift), ptr(self.cand_count),
              ptr(self.reference_positions), ptr(self.reference_wraps), ptr(self.wrap_delta), ptr(self._cell_ws),
              self._cell_ws.numel(), ptr(self.refresh_flags), stream(self.device))
-        self._candidate_initialized = True
+        self._candidate_owner._candidate_initialized = True
 
     def assert_candidate_capacity(self) -> None:
         """Raise on the slow path if a candidate row was truncated (host read)."""
@@ -336,7 +356,7 @@ class FixedCapacityGraphBuilder:
         pos = self._positions(positions)
         if rebuild_candidates:
             self.refresh_candidates(pos)
-        elif not self._candidate_initialized:
+        elif not self._candidate_owner._candidate_initialized:
             raise RuntimeError("refresh_candidates must run before candidate reuse")
         if flags is None:
             flags = self.flags
