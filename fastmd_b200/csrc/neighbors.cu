@@ -900,6 +900,31 @@ __global__ void copy_wrapped_kernel(const float4* __restrict__ src, int64_t n, f
     }
 }
 
+// float64 model positions of a float64 build (fixed_capacity_builder.py:464
+// _float64_prologue_kernel): the float32 wrap of the rounded coordinates gives
+// the whole lattice vectors w, removed from the float64 coordinates with the
+// float64 cell: out = p - ((w0 c[0] + w1 c[1]) + w2 c[2]), rounded per operation
+struct Cell64 {
+    double c[9];
+};
+
+__global__ void model_positions_f64_kernel(const double* __restrict__ p, int64_t n, Cell9 cell, Cell64 cell64,
+                                           double* __restrict__ out) {
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+        const double x = p[3 * i], y = p[3 * i + 1], z = p[3 * i + 2];
+        float3 w, f;
+        int3 wr;
+        wrap_atom(make_float3(float(x), float(y), float(z)), cell, w, wr, f);
+        const double v0 = double(wr.x), v1 = double(wr.y), v2 = double(wr.z);
+        const double* c = cell64.c;
+        out[3 * i] = __dsub_rn(x, __dadd_rn(__dadd_rn(__dmul_rn(v0, c[0]), __dmul_rn(v1, c[3])), __dmul_rn(v2, c[6])));
+        out[3 * i + 1] =
+            __dsub_rn(y, __dadd_rn(__dadd_rn(__dmul_rn(v0, c[1]), __dmul_rn(v1, c[4])), __dmul_rn(v2, c[7])));
+        out[3 * i + 2] =
+            __dsub_rn(z, __dadd_rn(__dadd_rn(__dmul_rn(v0, c[2]), __dmul_rn(v1, c[5])), __dmul_rn(v2, c[8])));
+    }
+}
+
 // ------------------------------------------------------------------ host
 
 inline size_t align_up(size_t x) { return (x + 255) & ~size_t(255); }
@@ -1306,6 +1331,21 @@ fmd_status fmd_refilter_edges_noalloc(const float* positions, const float* cell_
                               cand_shift, cand_count, bmax, cutoff, skin, e_capacity, pad_image_host, minimum_image,
                               wrapped, wrap_delta, edge_index, edge_image, recv_off, send_off, send_perm, n_edges,
                               max_displacement, scratch, kNoAllocScratchBytes, flags, stream);
+}
+
+fmd_status fmd_model_positions_f64(const double* positions, int64_t n_atoms, const float* cell_host,
+                                   const double* cell64_host, double* out, void* stream) {
+    if (n_atoms < 0 || cell_host == nullptr || cell64_host == nullptr) return FMD_ERR_INVALID_ARGUMENT;
+    if (n_atoms == 0) return FMD_OK;
+    if (positions == nullptr || out == nullptr) return FMD_ERR_INVALID_ARGUMENT;
+    Cell9 cell;
+    if (!make_cell(cell_host, cell)) return FMD_ERR_INVALID_ARGUMENT;
+    Cell64 cell64;
+    for (int k = 0; k < 9; ++k) cell64.c[k] = cell64_host[k];
+    constexpr int threads = 256;
+    model_positions_f64_kernel<<<grid_for(n_atoms, threads), threads, 0, as_stream(stream)>>>(positions, n_atoms, cell,
+                                                                                           cell64, out);
+    return check_launch();
 }
 
 }  // extern "C"

@@ -198,7 +198,7 @@ class FixedCapacityGraphBuilder:
                  n_dummy: int = 0, device="cuda", candidate_cutoff: float | None = None,
                  padding: PaddingRule | None = None, replicas: int = 1, max_neighbors: int | None = None,
                  minimum_image: bool = False, candidates_from: "FixedCapacityGraphBuilder | None" = None,
-                 **unused) -> None:
+                 positions_dtype: torch.dtype = torch.float32, **unused) -> None:
         self.edges_only = line_graph_cutoff is None
         if pbc is not None and not bool(torch.as_tensor(pbc).all()):
             raise ValueError("this build implements fully periodic cells")
@@ -219,6 +219,9 @@ class FixedCapacityGraphBuilder:
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise _lib.FastMDLibraryError("the graph builders run on CUDA devices only")
+        if positions_dtype not in (torch.float32, torch.float64):
+            raise ValueError(f"positions_dtype must be float32 or float64, got {positions_dtype}")
+        self.positions_dtype = positions_dtype
         self.minimum_image = bool(minimum_image)
         self.padding = padding
         self.cell = cell.detach().to(device=self.device, dtype=torch.float32).reshape(3, 3).contiguous()
@@ -259,9 +262,19 @@ class FixedCapacityGraphBuilder:
         self._refilter_ws = torch.empty(max(int(nbytes.value), 1), dtype=torch.uint8, device=dev)
         self.positions32 = torch.zeros(N, 3, dtype=torch.float32, device=dev)
         rows = N + self.n_dummy  # sink rows after the real atoms (at the origin, species 1)
+        # float64 positions (fixed_capacity_builder.py:2315): the edges come from the float32 wrap of the
+        # rounded coordinates; the published positions are the float64 coordinates minus the same whole
+        # lattice vectors of the float64 cell (the caller's cell in float64)
+        self.float64 = positions_dtype == torch.float64
+        if self.float64:
+            cell64 = cell.detach().to(dtype=torch.float64).reshape(3, 3)
+            self._cell64_host = np.ascontiguousarray(cell64.cpu().numpy().reshape(9))
+            self._cell64_ptr = self._cell64_host.ctypes.data_as(ctypes.c_void_p)
+            self.wrapped32 = torch.zeros(N, 3, dtype=torch.float32, device=dev)
+            self._positions64 = torch.zeros(N, 3, dtype=torch.float64, device=dev)
         self.batch = GraphBatch(
-            positions=torch.zeros(rows, 3, dtype=torch.float32, device=dev),
-            cell=self.cell,
+            positions=torch.zeros(rows, 3, dtype=positions_dtype, device=dev),
+            cell=cell64.to(dev).contiguous() if self.float64 else self.cell,
             species=torch.cat([species.repeat(self.replicas), torch.ones(self.n_dummy, **i32)]),
             n_real=N,
             edge_index=torch.zeros(E, 2, **i32),
@@ -314,7 +327,7 @@ class FixedCapacityGraphBuilder:
             atom_graph_cutoff=self.atom_graph_cutoff, line_graph_cutoff=self.line_graph_cutoff,
             n_dummy=self.n_dummy, device=self.device, candidate_cutoff=self.candidate_cutoff,
             padding=self.padding, replicas=self.replicas, max_neighbors=self.buffer_max,
-            minimum_image=self.minimum_image)
+            minimum_image=self.minimum_image, positions_dtype=self.positions_dtype)
 
     # ------------------------------------------------------------------ inputs
     def _positions(self, positions: Tensor) -> Tensor:
@@ -361,16 +374,24 @@ class FixedCapacityGraphBuilder:
         if flags is None:
             flags = self.flags
             flags.copy_(self.refresh_flags)
+        wrapped = self.wrapped32 if self.float64 else self.batch.positions
         call("fmd_refilter_edges", ptr(pos), self._cell_ptr, self.n_atoms, self.replicas,
              ptr(self.reference_positions), ptr(self.reference_wraps), ptr(self.cand_nbr), ptr(self.cand_shift),
              ptr(self.cand_count), self.buffer_max, self.atom_graph_cutoff, self.skin, self.e_capacity,
-             self._pad_image_host, int(self.minimum_image), ptr(self.batch.positions), ptr(self.wrap_delta), ptr(self.batch.edge_index),
-             ptr(self.batch.edge_image), ptr(self.batch.recv_off), ptr(self.batch.send_off),
+             self._pad_image_host, int(self.minimum_image), ptr(wrapped), ptr(self.wrap_delta),
+             ptr(self.batch.edge_index), ptr(self.batch.edge_image), ptr(self.batch.recv_off), ptr(self.batch.send_off),
              ptr(self.batch.send_perm), ptr(self.batch.n_edges), ptr(self.max_displacement), ptr(self._refilter_ws),
              self._refilter_ws.numel(), ptr(flags), stream(self.device))
+        if self.float64:
+            p64 = positions
+            if not (p64.dtype == torch.float64 and p64.is_contiguous() and p64.device == self.device):
+                p64 = self._positions64
+                p64.copy_(positions)
+            call("fmd_model_positions_f64", ptr(p64), self.n_real, self._cell_ptr, self._cell64_ptr,
+                 ptr(self.batch.positions), stream(self.device))
         if not self.edges_only:
             b = self.batch
-            call("fmd_bond_graph", ptr(b.positions), self._cell_ptr, self.n_real, ptr(b.edge_index), ptr(b.edge_image),
+            call("fmd_bond_graph", ptr(wrapped), self._cell_ptr, self.n_real, ptr(b.edge_index), ptr(b.edge_image),
                  ptr(b.n_edges), self.u_capacity, self.t_capacity, self.line_graph_cutoff,
                  0 if self.padding.kind == "sink_atoms" else 1, self.n_dummy, self._bond_pad_image, ptr(self._bond_ws),
                  self._bond_ws.numel(), ptr(b.directed2undirected), ptr(b.undirected2directed), ptr(b.line_graph),

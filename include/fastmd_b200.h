@@ -251,6 +251,18 @@ FMD_API fmd_status fmd_neighbor_list(const float* positions, const float* cell_h
                                      int64_t* offsets, void* workspace, size_t workspace_bytes,
                                      int32_t* flags, void* stream);
 
+/* Float64 model positions of a float64 build: out[i] = p[i] - ((w0 c64[0] +
+ * w1 c64[1]) + w2 c64[2]) (rows of the float64 cell, each operation rounded),
+ * w = floor(float32(p[i]) @ inv(cell)) the whole lattice vectors of the
+ * re-filter's float32 wrap (cell_host float32 row-major, its inverse the
+ * float64 inverse rounded once), so the float64 positions and the float32
+ * edges describe the same images. positions, out [n_atoms, 3] float64.
+ * Replaces the float64 part of _float64_prologue_kernel
+ * (fastmd/graph/fixed_capacity_builder.py:464) and the float64 addmm of the
+ * build (:2266). */
+FMD_API fmd_status fmd_model_positions_f64(const double* positions, int64_t n_atoms, const float* cell_host,
+                                           const double* cell64_host, double* out, void* stream);
+
 /* ------------------------------------------- dense layers (D2), IEEE FP32 */
 
 /* y[m, n] (=|+=) act(a'[m, :] . op(w) + bias) on the CUDA cores, IEEE FP32,

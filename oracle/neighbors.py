@@ -178,3 +178,23 @@ def estimate_max_neighbors(cutoff, atomic_density=0.35, safety_factor=5.0):
         return 0
     expected = max(1, safety_factor * atomic_density * (4.0 / 3.0) * math.pi * cutoff**3)
     return int(math.ceil(expected / 16)) * 16
+
+
+def float64_prologue(positions64, cell64, reference32, reference_wraps, skin, inv_cell=None):
+    """The float64 build's prologue (``_float64_prologue_kernel``, fixed_capacity_builder.py:464):
+    the float32 wrap of the rounded coordinates ``q`` (``wrap``), the float64 model positions
+    ``p - ((w0 c[0] + w1 c[1]) + w2 c[2])`` (the same whole lattice vectors of the float64 cell),
+    the wrap delta against the refresh, the largest float32 displacement ``q - reference`` and the
+    skin test ``2 max <= skin + 1e-6``. Returns a dict of those arrays."""
+    p = np.asarray(positions64, np.float64)
+    c64 = np.asarray(cell64, np.float64)
+    q = p.astype(f32)
+    wrapped, wraps, frac = wrap(q, c64.astype(f32), inv_cell)
+    v = wraps.astype(np.float64)
+    model = p - ((v[:, 0:1] * c64[0] + v[:, 1:2] * c64[1]) + v[:, 2:3] * c64[2])
+    d = (q - np.asarray(reference32, f32)).astype(f32)
+    dd = ((d[:, 0] * d[:, 0] + d[:, 1] * d[:, 1]).astype(f32) + d[:, 2] * d[:, 2]).astype(f32)
+    largest = np.sqrt(dd.max(initial=f32(0))).astype(f32)
+    return {"wrapped": wrapped, "frac": frac, "model_positions": model,
+            "wrap_delta": (wraps - np.asarray(reference_wraps, np.int32)).astype(np.int32),
+            "max_displacement": largest, "candidate_valid": bool(largest * f32(2) <= f32(skin + 1.0e-6))}

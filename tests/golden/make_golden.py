@@ -25,7 +25,10 @@ used) and runs, on CPU:
   undirected-pair expansion ``_directed_pair_average_fwd/_bwd`` / ``_undirected_pair_expand_fwd/_bwd``
   (fastmd/models/matris/op/triton_directed_pair_aggregate.py:61/:83/:105/:127), the
   residual add ``_residual_add_fwd`` / ``_residual_add_bwd``
-  (fastmd/models/matris/op/triton_residual_add.py:40/:64), and the
+  (fastmd/models/matris/op/triton_residual_add.py:40/:64), the float64 build prologue
+  ``_float64_prologue_kernel`` (fastmd/graph/fixed_capacity_builder.py:464), the fixed-capacity
+  MatRIS bond graph (the builder's ``_materialize_pairs`` / ``_materialize_line_graph`` /
+  ``_substitute_overflow_topology``, :2001/:2101/:2163, called unbound on a stand-in), and the
   fixed-capacity re-filter ``_count_neighbors_kernel`` /
   ``_materialize_neighbors_kernel`` (fastmd/graph/fixed_capacity_builder.py:98/:189)
   on candidate lists of a dense search, followed by the reference's
@@ -683,6 +686,47 @@ def bond_graph_cases(torch, fcb):
     return out
 
 
+def float64_cases(torch, fcb):
+    """The float64 edges-only build's prologue, ``_float64_prologue_kernel`` (fixed_capacity_builder.py:464):
+    float32 wrap of the rounded coordinates, the float64 model positions (coordinates minus the same whole
+    lattice vectors of the float64 cell), the wrap delta and the skin test against a refresh snapshot, on
+    a triclinic cell and the perovskite's cubic one, coordinates spread over several lattice images."""
+    out = {}
+    rng = np.random.default_rng(41)
+    cells = {"tric": np.array([[7.5, 0.0, 0.0], [1.9, 8.1, 0.0], [-1.2, 2.3, 9.4]]),
+             "cubic": np.eye(3) * 18.6}
+    for tag, cell64 in cells.items():
+        n = 97
+        frac = rng.uniform(-1.5, 2.5, (n, 3))
+        ref64 = frac @ cell64
+        pos64 = ref64 + rng.normal(0.0, 0.15, (n, 3))  # some atoms cross a cell face since the refresh
+        if tag == "cubic":
+            pos64[5] += 0.9 * cell64[0]  # and one moves far beyond half the skin
+        cell32 = torch.from_numpy(cell64.astype(np.float32))
+        inv32 = torch.linalg.inv(cell32.double()).float()
+        q_ref = torch.from_numpy(ref64.astype(np.float32))
+        ref_wraps = torch.floor((q_ref.unsqueeze(-1) * inv32.unsqueeze(-3)).sum(dim=-2)).to(torch.int32)
+        frac_out = torch.zeros(n, 3)
+        wrapped = torch.zeros(n, 3)
+        wrap_delta = torch.zeros(n, 3, dtype=torch.int32)
+        model = torch.zeros(n, 3, dtype=torch.float64)
+        max_disp = torch.zeros(1)
+        valid = torch.zeros(1, dtype=torch.bool)
+        iso = torch.zeros(1, dtype=torch.int32)
+        skin = 2.0
+        fcb._float64_prologue_kernel[(1,)](
+            torch.from_numpy(pos64), inv32.contiguous(), cell32.contiguous(), torch.from_numpy(cell64).contiguous(),
+            q_ref, ref_wraps, torch.ones(1, dtype=torch.bool), frac_out, wrapped, wrap_delta, model, max_disp, valid,
+            iso, skin + 1.0e-6, N=n, BLOCK=128)
+        out.update({f"f64_{tag}_cell": cell64, f"f64_{tag}_positions": pos64, f"f64_{tag}_reference": ref64,
+                    f"f64_{tag}_inv32": inv32.numpy(), f"f64_{tag}_ref_wraps": ref_wraps.numpy(),
+                    f"f64_{tag}_frac": frac_out.numpy(), f"f64_{tag}_wrapped": wrapped.numpy(),
+                    f"f64_{tag}_wrap_delta": wrap_delta.numpy(), f"f64_{tag}_model_positions": model.numpy(),
+                    f"f64_{tag}_max_displacement": max_disp.numpy(), f"f64_{tag}_candidate_valid": valid.numpy(),
+                    f"f64_{tag}_skin": np.array([skin])})
+    return out
+
+
 def radial_cases(torch):
     """The reference's radial basis (fastmd/models/matris/basis_function.py:139 BesselExpansion with the
     PolynomialEnvelope of :31) at the MACE setting (8 functions, rc 6, p 5) and MatRIS's (7, 6, 8)."""
@@ -732,6 +776,7 @@ def main(reference: str, only: list[str]) -> None:
         "pair_aggregate": lambda: pair_aggregate_cases(torch, pa),
         "residual_add": lambda: residual_add_cases(torch, ra),
         "bond_graph": lambda: bond_graph_cases(torch, fcb),
+        "float64": lambda: float64_cases(torch, fcb),
     }
     for name, make in fixtures.items():
         if not only or name in only:
