@@ -356,12 +356,17 @@ __global__ void __launch_bounds__(128) message_fused_kernel(GraphArgs g, FusedWe
 
 // ------------------------------------------------------------ node kernels
 //
-// A CTA of 4*C threads owns a group of kG = 4 same-element atoms. Channel
+// A CTA of 4*C threads owns a group of G same-element atoms: G = kG = 4
+// (the element groups of the host), or G = 1 (each entry of the group table
+// on its own CTA, empty entries skipped) when there are fewer groups than SMs,
+// so a small system fills the GPU with 4x the CTAs. Channel
 // mixings [rows x C] . [C x C] split the reduction over c into 4 quarters
 // (thread (k, q) = output channel k, quarter q): each thread issues its 32
 // weight loads at once, so a matrix costs one L2 round trip; the quarters
 // are combined in a fixed order in shared memory. Elementwise phases use
-// thread (k, g) = channel k of atom g.
+// thread (k, g) = channel k of atom g (g >= G: idle rows of the 4-atom
+// shared-memory tiles, never written to global memory). The arithmetic of an
+// atom's row does not depend on G: both forms give the same bits.
 
 constexpr int kGV = kG * 3;
 constexpr int kQ = 4;  // reduction quarters (== kG: the same threads serve both layouts)
@@ -429,20 +434,29 @@ __device__ __forceinline__ float atom_sum(float x, float (*sc)[32]) {
     return y;
 }
 
+// the atoms of work unit grp: G consecutive entries of the group table, -1 past them
+template <int G>
 __device__ __forceinline__ void group_atoms(const FusedState& st, int64_t grp, int (&atoms)[kG]) {
 #pragma unroll
-    for (int g = 0; g < kG; ++g) atoms[g] = st.groups[grp * kG + g];
+    for (int g = 0; g < kG; ++g) atoms[g] = g < G ? st.groups[grp * G + g] : -1;
+}
+
+// work units of the node kernels: groups of 4, or single entries of the group table
+template <int G>
+__device__ __forceinline__ int64_t node_units(const FusedState& st) {
+    return st.n_groups * (kG / G);
 }
 
 // forward node update of a non-last layer L
-template <int C>
+template <int C, int G>
 __global__ void __launch_bounds__(kQ * C) node_fwd_kernel(FusedWeights w, FusedState st, int L) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     NodeSmem<C>& m = *reinterpret_cast<NodeSmem<C>*>(smem_raw);
     const int k = threadIdx.x % C, g = threadIdx.x / C;
-    for (int64_t grp = blockIdx.x; grp < st.n_groups; grp += gridDim.x) {
+    for (int64_t grp = blockIdx.x; grp < node_units<G>(st); grp += gridDim.x) {
         int atoms[kG];
-        group_atoms(st, grp, atoms);
+        group_atoms<G>(st, grp, atoms);
+        if (atoms[0] < 0) continue;  // an empty entry of the table (uniform over the CTA)
         const int64_t z = st.elem[atoms[0]];
         const int my = atoms[g];
         const int64_t i = my < 0 ? atoms[0] : my;
@@ -456,8 +470,8 @@ __global__ void __launch_bounds__(kQ * C) node_fwd_kernel(FusedWeights w, FusedS
             for (int c = 0; c < 3; ++c) m.tv[g * 3 + c][k] = st.v_out[L - 1][i * 3 * C + c * C + k];
         }
         __syncthreads();
-        mix_rows<C, kG, kGV>(m.s, w.lin0t[L], m.v, w.lin1t[L], m.s, m.v, m.red);
-        if (L > 0) mix_rows<C, kG, kGV>(m.t, w.skip0[L] + z * C * C, m.tv, w.skip1[L] + z * C * C, m.t, m.tv, m.red);
+        mix_rows<C, G, 3 * G>(m.s, w.lin0t[L], m.v, w.lin1t[L], m.s, m.v, m.red);
+        if (L > 0) mix_rows<C, G, 3 * G>(m.t, w.skip0[L] + z * C * C, m.tv, w.skip1[L] + z * C * C, m.t, m.tv, m.red);
         // symmetric contraction (thread (k, g))
         const float aa = m.s[g][k];
         const float vx = m.v[g * 3][k], vy = m.v[g * 3 + 1][k], vz = m.v[g * 3 + 2][k];
@@ -478,7 +492,7 @@ __global__ void __launch_bounds__(kQ * C) node_fwd_kernel(FusedWeights w, FusedS
         m.v[g * 3 + 1][k] = cc * vy;
         m.v[g * 3 + 2][k] = cc * vz;
         __syncthreads();
-        mix_rows<C, kG, kGV>(m.s, w.out0t[L], m.v, w.out1t[L], m.s, m.v, m.red);
+        mix_rows<C, G, 3 * G>(m.s, w.out0t[L], m.v, w.out1t[L], m.s, m.v, m.red);
         float so = m.s[g][k];
         float vo[3] = {m.v[g * 3][k], m.v[g * 3 + 1][k], m.v[g * 3 + 2][k]};
         if (L > 0) {
@@ -501,7 +515,7 @@ __global__ void __launch_bounds__(kQ * C) node_fwd_kernel(FusedWeights w, FusedS
         for (int c = 0; c < 3; ++c) m.v[g * 3 + c][k] = vo[c];
         __syncthreads();
         // the next layer's up-mixing
-        mix_rows<C, kG, kGV>(m.s, w.up0t[L + 1], m.v, w.up1t[L + 1], m.s, m.v, m.red);
+        mix_rows<C, G, 3 * G>(m.s, w.up0t[L + 1], m.v, w.up1t[L + 1], m.s, m.v, m.red);
         if (my >= 0) {
             st.s_t[L + 1][my * int64_t(C) + k] = m.s[g][k];
 #pragma unroll
@@ -511,16 +525,17 @@ __global__ void __launch_bounds__(kQ * C) node_fwd_kernel(FusedWeights w, FusedS
 }
 
 // the last layer: node update, readout, node energies, and the backward to dA(L)
-template <int C>
+template <int C, int G>
 __global__ void __launch_bounds__(kQ * C) node_last_kernel(FusedWeights w, FusedState st, int L) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     NodeSmem<C>& m = *reinterpret_cast<NodeSmem<C>*>(smem_raw);
     const int k = threadIdx.x % C, g = threadIdx.x / C;
     const int RH = w.readout_hidden;
     for (int idx = threadIdx.x; idx < RH * C; idx += kQ * C) m.ra[idx / C][idx % C] = w.ra[idx];
-    for (int64_t grp = blockIdx.x; grp < st.n_groups; grp += gridDim.x) {
+    for (int64_t grp = blockIdx.x; grp < node_units<G>(st); grp += gridDim.x) {
         int atoms[kG];
-        group_atoms(st, grp, atoms);
+        group_atoms<G>(st, grp, atoms);
+        if (atoms[0] < 0) continue;  // an empty entry of the table (uniform over the CTA)
         const int64_t z = st.elem[atoms[0]];
         const int my = atoms[g];
         const int64_t i = my < 0 ? atoms[0] : my;
@@ -530,8 +545,8 @@ __global__ void __launch_bounds__(kQ * C) node_last_kernel(FusedWeights w, Fused
         for (int c = 0; c < 3; ++c) m.v[g * 3 + c][k] = st.A1[L][i * 3 * C + c * C + k];
         m.t[g][k] = L > 0 ? st.s_out[L - 1][i * C + k] : 0.f;
         __syncthreads();
-        mix_rows<C, kG, kGV>(m.s, w.lin0t[L], m.v, w.lin1t[L], m.s, m.v, m.red);
-        if (L > 0) mix_rows<C, kG, 0>(m.t, w.skip0[L] + z * C * C, nullptr, nullptr, m.t, nullptr, m.red);
+        mix_rows<C, G, 3 * G>(m.s, w.lin0t[L], m.v, w.lin1t[L], m.s, m.v, m.red);
+        if (L > 0) mix_rows<C, G, 0>(m.t, w.skip0[L] + z * C * C, nullptr, nullptr, m.t, nullptr, m.red);
         const float aa = m.s[g][k];
         const float vx = m.v[g * 3][k], vy = m.v[g * 3 + 1][k], vz = m.v[g * 3 + 2][k];
         const float q = (vx * vx + vy * vy) + vz * vz;
@@ -540,7 +555,7 @@ __global__ void __launch_bounds__(kQ * C) node_last_kernel(FusedWeights w, Fused
         __syncthreads();
         m.s[g][k] = b0;
         __syncthreads();
-        mix_rows<C, kG, 0>(m.s, w.out0t[L], nullptr, nullptr, m.s, nullptr, m.red);
+        mix_rows<C, G, 0>(m.s, w.out0t[L], nullptr, nullptr, m.s, nullptr, m.red);
         const float so = m.s[g][k] + (L > 0 ? m.t[g][k] : 0.f);
         float e0_term = 0.f;
         if (L == 0) e0_term = atom_sum<C>(so * w.r0[k], m.sc);  // a one-layer model: readout 0 as well
@@ -548,7 +563,7 @@ __global__ void __launch_bounds__(kQ * C) node_last_kernel(FusedWeights w, Fused
         m.s[g][k] = so;
         __syncthreads();
         // readout MLP: pre_j = s . ra_j
-        for (int idx = threadIdx.x; idx < kG * RH; idx += kQ * C) {
+        for (int idx = threadIdx.x; idx < G * RH; idx += kQ * C) {
             const int gg = idx / RH, j = idx % RH;
             float acc = 0.f;
             for (int c = 0; c < C; ++c) acc = fmaf(m.s[gg][c], m.ra[j][c], acc);
@@ -571,10 +586,10 @@ __global__ void __launch_bounds__(kQ * C) node_last_kernel(FusedWeights w, Fused
         m.t[g][k] = ds;
         __syncthreads();
         if (L > 0) {
-            mix_rows<C, kG, 0>(m.t, w.skip0t[L] + z * C * C, nullptr, nullptr, m.v, nullptr, m.red);
+            mix_rows<C, G, 0>(m.t, w.skip0t[L] + z * C * C, nullptr, nullptr, m.v, nullptr, m.red);
             if (my >= 0) st.ds_skip[L][my * int64_t(C) + k] = m.v[g][k];
         }
-        mix_rows<C, kG, 0>(m.t, w.out0[L], nullptr, nullptr, m.t, nullptr, m.red);
+        mix_rows<C, G, 0>(m.t, w.out0[L], nullptr, nullptr, m.t, nullptr, m.red);
         const float db0 = m.t[g][k];
         const float gq = db0 * (p0[2 * C] + p0[4 * C] * aa);
         const float da = db0 * (((p0[0] + 2.f * p0[C] * aa) + 3.f * p0[3 * C] * aa * aa) + p0[4 * C] * q);
@@ -584,7 +599,7 @@ __global__ void __launch_bounds__(kQ * C) node_last_kernel(FusedWeights w, Fused
         m.v[g * 3 + 1][k] = 2.f * gq * vy;
         m.v[g * 3 + 2][k] = 2.f * gq * vz;
         __syncthreads();
-        mix_rows<C, kG, kGV>(m.s, w.lin0[L], m.v, w.lin1[L], m.s, m.v, m.red);
+        mix_rows<C, G, 3 * G>(m.s, w.lin0[L], m.v, w.lin1[L], m.s, m.v, m.red);
         if (my >= 0) {
             st.dA0[L][my * int64_t(C) + k] = m.s[g][k];
 #pragma unroll
@@ -666,26 +681,33 @@ __global__ void __launch_bounds__(128) msg_bwd_edge_kernel(GraphArgs g, FusedWei
 // per sender: the gathered rows' gradient of layer L (ds_t, dv_t), the up-mixing backward into
 // layer L-1's outputs, and layer L-1's node backward (to dA(L-1)). One atom group per CTA; the
 // C threads of atom g reduce its sender run (warps over edges).
-template <int C>
+template <int C, int G>
 __global__ void __launch_bounds__(kQ * C) sender_node_kernel(GraphArgs gr, FusedWeights w, FusedState st, int L) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     NodeSmem<C>& m = *reinterpret_cast<NodeSmem<C>*>(smem_raw);
-    constexpr int CPL = C / 32, NW = C / 32;  // warps per atom
+    // the C / 32 warps of atom g reduce its sender run (the same order whatever G: the results do not
+    // depend on the grouping); with G < kG the warps of the idle atom slots skip it
+    constexpr int CPL = C / 32, NW = C / 32;
     const int k = threadIdx.x % C, g = threadIdx.x / C;
-    const int lane = threadIdx.x & 31, wa = k >> 5;  // warp index within the atom
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int ga = warp / NW, wa = warp % NW;  // ga == g
+    float (*redf)[C] = reinterpret_cast<float (*)[C]>(&m.red[0][0][0]);  // [4 * warps][C] partials
     const int P = 4;
     const float* R = st.R[L];
     const int Lp = L - 1;
-    for (int64_t grp = blockIdx.x; grp < st.n_groups; grp += gridDim.x) {
+    for (int64_t grp = blockIdx.x; grp < node_units<G>(st); grp += gridDim.x) {
         int atoms[kG];
-        group_atoms(st, grp, atoms);
+        group_atoms<G>(st, grp, atoms);
+        if (atoms[0] < 0) continue;  // an empty entry of the table (uniform over the CTA)
         const int64_t z = st.elem[atoms[0]];
         const int my = atoms[g];
         const int64_t j = my < 0 ? atoms[0] : my;
+        const int mw = atoms[ga];
+        const int64_t jw = mw < 0 ? atoms[0] : mw;
         float ds[CPL], dx[CPL], dy[CPL], dz[CPL];
 #pragma unroll
         for (int qq = 0; qq < CPL; ++qq) ds[qq] = dx[qq] = dy[qq] = dz[qq] = 0.f;
-        for (int64_t t = gr.send_off[j] + wa; t < gr.send_off[j + 1]; t += NW) {
+        for (int64_t t = gr.send_off[jw] + wa; ga < G && t < gr.send_off[jw + 1]; t += NW) {
             const int64_t e = gr.send_perm[t];
             const int64_t i = gr.edge_index[2 * e];
             const float4 y = st.ysh[e];
@@ -706,28 +728,29 @@ __global__ void __launch_bounds__(kQ * C) sender_node_kernel(GraphArgs gr, Fused
             }
         }
         __syncthreads();
-        // warp partials of atom g -> red[g-th quarter block] (reuse red as [warp][4][C] per atom)
+        // warp partials of atom ga -> rows (ga * NW + wa) * 4 + (s, x, y, z) of the partial block
 #pragma unroll
         for (int qq = 0; qq < CPL; ++qq) {
             const int kk = lane * CPL + qq;
-            m.red[g][wa * 4 + 0][kk] = ds[qq];
-            m.red[g][wa * 4 + 1][kk] = dx[qq];
-            m.red[g][wa * 4 + 2][kk] = dy[qq];
-            m.red[g][wa * 4 + 3][kk] = dz[qq];
+            redf[(ga * NW + wa) * 4 + 0][kk] = ds[qq];
+            redf[(ga * NW + wa) * 4 + 1][kk] = dx[qq];
+            redf[(ga * NW + wa) * 4 + 2][kk] = dy[qq];
+            redf[(ga * NW + wa) * 4 + 3][kk] = dz[qq];
         }
         __syncthreads();
         {
             float sum[4] = {0.f, 0.f, 0.f, 0.f};
-            for (int wv = 0; wv < NW; ++wv)
+            if (g < G)
+                for (int wv = 0; wv < NW; ++wv)
 #pragma unroll
-                for (int c = 0; c < 4; ++c) sum[c] += m.red[g][wv * 4 + c][k];
+                    for (int c = 0; c < 4; ++c) sum[c] += redf[(g * NW + wv) * 4 + c][k];
             m.s[g][k] = sum[0];
 #pragma unroll
             for (int c = 0; c < 3; ++c) m.v[g * 3 + c][k] = sum[1 + c];
         }
         __syncthreads();
         // up-mixing backward into layer Lp's outputs, plus the skip and readout parts
-        mix_rows<C, kG, kGV>(m.s, w.up0[L], m.v, w.up1[L], m.s, m.v, m.red);
+        mix_rows<C, G, 3 * G>(m.s, w.up0[L], m.v, w.up1[L], m.s, m.v, m.red);
         float dsi = m.s[g][k];
         float dvi[3] = {m.v[g * 3][k], m.v[g * 3 + 1][k], m.v[g * 3 + 2][k]};
         if (st.ds_skip[L]) dsi += st.ds_skip[L][j * C + k];
@@ -741,9 +764,9 @@ __global__ void __launch_bounds__(kQ * C) sender_node_kernel(GraphArgs gr, Fused
         for (int c = 0; c < 3; ++c) m.tv[g * 3 + c][k] = dvi[c];
         __syncthreads();
         // layer Lp: out-mixing backward (into s/v) and skip backward (t/tv in place)
-        mix_rows<C, kG, kGV>(m.t, w.out0[Lp], m.tv, w.out1[Lp], m.s, m.v, m.red);
+        mix_rows<C, G, 3 * G>(m.t, w.out0[Lp], m.tv, w.out1[Lp], m.s, m.v, m.red);
         if (Lp > 0) {
-            mix_rows<C, kG, kGV>(m.t, w.skip0t[Lp] + z * C * C, m.tv, w.skip1t[Lp] + z * C * C, m.t, m.tv, m.red);
+            mix_rows<C, G, 3 * G>(m.t, w.skip0t[Lp] + z * C * C, m.tv, w.skip1t[Lp] + z * C * C, m.t, m.tv, m.red);
             if (my >= 0) {
                 st.ds_skip[Lp][my * int64_t(C) + k] = m.t[g][k];
 #pragma unroll
@@ -771,7 +794,7 @@ __global__ void __launch_bounds__(kQ * C) sender_node_kernel(GraphArgs gr, Fused
         m.v[g * 3 + 1][k] = cc * by + 2.f * gq * vy;
         m.v[g * 3 + 2][k] = cc * bz + 2.f * gq * vz;
         __syncthreads();
-        mix_rows<C, kG, kGV>(m.s, w.lin0[Lp], m.v, w.lin1[Lp], m.s, m.v, m.red);
+        mix_rows<C, G, 3 * G>(m.s, w.lin0[Lp], m.v, w.lin1[Lp], m.s, m.v, m.red);
         if (my >= 0) {
             st.dA0[Lp][my * int64_t(C) + k] = m.s[g][k];
 #pragma unroll
@@ -1141,7 +1164,10 @@ fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeigh
     const int64_t n_tiles = (ea.n_edges + kTF - 1) / kTF;
     const int edge_grid = int(n_tiles < int64_t(kNumSMs) * 8 ? n_tiles : int64_t(kNumSMs) * 8);
     const int atom_grid = int(ga.n_atoms < int64_t(kNumSMs) * 16 ? ga.n_atoms : int64_t(kNumSMs) * 16);
-    const int group_grid = int(st.n_groups < int64_t(kNumSMs) * 16 ? st.n_groups : int64_t(kNumSMs) * 16);
+    // fewer groups than SMs: one CTA per entry of the group table (4x the CTAs, the same results)
+    const bool single = st.n_groups < kNumSMs;
+    const int64_t units = single ? st.n_groups * kG : st.n_groups;
+    const int group_grid = int(units < int64_t(kNumSMs) * 16 ? units : int64_t(kNumSMs) * 16);
     const int64_t b_tiles = (ea.n_edges + kTB - 1) / kTB;
     const int bwd_grid = int(b_tiles < int64_t(kNumSMs) * 8 ? b_tiles : int64_t(kNumSMs) * 8);
     const size_t node_smem = sizeof(NodeSmem<C>);
@@ -1149,17 +1175,18 @@ fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeigh
     fmd_status stt;
     if ((stt = grant((const void*)edge_fwd_kernel<C>, sizeof(EdgeFwdSmem), 3 + 2 * slot)) != FMD_OK) return stt;
     if ((stt = grant((const void*)edge_bwd_kernel<C>, sizeof(EdgeBwdSmem), 4 + 2 * slot)) != FMD_OK) return stt;
-    if ((stt = grant((const void*)node_fwd_kernel<C>, node_smem, slot)) != FMD_OK) return stt;
-    // the three node kernels share one NodeSmem size: grant each (slot bookkeeping per kernel family)
+    // the six node kernels (three, for 4 and 1 atoms per CTA) share one NodeSmem size: grant each once
     {
         static size_t last_granted[3] = {};
         if (node_smem > 48 * 1024 && node_smem > last_granted[slot]) {
-            cudaError_t err = cudaFuncSetAttribute((const void*)node_last_kernel<C>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, int(node_smem));
-            if (err == cudaSuccess)
-                err = cudaFuncSetAttribute((const void*)sender_node_kernel<C>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, int(node_smem));
-            if (err != cudaSuccess) return record_cuda_error(err);
+            const void* kernels[6] = {(const void*)node_fwd_kernel<C, kG>,    (const void*)node_fwd_kernel<C, 1>,
+                                      (const void*)node_last_kernel<C, kG>,   (const void*)node_last_kernel<C, 1>,
+                                      (const void*)sender_node_kernel<C, kG>, (const void*)sender_node_kernel<C, 1>};
+            for (const void* kernel : kernels) {
+                const cudaError_t err =
+                    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(node_smem));
+                if (err != cudaSuccess) return record_cuda_error(err);
+            }
             last_granted[slot] = node_smem;
         }
     }
@@ -1179,12 +1206,21 @@ fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeigh
             if (l == 0) message_fused_kernel<C, 2><<<atom_grid, 128, 0, s>>>(ga, w, st, l);
             else message_fused_kernel<C, 4><<<atom_grid, 128, 0, s>>>(ga, w, st, l);
         }
-        if (l < L - 1 && on(2)) node_fwd_kernel<C><<<group_grid, kQ * C, node_smem, s>>>(w, st, l);
+        if (l < L - 1 && on(2)) {
+            if (single) node_fwd_kernel<C, 1><<<group_grid, kQ * C, node_smem, s>>>(w, st, l);
+            else node_fwd_kernel<C, kG><<<group_grid, kQ * C, node_smem, s>>>(w, st, l);
+        }
     }
-    if (on(3)) node_last_kernel<C><<<group_grid, kQ * C, node_smem, s>>>(w, st, L - 1);
+    if (on(3)) {
+        if (single) node_last_kernel<C, 1><<<group_grid, kQ * C, node_smem, s>>>(w, st, L - 1);
+        else node_last_kernel<C, kG><<<group_grid, kQ * C, node_smem, s>>>(w, st, L - 1);
+    }
     for (int l = L - 1; l >= 1; --l) {
         if (on(4)) msg_bwd_edge_kernel<C, 4><<<atom_grid, 128, 0, s>>>(ga, w, st, l, l != L - 1);
-        if (on(5)) sender_node_kernel<C><<<group_grid, kQ * C, node_smem, s>>>(ga, w, st, l);
+        if (on(5)) {
+            if (single) sender_node_kernel<C, 1><<<group_grid, kQ * C, node_smem, s>>>(ga, w, st, l);
+            else sender_node_kernel<C, kG><<<group_grid, kQ * C, node_smem, s>>>(ga, w, st, l);
+        }
     }
     if (on(4)) msg_bwd_edge_kernel<C, 2><<<atom_grid, 128, 0, s>>>(ga, w, st, 0, L != 1);
     if (tc && b_tiles > 0 && on(6)) {

@@ -185,10 +185,12 @@ def test_fused_step_matches_fp64_oracle(cuda, channels, layers, seed):
     _close(fu.cpu().numpy(), forces.cpu().numpy().astype(np.float64))
 
 
-def test_fused_replica_union_equals_single_systems(cuda):
+@pytest.mark.parametrize("R", [3, 5])
+def test_fused_replica_union_equals_single_systems(cuda, R):
+    """R = 5: the union's 175 atom groups run 4 atoms per CTA, a single system's 35 one atom per CTA
+    (fewer groups than SMs); the results do not depend on the grouping."""
     from fastmd_b200.mace import MACEModel
 
-    R = 3
     systems = [_system(seed) for seed in range(R)]
     cell, numbers = systems[0][1], systems[0][2]
     model = MACEModel(device=cuda)
