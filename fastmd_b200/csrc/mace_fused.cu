@@ -206,10 +206,11 @@ __device__ __forceinline__ int64_t real_edges(const EdgeArgs& a) {
     return n < a.n_edges ? n : a.n_edges;
 }
 
-// R[e][n] = sum_c h3[e][c] W4^T[c][n] for one tile, PC columns (thread columns t, t+256, ...)
+// R[e][n] = sum_c h3[e][c] W4^T[c][n] for one tile, PC columns (thread columns t, t+256, ...), W4^T
+// staged in shared memory
 template <int PC>
-__device__ __forceinline__ void radial_out(const float (*h)[kHS], const float* __restrict__ w4t, float* __restrict__ R,
-                                           int64_t e0, int ne) {
+__device__ __forceinline__ void radial_out(const float (*h)[kHS], const float* w4s, float* __restrict__ R, int64_t e0,
+                                           int ne) {
 #pragma unroll
     for (int n = threadIdx.x; n < PC; n += 256) {
         float acc[kTF];
@@ -217,8 +218,8 @@ __device__ __forceinline__ void radial_out(const float (*h)[kHS], const float* _
         for (int e = 0; e < kTF; ++e) acc[e] = 0.f;
 #pragma unroll 4
         for (int c = 0; c < kH; c += 4) {
-            const float w0 = w4t[(c + 0) * PC + n], w1 = w4t[(c + 1) * PC + n];
-            const float w2 = w4t[(c + 2) * PC + n], w3 = w4t[(c + 3) * PC + n];
+            const float w0 = w4s[(c + 0) * PC + n], w1 = w4s[(c + 1) * PC + n];
+            const float w2 = w4s[(c + 2) * PC + n], w3 = w4s[(c + 3) * PC + n];
 #pragma unroll
             for (int e = 0; e < kTF; ++e) {
                 const float4 x = *reinterpret_cast<const float4*>(&h[e][c]);
@@ -231,11 +232,22 @@ __device__ __forceinline__ void radial_out(const float (*h)[kHS], const float* _
     }
 }
 
-// geometry, radial features and the radial MLP of every layer for one 16-edge tile
+// stage W4^T [kH][PC] of one layer in shared memory (float4 loads issued together)
+template <int PC>
+__device__ __forceinline__ void stage_w4(float* w4s, const float* __restrict__ w4t) {
+    const float4* src = reinterpret_cast<const float4*>(w4t);
+    float4* dst = reinterpret_cast<float4*>(w4s);
+#pragma unroll 8
+    for (int idx = threadIdx.x; idx < kH * PC / 4; idx += 256) dst[idx] = src[idx];
+}
+
+// geometry, radial features and the radial MLP of every layer for one 16-edge tile (the output
+// weights W4^T of the layer staged in shared memory after the struct: kH x 4C floats)
 template <int C>
 __global__ void __launch_bounds__(256) edge_fwd_kernel(EdgeArgs a, FusedWeights w, FusedState st) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     EdgeFwdSmem& m = *reinterpret_cast<EdgeFwdSmem*>(smem_raw);
+    float* w4s = reinterpret_cast<float*>(smem_raw + sizeof(EdgeFwdSmem));
     const int t = threadIdx.x;
     const float pref = sqrtf(2.0f / w.r_max);
     const int64_t n_edges = real_edges(a);
@@ -269,6 +281,8 @@ __global__ void __launch_bounds__(256) edge_fwd_kernel(EdgeArgs a, FusedWeights 
         for (int L = 0; L < w.n_layers; ++L) {
             __syncthreads();
             stage_radial(m.w1, m.w2, m.w3, w, L);
+            if (L == 0) stage_w4<2 * C>(w4s, w.w4t[L]);
+            else stage_w4<4 * C>(w4s, w.w4t[L]);
             __syncthreads();
             for (int idx = t; idx < kTF * kH; idx += 256) {
                 const int e = idx / kH, k = idx % kH;
@@ -281,8 +295,8 @@ __global__ void __launch_bounds__(256) edge_fwd_kernel(EdgeArgs a, FusedWeights 
             __syncthreads();
             hidden_layer<kTF, true>(m.h[1], m.w3, m.h[0], nullptr);
             __syncthreads();
-            if (L == 0) radial_out<2 * C>(m.h[0], w.w4t[L], st.R[L], e0, ne);
-            else radial_out<4 * C>(m.h[0], w.w4t[L], st.R[L], e0, ne);
+            if (L == 0) radial_out<2 * C>(m.h[0], w4s, st.R[L], e0, ne);
+            else radial_out<4 * C>(m.h[0], w4s, st.R[L], e0, ne);
         }
     }
 }
@@ -608,10 +622,12 @@ __global__ void __launch_bounds__(kQ * C) node_last_kernel(FusedWeights w, Fused
     }
 }
 
-// per receiver run: dR(l) and dY (warp per edge, lane channels; dY accumulated over layers)
+// per receiver run: dR(l) and dY (warp per edge, lane channels; dY accumulated over layers); every
+// output is one edge's, so the kMsgBwdWarps warps of a receiver give the same bits in any number
+constexpr int kMsgBwdWarps = 8;
 template <int C, int P>
-__global__ void __launch_bounds__(128) msg_bwd_edge_kernel(GraphArgs g, FusedWeights w, FusedState st, int L,
-                                                           int accumulate_dy) {
+__global__ void __launch_bounds__(32 * kMsgBwdWarps) msg_bwd_edge_kernel(GraphArgs g, FusedWeights w, FusedState st,
+                                                                        int L, int accumulate_dy) {
     constexpr int CPL = C / 32;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float* R = st.R[L];
@@ -627,7 +643,7 @@ __global__ void __launch_bounds__(128) msg_bwd_edge_kernel(GraphArgs g, FusedWei
             gz[q] = st.dA1[L][i * 3 * C + 2 * C + k] * w.inv_avg;
         }
         const int64_t beg = g.recv_off[i], end = g.recv_off[i + 1];
-        for (int64_t e = beg + warp; e < end; e += 4) {
+        for (int64_t e = beg + warp; e < end; e += kMsgBwdWarps) {
             const int64_t j = g.edge_index[2 * e + 1];
             const float4 y = st.ysh[e];
             const float* Re = R + e * (P * C);
@@ -1173,7 +1189,8 @@ fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeigh
     const size_t node_smem = sizeof(NodeSmem<C>);
     const int slot = C == 32 ? 0 : (C == 64 ? 1 : 2);
     fmd_status stt;
-    if ((stt = grant((const void*)edge_fwd_kernel<C>, sizeof(EdgeFwdSmem), 3 + 2 * slot)) != FMD_OK) return stt;
+    const size_t fwd_smem = sizeof(EdgeFwdSmem) + sizeof(float) * kH * 4 * C;  // + the staged W4^T
+    if ((stt = grant((const void*)edge_fwd_kernel<C>, fwd_smem, 3 + 2 * slot)) != FMD_OK) return stt;
     if ((stt = grant((const void*)edge_bwd_kernel<C>, sizeof(EdgeBwdSmem), 4 + 2 * slot)) != FMD_OK) return stt;
     // the six node kernels (three, for 4 and 1 atoms per CTA) share one NodeSmem size: grant each once
     {
@@ -1199,7 +1216,7 @@ fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeigh
         if ((stt = check_launch()) != FMD_OK) return stt;
         if ((stt = radial_tc_forward(w, st, ea.n_edges, C, s)) != FMD_OK) return stt;
     } else if (n_tiles > 0 && on(0)) {
-        edge_fwd_kernel<C><<<edge_grid, 256, sizeof(EdgeFwdSmem), s>>>(ea, w, st);
+        edge_fwd_kernel<C><<<edge_grid, 256, fwd_smem, s>>>(ea, w, st);
     }
     for (int l = 0; l < L; ++l) {
         if (on(1)) {
@@ -1216,13 +1233,13 @@ fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeigh
         else node_last_kernel<C, kG><<<group_grid, kQ * C, node_smem, s>>>(w, st, L - 1);
     }
     for (int l = L - 1; l >= 1; --l) {
-        if (on(4)) msg_bwd_edge_kernel<C, 4><<<atom_grid, 128, 0, s>>>(ga, w, st, l, l != L - 1);
+        if (on(4)) msg_bwd_edge_kernel<C, 4><<<atom_grid, 32 * kMsgBwdWarps, 0, s>>>(ga, w, st, l, l != L - 1);
         if (on(5)) {
             if (single) sender_node_kernel<C, 1><<<group_grid, kQ * C, node_smem, s>>>(ga, w, st, l);
             else sender_node_kernel<C, kG><<<group_grid, kQ * C, node_smem, s>>>(ga, w, st, l);
         }
     }
-    if (on(4)) msg_bwd_edge_kernel<C, 2><<<atom_grid, 128, 0, s>>>(ga, w, st, 0, L != 1);
+    if (on(4)) msg_bwd_edge_kernel<C, 2><<<atom_grid, 32 * kMsgBwdWarps, 0, s>>>(ga, w, st, 0, L != 1);
     if (tc && b_tiles > 0 && on(6)) {
         if ((stt = check_launch()) != FMD_OK) return stt;
         if ((stt = radial_tc_backward(w, st, ea.n_edges, C, s)) != FMD_OK) return stt;
