@@ -1136,28 +1136,55 @@ bool use_radial_tc(const FusedWeights& w, const FusedState& st, int64_t n_edges)
     return true;
 }
 
-// forces F_a = sum over received edges of g_r - sum over sent edges of g_r, and the energies
-__global__ void forces_kernel(GraphArgs g, const float* __restrict__ g_r, const double* __restrict__ node_energy,
-                              int64_t atoms_per_system, float* __restrict__ forces, double* __restrict__ total) {
-    __shared__ double s_part[32];
-    const int64_t sys = blockIdx.x;
-    double acc_e = 0.0;
-    for (int64_t t = threadIdx.x; t < atoms_per_system * 3; t += blockDim.x) {
-        const int64_t a = sys * atoms_per_system + t / 3;
-        const int c = int(t % 3);
-        float f = 0.f;
-        for (int64_t e = g.recv_off[a]; e < g.recv_off[a + 1]; ++e) f += g_r[3 * e + c];
-        for (int64_t s = g.send_off[a]; s < g.send_off[a + 1]; ++s) f -= g_r[3 * int64_t(g.send_perm[s]) + c];
-        forces[3 * a + c] = f;
-        if (c == 0) acc_e += node_energy[a];
+// forces F_a = sum over received edges of g_r - sum over sent edges of g_r (a warp per atom: lanes over
+// the atom's edges, a fixed xor tree over the lanes), and the per-system energy sums (the first CTA of
+// each system, a fixed assignment of atoms to threads): grid (atom chunks, systems)
+constexpr int kForceWarps = 8;
+__global__ void __launch_bounds__(32 * kForceWarps) forces_kernel(GraphArgs g, const float* __restrict__ g_r,
+                                                                  const double* __restrict__ node_energy,
+                                                                  int64_t atoms_per_system, float* __restrict__ forces,
+                                                                  double* __restrict__ total) {
+    __shared__ double s_part[kForceWarps];
+    const int64_t sys = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int64_t la = int64_t(blockIdx.x) * kForceWarps + warp; la < atoms_per_system;
+         la += int64_t(gridDim.x) * kForceWarps) {
+        const int64_t a = sys * atoms_per_system + la;
+        float fx = 0.f, fy = 0.f, fz = 0.f;
+        for (int64_t e = g.recv_off[a] + lane; e < g.recv_off[a + 1]; e += 32) {
+            fx += g_r[3 * e];
+            fy += g_r[3 * e + 1];
+            fz += g_r[3 * e + 2];
+        }
+        for (int64_t t = g.send_off[a] + lane; t < g.send_off[a + 1]; t += 32) {
+            const int64_t e = g.send_perm[t];
+            fx -= g_r[3 * e];
+            fy -= g_r[3 * e + 1];
+            fz -= g_r[3 * e + 2];
+        }
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) {
+            fx += __shfl_xor_sync(0xffffffffu, fx, d);
+            fy += __shfl_xor_sync(0xffffffffu, fy, d);
+            fz += __shfl_xor_sync(0xffffffffu, fz, d);
+        }
+        if (lane == 0) {
+            forces[3 * a] = fx;
+            forces[3 * a + 1] = fy;
+            forces[3 * a + 2] = fz;
+        }
     }
+    if (blockIdx.x != 0) return;
+    double acc_e = 0.0;
+    for (int64_t la = threadIdx.x; la < atoms_per_system; la += blockDim.x)
+        acc_e += node_energy[sys * atoms_per_system + la];
     for (int d = 16; d > 0; d >>= 1) acc_e += __shfl_xor_sync(0xffffffffu, acc_e, d);
-    if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = acc_e;
+    if (lane == 0) s_part[warp] = acc_e;
     __syncthreads();
     if (threadIdx.x == 0) {
-        double s = 0.0;
-        for (int wv = 0; wv < (int)(blockDim.x >> 5); ++wv) s += s_part[wv];
-        total[sys] = s;
+        double sum = 0.0;
+        for (int wv = 0; wv < kForceWarps; ++wv) sum += s_part[wv];
+        total[sys] = sum;
     }
 }
 
@@ -1247,7 +1274,12 @@ fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeigh
     } else if (b_tiles > 0 && on(6)) {
         edge_bwd_kernel<C><<<bwd_grid, 256, sizeof(EdgeBwdSmem), s>>>(ea, w, st);
     }
-    if (on(7)) forces_kernel<<<n_systems, 256, 0, s>>>(ga, st.g_r, st.node_energy, atoms_per_system, forces, total);
+    if (on(7)) {
+        int64_t chunks = (atoms_per_system + kForceWarps - 1) / kForceWarps;
+        if (chunks > 64) chunks = 64;
+        forces_kernel<<<dim3(unsigned(chunks), unsigned(n_systems)), 32 * kForceWarps, 0, s>>>(
+            ga, st.g_r, st.node_energy, atoms_per_system, forces, total);
+    }
     return check_launch();
 }
 
