@@ -157,27 +157,28 @@ struct EdgeFwdSmem {
     float w3[kH][kWS];
 };
 
-// stage one layer's radial weights W1^T, W2^T, W3^T in shared memory (float4 loads, unrolled)
+// stage one layer's radial weights W1^T, W2^T, W3^T in shared memory (float4 loads, unrolled; NT threads)
+template <int NT = 256>
 __device__ __forceinline__ void stage_radial(float (*w1)[kH], float (*w2)[kWS], float (*w3)[kWS],
                                              const FusedWeights& w, int L) {
     const float4* g2 = reinterpret_cast<const float4*>(w.w2t[L]);
     const float4* g3 = reinterpret_cast<const float4*>(w.w3t[L]);
 #pragma unroll
-    for (int r = 0; r < kH * kH / 4 / 256; ++r) {
-        const int idx = threadIdx.x + 256 * r;  // float4 index
+    for (int r = 0; r < kH * kH / 4 / NT; ++r) {
+        const int idx = threadIdx.x + NT * r;  // float4 index
         const float4 a = g2[idx], b = g3[idx];
         const int row = (idx * 4) / kH, col = (idx * 4) % kH;
         w2[row][col] = a.x; w2[row][col + 1] = a.y; w2[row][col + 2] = a.z; w2[row][col + 3] = a.w;
         w3[row][col] = b.x; w3[row][col + 1] = b.y; w3[row][col + 2] = b.z; w3[row][col + 3] = b.w;
     }
-    for (int idx = threadIdx.x; idx < w.n_basis * kH; idx += 256) w1[idx / kH][idx % kH] = w.w1t[L][idx];
+    for (int idx = threadIdx.x; idx < w.n_basis * kH; idx += NT) w1[idx / kH][idx % kH] = w.w1t[L][idx];
 }
 
-// out[e][k] = act(sum_c in[e][c] W[c][k]) for the tile (thread k = t % 64, 4 edge groups)
-template <int TE, bool ACT>
+// out[e][k] = act(sum_c in[e][c] W[c][k]) for the tile (thread k = t % 64, NT / 64 edge groups)
+template <int TE, bool ACT, int NT = 256>
 __device__ __forceinline__ void hidden_layer(const float (*in)[kHS], const float (*W)[kWS], float (*out)[kHS],
                                              float (*pre)[kHS]) {
-    constexpr int EPG = TE / 4;
+    constexpr int EPG = TE / (NT / kH);
     const int k = threadIdx.x % kH, eg = threadIdx.x / kH;
     float acc[EPG];
 #pragma unroll
@@ -311,11 +312,14 @@ struct GraphArgs {
     int64_t n_atoms;
 };
 
-// A(l) of every receiver; warps over the receiver's edges, fixed-order combine of the 4 warp partials
+// A(l) of every receiver; kMsgWarps warps over the receiver's edges, fixed-order combine of the warp
+// partials (a pairwise tree)
+constexpr int kMsgWarps = 8;
 template <int C, int P>
-__global__ void __launch_bounds__(128) message_fused_kernel(GraphArgs g, FusedWeights w, FusedState st, int L) {
+__global__ void __launch_bounds__(32 * kMsgWarps) message_fused_kernel(GraphArgs g, FusedWeights w, FusedState st,
+                                                                      int L) {
     constexpr int CPL = C / 32;
-    __shared__ float s_part[4][4][C];
+    __shared__ float s_part[kMsgWarps][4][C];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float* R = st.R[L];
     const float* v_t = st.v_t[L];
@@ -324,7 +328,7 @@ __global__ void __launch_bounds__(128) message_fused_kernel(GraphArgs g, FusedWe
 #pragma unroll
         for (int q = 0; q < CPL; ++q) a0[q] = ax[q] = ay[q] = az[q] = 0.f;
         const int64_t beg = g.recv_off[i], end = g.recv_off[i + 1];
-        for (int64_t e = beg + warp; e < end; e += 4) {
+        for (int64_t e = beg + warp; e < end; e += kMsgWarps) {
             const int64_t j = g.edge_index[2 * e + 1];
             const float4 y = st.ysh[e];
             const float* Re = R + e * (P * C);
@@ -357,10 +361,16 @@ __global__ void __launch_bounds__(128) message_fused_kernel(GraphArgs g, FusedWe
             s_part[warp][3][k] = az[q];
         }
         __syncthreads();
-        for (int idx = threadIdx.x; idx < 4 * C; idx += 128) {
+        for (int idx = threadIdx.x; idx < 4 * C; idx += 32 * kMsgWarps) {
             const int comp = idx / C, k = idx % C;
-            const float v = ((s_part[0][comp][k] + s_part[1][comp][k]) + (s_part[2][comp][k] + s_part[3][comp][k])) *
-                            w.inv_avg;
+            float part[kMsgWarps];
+#pragma unroll
+            for (int wv = 0; wv < kMsgWarps; ++wv) part[wv] = s_part[wv][comp][k];
+#pragma unroll
+            for (int width = kMsgWarps / 2; width > 0; width /= 2)
+#pragma unroll
+                for (int wv = 0; wv < width; ++wv) part[wv] = part[wv] + part[wv + width];
+            const float v = part[0] * w.inv_avg;
             if (comp == 0) st.A0[L][i * C + k] = v;
             else st.A1[L][i * 3 * C + (comp - 1) * C + k] = v;
         }
@@ -821,6 +831,9 @@ __global__ void __launch_bounds__(kQ * C) sender_node_kernel(GraphArgs gr, Fused
 
 // ---------------------------------------------------------------- edge backward
 
+constexpr int kBT = 512;        // threads of the backward edge kernel
+constexpr int kBQ = kBT / kH;   // column blocks of dR . W4 (thread (k, block))
+
 struct EdgeBwdSmem {
     float phi[kTB][16];
     float dphi[kTB][16];
@@ -831,14 +844,14 @@ struct EdgeBwdSmem {
     float w2[kH][kWS];
     float w3[kH][kWS];
     float dR[kTB][kMaxPC];      // the tile's dR rows
-    float red[4][kTB][kH];      // quarter partials of dR . W4
+    float red[kBQ][kTB][kH];    // partials of dR . W4 over kBQ column blocks
 };
 
-// dh3[e][k] = sum_n dR[e][n] W4[n][k]: thread (k, quarter of n), float4 broadcast reads of dR
+// dh3[e][k] = sum_n dR[e][n] W4[n][k]: thread (k, block of n), float4 broadcast reads of dR
 template <int PC>
 __device__ __forceinline__ void radial_out_bwd(const float (*dR)[kMaxPC], const float* __restrict__ W4,
                                                float (*red)[kTB][kH]) {
-    constexpr int NQ = PC / 4;
+    constexpr int NQ = PC / kBQ;
     const int k = threadIdx.x % kH, qt = threadIdx.x / kH;
     float acc[kTB];
 #pragma unroll
@@ -861,10 +874,10 @@ __device__ __forceinline__ void radial_out_bwd(const float (*dR)[kMaxPC], const 
 // stage the tile's dR rows (float4, unrolled)
 template <int PC>
 __device__ __forceinline__ void stage_dr(float (*dst)[kMaxPC], const float* __restrict__ dR, int64_t e0, int ne) {
-    constexpr int V = (kTB * PC / 4 + 255) / 256;  // float4 per thread (the last round partial)
+    constexpr int V = (kTB * PC / 4 + kBT - 1) / kBT;  // float4 per thread (the last round partial)
 #pragma unroll
     for (int r = 0; r < V; ++r) {
-        const int idx = threadIdx.x + 256 * r;
+        const int idx = threadIdx.x + kBT * r;
         if (idx >= kTB * PC / 4) break;
         const int e = (idx * 4) / PC, n = (idx * 4) % PC;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -876,7 +889,7 @@ __device__ __forceinline__ void stage_dr(float (*dst)[kMaxPC], const float* __re
 // out[e][k] = (sum_c g[e][c] W[k][c]) * silu'(pre[e][k]) (the transpose walk of a staged W^T)
 __device__ __forceinline__ void hidden_bwd(const float (*g)[kHS], const float (*W)[kWS], const float (*pre)[kHS],
                                            float (*out)[kHS]) {
-    constexpr int EPG = kTB / 4;
+    constexpr int EPG = kTB / kBQ;
     const int k = threadIdx.x % kH, eg = threadIdx.x / kH;
     float acc[EPG];
 #pragma unroll
@@ -933,7 +946,7 @@ __device__ __forceinline__ void geometry_grad(const FusedWeights& w, const Fused
 // the radial MLP backward of every layer (the forward recomputed from the distances) and the
 // geometry backward: g_r [E][3] = dE/dr_e
 template <int C>
-__global__ void __launch_bounds__(256) edge_bwd_kernel(EdgeArgs a, FusedWeights w, FusedState st) {
+__global__ void __launch_bounds__(kBT) edge_bwd_kernel(EdgeArgs a, FusedWeights w, FusedState st) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     EdgeBwdSmem& m = *reinterpret_cast<EdgeBwdSmem*>(smem_raw);
     const int t = threadIdx.x;
@@ -957,12 +970,12 @@ __global__ void __launch_bounds__(256) edge_bwd_kernel(EdgeArgs a, FusedWeights 
         }
         for (int L = 0; L < w.n_layers; ++L) {
             __syncthreads();
-            stage_radial(m.w1, m.w2, m.w3, w, L);
+            stage_radial<kBT>(m.w1, m.w2, m.w3, w, L);
             if (L == 0) stage_dr<2 * C>(m.dR, st.dR[L], e0, ne);
             else stage_dr<4 * C>(m.dR, st.dR[L], e0, ne);
             __syncthreads();
             // forward recompute
-            for (int idx = t; idx < kTB * kH; idx += 256) {
+            for (int idx = t; idx < kTB * kH; idx += kBT) {
                 const int e = idx / kH, k = idx % kH;
                 float acc = 0.f;
                 for (int n = 0; n < w.n_basis; ++n) acc = fmaf(m.phi[e][n], m.w1[n][k], acc);
@@ -970,16 +983,22 @@ __global__ void __launch_bounds__(256) edge_bwd_kernel(EdgeArgs a, FusedWeights 
                 m.h[0][e][k] = silu_f(acc);
             }
             __syncthreads();
-            hidden_layer<kTB, true>(m.h[0], m.w2, m.h[1], m.p[1]);
+            hidden_layer<kTB, true, kBT>(m.h[0], m.w2, m.h[1], m.p[1]);
             __syncthreads();
-            hidden_layer<kTB, false>(m.h[1], m.w3, m.g[1], m.p[2]);  // only the pre-activation is kept
+            hidden_layer<kTB, false, kBT>(m.h[1], m.w3, m.g[1], m.p[2]);  // only the pre-activation is kept
             if (L == 0) radial_out_bwd<2 * C>(m.dR, w.w4[L], m.red);
             else radial_out_bwd<4 * C>(m.dR, w.w4[L], m.red);
             __syncthreads();
-            for (int idx = t; idx < kTB * kH; idx += 256) {
+            for (int idx = t; idx < kTB * kH; idx += kBT) {
                 const int e = idx / kH, k = idx % kH;
-                const float gsum = (m.red[0][e][k] + m.red[1][e][k]) + (m.red[2][e][k] + m.red[3][e][k]);
-                m.g[0][e][k] = gsum * silu_g(m.p[2][e][k]);
+                float part[kBQ];
+#pragma unroll
+                for (int b = 0; b < kBQ; ++b) part[b] = m.red[b][e][k];
+#pragma unroll
+                for (int width = kBQ / 2; width > 0; width /= 2)
+#pragma unroll
+                    for (int b = 0; b < width; ++b) part[b] = part[b] + part[b + width];
+                m.g[0][e][k] = part[0] * silu_g(m.p[2][e][k]);
             }
             __syncthreads();
             hidden_bwd(m.g[0], m.w3, m.p[1], m.g[1]);
@@ -987,7 +1006,7 @@ __global__ void __launch_bounds__(256) edge_bwd_kernel(EdgeArgs a, FusedWeights 
             hidden_bwd(m.g[1], m.w2, m.p[0], m.g[0]);
             __syncthreads();
             // dphi += g1 . W1 (W1[c][n] = W1^T[n][c])
-            for (int idx = t; idx < kTB * w.n_basis; idx += 256) {
+            for (int idx = t; idx < kTB * w.n_basis; idx += kBT) {
                 const int e = idx / w.n_basis, n = idx % w.n_basis;
                 float acc = 0.f;
 #pragma unroll 16
@@ -1247,8 +1266,8 @@ fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeigh
     }
     for (int l = 0; l < L; ++l) {
         if (on(1)) {
-            if (l == 0) message_fused_kernel<C, 2><<<atom_grid, 128, 0, s>>>(ga, w, st, l);
-            else message_fused_kernel<C, 4><<<atom_grid, 128, 0, s>>>(ga, w, st, l);
+            if (l == 0) message_fused_kernel<C, 2><<<atom_grid, 32 * kMsgWarps, 0, s>>>(ga, w, st, l);
+            else message_fused_kernel<C, 4><<<atom_grid, 32 * kMsgWarps, 0, s>>>(ga, w, st, l);
         }
         if (l < L - 1 && on(2)) {
             if (single) node_fwd_kernel<C, 1><<<group_grid, kQ * C, node_smem, s>>>(w, st, l);
@@ -1272,7 +1291,7 @@ fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeigh
         if ((stt = radial_tc_backward(w, st, ea.n_edges, C, s)) != FMD_OK) return stt;
         edge_geom_bwd_tc_kernel<<<geom_grid, 256, 0, s>>>(ea, w, st);
     } else if (b_tiles > 0 && on(6)) {
-        edge_bwd_kernel<C><<<bwd_grid, 256, sizeof(EdgeBwdSmem), s>>>(ea, w, st);
+        edge_bwd_kernel<C><<<bwd_grid, kBT, sizeof(EdgeBwdSmem), s>>>(ea, w, st);
     }
     if (on(7)) {
         int64_t chunks = (atoms_per_system + kForceWarps - 1) / kForceWarps;
