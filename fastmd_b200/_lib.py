@@ -62,6 +62,7 @@ _SIGNATURES: dict[str, list] = {
     "fmd_line_graph_workspace_bytes": [_I64, _I64, POINTER(c_size_t)],
     "fmd_line_graph": [_P, _P, _P, _I64, _I64, c_float, _I32, _I64, _P, c_size_t, _P, _P, _P, _P],
     "fmd_model_positions_f64": [_P, _I64, _P, _P, _P, _P],
+    "fmd_pad_vector_override": [_P, _I64, _P, _P, _P],
     "fmd_bond_graph_workspace_bytes": [_I64, _I64, POINTER(c_size_t)],
     "fmd_bond_graph": [_P, _P, _I64, _P, _P, _P, _I64, _I64, c_float, _I32, _I64, _P, _P, c_size_t, _P, _P, _P, _P,
                        _P, _P],

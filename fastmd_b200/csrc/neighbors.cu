@@ -925,6 +925,19 @@ __global__ void model_positions_f64_kernel(const double* __restrict__ p, int64_t
     }
 }
 
+// the edge-vector override of exact-rc loop padding (fixed_capacity_builder.py:324
+// _pad_self_loops_kernel, HAS_OVERRIDE): the padded rows' vector, 0 on the real rows
+__global__ void pad_vector_override_kernel(const int64_t* __restrict__ n_edges, int64_t e_capacity, float3 v,
+                                           float* __restrict__ out) {
+    const int64_t total = *n_edges < e_capacity ? *n_edges : e_capacity;
+    for (int64_t r = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; r < e_capacity; r += int64_t(gridDim.x) * blockDim.x) {
+        const bool pad = r >= total;
+        out[3 * r] = pad ? v.x : 0.f;
+        out[3 * r + 1] = pad ? v.y : 0.f;
+        out[3 * r + 2] = pad ? v.z : 0.f;
+    }
+}
+
 // ------------------------------------------------------------------ host
 
 inline size_t align_up(size_t x) { return (x + 255) & ~size_t(255); }
@@ -1331,6 +1344,18 @@ fmd_status fmd_refilter_edges_noalloc(const float* positions, const float* cell_
                               cand_shift, cand_count, bmax, cutoff, skin, e_capacity, pad_image_host, minimum_image,
                               wrapped, wrap_delta, edge_index, edge_image, recv_off, send_off, send_perm, n_edges,
                               max_displacement, scratch, kNoAllocScratchBytes, flags, stream);
+}
+
+fmd_status fmd_pad_vector_override(const int64_t* n_edges, int64_t e_capacity, const float* pad_vector_host,
+                                   float* edge_vec_override, void* stream) {
+    if (e_capacity < 0 || pad_vector_host == nullptr) return FMD_ERR_INVALID_ARGUMENT;
+    if (e_capacity == 0) return FMD_OK;
+    if (n_edges == nullptr || edge_vec_override == nullptr) return FMD_ERR_INVALID_ARGUMENT;
+    constexpr int threads = 256;
+    const float3 v = make_float3(pad_vector_host[0], pad_vector_host[1], pad_vector_host[2]);
+    pad_vector_override_kernel<<<grid_for(e_capacity, threads), threads, 0, as_stream(stream)>>>(n_edges, e_capacity, v,
+                                                                                              edge_vec_override);
+    return check_launch();
 }
 
 fmd_status fmd_model_positions_f64(const double* positions, int64_t n_atoms, const float* cell_host,

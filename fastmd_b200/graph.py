@@ -49,18 +49,39 @@ class NeighborOverflowError(RuntimeError):
 
 @dataclass(frozen=True)
 class PaddingRule:
-    """The form of padded edge rows (protocol.py:69). Edges-only builds here pad with far
-    self-loops: a loop of a real atom, round robin, with an integer image at least twice the
-    cutoff long (zero contribution under an exact radial cutoff, never a zero length)."""
+    """The form of padded edge rows (fastmd/adapters/protocol.py:69): ``far_self_loops`` (a loop of a
+    real atom, round robin, with an integer image at least twice the cutoff long: zero contribution
+    under an exact radial cutoff, never a zero length), ``sink_atoms`` (loops of ``n_dummy`` sink rows,
+    builds with a line graph) or ``exact_rc_loops`` (a loop of a real atom with image 0 whose edge vector
+    the model takes from ``GraphBatch.edge_vec_override``: ``pad_vector``, by default ``(cutoff, 0, 0)``,
+    exactly at the cutoff)."""
 
     kind: str = "far_self_loops"
     min_length: float = 0.0
+    pad_vector: tuple | None = None
 
     def __post_init__(self):
         if self.kind not in ("far_self_loops", "sink_atoms", "exact_rc_loops"):
             raise ValueError(f"unknown kind {self.kind!r}")
         if not (self.min_length >= 0.0 and math.isfinite(self.min_length)):
             raise ValueError("min_length must be finite and >= 0")
+        if self.min_length and self.kind != "far_self_loops":
+            raise ValueError("min_length applies to far_self_loops only")
+        if self.pad_vector is not None:
+            if self.kind != "exact_rc_loops":
+                raise ValueError("pad_vector applies to exact_rc_loops only")
+            if len(self.pad_vector) != 3 or not all(math.isfinite(float(v)) for v in self.pad_vector):
+                raise ValueError("pad_vector must be three finite numbers")
+
+
+def exact_rc_pad_vector(padding: PaddingRule, cutoff: float) -> tuple[float, float, float]:
+    """The padded rows' edge vector of ``exact_rc_loops`` (fixed_capacity_builder.py:1008-1014): the
+    rule's ``pad_vector`` or ``(cutoff, 0, 0)``; its float32 length must not be inside the cutoff (nor 0)."""
+    vector = tuple(float(v) for v in (padding.pad_vector or (cutoff, 0.0, 0.0)))
+    length = float(np.linalg.norm(np.asarray(vector, np.float32)).astype(np.float32))
+    if not length >= float(np.float32(cutoff)) or length == 0.0:
+        raise ValueError(f"exact_rc_loops: pad_vector {vector} is shorter than the cutoff {cutoff}")
+    return vector
 
 
 @dataclass
@@ -82,6 +103,7 @@ class GraphBatch:
     replicas: int = 1
     element: Tensor | None = None    # model element rows (set by a model's prepare)
     element64: Tensor | None = None
+    edge_vec_override: Tensor | None = None    # [E_cap, 3] float32: exact_rc_loops padded rows' vector, else 0
     directed2undirected: Tensor | None = None  # [E_cap] int32 (a builder with a line graph)
     undirected2directed: Tensor | None = None  # [U_cap] int32
     line_graph: Tensor | None = None           # [T_cap, 5] int32 [atom, u1, e1, u2, e2]
@@ -204,8 +226,8 @@ class FixedCapacityGraphBuilder:
             raise ValueError("this build implements fully periodic cells")
         if self.edges_only:
             padding = PaddingRule("far_self_loops") if padding is None else padding
-            if padding.kind != "far_self_loops":
-                raise ValueError("edges-only builds pad with far self-loops here")
+            if padding.kind not in ("far_self_loops", "exact_rc_loops"):
+                raise ValueError("edges-only builds pad with far self-loops or exact-rc loops here")
             if int(u_capacity) <= 0 or t_capacity != 0:
                 raise ValueError("an edges-only builder needs u_capacity > 0 and t_capacity == 0")
         else:
@@ -239,7 +261,12 @@ class FixedCapacityGraphBuilder:
         self.candidate_cutoff = float(candidate_cutoff or (self.atom_graph_cutoff + 1.0e-6))
         self.skin = self.candidate_cutoff - self.atom_graph_cutoff
         self.buffer_max = int(max_neighbors or estimate_max_neighbors(self.candidate_cutoff, safety_factor=2.0))
-        image, length = self_loop_image(self.cell, self.atom_graph_cutoff, padding.min_length)
+        if padding.kind == "exact_rc_loops":  # loops with image 0, the edge vector overridden
+            self.pad_vector = exact_rc_pad_vector(padding, self.atom_graph_cutoff)
+            image, length = (0, 0, 0), float(np.linalg.norm(self.pad_vector))
+            self._pad_vector_host = (ctypes.c_float * 3)(*self.pad_vector)
+        else:
+            image, length = self_loop_image(self.cell, self.atom_graph_cutoff, padding.min_length)
         self.pad_image = image
         self.pad_length = length
         self._pad_image_host = (ctypes.c_int32 * 3)(*image)  # sink padding: the bond graph rewrites the loops
@@ -287,6 +314,8 @@ class FixedCapacityGraphBuilder:
             send_perm=torch.zeros(E, **i32),
             replicas=self.replicas,
         )
+        if padding.kind == "exact_rc_loops":
+            self.batch.edge_vec_override = torch.zeros(E, 3, dtype=torch.float32, device=dev)
         self.n_triplets = None
         if not self.edges_only:
             U, T = self.u_capacity, self.t_capacity
@@ -382,6 +411,9 @@ class FixedCapacityGraphBuilder:
              ptr(self.batch.edge_index), ptr(self.batch.edge_image), ptr(self.batch.recv_off), ptr(self.batch.send_off),
              ptr(self.batch.send_perm), ptr(self.batch.n_edges), ptr(self.max_displacement), ptr(self._refilter_ws),
              self._refilter_ws.numel(), ptr(flags), stream(self.device))
+        if self.padding.kind == "exact_rc_loops":
+            call("fmd_pad_vector_override", ptr(self.batch.n_edges), self.e_capacity, self._pad_vector_host,
+                 ptr(self.batch.edge_vec_override), stream(self.device))
         if self.float64:
             p64 = positions
             if not (p64.dtype == torch.float64 and p64.is_contiguous() and p64.device == self.device):

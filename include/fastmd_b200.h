@@ -251,6 +251,15 @@ FMD_API fmd_status fmd_neighbor_list(const float* positions, const float* cell_h
                                      int64_t* offsets, void* workspace, size_t workspace_bytes,
                                      int32_t* flags, void* stream);
 
+/* The edge-vector override of exact-rc self-loop padding: for every row r <
+ * e_capacity, edge_vec_override[r] = pad_vector_host (3 floats) on the padded
+ * rows (r >= min(*n_edges, e_capacity)), 0 on the real rows. The padded rows
+ * themselves are fmd_refilter_edges' loops with pad_image (0, 0, 0).
+ * Replaces the HAS_OVERRIDE part of _pad_self_loops_kernel
+ * (fastmd/graph/fixed_capacity_builder.py:324). */
+FMD_API fmd_status fmd_pad_vector_override(const int64_t* n_edges, int64_t e_capacity, const float* pad_vector_host,
+                                           float* edge_vec_override, void* stream);
+
 /* Float64 model positions of a float64 build: out[i] = p[i] - ((w0 c64[0] +
  * w1 c64[1]) + w2 c64[2]) (rows of the float64 cell, each operation rounded),
  * w = floor(float32(p[i]) @ inv(cell)) the whole lattice vectors of the

@@ -198,3 +198,12 @@ def float64_prologue(positions64, cell64, reference32, reference_wraps, skin, in
     return {"wrapped": wrapped, "frac": frac, "model_positions": model,
             "wrap_delta": (wraps - np.asarray(reference_wraps, np.int32)).astype(np.int32),
             "max_displacement": largest, "candidate_valid": bool(largest * f32(2) <= f32(skin + 1.0e-6))}
+
+
+def pad_vector_override(n_edges, e_capacity, vector):
+    """The edge-vector override of exact-rc loop padding (``_pad_self_loops_kernel`` with
+    ``HAS_OVERRIDE``, fixed_capacity_builder.py:324): ``vector`` on rows ``>= min(n_edges, e_capacity)``,
+    0 on the real rows; [e_capacity, 3] float32."""
+    out = np.zeros((e_capacity, 3), f32)
+    out[min(n_edges, e_capacity):] = np.asarray(vector, f32)
+    return out

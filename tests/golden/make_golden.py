@@ -727,6 +727,29 @@ def float64_cases(torch, fcb):
     return out
 
 
+def padding_cases(torch, fcb):
+    """The edges-only padding rows: ``_pad_self_loops_kernel`` (fixed_capacity_builder.py:324) with the far
+    self-loop image of a cubic 18.6 A cell (no override) and with image 0 and the exact-rc override vector
+    (6, 0, 0) at a 6 A cutoff (HAS_OVERRIDE), for 2,054 real edges of 2,200 rows over 135 atoms (the config-1
+    count)."""
+    out = {}
+    total, e_cap, n = 2054, 2200, 135
+    for tag, image, vector, override in (("far", (1, 0, 0), (0.0, 0.0, 0.0), False),
+                                         ("exact_rc", (0, 0, 0), (6.0, 0.0, 0.0), True)):
+        center = torch.full((e_cap,), -7, dtype=torch.int32)
+        neighbor = torch.full((e_cap,), -7, dtype=torch.int32)
+        images = torch.full((e_cap, 3), -7, dtype=torch.int32)
+        vec = torch.full((e_cap, 3), -7.0)
+        fcb._pad_self_loops_kernel[((e_cap + 255) // 256,)](
+            torch.tensor([total], dtype=torch.int64), center, neighbor, images, vec if override else images,
+            *image, *vector, torch.zeros(1, dtype=torch.int32), N=n, E_CAP=e_cap, BLOCK=256, HAS_OVERRIDE=override)
+        out.update({f"pad_{tag}_meta": np.array([total, e_cap, n], dtype=np.int64),
+                    f"pad_{tag}_center": center.numpy(), f"pad_{tag}_neighbor": neighbor.numpy(),
+                    f"pad_{tag}_images": images.numpy(), f"pad_{tag}_override": vec.numpy(),
+                    f"pad_{tag}_image": np.array(image, np.int32), f"pad_{tag}_vector": np.array(vector, np.float32)})
+    return out
+
+
 def radial_cases(torch):
     """The reference's radial basis (fastmd/models/matris/basis_function.py:139 BesselExpansion with the
     PolynomialEnvelope of :31) at the MACE setting (8 functions, rc 6, p 5) and MatRIS's (7, 6, 8)."""
@@ -777,6 +800,7 @@ def main(reference: str, only: list[str]) -> None:
         "residual_add": lambda: residual_add_cases(torch, ra),
         "bond_graph": lambda: bond_graph_cases(torch, fcb),
         "float64": lambda: float64_cases(torch, fcb),
+        "padding": lambda: padding_cases(torch, fcb),
     }
     for name, make in fixtures.items():
         if not only or name in only:

@@ -196,3 +196,27 @@ def test_ragged_c2_scale_properties(cuda):
     missing = (~found).nonzero().flatten()
     assert missing.numel() <= 10 and bool(((d[missing] - 6.0).abs() < 1e-5).all())
     assert float(d.max()) < 6.0
+
+
+@pytest.mark.parametrize("tag", ["far", "exact_rc"])
+def test_padding_rows_equal_the_reference(cuda, tag):
+    """The padded rows of a build (2,054 real edges of 2,200 rows) equal the reference's
+    ``_pad_self_loops_kernel`` rows; exact-rc padding also publishes the override vector (SevenNet's
+    ``PaddingRule("exact_rc_loops")``, sevennet.py:16-22)."""
+    from fastmd_b200.graph import PaddingRule
+
+    g = golden("padding")
+    total, e_cap, n = (int(v) for v in g[f"pad_{tag}_meta"])
+    pos, cell, numbers, _ = _perov(0)
+    padding = PaddingRule("exact_rc_loops") if tag == "exact_rc" else None  # pad vector (rc, 0, 0) = (6, 0, 0)
+    b = _builder(cell, numbers, e_cap // 2, cuda, padding=padding)
+    batch, status = b.build(torch.from_numpy(pos.astype(np.float32)).to(cuda))
+    assert int(status.flags.item()) == 0 and int(batch.n_edges.item()) == total
+    ei = batch.edge_index.cpu().numpy()
+    np.testing.assert_array_equal(ei[total:, 0], g[f"pad_{tag}_center"][total:])
+    np.testing.assert_array_equal(ei[total:, 1], g[f"pad_{tag}_neighbor"][total:])
+    np.testing.assert_array_equal(batch.edge_image.cpu().numpy()[total:], g[f"pad_{tag}_images"][total:])
+    if tag == "exact_rc":
+        np.testing.assert_array_equal(batch.edge_vec_override.cpu().numpy(), g["pad_exact_rc_override"])
+    else:
+        assert batch.edge_vec_override is None
