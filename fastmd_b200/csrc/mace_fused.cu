@@ -304,6 +304,33 @@ __global__ void __launch_bounds__(256) edge_fwd_kernel(EdgeArgs a, FusedWeights 
 
 // ------------------------------------------------------------------ messages
 
+// N consecutive floats of a lane (16-, 8- or 4-byte aligned rows): one vector access
+template <int N>
+__device__ __forceinline__ void ldv(const float* p, float (&v)[N]) {
+    if constexpr (N == 4) {
+        const float4 x = *reinterpret_cast<const float4*>(p);
+        v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+    } else if constexpr (N == 2) {
+        const float2 x = *reinterpret_cast<const float2*>(p);
+        v[0] = x.x; v[1] = x.y;
+    } else {
+#pragma unroll
+        for (int q = 0; q < N; ++q) v[q] = p[q];
+    }
+}
+
+template <int N>
+__device__ __forceinline__ void stv(float* p, const float (&v)[N]) {
+    if constexpr (N == 4) {
+        *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    } else if constexpr (N == 2) {
+        *reinterpret_cast<float2*>(p) = make_float2(v[0], v[1]);
+    } else {
+#pragma unroll
+        for (int q = 0; q < N; ++q) p[q] = v[q];
+    }
+}
+
 struct GraphArgs {
     const int32_t* edge_index;
     const int64_t* recv_off;
@@ -331,24 +358,33 @@ __global__ void __launch_bounds__(32 * kMsgWarps) message_fused_kernel(GraphArgs
         for (int64_t e = beg + warp; e < end; e += kMsgWarps) {
             const int64_t j = g.edge_index[2 * e + 1];
             const float4 y = st.ysh[e];
-            const float* Re = R + e * (P * C);
-            const float* srow = (L == 0) ? w.s_t0 + int64_t(st.elem[j]) * C : st.s_t[L] + j * C;
+            const float* Re = R + e * (P * C) + lane * CPL;
+            const float* srow = ((L == 0) ? w.s_t0 + int64_t(st.elem[j]) * C : st.s_t[L] + j * C) + lane * CPL;
+            float sv[CPL], r0[CPL], r1[CPL], r2[CPL], r3[CPL], vx[CPL], vy[CPL], vz[CPL];
+            ldv<CPL>(srow, sv);
+            ldv<CPL>(Re, r0);
+            ldv<CPL>(Re + C, r1);
+            if constexpr (P == 4) {
+                const float* vrow = v_t + j * 3 * C + lane * CPL;
+                ldv<CPL>(Re + 2 * C, r2);
+                ldv<CPL>(Re + 3 * C, r3);
+                ldv<CPL>(vrow, vx);
+                ldv<CPL>(vrow + C, vy);
+                ldv<CPL>(vrow + 2 * C, vz);
+            }
 #pragma unroll
             for (int q = 0; q < CPL; ++q) {
-                const int k = lane * CPL + q;
-                const float s = srow[k];
-                a0[q] = fmaf(Re[k], s, a0[q]);
-                const float m1 = Re[C + k] * s;
+                const float s = sv[q];
+                a0[q] = fmaf(r0[q], s, a0[q]);
+                const float m1 = r1[q] * s;
                 ax[q] = fmaf(m1, y.x, ax[q]);
                 ay[q] = fmaf(m1, y.y, ay[q]);
                 az[q] = fmaf(m1, y.z, az[q]);
                 if constexpr (P == 4) {
-                    const float vx = v_t[j * 3 * C + k], vy = v_t[j * 3 * C + C + k], vz = v_t[j * 3 * C + 2 * C + k];
-                    const float r2 = Re[2 * C + k], r3 = Re[3 * C + k];
-                    ax[q] = fmaf(r2, vx, ax[q]);
-                    ay[q] = fmaf(r2, vy, ay[q]);
-                    az[q] = fmaf(r2, vz, az[q]);
-                    a0[q] = fmaf(r3 * kIS3, (vx * y.x + vy * y.y) + vz * y.z, a0[q]);
+                    ax[q] = fmaf(r2[q], vx[q], ax[q]);
+                    ay[q] = fmaf(r2[q], vy[q], ay[q]);
+                    az[q] = fmaf(r2[q], vz[q], az[q]);
+                    a0[q] = fmaf(r3[q] * kIS3, (vx[q] * y.x + vy[q] * y.y) + vz[q] * y.z, a0[q]);
                 }
             }
         }
@@ -656,31 +692,44 @@ __global__ void __launch_bounds__(32 * kMsgBwdWarps) msg_bwd_edge_kernel(GraphAr
         for (int64_t e = beg + warp; e < end; e += kMsgBwdWarps) {
             const int64_t j = g.edge_index[2 * e + 1];
             const float4 y = st.ysh[e];
-            const float* Re = R + e * (P * C);
-            float* dRe = dR + e * (P * C);
-            const float* srow = (L == 0) ? w.s_t0 + int64_t(st.elem[j]) * C : st.s_t[L] + j * C;
+            const float* Re = R + e * (P * C) + lane * CPL;
+            float* dRe = dR + e * (P * C) + lane * CPL;
+            const float* srow = ((L == 0) ? w.s_t0 + int64_t(st.elem[j]) * C : st.s_t[L] + j * C) + lane * CPL;
+            float sv[CPL], r1[CPL], r3[CPL], vx[CPL], vy[CPL], vz[CPL], o0[CPL], o1[CPL], o2[CPL], o3[CPL];
+            ldv<CPL>(srow, sv);
+            ldv<CPL>(Re + C, r1);
+            if constexpr (P == 4) {
+                const float* vrow = st.v_t[L] + j * 3 * C + lane * CPL;
+                ldv<CPL>(Re + 3 * C, r3);
+                ldv<CPL>(vrow, vx);
+                ldv<CPL>(vrow + C, vy);
+                ldv<CPL>(vrow + 2 * C, vz);
+            }
             float px = 0.f, py = 0.f, pz = 0.f;
 #pragma unroll
             for (int q = 0; q < CPL; ++q) {
-                const int k = lane * CPL + q;
-                const float s = srow[k];
+                const float s = sv[q];
                 const float gdy = (gx[q] * y.x + gy[q] * y.y) + gz[q] * y.z;
-                dRe[k] = g0[q] * s;
-                dRe[C + k] = s * gdy;
-                const float c1 = Re[C + k] * s;
+                o0[q] = g0[q] * s;
+                o1[q] = s * gdy;
+                const float c1 = r1[q] * s;
                 px = fmaf(c1, gx[q], px);
                 py = fmaf(c1, gy[q], py);
                 pz = fmaf(c1, gz[q], pz);
                 if constexpr (P == 4) {
-                    const float* vrow = st.v_t[L] + j * 3 * C;
-                    const float vx = vrow[k], vy = vrow[C + k], vz = vrow[2 * C + k];
-                    dRe[2 * C + k] = (gx[q] * vx + gy[q] * vy) + gz[q] * vz;
-                    dRe[3 * C + k] = g0[q] * ((vx * y.x + vy * y.y) + vz * y.z) * kIS3;
-                    const float c3 = Re[3 * C + k] * g0[q] * kIS3;
-                    px = fmaf(c3, vx, px);
-                    py = fmaf(c3, vy, py);
-                    pz = fmaf(c3, vz, pz);
+                    o2[q] = (gx[q] * vx[q] + gy[q] * vy[q]) + gz[q] * vz[q];
+                    o3[q] = g0[q] * ((vx[q] * y.x + vy[q] * y.y) + vz[q] * y.z) * kIS3;
+                    const float c3 = r3[q] * g0[q] * kIS3;
+                    px = fmaf(c3, vx[q], px);
+                    py = fmaf(c3, vy[q], py);
+                    pz = fmaf(c3, vz[q], pz);
                 }
+            }
+            stv<CPL>(dRe, o0);
+            stv<CPL>(dRe + C, o1);
+            if constexpr (P == 4) {
+                stv<CPL>(dRe + 2 * C, o2);
+                stv<CPL>(dRe + 3 * C, o3);
             }
 #pragma unroll
             for (int d = 16; d > 0; d >>= 1) {
@@ -737,17 +786,27 @@ __global__ void __launch_bounds__(kQ * C) sender_node_kernel(GraphArgs gr, Fused
             const int64_t e = gr.send_perm[t];
             const int64_t i = gr.edge_index[2 * e];
             const float4 y = st.ysh[e];
-            const float* Re = R + e * (P * C);
+            const float* Re = R + e * (P * C) + lane * CPL;
+            const float* a0 = st.dA0[L] + i * C + lane * CPL;
+            const float* a1 = st.dA1[L] + i * 3 * C + lane * CPL;
+            float r0[CPL], r1[CPL], r2v[CPL], r3v[CPL], d0[CPL], dxv[CPL], dyv[CPL], dzv[CPL];
+            ldv<CPL>(Re, r0);
+            ldv<CPL>(Re + C, r1);
+            ldv<CPL>(Re + 2 * C, r2v);
+            ldv<CPL>(Re + 3 * C, r3v);
+            ldv<CPL>(a0, d0);
+            ldv<CPL>(a1, dxv);
+            ldv<CPL>(a1 + C, dyv);
+            ldv<CPL>(a1 + 2 * C, dzv);
 #pragma unroll
             for (int qq = 0; qq < CPL; ++qq) {
-                const int kk = lane * CPL + qq;
-                const float g0 = st.dA0[L][i * C + kk] * w.inv_avg;
-                const float gx = st.dA1[L][i * 3 * C + kk] * w.inv_avg;
-                const float gy = st.dA1[L][i * 3 * C + C + kk] * w.inv_avg;
-                const float gz = st.dA1[L][i * 3 * C + 2 * C + kk] * w.inv_avg;
-                ds[qq] = fmaf(Re[kk], g0, ds[qq]);
-                ds[qq] = fmaf(Re[C + kk], (gx * y.x + gy * y.y) + gz * y.z, ds[qq]);
-                const float r2 = Re[2 * C + kk], r3 = Re[3 * C + kk] * g0 * kIS3;
+                const float g0 = d0[qq] * w.inv_avg;
+                const float gx = dxv[qq] * w.inv_avg;
+                const float gy = dyv[qq] * w.inv_avg;
+                const float gz = dzv[qq] * w.inv_avg;
+                ds[qq] = fmaf(r0[qq], g0, ds[qq]);
+                ds[qq] = fmaf(r1[qq], (gx * y.x + gy * y.y) + gz * y.z, ds[qq]);
+                const float r2 = r2v[qq], r3 = r3v[qq] * g0 * kIS3;
                 dx[qq] = fmaf(r2, gx, fmaf(r3, y.x, dx[qq]));
                 dy[qq] = fmaf(r2, gy, fmaf(r3, y.y, dy[qq]));
                 dz[qq] = fmaf(r2, gz, fmaf(r3, y.z, dz[qq]));
