@@ -454,7 +454,7 @@ __device__ __forceinline__ void mix_rows(const float (*xs)[C], const float* __re
     float acc[NS + NV];
 #pragma unroll
     for (int r = 0; r < NS + NV; ++r) acc[r] = 0.f;
-#pragma unroll
+#pragma unroll 8
     for (int cc = 0; cc < CQ; ++cc) {
         const int c = q * CQ + cc;
         if constexpr (NS > 0) {
@@ -509,7 +509,7 @@ __device__ __forceinline__ int64_t node_units(const FusedState& st) {
 
 // forward node update of a non-last layer L
 template <int C, int G>
-__global__ void __launch_bounds__(kQ * C) node_fwd_kernel(FusedWeights w, FusedState st, int L) {
+__global__ void __launch_bounds__(kQ * C, 2) node_fwd_kernel(FusedWeights w, FusedState st, int L) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     NodeSmem<C>& m = *reinterpret_cast<NodeSmem<C>*>(smem_raw);
     const int k = threadIdx.x % C, g = threadIdx.x / C;
@@ -586,7 +586,7 @@ __global__ void __launch_bounds__(kQ * C) node_fwd_kernel(FusedWeights w, FusedS
 
 // the last layer: node update, readout, node energies, and the backward to dA(L)
 template <int C, int G>
-__global__ void __launch_bounds__(kQ * C) node_last_kernel(FusedWeights w, FusedState st, int L) {
+__global__ void __launch_bounds__(kQ * C, 2) node_last_kernel(FusedWeights w, FusedState st, int L) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     NodeSmem<C>& m = *reinterpret_cast<NodeSmem<C>*>(smem_raw);
     const int k = threadIdx.x % C, g = threadIdx.x / C;
@@ -757,7 +757,7 @@ __global__ void __launch_bounds__(32 * kMsgBwdWarps) msg_bwd_edge_kernel(GraphAr
 // layer L-1's outputs, and layer L-1's node backward (to dA(L-1)). One atom group per CTA; the
 // C threads of atom g reduce its sender run (warps over edges).
 template <int C, int G>
-__global__ void __launch_bounds__(kQ * C) sender_node_kernel(GraphArgs gr, FusedWeights w, FusedState st, int L) {
+__global__ void __launch_bounds__(kQ * C, 2) sender_node_kernel(GraphArgs gr, FusedWeights w, FusedState st, int L) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     NodeSmem<C>& m = *reinterpret_cast<NodeSmem<C>*>(smem_raw);
     // the C / 32 warps of atom g reduce its sender run (the same order whatever G: the results do not
@@ -1305,8 +1305,11 @@ fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeigh
                                       (const void*)node_last_kernel<C, kG>,   (const void*)node_last_kernel<C, 1>,
                                       (const void*)sender_node_kernel<C, kG>, (const void*)sender_node_kernel<C, 1>};
             for (const void* kernel : kernels) {
-                const cudaError_t err =
+                cudaError_t err =
                     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(node_smem));
+                // the largest shared-memory carveout: two CTAs of a node kernel per SM
+                if (err == cudaSuccess)
+                    err = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
                 if (err != cudaSuccess) return record_cuda_error(err);
             }
             last_granted[slot] = node_smem;
