@@ -87,6 +87,10 @@ _SIGNATURES: dict[str, list] = {
     "fmd_element_linear": [_P, _I64, _I32, _P, _P, _I32, _I32, _I32, _P, _I32, _P],
     "fmd_mace_node_energy": [_P, _I32, _I64, _P, _P, c_double, c_double, _I64, _I32, _P, _P, _P],
     "fmd_mace_node_energy_bwd": [_P, c_double, _I64, _I32, _P, _P],
+    "fmd_nequip_edge_basis": [_P, _P, _P, _P, _P, _P, _I64, c_float, _I32, _I32, _P, _P, _P, _P],
+    "fmd_nequip_edge_basis_bwd": [_P, _P, _P, _P, _P, _I64, c_float, _I32, _I32, _P, _P],
+    "fmd_nequip_conv": [_P, _P, _P, _P, _P, _P, _I64, c_float, _P, _P],
+    "fmd_nequip_conv_bwd": [_P, _P, _P, _P, _P, _P, _P, _P, _I64, c_float, _P, _P, _P, _P, _P],
     "fmd_nhc_pre_force": [_P, _P, _P, _I64, _I32, _I32, _I32, _I32, _P, _P],
     "fmd_nhc_post_force": [_P, _P, _P, _I64, _I32, _I32, _I32, _I32, _P, _P, _P, _P],
 }

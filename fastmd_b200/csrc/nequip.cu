@@ -1,0 +1,487 @@
+// NequIP-architecture (SevenNet-0-style) kernels: the edge basis (spherical
+// harmonics l <= 2 and Bessel radial functions) with its backward, and the
+// radial-weighted tensor-product convolution with its two backward kernels.
+//
+// Layouts. Node features x [N, 480] = [128 x l0 | 64 x l1 (3) | 32 x l2 (5)]
+// (channel-major, m-minor). Messages m [N, 3136] = [224 x l0 | 384 x l1 |
+// 352 x l2]: the outputs of the 15 coupling paths (l1, l2 -> l3), in path
+// order (l1, then l2, then l3), grouped by l3. Per-edge weights W [E, 960]:
+// one weight per (path, channel of l1). Edge harmonics Y [E, 9] =
+// [1 | sqrt3 u | sqrt15 xy, sqrt15 yz, sqrt5/2 (3z^2 - 1), sqrt15 xz,
+// sqrt15/2 (x^2 - y^2)] of the unit edge vector u; CG [615] the 15 dense
+// coupling tensors [2 l3 + 1][2 l1 + 1][2 l2 + 1] in path order.
+//
+// Convolution (one warp per receiver i, its edges in CSR order, a lane per
+// channel u; the receiver's 3136 accumulators in shared memory, each owned
+// by one lane: deterministic):
+//   m[i, path, u, m3] = inv_avg * sum_e W[e, path, u] sum_{m1, m2}
+//                       CG[m3, m1, m2] x[j(e), l1, u, m1] Y[e, l2, m2]
+// Backward per receiver (dW, dY of its edges) and per sender (dx of the atom
+// through its sender CSR), the same sums transposed. Each path is a template
+// instance: the coupling loops unroll with compile-time indices.
+
+#include <utility>
+
+#include "common.cuh"
+
+namespace fmd {
+namespace {
+
+constexpr int kXW = 480;
+constexpr int kMW = 3136;
+constexpr int kWW = 960;
+constexpr int kCGN = 615;
+constexpr int kNqWarps = 4;
+
+__host__ __device__ constexpr int dim_of(int l) { return 2 * l + 1; }
+__host__ __device__ constexpr int mult_of(int l) { return l == 0 ? 128 : (l == 1 ? 64 : 32); }
+__host__ __device__ constexpr int x_off(int l) { return l == 0 ? 0 : (l == 1 ? 128 : 320); }
+__host__ __device__ constexpr int y_off(int l) { return l == 0 ? 0 : (l == 1 ? 1 : 4); }
+
+// the 15 paths with their offsets (weights, message columns, coupling tensor)
+struct PathInfo {
+    int l1, l2, l3, w_off, m_off, cg_off;
+};
+constexpr PathInfo kPaths[15] = {
+    {0, 0, 0, 0, 0, 0},        {0, 1, 1, 128, 224, 1},    {0, 2, 2, 256, 1376, 10},  {1, 0, 1, 384, 608, 35},
+    {1, 1, 0, 448, 128, 44},   {1, 1, 1, 512, 800, 53},   {1, 1, 2, 576, 2016, 80},  {1, 2, 1, 640, 992, 125},
+    {1, 2, 2, 704, 2336, 170}, {2, 0, 2, 768, 2656, 245}, {2, 1, 1, 800, 1184, 270}, {2, 1, 2, 832, 2816, 315},
+    {2, 2, 0, 864, 192, 390},  {2, 2, 1, 896, 1280, 415}, {2, 2, 2, 928, 2976, 490}};
+
+struct Cell3 {
+    float c[9];
+};
+
+// ------------------------------------------------------------------ edge basis
+
+struct BasisArgs {
+    const float* pos;
+    Cell3 cell;
+    const int32_t* edge_index;
+    const float* edge_image;
+    const float* override_vec;  // padded rows' edge vector (exact-rc loops), or null
+    const int64_t* n_real;      // rows past it take the override vector (null: every row is real)
+    int64_t n_edges;
+    float r_max;
+    int n_basis, poly_p;
+    float* Y;                   // [E, 9]
+    float* B;                   // [E, n_basis]
+    float* geo;                 // [E, 4] unit vector and length
+};
+
+__device__ __forceinline__ float envelope(float x, int p, float& dx) {
+    if (!(x < 1.f)) {
+        dx = 0.f;
+        return 0.f;
+    }
+    const float pf = float(p);
+    const float xp = powf(x, pf - 1.f) * x;  // x^p
+    const float a = (pf + 1.f) * (pf + 2.f) / 2.f, b = pf * (pf + 2.f), c = pf * (pf + 1.f) / 2.f;
+    const float env = 1.f - a * xp + b * xp * x - c * xp * x * x;
+    dx = (-a * pf * xp + b * (pf + 1.f) * xp * x - c * (pf + 2.f) * xp * x * x) / x;
+    return env;
+}
+
+__global__ void nq_basis_kernel(BasisArgs a) {
+    const int64_t n_real = a.n_real ? *a.n_real : a.n_edges;
+    for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < a.n_edges; e += int64_t(gridDim.x) * blockDim.x) {
+        float rx, ry, rz;
+        if (e < n_real || a.override_vec == nullptr) {
+            const int64_t i = a.edge_index[2 * e], j = a.edge_index[2 * e + 1];
+            const float ix = a.edge_image[3 * e], iy = a.edge_image[3 * e + 1], iz = a.edge_image[3 * e + 2];
+            const float* c = a.cell.c;
+            rx = (a.pos[3 * j] - a.pos[3 * i]) + ((ix * c[0] + iy * c[3]) + iz * c[6]);
+            ry = (a.pos[3 * j + 1] - a.pos[3 * i + 1]) + ((ix * c[1] + iy * c[4]) + iz * c[7]);
+            rz = (a.pos[3 * j + 2] - a.pos[3 * i + 2]) + ((ix * c[2] + iy * c[5]) + iz * c[8]);
+        } else {
+            rx = a.override_vec[3 * e];
+            ry = a.override_vec[3 * e + 1];
+            rz = a.override_vec[3 * e + 2];
+        }
+        const float d = sqrtf((rx * rx + ry * ry) + rz * rz);
+        const float inv = d > 0.f ? 1.f / d : 0.f;
+        const float x = rx * inv, y = ry * inv, z = rz * inv;
+        const float s3 = 1.7320508075688772f, s5 = 2.23606797749979f, s15 = 3.872983346207417f;
+        float* Ye = a.Y + 9 * e;
+        Ye[0] = 1.f;
+        Ye[1] = s3 * x;
+        Ye[2] = s3 * y;
+        Ye[3] = s3 * z;
+        Ye[4] = s15 * x * y;
+        Ye[5] = s15 * y * z;
+        Ye[6] = s5 * 0.5f * (3.f * z * z - 1.f);
+        Ye[7] = s15 * x * z;
+        Ye[8] = s15 * 0.5f * (x * x - y * y);
+        float denv;
+        const float env = envelope(d / a.r_max, a.poly_p, denv);
+        const float pref = sqrtf(2.f / a.r_max);
+        for (int n = 0; n < a.n_basis; ++n) {
+            const float k = float(n + 1) * 3.14159265358979323846f / a.r_max;
+            a.B[int64_t(a.n_basis) * e + n] = d > 0.f ? pref * sinf(k * d) * inv * env : 0.f;
+        }
+        a.geo[4 * e] = x;
+        a.geo[4 * e + 1] = y;
+        a.geo[4 * e + 2] = z;
+        a.geo[4 * e + 3] = d;
+    }
+}
+
+// g[e] = dE/d(edge vector) from dY and dB (padded override rows: 0)
+__global__ void nq_basis_bwd_kernel(BasisArgs a, const float* __restrict__ dY, const float* __restrict__ dB,
+                                    float* __restrict__ g) {
+    const int64_t n_real = a.n_real ? *a.n_real : a.n_edges;
+    for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < a.n_edges; e += int64_t(gridDim.x) * blockDim.x) {
+        const float x = a.geo[4 * e], y = a.geo[4 * e + 1], z = a.geo[4 * e + 2], d = a.geo[4 * e + 3];
+        float gx = 0.f, gy = 0.f, gz = 0.f;
+        if ((e < n_real || a.override_vec == nullptr) && d > 0.f) {
+            const float s3 = 1.7320508075688772f, s5 = 2.23606797749979f, s15 = 3.872983346207417f;
+            const float* q = dY + 9 * e;
+            // dE/du from the harmonics
+            float ux = s3 * q[1] + s15 * (y * q[4] + z * q[7] + x * q[8]);
+            float uy = s3 * q[2] + s15 * (x * q[4] + z * q[5] - y * q[8]);
+            float uz = s3 * q[3] + s15 * (y * q[5] + x * q[7]) + 3.f * s5 * z * q[6];
+            const float inv = 1.f / d;
+            const float gu = (ux * x + uy * y) + uz * z;
+            gx = (ux - gu * x) * inv;
+            gy = (uy - gu * y) * inv;
+            gz = (uz - gu * z) * inv;
+            // dE/dd from the radial functions
+            float denv;
+            const float env = envelope(d / a.r_max, a.poly_p, denv);
+            const float pref = sqrtf(2.f / a.r_max);
+            float gd = 0.f;
+            for (int n = 0; n < a.n_basis; ++n) {
+                const float k = float(n + 1) * 3.14159265358979323846f / a.r_max;
+                float sn, cs;
+                sincosf(k * d, &sn, &cs);
+                const float b = pref * sn * inv;
+                const float db = pref * (k * cs * d - sn) * inv * inv;
+                gd += dB[int64_t(a.n_basis) * e + n] * (db * env + b * denv / a.r_max);
+            }
+            gx += gd * x;
+            gy += gd * y;
+            gz += gd * z;
+        }
+        g[3 * e] = gx;
+        g[3 * e + 1] = gy;
+        g[3 * e + 2] = gz;
+    }
+}
+
+// ------------------------------------------------------------------ convolution
+
+struct ConvArgs {
+    const float* x;          // [N, 480]
+    const float* Y;          // [E, 9]
+    const float* W;          // [E, 960]
+    const float* cg;         // [615]
+    const int32_t* edge_index;
+    const int64_t* recv_off;  // [N + 1] receiver CSR (rows sorted by centre)
+    const int64_t* send_off;  // [N + 1] sender CSR
+    const int32_t* send_perm;
+    int64_t n_atoms;
+    float inv_avg;
+};
+
+// one path's contribution of edge e (lane channels u) into the receiver's accumulators
+template <int P>
+__device__ __forceinline__ void path_fwd(const ConvArgs& a, const float* cg, const float* y, int64_t e, int64_t j,
+                                         float* acc, int lane) {
+    constexpr PathInfo pi = kPaths[P];
+    constexpr int n1 = dim_of(pi.l1), n2 = dim_of(pi.l2), n3 = dim_of(pi.l3), U = mult_of(pi.l1);
+    for (int u = lane; u < U; u += 32) {
+        const float w = a.W[e * kWW + pi.w_off + u];
+        float xv[n1];
+#pragma unroll
+        for (int m1 = 0; m1 < n1; ++m1) xv[m1] = a.x[j * kXW + x_off(pi.l1) + u * n1 + m1];
+#pragma unroll
+        for (int m3 = 0; m3 < n3; ++m3) {
+            float s = 0.f;
+#pragma unroll
+            for (int m1 = 0; m1 < n1; ++m1)
+#pragma unroll
+                for (int m2 = 0; m2 < n2; ++m2)
+                    s = fmaf(cg[pi.cg_off + (m3 * n1 + m1) * n2 + m2], xv[m1] * y[y_off(pi.l2) + m2], s);
+            acc[pi.m_off + u * n3 + m3] = fmaf(w, s, acc[pi.m_off + u * n3 + m3]);
+        }
+    }
+}
+
+template <int... P>
+__device__ __forceinline__ void all_paths_fwd(const ConvArgs& a, const float* cg, const float* y, int64_t e,
+                                              int64_t j, float* acc, int lane, std::integer_sequence<int, P...>) {
+    (path_fwd<P>(a, cg, y, e, j, acc, lane), ...);
+}
+
+__global__ void __launch_bounds__(32 * kNqWarps) nq_conv_kernel(ConvArgs a, float* __restrict__ m) {
+    extern __shared__ __align__(16) float nq_smem[];
+    float* cg = nq_smem;                                   // [616]
+    float* acc = nq_smem + 616 + (threadIdx.x >> 5) * kMW;  // this warp's receiver
+    for (int t = threadIdx.x; t < kCGN; t += blockDim.x) cg[t] = a.cg[t];
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    for (int64_t i = int64_t(blockIdx.x) * kNqWarps + (threadIdx.x >> 5); i < a.n_atoms;
+         i += int64_t(gridDim.x) * kNqWarps) {
+        for (int t = lane; t < kMW; t += 32) acc[t] = 0.f;
+        __syncwarp();
+        for (int64_t e = a.recv_off[i]; e < a.recv_off[i + 1]; ++e) {
+            const int64_t j = a.edge_index[2 * e + 1];
+            float y[9];
+#pragma unroll
+            for (int q = 0; q < 9; ++q) y[q] = a.Y[9 * e + q];
+            all_paths_fwd(a, cg, y, e, j, acc, lane, std::make_integer_sequence<int, 15>{});
+        }
+        __syncwarp();
+        for (int t = lane; t < kMW; t += 32) m[i * kMW + t] = acc[t] * a.inv_avg;
+        __syncwarp();
+    }
+}
+
+// dW[e, path, u] and the lane's share of dY[e] of one path (dm: the receiver's message gradient)
+template <int P>
+__device__ __forceinline__ void path_bwd_edge(const ConvArgs& a, const float* cg, const float* y, const float* dm,
+                                              int64_t e, int64_t j, float* dW, float* dy, int lane) {
+    constexpr PathInfo pi = kPaths[P];
+    constexpr int n1 = dim_of(pi.l1), n2 = dim_of(pi.l2), n3 = dim_of(pi.l3), U = mult_of(pi.l1);
+    for (int u = lane; u < U; u += 32) {
+        const float w = a.W[e * kWW + pi.w_off + u];
+        float xv[n1];
+#pragma unroll
+        for (int m1 = 0; m1 < n1; ++m1) xv[m1] = a.x[j * kXW + x_off(pi.l1) + u * n1 + m1];
+        float gw = 0.f;
+#pragma unroll
+        for (int m3 = 0; m3 < n3; ++m3) {
+            const float g = dm[pi.m_off + u * n3 + m3];
+            float s = 0.f;
+#pragma unroll
+            for (int m1 = 0; m1 < n1; ++m1)
+#pragma unroll
+                for (int m2 = 0; m2 < n2; ++m2) {
+                    const float c = cg[pi.cg_off + (m3 * n1 + m1) * n2 + m2];
+                    s = fmaf(c, xv[m1] * y[y_off(pi.l2) + m2], s);
+                    dy[y_off(pi.l2) + m2] = fmaf(w * g * c, xv[m1], dy[y_off(pi.l2) + m2]);
+                }
+            gw = fmaf(g, s, gw);
+        }
+        dW[e * kWW + pi.w_off + u] = gw;
+    }
+}
+
+template <int... P>
+__device__ __forceinline__ void all_paths_bwd_edge(const ConvArgs& a, const float* cg, const float* y,
+                                                   const float* dm, int64_t e, int64_t j, float* dW, float* dy,
+                                                   int lane, std::integer_sequence<int, P...>) {
+    (path_bwd_edge<P>(a, cg, y, dm, e, j, dW, dy, lane), ...);
+}
+
+// per receiver: dW and dY of its edges (dY: lane partials folded by a fixed xor tree)
+__global__ void __launch_bounds__(32 * kNqWarps) nq_conv_bwd_edge_kernel(ConvArgs a, const float* __restrict__ dmsg,
+                                                                         float* __restrict__ dW,
+                                                                         float* __restrict__ dY) {
+    extern __shared__ __align__(16) float nq_smem[];
+    float* cg = nq_smem;
+    float* dm = nq_smem + 616 + (threadIdx.x >> 5) * kMW;
+    for (int t = threadIdx.x; t < kCGN; t += blockDim.x) cg[t] = a.cg[t];
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    for (int64_t i = int64_t(blockIdx.x) * kNqWarps + (threadIdx.x >> 5); i < a.n_atoms;
+         i += int64_t(gridDim.x) * kNqWarps) {
+        for (int t = lane; t < kMW; t += 32) dm[t] = dmsg[i * kMW + t] * a.inv_avg;
+        __syncwarp();
+        for (int64_t e = a.recv_off[i]; e < a.recv_off[i + 1]; ++e) {
+            const int64_t j = a.edge_index[2 * e + 1];
+            float y[9], dy[9];
+#pragma unroll
+            for (int q = 0; q < 9; ++q) {
+                y[q] = a.Y[9 * e + q];
+                dy[q] = 0.f;
+            }
+            all_paths_bwd_edge(a, cg, y, dm, e, j, dW, dy, lane, std::make_integer_sequence<int, 15>{});
+#pragma unroll
+            for (int q = 0; q < 9; ++q)
+                for (int d = 16; d > 0; d >>= 1) dy[q] += __shfl_xor_sync(0xffffffffu, dy[q], d);
+            if (lane == 0)
+#pragma unroll
+                for (int q = 0; q < 9; ++q) dY[9 * e + q] = dy[q];
+        }
+        __syncwarp();
+    }
+}
+
+// dx[j, l1, u, m1] += W[e, path, u] sum_{m3, m2} CG[m3, m1, m2] dm[i, path, u, m3] Y[e, l2, m2]
+template <int P>
+__device__ __forceinline__ void path_bwd_x(const ConvArgs& a, const float* cg, const float* y, const float* dmi,
+                                           int64_t e, float* dx, int lane) {
+    constexpr PathInfo pi = kPaths[P];
+    constexpr int n1 = dim_of(pi.l1), n2 = dim_of(pi.l2), n3 = dim_of(pi.l3), U = mult_of(pi.l1);
+    for (int u = lane; u < U; u += 32) {
+        const float w = a.W[e * kWW + pi.w_off + u];
+#pragma unroll
+        for (int m1 = 0; m1 < n1; ++m1) {
+            float s = 0.f;
+#pragma unroll
+            for (int m3 = 0; m3 < n3; ++m3) {
+                const float g = dmi[pi.m_off + u * n3 + m3];
+#pragma unroll
+                for (int m2 = 0; m2 < n2; ++m2)
+                    s = fmaf(cg[pi.cg_off + (m3 * n1 + m1) * n2 + m2], g * y[y_off(pi.l2) + m2], s);
+            }
+            dx[x_off(pi.l1) + u * n1 + m1] = fmaf(w, s, dx[x_off(pi.l1) + u * n1 + m1]);
+        }
+    }
+}
+
+template <int... P>
+__device__ __forceinline__ void all_paths_bwd_x(const ConvArgs& a, const float* cg, const float* y, const float* dmi,
+                                                int64_t e, float* dx, int lane, std::integer_sequence<int, P...>) {
+    (path_bwd_x<P>(a, cg, y, dmi, e, dx, lane), ...);
+}
+
+// per sender j: dx[j] over its sender run (the receivers' message gradients read from global memory)
+__global__ void __launch_bounds__(32 * kNqWarps) nq_conv_bwd_x_kernel(ConvArgs a, const float* __restrict__ dmsg,
+                                                                      float* __restrict__ dx_out) {
+    extern __shared__ __align__(16) float nq_smem[];
+    float* cg = nq_smem;
+    float* dx = nq_smem + 616 + (threadIdx.x >> 5) * kXW;
+    for (int t = threadIdx.x; t < kCGN; t += blockDim.x) cg[t] = a.cg[t];
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    for (int64_t j = int64_t(blockIdx.x) * kNqWarps + (threadIdx.x >> 5); j < a.n_atoms;
+         j += int64_t(gridDim.x) * kNqWarps) {
+        for (int t = lane; t < kXW; t += 32) dx[t] = 0.f;
+        __syncwarp();
+        for (int64_t s = a.send_off[j]; s < a.send_off[j + 1]; ++s) {
+            const int64_t e = a.send_perm[s];
+            const int64_t i = a.edge_index[2 * e];
+            float y[9];
+#pragma unroll
+            for (int q = 0; q < 9; ++q) y[q] = a.Y[9 * e + q];
+            all_paths_bwd_x(a, cg, y, dmsg + i * kMW, e, dx, lane, std::make_integer_sequence<int, 15>{});
+        }
+        __syncwarp();
+        for (int t = lane; t < kXW; t += 32) dx_out[j * kXW + t] = dx[t] * a.inv_avg;
+        __syncwarp();
+    }
+}
+
+bool make_cell3(const float* host, Cell3& c) {
+    if (host == nullptr) return false;
+    for (int k = 0; k < 9; ++k) c.c[k] = host[k];
+    return true;
+}
+
+inline int grid_of(int64_t work, int per) {
+    const int64_t g = (work + per - 1) / per;
+    return int(g < 148 * 32 ? (g > 0 ? g : 1) : 148 * 32);
+}
+
+size_t conv_smem(int per_warp) { return sizeof(float) * (616 + size_t(kNqWarps) * per_warp); }
+
+}  // namespace
+}  // namespace fmd
+
+using namespace fmd;
+
+extern "C" {
+
+fmd_status fmd_nequip_edge_basis(const float* positions, const float* cell_host, const int32_t* edge_index,
+                                 const float* edge_image, const float* override_vec, const int64_t* n_real,
+                                 int64_t n_edges, float r_max, int32_t n_basis, int32_t poly_p, float* Y, float* B,
+                                 float* geo, void* stream) {
+    BasisArgs a{};
+    if (n_edges < 0 || !(r_max > 0.f) || n_basis < 1 || n_basis > 32 || poly_p < 2 || !make_cell3(cell_host, a.cell))
+        return FMD_ERR_INVALID_ARGUMENT;
+    if (n_edges == 0) return FMD_OK;
+    if (positions == nullptr || edge_index == nullptr || edge_image == nullptr || Y == nullptr || B == nullptr ||
+        geo == nullptr)
+        return FMD_ERR_INVALID_ARGUMENT;
+    a.pos = positions;
+    a.edge_index = edge_index;
+    a.edge_image = edge_image;
+    a.override_vec = override_vec;
+    a.n_real = n_real;
+    a.n_edges = n_edges;
+    a.r_max = r_max;
+    a.n_basis = n_basis;
+    a.poly_p = poly_p;
+    a.Y = Y;
+    a.B = B;
+    a.geo = geo;
+    nq_basis_kernel<<<grid_of(n_edges, 256), 256, 0, as_stream(stream)>>>(a);
+    return check_launch();
+}
+
+fmd_status fmd_nequip_edge_basis_bwd(const float* geo, const float* dY, const float* dB, const float* override_vec,
+                                     const int64_t* n_real, int64_t n_edges, float r_max, int32_t n_basis,
+                                     int32_t poly_p, float* grad_vec, void* stream) {
+    BasisArgs a{};
+    if (n_edges < 0 || !(r_max > 0.f) || n_basis < 1 || n_basis > 32 || poly_p < 2) return FMD_ERR_INVALID_ARGUMENT;
+    if (n_edges == 0) return FMD_OK;
+    if (geo == nullptr || dY == nullptr || dB == nullptr || grad_vec == nullptr) return FMD_ERR_INVALID_ARGUMENT;
+    a.geo = const_cast<float*>(geo);
+    a.override_vec = override_vec;
+    a.n_real = n_real;
+    a.n_edges = n_edges;
+    a.r_max = r_max;
+    a.n_basis = n_basis;
+    a.poly_p = poly_p;
+    nq_basis_bwd_kernel<<<grid_of(n_edges, 256), 256, 0, as_stream(stream)>>>(a, dY, dB, grad_vec);
+    return check_launch();
+}
+
+static fmd_status conv_args(ConvArgs& a, const float* x, const float* Y, const float* W, const float* cg,
+                            const int32_t* edge_index, const int64_t* recv_off, const int64_t* send_off,
+                            const int32_t* send_perm, int64_t n_atoms, float inv_avg) {
+    if (n_atoms < 0 || !(inv_avg > 0.f)) return FMD_ERR_INVALID_ARGUMENT;
+    if (x == nullptr || cg == nullptr || recv_off == nullptr) return FMD_ERR_INVALID_ARGUMENT;
+    a = ConvArgs{x, Y, W, cg, edge_index, recv_off, send_off, send_perm, n_atoms, inv_avg};
+    return FMD_OK;
+}
+
+static fmd_status grant_once(const void* kernel, size_t bytes, bool& done) {
+    if (done || bytes <= 48 * 1024) return FMD_OK;
+    const cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+    if (err != cudaSuccess) return record_cuda_error(err);
+    done = true;
+    return FMD_OK;
+}
+
+fmd_status fmd_nequip_conv(const float* x, const float* Y, const float* W, const float* cg,
+                           const int32_t* edge_index, const int64_t* recv_off, int64_t n_atoms, float inv_avg,
+                           float* messages, void* stream) {
+    ConvArgs a;
+    fmd_status st = conv_args(a, x, Y, W, cg, edge_index, recv_off, nullptr, nullptr, n_atoms, inv_avg);
+    if (st != FMD_OK) return st;
+    if (n_atoms == 0) return FMD_OK;
+    if (messages == nullptr) return FMD_ERR_INVALID_ARGUMENT;
+    static bool granted = false;
+    const size_t smem = conv_smem(kMW);
+    if ((st = grant_once((const void*)nq_conv_kernel, smem, granted)) != FMD_OK) return st;
+    nq_conv_kernel<<<grid_of(n_atoms, kNqWarps), 32 * kNqWarps, smem, as_stream(stream)>>>(a, messages);
+    return check_launch();
+}
+
+fmd_status fmd_nequip_conv_bwd(const float* x, const float* Y, const float* W, const float* cg,
+                               const int32_t* edge_index, const int64_t* recv_off, const int64_t* send_off,
+                               const int32_t* send_perm, int64_t n_atoms, float inv_avg, const float* grad_messages,
+                               float* grad_x, float* grad_W, float* grad_Y, void* stream) {
+    ConvArgs a;
+    fmd_status st = conv_args(a, x, Y, W, cg, edge_index, recv_off, send_off, send_perm, n_atoms, inv_avg);
+    if (st != FMD_OK) return st;
+    if (n_atoms == 0) return FMD_OK;
+    if (grad_messages == nullptr || grad_x == nullptr || grad_W == nullptr || grad_Y == nullptr ||
+        send_off == nullptr)
+        return FMD_ERR_INVALID_ARGUMENT;
+    static bool granted_e = false, granted_x = false;
+    const size_t smem_e = conv_smem(kMW), smem_x = conv_smem(kXW);
+    if ((st = grant_once((const void*)nq_conv_bwd_edge_kernel, smem_e, granted_e)) != FMD_OK) return st;
+    if ((st = grant_once((const void*)nq_conv_bwd_x_kernel, smem_x, granted_x)) != FMD_OK) return st;
+    const cudaStream_t s = as_stream(stream);
+    nq_conv_bwd_edge_kernel<<<grid_of(n_atoms, kNqWarps), 32 * kNqWarps, smem_e, s>>>(a, grad_messages, grad_W,
+                                                                                       grad_Y);
+    if ((st = check_launch()) != FMD_OK) return st;
+    nq_conv_bwd_x_kernel<<<grid_of(n_atoms, kNqWarps), 32 * kNqWarps, smem_x, s>>>(a, grad_messages, grad_x);
+    return check_launch();
+}
+
+}  // extern "C"

@@ -1,0 +1,222 @@
+"""NequIP-architecture (SevenNet-0-style) potential on this build's kernels: BASELINE config 3's model.
+
+The reference wraps upstream SevenNet (fastmd/models/sevennet.py, ``sevenn==0.13.0``: an E(3)-equivariant
+NequIP network); this is the same architecture family with random weights, as config 3 asks: species
+embedding to 128x0e; 5 interaction blocks on node features 128x0e + 64x1e + 32x2e (no parity), each a
+self-connection (an element-dependent linear per l), a linear per l, a tensor-product convolution
+over the neighbours weighted per edge by a radial network (8 Bessel functions with a polynomial
+envelope -> 64 -> 64 -> 960 path weights, SiLU, no bias) over the 15 couplings l1 (x) l2 -> l3 of the
+spherical harmonics up to l = 2, normalised by the average neighbour count, a second linear per l
+and a gated nonlinearity (SiLU on the scalars, sigmoid gates on l = 1, 2), plus the self-connection;
+then a scalar readout 128 -> 64 -> 1, scaled and shifted, summed per system in FP64. Forces are minus
+the position gradient, through the autograd graph of this build's kernels: the edge basis and its
+backward (``fmd_nequip_edge_basis``), the convolution and its backward (``fmd_nequip_conv``), the
+linears on the tcgen05 wide GEMM (``precision="tf32x3"``) or its IEEE path (``"ieee"``), the position
+gradient summed over the receiver and sender CSRs (``fmd_csr_segment_sum``). Element indices are
+atomic number - 1 (89 elements). The padded rows of an exact-rc build (``PaddingRule("exact_rc_loops")``,
+fastmd/models/sevennet.py:16-22) read the override vector, which the envelope maps to zero.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+from torch import Tensor
+from torch.autograd import Function
+
+from . import _lib, ops, wide_gemm
+from ._lib import call, ptr, stream
+from .graph import _host_cell
+
+MULT = (128, 64, 32)
+DIM = (1, 3, 5)
+PATHS = [(l1, l2, l3) for l1 in range(3) for l2 in range(3) for l3 in range(3) if abs(l1 - l2) <= l3 <= l1 + l2]
+X_WIDTH = sum(m * d for m, d in zip(MULT, DIM))          # 480
+M_MULT = tuple(sum(MULT[p[0]] for p in PATHS if p[2] == l) for l in range(3))  # (224, 384, 352)
+W_WIDTH = sum(MULT[p[0]] for p in PATHS)                  # 960
+
+
+@dataclass(frozen=True)
+class NequIPConfig:
+    num_layers: int = 5
+    r_max: float = 5.0
+    num_bessel: int = 8
+    poly_p: int = 6
+    radial_hidden: int = 64
+    avg_num_neighbors: float = 11.0
+    n_elements: int = 89
+    readout_hidden: int = 64
+    scale: float = 1.0
+    shift: float = 0.0
+
+
+def init_weights(config: NequIPConfig, seed: int = 1) -> dict[str, np.ndarray]:
+    """Random float32 weights (normal, scaled by 1 / sqrt(fan-in))."""
+    rng = np.random.default_rng(seed)
+
+    def normal(*shape, fan_in):
+        return (rng.standard_normal(shape) / np.sqrt(fan_in)).astype(np.float32)
+
+    w = {"embed": rng.standard_normal((config.n_elements, MULT[0])).astype(np.float32)}
+    H = config.radial_hidden
+    for L in range(config.num_layers):
+        for l in range(3):
+            w[f"L{L}.sc{l}"] = normal(config.n_elements, MULT[l], MULT[l], fan_in=MULT[l])
+            w[f"L{L}.lin1_{l}"] = normal(MULT[l], MULT[l], fan_in=MULT[l])
+        w[f"L{L}.rad1"] = normal(H, config.num_bessel, fan_in=config.num_bessel)
+        w[f"L{L}.rad2"] = normal(H, H, fan_in=H)
+        w[f"L{L}.rad3"] = normal(W_WIDTH, H, fan_in=H)
+        w[f"L{L}.lin2_0"] = normal(M_MULT[0], MULT[0] + MULT[1] + MULT[2], fan_in=M_MULT[0])
+        w[f"L{L}.lin2_1"] = normal(M_MULT[1], MULT[1], fan_in=M_MULT[1])
+        w[f"L{L}.lin2_2"] = normal(M_MULT[2], MULT[2], fan_in=M_MULT[2])
+    w["readout1"] = normal(config.readout_hidden, MULT[0], fan_in=MULT[0])
+    w["readout2"] = normal(1, config.readout_hidden, fan_in=config.readout_hidden)
+    return w
+
+
+def coupling_table() -> np.ndarray:
+    """The 615 dense coupling constants of the 15 paths (in path order), float32."""
+    from ._coupling import clebsch_gordan
+
+    return np.concatenate([clebsch_gordan(*p).reshape(-1) for p in PATHS]).astype(np.float32)
+
+
+class _EdgeBasis(Function):
+    """(Y [E, 9], B [E, n_basis]) of the edges; the backward returns the position gradient."""
+
+    @staticmethod
+    def forward(ctx, pos, model, batch):
+        E = int(batch.edge_index.shape[0])
+        dev = pos.device
+        c = model.config
+        Y = torch.empty(E, 9, device=dev)
+        B = torch.empty(E, c.num_bessel, device=dev)
+        geo = torch.empty(E, 4, device=dev)
+        _, cell_ptr = _host_cell(batch.cell)
+        override = getattr(batch, "edge_vec_override", None)
+        call("fmd_nequip_edge_basis", ptr(pos), cell_ptr, ptr(batch.edge_index), ptr(batch.edge_image), ptr(override),
+             ptr(batch.n_edges) if override is not None else None, E, c.r_max, c.num_bessel, c.poly_p, ptr(Y), ptr(B),
+             ptr(geo), stream(dev))
+        ctx.model, ctx.batch = model, batch
+        ctx.save_for_backward(geo)
+        return Y, B
+
+    @staticmethod
+    def backward(ctx, dY, dB):
+        (geo,) = ctx.saved_tensors
+        batch, c = ctx.batch, ctx.model.config
+        E, N = int(geo.shape[0]), batch.n_real
+        g = torch.empty(E, 3, device=geo.device)
+        override = getattr(batch, "edge_vec_override", None)
+        call("fmd_nequip_edge_basis_bwd", ptr(geo), ptr(dY.contiguous()), ptr(dB.contiguous()), ptr(override),
+             ptr(batch.n_edges) if override is not None else None, E, c.r_max, c.num_bessel, c.poly_p, ptr(g),
+             stream(geo.device))
+        # dE/dpos_a = sum over sent edges (a = neighbour) - sum over received edges (a = centre)
+        n_pos = batch.positions.shape[0]
+        recv = ops.csr_segment_sum(g, batch.edge_index[:, 0].long(), N, None, batch.recv_off[:N + 1], True)
+        send = ops.csr_segment_sum(g, batch.edge_index[:, 1].long(), N, batch.send_perm.long(),
+                                   batch.send_off[:N + 1])
+        grad = torch.zeros(n_pos, 3, device=geo.device)
+        grad[:N] = send - recv
+        return grad, None, None
+
+
+class _Conv(Function):
+    @staticmethod
+    def forward(ctx, x, Y, W, model, batch):
+        N = batch.n_real
+        m = torch.empty(N, int(sum(M_MULT[l] * DIM[l] for l in range(3))), device=x.device)
+        call("fmd_nequip_conv", ptr(x), ptr(Y), ptr(W), ptr(model.cg), ptr(batch.edge_index), ptr(batch.recv_off), N,
+             1.0 / model.config.avg_num_neighbors, ptr(m), stream(x.device))
+        ctx.save_for_backward(x, Y, W)
+        ctx.model, ctx.batch = model, batch
+        return m
+
+    @staticmethod
+    def backward(ctx, dm):
+        x, Y, W = ctx.saved_tensors
+        model, batch = ctx.model, ctx.batch
+        gx, gW, gY = torch.empty_like(x), torch.empty_like(W), torch.empty_like(Y)
+        call("fmd_nequip_conv_bwd", ptr(x), ptr(Y), ptr(W), ptr(model.cg), ptr(batch.edge_index), ptr(batch.recv_off),
+             ptr(batch.send_off), ptr(batch.send_perm), batch.n_real, 1.0 / model.config.avg_num_neighbors,
+             ptr(dm.contiguous()), ptr(gx), ptr(gW), ptr(gY), stream(x.device))
+        return gx, gY, gW, None, None
+
+
+def _split(x: Tensor, widths) -> list[Tensor]:
+    """[N, sum(m d)] -> per l [N, m, d] views."""
+    out, off = [], 0
+    for m, d in widths:
+        out.append(x[:, off:off + m * d].reshape(-1, m, d))
+        off += m * d
+    return out
+
+
+class NequIPModel:
+    """The config-3 potential on the device. ``energy_forces(batch)`` -> (energy [1] fp64, forces [N, 3])
+    for a ``GraphBatch`` of one system (receiver and sender CSRs of its edges)."""
+
+    def __init__(self, config: NequIPConfig | None = None, weights: dict | None = None, *, seed: int = 1,
+                 device="cuda", precision: str = "tf32x3") -> None:
+        self.config = config or NequIPConfig()
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise _lib.FastMDLibraryError("the NequIP kernels run on CUDA devices only")
+        host = weights if weights is not None else init_weights(self.config, seed)
+        self.host_weights = host
+        self.w = {k: torch.as_tensor(v, dtype=torch.float32, device=self.device) for k, v in host.items()}
+        # the matrices the GEMM reads as [out, in]
+        self.lin = {k: v.t().contiguous() for k, v in self.w.items() if ".lin" in k}
+        self.sc = {k: v.transpose(1, 2).contiguous() for k, v in self.w.items() if ".sc" in k}
+        self.precision = precision
+        self.cg = torch.as_tensor(coupling_table(), device=self.device)
+
+    def _linear(self, x, weight):
+        return wide_gemm.linear(x, weight, precision=self.precision)
+
+    def _per_l(self, xl: Tensor, weight: Tensor) -> Tensor:
+        """[N, u, d] @ W [u, v] -> [N, v, d] (W given as [v, u])."""
+        n, u, d = xl.shape
+        rows = xl.transpose(1, 2).reshape(n * d, u)
+        return self._linear(rows, weight).reshape(n, d, -1).transpose(1, 2)
+
+    def _self_connection(self, xl: Tensor, L: int, l: int, elem: Tensor, groups) -> Tensor:
+        n, u, d = xl.shape
+        out = torch.zeros(n, u, d, device=xl.device)
+        for z, idx in groups:
+            out = out.index_copy(0, idx, self._per_l(xl.index_select(0, idx), self.sc[f"L{L}.sc{l}"][z]))
+        return out
+
+    def energy_forces(self, batch) -> tuple[Tensor, Tensor]:
+        c = self.config
+        N = batch.n_real
+        elem = (batch.species[:N].long() - 1)
+        groups = [(int(z), (elem == z).nonzero().reshape(-1)) for z in torch.unique(elem).tolist()]
+        with torch.enable_grad():
+            pos = batch.positions.detach().requires_grad_(True)
+            Y, B = _EdgeBasis.apply(pos, self, batch)
+            x = torch.cat([self.w["embed"][elem], torch.zeros(N, X_WIDTH - MULT[0], device=self.device)], 1)
+            for L in range(c.num_layers):
+                xs = _split(x, zip(MULT, DIM))
+                sc = [self._self_connection(xs[l], L, l, elem, groups) for l in range(3)]
+                h = torch.cat([self._per_l(xs[l], self.lin[f"L{L}.lin1_{l}"]).reshape(N, -1) for l in range(3)], 1)
+                r = torch.nn.functional.silu(self._linear(B, self.w[f"L{L}.rad1"]))
+                r = torch.nn.functional.silu(self._linear(r, self.w[f"L{L}.rad2"]))
+                W = self._linear(r, self.w[f"L{L}.rad3"])
+                m = _Conv.apply(h.contiguous(), Y, W.contiguous(), self, batch)
+                ms = _split(m, zip(M_MULT, DIM))
+                o = [self._per_l(ms[l], self.lin[f"L{L}.lin2_{l}"]) for l in range(3)]
+                scal = torch.nn.functional.silu(o[0][:, :MULT[0], 0])
+                gates = torch.sigmoid(o[0][:, MULT[0]:, 0])
+                g1 = o[1] * gates[:, :MULT[1], None]
+                g2 = o[2] * gates[:, MULT[1]:, None]
+                x = torch.cat([scal + sc[0][:, :, 0], (g1 + sc[1]).reshape(N, -1), (g2 + sc[2]).reshape(N, -1)], 1)
+            hid = self._linear(x[:, :MULT[0]].contiguous(), self.w["readout1"])
+            e_atom = self._linear(hid, self.w["readout2"])[:, 0] * c.scale + c.shift
+            energy = e_atom.double().sum()
+            (grad,) = torch.autograd.grad(energy, pos)
+        return energy.detach().reshape(1), (-grad[:N]).detach()
+
+
+__all__ = ["NequIPConfig", "NequIPModel", "coupling_table", "init_weights", "PATHS"]

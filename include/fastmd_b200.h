@@ -745,6 +745,45 @@ FMD_API fmd_status fmd_mace_fused_step(const fmd_mace_fused_weights* weights, co
                                        int32_t n_systems, int32_t channels, float* forces, double* energy,
                                        int32_t stages, void* stream);
 
+/* ------------------- NequIP-architecture (SevenNet-0-style) backbone (config 3) */
+
+/* Per edge e (centre i receives from neighbour j with its image): the edge
+ * vector r = pos[j] - pos[i] + image @ cell (rows at or past *n_real take
+ * override_vec[e] instead when it is given: exact-rc padding), the real
+ * spherical harmonics Y [E, 9] = [1 | sqrt3 u | sqrt15 xy, sqrt15 yz,
+ * sqrt5/2 (3z^2 - 1), sqrt15 xz, sqrt15/2 (x^2 - y^2)] of u = r / |r|, the
+ * radial functions B [E, n_basis] = sqrt(2/rc) sin(n pi d / rc) / d times the
+ * polynomial envelope of order poly_p, and geo [E, 4] = (u, d) for the
+ * backward. The NequIP/SevenNet edge embedding (fastmd/models/sevennet.py,
+ * upstream sevenn 0.13.0). */
+FMD_API fmd_status fmd_nequip_edge_basis(const float* positions, const float* cell_host, const int32_t* edge_index,
+                                         const float* edge_image, const float* override_vec, const int64_t* n_real,
+                                         int64_t n_edges, float r_max, int32_t n_basis, int32_t poly_p, float* Y,
+                                         float* B, float* geo, void* stream);
+/* grad_vec [E, 3] = dE/dr of every edge from dY [E, 9] and dB [E, n_basis]
+ * (override rows: 0). */
+FMD_API fmd_status fmd_nequip_edge_basis_bwd(const float* geo, const float* dY, const float* dB,
+                                             const float* override_vec, const int64_t* n_real, int64_t n_edges,
+                                             float r_max, int32_t n_basis, int32_t poly_p, float* grad_vec,
+                                             void* stream);
+/* The radial-weighted tensor-product convolution of node features x
+ * [N, 480] (128 x l0 | 64 x l1 | 32 x l2, channel-major) over the 15
+ * coupling paths (l1, l2 -> l3 <= 2, path order l1, l2, l3): messages
+ * [N, 3136] = inv_avg * sum over the receiver's edges (recv_off, rows sorted
+ * by centre) of W[e, path, u] CG[path] . (x[j, l1, u] (x) Y[e, l2]); W
+ * [E, 960], cg the 615 dense coupling constants. Deterministic (one warp per
+ * receiver, its edges in order). */
+FMD_API fmd_status fmd_nequip_conv(const float* x, const float* Y, const float* W, const float* cg,
+                                   const int32_t* edge_index, const int64_t* recv_off, int64_t n_atoms, float inv_avg,
+                                   float* messages, void* stream);
+/* Its backward from grad_messages [N, 3136]: grad_W [E, 960] and grad_Y
+ * [E, 9] per receiver, grad_x [N, 480] per sender (send_off / send_perm). */
+FMD_API fmd_status fmd_nequip_conv_bwd(const float* x, const float* Y, const float* W, const float* cg,
+                                       const int32_t* edge_index, const int64_t* recv_off, const int64_t* send_off,
+                                       const int32_t* send_perm, int64_t n_atoms, float inv_avg,
+                                       const float* grad_messages, float* grad_x, float* grad_W, float* grad_Y,
+                                       void* stream);
+
 /* -------------------------------------- Nose-Hoover chain integrator (F1/F3) */
 
 /* Flat fp64 state of R replicas of n atoms each and chain length M:
