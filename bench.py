@@ -52,7 +52,7 @@ def _args():
     p.add_argument("--steps-per-launch", type=int, default=10)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-ops", action="store_true", help="skip the config-2 op microbenchmark")
-    p.add_argument("--op", choices=["wide_gemm", "hbm_ops", "bond_graph"], default=None,
+    p.add_argument("--op", choices=["wide_gemm", "hbm_ops", "bond_graph", "nequip"], default=None,
                    help="time one op alone (the profiling entry of profiles/): prints its own JSON line")
     p.add_argument("--rows", type=int, default=300_000, help="rows of --op wide_gemm")
     p.add_argument("--atoms", type=int, default=25_000, help="atoms of --op hbm_ops (config 2's box density)")
@@ -700,6 +700,49 @@ def _op_bond_graph(args):
     return out
 
 
+def _op_nequip(args):
+    """``--op nequip``: BASELINE config 3, a 10x10x10 ABX3 supercell (5,000 atoms, jitter seed 3) under the
+    NequIP-architecture (SevenNet-0-style) potential (5 interaction blocks, 128x0e + 64x1e + 32x2e, rc
+    5 A, random weights, the linears on the 3xTF32 tensor-core GEMM), NVT-NHC at 500 K with dt 0.25 fs,
+    in the whole_step mode (windows of 10 steps as one CUDA graph; eager if the capture is refused);
+    ``--steps`` timed steps after ``--warmup`` (CUDA events around the timed windows)."""
+    import torch
+
+    from fastmd_b200 import units
+    from fastmd_b200.nequip import NequIPConfig, NequIPModel
+    from fastmd_b200.structures import perovskite
+    from fastmd_b200.whole_step import GPUResidentMolecularDynamics
+
+    dev = torch.device("cuda", 0)
+    pos, cell, numbers, masses = perovskite(reps=10, seed=3)
+    model = NequIPModel(NequIPConfig(), device=dev)
+    steps = max(10, args.steps // 10 * 10)
+    out = {"op": "nequip", "atoms": int(pos.shape[0]), "layers": 5}
+    for execution in ("whole_step", "eager"):
+        try:
+            md = GPUResidentMolecularDynamics(model, positions=pos, cell=cell, atomic_numbers=numbers, masses=masses,
+                                              temperature_K=TEMPERATURE, timestep=0.25 * units.fs,
+                                              tdamp=25 * units.fs, steps_per_launch=10, execution=execution,
+                                              device=dev)
+        except Exception as error:  # a capture the driver refuses: report it and time the eager mode
+            out[f"{execution}_error"] = f"{type(error).__name__}: {str(error)[:200]}"
+            continue
+        md.run(max(10, args.warmup // 10 * 10))
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        md.run(steps)
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / steps
+        out.update({"execution": execution, "steps": steps, "ms_per_step": round(ms, 4),
+                    "atom_steps_per_s": round(pos.shape[0] / ms * 1e3, 1),
+                    "edges": int(md.builder.batch.n_edges.item()) if execution == "whole_step" else None,
+                    "temperature_K": round(float(md.integrator.temperature()), 1)})
+        break
+    return out
+
+
 def _op(args):
     """One op alone on cuda:0, the profiling entry: ``--op wide_gemm`` runs the config-2 first edge
     layer (264 -> 256, bias, SiLU, 3xTF32 on tcgen05) over ``--rows`` rows, 3 warm-up launches then
@@ -709,6 +752,8 @@ def _op(args):
         return _op_hbm(args)
     if args.op == "bond_graph":
         return _op_bond_graph(args)
+    if args.op == "nequip":
+        return _op_nequip(args)
     import torch
 
     from fastmd_b200 import wide_gemm

@@ -93,7 +93,7 @@ class _EdgeBasis(Function):
         Y = torch.empty(E, 9, device=dev)
         B = torch.empty(E, c.num_bessel, device=dev)
         geo = torch.empty(E, 4, device=dev)
-        _, cell_ptr = _host_cell(batch.cell)
+        cell_ptr = model.cell_ptr(batch)
         override = getattr(batch, "edge_vec_override", None)
         call("fmd_nequip_edge_basis", ptr(pos), cell_ptr, ptr(batch.edge_index), ptr(batch.edge_image), ptr(override),
              ptr(batch.n_edges) if override is not None else None, E, c.r_max, c.num_bessel, c.poly_p, ptr(Y), ptr(B),
@@ -172,6 +172,23 @@ class NequIPModel:
         self.precision = precision
         self.cg = torch.as_tensor(coupling_table(), device=self.device)
 
+    # ------------------------------------------------------------ per-system state (no host work per call)
+    def prepare(self, batch):
+        """The element groups and the host cell of ``batch``'s system (host reads, once per system; not
+        inside a capture); returns the batch."""
+        N = batch.n_real
+        elem = batch.species[:N].long() - 1
+        if int(elem.min()) < 0 or int(elem.max()) >= self.config.n_elements:
+            raise ValueError(f"atomic numbers outside 1..{self.config.n_elements}")
+        self._elem = elem
+        self._groups = [(int(z), (elem == z).nonzero().reshape(-1)) for z in torch.unique(elem).tolist()]
+        self._cell_host, self._cell_ptr = _host_cell(batch.cell)
+        self._prepared = (batch.species.data_ptr(), batch.cell.data_ptr())
+        return batch
+
+    def cell_ptr(self, batch):
+        return self._cell_ptr
+
     def _linear(self, x, weight):
         return wide_gemm.linear(x, weight, precision=self.precision)
 
@@ -188,11 +205,16 @@ class NequIPModel:
             out = out.index_copy(0, idx, self._per_l(xl.index_select(0, idx), self.sc[f"L{L}.sc{l}"][z]))
         return out
 
-    def energy_forces(self, batch) -> tuple[Tensor, Tensor]:
+    def energy_forces(self, batch, n_systems: int = 1) -> tuple[Tensor, Tensor]:
+        """(energy [1] fp64, forces [N, 3]) of one system; capturable in a CUDA graph once ``prepare``
+        ran for the system (no host synchronisation)."""
+        if n_systems != 1:
+            raise ValueError("the NequIP model evaluates one system per batch")
+        if getattr(self, "_prepared", None) != (batch.species.data_ptr(), batch.cell.data_ptr()):
+            self.prepare(batch)
         c = self.config
         N = batch.n_real
-        elem = (batch.species[:N].long() - 1)
-        groups = [(int(z), (elem == z).nonzero().reshape(-1)) for z in torch.unique(elem).tolist()]
+        elem, groups = self._elem, self._groups
         with torch.enable_grad():
             pos = batch.positions.detach().requires_grad_(True)
             Y, B = _EdgeBasis.apply(pos, self, batch)
@@ -217,6 +239,8 @@ class NequIPModel:
             energy = e_atom.double().sum()
             (grad,) = torch.autograd.grad(energy, pos)
         return energy.detach().reshape(1), (-grad[:N]).detach()
+
+    energy_forces_fused = energy_forces
 
 
 __all__ = ["NequIPConfig", "NequIPModel", "coupling_table", "init_weights", "PATHS"]

@@ -53,3 +53,23 @@ def test_padded_exact_rc_build_equals_the_ragged_build(cuda):
     assert int(status.flags.item()) == 0 and int(batch.n_edges.item()) < 2400
     e2, f2 = model.energy_forces(batch)
     assert torch.equal(e1, e2) and torch.equal(f1, f2)
+
+
+def test_md_whole_step_equals_eager(cuda):
+    """NVT MD under the NequIP potential: the whole_step mode (windows captured as CUDA graphs, the
+    autograd force evaluation inside) gives the eager mode's trajectory bit for bit."""
+    from fastmd_b200 import units
+    from fastmd_b200.nequip import NequIPConfig, NequIPModel
+    from fastmd_b200.structures import perovskite
+    from fastmd_b200.whole_step import GPUResidentMolecularDynamics
+
+    pos, cell, numbers, masses = perovskite(seed=2)
+    model = NequIPModel(NequIPConfig(num_layers=2), device=cuda)
+    runs = {}
+    for execution in ("whole_step", "eager"):
+        md = GPUResidentMolecularDynamics(model, positions=pos, cell=cell, atomic_numbers=numbers, masses=masses,
+                                          temperature_K=500.0, timestep=0.25 * units.fs, tdamp=25 * units.fs,
+                                          steps_per_launch=5, execution=execution, device=cuda)
+        md.run(20)
+        runs[execution] = md.integrator.state.flat.clone()
+    assert torch.equal(runs["whole_step"], runs["eager"])
