@@ -56,6 +56,7 @@ def _args():
                    help="time one op alone (the profiling entry of profiles/): prints its own JSON line")
     p.add_argument("--rows", type=int, default=300_000, help="rows of --op wide_gemm")
     p.add_argument("--atoms", type=int, default=25_000, help="atoms of --op hbm_ops (config 2's box density)")
+    p.add_argument("--reps", type=int, default=10, help="ABX3 supercell repeats of --op nequip (config 3: 10)")
     return p.parse_args()
 
 
@@ -701,7 +702,8 @@ def _op_bond_graph(args):
 
 
 def _op_nequip(args):
-    """``--op nequip``: BASELINE config 3, a 10x10x10 ABX3 supercell (5,000 atoms, jitter seed 3) under the
+    """``--op nequip``: BASELINE config 3, a 10x10x10 ABX3 supercell (5,000 atoms, jitter seed 3; ``--reps``
+    sets the repeats) under the
     NequIP-architecture (SevenNet-0-style) potential (5 interaction blocks, 128x0e + 64x1e + 32x2e, rc
     5 A, random weights, the linears on the 3xTF32 tensor-core GEMM), NVT-NHC at 500 K with dt 0.25 fs,
     in the whole_step mode (windows of 10 steps as one CUDA graph; eager if the capture is refused);
@@ -714,7 +716,7 @@ def _op_nequip(args):
     from fastmd_b200.whole_step import GPUResidentMolecularDynamics
 
     dev = torch.device("cuda", 0)
-    pos, cell, numbers, masses = perovskite(reps=10, seed=3)
+    pos, cell, numbers, masses = perovskite(reps=args.reps, seed=3)
     model = NequIPModel(NequIPConfig(), device=dev)
     steps = max(10, args.steps // 10 * 10)
     out = {"op": "nequip", "atoms": int(pos.shape[0]), "layers": 5}
