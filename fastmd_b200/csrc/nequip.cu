@@ -14,8 +14,10 @@
 // Convolution (one warp per receiver i, its edges in CSR order, a lane per
 // channel u; the receiver's 3136 accumulators in shared memory, each owned
 // by one lane: deterministic):
-//   m[i, path, u, m3] = inv_avg * sum_e W[e, path, u] sum_{m1, m2}
-//                       CG[m3, m1, m2] x[j(e), l1, u, m1] Y[e, l2, m2]
+//   m[i, path, u, m3] = inv_avg * sum_e W[e, path, u] sum_m1 A_e[path][m3][m1] x[j(e), l1, u, m1]
+// with the edge's coupling matrices A_e[path][m3][m1] = sum_m2 CG[m3, m1, m2]
+// Y[e, l2, m2] formed once per edge (179 floats) and shared by all channels:
+// 8,512 FMA per edge and layer instead of 29,760.
 // Backward per receiver (dW, dY of its edges) and per sender (dx of the atom
 // through its sender CSR), the same sums transposed. Each path is a template
 // instance: the coupling loops unroll with compile-time indices.
@@ -183,12 +185,54 @@ struct ConvArgs {
     float inv_avg;
 };
 
-// one path's contribution of edge e (lane channels u) into the receiver's accumulators
+// A[path][m3][m1] = sum_m2 CG[path][m3, m1, m2] Y[e, l2, m2]: the edge's coupling matrices, shared by
+// every channel u of a path (179 floats per edge); the lanes split their entries
+__host__ __device__ constexpr int a_size(int P) { return dim_of(kPaths[P].l3) * dim_of(kPaths[P].l1); }
+__host__ __device__ constexpr int a_off(int P) {
+    int s = 0;
+    for (int q = 0; q < P; ++q) s += a_size(q);
+    return s;
+}
+constexpr int kAW = a_off(15);  // 179
+constexpr int kTP = 25;         // the largest a_size
+
 template <int P>
-__device__ __forceinline__ void path_fwd(const ConvArgs& a, const float* cg, const float* y, int64_t e, int64_t j,
-                                         float* acc, int lane) {
+__device__ __forceinline__ void path_coupling(const float* cg, const float* y, float* aw, int lane) {
     constexpr PathInfo pi = kPaths[P];
-    constexpr int n1 = dim_of(pi.l1), n2 = dim_of(pi.l2), n3 = dim_of(pi.l3), U = mult_of(pi.l1);
+    constexpr int n1 = dim_of(pi.l1), n2 = dim_of(pi.l2);
+    for (int t = lane; t < a_size(P); t += 32) {
+        const int m3 = t / n1, m1 = t - m3 * n1;
+        float s = 0.f;
+#pragma unroll
+        for (int m2 = 0; m2 < n2; ++m2) s = fmaf(cg[pi.cg_off + (m3 * n1 + m1) * n2 + m2], y[y_off(pi.l2) + m2], s);
+        aw[a_off(P) + t] = s;
+    }
+}
+
+template <int... P>
+__device__ __forceinline__ void edge_couplings(const float* cg, const float* y, float* aw, int lane,
+                                               std::integer_sequence<int, P...>) {
+    (path_coupling<P>(cg, y, aw, lane), ...);
+}
+
+// the coupling matrices of edge e in the warp's aw (ends with a warp barrier)
+__device__ __forceinline__ void load_couplings(const ConvArgs& a, const float* cg, int64_t e, float* aw, int lane) {
+    float y[9];
+#pragma unroll
+    for (int q = 0; q < 9; ++q) y[q] = a.Y[9 * e + q];
+    __syncwarp();  // the previous edge's readers are done
+    edge_couplings(cg, y, aw, lane, std::make_integer_sequence<int, 15>{});
+    __syncwarp();
+}
+
+// one path's contribution of edge e (lane channels u) into the receiver's accumulators:
+// acc[u, m3] += W[e, path, u] sum_m1 A[m3][m1] x[j, l1, u, m1]
+template <int P>
+__device__ __forceinline__ void path_fwd(const ConvArgs& a, const float* aw, int64_t e, int64_t j, float* acc,
+                                         int lane) {
+    constexpr PathInfo pi = kPaths[P];
+    constexpr int n1 = dim_of(pi.l1), n3 = dim_of(pi.l3), U = mult_of(pi.l1);
+#pragma unroll 1
     for (int u = lane; u < U; u += 32) {
         const float w = a.W[e * kWW + pi.w_off + u];
         float xv[n1];
@@ -198,38 +242,34 @@ __device__ __forceinline__ void path_fwd(const ConvArgs& a, const float* cg, con
         for (int m3 = 0; m3 < n3; ++m3) {
             float s = 0.f;
 #pragma unroll
-            for (int m1 = 0; m1 < n1; ++m1)
-#pragma unroll
-                for (int m2 = 0; m2 < n2; ++m2)
-                    s = fmaf(cg[pi.cg_off + (m3 * n1 + m1) * n2 + m2], xv[m1] * y[y_off(pi.l2) + m2], s);
+            for (int m1 = 0; m1 < n1; ++m1) s = fmaf(aw[a_off(P) + m3 * n1 + m1], xv[m1], s);
             acc[pi.m_off + u * n3 + m3] = fmaf(w, s, acc[pi.m_off + u * n3 + m3]);
         }
     }
 }
 
 template <int... P>
-__device__ __forceinline__ void all_paths_fwd(const ConvArgs& a, const float* cg, const float* y, int64_t e,
-                                              int64_t j, float* acc, int lane, std::integer_sequence<int, P...>) {
-    (path_fwd<P>(a, cg, y, e, j, acc, lane), ...);
+__device__ __forceinline__ void all_paths_fwd(const ConvArgs& a, const float* aw, int64_t e, int64_t j, float* acc,
+                                              int lane, std::integer_sequence<int, P...>) {
+    (path_fwd<P>(a, aw, e, j, acc, lane), ...);
 }
 
+// warp shared memory of the kernels: [cg 616 | per warp: rows, A 179 (, T partials 32 x 25)]
 __global__ void __launch_bounds__(32 * kNqWarps) nq_conv_kernel(ConvArgs a, float* __restrict__ m) {
     extern __shared__ __align__(16) float nq_smem[];
-    float* cg = nq_smem;                                   // [616]
-    float* acc = nq_smem + 616 + (threadIdx.x >> 5) * kMW;  // this warp's receiver
+    float* cg = nq_smem;                                            // [616]
+    float* acc = nq_smem + 616 + (threadIdx.x >> 5) * (kMW + kAW);  // this warp's receiver
+    float* aw = acc + kMW;
     for (int t = threadIdx.x; t < kCGN; t += blockDim.x) cg[t] = a.cg[t];
     __syncthreads();
     const int lane = threadIdx.x & 31;
     for (int64_t i = int64_t(blockIdx.x) * kNqWarps + (threadIdx.x >> 5); i < a.n_atoms;
          i += int64_t(gridDim.x) * kNqWarps) {
         for (int t = lane; t < kMW; t += 32) acc[t] = 0.f;
-        __syncwarp();
         for (int64_t e = a.recv_off[i]; e < a.recv_off[i + 1]; ++e) {
             const int64_t j = a.edge_index[2 * e + 1];
-            float y[9];
-#pragma unroll
-            for (int q = 0; q < 9; ++q) y[q] = a.Y[9 * e + q];
-            all_paths_fwd(a, cg, y, e, j, acc, lane, std::make_integer_sequence<int, 15>{});
+            load_couplings(a, cg, e, aw, lane);
+            all_paths_fwd(a, aw, e, j, acc, lane, std::make_integer_sequence<int, 15>{});
         }
         __syncwarp();
         for (int t = lane; t < kMW; t += 32) m[i * kMW + t] = acc[t] * a.inv_avg;
@@ -237,12 +277,17 @@ __global__ void __launch_bounds__(32 * kNqWarps) nq_conv_kernel(ConvArgs a, floa
     }
 }
 
-// dW[e, path, u] and the lane's share of dY[e] of one path (dm: the receiver's message gradient)
+// dW[e, path, u] = sum_m3 g[u, m3] sum_m1 A[m3][m1] x[u, m1]; the lane's share of dY[e]: the path's
+// T[m3][m1] = sum_u W g[u, m3] x[u, m1] folded over the lanes (fixed order), times CG
 template <int P>
-__device__ __forceinline__ void path_bwd_edge(const ConvArgs& a, const float* cg, const float* y, const float* dm,
-                                              int64_t e, int64_t j, float* dW, float* dy, int lane) {
+__device__ __forceinline__ void path_bwd_edge(const ConvArgs& a, const float* cg, const float* aw, const float* dm,
+                                              float* tp, int64_t e, int64_t j, float* dW, float* dy, int lane) {
     constexpr PathInfo pi = kPaths[P];
     constexpr int n1 = dim_of(pi.l1), n2 = dim_of(pi.l2), n3 = dim_of(pi.l3), U = mult_of(pi.l1);
+    float t[n3 * n1];
+#pragma unroll
+    for (int q = 0; q < n3 * n1; ++q) t[q] = 0.f;
+#pragma unroll 1
     for (int u = lane; u < U; u += 32) {
         const float w = a.W[e * kWW + pi.w_off + u];
         float xv[n1];
@@ -254,24 +299,33 @@ __device__ __forceinline__ void path_bwd_edge(const ConvArgs& a, const float* cg
             const float g = dm[pi.m_off + u * n3 + m3];
             float s = 0.f;
 #pragma unroll
-            for (int m1 = 0; m1 < n1; ++m1)
-#pragma unroll
-                for (int m2 = 0; m2 < n2; ++m2) {
-                    const float c = cg[pi.cg_off + (m3 * n1 + m1) * n2 + m2];
-                    s = fmaf(c, xv[m1] * y[y_off(pi.l2) + m2], s);
-                    dy[y_off(pi.l2) + m2] = fmaf(w * g * c, xv[m1], dy[y_off(pi.l2) + m2]);
-                }
+            for (int m1 = 0; m1 < n1; ++m1) {
+                s = fmaf(aw[a_off(P) + m3 * n1 + m1], xv[m1], s);
+                t[m3 * n1 + m1] = fmaf(w * g, xv[m1], t[m3 * n1 + m1]);
+            }
             gw = fmaf(g, s, gw);
         }
         dW[e * kWW + pi.w_off + u] = gw;
     }
+#pragma unroll
+    for (int q = 0; q < n3 * n1; ++q) tp[lane * kTP + q] = t[q];
+    __syncwarp();
+    if (lane < n3 * n1) {
+        float tq = 0.f;
+        for (int l = 0; l < 32; ++l) tq += tp[l * kTP + lane];
+        const int m3 = lane / n1, m1 = lane - m3 * n1;
+#pragma unroll
+        for (int m2 = 0; m2 < n2; ++m2)
+            dy[y_off(pi.l2) + m2] = fmaf(cg[pi.cg_off + (m3 * n1 + m1) * n2 + m2], tq, dy[y_off(pi.l2) + m2]);
+    }
+    __syncwarp();
 }
 
 template <int... P>
-__device__ __forceinline__ void all_paths_bwd_edge(const ConvArgs& a, const float* cg, const float* y,
-                                                   const float* dm, int64_t e, int64_t j, float* dW, float* dy,
-                                                   int lane, std::integer_sequence<int, P...>) {
-    (path_bwd_edge<P>(a, cg, y, dm, e, j, dW, dy, lane), ...);
+__device__ __forceinline__ void all_paths_bwd_edge(const ConvArgs& a, const float* cg, const float* aw,
+                                                   const float* dm, float* tp, int64_t e, int64_t j, float* dW,
+                                                   float* dy, int lane, std::integer_sequence<int, P...>) {
+    (path_bwd_edge<P>(a, cg, aw, dm, tp, e, j, dW, dy, lane), ...);
 }
 
 // per receiver: dW and dY of its edges (dY: lane partials folded by a fixed xor tree)
@@ -280,23 +334,24 @@ __global__ void __launch_bounds__(32 * kNqWarps) nq_conv_bwd_edge_kernel(ConvArg
                                                                          float* __restrict__ dY) {
     extern __shared__ __align__(16) float nq_smem[];
     float* cg = nq_smem;
-    float* dm = nq_smem + 616 + (threadIdx.x >> 5) * kMW;
+    float* dm = nq_smem + 616 + (threadIdx.x >> 5) * (kMW + kAW + 32 * kTP);
+    float* aw = dm + kMW;
+    float* tp = aw + kAW;
     for (int t = threadIdx.x; t < kCGN; t += blockDim.x) cg[t] = a.cg[t];
     __syncthreads();
     const int lane = threadIdx.x & 31;
     for (int64_t i = int64_t(blockIdx.x) * kNqWarps + (threadIdx.x >> 5); i < a.n_atoms;
          i += int64_t(gridDim.x) * kNqWarps) {
+        __syncwarp();
         for (int t = lane; t < kMW; t += 32) dm[t] = dmsg[i * kMW + t] * a.inv_avg;
         __syncwarp();
         for (int64_t e = a.recv_off[i]; e < a.recv_off[i + 1]; ++e) {
             const int64_t j = a.edge_index[2 * e + 1];
-            float y[9], dy[9];
+            load_couplings(a, cg, e, aw, lane);
+            float dy[9];
 #pragma unroll
-            for (int q = 0; q < 9; ++q) {
-                y[q] = a.Y[9 * e + q];
-                dy[q] = 0.f;
-            }
-            all_paths_bwd_edge(a, cg, y, dm, e, j, dW, dy, lane, std::make_integer_sequence<int, 15>{});
+            for (int q = 0; q < 9; ++q) dy[q] = 0.f;
+            all_paths_bwd_edge(a, cg, aw, dm, tp, e, j, dW, dy, lane, std::make_integer_sequence<int, 15>{});
 #pragma unroll
             for (int q = 0; q < 9; ++q)
                 for (int d = 16; d > 0; d >>= 1) dy[q] += __shfl_xor_sync(0xffffffffu, dy[q], d);
@@ -304,37 +359,35 @@ __global__ void __launch_bounds__(32 * kNqWarps) nq_conv_bwd_edge_kernel(ConvArg
 #pragma unroll
                 for (int q = 0; q < 9; ++q) dY[9 * e + q] = dy[q];
         }
-        __syncwarp();
     }
 }
 
-// dx[j, l1, u, m1] += W[e, path, u] sum_{m3, m2} CG[m3, m1, m2] dm[i, path, u, m3] Y[e, l2, m2]
+// dx[j, l1, u, m1] += W[e, path, u] sum_m3 A[m3][m1] dm[i, path, u, m3]
 template <int P>
-__device__ __forceinline__ void path_bwd_x(const ConvArgs& a, const float* cg, const float* y, const float* dmi,
-                                           int64_t e, float* dx, int lane) {
+__device__ __forceinline__ void path_bwd_x(const ConvArgs& a, const float* aw, const float* dmi, int64_t e,
+                                           float* dx, int lane) {
     constexpr PathInfo pi = kPaths[P];
-    constexpr int n1 = dim_of(pi.l1), n2 = dim_of(pi.l2), n3 = dim_of(pi.l3), U = mult_of(pi.l1);
+    constexpr int n1 = dim_of(pi.l1), n3 = dim_of(pi.l3), U = mult_of(pi.l1);
+#pragma unroll 1
     for (int u = lane; u < U; u += 32) {
         const float w = a.W[e * kWW + pi.w_off + u];
+        float g[n3];
+#pragma unroll
+        for (int m3 = 0; m3 < n3; ++m3) g[m3] = dmi[pi.m_off + u * n3 + m3];
 #pragma unroll
         for (int m1 = 0; m1 < n1; ++m1) {
             float s = 0.f;
 #pragma unroll
-            for (int m3 = 0; m3 < n3; ++m3) {
-                const float g = dmi[pi.m_off + u * n3 + m3];
-#pragma unroll
-                for (int m2 = 0; m2 < n2; ++m2)
-                    s = fmaf(cg[pi.cg_off + (m3 * n1 + m1) * n2 + m2], g * y[y_off(pi.l2) + m2], s);
-            }
+            for (int m3 = 0; m3 < n3; ++m3) s = fmaf(aw[a_off(P) + m3 * n1 + m1], g[m3], s);
             dx[x_off(pi.l1) + u * n1 + m1] = fmaf(w, s, dx[x_off(pi.l1) + u * n1 + m1]);
         }
     }
 }
 
 template <int... P>
-__device__ __forceinline__ void all_paths_bwd_x(const ConvArgs& a, const float* cg, const float* y, const float* dmi,
-                                                int64_t e, float* dx, int lane, std::integer_sequence<int, P...>) {
-    (path_bwd_x<P>(a, cg, y, dmi, e, dx, lane), ...);
+__device__ __forceinline__ void all_paths_bwd_x(const ConvArgs& a, const float* aw, const float* dmi, int64_t e,
+                                                float* dx, int lane, std::integer_sequence<int, P...>) {
+    (path_bwd_x<P>(a, aw, dmi, e, dx, lane), ...);
 }
 
 // per sender j: dx[j] over its sender run (the receivers' message gradients read from global memory)
@@ -342,25 +395,23 @@ __global__ void __launch_bounds__(32 * kNqWarps) nq_conv_bwd_x_kernel(ConvArgs a
                                                                       float* __restrict__ dx_out) {
     extern __shared__ __align__(16) float nq_smem[];
     float* cg = nq_smem;
-    float* dx = nq_smem + 616 + (threadIdx.x >> 5) * kXW;
+    float* dx = nq_smem + 616 + (threadIdx.x >> 5) * (kXW + kAW);
+    float* aw = dx + kXW;
     for (int t = threadIdx.x; t < kCGN; t += blockDim.x) cg[t] = a.cg[t];
     __syncthreads();
     const int lane = threadIdx.x & 31;
     for (int64_t j = int64_t(blockIdx.x) * kNqWarps + (threadIdx.x >> 5); j < a.n_atoms;
          j += int64_t(gridDim.x) * kNqWarps) {
-        for (int t = lane; t < kXW; t += 32) dx[t] = 0.f;
         __syncwarp();
+        for (int t = lane; t < kXW; t += 32) dx[t] = 0.f;
         for (int64_t s = a.send_off[j]; s < a.send_off[j + 1]; ++s) {
             const int64_t e = a.send_perm[s];
             const int64_t i = a.edge_index[2 * e];
-            float y[9];
-#pragma unroll
-            for (int q = 0; q < 9; ++q) y[q] = a.Y[9 * e + q];
-            all_paths_bwd_x(a, cg, y, dmsg + i * kMW, e, dx, lane, std::make_integer_sequence<int, 15>{});
+            load_couplings(a, cg, e, aw, lane);
+            all_paths_bwd_x(a, aw, dmsg + i * kMW, e, dx, lane, std::make_integer_sequence<int, 15>{});
         }
         __syncwarp();
         for (int t = lane; t < kXW; t += 32) dx_out[j * kXW + t] = dx[t] * a.inv_avg;
-        __syncwarp();
     }
 }
 
@@ -455,7 +506,7 @@ fmd_status fmd_nequip_conv(const float* x, const float* Y, const float* W, const
     if (n_atoms == 0) return FMD_OK;
     if (messages == nullptr) return FMD_ERR_INVALID_ARGUMENT;
     static bool granted = false;
-    const size_t smem = conv_smem(kMW);
+    const size_t smem = conv_smem(kMW + kAW);
     if ((st = grant_once((const void*)nq_conv_kernel, smem, granted)) != FMD_OK) return st;
     nq_conv_kernel<<<grid_of(n_atoms, kNqWarps), 32 * kNqWarps, smem, as_stream(stream)>>>(a, messages);
     return check_launch();
@@ -473,7 +524,7 @@ fmd_status fmd_nequip_conv_bwd(const float* x, const float* Y, const float* W, c
         send_off == nullptr)
         return FMD_ERR_INVALID_ARGUMENT;
     static bool granted_e = false, granted_x = false;
-    const size_t smem_e = conv_smem(kMW), smem_x = conv_smem(kXW);
+    const size_t smem_e = conv_smem(kMW + kAW + 32 * kTP), smem_x = conv_smem(kXW + kAW);
     if ((st = grant_once((const void*)nq_conv_bwd_edge_kernel, smem_e, granted_e)) != FMD_OK) return st;
     if ((st = grant_once((const void*)nq_conv_bwd_x_kernel, smem_x, granted_x)) != FMD_OK) return st;
     const cudaStream_t s = as_stream(stream);
