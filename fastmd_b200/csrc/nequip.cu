@@ -195,6 +195,15 @@ __host__ __device__ constexpr int a_off(int P) {
 }
 constexpr int kAW = a_off(15);  // 179
 constexpr int kTP = 25;         // the largest a_size
+// per-warp shared-memory strides (floats): the staged weight/feature rows start 16-byte aligned (a multiple
+// of 4 floats from the 16-byte aligned base, 616 floats of CG table first)
+constexpr int kFwdRows = kMW + kAW + 1;                 // offset of the weight row in a forward warp slot
+constexpr int kFwdStride = kFwdRows + kWW + kXW;        // 4756
+constexpr int kBwdRows = kMW + kAW + 32 * kTP + 1;      // offset of the weight row in a backward warp slot
+constexpr int kBwdStride = kBwdRows + kWW + kXW;        // 5556
+static_assert(616 % 4 == 0 && kFwdRows % 4 == 0 && kFwdStride % 4 == 0 && kBwdRows % 4 == 0 &&
+                  kBwdStride % 4 == 0 && kWW % 4 == 0 && kXW % 4 == 0,
+              "staged rows must stay 16-byte aligned");
 
 template <int P>
 __device__ __forceinline__ void path_coupling(const float* cg, const float* y, float* aw, int lane) {
@@ -225,19 +234,38 @@ __device__ __forceinline__ void load_couplings(const ConvArgs& a, const float* c
     __syncwarp();
 }
 
+// the edge's weight row (960 floats) and its sender's feature row (480 floats) in the warp's shared
+// memory: 16-byte loads issued together (one memory round trip per edge instead of one per path)
+__device__ __forceinline__ void stage_rows(const ConvArgs& a, int64_t e, int64_t j, float* ws, float* xs, int lane) {
+    const float4* wsrc = reinterpret_cast<const float4*>(a.W + e * kWW);
+    const float4* xsrc = reinterpret_cast<const float4*>(a.x + j * kXW);
+    float4 wv[(kWW / 4 + 31) / 32], xv[(kXW / 4 + 31) / 32];
+#pragma unroll
+    for (int r = 0; r < (kWW / 4 + 31) / 32; ++r)
+        if (lane + 32 * r < kWW / 4) wv[r] = wsrc[lane + 32 * r];
+#pragma unroll
+    for (int r = 0; r < (kXW / 4 + 31) / 32; ++r)
+        if (lane + 32 * r < kXW / 4) xv[r] = xsrc[lane + 32 * r];
+#pragma unroll
+    for (int r = 0; r < (kWW / 4 + 31) / 32; ++r)
+        if (lane + 32 * r < kWW / 4) reinterpret_cast<float4*>(ws)[lane + 32 * r] = wv[r];
+#pragma unroll
+    for (int r = 0; r < (kXW / 4 + 31) / 32; ++r)
+        if (lane + 32 * r < kXW / 4) reinterpret_cast<float4*>(xs)[lane + 32 * r] = xv[r];
+}
+
 // one path's contribution of edge e (lane channels u) into the receiver's accumulators:
 // acc[u, m3] += W[e, path, u] sum_m1 A[m3][m1] x[j, l1, u, m1]
 template <int P>
-__device__ __forceinline__ void path_fwd(const ConvArgs& a, const float* aw, int64_t e, int64_t j, float* acc,
-                                         int lane) {
+__device__ __forceinline__ void path_fwd(const float* ws, const float* xs, const float* aw, float* acc, int lane) {
     constexpr PathInfo pi = kPaths[P];
     constexpr int n1 = dim_of(pi.l1), n3 = dim_of(pi.l3), U = mult_of(pi.l1);
 #pragma unroll 1
     for (int u = lane; u < U; u += 32) {
-        const float w = a.W[e * kWW + pi.w_off + u];
+        const float w = ws[pi.w_off + u];
         float xv[n1];
 #pragma unroll
-        for (int m1 = 0; m1 < n1; ++m1) xv[m1] = a.x[j * kXW + x_off(pi.l1) + u * n1 + m1];
+        for (int m1 = 0; m1 < n1; ++m1) xv[m1] = xs[x_off(pi.l1) + u * n1 + m1];
 #pragma unroll
         for (int m3 = 0; m3 < n3; ++m3) {
             float s = 0.f;
@@ -249,17 +277,19 @@ __device__ __forceinline__ void path_fwd(const ConvArgs& a, const float* aw, int
 }
 
 template <int... P>
-__device__ __forceinline__ void all_paths_fwd(const ConvArgs& a, const float* aw, int64_t e, int64_t j, float* acc,
-                                              int lane, std::integer_sequence<int, P...>) {
-    (path_fwd<P>(a, aw, e, j, acc, lane), ...);
+__device__ __forceinline__ void all_paths_fwd(const float* ws, const float* xs, const float* aw, float* acc, int lane,
+                                              std::integer_sequence<int, P...>) {
+    (path_fwd<P>(ws, xs, aw, acc, lane), ...);
 }
 
 // warp shared memory of the kernels: [cg 616 | per warp: rows, A 179 (, T partials 32 x 25)]
 __global__ void __launch_bounds__(32 * kNqWarps) nq_conv_kernel(ConvArgs a, float* __restrict__ m) {
     extern __shared__ __align__(16) float nq_smem[];
     float* cg = nq_smem;                                            // [616]
-    float* acc = nq_smem + 616 + (threadIdx.x >> 5) * (kMW + kAW);  // this warp's receiver
+    float* acc = nq_smem + 616 + (threadIdx.x >> 5) * kFwdStride;  // this warp's receiver
     float* aw = acc + kMW;
+    float* ws = acc + kFwdRows;
+    float* xs = ws + kWW;
     for (int t = threadIdx.x; t < kCGN; t += blockDim.x) cg[t] = a.cg[t];
     __syncthreads();
     const int lane = threadIdx.x & 31;
@@ -268,8 +298,10 @@ __global__ void __launch_bounds__(32 * kNqWarps) nq_conv_kernel(ConvArgs a, floa
         for (int t = lane; t < kMW; t += 32) acc[t] = 0.f;
         for (int64_t e = a.recv_off[i]; e < a.recv_off[i + 1]; ++e) {
             const int64_t j = a.edge_index[2 * e + 1];
+            __syncwarp();
+            stage_rows(a, e, j, ws, xs, lane);
             load_couplings(a, cg, e, aw, lane);
-            all_paths_fwd(a, aw, e, j, acc, lane, std::make_integer_sequence<int, 15>{});
+            all_paths_fwd(ws, xs, aw, acc, lane, std::make_integer_sequence<int, 15>{});
         }
         __syncwarp();
         for (int t = lane; t < kMW; t += 32) m[i * kMW + t] = acc[t] * a.inv_avg;
@@ -280,8 +312,8 @@ __global__ void __launch_bounds__(32 * kNqWarps) nq_conv_kernel(ConvArgs a, floa
 // dW[e, path, u] = sum_m3 g[u, m3] sum_m1 A[m3][m1] x[u, m1]; the lane's share of dY[e]: the path's
 // T[m3][m1] = sum_u W g[u, m3] x[u, m1] folded over the lanes (fixed order), times CG
 template <int P>
-__device__ __forceinline__ void path_bwd_edge(const ConvArgs& a, const float* cg, const float* aw, const float* dm,
-                                              float* tp, int64_t e, int64_t j, float* dW, float* dy, int lane) {
+__device__ __forceinline__ void path_bwd_edge(const float* ws, const float* xs, const float* cg, const float* aw,
+                                              const float* dm, float* tp, int64_t e, float* dW, float* dy, int lane) {
     constexpr PathInfo pi = kPaths[P];
     constexpr int n1 = dim_of(pi.l1), n2 = dim_of(pi.l2), n3 = dim_of(pi.l3), U = mult_of(pi.l1);
     float t[n3 * n1];
@@ -289,10 +321,10 @@ __device__ __forceinline__ void path_bwd_edge(const ConvArgs& a, const float* cg
     for (int q = 0; q < n3 * n1; ++q) t[q] = 0.f;
 #pragma unroll 1
     for (int u = lane; u < U; u += 32) {
-        const float w = a.W[e * kWW + pi.w_off + u];
+        const float w = ws[pi.w_off + u];
         float xv[n1];
 #pragma unroll
-        for (int m1 = 0; m1 < n1; ++m1) xv[m1] = a.x[j * kXW + x_off(pi.l1) + u * n1 + m1];
+        for (int m1 = 0; m1 < n1; ++m1) xv[m1] = xs[x_off(pi.l1) + u * n1 + m1];
         float gw = 0.f;
 #pragma unroll
         for (int m3 = 0; m3 < n3; ++m3) {
@@ -322,10 +354,10 @@ __device__ __forceinline__ void path_bwd_edge(const ConvArgs& a, const float* cg
 }
 
 template <int... P>
-__device__ __forceinline__ void all_paths_bwd_edge(const ConvArgs& a, const float* cg, const float* aw,
-                                                   const float* dm, float* tp, int64_t e, int64_t j, float* dW,
-                                                   float* dy, int lane, std::integer_sequence<int, P...>) {
-    (path_bwd_edge<P>(a, cg, aw, dm, tp, e, j, dW, dy, lane), ...);
+__device__ __forceinline__ void all_paths_bwd_edge(const float* ws, const float* xs, const float* cg, const float* aw,
+                                                   const float* dm, float* tp, int64_t e, float* dW, float* dy,
+                                                   int lane, std::integer_sequence<int, P...>) {
+    (path_bwd_edge<P>(ws, xs, cg, aw, dm, tp, e, dW, dy, lane), ...);
 }
 
 // per receiver: dW and dY of its edges (dY: lane partials folded by a fixed xor tree)
@@ -334,9 +366,11 @@ __global__ void __launch_bounds__(32 * kNqWarps) nq_conv_bwd_edge_kernel(ConvArg
                                                                          float* __restrict__ dY) {
     extern __shared__ __align__(16) float nq_smem[];
     float* cg = nq_smem;
-    float* dm = nq_smem + 616 + (threadIdx.x >> 5) * (kMW + kAW + 32 * kTP);
+    float* dm = nq_smem + 616 + (threadIdx.x >> 5) * kBwdStride;
     float* aw = dm + kMW;
     float* tp = aw + kAW;
+    float* ws = dm + kBwdRows;
+    float* xs = ws + kWW;
     for (int t = threadIdx.x; t < kCGN; t += blockDim.x) cg[t] = a.cg[t];
     __syncthreads();
     const int lane = threadIdx.x & 31;
@@ -347,11 +381,13 @@ __global__ void __launch_bounds__(32 * kNqWarps) nq_conv_bwd_edge_kernel(ConvArg
         __syncwarp();
         for (int64_t e = a.recv_off[i]; e < a.recv_off[i + 1]; ++e) {
             const int64_t j = a.edge_index[2 * e + 1];
+            __syncwarp();
+            stage_rows(a, e, j, ws, xs, lane);
             load_couplings(a, cg, e, aw, lane);
             float dy[9];
 #pragma unroll
             for (int q = 0; q < 9; ++q) dy[q] = 0.f;
-            all_paths_bwd_edge(a, cg, aw, dm, tp, e, j, dW, dy, lane, std::make_integer_sequence<int, 15>{});
+            all_paths_bwd_edge(ws, xs, cg, aw, dm, tp, e, dW, dy, lane, std::make_integer_sequence<int, 15>{});
 #pragma unroll
             for (int q = 0; q < 9; ++q)
                 for (int d = 16; d > 0; d >>= 1) dy[q] += __shfl_xor_sync(0xffffffffu, dy[q], d);
@@ -485,6 +521,9 @@ static fmd_status conv_args(ConvArgs& a, const float* x, const float* Y, const f
                             const int32_t* send_perm, int64_t n_atoms, float inv_avg) {
     if (n_atoms < 0 || !(inv_avg > 0.f)) return FMD_ERR_INVALID_ARGUMENT;
     if (x == nullptr || cg == nullptr || recv_off == nullptr) return FMD_ERR_INVALID_ARGUMENT;
+    // rows are staged with 16-byte loads
+    if (reinterpret_cast<uintptr_t>(x) % 16 != 0 || reinterpret_cast<uintptr_t>(W) % 16 != 0)
+        return FMD_ERR_INVALID_ARGUMENT;
     a = ConvArgs{x, Y, W, cg, edge_index, recv_off, send_off, send_perm, n_atoms, inv_avg};
     return FMD_OK;
 }
@@ -506,7 +545,7 @@ fmd_status fmd_nequip_conv(const float* x, const float* Y, const float* W, const
     if (n_atoms == 0) return FMD_OK;
     if (messages == nullptr) return FMD_ERR_INVALID_ARGUMENT;
     static bool granted = false;
-    const size_t smem = conv_smem(kMW + kAW);
+    const size_t smem = conv_smem(kFwdStride);
     if ((st = grant_once((const void*)nq_conv_kernel, smem, granted)) != FMD_OK) return st;
     nq_conv_kernel<<<grid_of(n_atoms, kNqWarps), 32 * kNqWarps, smem, as_stream(stream)>>>(a, messages);
     return check_launch();
@@ -524,7 +563,7 @@ fmd_status fmd_nequip_conv_bwd(const float* x, const float* Y, const float* W, c
         send_off == nullptr)
         return FMD_ERR_INVALID_ARGUMENT;
     static bool granted_e = false, granted_x = false;
-    const size_t smem_e = conv_smem(kMW + kAW + 32 * kTP), smem_x = conv_smem(kXW + kAW);
+    const size_t smem_e = conv_smem(kBwdStride), smem_x = conv_smem(kXW + kAW);
     if ((st = grant_once((const void*)nq_conv_bwd_edge_kernel, smem_e, granted_e)) != FMD_OK) return st;
     if ((st = grant_once((const void*)nq_conv_bwd_x_kernel, smem_x, granted_x)) != FMD_OK) return st;
     const cudaStream_t s = as_stream(stream);
