@@ -2,10 +2,12 @@
 // harmonics l <= 2 and Bessel radial functions) with its backward, and the
 // radial-weighted tensor-product convolution with its two backward kernels.
 //
-// Layouts. Node features x [N, 480] = [128 x l0 | 64 x l1 (3) | 32 x l2 (5)]
-// (channel-major, m-minor). Messages m [N, 3136] = [224 x l0 | 384 x l1 |
-// 352 x l2]: the outputs of the 15 coupling paths (l1, l2 -> l3), in path
-// order (l1, then l2, then l3), grouped by l3. Per-edge weights W [E, 960]:
+// Layouts (planar by l, m-major inside a plane, so that every per-l linear
+// reads a plane as one [N (2l + 1), channels] matrix). Node features x: the
+// planes [N, 128] (l0) | [N, 3, 64] (l1) | [N, 5, 32] (l2), 480 N floats.
+// Messages m: [N, 224] | [N, 3, 384] | [N, 5, 352], 3136 N floats; inside a
+// plane the channels are the outputs of the coupling paths (l1, l2 -> l3)
+// with that l3, in path order (l1, then l2). Per-edge weights W [E, 960]:
 // one weight per (path, channel of l1). Edge harmonics Y [E, 9] =
 // [1 | sqrt3 u | sqrt15 xy, sqrt15 yz, sqrt5/2 (3z^2 - 1), sqrt15 xz,
 // sqrt15/2 (x^2 - y^2)] of the unit edge vector u; CG [615] the 15 dense
@@ -38,6 +40,8 @@ constexpr int kNqWarps = 4;
 __host__ __device__ constexpr int dim_of(int l) { return 2 * l + 1; }
 __host__ __device__ constexpr int mult_of(int l) { return l == 0 ? 128 : (l == 1 ? 64 : 32); }
 __host__ __device__ constexpr int x_off(int l) { return l == 0 ? 0 : (l == 1 ? 128 : 320); }
+__host__ __device__ constexpr int m_off_of(int l) { return l == 0 ? 0 : (l == 1 ? 224 : 1376); }
+__host__ __device__ constexpr int m_mult(int l) { return l == 0 ? 224 : (l == 1 ? 384 : 352); }
 __host__ __device__ constexpr int y_off(int l) { return l == 0 ? 0 : (l == 1 ? 1 : 4); }
 
 // the 15 paths with their offsets (weights, message columns, coupling tensor)
@@ -49,6 +53,36 @@ constexpr PathInfo kPaths[15] = {
     {1, 1, 0, 448, 128, 44},   {1, 1, 1, 512, 800, 53},   {1, 1, 2, 576, 2016, 80},  {1, 2, 1, 640, 992, 125},
     {1, 2, 2, 704, 2336, 170}, {2, 0, 2, 768, 2656, 245}, {2, 1, 1, 800, 1184, 270}, {2, 1, 2, 832, 2816, 315},
     {2, 2, 0, 864, 192, 390},  {2, 2, 1, 896, 1280, 415}, {2, 2, 2, 928, 2976, 490}};
+
+// a path's channel offset inside its l3 plane, and the staged-row index of its message (u, m3)
+__host__ __device__ constexpr int c_off(const PathInfo& pi) {
+    return (pi.m_off - m_off_of(pi.l3)) / dim_of(pi.l3);
+}
+__host__ __device__ constexpr int m_idx(const PathInfo& pi, int u, int m3) {
+    return m_off_of(pi.l3) + m3 * m_mult(pi.l3) + c_off(pi) + u;
+}
+__host__ __device__ constexpr int x_idx(int l, int u, int m) { return x_off(l) + m * mult_of(l) + u; }
+// every path's channels tile its l3 plane without gaps or overlaps, in path order
+__host__ __device__ constexpr bool planes_tile() {
+    int next[3] = {0, 0, 0};
+    for (int p = 0; p < 15; ++p) {
+        const PathInfo& pi = kPaths[p];
+        if ((pi.m_off - m_off_of(pi.l3)) % dim_of(pi.l3) != 0 || c_off(pi) != next[pi.l3]) return false;
+        next[pi.l3] += mult_of(pi.l1);
+    }
+    return next[0] == m_mult(0) && next[1] == m_mult(1) && next[2] == m_mult(2);
+}
+static_assert(planes_tile(), "message planes");
+
+// the planar address of column t (0..479 / 0..3135) of atom row r
+__device__ __forceinline__ int64_t x_planar(int64_t n, int64_t r, int t) {
+    const int l = t < 128 ? 0 : (t < 320 ? 1 : 2);
+    return n * x_off(l) + r * (dim_of(l) * mult_of(l)) + (t - x_off(l));
+}
+__device__ __forceinline__ int64_t m_planar(int64_t n, int64_t r, int t) {
+    const int l = t < 224 ? 0 : (t < 1376 ? 1 : 2);
+    return n * m_off_of(l) + r * (dim_of(l) * m_mult(l)) + (t - m_off_of(l));
+}
 
 struct Cell3 {
     float c[9];
@@ -173,7 +207,7 @@ __global__ void nq_basis_bwd_kernel(BasisArgs a, const float* __restrict__ dY, c
 // ------------------------------------------------------------------ convolution
 
 struct ConvArgs {
-    const float* x;          // [N, 480]
+    const float* x;          // 480 N floats, planar
     const float* Y;          // [E, 9]
     const float* W;          // [E, 960]
     const float* cg;         // [615]
@@ -238,14 +272,14 @@ __device__ __forceinline__ void load_couplings(const ConvArgs& a, const float* c
 // memory: 16-byte loads issued together (one memory round trip per edge instead of one per path)
 __device__ __forceinline__ void stage_rows(const ConvArgs& a, int64_t e, int64_t j, float* ws, float* xs, int lane) {
     const float4* wsrc = reinterpret_cast<const float4*>(a.W + e * kWW);
-    const float4* xsrc = reinterpret_cast<const float4*>(a.x + j * kXW);
     float4 wv[(kWW / 4 + 31) / 32], xv[(kXW / 4 + 31) / 32];
 #pragma unroll
     for (int r = 0; r < (kWW / 4 + 31) / 32; ++r)
         if (lane + 32 * r < kWW / 4) wv[r] = wsrc[lane + 32 * r];
 #pragma unroll
-    for (int r = 0; r < (kXW / 4 + 31) / 32; ++r)
-        if (lane + 32 * r < kXW / 4) xv[r] = xsrc[lane + 32 * r];
+    for (int r = 0; r < (kXW / 4 + 31) / 32; ++r)  // the plane pieces are whole float4s (128, 192, 160)
+        if (lane + 32 * r < kXW / 4)
+            xv[r] = *reinterpret_cast<const float4*>(a.x + x_planar(a.n_atoms, j, 4 * (lane + 32 * r)));
 #pragma unroll
     for (int r = 0; r < (kWW / 4 + 31) / 32; ++r)
         if (lane + 32 * r < kWW / 4) reinterpret_cast<float4*>(ws)[lane + 32 * r] = wv[r];
@@ -255,7 +289,7 @@ __device__ __forceinline__ void stage_rows(const ConvArgs& a, int64_t e, int64_t
 }
 
 // one path's contribution of edge e (lane channels u) into the receiver's accumulators:
-// acc[u, m3] += W[e, path, u] sum_m1 A[m3][m1] x[j, l1, u, m1]
+// acc[m3, u] += W[e, path, u] sum_m1 A[m3][m1] x[j, l1, m1, u]
 template <int P>
 __device__ __forceinline__ void path_fwd(const float* ws, const float* xs, const float* aw, float* acc, int lane) {
     constexpr PathInfo pi = kPaths[P];
@@ -265,13 +299,13 @@ __device__ __forceinline__ void path_fwd(const float* ws, const float* xs, const
         const float w = ws[pi.w_off + u];
         float xv[n1];
 #pragma unroll
-        for (int m1 = 0; m1 < n1; ++m1) xv[m1] = xs[x_off(pi.l1) + u * n1 + m1];
+        for (int m1 = 0; m1 < n1; ++m1) xv[m1] = xs[x_idx(pi.l1, u, m1)];
 #pragma unroll
         for (int m3 = 0; m3 < n3; ++m3) {
             float s = 0.f;
 #pragma unroll
             for (int m1 = 0; m1 < n1; ++m1) s = fmaf(aw[a_off(P) + m3 * n1 + m1], xv[m1], s);
-            acc[pi.m_off + u * n3 + m3] = fmaf(w, s, acc[pi.m_off + u * n3 + m3]);
+            acc[m_idx(pi, u, m3)] = fmaf(w, s, acc[m_idx(pi, u, m3)]);
         }
     }
 }
@@ -304,7 +338,7 @@ __global__ void __launch_bounds__(32 * kNqWarps) nq_conv_kernel(ConvArgs a, floa
             all_paths_fwd(ws, xs, aw, acc, lane, std::make_integer_sequence<int, 15>{});
         }
         __syncwarp();
-        for (int t = lane; t < kMW; t += 32) m[i * kMW + t] = acc[t] * a.inv_avg;
+        for (int t = lane; t < kMW; t += 32) m[m_planar(a.n_atoms, i, t)] = acc[t] * a.inv_avg;
         __syncwarp();
     }
 }
@@ -324,11 +358,11 @@ __device__ __forceinline__ void path_bwd_edge(const float* ws, const float* xs, 
         const float w = ws[pi.w_off + u];
         float xv[n1];
 #pragma unroll
-        for (int m1 = 0; m1 < n1; ++m1) xv[m1] = xs[x_off(pi.l1) + u * n1 + m1];
+        for (int m1 = 0; m1 < n1; ++m1) xv[m1] = xs[x_idx(pi.l1, u, m1)];
         float gw = 0.f;
 #pragma unroll
         for (int m3 = 0; m3 < n3; ++m3) {
-            const float g = dm[pi.m_off + u * n3 + m3];
+            const float g = dm[m_idx(pi, u, m3)];
             float s = 0.f;
 #pragma unroll
             for (int m1 = 0; m1 < n1; ++m1) {
@@ -377,7 +411,7 @@ __global__ void __launch_bounds__(32 * kNqWarps) nq_conv_bwd_edge_kernel(ConvArg
     for (int64_t i = int64_t(blockIdx.x) * kNqWarps + (threadIdx.x >> 5); i < a.n_atoms;
          i += int64_t(gridDim.x) * kNqWarps) {
         __syncwarp();
-        for (int t = lane; t < kMW; t += 32) dm[t] = dmsg[i * kMW + t] * a.inv_avg;
+        for (int t = lane; t < kMW; t += 32) dm[t] = dmsg[m_planar(a.n_atoms, i, t)] * a.inv_avg;
         __syncwarp();
         for (int64_t e = a.recv_off[i]; e < a.recv_off[i + 1]; ++e) {
             const int64_t j = a.edge_index[2 * e + 1];
@@ -398,9 +432,9 @@ __global__ void __launch_bounds__(32 * kNqWarps) nq_conv_bwd_edge_kernel(ConvArg
     }
 }
 
-// dx[j, l1, u, m1] += W[e, path, u] sum_m3 A[m3][m1] dm[i, path, u, m3]
+// dx[j, l1, m1, u] += W[e, path, u] sum_m3 A[m3][m1] dm[i, l3, m3, path channel u]
 template <int P>
-__device__ __forceinline__ void path_bwd_x(const ConvArgs& a, const float* aw, const float* dmi, int64_t e,
+__device__ __forceinline__ void path_bwd_x(const ConvArgs& a, const float* aw, const float* const* dmi, int64_t e,
                                            float* dx, int lane) {
     constexpr PathInfo pi = kPaths[P];
     constexpr int n1 = dim_of(pi.l1), n3 = dim_of(pi.l3), U = mult_of(pi.l1);
@@ -409,19 +443,19 @@ __device__ __forceinline__ void path_bwd_x(const ConvArgs& a, const float* aw, c
         const float w = a.W[e * kWW + pi.w_off + u];
         float g[n3];
 #pragma unroll
-        for (int m3 = 0; m3 < n3; ++m3) g[m3] = dmi[pi.m_off + u * n3 + m3];
+        for (int m3 = 0; m3 < n3; ++m3) g[m3] = dmi[pi.l3][m3 * m_mult(pi.l3) + c_off(pi) + u];
 #pragma unroll
         for (int m1 = 0; m1 < n1; ++m1) {
             float s = 0.f;
 #pragma unroll
             for (int m3 = 0; m3 < n3; ++m3) s = fmaf(aw[a_off(P) + m3 * n1 + m1], g[m3], s);
-            dx[x_off(pi.l1) + u * n1 + m1] = fmaf(w, s, dx[x_off(pi.l1) + u * n1 + m1]);
+            dx[x_idx(pi.l1, u, m1)] = fmaf(w, s, dx[x_idx(pi.l1, u, m1)]);
         }
     }
 }
 
 template <int... P>
-__device__ __forceinline__ void all_paths_bwd_x(const ConvArgs& a, const float* aw, const float* dmi, int64_t e,
+__device__ __forceinline__ void all_paths_bwd_x(const ConvArgs& a, const float* aw, const float* const* dmi, int64_t e,
                                                 float* dx, int lane, std::integer_sequence<int, P...>) {
     (path_bwd_x<P>(a, aw, dmi, e, dx, lane), ...);
 }
@@ -444,10 +478,79 @@ __global__ void __launch_bounds__(32 * kNqWarps) nq_conv_bwd_x_kernel(ConvArgs a
             const int64_t e = a.send_perm[s];
             const int64_t i = a.edge_index[2 * e];
             load_couplings(a, cg, e, aw, lane);
-            all_paths_bwd_x(a, aw, dmsg + i * kMW, e, dx, lane, std::make_integer_sequence<int, 15>{});
+            // the receiver's message-gradient rows of the three planes
+            const float* dmi[3] = {dmsg + m_planar(a.n_atoms, i, 0), dmsg + m_planar(a.n_atoms, i, m_off_of(1)),
+                                   dmsg + m_planar(a.n_atoms, i, m_off_of(2))};
+            all_paths_bwd_x(a, aw, dmi, e, dx, lane, std::make_integer_sequence<int, 15>{});
         }
         __syncwarp();
-        for (int t = lane; t < kXW; t += 32) dx_out[j * kXW + t] = dx[t] * a.inv_avg;
+        for (int t = lane; t < kXW; t += 32) dx_out[x_planar(a.n_atoms, j, t)] = dx[t] * a.inv_avg;
+    }
+}
+
+// ------------------------------------------------------------------ gate
+//
+// The gated nonlinearity closing an interaction block, plus its self-connection:
+//   x0[n, c] = silu(o0[n, c]) + sc0[n, c]                          (c < 128)
+//   x1[n, m, c] = o1[n, m, c] sigmoid(o0[n, 128 + c]) + sc1[n, m, c]  (c < 64)
+//   x2[n, m, c] = o2[n, m, c] sigmoid(o0[n, 192 + c]) + sc2[n, m, c]  (c < 32)
+// (o0 [N, 224], o1 [N, 3, 64], o2 [N, 5, 32]). One thread per output element over the three planes;
+// the backward, one thread per element of d o0 / d o1 / d o2, sums a gate's 3 or 5 products in order.
+
+__device__ __forceinline__ float sigmoid_f(float v) { return 1.f / (1.f + expf(-v)); }
+
+__global__ void __launch_bounds__(256) nq_gate_kernel(const float* __restrict__ o0, const float* __restrict__ o1,
+                                                       const float* __restrict__ o2, const float* __restrict__ sc0,
+                                                       const float* __restrict__ sc1, const float* __restrict__ sc2,
+                                                       int64_t n, float* __restrict__ x0, float* __restrict__ x1,
+                                                       float* __restrict__ x2) {
+    const int64_t total = n * kXW;
+    for (int64_t t = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; t < total; t += int64_t(gridDim.x) * blockDim.x) {
+        if (t < n * 128) {
+            const float v = o0[(t >> 7) * 224 + (t & 127)];
+            x0[t] = v * sigmoid_f(v) + sc0[t];
+        } else if (t < n * 320) {
+            const int64_t q = t - n * 128, a = q / 192;
+            x1[q] = o1[q] * sigmoid_f(o0[a * 224 + 128 + (q & 63)]) + sc1[q];
+        } else {
+            const int64_t q = t - n * 320, a = q / 160;
+            x2[q] = o2[q] * sigmoid_f(o0[a * 224 + 192 + (q & 31)]) + sc2[q];
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256) nq_gate_bwd_kernel(const float* __restrict__ o0, const float* __restrict__ o1,
+                                                           const float* __restrict__ o2, const float* __restrict__ dx0,
+                                                           const float* __restrict__ dx1,
+                                                           const float* __restrict__ dx2, int64_t n,
+                                                           float* __restrict__ do0, float* __restrict__ do1,
+                                                           float* __restrict__ do2) {
+    const int64_t total = n * (224 + 192 + 160);
+    for (int64_t t = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; t < total; t += int64_t(gridDim.x) * blockDim.x) {
+        if (t < n * 224) {
+            const int64_t a = t / 224;
+            const int k = int(t - a * 224);
+            const float v = o0[t], sg = sigmoid_f(v);
+            if (k < 128) {
+                do0[t] = dx0[a * 128 + k] * (sg * (1.f + v * (1.f - sg)));
+            } else if (k < 192) {
+                float acc = 0.f;
+#pragma unroll
+                for (int m = 0; m < 3; ++m) acc += dx1[a * 192 + m * 64 + (k - 128)] * o1[a * 192 + m * 64 + (k - 128)];
+                do0[t] = acc * (sg * (1.f - sg));
+            } else {
+                float acc = 0.f;
+#pragma unroll
+                for (int m = 0; m < 5; ++m) acc += dx2[a * 160 + m * 32 + (k - 192)] * o2[a * 160 + m * 32 + (k - 192)];
+                do0[t] = acc * (sg * (1.f - sg));
+            }
+        } else if (t < n * 416) {
+            const int64_t q = t - n * 224, a = q / 192;
+            do1[q] = dx1[q] * sigmoid_f(o0[a * 224 + 128 + (q & 63)]);
+        } else {
+            const int64_t q = t - n * 416, a = q / 160;
+            do2[q] = dx2[q] * sigmoid_f(o0[a * 224 + 192 + (q & 31)]);
+        }
     }
 }
 
@@ -571,6 +674,30 @@ fmd_status fmd_nequip_conv_bwd(const float* x, const float* Y, const float* W, c
                                                                                        grad_Y);
     if ((st = check_launch()) != FMD_OK) return st;
     nq_conv_bwd_x_kernel<<<grid_of(n_atoms, kNqWarps), 32 * kNqWarps, smem_x, s>>>(a, grad_messages, grad_x);
+    return check_launch();
+}
+
+fmd_status fmd_nequip_gate(const float* o0, const float* o1, const float* o2, const float* sc0, const float* sc1,
+                           const float* sc2, int64_t n_atoms, float* x0, float* x1, float* x2, void* stream) {
+    if (n_atoms < 0) return FMD_ERR_INVALID_ARGUMENT;
+    if (n_atoms == 0) return FMD_OK;
+    if (o0 == nullptr || o1 == nullptr || o2 == nullptr || sc0 == nullptr || sc1 == nullptr || sc2 == nullptr ||
+        x0 == nullptr || x1 == nullptr || x2 == nullptr)
+        return FMD_ERR_INVALID_ARGUMENT;
+    nq_gate_kernel<<<grid_of(n_atoms * kXW, 256), 256, 0, as_stream(stream)>>>(o0, o1, o2, sc0, sc1, sc2, n_atoms, x0,
+                                                                                 x1, x2);
+    return check_launch();
+}
+
+fmd_status fmd_nequip_gate_bwd(const float* o0, const float* o1, const float* o2, const float* dx0, const float* dx1,
+                               const float* dx2, int64_t n_atoms, float* do0, float* do1, float* do2, void* stream) {
+    if (n_atoms < 0) return FMD_ERR_INVALID_ARGUMENT;
+    if (n_atoms == 0) return FMD_OK;
+    if (o0 == nullptr || o1 == nullptr || o2 == nullptr || dx0 == nullptr || dx1 == nullptr || dx2 == nullptr ||
+        do0 == nullptr || do1 == nullptr || do2 == nullptr)
+        return FMD_ERR_INVALID_ARGUMENT;
+    nq_gate_bwd_kernel<<<grid_of(n_atoms * 576, 256), 256, 0, as_stream(stream)>>>(o0, o1, o2, dx0, dx1, dx2, n_atoms,
+                                                                                     do0, do1, do2);
     return check_launch();
 }
 

@@ -122,35 +122,72 @@ class _EdgeBasis(Function):
         return grad, None, None
 
 
+def _planes(flat: Tensor, n: int, mults) -> tuple[Tensor, ...]:
+    """The l planes of a planar buffer as [n (2l + 1), mult] matrices (views)."""
+    out, off = [], 0
+    for m, d in zip(mults, DIM):
+        out.append(flat[off:off + n * m * d].view(n * d, m))
+        off += n * m * d
+    return tuple(out)
+
+
 class _Conv(Function):
+    """Messages (three planes [N, 224], [3N, 384], [5N, 352]) of the node features x (the planar buffer
+    of 480 N floats); the backward returns the gradients of x, Y and W."""
+
     @staticmethod
     def forward(ctx, x, Y, W, model, batch):
         N = batch.n_real
-        m = torch.empty(N, int(sum(M_MULT[l] * DIM[l] for l in range(3))), device=x.device)
+        m = torch.empty(N * sum(M_MULT[l] * DIM[l] for l in range(3)), device=x.device)
         call("fmd_nequip_conv", ptr(x), ptr(Y), ptr(W), ptr(model.cg), ptr(batch.edge_index), ptr(batch.recv_off), N,
              1.0 / model.config.avg_num_neighbors, ptr(m), stream(x.device))
         ctx.save_for_backward(x, Y, W)
         ctx.model, ctx.batch = model, batch
-        return m
+        return _planes(m, N, M_MULT)
 
     @staticmethod
-    def backward(ctx, dm):
+    def backward(ctx, *dm):
         x, Y, W = ctx.saved_tensors
         model, batch = ctx.model, ctx.batch
+        N = batch.n_real
+        dm = torch.cat([(g if g is not None else torch.zeros(N * M_MULT[l] * DIM[l], device=x.device)).reshape(-1)
+                        for l, g in enumerate(dm)])
         gx, gW, gY = torch.empty_like(x), torch.empty_like(W), torch.empty_like(Y)
         call("fmd_nequip_conv_bwd", ptr(x), ptr(Y), ptr(W), ptr(model.cg), ptr(batch.edge_index), ptr(batch.recv_off),
-             ptr(batch.send_off), ptr(batch.send_perm), batch.n_real, 1.0 / model.config.avg_num_neighbors,
-             ptr(dm.contiguous()), ptr(gx), ptr(gW), ptr(gY), stream(x.device))
+             ptr(batch.send_off), ptr(batch.send_perm), N, 1.0 / model.config.avg_num_neighbors, ptr(dm), ptr(gx),
+             ptr(gW), ptr(gY), stream(x.device))
         return gx, gY, gW, None, None
 
 
-def _split(x: Tensor, widths) -> list[Tensor]:
-    """[N, sum(m d)] -> per l [N, m, d] views."""
-    out, off = [], 0
-    for m, d in widths:
-        out.append(x[:, off:off + m * d].reshape(-1, m, d))
-        off += m * d
-    return out
+class _Gate(Function):
+    """(x0 [N, 128], x1 [3N, 64], x2 [5N, 32]) = the gated nonlinearity of the second linear's outputs
+    (o0 [N, 224], o1 [3N, 64], o2 [5N, 32]) plus the self-connection planes sc (``fmd_nequip_gate``)."""
+
+    @staticmethod
+    def forward(ctx, o0, o1, o2, sc0, sc1, sc2):
+        n = o0.shape[0]
+        o0, o1, o2 = o0.contiguous(), o1.contiguous(), o2.contiguous()
+        x = [torch.empty(n * DIM[l], MULT[l], device=o0.device) for l in range(3)]
+        call("fmd_nequip_gate", ptr(o0), ptr(o1), ptr(o2), ptr(sc0.contiguous()), ptr(sc1.contiguous()),
+             ptr(sc2.contiguous()), n, ptr(x[0]), ptr(x[1]), ptr(x[2]), stream(o0.device))
+        ctx.save_for_backward(o0, o1, o2)
+        return tuple(x)
+
+    @staticmethod
+    def backward(ctx, dx0, dx1, dx2):
+        o0, o1, o2 = ctx.saved_tensors
+        n = o0.shape[0]
+        dx = [g.contiguous() if g is not None else torch.zeros(n * DIM[l], MULT[l], device=o0.device)
+              for l, g in enumerate((dx0, dx1, dx2))]
+        do = [torch.empty_like(o0), torch.empty_like(o1), torch.empty_like(o2)]
+        call("fmd_nequip_gate_bwd", ptr(o0), ptr(o1), ptr(o2), ptr(dx[0]), ptr(dx[1]), ptr(dx[2]), n, ptr(do[0]),
+             ptr(do[1]), ptr(do[2]), stream(o0.device))
+        return do[0], do[1], do[2], dx[0], dx[1], dx[2]
+
+
+def gate(o0: Tensor, o1: Tensor, o2: Tensor, sc0: Tensor, sc1: Tensor, sc2: Tensor) -> tuple[Tensor, Tensor, Tensor]:
+    """The block's gated nonlinearity plus self-connection on the device (differentiable)."""
+    return _Gate.apply(o0, o1, o2, sc0, sc1, sc2)
 
 
 class NequIPModel:
@@ -192,18 +229,15 @@ class NequIPModel:
     def _linear(self, x, weight):
         return wide_gemm.linear(x, weight, precision=self.precision)
 
-    def _per_l(self, xl: Tensor, weight: Tensor) -> Tensor:
-        """[N, u, d] @ W [u, v] -> [N, v, d] (W given as [v, u])."""
-        n, u, d = xl.shape
-        rows = xl.transpose(1, 2).reshape(n * d, u)
-        return self._linear(rows, weight).reshape(n, d, -1).transpose(1, 2)
-
-    def _self_connection(self, xl: Tensor, L: int, l: int, elem: Tensor, groups) -> Tensor:
-        n, u, d = xl.shape
-        out = torch.zeros(n, u, d, device=xl.device)
+    def _self_connection(self, xl: Tensor, n: int, L: int, l: int, groups) -> Tensor:
+        """The element-dependent linear of plane ``xl`` [n d, u] (atom rows gathered per element)."""
+        d, u = DIM[l], MULT[l]
+        rows = xl.view(n, d * u)
+        out = torch.zeros(n, d * u, device=xl.device)
         for z, idx in groups:
-            out = out.index_copy(0, idx, self._per_l(xl.index_select(0, idx), self.sc[f"L{L}.sc{l}"][z]))
-        return out
+            y = self._linear(rows.index_select(0, idx).view(-1, u), self.sc[f"L{L}.sc{l}"][z])
+            out = out.index_copy(0, idx, y.view(-1, d * u))
+        return out.view(n * d, u)
 
     def energy_forces(self, batch, n_systems: int = 1) -> tuple[Tensor, Tensor]:
         """(energy [1] fp64, forces [N, 3]) of one system; capturable in a CUDA graph once ``prepare``
@@ -218,23 +252,20 @@ class NequIPModel:
         with torch.enable_grad():
             pos = batch.positions.detach().requires_grad_(True)
             Y, B = _EdgeBasis.apply(pos, self, batch)
-            x = torch.cat([self.w["embed"][elem], torch.zeros(N, X_WIDTH - MULT[0], device=self.device)], 1)
+            # node features as planes [N (2l + 1), mult]; l = 1, 2 start at exact zeros
+            x = [self.w["embed"][elem], None, None]
             for L in range(c.num_layers):
-                xs = _split(x, zip(MULT, DIM))
-                sc = [self._self_connection(xs[l], L, l, elem, groups) for l in range(3)]
-                h = torch.cat([self._per_l(xs[l], self.lin[f"L{L}.lin1_{l}"]).reshape(N, -1) for l in range(3)], 1)
+                zero = lambda l: torch.zeros(N * DIM[l], MULT[l], device=self.device)  # noqa: E731
+                # a linear map of an exact zero plane is an exact zero plane: not launched
+                sc = [self._self_connection(x[l], N, L, l, groups) if x[l] is not None else zero(l) for l in range(3)]
+                h = [self._linear(x[l], self.lin[f"L{L}.lin1_{l}"]) if x[l] is not None else zero(l) for l in range(3)]
                 r = torch.nn.functional.silu(self._linear(B, self.w[f"L{L}.rad1"]))
                 r = torch.nn.functional.silu(self._linear(r, self.w[f"L{L}.rad2"]))
                 W = self._linear(r, self.w[f"L{L}.rad3"])
-                m = _Conv.apply(h.contiguous(), Y, W.contiguous(), self, batch)
-                ms = _split(m, zip(M_MULT, DIM))
-                o = [self._per_l(ms[l], self.lin[f"L{L}.lin2_{l}"]) for l in range(3)]
-                scal = torch.nn.functional.silu(o[0][:, :MULT[0], 0])
-                gates = torch.sigmoid(o[0][:, MULT[0]:, 0])
-                g1 = o[1] * gates[:, :MULT[1], None]
-                g2 = o[2] * gates[:, MULT[1]:, None]
-                x = torch.cat([scal + sc[0][:, :, 0], (g1 + sc[1]).reshape(N, -1), (g2 + sc[2]).reshape(N, -1)], 1)
-            hid = self._linear(x[:, :MULT[0]].contiguous(), self.w["readout1"])
+                m = _Conv.apply(torch.cat([p.reshape(-1) for p in h]), Y, W.contiguous(), self, batch)
+                o = [self._linear(m[l], self.lin[f"L{L}.lin2_{l}"]) for l in range(3)]
+                x = list(_Gate.apply(*o, *sc))
+            hid = self._linear(x[0].contiguous(), self.w["readout1"])
             e_atom = self._linear(hid, self.w["readout2"])[:, 0] * c.scale + c.shift
             energy = e_atom.double().sum()
             (grad,) = torch.autograd.grad(energy, pos)
@@ -243,4 +274,4 @@ class NequIPModel:
     energy_forces_fused = energy_forces
 
 
-__all__ = ["NequIPConfig", "NequIPModel", "coupling_table", "init_weights", "PATHS"]
+__all__ = ["NequIPConfig", "NequIPModel", "coupling_table", "gate", "init_weights", "PATHS"]

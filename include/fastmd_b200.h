@@ -766,23 +766,41 @@ FMD_API fmd_status fmd_nequip_edge_basis_bwd(const float* geo, const float* dY, 
                                              const float* override_vec, const int64_t* n_real, int64_t n_edges,
                                              float r_max, int32_t n_basis, int32_t poly_p, float* grad_vec,
                                              void* stream);
-/* The radial-weighted tensor-product convolution of node features x
- * [N, 480] (128 x l0 | 64 x l1 | 32 x l2, channel-major) over the 15
- * coupling paths (l1, l2 -> l3 <= 2, path order l1, l2, l3): messages
- * [N, 3136] = inv_avg * sum over the receiver's edges (recv_off, rows sorted
- * by centre) of W[e, path, u] CG[path] . (x[j, l1, u] (x) Y[e, l2]); W
- * [E, 960], cg the 615 dense coupling constants. Deterministic (one warp per
- * receiver, its edges in order). */
+/* The radial-weighted tensor-product convolution of node features x (480 N
+ * floats, planar: [N, 128] l0 | [N, 3, 64] l1 | [N, 5, 32] l2; 16-byte
+ * aligned) over the 15 coupling paths (l1, l2 -> l3 <= 2, path order l1, l2,
+ * l3): messages (3136 N floats, planar: [N, 224] | [N, 3, 384] | [N, 5, 352],
+ * a plane's channels the paths with that l3 in path order) = inv_avg * sum
+ * over the receiver's edges (recv_off, rows sorted by centre) of W[e, path, u]
+ * CG[path] . (x[j, l1, :, u] (x) Y[e, l2]); W [E, 960] (16-byte aligned), cg
+ * the 615 dense coupling constants. Deterministic (one warp per receiver, its
+ * edges in order). */
 FMD_API fmd_status fmd_nequip_conv(const float* x, const float* Y, const float* W, const float* cg,
                                    const int32_t* edge_index, const int64_t* recv_off, int64_t n_atoms, float inv_avg,
                                    float* messages, void* stream);
-/* Its backward from grad_messages [N, 3136]: grad_W [E, 960] and grad_Y
- * [E, 9] per receiver, grad_x [N, 480] per sender (send_off / send_perm). */
+/* Its backward from grad_messages (the messages' planar layout): grad_W
+ * [E, 960] and grad_Y [E, 9] per receiver, grad_x (x's planar layout) per
+ * sender (send_off / send_perm). */
 FMD_API fmd_status fmd_nequip_conv_bwd(const float* x, const float* Y, const float* W, const float* cg,
                                        const int32_t* edge_index, const int64_t* recv_off, const int64_t* send_off,
                                        const int32_t* send_perm, int64_t n_atoms, float inv_avg,
                                        const float* grad_messages, float* grad_x, float* grad_W, float* grad_Y,
                                        void* stream);
+
+/* The gated nonlinearity closing an interaction block, plus its
+ * self-connection sc (SevenNet's gate after the second linear): x0 =
+ * silu(o0[:, :128]) + sc0; x1[n, m, c] = o1[n, m, c] sigmoid(o0[n, 128 + c]) +
+ * sc1[n, m, c]; x2[n, m, c] = o2[n, m, c] sigmoid(o0[n, 192 + c]) +
+ * sc2[n, m, c]. o0 [N, 224], o1 / sc1 / x1 [N, 3, 64], o2 / sc2 / x2
+ * [N, 5, 32], sc0 / x0 [N, 128], all contiguous. */
+FMD_API fmd_status fmd_nequip_gate(const float* o0, const float* o1, const float* o2, const float* sc0,
+                                   const float* sc1, const float* sc2, int64_t n_atoms, float* x0, float* x1,
+                                   float* x2, void* stream);
+/* Its backward: grad_o0 / grad_o1 / grad_o2 from grad_x0 / grad_x1 / grad_x2
+ * (the self-connection's gradient is grad_x itself). */
+FMD_API fmd_status fmd_nequip_gate_bwd(const float* o0, const float* o1, const float* o2, const float* grad_x0,
+                                       const float* grad_x1, const float* grad_x2, int64_t n_atoms, float* grad_o0,
+                                       float* grad_o1, float* grad_o2, void* stream);
 
 /* -------------------------------------- Nose-Hoover chain integrator (F1/F3) */
 
