@@ -554,6 +554,43 @@ __global__ void __launch_bounds__(256) nq_gate_bwd_kernel(const float* __restric
     }
 }
 
+// ------------------------------------------------------------------ self-connection
+//
+// The element-dependent linear of every plane: out[n, m, c] = sum_u x[n, m, u] w_l[z(n), u, c]
+// (forward) or sum_u x[n, m, u] w_l[z(n), c, u] (transposed: the input gradient), w_l [elements, U, U].
+// One thread per output element over the three planes (480 per atom), its U products summed in u order;
+// the atom's row stays in L1, the weight column is read across the warp's consecutive c.
+
+template <bool T>
+__global__ void __launch_bounds__(256) nq_self_conn_kernel(const float* __restrict__ x0, const float* __restrict__ x1,
+                                                            const float* __restrict__ x2,
+                                                            const int64_t* __restrict__ elem,
+                                                            const float* __restrict__ w0, const float* __restrict__ w1,
+                                                            const float* __restrict__ w2, int64_t n,
+                                                            float* __restrict__ o0, float* __restrict__ o1,
+                                                            float* __restrict__ o2) {
+    const int64_t total = n * kXW;
+    for (int64_t t = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; t < total; t += int64_t(gridDim.x) * blockDim.x) {
+        const float *x, *w;
+        float* o;
+        int64_t q, a;
+        int U;
+        if (t < n * 128) {
+            q = t, a = t >> 7, U = 128, x = x0, w = w0, o = o0;
+        } else if (t < n * 320) {
+            q = t - n * 128, a = q / 192, U = 64, x = x1, w = w1, o = o1;
+        } else {
+            q = t - n * 320, a = q / 160, U = 32, x = x2, w = w2, o = o2;
+        }
+        const int c = int(q & (U - 1));
+        const float* xr = x + (q - c);  // the row (n, m) of the plane
+        const float* wz = w + elem[a] * int64_t(U) * U;
+        float acc = 0.f;
+        for (int u = 0; u < U; ++u) acc = fmaf(xr[u], T ? wz[c * U + u] : wz[u * U + c], acc);
+        o[q] = acc;
+    }
+}
+
 bool make_cell3(const float* host, Cell3& c) {
     if (host == nullptr) return false;
     for (int k = 0; k < 9; ++k) c.c[k] = host[k];
@@ -698,6 +735,24 @@ fmd_status fmd_nequip_gate_bwd(const float* o0, const float* o1, const float* o2
         return FMD_ERR_INVALID_ARGUMENT;
     nq_gate_bwd_kernel<<<grid_of(n_atoms * 576, 256), 256, 0, as_stream(stream)>>>(o0, o1, o2, dx0, dx1, dx2, n_atoms,
                                                                                      do0, do1, do2);
+    return check_launch();
+}
+
+fmd_status fmd_nequip_self_connection(const float* x0, const float* x1, const float* x2, const int64_t* elem,
+                                      const float* w0, const float* w1, const float* w2, int64_t n_atoms,
+                                      int32_t transposed, float* out0, float* out1, float* out2, void* stream) {
+    if (n_atoms < 0 || (transposed != 0 && transposed != 1)) return FMD_ERR_INVALID_ARGUMENT;
+    if (n_atoms == 0) return FMD_OK;
+    if (x0 == nullptr || x1 == nullptr || x2 == nullptr || elem == nullptr || w0 == nullptr || w1 == nullptr ||
+        w2 == nullptr || out0 == nullptr || out1 == nullptr || out2 == nullptr)
+        return FMD_ERR_INVALID_ARGUMENT;
+    const int g = grid_of(n_atoms * kXW, 256);
+    if (transposed)
+        nq_self_conn_kernel<true><<<g, 256, 0, as_stream(stream)>>>(x0, x1, x2, elem, w0, w1, w2, n_atoms, out0, out1,
+                                                                    out2);
+    else
+        nq_self_conn_kernel<false><<<g, 256, 0, as_stream(stream)>>>(x0, x1, x2, elem, w0, w1, w2, n_atoms, out0,
+                                                                     out1, out2);
     return check_launch();
 }
 

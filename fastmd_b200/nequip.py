@@ -159,6 +159,31 @@ class _Conv(Function):
         return gx, gY, gW, None, None
 
 
+class _SelfConnection(Function):
+    """The element-dependent linear of the three feature planes (``fmd_nequip_self_connection``); its
+    input gradient is the same kernel on the transposed weights ``t0, t1, t2`` (frozen; kept as copies
+    so that both directions read a weight row across the warp's consecutive output channels)."""
+
+    @staticmethod
+    def forward(ctx, x0, x1, x2, elem, w0, w1, w2, t0, t1, t2):
+        n = x0.shape[0]
+        xs = [x0.contiguous(), x1.contiguous(), x2.contiguous()]
+        out = [torch.empty_like(t) for t in xs]
+        call("fmd_nequip_self_connection", ptr(xs[0]), ptr(xs[1]), ptr(xs[2]), ptr(elem), ptr(w0), ptr(w1), ptr(w2), n,
+             0, ptr(out[0]), ptr(out[1]), ptr(out[2]), stream(x0.device))
+        ctx.save_for_backward(elem, t0, t1, t2)
+        return tuple(out)
+
+    @staticmethod
+    def backward(ctx, g0, g1, g2):
+        elem, t0, t1, t2 = ctx.saved_tensors
+        gs = [g.contiguous() for g in (g0, g1, g2)]
+        dx = [torch.empty_like(g) for g in gs]
+        call("fmd_nequip_self_connection", ptr(gs[0]), ptr(gs[1]), ptr(gs[2]), ptr(elem), ptr(t0), ptr(t1), ptr(t2),
+             gs[0].shape[0], 0, ptr(dx[0]), ptr(dx[1]), ptr(dx[2]), stream(gs[0].device))
+        return dx[0], dx[1], dx[2], None, None, None, None, None, None, None
+
+
 class _Gate(Function):
     """(x0 [N, 128], x1 [3N, 64], x2 [5N, 32]) = the gated nonlinearity of the second linear's outputs
     (o0 [N, 224], o1 [3N, 64], o2 [5N, 32]) plus the self-connection planes sc (``fmd_nequip_gate``)."""
@@ -205,20 +230,20 @@ class NequIPModel:
         self.w = {k: torch.as_tensor(v, dtype=torch.float32, device=self.device) for k, v in host.items()}
         # the matrices the GEMM reads as [out, in]
         self.lin = {k: v.t().contiguous() for k, v in self.w.items() if ".lin" in k}
-        self.sc = {k: v.transpose(1, 2).contiguous() for k, v in self.w.items() if ".sc" in k}
+        # self-connection weights [elements, out, in] for the input gradient
+        self.sc_t = {k: v.transpose(1, 2).contiguous() for k, v in self.w.items() if ".sc" in k}
         self.precision = precision
         self.cg = torch.as_tensor(coupling_table(), device=self.device)
 
     # ------------------------------------------------------------ per-system state (no host work per call)
     def prepare(self, batch):
-        """The element groups and the host cell of ``batch``'s system (host reads, once per system; not
+        """The element rows and the host cell of ``batch``'s system (host reads, once per system; not
         inside a capture); returns the batch."""
         N = batch.n_real
         elem = batch.species[:N].long() - 1
         if int(elem.min()) < 0 or int(elem.max()) >= self.config.n_elements:
             raise ValueError(f"atomic numbers outside 1..{self.config.n_elements}")
-        self._elem = elem
-        self._groups = [(int(z), (elem == z).nonzero().reshape(-1)) for z in torch.unique(elem).tolist()]
+        self._elem = elem.contiguous()
         self._cell_host, self._cell_ptr = _host_cell(batch.cell)
         self._prepared = (batch.species.data_ptr(), batch.cell.data_ptr())
         return batch
@@ -229,16 +254,6 @@ class NequIPModel:
     def _linear(self, x, weight):
         return wide_gemm.linear(x, weight, precision=self.precision)
 
-    def _self_connection(self, xl: Tensor, n: int, L: int, l: int, groups) -> Tensor:
-        """The element-dependent linear of plane ``xl`` [n d, u] (atom rows gathered per element)."""
-        d, u = DIM[l], MULT[l]
-        rows = xl.view(n, d * u)
-        out = torch.zeros(n, d * u, device=xl.device)
-        for z, idx in groups:
-            y = self._linear(rows.index_select(0, idx).view(-1, u), self.sc[f"L{L}.sc{l}"][z])
-            out = out.index_copy(0, idx, y.view(-1, d * u))
-        return out.view(n * d, u)
-
     def energy_forces(self, batch, n_systems: int = 1) -> tuple[Tensor, Tensor]:
         """(energy [1] fp64, forces [N, 3]) of one system; capturable in a CUDA graph once ``prepare``
         ran for the system (no host synchronisation)."""
@@ -248,7 +263,7 @@ class NequIPModel:
             self.prepare(batch)
         c = self.config
         N = batch.n_real
-        elem, groups = self._elem, self._groups
+        elem = self._elem
         with torch.enable_grad():
             pos = batch.positions.detach().requires_grad_(True)
             Y, B = _EdgeBasis.apply(pos, self, batch)
@@ -257,8 +272,10 @@ class NequIPModel:
             for L in range(c.num_layers):
                 zero = lambda l: torch.zeros(N * DIM[l], MULT[l], device=self.device)  # noqa: E731
                 # a linear map of an exact zero plane is an exact zero plane: not launched
-                sc = [self._self_connection(x[l], N, L, l, groups) if x[l] is not None else zero(l) for l in range(3)]
                 h = [self._linear(x[l], self.lin[f"L{L}.lin1_{l}"]) if x[l] is not None else zero(l) for l in range(3)]
+                sc = _SelfConnection.apply(*[x[l] if x[l] is not None else zero(l) for l in range(3)], elem,
+                                           *[self.w[f"L{L}.sc{l}"] for l in range(3)],
+                                           *[self.sc_t[f"L{L}.sc{l}"] for l in range(3)])
                 r = torch.nn.functional.silu(self._linear(B, self.w[f"L{L}.rad1"]))
                 r = torch.nn.functional.silu(self._linear(r, self.w[f"L{L}.rad2"]))
                 W = self._linear(r, self.w[f"L{L}.rad3"])

@@ -787,6 +787,16 @@ FMD_API fmd_status fmd_nequip_conv_bwd(const float* x, const float* Y, const flo
                                        const float* grad_messages, float* grad_x, float* grad_W, float* grad_Y,
                                        void* stream);
 
+/* The self-connection of the three feature planes (x0 [N, 128], x1
+ * [N, 3, 64], x2 [N, 5, 32]): out_l[n, m, c] = sum_u x_l[n, m, u]
+ * w_l[elem[n], u, c], w_l [elements, U, U] (SevenNet's element-dependent
+ * self-connection linear); transposed = 1 takes w_l[elem[n], c, u] instead
+ * (the input gradient). elem: the atoms' element rows (atomic number - 1),
+ * checked by the caller. */
+FMD_API fmd_status fmd_nequip_self_connection(const float* x0, const float* x1, const float* x2, const int64_t* elem,
+                                              const float* w0, const float* w1, const float* w2, int64_t n_atoms,
+                                              int32_t transposed, float* out0, float* out1, float* out2,
+                                              void* stream);
 /* The gated nonlinearity closing an interaction block, plus its
  * self-connection sc (SevenNet's gate after the second linear): x0 =
  * silu(o0[:, :128]) + sc0; x1[n, m, c] = o1[n, m, c] sigmoid(o0[n, 128 + c]) +

@@ -106,3 +106,24 @@ def test_gate_of_no_atoms_is_a_no_op(cuda):
 
     ins = [torch.zeros(0, w, device=cuda) for w in (224, 64, 32, 128, 64, 32)]
     assert [tuple(t.shape) for t in gate(*ins)] == [(0, 128), (0, 64), (0, 32)]
+
+
+def test_self_connection_matches_torch_fp32(cuda):
+    """fmd_nequip_self_connection (out[n, m] = x[n, m] @ w[elem[n]]) and its transposed input gradient
+    against torch FP32 einsums: within 1e-5 relative of the largest value."""
+    from fastmd_b200.nequip import _SelfConnection
+
+    g = torch.Generator(device="cpu").manual_seed(9)
+    n, n_elem = 777, 89
+    elem = torch.randint(0, n_elem, (n,), generator=g).to(cuda)
+    w = [torch.randn(n_elem, u, u, generator=g).to(cuda) / u ** 0.5 for u in (128, 64, 32)]
+    xs = [torch.randn(n * d, u, generator=g).to(cuda).requires_grad_(True) for d, u in ((1, 128), (3, 64), (5, 32))]
+    out = _SelfConnection.apply(*xs, elem, *w, *[wl.transpose(1, 2).contiguous() for wl in w])
+    ref_x = [t.detach().clone().requires_grad_(True) for t in xs]
+    ref = [torch.einsum("nmu,nuv->nmv", t.view(n, d, -1), wl[elem]).reshape(n * d, -1)
+           for t, d, wl in zip(ref_x, (1, 3, 5), w)]
+    for a, b in zip(out, ref):
+        assert (a - b).abs().max() <= 1e-5 * b.abs().max()
+    up = [torch.randn(t.shape, generator=g).to(cuda) for t in ref]
+    for a, b in zip(torch.autograd.grad(out, xs, up), torch.autograd.grad(ref, ref_x, up)):
+        assert (a - b).abs().max() <= 1e-5 * b.abs().max()
