@@ -13,9 +13,9 @@
 // sqrt15/2 (x^2 - y^2)] of the unit edge vector u; CG [615] the 15 dense
 // coupling tensors [2 l3 + 1][2 l1 + 1][2 l2 + 1] in path order.
 //
-// Convolution (one warp per receiver i, its edges in CSR order, a lane per
-// channel u; the receiver's 3136 accumulators in shared memory, each owned
-// by one lane: deterministic):
+// Convolution (one block of 4 warps per receiver i, its edges in CSR order;
+// each warp owns a fixed set of paths, a lane per channel u; the receiver's
+// 3136 accumulators in shared memory, each owned by one lane: deterministic):
 //   m[i, path, u, m3] = inv_avg * sum_e W[e, path, u] sum_m1 A_e[path][m3][m1] x[j(e), l1, u, m1]
 // with the edge's coupling matrices A_e[path][m3][m1] = sum_m2 CG[m3, m1, m2]
 // Y[e, l2, m2] formed once per edge (179 floats) and shared by all channels:
@@ -229,16 +229,6 @@ __host__ __device__ constexpr int a_off(int P) {
 }
 constexpr int kAW = a_off(15);  // 179
 constexpr int kTP = 25;         // the largest a_size
-// per-warp shared-memory strides (floats): the staged weight/feature rows start 16-byte aligned (a multiple
-// of 4 floats from the 16-byte aligned base, 616 floats of CG table first)
-constexpr int kFwdRows = kMW + kAW + 1;                 // offset of the weight row in a forward warp slot
-constexpr int kFwdStride = kFwdRows + kWW + kXW;        // 4756
-constexpr int kBwdRows = kMW + kAW + 32 * kTP + 1;      // offset of the weight row in a backward warp slot
-constexpr int kBwdStride = kBwdRows + kWW + kXW;        // 5556
-static_assert(616 % 4 == 0 && kFwdRows % 4 == 0 && kFwdStride % 4 == 0 && kBwdRows % 4 == 0 &&
-                  kBwdStride % 4 == 0 && kWW % 4 == 0 && kXW % 4 == 0,
-              "staged rows must stay 16-byte aligned");
-
 template <int P>
 __device__ __forceinline__ void path_coupling(const float* cg, const float* y, float* aw, int lane) {
     constexpr PathInfo pi = kPaths[P];
@@ -266,26 +256,6 @@ __device__ __forceinline__ void load_couplings(const ConvArgs& a, const float* c
     __syncwarp();  // the previous edge's readers are done
     edge_couplings(cg, y, aw, lane, std::make_integer_sequence<int, 15>{});
     __syncwarp();
-}
-
-// the edge's weight row (960 floats) and its sender's feature row (480 floats) in the warp's shared
-// memory: 16-byte loads issued together (one memory round trip per edge instead of one per path)
-__device__ __forceinline__ void stage_rows(const ConvArgs& a, int64_t e, int64_t j, float* ws, float* xs, int lane) {
-    const float4* wsrc = reinterpret_cast<const float4*>(a.W + e * kWW);
-    float4 wv[(kWW / 4 + 31) / 32], xv[(kXW / 4 + 31) / 32];
-#pragma unroll
-    for (int r = 0; r < (kWW / 4 + 31) / 32; ++r)
-        if (lane + 32 * r < kWW / 4) wv[r] = wsrc[lane + 32 * r];
-#pragma unroll
-    for (int r = 0; r < (kXW / 4 + 31) / 32; ++r)  // the plane pieces are whole float4s (128, 192, 160)
-        if (lane + 32 * r < kXW / 4)
-            xv[r] = *reinterpret_cast<const float4*>(a.x + x_planar(a.n_atoms, j, 4 * (lane + 32 * r)));
-#pragma unroll
-    for (int r = 0; r < (kWW / 4 + 31) / 32; ++r)
-        if (lane + 32 * r < kWW / 4) reinterpret_cast<float4*>(ws)[lane + 32 * r] = wv[r];
-#pragma unroll
-    for (int r = 0; r < (kXW / 4 + 31) / 32; ++r)
-        if (lane + 32 * r < kXW / 4) reinterpret_cast<float4*>(xs)[lane + 32 * r] = xv[r];
 }
 
 // one path's contribution of edge e (lane channels u) into the receiver's accumulators:
@@ -316,33 +286,96 @@ __device__ __forceinline__ void all_paths_fwd(const float* ws, const float* xs, 
     (path_fwd<P>(ws, xs, aw, acc, lane), ...);
 }
 
-// warp shared memory of the kernels: [cg 616 | per warp: rows, A 179 (, T partials 32 x 25)]
-__global__ void __launch_bounds__(32 * kNqWarps) nq_conv_kernel(ConvArgs a, float* __restrict__ m) {
-    extern __shared__ __align__(16) float nq_smem[];
-    float* cg = nq_smem;                                            // [616]
-    float* acc = nq_smem + 616 + (threadIdx.x >> 5) * kFwdStride;  // this warp's receiver
-    float* aw = acc + kMW;
-    float* ws = acc + kFwdRows;
-    float* xs = ws + kWW;
-    for (int t = threadIdx.x; t < kCGN; t += blockDim.x) cg[t] = a.cg[t];
-    __syncthreads();
-    const int lane = threadIdx.x & 31;
-    for (int64_t i = int64_t(blockIdx.x) * kNqWarps + (threadIdx.x >> 5); i < a.n_atoms;
-         i += int64_t(gridDim.x) * kNqWarps) {
-        for (int t = lane; t < kMW; t += 32) acc[t] = 0.f;
-        for (int64_t e = a.recv_off[i]; e < a.recv_off[i + 1]; ++e) {
-            const int64_t j = a.edge_index[2 * e + 1];
-            __syncwarp();
-            stage_rows(a, e, j, ws, xs, lane);
-            load_couplings(a, cg, e, aw, lane);
-            all_paths_fwd(ws, xs, aw, acc, lane, std::make_integer_sequence<int, 15>{});
-        }
-        __syncwarp();
-        for (int t = lane; t < kMW; t += 32) m[m_planar(a.n_atoms, i, t)] = acc[t] * a.inv_avg;
-        __syncwarp();
+// A receiver's edges are shared by the 4 warps of its block: each warp owns a fixed set of paths
+// (disjoint message columns, disjoint dW columns), balanced by FMA count per edge (U n3 n1 summed:
+// 2048, 2080, 2176, 2208 of 8512). The block stages the edge's weight and sender rows once; a warp
+// forms only its own paths' coupling matrices.
+constexpr int kRecvThreads = 128;
+using Warp0Paths = std::integer_sequence<int, 6, 8, 0>;
+using Warp1Paths = std::integer_sequence<int, 9, 11, 10>;
+using Warp2Paths = std::integer_sequence<int, 14, 2, 3, 12>;
+using Warp3Paths = std::integer_sequence<int, 5, 7, 1, 13, 4>;
+
+template <int... P>
+__device__ __forceinline__ void couplings_of(const float* cg, const float* y, float* aw, int lane,
+                                             std::integer_sequence<int, P...>) {
+    (path_coupling<P>(cg, y, aw, lane), ...);
+}
+
+__device__ __forceinline__ void warp_couplings(int warp, const float* cg, const float* y, float* aw, int lane) {
+    switch (warp) {
+        case 0: couplings_of(cg, y, aw, lane, Warp0Paths{}); break;
+        case 1: couplings_of(cg, y, aw, lane, Warp1Paths{}); break;
+        case 2: couplings_of(cg, y, aw, lane, Warp2Paths{}); break;
+        default: couplings_of(cg, y, aw, lane, Warp3Paths{}); break;
     }
 }
 
+// the edge's weight row (240 float4) and its sender's feature row (120 float4, from the three planes)
+// staged by the block's 128 threads, all loads issued before the stores
+__device__ __forceinline__ void stage_rows_block(const ConvArgs& a, int64_t e, int64_t j, float* ws, float* xs,
+                                                 int tid) {
+    constexpr int NW = kWW / 4, NX = kXW / 4;
+    const float4* wsrc = reinterpret_cast<const float4*>(a.W + e * kWW);
+    float4 v[3];
+#pragma unroll
+    for (int r = 0; r < 3; ++r) {
+        const int q = tid + kRecvThreads * r;
+        if (q < NW)
+            v[r] = wsrc[q];
+        else if (q < NW + NX)
+            v[r] = *reinterpret_cast<const float4*>(a.x + x_planar(a.n_atoms, j, 4 * (q - NW)));
+    }
+#pragma unroll
+    for (int r = 0; r < 3; ++r) {
+        const int q = tid + kRecvThreads * r;
+        if (q < NW)
+            reinterpret_cast<float4*>(ws)[q] = v[r];
+        else if (q < NW + NX)
+            reinterpret_cast<float4*>(xs)[q - NW] = v[r];
+    }
+}
+
+__device__ __forceinline__ void load_y(const ConvArgs& a, int64_t e, float* y) {
+#pragma unroll
+    for (int q = 0; q < 9; ++q) y[q] = a.Y[9 * e + q];
+}
+
+// block shared memory: [cg 616 | acc 3136 | A 179 + 1 | W row 960 | x row 480]
+constexpr int kFwdBlock = 616 + kMW + kAW + 1 + kWW + kXW;
+static_assert((616 + kMW + kAW + 1) % 4 == 0 && (616 + kMW + kAW + 1 + kWW) % 4 == 0, "16-byte staged rows");
+
+__global__ void __launch_bounds__(kRecvThreads) nq_conv_kernel(ConvArgs a, float* __restrict__ m) {
+    extern __shared__ __align__(16) float nq_smem[];
+    float* cg = nq_smem;
+    float* acc = cg + 616;
+    float* aw = acc + kMW;
+    float* ws = aw + kAW + 1;
+    float* xs = ws + kWW;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int t = tid; t < kCGN; t += kRecvThreads) cg[t] = a.cg[t];
+    for (int64_t i = blockIdx.x; i < a.n_atoms; i += gridDim.x) {
+        __syncthreads();  // the previous receiver's messages are written out
+        for (int t = tid; t < kMW; t += kRecvThreads) acc[t] = 0.f;
+        for (int64_t e = a.recv_off[i]; e < a.recv_off[i + 1]; ++e) {
+            const int64_t j = a.edge_index[2 * e + 1];
+            float y[9];
+            load_y(a, e, y);
+            __syncthreads();  // the previous edge's rows are consumed
+            stage_rows_block(a, e, j, ws, xs, tid);
+            warp_couplings(warp, cg, y, aw, lane);
+            __syncthreads();
+            switch (warp) {
+                case 0: all_paths_fwd(ws, xs, aw, acc, lane, Warp0Paths{}); break;
+                case 1: all_paths_fwd(ws, xs, aw, acc, lane, Warp1Paths{}); break;
+                case 2: all_paths_fwd(ws, xs, aw, acc, lane, Warp2Paths{}); break;
+                default: all_paths_fwd(ws, xs, aw, acc, lane, Warp3Paths{}); break;
+            }
+        }
+        __syncthreads();
+        for (int t = tid; t < kMW; t += kRecvThreads) m[m_planar(a.n_atoms, i, t)] = acc[t] * a.inv_avg;
+    }
+}
 // dW[e, path, u] = sum_m3 g[u, m3] sum_m1 A[m3][m1] x[u, m1]; the lane's share of dY[e]: the path's
 // T[m3][m1] = sum_u W g[u, m3] x[u, m1] folded over the lanes (fixed order), times CG
 template <int P>
@@ -394,40 +427,51 @@ __device__ __forceinline__ void all_paths_bwd_edge(const float* ws, const float*
     (path_bwd_edge<P>(ws, xs, cg, aw, dm, tp, e, dW, dy, lane), ...);
 }
 
-// per receiver: dW and dY of its edges (dY: lane partials folded by a fixed xor tree)
-__global__ void __launch_bounds__(32 * kNqWarps) nq_conv_bwd_edge_kernel(ConvArgs a, const float* __restrict__ dmsg,
-                                                                         float* __restrict__ dW,
-                                                                         float* __restrict__ dY) {
+// per receiver: dW and dY of its edges; each warp its own paths (dW columns disjoint), dY from the
+// warps' lane-folded partials summed in warp order
+constexpr int kBwdBlock = 616 + kMW + kAW + 1 + kWW + kXW + 4 * 32 * kTP + 36;
+
+__global__ void __launch_bounds__(kRecvThreads) nq_conv_bwd_edge_kernel(ConvArgs a, const float* __restrict__ dmsg,
+                                                                        float* __restrict__ dW,
+                                                                        float* __restrict__ dY) {
     extern __shared__ __align__(16) float nq_smem[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float* cg = nq_smem;
-    float* dm = nq_smem + 616 + (threadIdx.x >> 5) * kBwdStride;
+    float* dm = cg + 616;
     float* aw = dm + kMW;
-    float* tp = aw + kAW;
-    float* ws = dm + kBwdRows;
+    float* ws = aw + kAW + 1;
     float* xs = ws + kWW;
-    for (int t = threadIdx.x; t < kCGN; t += blockDim.x) cg[t] = a.cg[t];
-    __syncthreads();
-    const int lane = threadIdx.x & 31;
-    for (int64_t i = int64_t(blockIdx.x) * kNqWarps + (threadIdx.x >> 5); i < a.n_atoms;
-         i += int64_t(gridDim.x) * kNqWarps) {
-        __syncwarp();
-        for (int t = lane; t < kMW; t += 32) dm[t] = dmsg[m_planar(a.n_atoms, i, t)] * a.inv_avg;
-        __syncwarp();
+    float* tp = xs + kXW + warp * 32 * kTP;
+    float* dyw = xs + kXW + 4 * 32 * kTP;  // [4][9]
+    for (int t = tid; t < kCGN; t += kRecvThreads) cg[t] = a.cg[t];
+    for (int64_t i = blockIdx.x; i < a.n_atoms; i += gridDim.x) {
+        __syncthreads();  // the previous receiver is done
+        for (int t = tid; t < kMW; t += kRecvThreads) dm[t] = dmsg[m_planar(a.n_atoms, i, t)] * a.inv_avg;
         for (int64_t e = a.recv_off[i]; e < a.recv_off[i + 1]; ++e) {
             const int64_t j = a.edge_index[2 * e + 1];
-            __syncwarp();
-            stage_rows(a, e, j, ws, xs, lane);
-            load_couplings(a, cg, e, aw, lane);
+            float y[9];
+            load_y(a, e, y);
+            __syncthreads();  // the previous edge's rows and dY partials are consumed
+            stage_rows_block(a, e, j, ws, xs, tid);
+            warp_couplings(warp, cg, y, aw, lane);
+            __syncthreads();
             float dy[9];
 #pragma unroll
             for (int q = 0; q < 9; ++q) dy[q] = 0.f;
-            all_paths_bwd_edge(ws, xs, cg, aw, dm, tp, e, dW, dy, lane, std::make_integer_sequence<int, 15>{});
+            switch (warp) {
+                case 0: all_paths_bwd_edge(ws, xs, cg, aw, dm, tp, e, dW, dy, lane, Warp0Paths{}); break;
+                case 1: all_paths_bwd_edge(ws, xs, cg, aw, dm, tp, e, dW, dy, lane, Warp1Paths{}); break;
+                case 2: all_paths_bwd_edge(ws, xs, cg, aw, dm, tp, e, dW, dy, lane, Warp2Paths{}); break;
+                default: all_paths_bwd_edge(ws, xs, cg, aw, dm, tp, e, dW, dy, lane, Warp3Paths{}); break;
+            }
 #pragma unroll
             for (int q = 0; q < 9; ++q)
                 for (int d = 16; d > 0; d >>= 1) dy[q] += __shfl_xor_sync(0xffffffffu, dy[q], d);
             if (lane == 0)
 #pragma unroll
-                for (int q = 0; q < 9; ++q) dY[9 * e + q] = dy[q];
+                for (int q = 0; q < 9; ++q) dyw[warp * 9 + q] = dy[q];
+            __syncthreads();
+            if (tid < 9) dY[9 * e + tid] = ((dyw[tid] + dyw[9 + tid]) + dyw[18 + tid]) + dyw[27 + tid];
         }
     }
 }
@@ -685,9 +729,9 @@ fmd_status fmd_nequip_conv(const float* x, const float* Y, const float* W, const
     if (n_atoms == 0) return FMD_OK;
     if (messages == nullptr) return FMD_ERR_INVALID_ARGUMENT;
     static bool granted = false;
-    const size_t smem = conv_smem(kFwdStride);
+    const size_t smem = sizeof(float) * kFwdBlock;
     if ((st = grant_once((const void*)nq_conv_kernel, smem, granted)) != FMD_OK) return st;
-    nq_conv_kernel<<<grid_of(n_atoms, kNqWarps), 32 * kNqWarps, smem, as_stream(stream)>>>(a, messages);
+    nq_conv_kernel<<<grid_of(n_atoms, 1), kRecvThreads, smem, as_stream(stream)>>>(a, messages);
     return check_launch();
 }
 
@@ -703,11 +747,11 @@ fmd_status fmd_nequip_conv_bwd(const float* x, const float* Y, const float* W, c
         send_off == nullptr)
         return FMD_ERR_INVALID_ARGUMENT;
     static bool granted_e = false, granted_x = false;
-    const size_t smem_e = conv_smem(kBwdStride), smem_x = conv_smem(kXW + kAW);
+    const size_t smem_e = sizeof(float) * kBwdBlock, smem_x = conv_smem(kXW + kAW);
     if ((st = grant_once((const void*)nq_conv_bwd_edge_kernel, smem_e, granted_e)) != FMD_OK) return st;
     if ((st = grant_once((const void*)nq_conv_bwd_x_kernel, smem_x, granted_x)) != FMD_OK) return st;
     const cudaStream_t s = as_stream(stream);
-    nq_conv_bwd_edge_kernel<<<grid_of(n_atoms, kNqWarps), 32 * kNqWarps, smem_e, s>>>(a, grad_messages, grad_W,
+    nq_conv_bwd_edge_kernel<<<grid_of(n_atoms, 1), kRecvThreads, smem_e, s>>>(a, grad_messages, grad_W,
                                                                                        grad_Y);
     if ((st = check_launch()) != FMD_OK) return st;
     nq_conv_bwd_x_kernel<<<grid_of(n_atoms, kNqWarps), 32 * kNqWarps, smem_x, s>>>(a, grad_messages, grad_x);
