@@ -35,7 +35,6 @@ constexpr int kXW = 480;
 constexpr int kMW = 3136;
 constexpr int kWW = 960;
 constexpr int kCGN = 615;
-constexpr int kNqWarps = 4;
 
 __host__ __device__ constexpr int dim_of(int l) { return 2 * l + 1; }
 __host__ __device__ constexpr int mult_of(int l) { return l == 0 ? 128 : (l == 1 ? 64 : 32); }
@@ -476,48 +475,53 @@ __global__ void __launch_bounds__(kRecvThreads) nq_conv_bwd_edge_kernel(ConvArgs
     }
 }
 
-// dx[j, l1, m1, u] += W[e, path, u] sum_m3 A[m3][m1] dm[i, l3, m3, path channel u]
-template <int P>
+// dx[j, l1, m1, u] += W[e, path, u] sum_m3 A[m3][m1] dm[i, l3, m3, path channel u] for the channels
+// u in [U0, U0 + 32) and the components m1 in [M0, M1)
+template <int P, int U0, int M0, int M1>
 __device__ __forceinline__ void path_bwd_x(const ConvArgs& a, const float* aw, const float* const* dmi, int64_t e,
                                            float* dx, int lane) {
     constexpr PathInfo pi = kPaths[P];
-    constexpr int n1 = dim_of(pi.l1), n3 = dim_of(pi.l3), U = mult_of(pi.l1);
-#pragma unroll 1
-    for (int u = lane; u < U; u += 32) {
-        const float w = a.W[e * kWW + pi.w_off + u];
-        float g[n3];
+    constexpr int n1 = dim_of(pi.l1), n3 = dim_of(pi.l3);
+    static_assert(U0 + 32 <= mult_of(pi.l1) && 0 <= M0 && M0 < M1 && M1 <= n1, "work item");
+    const int u = U0 + lane;
+    const float w = a.W[e * kWW + pi.w_off + u];
+    float g[n3];
 #pragma unroll
-        for (int m3 = 0; m3 < n3; ++m3) g[m3] = dmi[pi.l3][m3 * m_mult(pi.l3) + c_off(pi) + u];
+    for (int m3 = 0; m3 < n3; ++m3) g[m3] = dmi[pi.l3][m3 * m_mult(pi.l3) + c_off(pi) + u];
 #pragma unroll
-        for (int m1 = 0; m1 < n1; ++m1) {
-            float s = 0.f;
+    for (int m1 = M0; m1 < M1; ++m1) {
+        float s = 0.f;
 #pragma unroll
-            for (int m3 = 0; m3 < n3; ++m3) s = fmaf(aw[a_off(P) + m3 * n1 + m1], g[m3], s);
-            dx[x_idx(pi.l1, u, m1)] = fmaf(w, s, dx[x_idx(pi.l1, u, m1)]);
-        }
+        for (int m3 = 0; m3 < n3; ++m3) s = fmaf(aw[a_off(P) + m3 * n1 + m1], g[m3], s);
+        dx[x_idx(pi.l1, u, m1)] = fmaf(w, s, dx[x_idx(pi.l1, u, m1)]);
     }
 }
 
-template <int... P>
-__device__ __forceinline__ void all_paths_bwd_x(const ConvArgs& a, const float* aw, const float* const* dmi, int64_t e,
-                                                float* dx, int lane, std::integer_sequence<int, P...>) {
-    (path_bwd_x<P>(a, aw, dmi, e, dx, lane), ...);
+template <int U0, int M0, int M1, int... P>
+__device__ __forceinline__ void items_bwd_x(const ConvArgs& a, const float* aw, const float* const* dmi, int64_t e,
+                                            float* dx, int lane) {
+    (path_bwd_x<P, U0, M0, M1>(a, aw, dmi, e, dx, lane), ...);
 }
 
-// per sender j: dx[j] over its sender run (the receivers' message gradients read from global memory)
-__global__ void __launch_bounds__(32 * kNqWarps) nq_conv_bwd_x_kernel(ConvArgs a, const float* __restrict__ dmsg,
-                                                                      float* __restrict__ dx_out) {
+// per sender j: dx[j] over its sender run, a block of 4 warps; each warp owns the dx entries of fixed
+// (l1, 32-channel chunk, m1 range) items, so that every dx entry is summed by one lane in path and
+// edge order (FMA per edge: 2112, 2208, 2208, 1984 of 8512). Every warp forms the edge's full coupling
+// matrices in its own copy (no block barrier per edge); the receivers' message gradients are read from
+// global memory, coalesced over the lanes' channels.
+constexpr int kBxBlock = 616 + kXW + 4 * (kAW + 1);
+
+__global__ void __launch_bounds__(kRecvThreads) nq_conv_bwd_x_kernel(ConvArgs a, const float* __restrict__ dmsg,
+                                                                     float* __restrict__ dx_out) {
     extern __shared__ __align__(16) float nq_smem[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float* cg = nq_smem;
-    float* dx = nq_smem + 616 + (threadIdx.x >> 5) * (kXW + kAW);
-    float* aw = dx + kXW;
-    for (int t = threadIdx.x; t < kCGN; t += blockDim.x) cg[t] = a.cg[t];
-    __syncthreads();
-    const int lane = threadIdx.x & 31;
-    for (int64_t j = int64_t(blockIdx.x) * kNqWarps + (threadIdx.x >> 5); j < a.n_atoms;
-         j += int64_t(gridDim.x) * kNqWarps) {
-        __syncwarp();
-        for (int t = lane; t < kXW; t += 32) dx[t] = 0.f;
+    float* dx = cg + 616;
+    float* aw = dx + kXW + warp * (kAW + 1);
+    for (int t = tid; t < kCGN; t += kRecvThreads) cg[t] = a.cg[t];
+    for (int64_t j = blockIdx.x; j < a.n_atoms; j += gridDim.x) {
+        __syncthreads();  // the previous sender is written out (and cg is loaded)
+        for (int t = tid; t < kXW; t += kRecvThreads) dx[t] = 0.f;
+        __syncthreads();
         for (int64_t s = a.send_off[j]; s < a.send_off[j + 1]; ++s) {
             const int64_t e = a.send_perm[s];
             const int64_t i = a.edge_index[2 * e];
@@ -525,10 +529,27 @@ __global__ void __launch_bounds__(32 * kNqWarps) nq_conv_bwd_x_kernel(ConvArgs a
             // the receiver's message-gradient rows of the three planes
             const float* dmi[3] = {dmsg + m_planar(a.n_atoms, i, 0), dmsg + m_planar(a.n_atoms, i, m_off_of(1)),
                                    dmsg + m_planar(a.n_atoms, i, m_off_of(2))};
-            all_paths_bwd_x(a, aw, dmi, e, dx, lane, std::make_integer_sequence<int, 15>{});
+            switch (warp) {
+                case 0:
+                    items_bwd_x<0, 0, 3, 9, 10, 11, 12, 13, 14>(a, aw, dmi, e, dx, lane);
+                    break;
+                case 1:
+                    items_bwd_x<0, 0, 3, 3, 4, 5, 6, 7, 8>(a, aw, dmi, e, dx, lane);
+                    items_bwd_x<0, 0, 1, 0, 1, 2>(a, aw, dmi, e, dx, lane);
+                    break;
+                case 2:
+                    items_bwd_x<32, 0, 3, 3, 4, 5, 6, 7, 8>(a, aw, dmi, e, dx, lane);
+                    items_bwd_x<32, 0, 1, 0, 1, 2>(a, aw, dmi, e, dx, lane);
+                    break;
+                default:
+                    items_bwd_x<0, 3, 5, 9, 10, 11, 12, 13, 14>(a, aw, dmi, e, dx, lane);
+                    items_bwd_x<64, 0, 1, 0, 1, 2>(a, aw, dmi, e, dx, lane);
+                    items_bwd_x<96, 0, 1, 0, 1, 2>(a, aw, dmi, e, dx, lane);
+                    break;
+            }
         }
-        __syncwarp();
-        for (int t = lane; t < kXW; t += 32) dx_out[x_planar(a.n_atoms, j, t)] = dx[t] * a.inv_avg;
+        __syncthreads();
+        for (int t = tid; t < kXW; t += kRecvThreads) dx_out[x_planar(a.n_atoms, j, t)] = dx[t] * a.inv_avg;
     }
 }
 
@@ -646,7 +667,6 @@ inline int grid_of(int64_t work, int per) {
     return int(g < 148 * 32 ? (g > 0 ? g : 1) : 148 * 32);
 }
 
-size_t conv_smem(int per_warp) { return sizeof(float) * (616 + size_t(kNqWarps) * per_warp); }
 
 }  // namespace
 }  // namespace fmd
@@ -747,14 +767,14 @@ fmd_status fmd_nequip_conv_bwd(const float* x, const float* Y, const float* W, c
         send_off == nullptr)
         return FMD_ERR_INVALID_ARGUMENT;
     static bool granted_e = false, granted_x = false;
-    const size_t smem_e = sizeof(float) * kBwdBlock, smem_x = conv_smem(kXW + kAW);
+    const size_t smem_e = sizeof(float) * kBwdBlock, smem_x = sizeof(float) * kBxBlock;
     if ((st = grant_once((const void*)nq_conv_bwd_edge_kernel, smem_e, granted_e)) != FMD_OK) return st;
     if ((st = grant_once((const void*)nq_conv_bwd_x_kernel, smem_x, granted_x)) != FMD_OK) return st;
     const cudaStream_t s = as_stream(stream);
     nq_conv_bwd_edge_kernel<<<grid_of(n_atoms, 1), kRecvThreads, smem_e, s>>>(a, grad_messages, grad_W,
                                                                                        grad_Y);
     if ((st = check_launch()) != FMD_OK) return st;
-    nq_conv_bwd_x_kernel<<<grid_of(n_atoms, kNqWarps), 32 * kNqWarps, smem_x, s>>>(a, grad_messages, grad_x);
+    nq_conv_bwd_x_kernel<<<grid_of(n_atoms, 1), kRecvThreads, smem_x, s>>>(a, grad_messages, grad_x);
     return check_launch();
 }
 
