@@ -227,7 +227,6 @@ __host__ __device__ constexpr int a_off(int P) {
     return s;
 }
 constexpr int kAW = a_off(15);  // 179
-constexpr int kTP = 25;         // the largest a_size
 template <int P>
 __device__ __forceinline__ void path_coupling(const float* cg, const float* y, float* aw, int lane) {
     constexpr PathInfo pi = kPaths[P];
@@ -376,10 +375,10 @@ __global__ void __launch_bounds__(kRecvThreads) nq_conv_kernel(ConvArgs a, float
     }
 }
 // dW[e, path, u] = sum_m3 g[u, m3] sum_m1 A[m3][m1] x[u, m1]; the lane's share of dY[e]: the path's
-// T[m3][m1] = sum_u W g[u, m3] x[u, m1] folded over the lanes (fixed order), times CG
+// T[m3][m1] = sum_u W g[u, m3] x[u, m1] over the lane's channels, times CG (lanes added by the caller)
 template <int P>
 __device__ __forceinline__ void path_bwd_edge(const float* ws, const float* xs, const float* cg, const float* aw,
-                                              const float* dm, float* tp, int64_t e, float* dW, float* dy, int lane) {
+                                              const float* dm, int64_t e, float* dW, float* dy, int lane) {
     constexpr PathInfo pi = kPaths[P];
     constexpr int n1 = dim_of(pi.l1), n2 = dim_of(pi.l2), n3 = dim_of(pi.l3), U = mult_of(pi.l1);
     float t[n3 * n1];
@@ -405,30 +404,27 @@ __device__ __forceinline__ void path_bwd_edge(const float* ws, const float* xs, 
         }
         dW[e * kWW + pi.w_off + u] = gw;
     }
+    // the lane's share of dY[e, l2]: its partial T folded with the coupling constants (the lanes' sums
+    // are added by the caller's xor tree)
 #pragma unroll
-    for (int q = 0; q < n3 * n1; ++q) tp[lane * kTP + q] = t[q];
-    __syncwarp();
-    if (lane < n3 * n1) {
-        float tq = 0.f;
-        for (int l = 0; l < 32; ++l) tq += tp[l * kTP + lane];
-        const int m3 = lane / n1, m1 = lane - m3 * n1;
+    for (int m2 = 0; m2 < n2; ++m2) {
+        float acc = 0.f;
 #pragma unroll
-        for (int m2 = 0; m2 < n2; ++m2)
-            dy[y_off(pi.l2) + m2] = fmaf(cg[pi.cg_off + (m3 * n1 + m1) * n2 + m2], tq, dy[y_off(pi.l2) + m2]);
+        for (int q = 0; q < n3 * n1; ++q) acc = fmaf(cg[pi.cg_off + q * n2 + m2], t[q], acc);
+        dy[y_off(pi.l2) + m2] += acc;
     }
-    __syncwarp();
 }
 
 template <int... P>
 __device__ __forceinline__ void all_paths_bwd_edge(const float* ws, const float* xs, const float* cg, const float* aw,
-                                                   const float* dm, float* tp, int64_t e, float* dW, float* dy,
+                                                   const float* dm, int64_t e, float* dW, float* dy,
                                                    int lane, std::integer_sequence<int, P...>) {
-    (path_bwd_edge<P>(ws, xs, cg, aw, dm, tp, e, dW, dy, lane), ...);
+    (path_bwd_edge<P>(ws, xs, cg, aw, dm, e, dW, dy, lane), ...);
 }
 
 // per receiver: dW and dY of its edges; each warp its own paths (dW columns disjoint), dY from the
 // warps' lane-folded partials summed in warp order
-constexpr int kBwdBlock = 616 + kMW + kAW + 1 + kWW + kXW + 4 * 32 * kTP + 36;
+constexpr int kBwdBlock = 616 + kMW + kAW + 1 + kWW + kXW + 36;
 
 __global__ void __launch_bounds__(kRecvThreads) nq_conv_bwd_edge_kernel(ConvArgs a, const float* __restrict__ dmsg,
                                                                         float* __restrict__ dW,
@@ -440,8 +436,7 @@ __global__ void __launch_bounds__(kRecvThreads) nq_conv_bwd_edge_kernel(ConvArgs
     float* aw = dm + kMW;
     float* ws = aw + kAW + 1;
     float* xs = ws + kWW;
-    float* tp = xs + kXW + warp * 32 * kTP;
-    float* dyw = xs + kXW + 4 * 32 * kTP;  // [4][9]
+    float* dyw = xs + kXW;  // [4][9]
     for (int t = tid; t < kCGN; t += kRecvThreads) cg[t] = a.cg[t];
     for (int64_t i = blockIdx.x; i < a.n_atoms; i += gridDim.x) {
         __syncthreads();  // the previous receiver is done
@@ -458,10 +453,10 @@ __global__ void __launch_bounds__(kRecvThreads) nq_conv_bwd_edge_kernel(ConvArgs
 #pragma unroll
             for (int q = 0; q < 9; ++q) dy[q] = 0.f;
             switch (warp) {
-                case 0: all_paths_bwd_edge(ws, xs, cg, aw, dm, tp, e, dW, dy, lane, Warp0Paths{}); break;
-                case 1: all_paths_bwd_edge(ws, xs, cg, aw, dm, tp, e, dW, dy, lane, Warp1Paths{}); break;
-                case 2: all_paths_bwd_edge(ws, xs, cg, aw, dm, tp, e, dW, dy, lane, Warp2Paths{}); break;
-                default: all_paths_bwd_edge(ws, xs, cg, aw, dm, tp, e, dW, dy, lane, Warp3Paths{}); break;
+                case 0: all_paths_bwd_edge(ws, xs, cg, aw, dm, e, dW, dy, lane, Warp0Paths{}); break;
+                case 1: all_paths_bwd_edge(ws, xs, cg, aw, dm, e, dW, dy, lane, Warp1Paths{}); break;
+                case 2: all_paths_bwd_edge(ws, xs, cg, aw, dm, e, dW, dy, lane, Warp2Paths{}); break;
+                default: all_paths_bwd_edge(ws, xs, cg, aw, dm, e, dW, dy, lane, Warp3Paths{}); break;
             }
 #pragma unroll
             for (int q = 0; q < 9; ++q)
