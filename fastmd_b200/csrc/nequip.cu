@@ -618,8 +618,34 @@ __global__ void __launch_bounds__(256) nq_gate_bwd_kernel(const float* __restric
 //
 // The element-dependent linear of every plane: out[n, m, c] = sum_u x[n, m, u] w_l[z(n), u, c]
 // (forward) or sum_u x[n, m, u] w_l[z(n), c, u] (transposed: the input gradient), w_l [elements, U, U].
-// One thread per output element over the three planes (480 per atom), its U products summed in u order;
-// the atom's row stays in L1, the weight column is read across the warp's consecutive c.
+// One thread per (atom, plane, output channel c) computes the plane's 2l + 1 rows of the atom, so each
+// weight load serves every row; the atom's rows are read as float4 (broadcast across the warp, L1),
+// the weights across the warp's consecutive c; each output summed in u order.
+
+template <int U, int D, bool T>
+__device__ __forceinline__ void sc_plane(const float* __restrict__ x, const float* __restrict__ w, int64_t a, int c,
+                                         float* __restrict__ o) {
+    const float* xr = x + a * (D * U);
+    float acc[D];
+#pragma unroll
+    for (int m = 0; m < D; ++m) acc[m] = 0.f;
+#pragma unroll 4
+    for (int u = 0; u < U; u += 4) {
+        float wv[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) wv[k] = T ? w[c * U + u + k] : w[(u + k) * U + c];
+#pragma unroll
+        for (int m = 0; m < D; ++m) {
+            const float4 xv = *reinterpret_cast<const float4*>(xr + m * U + u);
+            acc[m] = fmaf(xv.x, wv[0], acc[m]);
+            acc[m] = fmaf(xv.y, wv[1], acc[m]);
+            acc[m] = fmaf(xv.z, wv[2], acc[m]);
+            acc[m] = fmaf(xv.w, wv[3], acc[m]);
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < D; ++m) o[a * (D * U) + m * U + c] = acc[m];
+}
 
 template <bool T>
 __global__ void __launch_bounds__(256) nq_self_conn_kernel(const float* __restrict__ x0, const float* __restrict__ x1,
@@ -629,25 +655,18 @@ __global__ void __launch_bounds__(256) nq_self_conn_kernel(const float* __restri
                                                             const float* __restrict__ w2, int64_t n,
                                                             float* __restrict__ o0, float* __restrict__ o1,
                                                             float* __restrict__ o2) {
-    const int64_t total = n * kXW;
+    const int64_t total = n * (128 + 64 + 32);
     for (int64_t t = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; t < total; t += int64_t(gridDim.x) * blockDim.x) {
-        const float *x, *w;
-        float* o;
-        int64_t q, a;
-        int U;
         if (t < n * 128) {
-            q = t, a = t >> 7, U = 128, x = x0, w = w0, o = o0;
-        } else if (t < n * 320) {
-            q = t - n * 128, a = q / 192, U = 64, x = x1, w = w1, o = o1;
+            const int64_t a = t >> 7;
+            sc_plane<128, 1, T>(x0, w0 + elem[a] * (128 * 128), a, int(t & 127), o0);
+        } else if (t < n * 192) {
+            const int64_t q = t - n * 128, a = q >> 6;
+            sc_plane<64, 3, T>(x1, w1 + elem[a] * (64 * 64), a, int(q & 63), o1);
         } else {
-            q = t - n * 320, a = q / 160, U = 32, x = x2, w = w2, o = o2;
+            const int64_t q = t - n * 192, a = q >> 5;
+            sc_plane<32, 5, T>(x2, w2 + elem[a] * (32 * 32), a, int(q & 31), o2);
         }
-        const int c = int(q & (U - 1));
-        const float* xr = x + (q - c);  // the row (n, m) of the plane
-        const float* wz = w + elem[a] * int64_t(U) * U;
-        float acc = 0.f;
-        for (int u = 0; u < U; ++u) acc = fmaf(xr[u], T ? wz[c * U + u] : wz[u * U + c], acc);
-        o[q] = acc;
     }
 }
 
@@ -805,7 +824,11 @@ fmd_status fmd_nequip_self_connection(const float* x0, const float* x1, const fl
     if (x0 == nullptr || x1 == nullptr || x2 == nullptr || elem == nullptr || w0 == nullptr || w1 == nullptr ||
         w2 == nullptr || out0 == nullptr || out1 == nullptr || out2 == nullptr)
         return FMD_ERR_INVALID_ARGUMENT;
-    const int g = grid_of(n_atoms * kXW, 256);
+    // the planes' rows are read as float4
+    if (reinterpret_cast<uintptr_t>(x0) % 16 != 0 || reinterpret_cast<uintptr_t>(x1) % 16 != 0 ||
+        reinterpret_cast<uintptr_t>(x2) % 16 != 0)
+        return FMD_ERR_INVALID_ARGUMENT;
+    const int g = grid_of(n_atoms * 224, 256);
     if (transposed)
         nq_self_conn_kernel<true><<<g, 256, 0, as_stream(stream)>>>(x0, x1, x2, elem, w0, w1, w2, n_atoms, out0, out1,
                                                                     out2);
