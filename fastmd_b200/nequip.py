@@ -230,6 +230,8 @@ class NequIPModel:
         self.w = {k: torch.as_tensor(v, dtype=torch.float32, device=self.device) for k, v in host.items()}
         # the matrices the GEMM reads as [out, in]
         self.lin = {k: v.t().contiguous() for k, v in self.w.items() if ".lin" in k}
+        # the layers' first radial layers stacked [layers * hidden, n_basis]: one GEMM for all layers
+        self.rad1_all = torch.cat([self.w[f"L{L}.rad1"] for L in range(self.config.num_layers)], 0).contiguous()
         # self-connection weights [elements, out, in] for the input gradient
         self.sc_t = {k: v.transpose(1, 2).contiguous() for k, v in self.w.items() if ".sc" in k}
         self.precision = precision
@@ -269,6 +271,8 @@ class NequIPModel:
             Y, B = _EdgeBasis.apply(pos, self, batch)
             # node features as planes [N (2l + 1), mult]; l = 1, 2 start at exact zeros
             x = [self.w["embed"][elem], None, None]
+            # the radial networks' first layers of every block in one GEMM (column views, no copies)
+            r1 = torch.split(torch.nn.functional.silu(self._linear(B, self.rad1_all)), c.radial_hidden, dim=1)
             for L in range(c.num_layers):
                 zero = lambda l: torch.zeros(N * DIM[l], MULT[l], device=self.device)  # noqa: E731
                 # a linear map of an exact zero plane is an exact zero plane: not launched
@@ -276,8 +280,7 @@ class NequIPModel:
                 sc = _SelfConnection.apply(*[x[l] if x[l] is not None else zero(l) for l in range(3)], elem,
                                            *[self.w[f"L{L}.sc{l}"] for l in range(3)],
                                            *[self.sc_t[f"L{L}.sc{l}"] for l in range(3)])
-                r = torch.nn.functional.silu(self._linear(B, self.w[f"L{L}.rad1"]))
-                r = torch.nn.functional.silu(self._linear(r, self.w[f"L{L}.rad2"]))
+                r = torch.nn.functional.silu(self._linear(r1[L], self.w[f"L{L}.rad2"]))
                 W = self._linear(r, self.w[f"L{L}.rad3"])
                 m = _Conv.apply(torch.cat([p.reshape(-1) for p in h]), Y, W.contiguous(), self, batch)
                 o = [self._linear(m[l], self.lin[f"L{L}.lin2_{l}"]) for l in range(3)]
