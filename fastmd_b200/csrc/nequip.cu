@@ -310,12 +310,11 @@ __device__ __forceinline__ void warp_couplings(int warp, const float* cg, const 
 }
 
 // the edge's weight row (240 float4) and its sender's feature row (120 float4, from the three planes)
-// staged by the block's 128 threads, all loads issued before the stores
-__device__ __forceinline__ void stage_rows_block(const ConvArgs& a, int64_t e, int64_t j, float* ws, float* xs,
-                                                 int tid) {
+// over the block's 128 threads: loaded into registers (issued one edge ahead, so that the loads fly
+// while the previous edge computes), then stored to shared memory
+__device__ __forceinline__ void load_rows_block(const ConvArgs& a, int64_t e, int64_t j, float4* v, int tid) {
     constexpr int NW = kWW / 4, NX = kXW / 4;
     const float4* wsrc = reinterpret_cast<const float4*>(a.W + e * kWW);
-    float4 v[3];
 #pragma unroll
     for (int r = 0; r < 3; ++r) {
         const int q = tid + kRecvThreads * r;
@@ -324,6 +323,10 @@ __device__ __forceinline__ void stage_rows_block(const ConvArgs& a, int64_t e, i
         else if (q < NW + NX)
             v[r] = *reinterpret_cast<const float4*>(a.x + x_planar(a.n_atoms, j, 4 * (q - NW)));
     }
+}
+
+__device__ __forceinline__ void store_rows_block(const float4* v, float* ws, float* xs, int tid) {
+    constexpr int NW = kWW / 4, NX = kXW / 4;
 #pragma unroll
     for (int r = 0; r < 3; ++r) {
         const int q = tid + kRecvThreads * r;
@@ -355,12 +358,15 @@ __global__ void __launch_bounds__(kRecvThreads) nq_conv_kernel(ConvArgs a, float
     for (int64_t i = blockIdx.x; i < a.n_atoms; i += gridDim.x) {
         __syncthreads();  // the previous receiver's messages are written out
         for (int t = tid; t < kMW; t += kRecvThreads) acc[t] = 0.f;
-        for (int64_t e = a.recv_off[i]; e < a.recv_off[i + 1]; ++e) {
-            const int64_t j = a.edge_index[2 * e + 1];
+        const int64_t e0 = a.recv_off[i], e1 = a.recv_off[i + 1];
+        float4 v[3];
+        if (e0 < e1) load_rows_block(a, e0, a.edge_index[2 * e0 + 1], v, tid);
+        for (int64_t e = e0; e < e1; ++e) {
             float y[9];
             load_y(a, e, y);
             __syncthreads();  // the previous edge's rows are consumed
-            stage_rows_block(a, e, j, ws, xs, tid);
+            store_rows_block(v, ws, xs, tid);
+            if (e + 1 < e1) load_rows_block(a, e + 1, a.edge_index[2 * (e + 1) + 1], v, tid);
             warp_couplings(warp, cg, y, aw, lane);
             __syncthreads();
             switch (warp) {
@@ -442,11 +448,12 @@ __global__ void __launch_bounds__(kRecvThreads) nq_conv_bwd_edge_kernel(ConvArgs
         __syncthreads();  // the previous receiver is done
         for (int t = tid; t < kMW; t += kRecvThreads) dm[t] = dmsg[m_planar(a.n_atoms, i, t)] * a.inv_avg;
         for (int64_t e = a.recv_off[i]; e < a.recv_off[i + 1]; ++e) {
-            const int64_t j = a.edge_index[2 * e + 1];
             float y[9];
             load_y(a, e, y);
+            float4 v[3];  // no prefetch here: its registers cost a resident block per SM
+            load_rows_block(a, e, a.edge_index[2 * e + 1], v, tid);
             __syncthreads();  // the previous edge's rows and dY partials are consumed
-            stage_rows_block(a, e, j, ws, xs, tid);
+            store_rows_block(v, ws, xs, tid);
             warp_couplings(warp, cg, y, aw, lane);
             __syncthreads();
             float dy[9];
