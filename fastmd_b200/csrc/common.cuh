@@ -18,6 +18,15 @@ fmd_status record_cuda_error(cudaError_t err);
 // Records `text (code)` for fmd_last_error() and returns `status`.
 fmd_status record_error_text(fmd_status status, const char* text, long long code);
 
+// Raises `kernel`'s dynamic shared-memory limit to `bytes` on the CURRENT device
+// when a launch there needs more than 48 KB and more than was granted on that
+// device before (max_carveout: also asks for the largest shared-memory carveout).
+// The attribute applies to the current device only, so the sizes granted are
+// kept per (device, kernel) under a lock; a size already granted on the device
+// makes no attribute call (so a launch inside a stream capture that follows an
+// eager launch of the same size makes none).
+fmd_status grant_dynamic_smem(const void* kernel, size_t bytes, bool max_carveout = false);
+
 inline fmd_status check_launch() {
     cudaError_t err = cudaGetLastError();
     return err == cudaSuccess ? FMD_OK : record_cuda_error(err);

@@ -15,6 +15,10 @@
 
 #include <stdio.h>
 
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "common.cuh"
 
 namespace fmd {
@@ -30,6 +34,24 @@ fmd_status record_cuda_error(cudaError_t err) {
 fmd_status record_error_text(fmd_status status, const char* text, long long code) {
     snprintf(g_last_error, sizeof(g_last_error), "%s (%lld)", text, code);
     return status;
+}
+
+fmd_status grant_dynamic_smem(const void* kernel, size_t bytes, bool max_carveout) {
+    if (bytes <= 48 * 1024) return FMD_OK;
+    int device = 0;
+    cudaError_t err = cudaGetDevice(&device);
+    if (err != cudaSuccess) return record_cuda_error(err);
+    static std::mutex mu;
+    static std::map<std::pair<int, const void*>, size_t> granted;
+    std::lock_guard<std::mutex> lock(mu);
+    size_t& done = granted[std::make_pair(device, kernel)];
+    if (bytes <= done) return FMD_OK;
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+    if (err == cudaSuccess && max_carveout)
+        err = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (err != cudaSuccess) return record_cuda_error(err);
+    done = bytes;
+    return FMD_OK;
 }
 
 constexpr int kMaxParts = 4;

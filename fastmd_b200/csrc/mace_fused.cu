@@ -1266,17 +1266,6 @@ __global__ void __launch_bounds__(32 * kForceWarps) forces_kernel(GraphArgs g, c
     }
 }
 
-// dynamic shared memory granted per kernel (raised once, before any capture of the same size)
-static size_t g_granted[16] = {};
-
-inline fmd_status grant(const void* kernel, size_t bytes, int slot) {
-    if (bytes <= 48 * 1024 || bytes <= g_granted[slot]) return FMD_OK;
-    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
-    if (err != cudaSuccess) return record_cuda_error(err);
-    g_granted[slot] = bytes;
-    return FMD_OK;
-}
-
 template <int C>
 fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeights& w, const FusedState& st,
                        int64_t atoms_per_system, int32_t n_systems, float* forces, double* total, int32_t stages,
@@ -1292,28 +1281,18 @@ fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeigh
     const int64_t b_tiles = (ea.n_edges + kTB - 1) / kTB;
     const int bwd_grid = int(b_tiles < int64_t(kNumSMs) * 8 ? b_tiles : int64_t(kNumSMs) * 8);
     const size_t node_smem = sizeof(NodeSmem<C>);
-    const int slot = C == 32 ? 0 : (C == 64 ? 1 : 2);
     fmd_status stt;
     const size_t fwd_smem = sizeof(EdgeFwdSmem) + sizeof(float) * kH * 4 * C;  // + the staged W4^T
-    if ((stt = grant((const void*)edge_fwd_kernel<C>, fwd_smem, 3 + 2 * slot)) != FMD_OK) return stt;
-    if ((stt = grant((const void*)edge_bwd_kernel<C>, sizeof(EdgeBwdSmem), 4 + 2 * slot)) != FMD_OK) return stt;
+    if ((stt = grant_dynamic_smem((const void*)edge_fwd_kernel<C>, fwd_smem)) != FMD_OK) return stt;
+    if ((stt = grant_dynamic_smem((const void*)edge_bwd_kernel<C>, sizeof(EdgeBwdSmem))) != FMD_OK) return stt;
     // the six node kernels (three, for 4 and 1 atoms per CTA) share one NodeSmem size: grant each once
     {
-        static size_t last_granted[3] = {};
-        if (node_smem > 48 * 1024 && node_smem > last_granted[slot]) {
-            const void* kernels[6] = {(const void*)node_fwd_kernel<C, kG>,    (const void*)node_fwd_kernel<C, 1>,
-                                      (const void*)node_last_kernel<C, kG>,   (const void*)node_last_kernel<C, 1>,
-                                      (const void*)sender_node_kernel<C, kG>, (const void*)sender_node_kernel<C, 1>};
-            for (const void* kernel : kernels) {
-                cudaError_t err =
-                    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(node_smem));
-                // the largest shared-memory carveout: two CTAs of a node kernel per SM
-                if (err == cudaSuccess)
-                    err = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-                if (err != cudaSuccess) return record_cuda_error(err);
-            }
-            last_granted[slot] = node_smem;
-        }
+        const void* kernels[6] = {(const void*)node_fwd_kernel<C, kG>,    (const void*)node_fwd_kernel<C, 1>,
+                                  (const void*)node_last_kernel<C, kG>,   (const void*)node_last_kernel<C, 1>,
+                                  (const void*)sender_node_kernel<C, kG>, (const void*)sender_node_kernel<C, 1>};
+        // the largest shared-memory carveout: two CTAs of a node kernel per SM
+        for (const void* kernel : kernels)
+            if ((stt = grant_dynamic_smem(kernel, node_smem, true)) != FMD_OK) return stt;
     }
     const int L = w.n_layers;
     const bool tc = use_radial_tc(w, st, ea.n_edges);

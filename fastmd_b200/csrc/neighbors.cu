@@ -942,18 +942,6 @@ __global__ void pad_vector_override_kernel(const int64_t* __restrict__ n_edges, 
 
 inline size_t align_up(size_t x) { return (x + 255) & ~size_t(255); }
 
-// Largest dynamic shared memory granted so far per kernel (per process; one device per process).
-// The attribute is raised only when a launch needs more, so a launch inside a CUDA-graph capture
-// that was preceded by an eager launch of the same size makes no attribute call.
-static size_t g_query_smem = 48 * 1024, g_count_smem = 48 * 1024, g_mat_smem = 48 * 1024;
-
-inline fmd_status allow_smem(const void* kernel, size_t bytes, size_t& granted) {
-    if (bytes <= granted) return FMD_OK;
-    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
-    if (err != cudaSuccess) return record_cuda_error(err);
-    granted = bytes;
-    return FMD_OK;
-}
 
 inline bool make_grid(const float* cell_host, double cutoff, Grid& g) {
     double c[9];
@@ -1079,7 +1067,7 @@ inline fmd_status run_cell_list(const float* positions, int64_t n_atoms, int32_t
     q.flags = flags;
     const size_t smem = query_smem(q.list_cap, q.off_cap);
     if (smem > 227 * 1024) return FMD_ERR_UNSUPPORTED;
-    if ((st = allow_smem(reinterpret_cast<const void*>(cell_query_kernel), smem, g_query_smem)) != FMD_OK) return st;
+    if ((st = grant_dynamic_smem(reinterpret_cast<const void*>(cell_query_kernel), smem)) != FMD_OK) return st;
     const int qgrid = int(cells < int64_t(kNumSMs) * 16 ? cells : int64_t(kNumSMs) * 16);
     cell_query_kernel<<<qgrid, kQueryWarps * 32, smem, s>>>(q);
     if ((st = check_launch()) != FMD_OK) return st;
@@ -1199,9 +1187,9 @@ fmd_status fmd_refilter_edges(const float* positions, const float* cell_host, in
     const size_t smem_count = (sizeof(float3) + sizeof(int3)) * size_t(n_atoms);
     const size_t smem_mat = size_t(smem);
     const int grid = n_systems * kRefCluster;  // a cluster of kRefCluster CTAs per system
-    fmd_status st0 = allow_smem(reinterpret_cast<const void*>(refilter_count_kernel), smem_count, g_count_smem);
+    fmd_status st0 = grant_dynamic_smem(reinterpret_cast<const void*>(refilter_count_kernel), smem_count);
     if (st0 != FMD_OK) return st0;
-    st0 = allow_smem(reinterpret_cast<const void*>(refilter_materialize_kernel), smem_mat, g_mat_smem);
+    st0 = grant_dynamic_smem(reinterpret_cast<const void*>(refilter_materialize_kernel), smem_mat);
     if (st0 != FMD_OK) return st0;
     refilter_count_kernel<<<grid, kRefThreads, smem_count, s>>>(a);
     fmd_status st = check_launch();

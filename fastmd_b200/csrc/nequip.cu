@@ -753,14 +753,6 @@ static fmd_status conv_args(ConvArgs& a, const float* x, const float* Y, const f
     return FMD_OK;
 }
 
-static fmd_status grant_once(const void* kernel, size_t bytes, bool& done) {
-    if (done || bytes <= 48 * 1024) return FMD_OK;
-    const cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
-    if (err != cudaSuccess) return record_cuda_error(err);
-    done = true;
-    return FMD_OK;
-}
-
 fmd_status fmd_nequip_conv(const float* x, const float* Y, const float* W, const float* cg,
                            const int32_t* edge_index, const int64_t* recv_off, int64_t n_atoms, float inv_avg,
                            float* messages, void* stream) {
@@ -769,9 +761,8 @@ fmd_status fmd_nequip_conv(const float* x, const float* Y, const float* W, const
     if (st != FMD_OK) return st;
     if (n_atoms == 0) return FMD_OK;
     if (messages == nullptr) return FMD_ERR_INVALID_ARGUMENT;
-    static bool granted = false;
     const size_t smem = sizeof(float) * kFwdBlock;
-    if ((st = grant_once((const void*)nq_conv_kernel, smem, granted)) != FMD_OK) return st;
+    if ((st = grant_dynamic_smem((const void*)nq_conv_kernel, smem)) != FMD_OK) return st;
     nq_conv_kernel<<<grid_of(n_atoms, 1), kRecvThreads, smem, as_stream(stream)>>>(a, messages);
     return check_launch();
 }
@@ -787,10 +778,9 @@ fmd_status fmd_nequip_conv_bwd(const float* x, const float* Y, const float* W, c
     if (grad_messages == nullptr || grad_x == nullptr || grad_W == nullptr || grad_Y == nullptr ||
         send_off == nullptr)
         return FMD_ERR_INVALID_ARGUMENT;
-    static bool granted_e = false, granted_x = false;
     const size_t smem_e = sizeof(float) * kBwdBlock, smem_x = sizeof(float) * kBxBlock;
-    if ((st = grant_once((const void*)nq_conv_bwd_edge_kernel, smem_e, granted_e)) != FMD_OK) return st;
-    if ((st = grant_once((const void*)nq_conv_bwd_x_kernel, smem_x, granted_x)) != FMD_OK) return st;
+    if ((st = grant_dynamic_smem((const void*)nq_conv_bwd_edge_kernel, smem_e)) != FMD_OK) return st;
+    if ((st = grant_dynamic_smem((const void*)nq_conv_bwd_x_kernel, smem_x)) != FMD_OK) return st;
     const cudaStream_t s = as_stream(stream);
     nq_conv_bwd_edge_kernel<<<grid_of(n_atoms, 1), kRecvThreads, smem_e, s>>>(a, grad_messages, grad_W,
                                                                                        grad_Y);

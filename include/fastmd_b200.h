@@ -196,7 +196,9 @@ FMD_API fmd_status fmd_refilter_workspace_bytes(int64_t n_atoms, int32_t n_syste
  * FixedCapacityGraphBuilder.build(rebuild_candidates=False)
  * (fixed_capacity_builder.py:2181: _count_neighbors_kernel :98,
  * _materialize_neighbors_kernel :189, _pad_self_loops_kernel :324,
- * _sort_edges :1968). At most 8192 atoms per system. */
+ * _sort_edges :1968). A system's atoms are staged in shared memory (32 bytes
+ * per atom + 4, at most 200 KB): at most 6,399 atoms per system; larger
+ * systems return FMD_ERR_UNSUPPORTED and launch nothing. */
 FMD_API fmd_status fmd_refilter_edges(const float* positions, const float* cell_host, int64_t n_atoms,
                                       int32_t n_systems, const float* ref_positions, const int32_t* ref_wraps,
                                       const int32_t* cand_nbr, const int32_t* cand_shift,
@@ -216,6 +218,8 @@ FMD_API fmd_status fmd_refilter_edges(const float* positions, const float* cell_
  * scratch is a static 1 MiB device array held by every GPU that loads the
  * library until exit, enough for n_atoms * n_systems <= 126,976 atoms (up to
  * 4,096 systems); larger calls return FMD_ERR_WORKSPACE and launch nothing.
+ * The per-system limit of fmd_refilter_edges holds too (at most 6,399 atoms
+ * per system, else FMD_ERR_UNSUPPORTED).
  * The first call on a device looks the array's device address up (once per
  * device, with that device current): make that first call before any stream
  * capture. All calls share the array, so calls that overlap on the GPU (two

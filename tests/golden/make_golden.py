@@ -810,5 +810,7 @@ def main(reference: str, only: list[str]) -> None:
 
 
 if __name__ == "__main__":
-    # make_golden.py [reference-root] [fixture ...]: every fixture unless some are named
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference", sys.argv[2:])
+    # make_golden.py <reference-root> [fixture ...]: every fixture unless some are named
+    if len(sys.argv) < 2:
+        sys.exit("usage: make_golden.py <reference-root> [fixture ...]")
+    main(sys.argv[1], sys.argv[2:])

@@ -220,3 +220,52 @@ def test_padding_rows_equal_the_reference(cuda, tag):
         np.testing.assert_array_equal(batch.edge_vec_override.cpu().numpy(), g["pad_exact_rc_override"])
     else:
         assert batch.edge_vec_override is None
+
+
+def _refilter_call(name, n_atoms, cuda, cand_count=0):
+    """One C-ABI call of the per-step re-filter (``fmd_refilter_edges`` or its allocation-free twin) on
+    real device buffers for one system of ``n_atoms`` atoms spread over a 60 A cube: returns the status."""
+    import ctypes
+
+    from fastmd_b200._lib import lib, ptr, stream
+
+    bmax, e_cap = 16, 1024
+    gen = torch.Generator(device=cuda).manual_seed(5)
+    pos = 60.0 * torch.rand((n_atoms, 3), device=cuda, generator=gen)
+    i32 = dict(dtype=torch.int32, device=cuda)
+    bufs = dict(ref=pos.clone(), wraps=torch.zeros((n_atoms, 3), **i32),
+                nbr=torch.full((n_atoms, bmax), n_atoms, **i32), shift=torch.zeros((n_atoms, bmax, 3), **i32),
+                count=torch.full((n_atoms,), cand_count, **i32), wrapped=torch.zeros_like(pos),
+                wrap_delta=torch.zeros((n_atoms, 3), **i32), edge_index=torch.zeros((e_cap, 2), **i32),
+                edge_image=torch.zeros((e_cap, 3), device=cuda), recv_off=torch.zeros(n_atoms + 1, dtype=torch.int64,
+                                                                                      device=cuda),
+                send_off=torch.zeros(n_atoms + 1, dtype=torch.int64, device=cuda), send_perm=torch.zeros(e_cap, **i32),
+                n_edges=torch.zeros(1, dtype=torch.int64, device=cuda), maxd=torch.zeros(1, device=cuda),
+                flags=torch.zeros(1, **i32))
+    cell = (ctypes.c_float * 9)(60, 0, 0, 0, 60, 0, 0, 0, 60)
+    pad = (ctypes.c_int32 * 3)(1, 0, 0)
+    b = bufs
+    common = [ptr(pos), ctypes.cast(cell, ctypes.c_void_p), n_atoms, 1, ptr(b["ref"]), ptr(b["wraps"]),
+              ptr(b["nbr"]), ptr(b["shift"]), ptr(b["count"]), bmax, 6.0, 2.0, e_cap, ctypes.cast(pad, ctypes.c_void_p),
+              0, ptr(b["wrapped"]), ptr(b["wrap_delta"]), ptr(b["edge_index"]), ptr(b["edge_image"]),
+              ptr(b["recv_off"]), ptr(b["send_off"]), ptr(b["send_perm"]), ptr(b["n_edges"]), ptr(b["maxd"])]
+    if name == "fmd_refilter_edges":
+        nbytes = ctypes.c_size_t(0)
+        assert lib().fmd_refilter_workspace_bytes(n_atoms, 1, ctypes.byref(nbytes)) == 0
+        ws = torch.empty(max(int(nbytes.value), 1), dtype=torch.uint8, device=cuda)
+        status = lib().fmd_refilter_edges(*common, ptr(ws), ctypes.c_size_t(ws.numel()), ptr(b["flags"]),
+                                          stream(cuda))
+    else:
+        status = lib().fmd_refilter_edges_noalloc(*common, ptr(b["flags"]), stream(cuda))
+    torch.cuda.synchronize()
+    if status == 0:
+        assert int(b["n_edges"].item()) == 0 and int(b["flags"].item()) == 0  # no candidates: no edges
+    return status
+
+
+@pytest.mark.parametrize("name", ["fmd_refilter_edges", "fmd_refilter_edges_noalloc"])
+def test_refilter_per_system_atom_limit(cuda, name):
+    """A system's atoms are staged in shared memory (32 bytes each + 4, within 200 KB): 6,399 atoms run,
+    6,400 return FMD_ERR_UNSUPPORTED and launch nothing."""
+    assert _refilter_call(name, 6399, cuda) == 0
+    assert _refilter_call(name, 6400, cuda) == 3  # FMD_ERR_UNSUPPORTED

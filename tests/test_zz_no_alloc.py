@@ -98,3 +98,31 @@ def test_noalloc_refilter_rejects_sizes_beyond_the_scratch(cuda):
         one, ctypes.cast(cell, ctypes.c_void_p), 2_000, 100, one, one, one, one, one, 16, 6.0, 2.0, 1024, None,
         0, one, one, one, one, one, one, one, one, one, one, None)
     assert status == 4
+
+
+def test_refilter_on_a_second_device_after_the_first():
+    """The dynamic shared-memory limit a launch raises applies to the current device only: a re-filter of a
+    system above 2,048 atoms (beyond the default 48 KB) on device 1 after one on device 0 must raise it again
+    there, for the workspace entry point and the allocation-free one, and give the same bits on both."""
+    from fastmd_b200.graph import FixedCapacityGraphBuilder
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two CUDA devices")
+    n, box = 3000, (3000 / 0.06) ** (1.0 / 3.0)
+    pos = torch.from_numpy(np.random.default_rng(4).uniform(0.0, box, (n, 3)).astype(np.float32))
+    cell = torch.eye(3) * box
+    results = []
+    for index in (0, 1):
+        dev = torch.device(f"cuda:{index}")
+        with torch.cuda.device(dev):
+            builder = FixedCapacityGraphBuilder(cell=cell, atomic_numbers=torch.full((n,), 14), u_capacity=120_000,
+                                                atom_graph_cutoff=6.0, candidate_cutoff=6.5, device=dev)
+            p = pos.to(dev)
+            builder.refresh_candidates(p)
+            builder.build(p, rebuild_candidates=False)
+            torch.cuda.synchronize(dev)
+            assert int(builder.flags.item()) == 0
+            _compare(builder, _noalloc_build(builder, p))
+            m = int(builder.batch.n_edges.item())
+            results.append((builder.batch.edge_index[:m].cpu(), builder.batch.edge_image[:m].cpu()))
+    assert torch.equal(results[0][0], results[1][0]) and torch.equal(results[0][1], results[1][1])
