@@ -1,0 +1,446 @@
+"""The bundled MatRIS potential (energy, forces, stress) on this library's kernels.
+
+The model of fastmd/models/matris/model.py:99 (``MatRIS``, forward :293, blocks
+interaction_block.py:882, readout readout.py:16/:143) evaluated on a graph from this build's
+builders (``FixedCapacityGraphBuilder`` with a line graph, the reference's fixed-capacity
+``radius_graph_view``) or from arrays (any directed edge list with its bond pairing and triplets,
+e.g. the reference's legacy CPU graph). Weights load from a MatRIS ``state_dict`` under the
+reference's own key names (``matris_params.parameter_shapes``).
+
+Execution: every contraction runs in ``fmd_gemm_tf32x3`` (tcgen05, FP32 accuracy) with the fused
+SiLU epilogues, the first layer of every gated MLP as the decomposed indexed projection
+(``decomposed_indexed_cat{3,4}_silu_linear``: the GEMM on the source rows, the gather-add-SiLU
+epilogue on the edge rows), the gated LayerNorm (+ residual) in ``fmd_gated_ln``, the channel
+softmax attention in the paired CSR segment attention, the refinement sums in the CSR segment sum,
+the bond maps in ``fmd_pair_aggregate``, the residuals in ``fmd_residual_add``; the geometry, the
+radial and three-body bases and the force/virial reduction in ``fmd_matris_*``. The energy is
+differentiated by autograd over those kernels with respect to the bond lengths and the edge unit
+vectors only; ``fmd_matris_forces`` turns those two gradients into forces and the stress (no
+autograd through positions, no strain leaf). Everything is capturable in a CUDA graph; tensors live
+on a CUDA device (there is no CPU path).
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+from torch import Tensor
+from torch.autograd import Function
+
+from . import _lib, wide_gemm
+from ._lib import call, ptr, stream
+from .decomposed_indexed_cat_silu_linear import (_GatherAddSilu, decomposed_indexed_cat3_silu_linear,
+                                                 decomposed_indexed_cat4_silu_linear)
+from .dispatch import OpDispatcher, _attention_csr, _directed_pair_index
+from .gated_ln import fused_gated_ln, fused_gated_ln_residual
+from .matris_params import MATRIS_10M, MatRISConfig, parameter_shapes, seeded_parameters
+from .ops import csr_offsets, gather_cat, segment_csr
+
+GPA = 160.21766208  # eV/A^3 -> GPa (readout.py:226)
+_ACT_SILU_GRAD, _ACT_INPUT_SILU = 2, 16
+_PAD = 8  # basis rows padded to 8 columns (16-byte rows for the projections)
+
+
+# ----------------------------------------------------------------------------- autograd pieces
+
+
+class _Bessel(Function):
+    """(rbf_atom, rbf_line) [U, 8] of the bond lengths [U] (``fmd_matris_bessel``)."""
+
+    @staticmethod
+    def forward(ctx, bond_len, freq_atom, freq_line, consts):
+        n_basis, rc_a, rc_l, p = consts
+        U = bond_len.shape[0]
+        dev = bond_len.device
+        rbf_a = torch.empty((U, _PAD), device=dev)
+        rbf_l = torch.empty((U, _PAD), device=dev)
+        call("fmd_matris_bessel", ptr(bond_len), None, U, U, ptr(freq_atom), ptr(freq_line), n_basis, rc_a, rc_l, p,
+             ptr(rbf_a), ptr(rbf_l), _PAD, stream(dev))
+        ctx.save_for_backward(bond_len, freq_atom, freq_line)
+        ctx.consts = consts
+        return rbf_a, rbf_l
+
+    @staticmethod
+    def backward(ctx, grad_a, grad_l):
+        bond_len, freq_atom, freq_line = ctx.saved_tensors
+        n_basis, rc_a, rc_l, p = ctx.consts
+        U = bond_len.shape[0]
+        dev = bond_len.device
+        grad_a = torch.zeros((U, _PAD), device=dev) if grad_a is None else grad_a.contiguous()
+        grad_l = torch.zeros((U, _PAD), device=dev) if grad_l is None else grad_l.contiguous()
+        grad_len = torch.empty(U, device=dev)
+        call("fmd_matris_bessel_bwd", ptr(bond_len), None, U, U, ptr(freq_atom), ptr(freq_line), n_basis, rc_a, rc_l,
+             p, ptr(grad_a), ptr(grad_l), _PAD, ptr(grad_len), stream(dev))
+        return grad_len, None, None, None
+
+
+class _ThreeBody(Function):
+    """Fourier basis [T, 8] of the triplet angles from the edge unit vectors (``fmd_matris_threebody``)."""
+
+    @staticmethod
+    def forward(ctx, unit, graph, freq):
+        T, E = graph.line_graph.shape[0], unit.shape[0]
+        dev = unit.device
+        basis = torch.empty((T, _PAD), device=dev)
+        call("fmd_matris_threebody", ptr(unit), ptr(graph.line_graph), T, E, ptr(freq), freq.numel(), ptr(basis),
+             _PAD, ptr(_lib.flags_word(dev)), stream(dev))
+        ctx.save_for_backward(unit, freq)
+        ctx.graph = graph
+        return basis
+
+    @staticmethod
+    def backward(ctx, grad_basis):
+        unit, freq = ctx.saved_tensors
+        g = ctx.graph
+        T, E = g.line_graph.shape[0], unit.shape[0]
+        dev = unit.device
+        grad_cos = torch.empty(max(T, 1), device=dev)
+        grad_unit = torch.zeros((E, 3), device=dev)
+        p1, o1, p2, o2 = g.line_csr
+        call("fmd_matris_threebody_bwd", ptr(unit), ptr(g.line_graph), T, E, ptr(freq), freq.numel(),
+             ptr(grad_basis.contiguous()), _PAD, ptr(g.pair_index), g.n_bonds, ptr(p1), ptr(o1), ptr(p2), ptr(o2),
+             ptr(grad_cos), ptr(grad_unit), stream(dev))
+        return grad_unit, None, None
+
+
+class _SiluChain(Function):
+    """``L_n(silu(... silu(L_1(x))))`` of frozen linears ``L_k(x) = x W_k^T (+ b_k)`` on the tensor cores,
+    each SiLU applied to the next layer's operand (``FMD_ACT_INPUT_SILU``); the backward forms
+    ``(dY W_k) * silu'(h)`` in the GEMM epilogue (``FMD_ACT_SILU_GRAD``)."""
+
+    @staticmethod
+    def forward(ctx, x, *layers):
+        hs = []
+        h = x
+        for k in range(0, len(layers), 2):
+            w, b = layers[k], layers[k + 1]
+            h = wide_gemm._launch(h if k == 0 else hs[-1], w, False, "tf32x3", b, act=_ACT_INPUT_SILU if k else 0)
+            hs.append(h)
+        ctx.save_for_backward(*hs[:-1], *layers[0::2])
+        ctx.n = len(layers) // 2
+        return hs[-1]
+
+    @staticmethod
+    def backward(ctx, grad):
+        saved = ctx.saved_tensors
+        n = ctx.n
+        hs, ws = saved[:n - 1], saved[n - 1:]
+        g = grad.contiguous()
+        for k in range(n - 1, 0, -1):
+            g = wide_gemm._launch(g, ws[k], True, "tf32x3", c=hs[k - 1], act=_ACT_SILU_GRAD)
+        return (wide_gemm._launch(g, ws[0], True, "tf32x3"), *([None] * (2 * n)))
+
+
+def _checked(pair):
+    if pair is None:
+        raise _lib.FastMDLibraryError("MatRIS: the decomposed first-layer projection declined its inputs")
+    return pair
+
+
+def _silu_chain(x: Tensor, layers: list) -> Tensor:
+    flat = []
+    for w, b in layers:
+        flat.extend([w, b])
+    return _SiluChain.apply(x, *flat)
+
+
+# ----------------------------------------------------------------------------- graph
+
+
+class MatRISGraph:
+    """One evaluation's graph on the device: edges [E, 2] (centre, neighbour) with images, the bond pairing
+    ``d2u`` [E] / ``u2d`` [U] and triplets [T, 5], plus the CSRs and dispatcher state derived from them
+    (rebuilt per graph; capture-safe)."""
+
+    def __init__(self, positions: Tensor, cell: Tensor, species: Tensor, edge_index: Tensor, edge_image: Tensor,
+                 d2u: Tensor, u2d: Tensor, line_graph: Tensor, n_real: int, *, centre_sorted: bool):
+        _lib.require_cuda(positions, cell, species, edge_index, edge_image, d2u, u2d, line_graph)
+        dev = positions.device
+        self.device = dev
+        self.positions = positions.to(torch.float32).contiguous()
+        self.cell = cell.to(device=dev, dtype=torch.float32).reshape(3, 3).contiguous()
+        self.species = species.to(torch.int64).contiguous()
+        self.element = (self.species - 1).contiguous()  # embedding row of each atom (Z - 1)
+        self.edge_index = edge_index.to(torch.int32).contiguous()
+        self.edge_image = edge_image.to(torch.float32).contiguous()
+        self.d2u = d2u.to(torch.int32).contiguous()
+        self.u2d = u2d.to(torch.int32).contiguous()
+        self.line_graph = line_graph.to(torch.int32).reshape(-1, 5).contiguous()
+        self.n_atoms = self.positions.shape[0]
+        self.n_edges = self.edge_index.shape[0]
+        self.n_bonds = self.u2d.shape[0]
+        self.n_triplets = self.line_graph.shape[0]
+        self.n_real = int(n_real)
+        if self.n_edges != 2 * self.n_bonds:
+            raise ValueError(f"{self.n_edges} directed edges for {self.n_bonds} bonds (need E == 2U)")
+        lg = self.line_graph.to(torch.int64)
+        self.centre = self.edge_index[:, 0].to(torch.int64)
+        self.neighbour = self.edge_index[:, 1].to(torch.int64)
+        self.u2d64 = self.u2d.to(torch.int64)
+        self.t_atom, self.t_u1, self.t_u2 = lg[:, 0].contiguous(), lg[:, 1].contiguous(), lg[:, 3].contiguous()
+        self.ops = OpDispatcher(identity_target_csr=("atom",) if centre_sorted else ())
+        self.atom = {"source_index": self.neighbour, "target_index": self.centre, "num_segment": self.n_atoms,
+                     "num_undirected": self.n_bonds, "_topology_graph_kind": "atom", "_ops": self.ops}
+        if centre_sorted:
+            self.atom["_target_segment_attention_offsets"] = csr_offsets(self.centre, self.n_atoms)
+        self.line = {"source_index": self.t_u2, "target_index": self.t_u1, "num_segment": self.n_bonds,
+                     "num_undirected": self.n_bonds, "_topology_graph_kind": "line", "_ops": self.ops}
+        self.ops.prepare_segment_csr(self.atom, self.n_atoms)
+        self.ops.prepare_segment_csr(self.line, self.n_bonds)
+        self.pair_index = _directed_pair_index(self.atom, self.d2u.to(torch.int64))
+        p1, o1, _ = _attention_csr(self.line, "target", self.t_u1, self.n_bonds, False)
+        p2, o2, _ = _attention_csr(self.line, "source", self.t_u2, self.n_bonds, False)
+        self.line_csr = (p1, o1, p2, o2)
+        recv_perm, recv_off, identity = _attention_csr(self.atom, "target", self.centre, self.n_atoms, centre_sorted)
+        self.recv = (None if identity else recv_perm, recv_off)
+        self.send = _attention_csr(self.atom, "source", self.neighbour, self.n_atoms, False)[:2]
+        # a line-graph layer acts only when some triplet is centred on a real atom (interaction_block.py:1044)
+        self.real_line = (self.t_atom < self.n_real).any()
+        self.volume = float(abs(np.linalg.det(self.cell.detach().cpu().double().numpy())))
+
+    @classmethod
+    def from_arrays(cls, positions, cell, numbers, edge_index, edge_image, d2u, u2d, line_graph, *, n_real=None,
+                    device="cuda") -> "MatRISGraph":
+        """A graph from host arrays (e.g. the reference's legacy CPU graph): edges in any order."""
+        ei = np.asarray(edge_index, np.int64).reshape(-1, 2)
+        sorted_centres = bool(np.all(np.diff(ei[:, 0]) >= 0))
+        dev = torch.device(device)
+        t = lambda a, dt: torch.as_tensor(np.asarray(a), dtype=dt).to(dev)  # noqa: E731
+        n = np.asarray(positions).shape[0]
+        return cls(t(positions, torch.float32), t(cell, torch.float32), t(numbers, torch.int64),
+                   t(ei, torch.int32), t(edge_image, torch.float32), t(d2u, torch.int32), t(u2d, torch.int32),
+                   t(np.asarray(line_graph).reshape(-1, 5), torch.int32), n if n_real is None else n_real,
+                   centre_sorted=sorted_centres)
+
+    @classmethod
+    def from_batch(cls, batch) -> "MatRISGraph":
+        """The graph of a ``FixedCapacityGraphBuilder`` batch with a line graph (capacity rows included: padding
+        sits on sink atoms past ``n_real``, which the energy leaves out)."""
+        if batch.line_graph is None:
+            raise ValueError("MatRIS needs a builder with a line graph (line_graph_cutoff, t_capacity)")
+        return cls(batch.positions, batch.cell, batch.species, batch.edge_index, batch.edge_image,
+                   batch.directed2undirected, batch.undirected2directed, batch.line_graph, batch.n_real,
+                   centre_sorted=True)
+
+
+# ----------------------------------------------------------------------------- model
+
+
+class _Gated:
+    """A GatedMLP's frozen weights (functions.py:395): the first layers of core and gate stacked
+    ``[2C, K]`` and cut into ``K / C`` column blocks (one per concatenated part), the second layers,
+    their biases (added inside the gated LayerNorm) and the two LayerNorms."""
+
+    def __init__(self, p: dict, key: str, parts: int, C: int):
+        w0 = torch.cat([p[f"{key}.mlp_core.layers.0.weight"], p[f"{key}.mlp_gate.layers.0.weight"]], 0)
+        self.w0 = w0.contiguous()
+        self.parts = tuple(w0[:, i * C:(i + 1) * C].contiguous() for i in range(parts))
+        self.b0 = torch.cat([p[f"{key}.mlp_core.layers.0.bias"], p[f"{key}.mlp_gate.layers.0.bias"]]).contiguous()
+        self.w3c, self.b3c = p[f"{key}.mlp_core.layers.3.weight"], p[f"{key}.mlp_core.layers.3.bias"]
+        self.w3g, self.b3g = p[f"{key}.mlp_gate.layers.3.weight"], p[f"{key}.mlp_gate.layers.3.bias"]
+        self.ln = (p[f"{key}.core_norm.weight"], p[f"{key}.core_norm.bias"], p[f"{key}.gate_norm.weight"],
+                   p[f"{key}.gate_norm.bias"])
+
+    def __call__(self, core: Tensor, gate: Tensor, residual: Tensor | None = None, res_weight: Tensor | None = None):
+        core_x = wide_gemm.linear(core, self.w3c)
+        gate_x = wide_gemm.linear(gate, self.w3g)
+        if residual is None:
+            return fused_gated_ln(core_x, gate_x, *self.ln, 1e-5, 1e-5, core_lb=self.b3c, gate_lb=self.b3g)
+        return fused_gated_ln_residual(core_x, gate_x, *self.ln, residual, res_weight, 1e-5, 1e-5,
+                                       core_lb=self.b3c, gate_lb=self.b3g)
+
+
+class MatRISModel:
+    """MatRIS on one CUDA device with frozen weights.
+
+    ``params``: a MatRIS ``state_dict`` (reference key names; tensors or arrays), default the seeded
+    random weights of ``matris_params.seeded_parameters(config, seed)``.
+    ``energy_forces_stress(graph)`` -> (energy [1] float64, forces [n_real, 3] float32,
+    stress [3, 3] float32 GPa); ``graph`` is a ``MatRISGraph`` or a builder batch.
+    """
+
+    def __init__(self, config: MatRISConfig = MATRIS_10M, params: dict | None = None, *, seed: int = 0,
+                 device="cuda"):
+        self.config = config
+        self.device = torch.device(device)
+        _lib.require_cuda(torch.empty(0, device=self.device))
+        if params is None:
+            params = seeded_parameters(config, seed)
+        expected = {k: s for k, s, _ in parameter_shapes(config)}
+        missing = set(expected) - set(params)
+        if missing:
+            raise KeyError(f"MatRIS parameters missing: {sorted(missing)[:5]} ...")
+        p = {k: torch.as_tensor(np.asarray(params[k].detach().cpu() if isinstance(params[k], Tensor) else params[k]),
+                                dtype=torch.float32).to(self.device).contiguous() for k in expected}
+        for k, shape in expected.items():
+            if tuple(p[k].shape) != tuple(shape):
+                raise ValueError(f"{k}: shape {tuple(p[k].shape)}, expected {shape}")
+        self.params = p
+        C, R = config.node_dim, config.num_radial
+
+        def padded(w, width=_PAD):
+            out = torch.zeros((w.shape[0], width), device=self.device)
+            out[:, :w.shape[1]] = w
+            return out
+
+        # atom embedding: a per-element table (positions do not enter it)
+        table = p["atom_embedding.embedding.weight"] @ p["atom_embedding.atom_swish_layer.linear.weight"].T
+        self.atom_table = torch.nn.functional.silu(table).contiguous()
+        self.freq_atom = p["edge_embedding.pairwise_rbf_expansion.frequencies"]
+        self.freq_line = p["edge_embedding.threebody_rbf_expansion.frequencies"]
+        self.freq_angle = p["three_body_embedding.expansion.frequencies"]
+        self.bessel_consts = (R, float(config.pairwise_cutoff), float(config.three_body_cutoff),
+                              float(config.envelope_exponent))
+        self.edge_w1 = padded(p["edge_embedding.edge_linear1.weight"])
+        self.edge_w2 = p["edge_embedding.edge_linear2.weight"]
+        self.edge_ln = (p["edge_embedding.edge_init_norm.weight"], p["edge_embedding.edge_init_norm.bias"])
+        self.edge_ws = p["edge_embedding.swish_layer.linear.weight"]
+        self.angle_w = padded(p["three_body_embedding.angle_embedding.weight"])
+        self.angle_ws = p["three_body_embedding.swish_layer.linear.weight"]
+        self.blocks = []
+        for b in range(config.num_layers):
+            blk = {}
+            for graph in ("atom", "line"):
+                key = f"interaction_block.{b}.attn_block_{graph}_graph"
+                blk[f"attn_{graph}"] = dict(
+                    edge=_Gated(p, f"{key}.edge_nonlinear_update", 3, C),
+                    node=_Gated(p, f"{key}.node_nonlinear_update", 3, C),
+                    logits=torch.cat([p[f"{key}.source_weight_linear.weight"],
+                                      p[f"{key}.target_weight_linear.weight"]], 0).contiguous(),
+                    node_res=p[f"{key}.node_res_weight"].reshape(-1), edge_res=p[f"{key}.edge_res_weight"].reshape(-1))
+                key = f"interaction_block.{b}.refine_block_{graph}_graph"
+                blk[f"refine_{graph}"] = dict(
+                    edge=_Gated(p, f"{key}.edge_nonlinear_update", 3 if graph == "atom" else 4, C),
+                    node_ffn=[(p[f"{key}.node_FFN.layers.0.weight"], None), (p[f"{key}.node_FFN.layers.3.weight"], None)],
+                    edge_ffn=[(p[f"{key}.edge_FFN.layers.0.weight"], None), (p[f"{key}.edge_FFN.layers.3.weight"], None)],
+                    envelope=padded(p[f"{key}.learnable_envelope.weight"]),
+                    node_res=p[f"{key}.node_res_weight"].reshape(-1), edge_res=p[f"{key}.edge_res_weight"].reshape(-1))
+            self.blocks.append(blk)
+        self.readout_ln = (p["readout_norm.weight"], p["readout_norm.bias"])
+        widths = [C, *config.energy_hidden, 1]
+        head = []
+        for i in range(len(widths) - 1):
+            w, bias = p[f"energy_head.energy_head.layers.{3 * i}.weight"], p[f"energy_head.energy_head.layers.{3 * i}.bias"]
+            if i == len(widths) - 2:  # the 1-wide output padded to 4 columns (16-byte rows)
+                w4 = torch.zeros((4, w.shape[1]), device=self.device)
+                w4[:1] = w
+                b4 = torch.zeros(4, device=self.device)
+                b4[:1] = bias
+                w, bias = w4, b4
+            head.append((w.contiguous(), bias.contiguous()))
+        self.head = head
+
+    # ------------------------------------------------------------------ layers
+
+    def _attention(self, layer: dict, nodes: Tensor, edges: Tensor, g: MatRISGraph, graph: dict, kind: str):
+        """Graph_Attention_Layer (interaction_block.py:291-481): returns (nodes', edges')."""
+        ops = graph["_ops"]
+        target, source, n_nodes = graph["target_index"], graph["source_index"], graph["num_segment"]
+        rows = ops.pair_expand(edges, g.d2u, graph) if kind == "atom" else edges
+        gm = layer["edge"]
+        core, gate = _checked(decomposed_indexed_cat3_silu_linear(rows, nodes, target, source, gm.parts, gm.b0))
+        msg = gm(core, gate)
+        logits = wide_gemm.linear(rows, layer["logits"])
+        C = edges.shape[1]
+        att_s, att_t = ops.segment_attention(logits[:, :C], msg, source, logits[:, C:], msg, target, n_nodes, graph)
+        nm = layer["node"]
+        pre = wide_gemm.linear(gather_cat([(nodes, None), (att_t, None), (att_s, None)]), nm.w0)
+        n_core, n_gate = _GatherAddSilu.apply(pre, nm.b0, 0)
+        new_nodes = nm(n_core, n_gate, nodes, layer["node_res"])
+        m = ops.pair_average(msg, g.d2u, graph) if kind == "atom" else msg
+        return new_nodes, ops.residual(m, edges, layer["edge_res"])
+
+    def _refine_atom(self, layer: dict, nodes: Tensor, bonds: Tensor, rbf_atom: Tensor, g: MatRISGraph,
+                     edge_update: bool):
+        """Refinement on the atom graph (interaction_block.py:580-848)."""
+        ops, graph = g.ops, g.atom
+        rows = ops.pair_expand(bonds, g.d2u, graph)
+        env = ops.pair_expand(wide_gemm.linear(rbf_atom, layer["envelope"]), g.d2u, graph)
+        gm = layer["edge"]
+        core, gate = _checked(decomposed_indexed_cat3_silu_linear(rows, nodes, g.centre, g.neighbour, gm.parts,
+                                                                  gm.b0))
+        raw = gm(core, gate)
+        red = ops.segment_sum_graph(raw, g.centre, g.n_atoms, graph, "target", weight=env)
+        new_nodes = ops.residual(_silu_chain(red, layer["node_ffn"]), nodes, layer["node_res"])
+        if not edge_update:
+            return new_nodes, bonds
+        delta = ops.pair_average(_silu_chain(raw, layer["edge_ffn"]), g.d2u, graph)
+        return new_nodes, ops.residual(delta, bonds, layer["edge_res"])
+
+    def _refine_line(self, layer: dict, bonds: Tensor, trips: Tensor, atoms: Tensor, rbf_line: Tensor,
+                     g: MatRISGraph, edge_update: bool):
+        """Refinement on the line graph (interaction_block.py:580-848): bonds are its nodes."""
+        ops, graph = g.ops, g.line
+        base = wide_gemm.linear(rbf_line, layer["envelope"])
+        env = ops.gather(base, g.t_u2) * ops.gather(base, g.t_u1)
+        gm = layer["edge"]
+        core, gate = _checked(decomposed_indexed_cat4_silu_linear(trips, atoms, g.t_atom, bonds, g.t_u1, g.t_u2,
+                                                                  gm.parts, gm.b0))
+        raw = gm(core, gate)
+        red = ops.segment_sum_graph(raw, g.t_u1, g.n_bonds, graph, "target", weight=env)
+        new_bonds = ops.residual(_silu_chain(red, layer["node_ffn"]), bonds, layer["node_res"])
+        if not edge_update:
+            return new_bonds, trips
+        return new_bonds, ops.residual(_silu_chain(raw, layer["edge_ffn"]), trips, layer["edge_res"])
+
+    # ------------------------------------------------------------------ evaluation
+
+    def _graph(self, graph) -> MatRISGraph:
+        return graph if isinstance(graph, MatRISGraph) else MatRISGraph.from_batch(graph)
+
+    def energy_forces_stress(self, graph, *, forces: bool = True, stress: bool = True):
+        g = self._graph(graph)
+        dev = g.device
+        s = stream(dev)
+        length = torch.empty(g.n_edges, device=dev)
+        unit = torch.empty((g.n_edges, 3), device=dev)
+        call("fmd_matris_geometry", ptr(g.positions), ptr(g.cell), ptr(g.edge_index), ptr(g.edge_image), g.n_edges,
+             g.n_atoms, ptr(length), ptr(unit), ptr(_lib.flags_word(dev)), s)
+        bond_len = length.index_select(0, g.u2d64)
+        need_grad = forces or stress
+        if need_grad:
+            bond_len.requires_grad_(True)
+            unit.requires_grad_(True)
+        with torch.set_grad_enabled(need_grad):
+            energy = self._energy(g, bond_len, unit)
+        if not need_grad:
+            return energy.detach(), None, None
+        grad_len, grad_unit = torch.autograd.grad(energy, [bond_len, unit], allow_unused=True)
+        out_forces = torch.empty((g.n_atoms, 3), device=dev)
+        rows = torch.empty((g.n_atoms, 9), dtype=torch.float64, device=dev) if stress else None
+        out_stress = torch.empty(9, device=dev) if stress else None
+        recv_perm, recv_off = g.recv
+        send_perm, send_off = g.send
+        call("fmd_matris_forces", ptr(length), ptr(unit.detach()), ptr(grad_len), ptr(grad_unit), ptr(g.d2u),
+             ptr(g.u2d), ptr(g.edge_index), g.n_edges, g.n_bonds, g.n_atoms, ptr(recv_perm), ptr(recv_off),
+             ptr(send_perm), ptr(send_off), GPA / g.volume, ptr(out_forces), ptr(rows), ptr(out_stress), None, s)
+        return (energy.detach().reshape(1), out_forces[:g.n_real],
+                out_stress.reshape(3, 3) if stress else None)
+
+    def energy(self, graph) -> Tensor:
+        return self.energy_forces_stress(graph, forces=False, stress=False)[0]
+
+    def _energy(self, g: MatRISGraph, bond_len: Tensor, unit: Tensor) -> Tensor:
+        C = self.config.node_dim
+        rbf_atom, rbf_line = _Bessel.apply(bond_len, self.freq_atom, self.freq_line, self.bessel_consts)
+        # embeddings (feature_embed.py:89-247, 373-475)
+        nodes = gather_cat([(self.atom_table, g.element)])
+        bonds = wide_gemm.linear(wide_gemm.linear(rbf_atom, self.edge_w1), self.edge_w2)
+        bonds = torch.nn.functional.layer_norm(bonds, (C,), *self.edge_ln, 1e-5)
+        bonds = torch.nn.functional.silu(wide_gemm.linear(bonds, self.edge_ws))
+        basis = _ThreeBody.apply(unit, g, self.freq_angle)
+        trips = torch.nn.functional.silu(wide_gemm.linear(wide_gemm.linear(basis, self.angle_w), self.angle_ws))
+        last = len(self.blocks) - 1
+        for b, blk in enumerate(self.blocks):
+            bonds_in = bonds
+            new_bonds, trips = self._attention(blk["attn_line"], bonds, trips, g, g.line, "line")
+            bonds = torch.where(g.real_line, new_bonds, bonds_in)
+            nodes, bonds = self._attention(blk["attn_atom"], nodes, bonds, g, g.atom, "atom")
+            new_bonds, trips = self._refine_line(blk["refine_line"], bonds, trips, nodes, rbf_line, g, b < last)
+            bonds = torch.where(g.real_line, new_bonds, bonds_in)
+            nodes, bonds = self._refine_atom(blk["refine_atom"], nodes, bonds, rbf_atom, g, b < last)
+        readout = torch.nn.functional.layer_norm(nodes, (C,), *self.readout_ln, 1e-5)
+        per_atom = _silu_chain(readout, self.head)[:, 0]
+        return per_atom[:g.n_real].double().sum()
+
+
+__all__ = ["MatRISModel", "MatRISGraph"]

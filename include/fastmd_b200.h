@@ -816,6 +816,87 @@ FMD_API fmd_status fmd_nequip_gate_bwd(const float* o0, const float* o1, const f
                                        const float* grad_x1, const float* grad_x2, int64_t n_atoms, float* grad_o0,
                                        float* grad_o1, float* grad_o2, void* stream);
 
+/* ------------------------------ MatRIS geometry, bases, forces (D1, E1) */
+
+/* Per directed edge e = (centre c, neighbour n) [E, 2] int32 with image
+ * [E, 3] float32 (lattice units): v = x[c] - (x[n] + image @ L) (image @ L
+ * summed over the lattice rows in order), length[e] = |v|, unit [E, 3] =
+ * v / |v|. `cell` is a DEVICE [3, 3] float32. An index outside [0, n_atoms)
+ * raises FMD_FLAG_INDEX_RANGE (the row reads atom 0). The edge geometry of
+ * fastmd/models/matris/processgraph.py:218-233 (process_graphs). */
+FMD_API fmd_status fmd_matris_geometry(const float* positions, const float* cell, const int32_t* edge_index,
+                                       const float* edge_image, int64_t n_edges, int64_t n_atoms, float* length,
+                                       float* unit, int32_t* flags, void* stream);
+
+/* Both Bessel bases of every bond u (length d = length[u2d[u]], or
+ * length[u] when u2d is NULL), written rbf_atom [U, ldr] (freq_atom,
+ * cutoff_atom) and rbf_line [U, ldr] (freq_line, cutoff_line), each
+ * env(d / rc) sqrt(2 / rc) sin(f d / rc) / d with the polynomial envelope of
+ * `exponent` in columns [0, n_basis) and zeros up to ldr (a padded K for the
+ * projections that follow). Replaces the two BesselExpansion calls of
+ * EdgeBasisEmbedding.forward_lengths (fastmd/models/matris/feature_embed.py:
+ * 212-247; basis_function.py:31, :139). The frequencies are DEVICE float32
+ * [n_basis]. */
+FMD_API fmd_status fmd_matris_bessel(const float* length, const int32_t* u2d, int64_t n_bonds, int64_t n_edges,
+                                     const float* freq_atom, const float* freq_line, int32_t n_basis,
+                                     float cutoff_atom, float cutoff_line, float exponent, float* rbf_atom,
+                                     float* rbf_line, int64_t ldr, void* stream);
+
+/* grad_length [U] = sum over both bases of grad_atom / grad_line [U, ldg] .
+ * d rbf / d length (frequencies frozen). The backward of fmd_matris_bessel. */
+FMD_API fmd_status fmd_matris_bessel_bwd(const float* length, const int32_t* u2d, int64_t n_bonds,
+                                         int64_t n_edges, const float* freq_atom, const float* freq_line,
+                                         int32_t n_basis, float cutoff_atom, float cutoff_line, float exponent,
+                                         const float* grad_atom, const float* grad_line, int64_t ldg,
+                                         float* grad_length, void* stream);
+
+/* Fourier basis of every triplet t = (atom, u1, e1, u2, e2) [T, 5] int32:
+ * theta = acos((unit[e1] . unit[e2]) (1 - 1e-6)), basis [T, ldb] =
+ * [2^-1/2, sin(f_k theta)..., cos(f_k theta)...] / sqrt(pi), zeros in the
+ * columns past 1 + 2 n_freq. Replaces ThreebodyEmbedding.forward_vectors + FourierExpansion
+ * (fastmd/models/matris/feature_embed.py:432-446, basis_function.py:102)
+ * and the basis part of _threebody_fourier_fwd
+ * (fastmd/models/matris/op/triton_threebody_fourier.py:48). */
+FMD_API fmd_status fmd_matris_threebody(const float* unit, const int32_t* line_graph, int64_t n_triplets,
+                                        int64_t n_edges, const float* freq, int32_t n_freq, float* basis,
+                                        int64_t ldb, int32_t* flags, void* stream);
+
+/* The backward of fmd_matris_threebody into the unit vectors, with no
+ * atomics: grad_cos [T] (scratch, written) = dE / d(unit[e1] . unit[e2]) per
+ * triplet, then for every bond u (pair_index [U, 2] int64: its two directed
+ * rows) grad_unit of both rows = the sum, in CSR order, of grad_cos[t]
+ * unit[e2] over the triplets whose first bond is u (perm1/off1, the CSR of
+ * column 1) and of grad_cos[t] unit[e1] over those whose second bond is u
+ * (perm2/off2, column 3). Every row named in pair_index is written.
+ * Replaces _threebody_fourier_bwd
+ * (fastmd/models/matris/op/triton_threebody_fourier.py:100). */
+FMD_API fmd_status fmd_matris_threebody_bwd(const float* unit, const int32_t* line_graph, int64_t n_triplets,
+                                            int64_t n_edges, const float* freq, int32_t n_freq,
+                                            const float* grad_basis, int64_t ldg, const int64_t* pair_index,
+                                            int64_t n_bonds, const int64_t* perm1, const int64_t* off1,
+                                            const int64_t* perm2, const int64_t* off2, float* grad_cos,
+                                            float* grad_unit, void* stream);
+
+/* Forces and stress of the MatRIS energy from the gradients of its two
+ * geometric leaves: grad_length [U] (bond lengths, on the bond's stored
+ * direction u2d[u]; may be NULL) and grad_unit [E, 3] (may be NULL). Per edge
+ * g_e = dE/dv_e = g_d unit + (g_u - (g_u . unit) unit) / length; forces [N, 3]
+ * = sum over the atom's neighbour edges of g_e - sum over its centre edges
+ * (recv_perm NULL: edges sorted by centre with offsets recv_off [N + 1];
+ * send_perm/send_off the CSR of the neighbour column), summed per atom in
+ * CSR order (no atomics). With virial_rows [N, 9] FP64 scratch, the per-atom
+ * virial v_e (x) g_e over the centre edges; with stress [9] and/or virial
+ * [9] (FP64), W = their sum over the atoms in a fixed order, stress =
+ * stress_scale (W + W^T) / 2 (stress_scale = 160.21766208 / volume for GPa).
+ * Replaces ForceStressHead.forward's autograd forces and strain stress
+ * (fastmd/models/matris/readout.py:200-230, processgraph.py:185-211). */
+FMD_API fmd_status fmd_matris_forces(const float* length, const float* unit, const float* grad_length,
+                                     const float* grad_unit, const int32_t* d2u, const int32_t* u2d,
+                                     const int32_t* edge_index, int64_t n_edges, int64_t n_bonds, int64_t n_atoms,
+                                     const int64_t* recv_perm, const int64_t* recv_off, const int64_t* send_perm,
+                                     const int64_t* send_off, double stress_scale, float* forces,
+                                     double* virial_rows, float* stress, double* virial, void* stream);
+
 /* -------------------------------------- Nose-Hoover chain integrator (F1/F3) */
 
 /* Flat fp64 state of R replicas of n atoms each and chain length M:

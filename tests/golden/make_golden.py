@@ -35,6 +35,9 @@ used) and runs, on CPU:
   canonical sort key (fixed_capacity_builder.py:1978-1996);
 * the radial basis ``BesselExpansion`` + ``PolynomialEnvelope``
   (fastmd/models/matris/basis_function.py:139, :31) at the MACE and MatRIS settings;
+* the bundled MatRIS-10M model itself (fastmd/models/matris/model.py:99) with seeded weights, its
+  energies, forces and stress in float32 and float64 on the config-0 perovskite over the reference's
+  legacy CPU graph (``matris_cases``; pymatgen placeholders, the graph fed by a dense search);
 * the torch backend of ``GPUNoseHooverChainNVT`` (fastmd/execution/gpu_nhc.py:709,
   ``backend="torch"``) with harmonic forces, and ``maxwell_boltzmann_momenta``
   (gpu_nhc.py:199).
@@ -67,6 +70,78 @@ def _install_stubs() -> None:
     ase.units = units
     sys.modules["ase"] = ase
     sys.modules["ase.units"] = units
+
+
+def _install_model_stubs() -> None:
+    """Placeholders for the two pymatgen modules the MatRIS model module imports at load time
+    (fastmd/models/matris/converter.py:9-10); the fixtures build the model's graph without them."""
+    for name in ("pymatgen", "pymatgen.core", "pymatgen.io", "pymatgen.io.ase"):
+        sys.modules.setdefault(name, types.ModuleType(name))
+    sys.modules["pymatgen.core"].Structure = type("Structure", (), {})
+    sys.modules["pymatgen.io.ase"].AseAtomsAdaptor = type("AseAtomsAdaptor", (), {})
+
+
+def matris_cases(torch):
+    """The reference's MatRIS-10M (fastmd/models/matris/model.py:99, ``OAM_10M`` of
+    fastmd/engine/memory_admission.py:228 with energy-head widths (256, 256)) with the seeded weights of
+    ``fastmd_b200.matris_params.seeded_parameters(seed=0)`` loaded into it, evaluated by ``forward(task="efs")``
+    (ForceStressHead autograd forces and strain stress, readout.py:200-230) in float32 and in float64, on the
+    config-0 perovskite (jitter seeds 0 and 1) over the reference's own CPU graph code (the legacy ``Graph``,
+    fastmd/models/matris/legacy_graph.py:135-334, as ``GraphConverter`` builds it, converter.py:110-154) fed
+    by a dense FP64 search within the 6 A cutoff in place of pymatgen's ``get_neighbor_list``."""
+    _install_model_stubs()
+    sys.path.insert(0, str(HERE.parents[1]))
+    from fastmd.graph.geometry import small_matmul
+    from fastmd.graph.radiusgraph import RadiusGraph
+    from fastmd.models.matris.converter import GraphConverter
+    from fastmd.models.matris.model import MatRIS
+    from fastmd_b200.matris_params import MATRIS_10M, parameter_shapes, seeded_parameters
+    from fastmd_b200.structures import perovskite
+    from oracle.neighbors import dense_pairs
+
+    params = seeded_parameters(MATRIS_10M, seed=0)
+    model = MatRIS(**MATRIS_10M.reference_kwargs())
+    state = model.state_dict()
+    assert set(state) == set(params) and all(tuple(state[k].shape) == s for k, s, _ in parameter_shapes(MATRIS_10M))
+    model.load_state_dict({k: torch.from_numpy(v) for k, v in params.items()})
+    model.eval()
+    out = {"matris_param_sum": np.array(sum(float(v.astype(np.float64).sum()) for v in params.values()))}
+    for seed in (0, 1):
+        pos, cell, numbers, _ = perovskite(seed=seed)
+        lattice = torch.tensor(cell, dtype=torch.float32)
+        frac = torch.tensor(pos @ np.linalg.inv(cell), dtype=torch.float32)
+        cart = small_matmul(frac, lattice)  # the coordinates the model sees (processgraph.py:96)
+        pairs = dense_pairs(cart.double().numpy(), cell, MATRIS_10M.pairwise_cutoff)
+        keys = sorted(pairs)
+        graph = GraphConverter._create_graph_legacy(
+            len(numbers), np.array([k[0] for k in keys]), np.array([k[1] for k in keys]),
+            np.array([k[2:] for k in keys], dtype=np.float64), np.array([pairs[k] for k in keys]))
+        atom_graph, d2u = graph.adjacency_list()
+        u2d = graph.undirected2directed()
+        line = graph.line_graph_adjacency_list(cutoff=MATRIS_10M.three_body_cutoff)
+        images = np.array([e.info["image"] for e in graph.directed_edges_list], dtype=np.float64)
+        tag = f"matris_s{seed}"
+        # the float64 evaluation's own coordinates (frac @ L in float64 of the same float32 inputs)
+        out[f"{tag}_positions64"] = small_matmul(frac.double(), lattice.double()).numpy()
+        out.update({f"{tag}_positions": cart.numpy(), f"{tag}_cell": lattice.numpy(), f"{tag}_numbers": numbers,
+                    f"{tag}_edge_index": np.asarray(atom_graph, np.int32).reshape(-1, 2),
+                    f"{tag}_edge_image": images.astype(np.float32), f"{tag}_d2u": np.asarray(d2u, np.int32),
+                    f"{tag}_u2d": np.asarray(u2d, np.int32), f"{tag}_line_graph": np.asarray(line, np.int32).reshape(-1, 5)})
+        for dtype, name in ((torch.float32, "32"), (torch.float64, "64")):
+            radius_graph = RadiusGraph(
+                graph_id=None, mp_id=None, composition=None, atomic_number=torch.tensor(numbers, dtype=torch.int32),
+                atom_frac_coord=frac.to(dtype), lattice=lattice.to(dtype),
+                neighbor_image=torch.tensor(images, dtype=dtype), atom_graph=torch.tensor(out[f"{tag}_edge_index"]),
+                atom_graph_cutoff=MATRIS_10M.pairwise_cutoff, line_graph=torch.tensor(out[f"{tag}_line_graph"]),
+                line_graph_cutoff=MATRIS_10M.three_body_cutoff, directed2undirected=torch.tensor(out[f"{tag}_d2u"]),
+                undirected2directed=torch.tensor(out[f"{tag}_u2d"]))
+            pred = model.to(dtype)([radius_graph], task="efs")
+            # "e" is per atom (is_intensive); the extensive energy is e * n (the adapter's extensive_energy)
+            out[f"{tag}_e{name}"] = np.array(float(pred["e"].double().item()) * len(numbers))
+            out[f"{tag}_f{name}"] = pred["f"][0].detach().double().numpy()
+            out[f"{tag}_s{name}"] = pred["s"][0].detach().double().numpy()
+        model.float()
+    return out
 
 
 def gather_cat_cases(torch, gc):
@@ -801,6 +876,7 @@ def main(reference: str, only: list[str]) -> None:
         "bond_graph": lambda: bond_graph_cases(torch, fcb),
         "float64": lambda: float64_cases(torch, fcb),
         "padding": lambda: padding_cases(torch, fcb),
+        "matris": lambda: matris_cases(torch),
     }
     for name, make in fixtures.items():
         if not only or name in only:
