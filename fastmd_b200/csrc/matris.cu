@@ -330,9 +330,9 @@ __global__ void forces_kernel(ForceArgs a, float* __restrict__ forces, double* _
     }
 }
 
-// stress[j][m] = scale * (W[j][m] + W[m][j]) / 2, W summed over the atoms in a fixed order in FP64
-__global__ void virial_reduce_kernel(const double* __restrict__ rows, int64_t n_atoms, double scale,
-                                     float* __restrict__ stress, double* __restrict__ virial) {
+// stress[j][m] = unit / |det L| * (W[j][m] + W[m][j]) / 2, W summed over the atoms in a fixed order in FP64
+__global__ void virial_reduce_kernel(const double* __restrict__ rows, int64_t n_atoms, const float* __restrict__ cell,
+                                     double unit, float* __restrict__ stress, double* __restrict__ virial) {
     __shared__ double part[kThreads][9];
     double acc[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
     for (int64_t i = threadIdx.x; i < n_atoms; i += blockDim.x)
@@ -348,6 +348,10 @@ __global__ void virial_reduce_kernel(const double* __restrict__ rows, int64_t n_
         __syncthreads();
     }
     if (threadIdx.x < 9) {
+        const double L[9] = {cell[0], cell[1], cell[2], cell[3], cell[4], cell[5], cell[6], cell[7], cell[8]};
+        const double det = L[0] * (L[4] * L[8] - L[5] * L[7]) - L[1] * (L[3] * L[8] - L[5] * L[6]) +
+                           L[2] * (L[3] * L[7] - L[4] * L[6]);
+        const double scale = unit / fabs(det);
         const int j = threadIdx.x / 3, m = threadIdx.x % 3;
         const double wjm = part[0][3 * j + m], wmj = part[0][3 * m + j];
         if (virial != nullptr) virial[threadIdx.x] = wjm;
@@ -458,19 +462,20 @@ fmd_status fmd_matris_forces(const float* length, const float* unit, const float
                              const float* grad_unit, const int32_t* d2u, const int32_t* u2d,
                              const int32_t* edge_index, int64_t n_edges, int64_t n_bonds, int64_t n_atoms,
                              const int64_t* recv_perm, const int64_t* recv_off, const int64_t* send_perm,
-                             const int64_t* send_off, double stress_scale, float* forces, double* virial_rows,
-                             float* stress, double* virial, void* stream) {
+                             const int64_t* send_off, const float* cell, double stress_unit, float* forces,
+                             double* virial_rows, float* stress, double* virial, void* stream) {
     if (n_edges < 0 || n_bonds < 0 || n_atoms < 1) return FMD_ERR_INVALID_ARGUMENT;
     if (length == nullptr || unit == nullptr || d2u == nullptr || u2d == nullptr || edge_index == nullptr ||
         recv_off == nullptr || send_perm == nullptr || send_off == nullptr || forces == nullptr)
         return FMD_ERR_INVALID_ARGUMENT;
-    if ((stress != nullptr || virial != nullptr) && virial_rows == nullptr) return FMD_ERR_INVALID_ARGUMENT;
+    if ((stress != nullptr || virial != nullptr) && (virial_rows == nullptr || cell == nullptr))
+        return FMD_ERR_INVALID_ARGUMENT;
     const cudaStream_t s = as_stream(stream);
     const ForceArgs a{length, unit, grad_length, grad_unit, d2u, u2d, edge_index, n_edges, n_bonds, n_atoms,
                       recv_perm, recv_off, send_perm, send_off};
     forces_kernel<<<grid_for(n_atoms * 32, kThreads), kThreads, 0, s>>>(a, forces, virial_rows);
     fmd_status st = check_launch();
     if (st != FMD_OK || (stress == nullptr && virial == nullptr)) return st;
-    virial_reduce_kernel<<<1, kThreads, 0, s>>>(virial_rows, n_atoms, stress_scale, stress, virial);
+    virial_reduce_kernel<<<1, kThreads, 0, s>>>(virial_rows, n_atoms, cell, stress_unit, stress, virial);
     return check_launch();
 }

@@ -33,7 +33,7 @@ from .decomposed_indexed_cat_silu_linear import (_GatherAddSilu, decomposed_inde
 from .dispatch import OpDispatcher, _attention_csr, _directed_pair_index
 from .gated_ln import fused_gated_ln, fused_gated_ln_residual
 from .matris_params import MATRIS_10M, MatRISConfig, parameter_shapes, seeded_parameters
-from .ops import csr_offsets, gather_cat, segment_csr
+from .ops import csr_offsets, csr_scope, gather_cat
 
 GPA = 160.21766208  # eV/A^3 -> GPa (readout.py:226)
 _ACT_SILU_GRAD, _ACT_INPUT_SILU = 2, 16
@@ -102,21 +102,46 @@ class _ThreeBody(Function):
         return grad_unit, None, None
 
 
+def _gemm_f32(a: Tensor, w: Tensor, transposed: bool, bias=None, a_pre=None, act: int = 0, y_pre=None) -> Tensor:
+    """IEEE FP32 ``a' @ B (+ bias)`` on the CUDA cores (``fmd_gemm_f32``): ``B = w^T`` (or ``w`` when
+    ``transposed``), ``a' = a * silu'(a_pre)`` when ``a_pre`` is given, SiLU output with ``act = 1`` (the
+    pre-activation into ``y_pre``)."""
+    m, k = a.shape
+    n = w.shape[1] if transposed else w.shape[0]
+    y = torch.empty((m, n), device=a.device)
+    if m:
+        call("fmd_gemm_f32", ptr(a), a.stride(0), ptr(a_pre), a_pre.stride(0) if a_pre is not None else 0, ptr(w),
+             w.stride(0), int(not transposed), ptr(bias), ptr(y), n, ptr(y_pre), n if y_pre is not None else 0, m, n,
+             k, act, 0, stream(a.device))
+    return y
+
+
 class _SiluChain(Function):
-    """``L_n(silu(... silu(L_1(x))))`` of frozen linears ``L_k(x) = x W_k^T (+ b_k)`` on the tensor cores,
-    each SiLU applied to the next layer's operand (``FMD_ACT_INPUT_SILU``); the backward forms
-    ``(dY W_k) * silu'(h)`` in the GEMM epilogue (``FMD_ACT_SILU_GRAD``)."""
+    """``L_n(silu(... silu(L_1(x))))`` of frozen linears ``L_k(x) = x W_k^T (+ b_k)``.
+
+    ``tf32x3``: on the tensor cores, each SiLU applied to the next layer's operand
+    (``FMD_ACT_INPUT_SILU``), the backward forming ``(dY W_k) * silu'(h)`` in the GEMM epilogue
+    (``FMD_ACT_SILU_GRAD``). ``ieee``: on the CUDA cores, each hidden layer writing its SiLU output and
+    its pre-activation, the backward multiplying the next operand by ``silu'(h)`` as it loads it."""
 
     @staticmethod
-    def forward(ctx, x, *layers):
+    def forward(ctx, x, precision, *layers):
+        n = len(layers) // 2
         hs = []
         h = x
-        for k in range(0, len(layers), 2):
-            w, b = layers[k], layers[k + 1]
-            h = wide_gemm._launch(h if k == 0 else hs[-1], w, False, "tf32x3", b, act=_ACT_INPUT_SILU if k else 0)
-            hs.append(h)
+        for k in range(n):
+            w, b = layers[2 * k], layers[2 * k + 1]
+            if precision == "tf32x3":
+                h = wide_gemm._launch(h if k == 0 else hs[-1], w, False, "tf32x3", b, act=_ACT_INPUT_SILU if k else 0)
+                hs.append(h)
+            elif k + 1 < n:
+                pre = torch.empty((h.shape[0], w.shape[0]), device=h.device)
+                h = _gemm_f32(h, w, False, b, act=1, y_pre=pre)
+                hs.append(pre)
+            else:
+                hs.append(_gemm_f32(h, w, False, b))
         ctx.save_for_backward(*hs[:-1], *layers[0::2])
-        ctx.n = len(layers) // 2
+        ctx.n, ctx.precision = n, precision
         return hs[-1]
 
     @staticmethod
@@ -125,9 +150,15 @@ class _SiluChain(Function):
         n = ctx.n
         hs, ws = saved[:n - 1], saved[n - 1:]
         g = grad.contiguous()
-        for k in range(n - 1, 0, -1):
-            g = wide_gemm._launch(g, ws[k], True, "tf32x3", c=hs[k - 1], act=_ACT_SILU_GRAD)
-        return (wide_gemm._launch(g, ws[0], True, "tf32x3"), *([None] * (2 * n)))
+        if ctx.precision == "tf32x3":
+            for k in range(n - 1, 0, -1):
+                g = wide_gemm._launch(g, ws[k], True, "tf32x3", c=hs[k - 1], act=_ACT_SILU_GRAD)
+            g = wide_gemm._launch(g, ws[0], True, "tf32x3")
+        else:
+            g = _gemm_f32(g, ws[n - 1], True)
+            for k in range(n - 2, -1, -1):
+                g = _gemm_f32(g, ws[k], True, a_pre=hs[k])
+        return (g, None, *([None] * (2 * n)))
 
 
 def _checked(pair):
@@ -136,11 +167,11 @@ def _checked(pair):
     return pair
 
 
-def _silu_chain(x: Tensor, layers: list) -> Tensor:
+def _silu_chain(x: Tensor, layers: list, precision: str) -> Tensor:
     flat = []
     for w, b in layers:
         flat.extend([w, b])
-    return _SiluChain.apply(x, *flat)
+    return _SiluChain.apply(x, precision, *flat)
 
 
 # ----------------------------------------------------------------------------- graph
@@ -195,7 +226,6 @@ class MatRISGraph:
         self.send = _attention_csr(self.atom, "source", self.neighbour, self.n_atoms, False)[:2]
         # a line-graph layer acts only when some triplet is centred on a real atom (interaction_block.py:1044)
         self.real_line = (self.t_atom < self.n_real).any()
-        self.volume = float(abs(np.linalg.det(self.cell.detach().cpu().double().numpy())))
 
     @classmethod
     def from_arrays(cls, positions, cell, numbers, edge_index, edge_image, d2u, u2d, line_graph, *, n_real=None,
@@ -230,7 +260,8 @@ class _Gated:
     ``[2C, K]`` and cut into ``K / C`` column blocks (one per concatenated part), the second layers,
     their biases (added inside the gated LayerNorm) and the two LayerNorms."""
 
-    def __init__(self, p: dict, key: str, parts: int, C: int):
+    def __init__(self, p: dict, key: str, parts: int, C: int, precision: str):
+        self.precision = precision
         w0 = torch.cat([p[f"{key}.mlp_core.layers.0.weight"], p[f"{key}.mlp_gate.layers.0.weight"]], 0)
         self.w0 = w0.contiguous()
         self.parts = tuple(w0[:, i * C:(i + 1) * C].contiguous() for i in range(parts))
@@ -241,8 +272,8 @@ class _Gated:
                    p[f"{key}.gate_norm.bias"])
 
     def __call__(self, core: Tensor, gate: Tensor, residual: Tensor | None = None, res_weight: Tensor | None = None):
-        core_x = wide_gemm.linear(core, self.w3c)
-        gate_x = wide_gemm.linear(gate, self.w3g)
+        core_x = wide_gemm.linear(core, self.w3c, precision=self.precision)
+        gate_x = wide_gemm.linear(gate, self.w3g, precision=self.precision)
         if residual is None:
             return fused_gated_ln(core_x, gate_x, *self.ln, 1e-5, 1e-5, core_lb=self.b3c, gate_lb=self.b3g)
         return fused_gated_ln_residual(core_x, gate_x, *self.ln, residual, res_weight, 1e-5, 1e-5,
@@ -259,8 +290,11 @@ class MatRISModel:
     """
 
     def __init__(self, config: MatRISConfig = MATRIS_10M, params: dict | None = None, *, seed: int = 0,
-                 device="cuda"):
+                 device="cuda", precision: str = "tf32x3"):
+        if precision not in wide_gemm.PRECISIONS:
+            raise ValueError(f"precision must be one of {wide_gemm.PRECISIONS}, got {precision!r}")
         self.config = config
+        self.precision = precision
         self.device = torch.device(device)
         _lib.require_cuda(torch.empty(0, device=self.device))
         if params is None:
@@ -302,14 +336,14 @@ class MatRISModel:
             for graph in ("atom", "line"):
                 key = f"interaction_block.{b}.attn_block_{graph}_graph"
                 blk[f"attn_{graph}"] = dict(
-                    edge=_Gated(p, f"{key}.edge_nonlinear_update", 3, C),
-                    node=_Gated(p, f"{key}.node_nonlinear_update", 3, C),
+                    edge=_Gated(p, f"{key}.edge_nonlinear_update", 3, C, precision),
+                    node=_Gated(p, f"{key}.node_nonlinear_update", 3, C, precision),
                     logits=torch.cat([p[f"{key}.source_weight_linear.weight"],
                                       p[f"{key}.target_weight_linear.weight"]], 0).contiguous(),
                     node_res=p[f"{key}.node_res_weight"].reshape(-1), edge_res=p[f"{key}.edge_res_weight"].reshape(-1))
                 key = f"interaction_block.{b}.refine_block_{graph}_graph"
                 blk[f"refine_{graph}"] = dict(
-                    edge=_Gated(p, f"{key}.edge_nonlinear_update", 3 if graph == "atom" else 4, C),
+                    edge=_Gated(p, f"{key}.edge_nonlinear_update", 3 if graph == "atom" else 4, C, precision),
                     node_ffn=[(p[f"{key}.node_FFN.layers.0.weight"], None), (p[f"{key}.node_FFN.layers.3.weight"], None)],
                     edge_ffn=[(p[f"{key}.edge_FFN.layers.0.weight"], None), (p[f"{key}.edge_FFN.layers.3.weight"], None)],
                     envelope=padded(p[f"{key}.learnable_envelope.weight"]),
@@ -337,13 +371,15 @@ class MatRISModel:
         target, source, n_nodes = graph["target_index"], graph["source_index"], graph["num_segment"]
         rows = ops.pair_expand(edges, g.d2u, graph) if kind == "atom" else edges
         gm = layer["edge"]
-        core, gate = _checked(decomposed_indexed_cat3_silu_linear(rows, nodes, target, source, gm.parts, gm.b0))
+        core, gate = _checked(decomposed_indexed_cat3_silu_linear(rows, nodes, target, source, gm.parts, gm.b0,
+                                                                  precision=self.precision))
         msg = gm(core, gate)
-        logits = wide_gemm.linear(rows, layer["logits"])
+        logits = wide_gemm.linear(rows, layer["logits"], precision=self.precision)
         C = edges.shape[1]
         att_s, att_t = ops.segment_attention(logits[:, :C], msg, source, logits[:, C:], msg, target, n_nodes, graph)
         nm = layer["node"]
-        pre = wide_gemm.linear(gather_cat([(nodes, None), (att_t, None), (att_s, None)]), nm.w0)
+        pre = wide_gemm.linear(gather_cat([(nodes, None), (att_t, None), (att_s, None)]), nm.w0,
+                               precision=self.precision)
         n_core, n_gate = _GatherAddSilu.apply(pre, nm.b0, 0)
         new_nodes = nm(n_core, n_gate, nodes, layer["node_res"])
         m = ops.pair_average(msg, g.d2u, graph) if kind == "atom" else msg
@@ -354,40 +390,85 @@ class MatRISModel:
         """Refinement on the atom graph (interaction_block.py:580-848)."""
         ops, graph = g.ops, g.atom
         rows = ops.pair_expand(bonds, g.d2u, graph)
-        env = ops.pair_expand(wide_gemm.linear(rbf_atom, layer["envelope"]), g.d2u, graph)
+        env = ops.pair_expand(wide_gemm.linear(rbf_atom, layer["envelope"], precision=self.precision), g.d2u,
+                              graph)
         gm = layer["edge"]
         core, gate = _checked(decomposed_indexed_cat3_silu_linear(rows, nodes, g.centre, g.neighbour, gm.parts,
-                                                                  gm.b0))
+                                                                  gm.b0, precision=self.precision))
         raw = gm(core, gate)
         red = ops.segment_sum_graph(raw, g.centre, g.n_atoms, graph, "target", weight=env)
-        new_nodes = ops.residual(_silu_chain(red, layer["node_ffn"]), nodes, layer["node_res"])
+        new_nodes = ops.residual(_silu_chain(red, layer["node_ffn"], self.precision), nodes, layer["node_res"])
         if not edge_update:
             return new_nodes, bonds
-        delta = ops.pair_average(_silu_chain(raw, layer["edge_ffn"]), g.d2u, graph)
+        delta = ops.pair_average(_silu_chain(raw, layer["edge_ffn"], self.precision), g.d2u, graph)
         return new_nodes, ops.residual(delta, bonds, layer["edge_res"])
 
     def _refine_line(self, layer: dict, bonds: Tensor, trips: Tensor, atoms: Tensor, rbf_line: Tensor,
                      g: MatRISGraph, edge_update: bool):
         """Refinement on the line graph (interaction_block.py:580-848): bonds are its nodes."""
         ops, graph = g.ops, g.line
-        base = wide_gemm.linear(rbf_line, layer["envelope"])
+        base = wide_gemm.linear(rbf_line, layer["envelope"], precision=self.precision)
         env = ops.gather(base, g.t_u2) * ops.gather(base, g.t_u1)
         gm = layer["edge"]
         core, gate = _checked(decomposed_indexed_cat4_silu_linear(trips, atoms, g.t_atom, bonds, g.t_u1, g.t_u2,
-                                                                  gm.parts, gm.b0))
+                                                                  gm.parts, gm.b0,
+                                                                  precision=self.precision))
         raw = gm(core, gate)
         red = ops.segment_sum_graph(raw, g.t_u1, g.n_bonds, graph, "target", weight=env)
-        new_bonds = ops.residual(_silu_chain(red, layer["node_ffn"]), bonds, layer["node_res"])
+        new_bonds = ops.residual(_silu_chain(red, layer["node_ffn"], self.precision), bonds, layer["node_res"])
         if not edge_update:
             return new_bonds, trips
-        return new_bonds, ops.residual(_silu_chain(raw, layer["edge_ffn"]), trips, layer["edge_res"])
+        return new_bonds, ops.residual(_silu_chain(raw, layer["edge_ffn"], self.precision), trips, layer["edge_res"])
 
     # ------------------------------------------------------------------ evaluation
 
     def _graph(self, graph) -> MatRISGraph:
         return graph if isinstance(graph, MatRISGraph) else MatRISGraph.from_batch(graph)
 
-    def energy_forces_stress(self, graph, *, forces: bool = True, stress: bool = True):
+    # ------------------------------------------------------------------ the MD drivers' model interface
+
+    @property
+    def cutoff(self) -> float:
+        """The atom-graph cutoff (A)."""
+        return float(self.config.pairwise_cutoff)
+
+    def builder_options(self, positions, cell, n_atoms: int, replicas: int = 1) -> dict:
+        """``FixedCapacityGraphBuilder`` arguments for this model: the line graph within the three-body cutoff,
+        sink padding with 4 sink atoms per replica, and capacities from one system's ragged graph at
+        ``positions`` (pairs x 1.08 rounded up to 32, triplets x 1.15 rounded up to 256; times the replica
+        count). One host read (set-up only)."""
+        from .graph import neighbor_list
+
+        pos = torch.as_tensor(np.asarray(positions)[:n_atoms], dtype=torch.float32).to(self.device)
+        centre, _, _, dist = neighbor_list(pos, torch.as_tensor(np.asarray(cell), dtype=torch.float32), self.cutoff)
+        centre, dist = centre.cpu().numpy(), dist.cpu().numpy()
+        pairs = (centre.shape[0] + 1) // 2
+        short = np.bincount(centre[dist < np.float32(self.config.three_body_cutoff)], minlength=n_atoms)
+        triplets = int((short * (short - 1)).sum())
+        u_cap = int(np.ceil(max(pairs * 1.08, pairs + 32) / 32.0)) * 32
+        t_cap = int(np.ceil(max(triplets * 1.15, triplets + 256) / 256.0)) * 256
+        return dict(u_capacity=u_cap * replicas, t_capacity=t_cap * replicas, n_dummy=4 * replicas,
+                    line_graph_cutoff=float(self.config.three_body_cutoff))
+
+    def prepare(self, batch) -> None:
+        """Nothing to prepare: the graph-derived state is rebuilt inside every evaluation."""
+
+    def energy_forces(self, batch, n_systems: int = 1):
+        """(energies [n_systems] float64, forces [n_real, 3] float32) of a builder batch whose real atoms are
+        ``n_systems`` equal-sized systems (a replica union)."""
+        energy, forces, _ = self.energy_forces_stress(batch, stress=False, n_systems=n_systems)
+        return energy, forces
+
+    energy_forces_fused = energy_forces
+
+    def energy_forces_stress(self, graph, *, forces: bool = True, stress: bool = True, n_systems: int = 1):
+        """(energies [n_systems] float64, forces [n_real, 3] float32, stress [3, 3] float32 GPa of the whole
+        graph) of ``graph``; forces and stress are None when not asked for. Each index tensor of the graph is
+        sorted into its CSR once per call (``ops.csr_scope``)."""
+        with csr_scope():
+            return self._evaluate(graph, forces, stress, int(n_systems))
+
+    def _evaluate(self, graph, forces: bool, stress: bool, n_systems: int):
         g = self._graph(graph)
         dev = g.device
         s = stream(dev)
@@ -401,10 +482,10 @@ class MatRISModel:
             bond_len.requires_grad_(True)
             unit.requires_grad_(True)
         with torch.set_grad_enabled(need_grad):
-            energy = self._energy(g, bond_len, unit)
+            energy = self._energy(g, bond_len, unit, n_systems)
         if not need_grad:
             return energy.detach(), None, None
-        grad_len, grad_unit = torch.autograd.grad(energy, [bond_len, unit], allow_unused=True)
+        grad_len, grad_unit = torch.autograd.grad(energy.sum(), [bond_len, unit], allow_unused=True)
         out_forces = torch.empty((g.n_atoms, 3), device=dev)
         rows = torch.empty((g.n_atoms, 9), dtype=torch.float64, device=dev) if stress else None
         out_stress = torch.empty(9, device=dev) if stress else None
@@ -412,23 +493,26 @@ class MatRISModel:
         send_perm, send_off = g.send
         call("fmd_matris_forces", ptr(length), ptr(unit.detach()), ptr(grad_len), ptr(grad_unit), ptr(g.d2u),
              ptr(g.u2d), ptr(g.edge_index), g.n_edges, g.n_bonds, g.n_atoms, ptr(recv_perm), ptr(recv_off),
-             ptr(send_perm), ptr(send_off), GPA / g.volume, ptr(out_forces), ptr(rows), ptr(out_stress), None, s)
-        return (energy.detach().reshape(1), out_forces[:g.n_real],
+             ptr(send_perm), ptr(send_off), ptr(g.cell), GPA, ptr(out_forces), ptr(rows), ptr(out_stress), None, s)
+        return (energy.detach(), out_forces[:g.n_real] if forces else None,
                 out_stress.reshape(3, 3) if stress else None)
 
     def energy(self, graph) -> Tensor:
         return self.energy_forces_stress(graph, forces=False, stress=False)[0]
 
-    def _energy(self, g: MatRISGraph, bond_len: Tensor, unit: Tensor) -> Tensor:
+    def _energy(self, g: MatRISGraph, bond_len: Tensor, unit: Tensor, n_systems: int) -> Tensor:
         C = self.config.node_dim
         rbf_atom, rbf_line = _Bessel.apply(bond_len, self.freq_atom, self.freq_line, self.bessel_consts)
         # embeddings (feature_embed.py:89-247, 373-475)
         nodes = gather_cat([(self.atom_table, g.element)])
-        bonds = wide_gemm.linear(wide_gemm.linear(rbf_atom, self.edge_w1), self.edge_w2)
+        prec = self.precision
+        bonds = wide_gemm.linear(wide_gemm.linear(rbf_atom, self.edge_w1, precision=prec), self.edge_w2,
+                                 precision=prec)
         bonds = torch.nn.functional.layer_norm(bonds, (C,), *self.edge_ln, 1e-5)
-        bonds = torch.nn.functional.silu(wide_gemm.linear(bonds, self.edge_ws))
+        bonds = torch.nn.functional.silu(wide_gemm.linear(bonds, self.edge_ws, precision=self.precision))
         basis = _ThreeBody.apply(unit, g, self.freq_angle)
-        trips = torch.nn.functional.silu(wide_gemm.linear(wide_gemm.linear(basis, self.angle_w), self.angle_ws))
+        trips = wide_gemm.linear(wide_gemm.linear(basis, self.angle_w, precision=prec), self.angle_ws, precision=prec)
+        trips = torch.nn.functional.silu(trips)
         last = len(self.blocks) - 1
         for b, blk in enumerate(self.blocks):
             bonds_in = bonds
@@ -439,8 +523,10 @@ class MatRISModel:
             bonds = torch.where(g.real_line, new_bonds, bonds_in)
             nodes, bonds = self._refine_atom(blk["refine_atom"], nodes, bonds, rbf_atom, g, b < last)
         readout = torch.nn.functional.layer_norm(nodes, (C,), *self.readout_ln, 1e-5)
-        per_atom = _silu_chain(readout, self.head)[:, 0]
-        return per_atom[:g.n_real].double().sum()
+        per_atom = _silu_chain(readout, self.head, self.precision)[:, 0]
+        if g.n_real % n_systems:
+            raise ValueError(f"{g.n_real} real atoms do not split into {n_systems} equal systems")
+        return per_atom[:g.n_real].double().reshape(n_systems, -1).sum(1)
 
 
 __all__ = ["MatRISModel", "MatRISGraph"]

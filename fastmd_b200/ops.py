@@ -19,7 +19,9 @@ CPU path.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
+import threading
 
 import torch
 from torch import Tensor
@@ -50,11 +52,41 @@ def _index(index: Tensor) -> Tensor:
 # ----------------------------------------------------------------------------- CSR metadata
 
 
+_CSR_SCOPES = threading.local()
+
+
+@contextlib.contextmanager
+def csr_scope():
+    """Within the scope, ``segment_csr`` of the same index tensor (and segment count) is built once: a model
+    evaluation whose layers gather, scatter and segment-reduce over the same few index tensors (forward and
+    backward) sorts each index once. Entries hold their index tensor, so a key cannot be reused by another
+    tensor in the scope; the cache dies with the scope. The indices must not change inside the scope."""
+    stack = getattr(_CSR_SCOPES, "stack", None)
+    if stack is None:
+        stack = _CSR_SCOPES.stack = []
+    stack.append({})
+    try:
+        yield
+    finally:
+        stack.pop()
+
+
 def segment_csr(segment: Tensor, num_segment: int) -> tuple[Tensor, Tensor]:
     """``(perm, off)``: the rows grouped by segment (ascending row order inside a
     run, a stable sort) and the int64 run offsets ``[num_segment + 1]``.
     Replaces ``segment_attention_csr_metadata`` (triton_segment_attention.py:824)."""
     _lib.require_cuda(segment)
+    stack = getattr(_CSR_SCOPES, "stack", None)
+    if stack:
+        key = (id(segment), segment.data_ptr(), segment.shape[0], int(num_segment))
+        hit = stack[-1].get(key)
+        if hit is None:
+            hit = stack[-1][key] = (segment, *_segment_csr(segment, num_segment))
+        return hit[1], hit[2]
+    return _segment_csr(segment, num_segment)
+
+
+def _segment_csr(segment: Tensor, num_segment: int) -> tuple[Tensor, Tensor]:
     segment = _index(segment)
     rows, num_segment = segment.shape[0], int(num_segment)
     perm = torch.empty(rows, dtype=torch.int64, device=segment.device)

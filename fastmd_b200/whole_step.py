@@ -28,8 +28,10 @@ import numpy as np
 import torch
 from torch import Tensor
 
-from fastmd_b200.graph import FLAG_CANDIDATE_OVERFLOW, FLAG_EDGE_OVERFLOW, FLAG_NONFINITE, FLAG_SKIN
-_INVALID = FLAG_SKIN | FLAG_CANDIDATE_OVERFLOW | FLAG_NONFINITE | FLAG_EDGE_OVERFLOW
+from fastmd_b200.graph import (FLAG_CANDIDATE_OVERFLOW, FLAG_EDGE_OVERFLOW, FLAG_NONFINITE, FLAG_SKIN,
+                               FLAG_TRIPLET_OVERFLOW)
+_GROW = FLAG_EDGE_OVERFLOW | FLAG_TRIPLET_OVERFLOW  # a capacity the step outgrew: a larger builder
+_INVALID = FLAG_SKIN | FLAG_CANDIDATE_OVERFLOW | FLAG_NONFINITE | _GROW
 from fastmd_b200.graph import FixedCapacityGraphBuilder, TensorGraphBuilder
 from fastmd_b200.gpu_nhc import GPUNoseHooverChainNVT, ReplicaNoseHooverChainNVT, maxwell_boltzmann_momenta
 from fastmd_b200.mace import MACEModel, element_index
@@ -45,7 +47,7 @@ class FixedCapacityOverflow(RuntimeError):
 
 
 class WholeStepGraphRunner:
-    def __init__(self, *, model: MACEModel, builder: FixedCapacityGraphBuilder, integrator, steps_per_launch: int = 1,
+    def __init__(self, *, model, builder: FixedCapacityGraphBuilder, integrator, steps_per_launch: int = 1,
                  warmup: int = 3, proactive_refresh_fraction: float = 0.25, fused: bool = True) -> None:
         if steps_per_launch <= 0:
             raise ValueError("steps_per_launch must be positive")
@@ -75,6 +77,9 @@ class WholeStepGraphRunner:
         if flags & FLAG_EDGE_OVERFLOW:
             raise FixedCapacityOverflow(f"{int(batch.n_edges.item())} edges exceed the capacity "
                                         f"{builder.e_capacity}")
+        if flags & FLAG_TRIPLET_OVERFLOW:
+            raise FixedCapacityOverflow(f"{int(builder.n_triplets.item())} triplets exceed the capacity "
+                                        f"{builder.t_capacity}")
         if flags & (FLAG_CANDIDATE_OVERFLOW | FLAG_NONFINITE):
             raise RuntimeError(f"invalid initial graph (flags {flags})")
         self._capture()
@@ -132,7 +137,7 @@ class WholeStepGraphRunner:
         self.integrator.restore()
         if flags & FLAG_NONFINITE:
             raise FloatingPointError("non-finite positions in the window")
-        if flags & FLAG_EDGE_OVERFLOW:
+        if flags & _GROW:
             self._grow()
         self.builder.refresh_candidates(self.integrator.positions32)
         self.refreshes += 1
@@ -141,7 +146,7 @@ class WholeStepGraphRunner:
         if not again & _INVALID:
             return
         self.integrator.restore()
-        if again & FLAG_EDGE_OVERFLOW:
+        if again & _GROW:
             self._grow()
             self.builder.refresh_candidates(self.integrator.positions32)
             self.graph.replay()
@@ -156,7 +161,7 @@ class WholeStepGraphRunner:
             integ.step_pre_force()
             batch, status = builder.build(integ.positions32, rebuild_candidates=True)
             flags = int(status.flags.item())
-            if flags & FLAG_EDGE_OVERFLOW:
+            if flags & _GROW:
                 self._grow()
                 batch, status = self.builder.build(integ.positions32, rebuild_candidates=True)
                 builder = self.builder
@@ -168,11 +173,19 @@ class WholeStepGraphRunner:
         self.eager_steps += self.steps_per_launch
 
     def _grow(self) -> None:
-        """A larger edge capacity (the needed edges + 10 %, pairs rounded to 32) and a recapture."""
+        """Larger capacities and a recapture: the edges (the needed edges + 10 %, pairs rounded to 32) when
+        they overflowed, the triplets of a line-graph builder (the needed + 15 %, rounded to 256) when those
+        did."""
         old = self.builder
         needed = int(old.batch.n_edges.item())
-        u = int(math.ceil(max(needed * 1.1 / 2, old.u_capacity + 32 * old.replicas) / 32.0)) * 32
-        self.builder = old.resized(u)
+        u = old.u_capacity
+        if needed > old.e_capacity:
+            u = int(math.ceil(max(needed * 1.1 / 2, old.u_capacity + 32 * old.replicas) / 32.0)) * 32
+        t = None
+        if old.n_triplets is not None and int(old.n_triplets.item()) > old.t_capacity:
+            wanted = int(old.n_triplets.item())
+            t = int(math.ceil(max(wanted * 1.15, old.t_capacity + 256 * old.replicas) / 256.0)) * 256
+        self.builder = old.resized(u, t)
         self.graph = None
         self.model.prepare(self.builder.batch)
         self.builder.refresh_candidates(self.integrator.positions32)
@@ -202,7 +215,7 @@ class GPUResidentMolecularDynamics:
     ``"whole_step"`` (windows of ``steps_per_launch`` steps as one CUDA graph), ``"model_graph"``
     or ``"eager"`` (one system; a ragged build per step)."""
 
-    def __init__(self, model: MACEModel, *, positions, cell, atomic_numbers, masses, temperature_K: float,
+    def __init__(self, model, *, positions, cell, atomic_numbers, masses, temperature_K: float,
                  timestep: float, tdamp: float, tchain: int = 3, tloop: int = 1, momenta=None, replicas: int = 1,
                  skin: float = 2.0, u_capacity: int | None = None, steps_per_launch: int = 10,
                  fused: bool = True, execution: str = "whole_step", device="cuda") -> None:
@@ -218,15 +231,24 @@ class GPUResidentMolecularDynamics:
         if momenta is None:
             momenta = np.concatenate([maxwell_boltzmann_momenta(masses, temperature_K, seed=r)
                                       for r in range(self.replicas)])
-        cutoff = model.config.r_max
-        if u_capacity is None:
-            # MACE's capacity tiers (mace.py:70, CapacityStep(32, 32, 1.02)) from the initial pair count
-            pairs = self._initial_pairs(positions[:n], cell, cutoff)
-            u_capacity = int(math.ceil(max(pairs * 1.08, pairs + 32) / 32.0)) * 32 * self.replicas
+        line_model = hasattr(model, "builder_options")  # a model with a bond graph (MatRIS)
+        if line_model and execution != "whole_step":
+            raise ValueError("a line-graph model (MatRIS) runs execution='whole_step' here")
+        cutoff = model.cutoff if line_model else model.config.r_max
+        if line_model:
+            options = model.builder_options(positions, cell, n, self.replicas)
+            if u_capacity is not None:
+                options["u_capacity"] = u_capacity
+        else:
+            if u_capacity is None:
+                # MACE's capacity tiers (mace.py:70, CapacityStep(32, 32, 1.02)) from the initial pair count
+                pairs = self._initial_pairs(positions[:n], cell, cutoff)
+                u_capacity = int(math.ceil(max(pairs * 1.08, pairs + 32) / 32.0)) * 32 * self.replicas
+            options = dict(u_capacity=u_capacity)
         self.builder = FixedCapacityGraphBuilder(
             cell=torch.as_tensor(np.asarray(cell), dtype=torch.float32), atomic_numbers=torch.as_tensor(atomic_numbers),
-            u_capacity=u_capacity, atom_graph_cutoff=cutoff, candidate_cutoff=cutoff + skin, device=self.device,
-            replicas=self.replicas)
+            atom_graph_cutoff=cutoff, candidate_cutoff=cutoff + skin, device=self.device, replicas=self.replicas,
+            **options)
         kw = dict(temperature_K=temperature_K, timestep=timestep, tdamp=tdamp, tchain=tchain, tloop=tloop,
                   force_dtype=torch.float32, device=self.device)
         if self.replicas == 1:
@@ -294,7 +316,9 @@ class GPUResidentMolecularDynamics:
         if self.replicas != 1:
             raise ValueError("a restart file holds one system")
         integ = self.integrator
-        e0 = np.asarray(self.model.weights_host["e0"], np.float64)[element_index(self.numbers)]
+        weights = getattr(self.model, "weights_host", None)  # MACE's per-element reference energies; MatRIS has none
+        e0 = (np.asarray(weights["e0"], np.float64)[element_index(self.numbers)] if weights is not None
+              else np.zeros(self.n_atoms))
         params = {"ensemble": "nvt_nhc", "tchain": integ.tchain, "tloop": integ.tloop, "timestep": integ.dt,
                   "tdamp": integ.tdamp, "execution": self.execution, **(parameters or {})}
         return RestartData(

@@ -887,15 +887,17 @@ FMD_API fmd_status fmd_matris_threebody_bwd(const float* unit, const int32_t* li
  * CSR order (no atomics). With virial_rows [N, 9] FP64 scratch, the per-atom
  * virial v_e (x) g_e over the centre edges; with stress [9] and/or virial
  * [9] (FP64), W = their sum over the atoms in a fixed order, stress =
- * stress_scale (W + W^T) / 2 (stress_scale = 160.21766208 / volume for GPa).
+ * stress_unit (W + W^T) / (2 |det cell|) (`cell` a DEVICE [3, 3] float32;
+ * stress_unit = 160.21766208 for GPa).
  * Replaces ForceStressHead.forward's autograd forces and strain stress
  * (fastmd/models/matris/readout.py:200-230, processgraph.py:185-211). */
 FMD_API fmd_status fmd_matris_forces(const float* length, const float* unit, const float* grad_length,
                                      const float* grad_unit, const int32_t* d2u, const int32_t* u2d,
                                      const int32_t* edge_index, int64_t n_edges, int64_t n_bonds, int64_t n_atoms,
                                      const int64_t* recv_perm, const int64_t* recv_off, const int64_t* send_perm,
-                                     const int64_t* send_off, double stress_scale, float* forces,
-                                     double* virial_rows, float* stress, double* virial, void* stream);
+                                     const int64_t* send_off, const float* cell, double stress_unit,
+                                     float* forces, double* virial_rows, float* stress, double* virial,
+                                     void* stream);
 
 /* -------------------------------------- Nose-Hoover chain integrator (F1/F3) */
 

@@ -48,3 +48,35 @@ class OracleMD:
         f, e = self.forces(q)
         self.nhc.post_force(f, e)
         return self.nhc
+
+
+class MatRISOracleMD(OracleMD):
+    """The same CPU MD step with the FP64 MatRIS oracle (``oracle.matris``): edges of a dense FP64 search
+    within the atom cutoff, the bond pairing and triplets of ``oracle.line_graph`` (the reference's
+    ``_build_d2u`` / ``_build_line_graph``), forces by autograd."""
+
+    def __init__(self, params, config, positions, cell, numbers, masses, momenta, **kw):
+        self.params = params
+        super().__init__(None, config, positions, cell, numbers, masses, momenta, **kw)
+
+    def graph(self, positions):
+        from oracle import line_graph as olg
+
+        wrapped, _, _ = onb.wrap(np.asarray(positions, np.float32), self.cell32, inv_cell=self.inv32)
+        pairs = onb.dense_pairs(wrapped, self.cell, self.config.pairwise_cutoff)
+        keys = sorted(pairs)
+        edges = np.array([k[:2] for k in keys], np.int64).reshape(-1, 2)
+        images = np.array([k[2:] for k in keys], np.int64).reshape(-1, 3)
+        dist = np.array([pairs[k] for k in keys])
+        d2u, u2d = olg.build_d2u(edges[:, 0], edges[:, 1], images, len(wrapped), presorted=True)
+        lines = olg.build_line_graph(edges[:, 0], d2u, dist, len(wrapped), self.config.three_body_cutoff,
+                                     presorted=True)
+        return wrapped, edges, images, d2u, u2d, lines
+
+    def forces(self, positions):
+        from oracle import matris as om
+
+        wrapped, edges, images, d2u, u2d, lines = self.graph(positions)
+        energy, forces, _ = om.energy_forces_stress(self.params, self.config, wrapped.astype(np.float64), self.cell,
+                                                    self.numbers, edges, images.astype(np.float64), d2u, u2d, lines)
+        return forces.astype(np.float32), float(energy)
