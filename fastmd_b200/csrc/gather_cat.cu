@@ -157,7 +157,21 @@ __global__ void gather_rows_bwd_kernel(const float* __restrict__ gout, int64_t l
         const int64_t start = off[n], end = off[n + 1];
         if constexpr (VEC == 4) {
             float4 acc = f4_zero();
-            for (int64_t j = start + slot; j < end; j += slots) {
+            int64_t j = start + slot;
+            // four rows' loads in flight, added in row order (the same sums as one row at a time)
+            for (; j + 3 * slots < end; j += 4 * slots) {
+                int64_t r[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) r[q] = perm ? perm[j + q * slots] : j + q * slots;
+                if (col_ok) {
+                    float4 x[4];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) x[q] = ldg4(gout + r[q] * ldgo + col0 + v * 4);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) acc = f4_add(acc, x[q]);
+                }
+            }
+            for (; j < end; j += slots) {
                 const int64_t r = perm ? perm[j] : j;
                 if (col_ok) acc = f4_add(acc, ldg4(gout + r * ldgo + col0 + v * 4));
             }

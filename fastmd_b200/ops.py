@@ -52,23 +52,25 @@ def _index(index: Tensor) -> Tensor:
 # ----------------------------------------------------------------------------- CSR metadata
 
 
-_CSR_SCOPES = threading.local()
+_CSR_SCOPES: list[dict] = []  # process-wide: autograd runs a CUDA backward on its own device thread
+_CSR_LOCK = threading.Lock()
 
 
 @contextlib.contextmanager
 def csr_scope():
     """Within the scope, ``segment_csr`` of the same index tensor (and segment count) is built once: a model
     evaluation whose layers gather, scatter and segment-reduce over the same few index tensors (forward and
-    backward) sorts each index once. Entries hold their index tensor, so a key cannot be reused by another
-    tensor in the scope; the cache dies with the scope. The indices must not change inside the scope."""
-    stack = getattr(_CSR_SCOPES, "stack", None)
-    if stack is None:
-        stack = _CSR_SCOPES.stack = []
-    stack.append({})
+    backward) sorts each index once. The scope is process-wide (the backward of an evaluation runs on
+    autograd's device thread while the caller waits), so evaluations must not overlap in time. Entries hold
+    their index tensor, so a key cannot be reused by another tensor in the scope; the cache dies with the
+    scope. The indices must not change inside the scope."""
+    with _CSR_LOCK:
+        _CSR_SCOPES.append({})
     try:
         yield
     finally:
-        stack.pop()
+        with _CSR_LOCK:
+            _CSR_SCOPES.pop()
 
 
 def segment_csr(segment: Tensor, num_segment: int) -> tuple[Tensor, Tensor]:
@@ -76,12 +78,12 @@ def segment_csr(segment: Tensor, num_segment: int) -> tuple[Tensor, Tensor]:
     run, a stable sort) and the int64 run offsets ``[num_segment + 1]``.
     Replaces ``segment_attention_csr_metadata`` (triton_segment_attention.py:824)."""
     _lib.require_cuda(segment)
-    stack = getattr(_CSR_SCOPES, "stack", None)
-    if stack:
+    if _CSR_SCOPES:
+        cache = _CSR_SCOPES[-1]
         key = (id(segment), segment.data_ptr(), segment.shape[0], int(num_segment))
-        hit = stack[-1].get(key)
+        hit = cache.get(key)
         if hit is None:
-            hit = stack[-1][key] = (segment, *_segment_csr(segment, num_segment))
+            hit = cache[key] = (segment, *_segment_csr(segment, num_segment))
         return hit[1], hit[2]
     return _segment_csr(segment, num_segment)
 
