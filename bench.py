@@ -9,11 +9,17 @@ potential (128 channels, l <= 1, correlation 3, 2 interactions, 8 Bessel,
 r_max 6 A, 89 elements; random weights, seed 1; IEEE FP32), whole-step
 CUDA-graph mode. One MD step = NHC half -> exact neighbour re-filter ->
 model energy and forces -> NHC half. ``--replicas R`` runs R independent
-135-atom replicas per GPU as one disjoint-union graph (config 4 uses 64).
+135-atom replicas per GPU as one disjoint-union graph; the default 64 is
+config 4's shard (64/128/256/512 replicas on 1/2/4/8 GPUs), so ``value`` is
+config 4's whole-job atom-steps/s at every N. At N = 1 the line also carries
+``config1`` (one 135-atom replica alone: its ms/step, roofline and the three
+execution modes) and ``config0_matris`` (the same system under MatRIS-10M,
+whole_step, beside the CPU port of the reference's config-0 path).
 
 Under torchrun (N > 1) every rank integrates its own replicas (seeds
 rank*R .. rank*R+R-1), no collective on the step path; the per-replica
-(E_pot, T) are all-gathered over NCCL once per window (the thermo log).
+(E_pot, T) are all-gathered over NCCL once per window (the thermo log),
+inside each timed window.
 
 ``--impl reference``: the CPU restatement of the same path (oracle/md.py:
 dense neighbour search, FP64 model with autograd forces, NHC) timed on the
@@ -48,7 +54,9 @@ def _args():
     p.add_argument("--steps", type=int, default=2000)
     p.add_argument("--warmup", type=int, default=100)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--replicas", type=int, default=1, help="135-atom replicas per GPU")
+    p.add_argument("--replicas", type=int, default=64,
+                   help="135-atom replicas per GPU (config 4 shards 64 per GPU; 1 = config 1 alone)")
+    p.add_argument("--no-matris", action="store_true", help="skip the config-0 MatRIS-10M leg")
     p.add_argument("--steps-per-launch", type=int, default=10)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-ops", action="store_true", help="skip the config-2 op microbenchmark")
@@ -61,8 +69,11 @@ def _args():
 
 
 def _config(args, world):
-    return {"workload": "config1: 135-atom CsSnI3 3x3x3, MACE-arch 128ch L1 corr3 2 layers, NVT-NHC whole_step"
-                        + (f", {args.replicas} replicas per GPU (config 4 sharding)" if args.replicas > 1 else ""),
+    workload = ("config4: 64 x 135-atom CsSnI3 replicas per B200 as one disjoint-union graph, MACE-arch"
+                if args.replicas == 64 else
+                f"{args.replicas} x 135-atom CsSnI3 replica(s) per B200" + (" (config 1)" if args.replicas == 1 else ""))
+    return {"workload": workload + " 128ch L1 corr3 2 layers, NVT-NHC whole_step; (E_pot, T) all-gathered over "
+                                   "NCCL once per window inside the timed region",
             "atoms_per_replica": 135, "replicas_per_gpu": args.replicas, "replicas_total": args.replicas * world,
             "dt_fs": 0.25, "temperature_K": TEMPERATURE, "tchain": 3, "tdamp_fs": 25.0,
             "steps_per_launch": args.steps_per_launch, "parallelism": f"replicas x{world} (no step-path collective)",
@@ -210,25 +221,36 @@ def _ours(args):
             log.gather(md.integrator.state.energy, md.integrator.temperature())
 
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
-    for _ in range(max(1, -(-args.warmup // S))):
+    # the clock sampler runs from the first warm-up window to the end of the timed region; the warm-up
+    # lasts at least the W steps asked for and at least ~1 s of work, so the record holds samples under load
+    clocks = _Clocks(local)
+    t_warm = time.perf_counter()
+    warm_windows = 0
+    while True:
         runner.launch()
-        runner.settle()
         thermo_log()
+        runner.settle()
+        warm_windows += 1
+        done = torch.tensor([float(warm_windows * S >= args.warmup and time.perf_counter() - t_warm >= 1.0)],
+                            device=device)
+        if world > 1:  # every rank leaves the warm-up together (the same collective steps on all ranks)
+            dist.all_reduce(done, op=dist.ReduceOp.MIN)
+        if float(done[0]) > 0:
+            break
     windows = args.steps // S
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(windows)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(windows)]
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    clocks = _Clocks(local)
     t0 = time.perf_counter()
     for w in range(windows):
         flush.zero_()
         starts[w].record()
         runner.launch()
+        thermo_log()  # the window's only collective, timed with it
         ends[w].record()
         runner.settle()
-        thermo_log()
     torch.cuda.synchronize()
     wall = time.perf_counter() - t0
     if world > 1:
@@ -257,6 +279,7 @@ def _ours(args):
     t1 = time.perf_counter()
     for _ in range(e2e_windows):
         md.step_host(out["positions"], out["momenta"], out)
+        thermo_log()
     e2e_s = time.perf_counter() - t1
     e2e_ms_step = 1e3 * e2e_s / (e2e_windows * S)
     e2e_t = torch.tensor([e2e_ms_step], dtype=torch.float64, device=device)
@@ -281,6 +304,18 @@ def _ours(args):
             modes = _execution_modes(md, model, systems[0], momenta, device)
         except Exception as error:  # noqa: BLE001 - the line still reports the measured step
             modes = {"error": f"{type(error).__name__}: {error}"}
+    config1 = None
+    if rank == 0 and world == 1 and R != 1:
+        try:
+            config1 = _config1(args, model, device, flush, S)
+        except Exception as error:  # noqa: BLE001 - the line still reports the measured step
+            config1 = {"error": f"{type(error).__name__}: {error}"}
+    matris = None
+    if rank == 0 and world == 1 and not args.no_matris:
+        try:
+            matris = _config0_matris(args, device, flush)
+        except Exception as error:  # noqa: BLE001 - the line still reports the measured step
+            matris = {"error": f"{type(error).__name__}: {error}"}
     ops = None
     if rank == 0 and world == 1 and not args.no_ops:
         try:
@@ -299,16 +334,116 @@ def _ours(args):
             "warmup": max(1, -(-args.warmup // S)) * S, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32 (NHC state f64)", "data": "synthetic",
             "config": _config(args, world), "wall_s_timed": wall,
+            "wall_ms_per_step": 1e3 * wall / (windows * S),
+            "timing": "value: CUDA-event time of each window (launch + the NCCL thermo-log all-gather), max over "
+                      "ranks; wall_ms_per_step: host clock over the same windows incl. the per-window settle",
             "e2e": {"value": e2e_value, "unit": UNIT, "ms_per_step": float(e2e_t[0]), "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "path": "GPUResidentMolecularDynamics.step_host: pinned host "
                     "positions+momenta in, positions/momenta/forces/energy out, per window of "
                     f"{S} steps"},
             "gpu_launches": launches_per_window * windows, "launches_per_step": launches_per_window / S,
             "roofline": roofline, "cpu_baseline": cpu, "clocks": clk, "ops_config2": ops,
-            "execution_modes": modes,
+            "execution_modes": modes, "config1": config1, "config0_matris": matris,
             "fallbacks": md.runner.fallbacks, "candidate_refreshes": md.runner.refreshes,
             "final_temperature_K": float(thermo_now["temperature"][0]),
             "final_conserved_eV": float(thermo_now["conserved_energy"][0])}
+
+
+def _timed_windows(runner, windows, flush, device):
+    """CUDA-event ms per window, each window after an L2 flush (the same protocol as the headline)."""
+    import torch
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(windows)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(windows)]
+    torch.cuda.synchronize(device)
+    for w in range(windows):
+        flush.zero_()
+        starts[w].record()
+        runner.launch()
+        ends[w].record()
+        runner.settle()
+    torch.cuda.synchronize(device)
+    return sum(a.elapsed_time(b) for a, b in zip(starts, ends))
+
+
+def _config1(args, model, device, flush, S):
+    """Config 1 alone: ms per MD step of ONE 135-atom replica (whole_step, same model), timed like the
+    headline over the same number of steps, with the roofline of its dominant fused stage and the three
+    execution modes."""
+    from fastmd_b200 import units
+    from fastmd_b200.gpu_nhc import maxwell_boltzmann_momenta
+    from fastmd_b200.whole_step import GPUResidentMolecularDynamics
+
+    pos, cell, numbers, masses = _system(0)
+    momenta = maxwell_boltzmann_momenta(masses, TEMPERATURE, seed=0)
+    md = GPUResidentMolecularDynamics(model, positions=pos, momenta=momenta, cell=cell, atomic_numbers=numbers,
+                                      masses=masses, temperature_K=TEMPERATURE, timestep=0.25 * units.fs,
+                                      tdamp=25 * units.fs, replicas=1, steps_per_launch=S, device=device)
+    for _ in range(max(3, -(-args.warmup // S))):
+        md.runner.launch()
+        md.runner.settle()
+    windows = max(args.steps // S, 1)
+    ms = _timed_windows(md.runner, windows, flush, device) / (windows * S)
+    out = {"workload": "config1: one 135-atom replica, MACE-arch, NVT-NHC whole_step", "ms_per_step": ms,
+           "atom_steps_per_s": 135e3 / ms, "steps": windows * S}
+    try:
+        out["roofline"] = _roofline(md, device)
+    except Exception as error:  # noqa: BLE001
+        out["roofline"] = {"error": f"{type(error).__name__}: {error}"}
+    if not args.no_ops:
+        try:
+            out["execution_modes"] = _execution_modes(md, model, (pos, cell, numbers, masses), momenta, device)
+        except Exception as error:  # noqa: BLE001
+            out["execution_modes"] = {"error": f"{type(error).__name__}: {error}"}
+    return out
+
+
+def _config0_matris(args, device, flush):
+    """Config 0 on the GPU: the 135-atom system under MatRIS-10M (seeded weights), NVT-NHC whole_step,
+    ms per MD step over up to 100 timed steps; beside it the CPU port of the reference's config-0 path
+    (oracle/md.py MatRISOracleMD: dense neighbour search, FP64 MatRIS with autograd forces, the NHC) on all
+    host threads, a bounded sample of 3 steps."""
+    import torch
+
+    from fastmd_b200 import units
+    from fastmd_b200.gpu_nhc import maxwell_boltzmann_momenta
+    from fastmd_b200.matris import MatRISModel
+    from fastmd_b200.matris_params import MATRIS_10M, seeded_parameters
+    from fastmd_b200.whole_step import GPUResidentMolecularDynamics
+
+    pos, cell, numbers, masses = _system(0)
+    momenta = maxwell_boltzmann_momenta(masses, TEMPERATURE, seed=0)
+    model = MatRISModel(MATRIS_10M, seed=0, device=device)
+    S = 10
+    md = GPUResidentMolecularDynamics(model, positions=pos, momenta=momenta, cell=cell, atomic_numbers=numbers,
+                                      masses=masses, temperature_K=TEMPERATURE, timestep=0.25 * units.fs,
+                                      tdamp=25 * units.fs, replicas=1, steps_per_launch=S, device=device)
+    for _ in range(3):
+        md.runner.launch()
+        md.runner.settle()
+    windows = max(1, min(args.steps, 100) // S)
+    ms = _timed_windows(md.runner, windows, flush, device) / (windows * S)
+    out = {"workload": "config0 on the GPU: 135-atom CsSnI3, MatRIS-10M (10 layers, 128 wide, energy head "
+                       "256/256, seeded weights), NVT-NHC whole_step, 3xTF32 tcgen05 GEMMs",
+           "ms_per_step": ms, "atom_steps_per_s": 135e3 / ms, "steps": windows * S,
+           "reference_published_h100_ms_per_step": 28.018}
+    if not args.no_cpu_baseline:
+        from oracle.md import MatRISOracleMD
+
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        ref = MatRISOracleMD(seeded_parameters(MATRIS_10M, 0), MATRIS_10M, pos, cell, numbers, masses, momenta,
+                             temperature_K=TEMPERATURE, timestep=0.25 * units.fs, tdamp=25 * units.fs)
+        t0 = time.perf_counter()
+        steps = 3
+        for _ in range(steps):
+            ref.step()
+        cpu_ms = 1e3 * (time.perf_counter() - t0) / steps
+        out["cpu_baseline"] = {"ms_per_step": cpu_ms, "cores": threads, "kind": "port",
+                               "sample": f"{steps} MD steps of the 135-atom system (MatRISOracleMD: FP64 MatRIS-10M "
+                                         f"forces by autograd, the reference's equations) on {threads} threads"}
+        out["speedup_vs_cpu_port"] = cpu_ms / ms
+    return out
 
 
 def _execution_modes(md_ws, model, system, momenta, device, steps=200, warmup=20):

@@ -102,6 +102,7 @@ _SIGNATURES: dict[str, list] = {
     "fmd_nequip_gate": [_P, _P, _P, _P, _P, _P, _I64, _P, _P, _P, _P],
     "fmd_nequip_gate_bwd": [_P, _P, _P, _P, _P, _P, _I64, _P, _P, _P, _P],
     "fmd_nhc_pre_force": [_P, _P, _P, _I64, _I32, _I32, _I32, _I32, _P, _P],
+    "fmd_nhc_post_pre_force": [_P, _P, _P, _I64, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P],
     "fmd_nhc_post_force": [_P, _P, _P, _I64, _I32, _I32, _I32, _I32, _P, _P, _P, _P],
 }
 _RESTYPES = {"fmd_status_string": ctypes.c_char_p, "fmd_last_error": ctypes.c_char_p}

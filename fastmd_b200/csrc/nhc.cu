@@ -219,40 +219,92 @@ __global__ void __launch_bounds__(THREADS) nhc_post_force_kernel(NhcArgs a) {
     }
 }
 
-template <bool PRE, int M, int EPT, int THREADS>
+// Step n's second half and step n+1's first half in one launch: p += dt/2 F(q_{n+1}); NHC(dt/2); F, E
+// cached; NHC(dt/2); p += dt/2 F(q_{n+1}); q += dt p / m. The momenta, forces and chain stay in registers
+// between the halves; every operation is the one of the two separate kernels in the same order, so the
+// state is bitwise that of nhc_post_force_kernel followed by nhc_pre_force_kernel.
+template <int M, int EPT, int THREADS>
+__global__ void __launch_bounds__(THREADS) nhc_post_pre_kernel(NhcArgs a) {
+    __shared__ double smem[32];
+    const int r = blockIdx.x;
+    const int64_t n3 = 3 * a.n_atoms;
+    const int64_t n3R = n3 * a.n_replicas;
+    double* q_ptr = a.state + int64_t(r) * n3;
+    double* p_ptr = a.state + n3R + int64_t(r) * n3;
+    double* f_ptr = a.state + 2 * n3R + int64_t(r) * n3;
+    const double* m_ptr = a.masses + int64_t(r) * a.n_atoms;
+    const double dt = a.consts[0];
+    const double dt2 = a.consts[1];
+    double p[EPT], m[EPT], f[EPT];
+    bool live[EPT];
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) {
+        const int64_t i = threadIdx.x + int64_t(k) * THREADS;
+        live[k] = i < n3;
+        m[k] = live[k] ? m_ptr[i / 3] : 1.0;
+        p[k] = 0.0;
+        f[k] = 0.0;
+        if (live[k]) {
+            const int64_t g = int64_t(r) * n3 + i;
+            f[k] = a.forces_f32 ? double(a.forces_f32[g]) : a.forces_f64[g];
+            p[k] = p_ptr[i] + kick_of(dt2, f[k], a.f32_kick);  // (4) of step n
+            f_ptr[i] = f[k];
+        }
+    }
+    Chain<M> c;
+    load_chain<M>(c, a, n3R, r);
+    nhc_half<M, EPT, THREADS>(p, m, live, c, a.consts, a.tloop, smem);  // (5) of step n
+    if (a.energy && threadIdx.x == 0) a.state[3 * n3R + 2 * int64_t(a.n_replicas) * M + r] = a.energy[r];
+    nhc_half<M, EPT, THREADS>(p, m, live, c, a.consts, a.tloop, smem);  // (1) of step n+1
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) {
+        if (!live[k]) continue;
+        const int64_t i = threadIdx.x + int64_t(k) * THREADS;
+        const double pk = p[k] + kick_of(dt2, f[k], a.f32_kick);  // (2)
+        const double q = q_ptr[i] + (dt * pk) / m[k];              // (3)
+        q_ptr[i] = q;
+        p_ptr[i] = pk;
+        if (a.positions32) a.positions32[int64_t(r) * n3 + i] = float(q);
+    }
+    store_chain<M>(c, a, n3R, r);
+}
+
+// KIND 0: pre-force half, 1: post-force half, 2: post-force half then the next pre-force half
+template <int KIND, int M, int EPT, int THREADS>
 inline void launch_nhc(const NhcArgs& a, cudaStream_t s) {
-    if (PRE) nhc_pre_force_kernel<M, EPT, THREADS><<<a.n_replicas, THREADS, 0, s>>>(a);
-    else nhc_post_force_kernel<M, EPT, THREADS><<<a.n_replicas, THREADS, 0, s>>>(a);
+    if (KIND == 0) nhc_pre_force_kernel<M, EPT, THREADS><<<a.n_replicas, THREADS, 0, s>>>(a);
+    else if (KIND == 1) nhc_post_force_kernel<M, EPT, THREADS><<<a.n_replicas, THREADS, 0, s>>>(a);
+    else nhc_post_pre_kernel<M, EPT, THREADS><<<a.n_replicas, THREADS, 0, s>>>(a);
 }
 
 // threads and elements per thread from 3n: the fewest threads (multiple of
 // 32, <= 1024) with at most EPT elements each
-template <bool PRE, int M>
+template <int KIND, int M>
 inline fmd_status dispatch_ept(const NhcArgs& a, cudaStream_t s) {
     const int64_t n3 = 3 * a.n_atoms;
-    if (n3 <= 128) launch_nhc<PRE, M, 1, 128>(a, s);
-    else if (n3 <= 512) launch_nhc<PRE, M, 1, 512>(a, s);
-    else if (n3 <= 1024) launch_nhc<PRE, M, 1, 1024>(a, s);
-    else if (n3 <= 2048) launch_nhc<PRE, M, 2, 1024>(a, s);
-    else if (n3 <= 4096) launch_nhc<PRE, M, 4, 1024>(a, s);
-    else if (n3 <= 8192) launch_nhc<PRE, M, 8, 1024>(a, s);
-    else if (n3 <= 16384) launch_nhc<PRE, M, 16, 1024>(a, s);
-    else if (n3 <= 32768) launch_nhc<PRE, M, 32, 1024>(a, s);
+    if (n3 <= 128) launch_nhc<KIND, M, 1, 128>(a, s);
+    else if (n3 <= 512) launch_nhc<KIND, M, 1, 512>(a, s);
+    else if (n3 <= 1024) launch_nhc<KIND, M, 1, 1024>(a, s);
+    else if (n3 <= 2048) launch_nhc<KIND, M, 2, 1024>(a, s);
+    else if (n3 <= 4096) launch_nhc<KIND, M, 4, 1024>(a, s);
+    else if (n3 <= 8192) launch_nhc<KIND, M, 8, 1024>(a, s);
+    else if (n3 <= 16384) launch_nhc<KIND, M, 16, 1024>(a, s);
+    else if (n3 <= 32768) launch_nhc<KIND, M, 32, 1024>(a, s);
     else return FMD_ERR_UNSUPPORTED;
     return check_launch();
 }
 
-template <bool PRE>
+template <int KIND>
 inline fmd_status dispatch_chain(const NhcArgs& a, int tchain, cudaStream_t s) {
     switch (tchain) {
-        case 1: return dispatch_ept<PRE, 1>(a, s);
-        case 2: return dispatch_ept<PRE, 2>(a, s);
-        case 3: return dispatch_ept<PRE, 3>(a, s);
-        case 4: return dispatch_ept<PRE, 4>(a, s);
-        case 5: return dispatch_ept<PRE, 5>(a, s);
-        case 6: return dispatch_ept<PRE, 6>(a, s);
-        case 7: return dispatch_ept<PRE, 7>(a, s);
-        case 8: return dispatch_ept<PRE, 8>(a, s);
+        case 1: return dispatch_ept<KIND, 1>(a, s);
+        case 2: return dispatch_ept<KIND, 2>(a, s);
+        case 3: return dispatch_ept<KIND, 3>(a, s);
+        case 4: return dispatch_ept<KIND, 4>(a, s);
+        case 5: return dispatch_ept<KIND, 5>(a, s);
+        case 6: return dispatch_ept<KIND, 6>(a, s);
+        case 7: return dispatch_ept<KIND, 7>(a, s);
+        case 8: return dispatch_ept<KIND, 8>(a, s);
         default: return FMD_ERR_UNSUPPORTED;
     }
 }
@@ -271,7 +323,7 @@ fmd_status fmd_nhc_pre_force(double* state, const double* masses, const double* 
         return FMD_ERR_INVALID_ARGUMENT;
     NhcArgs a{state, masses, consts, n_atoms, n_replicas, tloop, f32_kick, positions32,
               nullptr, nullptr, nullptr};
-    return dispatch_chain<true>(a, tchain, as_stream(stream));
+    return dispatch_chain<0>(a, tchain, as_stream(stream));
 }
 
 fmd_status fmd_nhc_post_force(double* state, const double* masses, const double* consts,
@@ -283,7 +335,19 @@ fmd_status fmd_nhc_post_force(double* state, const double* masses, const double*
         return FMD_ERR_INVALID_ARGUMENT;
     NhcArgs a{state, masses, consts, n_atoms, n_replicas, tloop, f32_kick, nullptr,
               forces_f32, forces_f64, energy};
-    return dispatch_chain<false>(a, tchain, as_stream(stream));
+    return dispatch_chain<1>(a, tchain, as_stream(stream));
+}
+
+fmd_status fmd_nhc_post_pre_force(double* state, const double* masses, const double* consts, int64_t n_atoms,
+                                  int32_t n_replicas, int32_t tchain, int32_t tloop, int32_t f32_kick,
+                                  const float* forces_f32, const double* forces_f64, const double* energy,
+                                  float* positions32, void* stream) {
+    if (state == nullptr || masses == nullptr || consts == nullptr || n_atoms < 1 || n_replicas < 1 ||
+        tloop < 1 || tchain < 1 || ((forces_f32 == nullptr) == (forces_f64 == nullptr)))
+        return FMD_ERR_INVALID_ARGUMENT;
+    NhcArgs a{state, masses, consts, n_atoms, n_replicas, tloop, f32_kick, positions32,
+              forces_f32, forces_f64, energy};
+    return dispatch_chain<2>(a, tchain, as_stream(stream));
 }
 
 }  // extern "C"

@@ -218,9 +218,8 @@ class _NoseHooverChain:
              stream(self.device))
         return self.state.q
 
-    def step_post_force(self, forces: Tensor, energy: Tensor | None = None) -> None:
-        """ASE ``step()`` second half: p += dt/2 F(q_{n+1}); NHC(dt/2); F (and E) cached.
-        ``forces``: ``(R*n, 3)`` float32 or float64 device tensor; ``energy``: R values or None."""
+    def _post_args(self, forces: Tensor, energy: Tensor | None):
+        """(float32 forces or None, float64 forces or None, float64 energies or None) for the kernels."""
         forces = forces.reshape(self.replicas * self.n_atoms, 3)
         if not forces.is_contiguous():
             forces = forces.contiguous()
@@ -233,9 +232,25 @@ class _NoseHooverChain:
             e = energy.reshape(-1).to(torch.float64)
             if e.numel() != self.replicas:
                 raise ValueError(f"energy needs one value per replica ({self.replicas})")
+        return f32, f64, e
+
+    def step_post_force(self, forces: Tensor, energy: Tensor | None = None) -> None:
+        """ASE ``step()`` second half: p += dt/2 F(q_{n+1}); NHC(dt/2); F (and E) cached.
+        ``forces``: ``(R*n, 3)`` float32 or float64 device tensor; ``energy``: R values or None."""
+        f32, f64, e = self._post_args(forces, energy)
         call("fmd_nhc_post_force", ptr(self.state.flat), ptr(self.masses), ptr(self.consts), self.n_atoms,
              self.replicas, self.tchain, self.tloop, int(self.f32_kick), ptr(f32), ptr(f64), ptr(e),
              stream(self.device))
+
+    def step_post_pre_force(self, forces: Tensor, energy: Tensor | None = None) -> Tensor:
+        """``step_post_force(forces, energy)`` then the next step's ``step_pre_force()`` in one kernel (the
+        same state, bitwise): the two halves between two force calls of a whole-step window. Returns the
+        fp64 positions of the next step."""
+        f32, f64, e = self._post_args(forces, energy)
+        call("fmd_nhc_post_pre_force", ptr(self.state.flat), ptr(self.masses), ptr(self.consts), self.n_atoms,
+             self.replicas, self.tchain, self.tloop, int(self.f32_kick), ptr(f32), ptr(f64), ptr(e),
+             ptr(self.positions32), stream(self.device))
+        return self.state.q
 
     def step(self, force_fn):
         """Full step: ``force_fn(q)`` returns forces or ``(forces, energy)``."""

@@ -86,14 +86,19 @@ class WholeStepGraphRunner:
 
     # --------------------------------------------------------------- window
     def _window_body(self) -> None:
+        """One window: the pre-force half, then per step the build and the model, and between two steps
+        the post-force half and the next pre-force half fused in one launch (``step_post_pre_force``)."""
         integ, builder, model = self.integrator, self.builder, self.model
         integ.backup()
         self.window_flags.copy_(builder.refresh_flags)
-        for _ in range(self.steps_per_launch):
-            integ.step_pre_force()
+        integ.step_pre_force()
+        for k in range(self.steps_per_launch):
             batch, _ = builder.build(integ.positions32, rebuild_candidates=False, flags=self.window_flags)
             energy, forces = self._evaluate(batch, n_systems=self.replicas)
-            integ.step_post_force(forces, energy)
+            if k + 1 < self.steps_per_launch:
+                integ.step_post_pre_force(forces, energy)
+            else:
+                integ.step_post_force(forces, energy)
 
     def _capture(self) -> None:
         snapshot = self.integrator.snapshot()

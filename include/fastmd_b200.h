@@ -924,6 +924,15 @@ FMD_API fmd_status fmd_nhc_post_force(double* state, const double* masses, const
                               int32_t f32_kick, const float* forces_f32, const double* forces_f64,
                               const double* energy, void* stream);
 
+/* fmd_nhc_post_force for step n followed by fmd_nhc_pre_force for step n+1
+ * in ONE launch (the state, bitwise, of the two calls in a row): the two
+ * halves that meet between two force calls inside a whole-step window. The
+ * reference runs them as two kernels (gpu_nhc.py:394 then :360). */
+FMD_API fmd_status fmd_nhc_post_pre_force(double* state, const double* masses, const double* consts,
+                                          int64_t n_atoms, int32_t n_replicas, int32_t tchain, int32_t tloop,
+                                          int32_t f32_kick, const float* forces_f32, const double* forces_f64,
+                                          const double* energy, float* positions32, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -119,3 +119,35 @@ def test_backup_restore_and_observables(cuda):
 def test_positions32_follow_the_drift(cuda):
     nhc, _, _, _, _ = _run("f64_m3_l1", cuda)
     assert torch.equal(nhc.positions32, nhc.positions.float())
+
+
+@pytest.mark.parametrize("tag", ["f32", "f64"])
+@pytest.mark.parametrize("replicas", [1, 3])
+def test_fused_post_pre_half_equals_the_two_halves(cuda, tag, replicas):
+    """fmd_nhc_post_pre_force (the two halves between two force calls in one launch) leaves the state,
+    the float32 positions and the cached forces and energies bitwise equal to post-force then pre-force."""
+    from fastmd_b200.gpu_nhc import GPUNoseHooverChainNVT, ReplicaNoseHooverChainNVT
+
+    rng = np.random.default_rng(3)
+    n = 135
+    masses = rng.uniform(100.0, 140.0, n)
+    q = rng.uniform(0.0, 18.6, (replicas * n, 3))
+    p = rng.normal(0.0, 2.0, (replicas * n, 3))
+    fdt = torch.float32 if tag == "f32" else torch.float64
+    kw = dict(temperature_K=500.0, timestep=0.0245, tdamp=2.45, tchain=3, tloop=1, force_dtype=fdt, device=cuda)
+    make = (lambda: GPUNoseHooverChainNVT(masses, q, p, **kw)) if replicas == 1 else (
+        lambda: ReplicaNoseHooverChainNVT(masses, q, p, replicas=replicas, **kw))
+    a, b = make(), make()
+    for nhc in (a, b):
+        nhc.set_forces(torch.zeros((replicas * n, 3), dtype=fdt, device=cuda), torch.zeros(replicas, device=cuda,
+                                                                                             dtype=torch.float64))
+        nhc.step_pre_force()
+    for step in range(4):
+        f = torch.from_numpy(rng.normal(0.0, 1.0, (replicas * n, 3))).to(cuda, fdt)
+        e = torch.from_numpy(rng.normal(-5.0, 1.0, replicas)).to(cuda)
+        a.step_post_force(f, e)
+        a.step_pre_force()
+        b.step_post_pre_force(f, e)
+        torch.cuda.synchronize()
+        assert torch.equal(a.state.flat, b.state.flat), step
+        assert torch.equal(a.positions32, b.positions32), step
