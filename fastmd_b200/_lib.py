@@ -74,6 +74,7 @@ _SIGNATURES: dict[str, list] = {
     "fmd_paired_segment_attention_bwd_rows": [_P, _I64, _P, _I64, _P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                               _P, _P, _I64, _I64, _I32, _I64, _P, _I64, _P, _I64, _P, _P, _P],
     "fmd_tf32_mma_rate": [_I32, _P, _P],
+    "fmd_wait_probe": [_I32, _P, _P],
     "fmd_tf32_split": [_P, _I64, _I64, _I64, _I32, _P, _P, _I64, _P],
     "fmd_gemm_tf32x3": [_P, _I64, _P, _P, _I64, _P, _P, _I64, _P, _I64, _I64, _I32, _I32, _I32, _I32, _P, _P],
     "fmd_matris_geometry": [_P, _P, _P, _P, _I64, _I64, _P, _P, _P, _P],

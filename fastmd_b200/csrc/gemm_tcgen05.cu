@@ -722,6 +722,25 @@ __global__ void __launch_bounds__(128, 1) tf32_mma_rate_kernel(int iters, int32_
     }
 }
 
+// Self-test of the bounded wait every pipeline barrier of this file uses (mbar_wait): one thread waits on
+// a fresh barrier of count 1; with arrive = 1 it arrives first (the wait completes), with arrive = 0
+// nothing ever arrives and the wait gives up after about a second, raising FMD_FLAG_WAIT_TIMEOUT. No copy,
+// no MMA and no TMEM is involved, so the expired wait leaves nothing in flight.
+__global__ void wait_probe_kernel(int arrive, int32_t* flags) {
+    __shared__ uint64_t bar;
+    __shared__ int32_t abort_word;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_word = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (arrive) mbar_arrive(&bar);
+        if (!mbar_wait(&bar, 0, &abort_word)) raise_flag(flags, FMD_FLAG_WAIT_TIMEOUT);
+    }
+}
+
 // ------------------------------------------------------------------- host
 
 using EncodeTiled = PFN_cuTensorMapEncodeTiled_v12000;
@@ -812,6 +831,12 @@ fmd_status fmd_tf32_split(const float* w, int64_t rows, int64_t cols, int64_t ld
     if (rows == 0 || cols == 0) return FMD_OK;
     tf32_split_kernel<<<grid_for(rows * cols, 256), 256, 0, as_stream(stream)>>>(w, rows, cols, ldw,
                                                                                  transpose != 0, hi, lo, ldo);
+    return check_launch();
+}
+
+fmd_status fmd_wait_probe(int32_t arrive, int32_t* flags, void* stream) {
+    if (flags == nullptr) return FMD_ERR_INVALID_ARGUMENT;
+    wait_probe_kernel<<<1, 32, 0, as_stream(stream)>>>(arrive != 0, flags);
     return check_launch();
 }
 

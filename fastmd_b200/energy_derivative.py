@@ -1,12 +1,18 @@
-"""Engine-owned force/stress derivative of an energy-tap model (fastmd/engine/energy_derivative.py:87).
+"""Forces and stress of an energy-tap model by the engine (the surface of fastmd/engine/energy_derivative.py:51,
+:87: ``engine_derivative(adapter)`` and ``EnergyDerivative(adapter)(batch, inputs, *, task, n_real)``).
 
-``EnergyDerivative(adapter)(batch, inputs, task="ef", n_real=None)`` evaluates
-``adapter.node_energy(inputs, positions, cell)`` at a fresh position leaf,
-sums the real rows in float64 and returns ``{"e": [1] fp64, "f": [forces]}``
-(``"s"`` for a task with stress: the strain leaf of the reference,
-energy_derivative.py:110-132). The model's ``node_energy`` is a
-``torch.autograd.Function`` over libfastmd_b200 kernels, so the derivative is
-its explicit backward.
+The model exposes ``node_energy(inputs, positions, cell)``: per-atom energies that are differentiable with
+respect to the Cartesian positions and the cell (for the MACE-architecture model a
+``torch.autograd.Function`` whose backward is the model's explicit edge backward, and whose cell gradient
+is its edge virial over the periodic images). One gradient call gives both partial derivatives,
+``G_x = dE/dx`` [N, 3] and ``G_L = dE/dL`` [3, 3] (rows of L the lattice vectors), and then
+
+* forces ``F = -G_x``;
+* stress (``task`` with ``"s"``), from the response of E to a homogeneous deformation of the whole crystal
+  (every position and lattice vector mapped by ``I + e``): ``dE/de = x^T G_x + L^T G_L``, symmetrised
+  (only the symmetric part of ``e`` strains the crystal) and divided by the cell volume, in eV/A^3.
+
+The energy is the float64 sum of the first ``n_real`` rows (padding rows follow the real atoms).
 """
 from __future__ import annotations
 
@@ -14,48 +20,51 @@ import torch
 from torch import Tensor
 
 
-def _times(rows: Tensor, matrix: Tensor) -> Tensor:
-    """``rows @ matrix`` for a [3, 3] matrix, row by row (no GEMM, no TF32)."""
-    return rows[:, 0:1] * matrix[0] + rows[:, 1:2] * matrix[1] + rows[:, 2:3] * matrix[2]
-
-
 def cell_volume(cell: Tensor) -> Tensor:
-    return torch.dot(cell[0], torch.linalg.cross(cell[1], cell[2])).abs()
+    """|det L| of a [3, 3] cell (rows are lattice vectors)."""
+    return torch.linalg.det(cell.to(torch.float64)).abs()
+
+
+def deformation_derivative(positions: Tensor, grad_positions: Tensor, cell: Tensor, grad_cell: Tensor) -> Tensor:
+    """``sym(x^T dE/dx + L^T dE/dL)`` in float64: the derivative of the energy with respect to a symmetric
+    homogeneous strain applied to positions and cell together."""
+    x, gx = positions.to(torch.float64), grad_positions.to(torch.float64)
+    lat, gl = cell.to(torch.float64), grad_cell.to(torch.float64)
+    w = x.transpose(0, 1) @ gx + lat.transpose(0, 1) @ gl
+    return 0.5 * (w + w.transpose(0, 1))
 
 
 class EnergyDerivative:
+    """The engine's derivative of an energy tap: ``{"e": [1] float64, "f": [forces], "s": [stress]}``."""
+
     stress_unit = "eV/A^3"
 
     def __init__(self, adapter) -> None:
         self.adapter = adapter
 
     def extensive_energy(self, energy: Tensor, atom_counts) -> Tensor:
+        """Energy taps return extensive energies already."""
         return energy
 
     def __call__(self, batch, inputs, *, task: str = "ef", n_real: int | None = None) -> dict:
-        stress = "s" in task
+        want_stress = "s" in task
+        positions = batch.positions.detach().requires_grad_(True)
+        cell = batch.cell.detach().requires_grad_(want_stress)
         with torch.enable_grad():
-            leaf = batch.positions.detach().requires_grad_(True)
-            positions, cell = leaf, batch.cell
-            leaves = (leaf,)
-            if stress:  # x' = x (1 + eps), cell' = cell (1 + eps), eps symmetric
-                strain = torch.zeros((3, 3), dtype=leaf.dtype, device=leaf.device, requires_grad=True)
-                symmetric = 0.5 * (strain + strain.transpose(0, 1))
-                positions = leaf + _times(leaf, symmetric)
-                cell = cell + _times(cell, symmetric)
-                leaves = (leaf, strain)
             energies = self.adapter.node_energy(inputs, positions, cell)
-            rows = energies.shape[0] if n_real is None else n_real
-            energy = energies[:rows].to(torch.float64).sum()
+            count = energies.shape[0] if n_real is None else int(n_real)
+            energy = energies[:count].to(torch.float64).sum()
+            leaves = [positions, cell] if want_stress else [positions]
             grads = torch.autograd.grad(energy, leaves)
-        out = {"e": energy.detach().reshape(1), "f": [-grads[0]]}
-        if stress:
-            out["s"] = [grads[1] / cell_volume(batch.cell)]
-        return out
+        result = {"e": energy.detach().reshape(1), "f": [-grads[0]]}
+        if want_stress:
+            virial = deformation_derivative(batch.positions, grads[0], batch.cell, grads[1])
+            result["s"] = [(virial / cell_volume(batch.cell)).to(grads[0].dtype)]
+        return result
 
 
 def engine_derivative(adapter) -> EnergyDerivative:
-    """The derivative the runtime runs for an energy-tap adapter (energy_derivative.py:51)."""
+    """The derivative the runtime runs for an adapter with an energy tap (``node_energy``)."""
     if not hasattr(adapter, "node_energy"):
         raise TypeError(f"model adapter {getattr(adapter, 'name', adapter)!r} has no energy tap (node_energy)")
     return EnergyDerivative(adapter)

@@ -128,22 +128,27 @@ class SkinTopologyRunner:
 
     # --------------------------------------------------------------- evaluation
     def _displacement(self, positions: np.ndarray) -> float:
-        """Host minimum-image largest displacement since the last refresh (A)."""
-        delta = positions - self._reference
-        delta -= np.rint(delta @ self._inv_cell) @ self.cell
-        return float(np.sqrt(np.einsum("ij,ij->i", delta, delta).max(initial=0.0)))
+        """The largest distance (A) any atom has moved since the candidates were last built, each atom's
+        move taken to its nearest periodic image: fractional moves folded into [-1/2, 1/2)."""
+        frac = (positions - self._reference) @ self._inv_cell
+        frac -= np.floor(frac + 0.5)
+        moved = frac @ self.cell
+        return float(np.sqrt((moved * moved).sum(axis=1)).max(initial=0.0))
 
     def _refresh(self, positions: np.ndarray) -> None:
-        """Refresh the candidates at the device positions and count their exact demand (one readback)."""
-        self.owner.refresh_candidates(self.positions)
-        _, status = self.owner.build(self.positions, rebuild_candidates=False)
-        capacity_valid, edges = torch.cat([status.candidate_capacity_valid.reshape(1).long(),
-                                           status.edge_count.long()]).tolist()
-        if not capacity_valid:
-            raise SkinTopologyUnavailable(
-                f"a candidate row exceeds {self.owner.buffer_max} slots within {self.owner.candidate_cutoff} A")
-        self._reference = np.array(positions, dtype=np.float64, copy=True)
-        self._demand = (edges + 1) // 2
+        """New candidates at the current device positions, then one exact build to learn the pair demand;
+        its status comes back in a single host read (truncated candidate rows end the skin reuse)."""
+        builder = self.owner
+        builder.refresh_candidates(self.positions)
+        _, status = builder.build(self.positions, rebuild_candidates=False)
+        readout = torch.stack([status.candidate_capacity_valid.reshape(()).to(torch.int64),
+                               status.edge_count.reshape(-1)[0].to(torch.int64)]).cpu()
+        truncated, n_edges = not bool(readout[0]), int(readout[1])
+        if truncated:
+            raise SkinTopologyUnavailable(f"candidate rows truncated: more than {builder.buffer_max} candidates "
+                                          f"of an atom within {builder.candidate_cutoff} A")
+        self._reference = np.array(positions, dtype=np.float64)
+        self._demand = -(-n_edges // 2)
         self.refreshes += 1
 
     def _launch(self, entry):

@@ -381,6 +381,15 @@ FMD_API fmd_status fmd_gather_add_silu(const float* p0, int64_t ldp0, const fmd_
 FMD_API fmd_status fmd_silu_pair_bwd(const float* grad_core, const float* grad_gate, const float* preact,
                                      int64_t rows, int32_t h, float* grad_pre, int64_t ldgp, void* stream);
 
+/* Self-test of the bounded mbarrier wait that every pipeline wait of the
+ * tensor-core kernels uses (no counterpart in the reference, whose Triton
+ * kernels have no bounded waits): one thread waits on a fresh barrier;
+ * arrive = 1 arrives first (no flag), arrive = 0 lets nothing arrive, the
+ * wait gives up after about a second and raises FMD_FLAG_WAIT_TIMEOUT in
+ * `flags` (device int32). Nothing is in flight when it gives up, so the
+ * context stays usable. */
+FMD_API fmd_status fmd_wait_probe(int32_t arrive, int32_t* flags, void* stream);
+
 /* The roofline denominator of fmd_gemm_tf32x3: one CTA per SM issuing `iters`
  * back-to-back tcgen05 kind::tf32 MMAs (M = 128, N = 128, K = 8, 262,144
  * flops each) with no data movement; time the launch with events on `stream`.

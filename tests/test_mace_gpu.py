@@ -100,8 +100,8 @@ def test_energy_derivative_autograd_route_equals_explicit_backward(cuda):
     assert torch.equal(out["f"][0], forces)
 
 
-def test_stress_strain_leaf_matches_fp64_oracle(cuda):
-    """EnergyDerivative(task="efs"): the reference's strain leaf through the model's cell gradient
+def test_stress_matches_fp64_oracle(cuda):
+    """EnergyDerivative(task="efs"): the deformation derivative from the position and cell gradients
     (fmd_mace_edge_virial) against the FP64 oracle's own strain leaf."""
     from fastmd_b200.energy_derivative import EnergyDerivative
     from fastmd_b200.mace import MACEModel
