@@ -43,6 +43,28 @@ class MatRISConfig:
         if self.node_dim % 4:
             raise ValueError("feature widths must be multiples of 4 (16-byte rows)")
 
+    @classmethod
+    def from_reference(cls, config: dict) -> "MatRISConfig":
+        """The architecture of a reference checkpoint's ``config`` dict (the constructor's keyword
+        arguments, model.py:107, saved by ``MatRIS.config``); raises for the variants this build does not
+        implement (norms other than LayerNorm, the SH three-body basis, plain MLP blocks, biases in the
+        interaction FFNs, the smoothed edge update)."""
+        kinds = {"norm_type": "layer", "three_body_expansion": "fourier", "graph_conv_mlp": "gatemlp"}
+        for key, want in kinds.items():
+            if str(config.get(key, want)).lower() != want:
+                raise NotImplementedError(f"MatRIS {key}={config.get(key)!r}: this build implements {want!r}")
+        if config.get("use_bias", False) or config.get("use_smoothed_for_delta_edge", False):
+            raise NotImplementedError("MatRIS use_bias / use_smoothed_for_delta_edge are not implemented here")
+        hidden = config.get("mlp_hidden_dims", (128, 128))
+        hidden = (int(hidden),) if isinstance(hidden, int) else tuple(int(h) for h in hidden)
+        return cls(num_layers=int(config.get("num_layers", 6)), node_dim=int(config.get("node_feat_dim", 128)),
+                   edge_dim=int(config.get("edge_feat_dim", 128)),
+                   three_body_dim=int(config.get("three_body_feat_dim", 128)), energy_hidden=hidden,
+                   num_radial=int(config.get("num_radial", 7)), num_angular=int(config.get("num_angular", 7)),
+                   envelope_exponent=int(config.get("envelope_exponent", 8)),
+                   pairwise_cutoff=float(config.get("pairwise_cutoff", 6.0)),
+                   three_body_cutoff=float(config.get("three_body_cutoff", 4.0)))
+
     @property
     def max_frequency(self) -> int:
         return (self.num_angular - 1) // 2

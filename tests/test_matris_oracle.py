@@ -48,3 +48,14 @@ def test_graph_counts():
         t = f"matris_s{seed}"
         assert g[f"{t}_edge_index"].shape[0] == 2 * g[f"{t}_u2d"].shape[0] > 2000  # about 2,054 directed edges
         assert g[f"{t}_line_graph"].shape[1] == 5 and g[f"{t}_line_graph"].shape[0] > 17_000
+
+
+def test_config_from_a_reference_checkpoint_config():
+    from fastmd_b200.matris_params import MatRISConfig
+
+    ref = MATRIS_10M.reference_kwargs()
+    assert MatRISConfig.from_reference(ref) == MATRIS_10M
+    with pytest.raises(NotImplementedError):
+        MatRISConfig.from_reference({**ref, "norm_type": "rms"})
+    with pytest.raises(NotImplementedError):
+        MatRISConfig.from_reference({**ref, "three_body_expansion": "SH"})
