@@ -158,17 +158,17 @@ __global__ void gather_rows_bwd_kernel(const float* __restrict__ gout, int64_t l
         if constexpr (VEC == 4) {
             float4 acc = f4_zero();
             int64_t j = start + slot;
-            // four rows' loads in flight, added in row order (the same sums as one row at a time)
-            for (; j + 3 * slots < end; j += 4 * slots) {
-                int64_t r[4];
+            // eight rows' loads in flight, added in row order (the same sums as one row at a time)
+            for (; j + 7 * slots < end; j += 8 * slots) {
+                int64_t r[8];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) r[q] = perm ? perm[j + q * slots] : j + q * slots;
+                for (int q = 0; q < 8; ++q) r[q] = perm ? perm[j + q * slots] : j + q * slots;
                 if (col_ok) {
-                    float4 x[4];
+                    float4 x[8];
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) x[q] = ldg4(gout + r[q] * ldgo + col0 + v * 4);
+                    for (int q = 0; q < 8; ++q) x[q] = ldg4(gout + r[q] * ldgo + col0 + v * 4);
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) acc = f4_add(acc, x[q]);
+                    for (int q = 0; q < 8; ++q) acc = f4_add(acc, x[q]);
                 }
             }
             for (; j < end; j += slots) {
