@@ -331,7 +331,7 @@ def _ours(args):
     if rank != 0:
         return None
     return {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": windows * S,
-            "warmup": max(1, -(-args.warmup // S)) * S, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "warmup": warm_windows * S, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32 (NHC state f64)", "data": "synthetic",
             "config": _config(args, world), "wall_s_timed": wall,
             "wall_ms_per_step": 1e3 * wall / (windows * S),

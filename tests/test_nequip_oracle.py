@@ -72,3 +72,21 @@ def test_energy_invariant_forces_covariant_and_gradient():
     ep, _ = onq.energy_forces(w, _Cfg, p1, cell, numbers, c, nb, im)
     em, _ = onq.energy_forces(w, _Cfg, p2, cell, numbers, c, nb, im)
     assert abs(-(ep - em) / (2 * h) - f[3, 1]) < 1e-5 * max(1.0, np.abs(f).max())
+
+
+def test_coupling_constants_equal_racah_clebsch_gordan():
+    """The NequIP coupling constants (derived numerically from equivariance) equal Racah's closed-form
+    Clebsch-Gordan coefficients moved into the same real basis, for all 15 paths up to l = 2, up to one
+    sign per path (the "positive largest entry" convention is not defined where several entries share the
+    largest magnitude; a path's sign is absorbed by its radial weights)."""
+    from fastmd_b200._coupling import _harmonics, clebsch_gordan
+    from fastmd_b200.nequip import PATHS
+    from oracle.clebsch import racah, real_clebsch_gordan
+
+    assert abs(racah(1, 1, 1, -1, 0, 0) - 1 / np.sqrt(3)) < 1e-15  # a textbook entry
+    assert abs(racah(1, 1, 1, 0, 2, 1) - 1 / np.sqrt(2)) < 1e-15
+    for l1, l2, l3 in PATHS:
+        mine = clebsch_gordan(l1, l2, l3)
+        ref = real_clebsch_gordan(l1, l2, l3, _harmonics)
+        err = min(np.abs(mine - ref).max(), np.abs(mine + ref).max())
+        assert err < 1e-9, (l1, l2, l3, err)
