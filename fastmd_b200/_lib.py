@@ -82,6 +82,8 @@ _SIGNATURES: dict[str, list] = {
     "fmd_matris_bessel_bwd": [_P, _P, _I64, _I64, _P, _P, _I32, c_float, c_float, c_float, _P, _P, _I64, _P, _P],
     "fmd_matris_threebody": [_P, _P, _I64, _I64, _P, _I32, _P, _I64, _P, _P],
     "fmd_matris_threebody_bwd": [_P, _P, _I64, _I64, _P, _I32, _P, _I64, _P, _I64, _P, _P, _P, _P, _P, _P, _P],
+    "fmd_matris_line_envelope": [_P, _I64, _P, _I64, _I64, _I32, _P, _I64, _P, _P],
+    "fmd_matris_line_envelope_bwd": [_P, _I64, _P, _I64, _I32, _P, _I64, _P, _P, _P, _P, _P, _I64, _P],
     "fmd_matris_forces": [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P, c_double, _P, _P, _P,
                           _P, _P],
     "fmd_mace_edge_geometry": [_P, _P, _P, _P, _I64, c_float, _I32, _I32, _P, _P, _P],

@@ -254,6 +254,58 @@ __global__ void threebody_fold_kernel(TripletArgs a, const float* __restrict__ g
     }
 }
 
+// env[t, :] = base[u2[t], :] * base[u1[t], :] (the source bond's envelope times the target bond's), float4
+// columns; width % 4 == 0, rows 16-byte aligned
+__global__ void line_envelope_kernel(const float* __restrict__ base, int64_t ldb, const int32_t* __restrict__ lg,
+                                     int64_t n_triplets, int64_t n_bonds, int width, float* __restrict__ env,
+                                     int64_t lde, int32_t* flags) {
+    const int wv = width / 4;
+    const int64_t total = n_triplets * wv;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t t = i / wv;
+        const int c = int(i - t * wv);
+        int64_t u1 = lg[5 * t + 1], u2 = lg[5 * t + 3];
+        if (u1 < 0 || u1 >= n_bonds || u2 < 0 || u2 >= n_bonds) {
+            raise_flag(flags, FMD_FLAG_INDEX_RANGE);
+            u1 = 0;
+            u2 = 0;
+        }
+        st4(env + t * lde + 4 * c, f4_mul(ldg4(base + u2 * ldb + 4 * c), ldg4(base + u1 * ldb + 4 * c)));
+    }
+}
+
+// grad_base[u] = sum over the triplets whose target bond is u (CSR perm1/off1) of g[t] * base[u2[t]], then
+// over those whose source bond is u (perm2/off2) of g[t] * base[u1[t]]: a warp per (bond, 128 columns),
+// the rows in CSR order (deterministic, no atomics)
+__global__ void line_envelope_bwd_kernel(const float* __restrict__ base, int64_t ldb, const int32_t* __restrict__ lg,
+                                         int64_t n_bonds, int width, const float* __restrict__ grad,
+                                         int64_t ldg, const int64_t* __restrict__ perm1,
+                                         const int64_t* __restrict__ off1, const int64_t* __restrict__ perm2,
+                                         const int64_t* __restrict__ off2, float* __restrict__ grad_base,
+                                         int64_t ldo) {
+    const int lane = threadIdx.x & 31;
+    const int chunks = (width / 4 + 31) / 32;
+    const int64_t warp = (blockIdx.x * int64_t(blockDim.x) + threadIdx.x) >> 5;
+    const int64_t n_warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t task = warp; task < n_bonds * chunks; task += n_warps) {
+        const int64_t u = task / chunks;
+        const int v = int(task - u * chunks) * 32 + lane;
+        if (v >= width / 4) continue;
+        float4 acc = f4_zero();
+        for (int side = 0; side < 2; ++side) {
+            const int64_t* perm = side == 0 ? perm1 : perm2;
+            const int64_t* off = side == 0 ? off1 : off2;
+            for (int64_t j = off[u]; j < off[u + 1]; ++j) {
+                const int64_t t = perm[j];
+                int64_t other = lg[5 * t + (side == 0 ? 3 : 1)];
+                if (other < 0 || other >= n_bonds) other = 0;
+                acc = f4_add(acc, f4_mul(ldg4(grad + t * ldg + 4 * v), ldg4(base + other * ldb + 4 * v)));
+            }
+        }
+        st4(grad_base + u * ldo + 4 * v, acc);
+    }
+}
+
 struct ForceArgs {
     const float* length;
     const float* unit;
@@ -455,6 +507,38 @@ fmd_status fmd_matris_threebody_bwd(const float* unit, const int32_t* line_graph
     if (n_bonds == 0) return FMD_OK;
     threebody_fold_kernel<<<grid_for(n_bonds * 32, kThreads), kThreads, 0, s>>>(a, grad_cos, pair_index, n_bonds,
                                                                                  perm1, off1, perm2, off2, grad_unit);
+    return check_launch();
+}
+
+static bool rows16(const float* p, int64_t ld) { return aligned16(p) && ld % 4 == 0; }
+
+fmd_status fmd_matris_line_envelope(const float* base, int64_t ldb, const int32_t* line_graph, int64_t n_triplets,
+                                    int64_t n_bonds, int32_t width, float* env, int64_t lde, int32_t* flags,
+                                    void* stream) {
+    if (n_triplets < 0 || n_bonds < 1 || width < 4 || width % 4 || ldb < width || lde < width)
+        return FMD_ERR_INVALID_ARGUMENT;
+    if (n_triplets == 0) return FMD_OK;
+    if (base == nullptr || line_graph == nullptr || env == nullptr) return FMD_ERR_INVALID_ARGUMENT;
+    if (!rows16(base, ldb) || !rows16(env, lde)) return FMD_ERR_UNSUPPORTED;
+    line_envelope_kernel<<<grid_for(n_triplets * (width / 4), kThreads), kThreads, 0, as_stream(stream)>>>(
+        base, ldb, line_graph, n_triplets, n_bonds, width, env, lde, flags);
+    return check_launch();
+}
+
+fmd_status fmd_matris_line_envelope_bwd(const float* base, int64_t ldb, const int32_t* line_graph, int64_t n_bonds,
+                                        int32_t width, const float* grad, int64_t ldg, const int64_t* perm1,
+                                        const int64_t* off1, const int64_t* perm2, const int64_t* off2,
+                                        float* grad_base, int64_t ldo, void* stream) {
+    if (n_bonds < 0 || width < 4 || width % 4 || ldb < width || ldg < width || ldo < width)
+        return FMD_ERR_INVALID_ARGUMENT;
+    if (n_bonds == 0) return FMD_OK;
+    if (base == nullptr || line_graph == nullptr || grad == nullptr || off1 == nullptr || off2 == nullptr ||
+        grad_base == nullptr)
+        return FMD_ERR_INVALID_ARGUMENT;
+    if (!rows16(base, ldb) || !rows16(grad, ldg) || !rows16(grad_base, ldo)) return FMD_ERR_UNSUPPORTED;
+    const int chunks = (width / 4 + 31) / 32;
+    line_envelope_bwd_kernel<<<grid_for(n_bonds * chunks * 32, kThreads), kThreads, 0, as_stream(stream)>>>(
+        base, ldb, line_graph, n_bonds, width, grad, ldg, perm1, off1, perm2, off2, grad_base, ldo);
     return check_launch();
 }
 

@@ -116,6 +116,34 @@ def _gemm_f32(a: Tensor, w: Tensor, transposed: bool, bias=None, a_pre=None, act
     return y
 
 
+class _LineEnvelope(Function):
+    """env [T, C] = base[u2] * base[u1] over the triplets (``fmd_matris_line_envelope``), the backward a CSR fold
+    per bond (``fmd_matris_line_envelope_bwd``)."""
+
+    @staticmethod
+    def forward(ctx, base, graph):
+        T, C = graph.line_graph.shape[0], base.shape[1]
+        base = base.contiguous()
+        env = torch.empty((T, C), device=base.device)
+        call("fmd_matris_line_envelope", ptr(base), base.stride(0), ptr(graph.line_graph), T, graph.n_bonds, C,
+             ptr(env), C, ptr(_lib.flags_word(base.device)), stream(base.device))
+        ctx.save_for_backward(base)
+        ctx.graph = graph
+        return env
+
+    @staticmethod
+    def backward(ctx, grad):
+        (base,) = ctx.saved_tensors
+        g = ctx.graph
+        grad = grad.contiguous()
+        out = torch.empty_like(base)
+        p1, o1, p2, o2 = g.line_csr
+        call("fmd_matris_line_envelope_bwd", ptr(base), base.stride(0), ptr(g.line_graph), g.n_bonds, base.shape[1],
+             ptr(grad), grad.stride(0), ptr(p1), ptr(o1), ptr(p2), ptr(o2), ptr(out), out.stride(0),
+             stream(base.device))
+        return out, None
+
+
 class _SiluChain(Function):
     """``L_n(silu(... silu(L_1(x))))`` of frozen linears ``L_k(x) = x W_k^T (+ b_k)``.
 
@@ -408,7 +436,7 @@ class MatRISModel:
         """Refinement on the line graph (interaction_block.py:580-848): bonds are its nodes."""
         ops, graph = g.ops, g.line
         base = wide_gemm.linear(rbf_line, layer["envelope"], precision=self.precision)
-        env = ops.gather(base, g.t_u2) * ops.gather(base, g.t_u1)
+        env = _LineEnvelope.apply(base, g)
         gm = layer["edge"]
         core, gate = _checked(decomposed_indexed_cat4_silu_linear(trips, atoms, g.t_atom, bonds, g.t_u1, g.t_u2,
                                                                   gm.parts, gm.b0,

@@ -886,6 +886,28 @@ FMD_API fmd_status fmd_matris_threebody_bwd(const float* unit, const int32_t* li
                                             const int64_t* perm2, const int64_t* off2, float* grad_cos,
                                             float* grad_unit, void* stream);
 
+/* The line graph's refinement envelope: env [T, width] = base[u2[t]] *
+ * base[u1[t]] per triplet t = (atom, u1, e1, u2, e2) [T, 5] int32 (the
+ * source bond's row of the learnable envelope base [U, width] times the
+ * target bond's), rows 16-byte aligned, width % 4 == 0 (else
+ * FMD_ERR_UNSUPPORTED). Replaces _line_envelope_fwd
+ * (fastmd/models/matris/op/triton_line_envelope.py:50) and the torch
+ * gather-product of Refinement.refinement_rows (interaction_block.py:650-668). */
+FMD_API fmd_status fmd_matris_line_envelope(const float* base, int64_t ldb, const int32_t* line_graph,
+                                            int64_t n_triplets, int64_t n_bonds, int32_t width, float* env,
+                                            int64_t lde, int32_t* flags, void* stream);
+
+/* Its backward, with no atomics: grad_base[u] = sum over the triplets whose
+ * target bond is u (perm1/off1: the CSR of column 1) of grad[t] * base[u2[t]],
+ * then over those whose source bond is u (perm2/off2, column 3) of grad[t] *
+ * base[u1[t]], in CSR order; every row of grad_base [U, width] is written.
+ * Replaces _line_envelope_bwd (triton_line_envelope.py:87). */
+FMD_API fmd_status fmd_matris_line_envelope_bwd(const float* base, int64_t ldb, const int32_t* line_graph,
+                                                int64_t n_bonds, int32_t width, const float* grad, int64_t ldg,
+                                                const int64_t* perm1, const int64_t* off1, const int64_t* perm2,
+                                                const int64_t* off2, float* grad_base, int64_t ldo,
+                                                void* stream);
+
 /* Forces and stress of the MatRIS energy from the gradients of its two
  * geometric leaves: grad_length [U] (bond lengths, on the bond's stored
  * direction u2d[u]; may be NULL) and grad_unit [E, 3] (may be NULL). Per edge

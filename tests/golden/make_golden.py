@@ -38,6 +38,8 @@ used) and runs, on CPU:
 * the bundled MatRIS-10M model itself (fastmd/models/matris/model.py:99) with seeded weights, its
   energies, forces and stress in float32 and float64 on the config-0 perovskite over the reference's
   legacy CPU graph (``matris_cases``; pymatgen placeholders, the graph fed by a dense search);
+* the line-graph envelope product ``_line_envelope_fwd/_bwd``
+  (fastmd/models/matris/op/triton_line_envelope.py:50/:87) under the interpreter;
 * the torch backend of ``GPUNoseHooverChainNVT`` (fastmd/execution/gpu_nhc.py:709,
   ``backend="torch"``) with harmonic forces, and ``maxwell_boltzmann_momenta``
   (gpu_nhc.py:199).
@@ -141,6 +143,29 @@ def matris_cases(torch):
             out[f"{tag}_f{name}"] = pred["f"][0].detach().double().numpy()
             out[f"{tag}_s{name}"] = pred["s"][0].detach().double().numpy()
         model.float()
+    return out
+
+
+def line_envelope_cases(torch, le):
+    """The reference's line-graph envelope product and its backward, ``_line_envelope_fwd`` /
+    ``_line_envelope_bwd`` (fastmd/models/matris/op/triton_line_envelope.py:50/:87), under the interpreter,
+    on a random bond table and triplet index pairs (source = column 3, target = column 1 of a line graph)."""
+    rng = np.random.default_rng(21)
+    out = {}
+    for tag, (U, T, D) in {"small": (37, 301, 32), "wide": (40, 256, 128)}.items():
+        base = rng.standard_normal((U, D)).astype(np.float32)
+        target = rng.integers(0, U, T).astype(np.int64)
+        source = rng.integers(0, U, T).astype(np.int64)
+        gout = rng.standard_normal((T, D)).astype(np.float32)
+        tb, ts, tt, tg = (torch.from_numpy(x) for x in (base, source, target, gout))
+        env = torch.empty((T, D))
+        BM, BD = 16, min(D, 128)
+        grid = ((T + BM - 1) // BM, (D + BD - 1) // BD)
+        le._line_envelope_fwd[grid](tb, ts, tt, env, T, D=D, S0=D, BM=BM, BD=BD)
+        grad = torch.zeros((U, D))
+        le._line_envelope_bwd[grid](tg, tb, ts, tt, grad, T, D=D, S0=D, GS0=D, BM=BM, BD=BD)
+        out.update({f"env_{tag}_base": base, f"env_{tag}_source": source, f"env_{tag}_target": target,
+                    f"env_{tag}_gout": gout, f"env_{tag}_out": env.numpy(), f"env_{tag}_grad": grad.numpy()})
     return out
 
 
@@ -860,6 +885,7 @@ def main(reference: str, only: list[str]) -> None:
     import fastmd.models.matris.op.triton_gated_ln as gl
     import fastmd.models.matris.op.triton_directed_pair_aggregate as pa
     import fastmd.models.matris.op.triton_residual_add as ra
+    import fastmd.models.matris.op.triton_line_envelope as le
 
     fixtures = {
         "gather_cat": lambda: gather_cat_cases(torch, gc),
@@ -877,6 +903,7 @@ def main(reference: str, only: list[str]) -> None:
         "float64": lambda: float64_cases(torch, fcb),
         "padding": lambda: padding_cases(torch, fcb),
         "matris": lambda: matris_cases(torch),
+        "line_envelope": lambda: line_envelope_cases(torch, le),
     }
     for name, make in fixtures.items():
         if not only or name in only:
