@@ -8,9 +8,9 @@ e.g. the reference's legacy CPU graph). Weights load from a MatRIS ``state_dict`
 reference's own key names (``matris_params.parameter_shapes``).
 
 Execution: every contraction runs in ``fmd_gemm_tf32x3`` (tcgen05, FP32 accuracy) with the fused
-SiLU epilogues, the first layer of every gated MLP as the decomposed indexed projection
-(``decomposed_indexed_cat{3,4}_silu_linear``: the GEMM on the source rows, the gather-add-SiLU
-epilogue on the edge rows), the gated LayerNorm (+ residual) in ``fmd_gated_ln``, the channel
+SiLU epilogues, the first layer of every gated MLP as the decomposed indexed projection (the GEMM on
+the source rows, one per gathered source with its parts' weight blocks stacked, and the
+gather-add-SiLU epilogue on the edge rows, ``fmd_gather_add_silu``), the gated LayerNorm (+ residual) in ``fmd_gated_ln``, the channel
 softmax attention in the paired CSR segment attention, the refinement sums in the CSR segment sum,
 the bond maps in ``fmd_pair_aggregate``, the residuals in ``fmd_residual_add``; the geometry, the
 radial and three-body bases and the force/virial reduction in ``fmd_matris_*``. The energy is
@@ -27,13 +27,12 @@ from torch import Tensor
 from torch.autograd import Function
 
 from . import _lib, wide_gemm
-from ._lib import call, ptr, stream
-from .decomposed_indexed_cat_silu_linear import (_GatherAddSilu, decomposed_indexed_cat3_silu_linear,
-                                                 decomposed_indexed_cat4_silu_linear)
+from ._lib import FmdCatPart, call, ptr, stream
+from .decomposed_indexed_cat_silu_linear import _GatherAddSilu
 from .dispatch import OpDispatcher, _attention_csr, _directed_pair_index
 from .gated_ln import fused_gated_ln, fused_gated_ln_residual
 from .matris_params import MATRIS_10M, MatRISConfig, parameter_shapes, seeded_parameters
-from .ops import csr_offsets, csr_scope, gather_cat
+from .ops import csr_offsets, csr_scope, gather_cat, segment_csr
 
 GPA = 160.21766208  # eV/A^3 -> GPa (readout.py:226)
 _ACT_SILU_GRAD, _ACT_INPUT_SILU = 2, 16
@@ -116,6 +115,56 @@ def _gemm_f32(a: Tensor, w: Tensor, transposed: bool, bias=None, a_pre=None, act
     return y
 
 
+class _PackedGatherAddSilu(Function):
+    """``(silu(pre[:, :H]), silu(pre[:, H:]))`` with ``pre = p0 + P_s[:, c : c + 2H][index] + ... + bias``
+    where several gathered parts may be column blocks of ONE projection ``P_s`` (a gathered source's
+    first-layer weights of all its parts stacked: one GEMM instead of one per part). The backward writes
+    each part's CSR row sums into its column block of ``grad_P`` directly (``fmd_gather_rows_bwd``), so a
+    shared source gets one gradient tensor and one input-gradient GEMM."""
+
+    @staticmethod
+    def forward(ctx, p0, bias, n_sources, blocks, *args):
+        # args: the n_sources projections, then one index per part; blocks: (source, column offset) per part
+        sources, indices = args[:n_sources], args[n_sources:]
+        rows, width = p0.shape
+        h = width // 2
+        dev = p0.device
+        pre = torch.empty((rows, width), device=dev)
+        core = torch.empty((rows, h), device=dev)
+        gate = torch.empty((rows, h), device=dev)
+        parts = (FmdCatPart * len(blocks))()
+        for k, ((src, col), idx) in enumerate(zip(blocks, indices)):
+            P = sources[src]
+            parts[k].src, parts[k].index, parts[k].ld, parts[k].n_src, parts[k].width = (
+                P.data_ptr() + 4 * col, ptr(idx), P.stride(0), P.shape[0], width)
+        call("fmd_gather_add_silu", ptr(p0), p0.stride(0), parts, len(blocks), ptr(bias), rows, h, ptr(pre),
+             ptr(core), ptr(gate), ptr(_lib.flags_word(dev)), stream(dev))
+        ctx.save_for_backward(pre, *indices)
+        ctx.shapes = [tuple(P.shape) for P in sources]
+        ctx.blocks = blocks
+        return core, gate
+
+    @staticmethod
+    def backward(ctx, grad_core, grad_gate):
+        pre, *indices = ctx.saved_tensors
+        rows, width = pre.shape
+        h = width // 2
+        dev = pre.device
+        s = stream(dev)
+        grad_core = torch.zeros((rows, h), device=dev) if grad_core is None else grad_core.contiguous()
+        grad_gate = torch.zeros((rows, h), device=dev) if grad_gate is None else grad_gate.contiguous()
+        grad_p0 = torch.empty((rows, width), device=dev)
+        call("fmd_silu_pair_bwd", ptr(grad_core), ptr(grad_gate), ptr(pre), rows, h, ptr(grad_p0), width, s)
+        grads = [torch.empty(shape, device=dev) for shape in ctx.shapes]
+        for (src, col), idx in zip(ctx.blocks, indices):
+            n_src, ld = ctx.shapes[src]
+            perm, off = segment_csr(idx, n_src)
+            if n_src:
+                call("fmd_gather_rows_bwd", ptr(grad_p0), width, 0, width, ptr(perm), ptr(off), n_src,
+                     grads[src].data_ptr() + 4 * col, ld, 0, s)
+        return (grad_p0, None, None, None, *grads, *([None] * len(indices)))
+
+
 class _LineEnvelope(Function):
     """env [T, C] = base[u2] * base[u1] over the triplets (``fmd_matris_line_envelope``), the backward a CSR fold
     per bond (``fmd_matris_line_envelope_bwd``)."""
@@ -187,12 +236,6 @@ class _SiluChain(Function):
             for k in range(n - 2, -1, -1):
                 g = _gemm_f32(g, ws[k], True, a_pre=hs[k])
         return (g, None, *([None] * (2 * n)))
-
-
-def _checked(pair):
-    if pair is None:
-        raise _lib.FastMDLibraryError("MatRIS: the decomposed first-layer projection declined its inputs")
-    return pair
 
 
 def _silu_chain(x: Tensor, layers: list, precision: str) -> Tensor:
@@ -293,6 +336,11 @@ class _Gated:
         w0 = torch.cat([p[f"{key}.mlp_core.layers.0.weight"], p[f"{key}.mlp_gate.layers.0.weight"]], 0)
         self.w0 = w0.contiguous()
         self.parts = tuple(w0[:, i * C:(i + 1) * C].contiguous() for i in range(parts))
+        # the gathered parts' first-layer blocks stacked per gathered source (one projection per source):
+        # cat3 [A | X[a] | X[b]] -> X (W_a; W_b); cat4 [A | Y[a] | X[b] | X[c]] -> Y W_a, X (W_b; W_c)
+        blocks = self.parts[1:]
+        self.sources = ((torch.cat(blocks, 0).contiguous(),) if parts == 3 else
+                        (blocks[0], torch.cat(blocks[1:], 0).contiguous()))
         self.b0 = torch.cat([p[f"{key}.mlp_core.layers.0.bias"], p[f"{key}.mlp_gate.layers.0.bias"]]).contiguous()
         self.w3c, self.b3c = p[f"{key}.mlp_core.layers.3.weight"], p[f"{key}.mlp_core.layers.3.bias"]
         self.w3g, self.b3g = p[f"{key}.mlp_gate.layers.3.weight"], p[f"{key}.mlp_gate.layers.3.bias"]
@@ -393,14 +441,27 @@ class MatRISModel:
 
     # ------------------------------------------------------------------ layers
 
+    def _first_layer(self, gm: _Gated, aligned: Tensor, gathered: list) -> tuple[Tensor, Tensor]:
+        """The SiLU halves of ``[aligned | gathered rows...] @ W0^T + b0`` by parts: ``aligned`` projected row
+        by row, each gathered source projected once on its own rows (all its parts' weight blocks stacked)
+        and its rows gathered and added in the epilogue (``gathered``: (source, [index per part]))."""
+        p0 = wide_gemm.linear(aligned, gm.parts[0], precision=self.precision)
+        sources, blocks, indices = [], [], []
+        width = gm.parts[0].shape[0]
+        for n, ((x, idxs), w) in enumerate(zip(gathered, gm.sources)):
+            sources.append(wide_gemm.linear(x, w, precision=self.precision))
+            for j, idx in enumerate(idxs):
+                blocks.append((n, j * width))
+                indices.append(idx)
+        return _PackedGatherAddSilu.apply(p0, gm.b0, len(sources), tuple(blocks), *sources, *indices)
+
     def _attention(self, layer: dict, nodes: Tensor, edges: Tensor, g: MatRISGraph, graph: dict, kind: str):
         """Graph_Attention_Layer (interaction_block.py:291-481): returns (nodes', edges')."""
         ops = graph["_ops"]
         target, source, n_nodes = graph["target_index"], graph["source_index"], graph["num_segment"]
         rows = ops.pair_expand(edges, g.d2u, graph) if kind == "atom" else edges
         gm = layer["edge"]
-        core, gate = _checked(decomposed_indexed_cat3_silu_linear(rows, nodes, target, source, gm.parts, gm.b0,
-                                                                  precision=self.precision))
+        core, gate = self._first_layer(gm, rows, [(nodes, [target, source])])
         msg = gm(core, gate)
         logits = wide_gemm.linear(rows, layer["logits"], precision=self.precision)
         C = edges.shape[1]
@@ -421,8 +482,7 @@ class MatRISModel:
         env = ops.pair_expand(wide_gemm.linear(rbf_atom, layer["envelope"], precision=self.precision), g.d2u,
                               graph)
         gm = layer["edge"]
-        core, gate = _checked(decomposed_indexed_cat3_silu_linear(rows, nodes, g.centre, g.neighbour, gm.parts,
-                                                                  gm.b0, precision=self.precision))
+        core, gate = self._first_layer(gm, rows, [(nodes, [g.centre, g.neighbour])])
         raw = gm(core, gate)
         red = ops.segment_sum_graph(raw, g.centre, g.n_atoms, graph, "target", weight=env)
         new_nodes = ops.residual(_silu_chain(red, layer["node_ffn"], self.precision), nodes, layer["node_res"])
@@ -438,9 +498,7 @@ class MatRISModel:
         base = wide_gemm.linear(rbf_line, layer["envelope"], precision=self.precision)
         env = _LineEnvelope.apply(base, g)
         gm = layer["edge"]
-        core, gate = _checked(decomposed_indexed_cat4_silu_linear(trips, atoms, g.t_atom, bonds, g.t_u1, g.t_u2,
-                                                                  gm.parts, gm.b0,
-                                                                  precision=self.precision))
+        core, gate = self._first_layer(gm, trips, [(atoms, [g.t_atom]), (bonds, [g.t_u1, g.t_u2])])
         raw = gm(core, gate)
         red = ops.segment_sum_graph(raw, g.t_u1, g.n_bonds, graph, "target", weight=env)
         new_bonds = ops.residual(_silu_chain(red, layer["node_ffn"], self.precision), bonds, layer["node_res"])
