@@ -454,18 +454,37 @@ __device__ __forceinline__ void mix_rows(const float (*xs)[C], const float* __re
     float acc[NS + NV];
 #pragma unroll
     for (int r = 0; r < NS + NV; ++r) acc[r] = 0.f;
-#pragma unroll 8
-    for (int cc = 0; cc < CQ; ++cc) {
+    // four input channels per step: one 16-byte shared-memory read of a row serves four FMAs (the row
+    // operands, not the FMA pipe, bound a one-channel loop); every accumulator still adds c in order
+    static_assert(CQ % 4 == 0, "a quarter of the channels must be a multiple of 4");
+#pragma unroll 2
+    for (int cc = 0; cc < CQ; cc += 4) {
         const int c = q * CQ + cc;
         if constexpr (NS > 0) {
-            const float w0 = W0[c * C + k];
+            float w0[4];
 #pragma unroll
-            for (int r = 0; r < NS; ++r) acc[r] = fmaf(xs[r][c], w0, acc[r]);
+            for (int j = 0; j < 4; ++j) w0[j] = W0[(c + j) * C + k];
+#pragma unroll
+            for (int r = 0; r < NS; ++r) {
+                const float4 x = *reinterpret_cast<const float4*>(&xs[r][c]);
+                acc[r] = fmaf(x.x, w0[0], acc[r]);
+                acc[r] = fmaf(x.y, w0[1], acc[r]);
+                acc[r] = fmaf(x.z, w0[2], acc[r]);
+                acc[r] = fmaf(x.w, w0[3], acc[r]);
+            }
         }
         if constexpr (NV > 0) {
-            const float w1 = W1[c * C + k];
+            float w1[4];
 #pragma unroll
-            for (int r = 0; r < NV; ++r) acc[NS + r] = fmaf(xv[r][c], w1, acc[NS + r]);
+            for (int j = 0; j < 4; ++j) w1[j] = W1[(c + j) * C + k];
+#pragma unroll
+            for (int r = 0; r < NV; ++r) {
+                const float4 x = *reinterpret_cast<const float4*>(&xv[r][c]);
+                acc[NS + r] = fmaf(x.x, w1[0], acc[NS + r]);
+                acc[NS + r] = fmaf(x.y, w1[1], acc[NS + r]);
+                acc[NS + r] = fmaf(x.z, w1[2], acc[NS + r]);
+                acc[NS + r] = fmaf(x.w, w1[3], acc[NS + r]);
+            }
         }
     }
 #pragma unroll

@@ -19,9 +19,12 @@ buffers, valid until the next ``run``.
 """
 from __future__ import annotations
 
+
 from dataclasses import dataclass
 
 import torch
+
+from fastmd_b200._capture import quiet_gc
 from torch import Tensor
 
 from .graph import GraphBatch, PaddingRule, self_loop_image
@@ -159,7 +162,7 @@ class BucketedGraphRunner:
         if self.pool is None:
             self.pool = torch.cuda.graph_pool_handle()
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, pool=self.pool):
+        with quiet_gc(), torch.cuda.graph(graph, pool=self.pool):
             energy, forces = self.model.energy_forces_fused(batch, n_systems=self.n_systems)
         self.captures += 1
         return {"graph": graph, "workspace": workspace, "energy": energy, "forces": forces, "u_cap": u_cap}

@@ -19,8 +19,11 @@ model's evaluation of a fresh build of the same positions.
 """
 from __future__ import annotations
 
+
 import numpy as np
 import torch
+
+from fastmd_b200._capture import quiet_gc
 
 from .graph import FixedCapacityGraphBuilder, fixed_capacity_exceeded
 from .model_graph import smallest_fitting_key, tier
@@ -100,7 +103,7 @@ class SkinTopologyRunner:
             if self.pool is None:
                 self.pool = torch.cuda.graph_pool_handle()
             graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, pool=self.pool):
+            with quiet_gc(), torch.cuda.graph(graph, pool=self.pool):
                 out = self._body(builder)
             entry.update(graph=graph, out=out)
             self.captures += 1

@@ -22,10 +22,13 @@ graph, fastmd_b200/model_graph.py) and ``eager`` (nothing captured).
 """
 from __future__ import annotations
 
+
 import math
 
 import numpy as np
 import torch
+
+from fastmd_b200._capture import quiet_gc
 from torch import Tensor
 
 from fastmd_b200.graph import (FLAG_CANDIDATE_OVERFLOW, FLAG_EDGE_OVERFLOW, FLAG_NONFINITE, FLAG_SKIN,
@@ -110,7 +113,7 @@ class WholeStepGraphRunner:
         torch.cuda.current_stream(self.device).wait_stream(side)
         self.integrator.load_snapshot(snapshot)
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
+        with quiet_gc(), torch.cuda.graph(graph):
             self._window_body()
         self.integrator.load_snapshot(snapshot)
         self.graph = graph
