@@ -35,6 +35,7 @@ _SIGNATURES: dict[str, list] = {
     "fmd_gather_cat": [POINTER(FmdCatPart), _I32, _I64, _P, _I64, _P, _P],
     "fmd_aligned_gather_cat3": [_P, _I64, _P, _I64, _I64, _P, _P, _I64, _I32, _P, _P, _P],
     "fmd_gather_rows_bwd": [_P, _I64, _I32, _I32, _P, _P, _I64, _P, _I64, _I32, _P],
+    "fmd_gather_rows_bwd_long": [_P, _I64, _I32, _I32, _P, _P, _I64, _P, _I64, _I32, _P],
     "fmd_copy_rows": [_P, _I64, _P, _I64, _I64, _I32, _P],
     "fmd_csr_offsets_sorted": [_P, _I64, _I64, _P, _P],
     "fmd_csr_build_workspace_bytes": [_I64, _I64, POINTER(c_size_t)],

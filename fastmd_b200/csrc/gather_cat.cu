@@ -220,6 +220,56 @@ __global__ void copy_rows_kernel(const float* __restrict__ src, int64_t lds, flo
 }
 
 // lanes per row slot: the smallest power of two holding the chunk's vectors
+// Long runs (tens to hundreds of rows per source row): a CTA of kLongWarps warps per (source row,
+// 128-column chunk); warp w sums rows w, w + kLongWarps, ... of the run (four rows' loads in flight), then
+// warp 0 adds the warps' partials in warp order. Deterministic; float4 columns only.
+constexpr int kLongWarps = 8;
+
+__global__ void __launch_bounds__(32 * kLongWarps) gather_rows_bwd_long_kernel(
+    const float* __restrict__ gout, int64_t ldgo, int col0, int width, const int64_t* __restrict__ perm,
+    const int64_t* __restrict__ off, int64_t n_src, float* __restrict__ grad, int64_t ldg, int accumulate) {
+    __shared__ float4 part[kLongWarps][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int width_v = width / 4;
+    const int n_col_chunks = (width_v + 31) / 32;
+    const int64_t n_tasks = n_src * n_col_chunks;
+    for (int64_t task = blockIdx.x; task < n_tasks; task += gridDim.x) {
+        const int64_t n = task / n_col_chunks;
+        const int v = int(task - n * n_col_chunks) * 32 + lane;
+        const bool col_ok = v < width_v;
+        const int64_t start = off[n], end = off[n + 1];
+        float4 acc = f4_zero();
+        int64_t j = start + warp;
+        for (; j + 3 * kLongWarps < end; j += 4 * kLongWarps) {
+            int64_t r[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) r[q] = perm ? perm[j + q * kLongWarps] : j + q * kLongWarps;
+            if (col_ok) {
+                float4 x[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) x[q] = ldg4(gout + r[q] * ldgo + col0 + v * 4);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) acc = f4_add(acc, x[q]);
+            }
+        }
+        for (; j < end; j += kLongWarps) {
+            const int64_t r = perm ? perm[j] : j;
+            if (col_ok) acc = f4_add(acc, ldg4(gout + r * ldgo + col0 + v * 4));
+        }
+        part[warp][lane] = acc;
+        __syncthreads();
+        if (warp == 0 && col_ok) {
+            float4 total = part[0][lane];
+#pragma unroll
+            for (int w = 1; w < kLongWarps; ++w) total = f4_add(total, part[w][lane]);
+            float* dst = grad + n * ldg + v * 4;
+            if (accumulate) total = f4_add(*reinterpret_cast<float4*>(dst), total);
+            st4(dst, total);
+        }
+        __syncthreads();
+    }
+}
+
 inline int lanes_for(int width_v) {
     int l = 1;
     while (l < width_v && l < 32) l <<= 1;
@@ -322,6 +372,22 @@ fmd_status fmd_gather_rows_bwd(const float* gout, int64_t ldgo, int32_t col0, in
     else
         gather_rows_bwd_kernel<1><<<grid, threads, 0, as_stream(stream)>>>(
             gout, ldgo, col0, width, perm, off, n_src, grad, ldg, accumulate, lanes);
+    return check_launch();
+}
+
+fmd_status fmd_gather_rows_bwd_long(const float* gout, int64_t ldgo, int32_t col0, int32_t width,
+                                   const int64_t* perm, const int64_t* off, int64_t n_src, float* grad, int64_t ldg,
+                                   int32_t accumulate, void* stream) {
+    if (gout == nullptr || off == nullptr || grad == nullptr || width < 0 || col0 < 0 || n_src < 0 ||
+        ldgo < col0 + width || ldg < width)
+        return FMD_ERR_INVALID_ARGUMENT;
+    if (n_src == 0 || width == 0) return FMD_OK;
+    if (!aligned16(gout) || !aligned16(grad) || ldgo % 4 || ldg % 4 || col0 % 4 || width % 4)
+        return FMD_ERR_UNSUPPORTED;
+    const int64_t tasks = n_src * ((width / 4 + 31) / 32);
+    const int grid = int(tasks < int64_t(kNumSMs) * 8 ? tasks : int64_t(kNumSMs) * 8);
+    gather_rows_bwd_long_kernel<<<grid, 32 * kLongWarps, 0, as_stream(stream)>>>(gout, ldgo, col0, width, perm, off,
+                                                                                 n_src, grad, ldg, accumulate);
     return check_launch();
 }
 

@@ -295,9 +295,31 @@ __global__ void line_envelope_bwd_kernel(const float* __restrict__ base, int64_t
         for (int side = 0; side < 2; ++side) {
             const int64_t* perm = side == 0 ? perm1 : perm2;
             const int64_t* off = side == 0 ? off1 : off2;
-            for (int64_t j = off[u]; j < off[u + 1]; ++j) {
+            const int col = side == 0 ? 3 : 1;
+            int64_t j = off[u];
+            const int64_t end = off[u + 1];
+            // four triplets' loads in flight, added in CSR order (the same sums as one at a time)
+            for (; j + 3 < end; j += 4) {
+                int64_t t[4], o[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) t[q] = perm[j + q];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    o[q] = lg[5 * t[q] + col];
+                    if (o[q] < 0 || o[q] >= n_bonds) o[q] = 0;
+                }
+                float4 x[4], y[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    x[q] = ldg4(grad + t[q] * ldg + 4 * v);
+                    y[q] = ldg4(base + o[q] * ldb + 4 * v);
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) acc = f4_add(acc, f4_mul(x[q], y[q]));
+            }
+            for (; j < end; ++j) {
                 const int64_t t = perm[j];
-                int64_t other = lg[5 * t + (side == 0 ? 3 : 1)];
+                int64_t other = lg[5 * t + col];
                 if (other < 0 || other >= n_bonds) other = 0;
                 acc = f4_add(acc, f4_mul(ldg4(grad + t * ldg + 4 * v), ldg4(base + other * ldb + 4 * v)));
             }

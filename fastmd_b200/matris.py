@@ -160,7 +160,9 @@ class _PackedGatherAddSilu(Function):
             n_src, ld = ctx.shapes[src]
             perm, off = segment_csr(idx, n_src)
             if n_src:
-                call("fmd_gather_rows_bwd", ptr(grad_p0), width, 0, width, ptr(perm), ptr(off), n_src,
+                # long runs (e.g. an atom's triplets): eight warps per source row
+                name = "fmd_gather_rows_bwd_long" if rows >= 64 * n_src else "fmd_gather_rows_bwd"
+                call(name, ptr(grad_p0), width, 0, width, ptr(perm), ptr(off), n_src,
                      grads[src].data_ptr() + 4 * col, ld, 0, s)
         return (grad_p0, None, None, None, *grads, *([None] * len(indices)))
 

@@ -104,6 +104,16 @@ FMD_API fmd_status fmd_gather_rows_bwd(const float* gout, int64_t ldgo, int32_t 
                                const int64_t* perm, const int64_t* off, int64_t n_src,
                                float* grad, int64_t ldg, int32_t accumulate, void* stream);
 
+/* fmd_gather_rows_bwd for long runs (tens to hundreds of rows gathered by
+ * each source row, e.g. the triplets of an atom): a CTA of 8 warps per
+ * source row and 128 columns, warp w summing rows w, w + 8, ... of the run,
+ * the partials added in warp order (deterministic; a different but fixed
+ * summation order from fmd_gather_rows_bwd). 16-byte aligned rows and
+ * widths, col0 and strides multiples of 4, else FMD_ERR_UNSUPPORTED. */
+FMD_API fmd_status fmd_gather_rows_bwd_long(const float* gout, int64_t ldgo, int32_t col0, int32_t width,
+                                            const int64_t* perm, const int64_t* off, int64_t n_src, float* grad,
+                                            int64_t ldg, int32_t accumulate, void* stream);
+
 /* Strided row copy dst[r, :w] = src[r, :w] (the aligned block's gradient). */
 FMD_API fmd_status fmd_copy_rows(const float* src, int64_t lds, float* dst, int64_t ldd, int64_t rows,
                          int32_t width, void* stream);

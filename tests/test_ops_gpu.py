@@ -160,3 +160,29 @@ def test_large_segment_sum_against_oracle(cuda):
     out = ops.csr_segment_sum(_t(V, cuda), segt, N, None, ops.csr_offsets(segt, N), True)
     ref = oops.segment_sum(V, seg, N)
     np.testing.assert_allclose(out.cpu().numpy(), ref, rtol=1e-5, atol=5e-5)
+
+
+def test_gather_rows_bwd_long_runs(cuda):
+    """fmd_gather_rows_bwd_long (eight warps per source row, for runs of tens to hundreds of rows) against
+    float64 row sums and against fmd_gather_rows_bwd, on sorted (identity) and permuted CSRs."""
+    from fastmd_b200._lib import call, ptr, stream
+    from fastmd_b200.ops import segment_csr
+
+    gen = np.random.default_rng(5)
+    rows, n_src, width = 17_850, 135, 256
+    for sorted_index in (True, False):
+        seg = gen.integers(0, n_src, rows)
+        if sorted_index:
+            seg = np.sort(seg)
+        idx = torch.from_numpy(seg.astype(np.int64)).to(cuda)
+        perm, off = segment_csr(idx, n_src)
+        gout = torch.from_numpy(gen.standard_normal((rows, width)).astype(np.float32)).to(cuda)
+        out = {}
+        for name in ("fmd_gather_rows_bwd_long", "fmd_gather_rows_bwd"):
+            grad = torch.full((n_src, width), float("nan"), device=cuda)
+            call(name, ptr(gout), width, 0, width, ptr(perm), ptr(off), n_src, ptr(grad), width, 0, stream(cuda))
+            out[name] = grad.cpu().numpy()
+        ref = np.zeros((n_src, width))
+        np.add.at(ref, seg, gout.cpu().numpy().astype(np.float64))
+        for grad in out.values():
+            assert np.abs(grad - ref).max() <= 2e-5 * np.abs(ref).max()
