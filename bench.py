@@ -60,7 +60,7 @@ def _args():
     p.add_argument("--steps-per-launch", type=int, default=10)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-ops", action="store_true", help="skip the config-2 op microbenchmark")
-    p.add_argument("--op", choices=["wide_gemm", "hbm_ops", "bond_graph", "nequip"], default=None,
+    p.add_argument("--op", choices=["wide_gemm", "hbm_ops", "bond_graph", "nequip", "matris"], default=None,
                    help="time one op alone (the profiling entry of profiles/): prints its own JSON line")
     p.add_argument("--rows", type=int, default=300_000, help="rows of --op wide_gemm")
     p.add_argument("--atoms", type=int, default=25_000, help="atoms of --op hbm_ops (config 2's box density)")
@@ -891,6 +891,12 @@ def _op(args):
         return _op_bond_graph(args)
     if args.op == "nequip":
         return _op_nequip(args)
+    if args.op == "matris":  # config 0 on the GPU: MatRIS-10M whole_step (``--steps`` up to 100 timed)
+        import torch
+
+        device = torch.device("cuda", 0)
+        flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+        return {"op": "matris_whole_step", **_config0_matris(args, device, flush)}
     import torch
 
     from fastmd_b200 import wide_gemm

@@ -274,57 +274,58 @@ __global__ void line_envelope_kernel(const float* __restrict__ base, int64_t ldb
     }
 }
 
-// grad_base[u] = sum over the triplets whose target bond is u (CSR perm1/off1) of g[t] * base[u2[t]], then
-// over those whose source bond is u (perm2/off2) of g[t] * base[u1[t]]: a warp per (bond, 128 columns),
-// the rows in CSR order (deterministic, no atomics)
-__global__ void line_envelope_bwd_kernel(const float* __restrict__ base, int64_t ldb, const int32_t* __restrict__ lg,
-                                         int64_t n_bonds, int width, const float* __restrict__ grad,
-                                         int64_t ldg, const int64_t* __restrict__ perm1,
-                                         const int64_t* __restrict__ off1, const int64_t* __restrict__ perm2,
-                                         const int64_t* __restrict__ off2, float* __restrict__ grad_base,
-                                         int64_t ldo) {
-    const int lane = threadIdx.x & 31;
+// grad_base[u] = sum over the triplets whose target bond is u (CSR perm1/off1) of g[t] * base[u2[t]], plus
+// over those whose source bond is u (perm2/off2) of g[t] * base[u1[t]]: a CTA of kEnvWarps warps per
+// (bond, 128 columns), warp w taking every kEnvWarps-th triplet of each side (two triplets' loads in flight),
+// the warp partials added in warp order (deterministic, no atomics)
+constexpr int kEnvWarps = 8;
+
+__global__ void __launch_bounds__(32 * kEnvWarps) line_envelope_bwd_kernel(
+    const float* __restrict__ base, int64_t ldb, const int32_t* __restrict__ lg, int64_t n_bonds, int width,
+    const float* __restrict__ grad, int64_t ldg, const int64_t* __restrict__ perm1, const int64_t* __restrict__ off1,
+    const int64_t* __restrict__ perm2, const int64_t* __restrict__ off2, float* __restrict__ grad_base, int64_t ldo) {
+    __shared__ float4 part[kEnvWarps][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int chunks = (width / 4 + 31) / 32;
-    const int64_t warp = (blockIdx.x * int64_t(blockDim.x) + threadIdx.x) >> 5;
-    const int64_t n_warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
-    for (int64_t task = warp; task < n_bonds * chunks; task += n_warps) {
+    for (int64_t task = blockIdx.x; task < n_bonds * chunks; task += gridDim.x) {
         const int64_t u = task / chunks;
         const int v = int(task - u * chunks) * 32 + lane;
-        if (v >= width / 4) continue;
+        const bool col_ok = v < width / 4;
         float4 acc = f4_zero();
         for (int side = 0; side < 2; ++side) {
             const int64_t* perm = side == 0 ? perm1 : perm2;
             const int64_t* off = side == 0 ? off1 : off2;
             const int col = side == 0 ? 3 : 1;
-            int64_t j = off[u];
             const int64_t end = off[u + 1];
-            // four triplets' loads in flight, added in CSR order (the same sums as one at a time)
-            for (; j + 3 < end; j += 4) {
-                int64_t t[4], o[4];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) t[q] = perm[j + q];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    o[q] = lg[5 * t[q] + col];
-                    if (o[q] < 0 || o[q] >= n_bonds) o[q] = 0;
+            int64_t j = off[u] + warp;
+            for (; j + kEnvWarps < end; j += 2 * kEnvWarps) {
+                const int64_t t0 = perm[j], t1 = perm[j + kEnvWarps];
+                int64_t o0 = lg[5 * t0 + col], o1 = lg[5 * t1 + col];
+                if (o0 < 0 || o0 >= n_bonds) o0 = 0;
+                if (o1 < 0 || o1 >= n_bonds) o1 = 0;
+                if (col_ok) {
+                    const float4 x0 = ldg4(grad + t0 * ldg + 4 * v), y0 = ldg4(base + o0 * ldb + 4 * v);
+                    const float4 x1 = ldg4(grad + t1 * ldg + 4 * v), y1 = ldg4(base + o1 * ldb + 4 * v);
+                    acc = f4_add(acc, f4_mul(x0, y0));
+                    acc = f4_add(acc, f4_mul(x1, y1));
                 }
-                float4 x[4], y[4];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    x[q] = ldg4(grad + t[q] * ldg + 4 * v);
-                    y[q] = ldg4(base + o[q] * ldb + 4 * v);
-                }
-#pragma unroll
-                for (int q = 0; q < 4; ++q) acc = f4_add(acc, f4_mul(x[q], y[q]));
             }
-            for (; j < end; ++j) {
+            for (; j < end; j += kEnvWarps) {
                 const int64_t t = perm[j];
-                int64_t other = lg[5 * t + col];
-                if (other < 0 || other >= n_bonds) other = 0;
-                acc = f4_add(acc, f4_mul(ldg4(grad + t * ldg + 4 * v), ldg4(base + other * ldb + 4 * v)));
+                int64_t o = lg[5 * t + col];
+                if (o < 0 || o >= n_bonds) o = 0;
+                if (col_ok) acc = f4_add(acc, f4_mul(ldg4(grad + t * ldg + 4 * v), ldg4(base + o * ldb + 4 * v)));
             }
         }
-        st4(grad_base + u * ldo + 4 * v, acc);
+        part[warp][lane] = acc;
+        __syncthreads();
+        if (warp == 0 && col_ok) {
+            float4 total = part[0][lane];
+#pragma unroll
+            for (int w = 1; w < kEnvWarps; ++w) total = f4_add(total, part[w][lane]);
+            st4(grad_base + u * ldo + 4 * v, total);
+        }
+        __syncthreads();
     }
 }
 
@@ -558,8 +559,9 @@ fmd_status fmd_matris_line_envelope_bwd(const float* base, int64_t ldb, const in
         grad_base == nullptr)
         return FMD_ERR_INVALID_ARGUMENT;
     if (!rows16(base, ldb) || !rows16(grad, ldg) || !rows16(grad_base, ldo)) return FMD_ERR_UNSUPPORTED;
-    const int chunks = (width / 4 + 31) / 32;
-    line_envelope_bwd_kernel<<<grid_for(n_bonds * chunks * 32, kThreads), kThreads, 0, as_stream(stream)>>>(
+    const int64_t tasks = n_bonds * ((width / 4 + 31) / 32);
+    const int grid = int(tasks < int64_t(kNumSMs) * 8 ? tasks : int64_t(kNumSMs) * 8);
+    line_envelope_bwd_kernel<<<grid, 32 * kEnvWarps, 0, as_stream(stream)>>>(
         base, ldb, line_graph, n_bonds, width, grad, ldg, perm1, off1, perm2, off2, grad_base, ldo);
     return check_launch();
 }

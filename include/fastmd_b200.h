@@ -910,7 +910,9 @@ FMD_API fmd_status fmd_matris_line_envelope(const float* base, int64_t ldb, cons
 /* Its backward, with no atomics: grad_base[u] = sum over the triplets whose
  * target bond is u (perm1/off1: the CSR of column 1) of grad[t] * base[u2[t]],
  * then over those whose source bond is u (perm2/off2, column 3) of grad[t] *
- * base[u1[t]], in CSR order; every row of grad_base [U, width] is written.
+ * base[u1[t]] (eight warps per bond, each taking every eighth triplet of
+ * a side, their partials added in warp order: deterministic); every row of
+ * grad_base [U, width] is written.
  * Replaces _line_envelope_bwd (triton_line_envelope.py:87). */
 FMD_API fmd_status fmd_matris_line_envelope_bwd(const float* base, int64_t ldb, const int32_t* line_graph,
                                                 int64_t n_bonds, int32_t width, const float* grad, int64_t ldg,
