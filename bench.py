@@ -65,6 +65,8 @@ def _args():
     p.add_argument("--rows", type=int, default=300_000, help="rows of --op wide_gemm")
     p.add_argument("--atoms", type=int, default=25_000, help="atoms of --op hbm_ops (config 2's box density)")
     p.add_argument("--reps", type=int, default=10, help="ABX3 supercell repeats of --op nequip (config 3: 10)")
+    p.add_argument("--kernels", action="store_true",
+                   help="--op matris: also list the step's kernels (CUPTI device times over one window)")
     return p.parse_args()
 
 
@@ -423,10 +425,25 @@ def _config0_matris(args, device, flush):
         md.runner.settle()
     windows = max(1, min(args.steps, 100) // S)
     ms = _timed_windows(md.runner, windows, flush, device) / (windows * S)
+    kernels = None
+    if getattr(args, "kernels", False):  # one window under CUPTI: per kernel name, launches and device time
+        from torch.profiler import ProfilerActivity, profile
+
+        torch.cuda.synchronize(device)
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            md.runner.launch()
+            torch.cuda.synchronize(device)
+        md.runner.settle()
+        rows = sorted(((e.device_time_total, e.count, e.key) for e in prof.key_averages()
+                       if e.device_time_total > 0), reverse=True)
+        total = sum(r[0] for r in rows)
+        kernels = {"window_steps": S, "kernel_us_per_step": total / S, "launches_per_step": sum(r[1] for r in rows) / S,
+                   "top": [{"kernel": k[:90], "us_per_step": round(t / S, 1), "launches_per_step": c / S,
+                            "share": round(t / total, 4)} for t, c, k in rows[:20]]}
     out = {"workload": "config0 on the GPU: 135-atom CsSnI3, MatRIS-10M (10 layers, 128 wide, energy head "
                        "256/256, seeded weights), NVT-NHC whole_step, 3xTF32 tcgen05 GEMMs",
            "ms_per_step": ms, "atom_steps_per_s": 135e3 / ms, "steps": windows * S,
-           "reference_published_h100_ms_per_step": 28.018}
+           "reference_published_h100_ms_per_step": 28.018, "kernels": kernels}
     if not args.no_cpu_baseline:
         from oracle.md import MatRISOracleMD
 
