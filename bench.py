@@ -554,15 +554,36 @@ def _roofline(md, device):
             6: (E * (16 + 12 + 12 + 4 * pc) + weights,
                 2.0 * E * sum(2 * (c.num_bessel * 64 + 2 * 64 * 64) + 64 * c.paths(L) * c.channels
                               for L in range(c.num_interactions)))}
+    # the node-side stages (2-layer model: node_fwd at layer 0, node_last and sender_node at layer 1); rows of
+    # C floats per atom read or written once, R rows of P_L C floats and 16 B of harmonics per edge, the
+    # C x C mixings once from HBM (per-element skip and product weights included)
+    C, Lz = c.channels, c.num_interactions - 1
+    mix = 4 * C * C
+    per_elem = 4 * c.num_elements * (2 * C * C + 9 * C)
+    if c.num_interactions == 2:
+        algo[2] = (N * 4 * 16 * C + 6 * mix + 4 * c.num_elements * 9 * C,
+                   2.0 * N * 4 * C * C * 4)
+        algo[3] = (N * (4 * 10 * C + 8) + 7 * mix + 4 * c.readout_hidden * C + per_elem,
+                   2.0 * N * C * C * (4 + 1 + 1 + 1 + 1 + 4) + 4.0 * N * c.readout_hidden * C)
+        algo[5] = (E * (4 * c.paths(Lz) * C + 16 + 4 + 4) + N * 4 * (4 * C + 4 * C + 4 * C + C) + 6 * mix
+                   + 4 * c.num_elements * 9 * C,
+                   2.0 * N * C * C * 4 * 3 + 2.0 * E * C * 12)
     bytes_, flops = algo.get(bit, (None, None))
     traffic = None
     tpath = ROOT / "profiles" / "traffic.json"
     if tpath.exists():
-        traffic = json.loads(tpath.read_text()).get(names[bit][0])
+        # DRAM bytes per launch from one ncu capture of the same stage; entries keyed by kernel and edge
+        # count scale with the edges processed (the per-edge rows dominate)
+        entry = json.loads(tpath.read_text()).get(names[bit][0])
+        if isinstance(entry, dict) and entry.get("edges"):
+            traffic = entry["dram_bytes"] * E / entry["edges"]
+        elif isinstance(entry, (int, float)):
+            traffic = entry
     out = {"kernel": names[bit][0], "bound": "hbm", "unit": "GB/s", "peak": hbm,
            "peak_source": f"{kind} (MEASURED_PEAKS.json hbm_gbs)" if kind == "measured" else "fallback 6650 GB/s",
-           "avg_launch_us": us, "stages_us": stages, "traffic": traffic,
-           "note": "135 atoms / 2,054 edges: every stage is latency-bound (see profiles/)"}
+           "avg_launch_us": us, "stages_us": stages, "traffic": traffic, "edges": E, "atoms": N,
+           "note": ("135 atoms / 2,054 edges: every stage is latency-bound" if N <= 135 else
+                    "node stages: gathers of edge rows and C x C channel mixings on the CUDA cores")}
     if bytes_ is not None:
         achieved = bytes_ / (us * 1e-6) / 1e9
         out.update({"achieved": achieved, "frac": achieved / hbm, "algorithmic_bytes_per_launch": bytes_,

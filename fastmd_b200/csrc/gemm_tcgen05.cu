@@ -34,11 +34,15 @@
 //               (tcgen05.st), double-buffered A operand
 //   warps 8-15  epilogue: TMEM -> registers, chunk sums, bias, residual,
 //               SiLU, stores; warp w reads TMEM lanes 32 (w % 4) .. +31 (its
-//               32 rows) and columns 64 ((w - 8) / 4) .. +63
+//               32 rows) and columns 64 ((w - 8) / 4) .. +63 (narrow tiles:
+//               32 ((w - 8) / 4) .. +31)
 // TMEM (512 columns): 3 chunk accumulators of 128 columns, then 2 A buffers
-// of 64 columns (x_hi k 0..31, x_lo k 0..31). Keeping A out of shared memory
-// halves the tensor core's shared-memory reads (B only), which at M = N = 128
-// in FP32 would otherwise use the whole shared-memory bandwidth.
+// of 64 columns (x_hi k 0..31, x_lo k 0..31); for n <= 64 (narrow) the
+// accumulators take 64 columns and 5 A buffers follow, so the splitter runs
+// stages ahead of the MMAs instead of one hand-off behind them, and the w
+// boxes hold n rows (rounded up to 16) instead of 128. Keeping A out of
+// shared memory halves the tensor core's shared-memory reads (B only), which
+// at M = N = 128 in FP32 would otherwise use the whole shared-memory bandwidth.
 // Every mbarrier wait is bounded (about a second): on expiry the CTA raises
 // FMD_FLAG_WAIT_TIMEOUT, waits (bounded) for its copies and MMAs in flight,
 // frees its TMEM and returns. No cluster launch and no multicast.
@@ -57,7 +61,7 @@ namespace {
 
 constexpr int kBM = 128, kBN = 128, kBK = 32, kChunkK = 64;
 static_assert(kBK == 32, "the stage MMA issue is written for 4 K-steps of 8");
-constexpr int kStages = 4, kAccBufs = 3, kABufs = 2;
+constexpr int kStages = 4, kAccBufs = 3, kABufs = 2, kNarrowABufs = 5;
 constexpr int kThreads = 512;
 constexpr int kSplitThreads = 128, kEpiThreads = 256;
 constexpr uint32_t kTileBytes = kBM * kBK * 4;    // 16 KB, one operand tile of one stage
@@ -66,14 +70,16 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAccCols = kBN;                // one chunk accumulator: 128 lanes x 128 fp32
 constexpr uint32_t kACols = 2 * kBK;              // one A buffer: x_hi then x_lo, 32 columns each
 constexpr uint32_t kABase = kAccBufs * kAccCols;  // 384
+constexpr uint32_t kNarrowAccCols = 64;           // n <= 64: one chunk accumulator of 64 columns
 static_assert(kABase + kABufs * kACols <= kTmemCols, "TMEM budget");
+static_assert(kAccBufs * kNarrowAccCols + kNarrowABufs * kACols <= kTmemCols, "TMEM budget (narrow)");
 constexpr unsigned long long kWaitNs = 1000000000ull;
 
 struct Ctrl {
     uint64_t full[kStages];        // TMA bytes landed (1 arrival + tx)
     uint64_t empty[kStages];       // MMAs of the stage done (tcgen05.commit)
-    uint64_t a_full[kABufs];       // x_hi/x_lo of a stage in TMEM (kSplitThreads arrivals)
-    uint64_t a_empty[kABufs];      // MMAs reading that A buffer done (tcgen05.commit)
+    uint64_t a_full[kNarrowABufs];   // x_hi/x_lo of a stage in TMEM (kSplitThreads arrivals)
+    uint64_t a_empty[kNarrowABufs];  // MMAs reading that A buffer done (tcgen05.commit)
     uint64_t acc_full[kAccBufs];   // chunk accumulator complete (tcgen05.commit)
     uint64_t acc_empty[kAccBufs];  // chunk accumulator read out (kEpiThreads arrivals)
     uint64_t drain;                // MMAs in flight on abort
@@ -101,6 +107,7 @@ struct WideArgs {
     int32_t in_silu;          // SiLU on the x operand before the split
     int32_t vec_c, vec_y;     // 16-byte row access valid
     int32_t tma_y;         // y stored through tmap_y (else direct stores)
+    uint32_t w_box_bytes;  // bytes of one w_hi / w_lo box (128 B per row of the box)
 };
 
 // ------------------------------------------------------------- PTX wrappers
@@ -379,6 +386,92 @@ __device__ __forceinline__ void finish_values(const WideArgs& g, int64_t row, in
     }
 }
 
+// The epilogue warps: warp (q, half) reads TMEM lanes 32 q .. +31 (its 32 rows) and the 32 PIECES
+// columns from 32 PIECES half of each chunk accumulator (PIECES = 2: 128-column tiles; 1: narrow tiles of
+// at most 64 columns), sums the chunks in FP32 (from zeros, as the reference starts from a zero
+// accumulator), finishes the values and stores them (32 x 32 TMA boxes staged in shared memory, or
+// direct row stores).
+template <int PIECES>
+__device__ __forceinline__ void epilogue_role(const WideArgs& g, const CUtensorMap* tmap_y, Ctrl& ctl,
+                                              volatile int32_t* abort, uint32_t tmem, unsigned char* epi_smem,
+                                              int warp, int lane, int tiles, int n_tiles, int chunks,
+                                              uint32_t acc_cols) {
+    constexpr int W = 32 * PIECES;
+    const int q = warp & 3, half = (warp - 8) >> 2;
+    int cb = 0;
+    uint32_t cph = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+        const int64_t row = int64_t(t / n_tiles) * kBM + q * 32 + lane;
+        const int col0 = (t % n_tiles) * kBN + half * W;
+        float acc[W];
+#pragma unroll
+        for (int j = 0; j < W; ++j) acc[j] = 0.0f;
+        bool ok = true;
+        for (int ch = 0; ch < chunks; ++ch) {
+            const bool got = mbar_wait(&ctl.acc_full[cb], cph, abort);
+            if (!__all_sync(0xffffffffu, got)) {  // warp-uniform: tcgen05.ld is .sync.aligned
+                *abort = 1;
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t ta = tmem + (uint32_t(q * 32) << 16) + uint32_t(cb) * acc_cols + uint32_t(half * W);
+#pragma unroll
+            for (int part = 0; part < 2 * PIECES; ++part) {
+                float v[16];
+                tmem_ld16(ta + uint32_t(part * 16), v);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) acc[part * 16 + j] += v[j];
+            }
+            tc_fence_before();
+            mbar_arrive(&ctl.acc_empty[cb]);
+            advance(cb, cph, kAccBufs);
+        }
+        if (!ok) break;
+        if (g.tma_y) {
+            // stage each 32 x 32 piece in this warp's box (row = lane, 128-byte swizzle) and let
+            // TMA store it: whole lines to L2 instead of 16-byte pieces of 32 rows
+            float* box = reinterpret_cast<float*>(epi_smem + (warp - 8) * kEpiBoxBytes);
+            const int row0 = int(row - lane);
+#pragma unroll
+            for (int piece = 0; piece < PIECES; ++piece) {
+                float o[32];
+                finish_values(g, row, col0 + piece * 32, acc + piece * 32, o);
+                if (lane == 0) bulk_wait_read_all();  // the previous store has read the box
+                __syncwarp();
+                float4* b4 = reinterpret_cast<float4*>(box + lane * 32);
+#pragma unroll
+                for (int c = 0; c < 8; ++c)
+                    b4[c ^ (lane & 7)] = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0 && row0 < g.m && col0 + piece * 32 < g.n)  // boxes with no element in y skipped
+                    tma_store_2d(tmap_y, box, col0 + piece * 32, row0);
+            }
+        } else if (row < g.m) {
+            float* yr = g.y + row * g.ldy;
+#pragma unroll
+            for (int piece = 0; piece < PIECES; ++piece) {
+                float o[32];
+                finish_values(g, row, col0 + piece * 32, acc + piece * 32, o);
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                    const int col = col0 + piece * 32 + j;
+                    if (col + 4 <= g.n && g.vec_y) {
+                        *reinterpret_cast<float4*>(yr + col) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
+                    } else {
+#pragma unroll
+                        for (int u = 0; u < 4; ++u)
+                            if (col + u < g.n) yr[col + u] = o[j + u];
+                    }
+                }
+            }
+        }
+    }
+    if (g.tma_y && lane == 0) bulk_wait_all();  // stores complete before the CTA exits
+}
+
+template <bool NARROW>
 __global__ void __launch_bounds__(kThreads, 1)
     wide_gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_wh,
                             const __grid_constant__ CUtensorMap tmap_wl, const __grid_constant__ CUtensorMap tmap_y,
@@ -396,13 +489,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int k_stages = (g.k + kBK - 1) / kBK;
     const int chunks = (g.k + kChunkK - 1) / kChunkK;
     constexpr int kStagesPerChunk = kChunkK / kBK;
+    constexpr int a_bufs = NARROW ? kNarrowABufs : kABufs;
+    constexpr uint32_t acc_cols = NARROW ? kNarrowAccCols : kAccCols;
+    constexpr uint32_t a_base = kAccBufs * acc_cols;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&ctl.full[s], 1);
             mbar_init(&ctl.empty[s], 1);
         }
-        for (int b = 0; b < kABufs; ++b) {
+        for (int b = 0; b < kNarrowABufs; ++b) {
             mbar_init(&ctl.a_full[b], kSplitThreads);
             mbar_init(&ctl.a_empty[b], 1);
         }
@@ -440,7 +536,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     unsigned char* st = ring + s * kStageBytes;
-                    mbar_expect_tx(&ctl.full[s], kStageBytes);
+                    mbar_expect_tx(&ctl.full[s], kTileBytes + 2 * g.w_box_bytes);
                     tma_load_2d(st, &tmap_x, &ctl.full[s], ks * kBK, m0);
                     tma_load_2d(st + kTileBytes, &tmap_wh, &ctl.full[s], ks * kBK, n0);
                     tma_load_2d(st + 2 * kTileBytes, &tmap_wl, &ctl.full[s], ks * kBK, n0);
@@ -474,7 +570,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t d = tmem + uint32_t(cb) * kAccCols;
+                    const uint32_t d = tmem + uint32_t(cb) * acc_cols;
                     const int ks_end = min(ks + kStagesPerChunk, k_stages);
                     uint32_t acc = 0;
                     for (; ks < ks_end; ++ks) {
@@ -485,7 +581,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tc_fence_after();
                         const uint32_t base = ring_addr + uint32_t(s) * kStageBytes;
                         const uint64_t wh = sw128_desc(base + kTileBytes), wl = sw128_desc(base + 2 * kTileBytes);
-                        const uint32_t xh = tmem + kABase + uint32_t(sa) * kACols, xl = xh + kBK;
+                        const uint32_t xh = tmem + a_base + uint32_t(sa) * kACols, xl = xh + kBK;
                         // the small cross terms first: x_lo w_hi, x_hi w_lo, then x_hi w_hi
                         if (acc)
                             tc_mma_k32_ts<1>(d, xl, wh, idesc);
@@ -498,7 +594,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tc_commit(&ctl.empty[s]);     // the stage's shared memory is free once these are done
                         tc_commit(&ctl.a_empty[sa]);  // and so is its A buffer
                         advance(s, ph, kStages);
-                        advance(sa, aph, kABufs);
+                        advance(sa, aph, a_bufs);
                     }
                     if (!ok) break;
                     tc_commit(&ctl.acc_full[cb]);
@@ -552,89 +648,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t ta = tmem + lane_addr + kABase + uint32_t(sa) * kACols;
+                const uint32_t ta = tmem + lane_addr + a_base + uint32_t(sa) * kACols;
                 tmem_st32(ta, h, false);
                 tmem_st32(ta + kBK, v, true);
                 tc_fence_before();
                 mbar_arrive(&ctl.a_full[sa]);
                 advance(s, ph, kStages);
-                advance(sa, aph, kABufs);
+                advance(sa, aph, a_bufs);
             }
         }
     } else if (warp >= 8) {
         // --------------------------------------------------------- epilogue
-        const int q = warp & 3, half = (warp - 8) >> 2;
-        int cb = 0;
-        uint32_t cph = 0;
-        for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-            const int64_t row = int64_t(t / n_tiles) * kBM + q * 32 + lane;
-            const int col0 = (t % n_tiles) * kBN + half * 64;
-            float acc[64];  // zeros + chunk sums, as the reference starts from a zero accumulator
-#pragma unroll
-            for (int j = 0; j < 64; ++j) acc[j] = 0.0f;
-            bool ok = true;
-            for (int ch = 0; ch < chunks; ++ch) {
-                const bool got = mbar_wait(&ctl.acc_full[cb], cph, abort);
-                if (!__all_sync(0xffffffffu, got)) {  // warp-uniform: tcgen05.ld is .sync.aligned
-                    *abort = 1;
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t ta = tmem + (uint32_t(q * 32) << 16) + uint32_t(cb) * kAccCols + uint32_t(half * 64);
-#pragma unroll
-                for (int part = 0; part < 4; ++part) {
-                    float v[16];
-                    tmem_ld16(ta + uint32_t(part * 16), v);
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) acc[part * 16 + j] += v[j];
-                }
-                tc_fence_before();
-                mbar_arrive(&ctl.acc_empty[cb]);
-                advance(cb, cph, kAccBufs);
-            }
-            if (!ok) break;
-            if (g.tma_y) {
-                // stage each 32 x 32 piece in this warp's box (row = lane, 128-byte swizzle) and let
-                // TMA store it: whole lines to L2 instead of 16-byte pieces of 32 rows
-                float* box = reinterpret_cast<float*>(epi_smem + (warp - 8) * kEpiBoxBytes);
-                const int row0 = int(row - lane);
-#pragma unroll
-                for (int piece = 0; piece < 2; ++piece) {
-                    float o[32];
-                    finish_values(g, row, col0 + piece * 32, acc + piece * 32, o);
-                    if (lane == 0) bulk_wait_read_all();  // the previous store has read the box
-                    __syncwarp();
-                    float4* b4 = reinterpret_cast<float4*>(box + lane * 32);
-#pragma unroll
-                    for (int c = 0; c < 8; ++c)
-                        b4[c ^ (lane & 7)] = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    __syncwarp();
-                    if (lane == 0 && row0 < g.m && col0 + piece * 32 < g.n)  // boxes with no element in y skipped
-                        tma_store_2d(&tmap_y, box, col0 + piece * 32, row0);
-                }
-            } else if (row < g.m) {
-                float* yr = g.y + row * g.ldy;
-#pragma unroll
-                for (int piece = 0; piece < 2; ++piece) {
-                    float o[32];
-                    finish_values(g, row, col0 + piece * 32, acc + piece * 32, o);
-#pragma unroll
-                    for (int j = 0; j < 32; j += 4) {
-                        const int col = col0 + piece * 32 + j;
-                        if (col + 4 <= g.n && g.vec_y) {
-                            *reinterpret_cast<float4*>(yr + col) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
-                        } else {
-#pragma unroll
-                            for (int u = 0; u < 4; ++u)
-                                if (col + u < g.n) yr[col + u] = o[j + u];
-                        }
-                    }
-                }
-            }
-        }
-        if (g.tma_y && lane == 0) bulk_wait_all();  // stores complete before the CTA exits
+        epilogue_role<NARROW ? 1 : 2>(g, &tmap_y, ctl, abort, tmem, epi_smem, warp, lane, tiles, n_tiles, chunks,
+                                      acc_cols);
     }
 
     tc_fence_before();
@@ -806,8 +832,11 @@ fmd_status device_info(DeviceInfo* out) {
         d.sm100 = major == 10;
         d.sms = sms;
         if (d.sm100) {
-            err = cudaFuncSetAttribute(wide_gemm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            err = cudaFuncSetAttribute(wide_gemm_tf32x3_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        int(kSmemBytes));
+            if (err == cudaSuccess)
+                err = cudaFuncSetAttribute(wide_gemm_tf32x3_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           int(kSmemBytes));
             if (err != cudaSuccess) return record_cuda_error(err);
         }
         d.ready = true;
@@ -881,10 +910,13 @@ fmd_status fmd_gemm_tf32x3(const float* x, int64_t ldx, const float* w_hi, const
         if (err == cudaSuccess) err = cudaSetDevice(dev_index);
         if (err != cudaSuccess) return record_cuda_error(err);
     }
+    // n <= 64: one narrow column tile; the w boxes hold its rows rounded up to 16 (the MMA's N)
+    const bool narrow = n <= int32_t(kNarrowAccCols);
+    const uint32_t w_rows = narrow ? uint32_t((n + 15) & ~15) : uint32_t(kBN);
     CUtensorMap tx, twh, twl;
     CUresult r = encode_operand(drv.encode, &tx, x, m, k, ldx);
-    if (r == CUDA_SUCCESS) r = encode_operand(drv.encode, &twh, w_hi, n, k, ldw);
-    if (r == CUDA_SUCCESS) r = encode_operand(drv.encode, &twl, w_lo, n, k, ldw);
+    if (r == CUDA_SUCCESS) r = encode_operand(drv.encode, &twh, w_hi, n, k, ldw, w_rows);
+    if (r == CUDA_SUCCESS) r = encode_operand(drv.encode, &twl, w_lo, n, k, ldw, w_rows);
     if (r != CUDA_SUCCESS) return record_error_text(FMD_ERR_CUDA, "cuTensorMapEncodeTiled failed, CUresult", r);
     // y through TMA stores (32 x 32 boxes) when its base and row stride allow it
     CUtensorMap ty;
@@ -907,8 +939,12 @@ fmd_status fmd_gemm_tf32x3(const float* x, int64_t ldx, const float* w_hi, const
     g.vec_c = c != nullptr && aligned16(c) && (ldc & 3) == 0;
     g.vec_y = aligned16(y) && (ldy & 3) == 0;
     g.tma_y = tma_y;
+    g.w_box_bytes = w_rows * uint32_t(kBK * sizeof(float));
     const int grid = int(tiles < dev.sms ? tiles : dev.sms);
-    wide_gemm_tf32x3_kernel<<<grid, kThreads, kSmemBytes, as_stream(stream)>>>(tx, twh, twl, ty, g);
+    if (narrow)
+        wide_gemm_tf32x3_kernel<true><<<grid, kThreads, kSmemBytes, as_stream(stream)>>>(tx, twh, twl, ty, g);
+    else
+        wide_gemm_tf32x3_kernel<false><<<grid, kThreads, kSmemBytes, as_stream(stream)>>>(tx, twh, twl, ty, g);
     return check_launch();
 }
 

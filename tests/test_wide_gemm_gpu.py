@@ -55,7 +55,9 @@ def test_tf32_split_bitwise():
 
 
 @pytest.mark.parametrize("m,n,k", [(1, 1, 1), (5, 7, 3), (129, 64, 64), (300, 128, 256), (1000, 256, 264),
-                                   (257, 264, 256), (4097, 96, 100), (700, 200, 1000)])
+                                   (257, 264, 256), (4097, 96, 100), (700, 200, 1000),
+                                   # narrow tiles (n <= 64: 64-column accumulators, five A buffers, n-row w boxes)
+                                   (40000, 64, 512), (2000, 33, 100), (700, 16, 40), (3000, 48, 64)])
 def test_linear_matches_oracle(m, n, k):
     from fastmd_b200 import wide_gemm
 
