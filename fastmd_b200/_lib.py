@@ -101,7 +101,9 @@ _SIGNATURES: dict[str, list] = {
     "fmd_nequip_edge_basis": [_P, _P, _P, _P, _P, _P, _I64, c_float, _I32, _I32, _P, _P, _P, _P],
     "fmd_nequip_edge_basis_bwd": [_P, _P, _P, _P, _P, _I64, c_float, _I32, _I32, _P, _P],
     "fmd_nequip_conv": [_P, _P, _P, _P, _P, _P, _I64, c_float, _P, _P],
-    "fmd_nequip_conv_bwd": [_P, _P, _P, _P, _P, _P, _P, _P, _I64, c_float, _P, _P, _P, _P, _P],
+    "fmd_nequip_conv_bwd": [_P, _P, _P, _P, _P, _P, _P, _P, _I64, c_float, _P, _P, _P, _P, _I32, _P],
+    "fmd_edge_forces": [_P, _P, _P, _P, _P, _I64, _P, _P],
+    "fmd_zero": [_P, _I64, _P],
     "fmd_nequip_self_connection": [_P, _P, _P, _P, _P, _P, _P, _I64, _I32, _P, _P, _P, _P],
     "fmd_nequip_gate": [_P, _P, _P, _P, _P, _P, _I64, _P, _P, _P, _P],
     "fmd_nequip_gate_bwd": [_P, _P, _P, _P, _P, _P, _I64, _P, _P, _P, _P],

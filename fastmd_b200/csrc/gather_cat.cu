@@ -391,6 +391,13 @@ fmd_status fmd_gather_rows_bwd_long(const float* gout, int64_t ldgo, int32_t col
     return check_launch();
 }
 
+fmd_status fmd_zero(void* dst, int64_t bytes, void* stream) {
+    if (bytes < 0 || (bytes > 0 && dst == nullptr)) return FMD_ERR_INVALID_ARGUMENT;
+    if (bytes == 0) return FMD_OK;
+    const cudaError_t err = cudaMemsetAsync(dst, 0, size_t(bytes), as_stream(stream));
+    return err == cudaSuccess ? FMD_OK : record_cuda_error(err);
+}
+
 fmd_status fmd_copy_rows(const float* src, int64_t lds, float* dst, int64_t ldd, int64_t rows,
                          int32_t width, void* stream) {
     if (src == nullptr || dst == nullptr || rows < 0 || width < 0 || lds < width || ldd < width)

@@ -21,28 +21,32 @@
 // inputs only, not on m, its tile or the grid.
 //
 // One persistent CTA per SM (512 threads) walks 128 x 128 output tiles, N
-// fastest (the column tiles of a row block run together and share x in L2):
-//   warp 0      TMA producer: x, w_hi, w_lo tiles [128 rows x 32 k] per K
-//               stage into a 4-stage shared-memory ring, 128-byte swizzle,
-//               zero fill past m, n and k
-//   warp 1      TMEM owner and MMA issuer (one thread): per stage 4 K-steps
-//               of 8, three products each, M = 128, N = 128 (or the tile's
-//               width); A (x_hi / x_lo) from TMEM, B (w) from shared memory
-//   warps 4-7   splitter: row r of the x tile (one thread per row, reading
-//               the swizzled tile) -> x_hi, x_lo in registers (computed while
-//               the A buffer's previous MMAs still run) -> TMEM lane r
-//               (tcgen05.st), double-buffered A operand
+// fastest (the column tiles of a row block run together and share x in L2).
+// A stage is 64 of K, one chunk:
+//   warp 0      TMA producer: x, w_hi, w_lo as two boxes [128 rows x 32 k]
+//               each per stage into a 2-stage shared-memory ring (3 stages
+//               for narrow tiles), 128-byte swizzle, zero fill past m, n, k
+//   warp 1      TMEM owner and MMA issuer (one thread): per stage 8 K-steps
+//               of 8, three products each, into the stage's own chunk
+//               accumulator, M = 128, N = 128 (or the tile's width); A
+//               (x_hi / x_lo) from TMEM, B (w) from shared memory; one commit
+//               releases the stage's shared memory and A buffer, one its
+//               accumulator
+//   warps 4-7   splitter: row r of the x boxes (one thread per row, reading
+//               the swizzled tile) -> x_hi, x_lo -> TMEM lane r (tcgen05.st),
+//               double-buffered A operand
 //   warps 8-15  epilogue: TMEM -> registers, chunk sums, bias, residual,
 //               SiLU, stores; warp w reads TMEM lanes 32 (w % 4) .. +31 (its
 //               32 rows) and columns 64 ((w - 8) / 4) .. +63 (narrow tiles:
 //               32 ((w - 8) / 4) .. +31)
-// TMEM (512 columns): 3 chunk accumulators of 128 columns, then 2 A buffers
-// of 64 columns (x_hi k 0..31, x_lo k 0..31); for n <= 64 (narrow) the
-// accumulators take 64 columns and 5 A buffers follow, so the splitter runs
-// stages ahead of the MMAs instead of one hand-off behind them, and the w
-// boxes hold n rows (rounded up to 16) instead of 128. Keeping A out of
-// shared memory halves the tensor core's shared-memory reads (B only), which
-// at M = N = 128 in FP32 would otherwise use the whole shared-memory bandwidth.
+// TMEM (512 columns): 2 chunk accumulators of 128 columns, then 2 A buffers
+// of 128 columns (x_hi k 0..63, x_lo k 0..63); for n <= 64 (narrow) 3
+// accumulators of 64 columns, and the w boxes hold n rows (rounded up to 16)
+// instead of 128. The single issuing thread pays a fixed cost per tcgen05
+// instruction whatever the MMA's N (measured: about 64 cycles per MMA, twice
+// that per commit, a few hundred per stage of waits), so the stage is as long
+// as the shared memory allows. Keeping A out of shared memory halves the
+// tensor core's shared-memory reads (B only).
 // Every mbarrier wait is bounded (about a second): on expiry the CTA raises
 // FMD_FLAG_WAIT_TIMEOUT, waits (bounded) for its copies and MMAs in flight,
 // frees its TMEM and returns. No cluster launch and no multicast.
@@ -59,30 +63,39 @@
 namespace fmd {
 namespace {
 
-constexpr int kBM = 128, kBN = 128, kBK = 32, kChunkK = 64;
-static_assert(kBK == 32, "the stage MMA issue is written for 4 K-steps of 8");
-constexpr int kStages = 4, kAccBufs = 3, kABufs = 2, kNarrowABufs = 5;
+// A stage is 64 of K: two TMA boxes of 32 (the 128-byte swizzle width) per operand. The single issuing
+// thread pays a fixed cost per tcgen05 instruction (about 64 cycles per MMA and twice that per commit,
+// whatever the MMA's N) plus a few hundred cycles per stage of waits and bookkeeping, so a stage of 24
+// MMAs and 2 commits (its shared memory and A buffer released by one commit, the chunk accumulator by
+// the other) keeps the tensor pipe fed where stages of 12 MMAs and 2.5 commits could not.
+constexpr int kBM = 128, kBN = 128, kBK = 32, kStageK = 2 * kBK, kChunkK = kStageK;
+static_assert(kBK == 32, "the stage MMA issue is written for 4 K-steps of 8 per box");
+constexpr int kStages = 2, kNarrowStages = 3, kMaxStages = 3;
+constexpr int kAccBufs = 2, kNarrowAccBufs = 3, kMaxAccBufs = 3, kABufs = 2;
+static_assert(kABufs == 2, "the splitter alternates two A buffers");
 constexpr int kThreads = 512;
 constexpr int kSplitThreads = 128, kEpiThreads = 256;
-constexpr uint32_t kTileBytes = kBM * kBK * 4;    // 16 KB, one operand tile of one stage
-constexpr uint32_t kStageBytes = 3 * kTileBytes;  // x (raw), w_hi, w_lo
+constexpr uint32_t kTileBytes = kBM * kBK * 4;             // 16 KB: one box of x (or of a 128-row w)
+constexpr uint32_t kStageBytes = 2 * 3 * kTileBytes;        // x, w_hi, w_lo: two boxes each (96 KB)
+// narrow tiles (n <= 64): w boxes of at most 64 rows, so 3 stages fit where 2 did
+constexpr uint32_t kNarrowWBytes = 64 * kBK * 4;                             // 8 KB
+constexpr uint32_t kNarrowStageBytes = 2 * (kTileBytes + 2 * kNarrowWBytes);  // 64 KB
+static_assert(kNarrowStages * kNarrowStageBytes <= kStages * kStageBytes, "narrow ring within the wide ring");
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kAccCols = kBN;                // one chunk accumulator: 128 lanes x 128 fp32
-constexpr uint32_t kACols = 2 * kBK;              // one A buffer: x_hi then x_lo, 32 columns each
-constexpr uint32_t kABase = kAccBufs * kAccCols;  // 384
-constexpr uint32_t kNarrowAccCols = 64;           // n <= 64: one chunk accumulator of 64 columns
-static_assert(kABase + kABufs * kACols <= kTmemCols, "TMEM budget");
-static_assert(kAccBufs * kNarrowAccCols + kNarrowABufs * kACols <= kTmemCols, "TMEM budget (narrow)");
+constexpr uint32_t kAccCols = kBN;         // one chunk accumulator: 128 lanes x 128 fp32
+constexpr uint32_t kACols = 2 * kStageK;   // one A buffer: x_hi then x_lo, 64 columns each
+constexpr uint32_t kNarrowAccCols = 64;    // n <= 64: one chunk accumulator of 64 columns
+static_assert(kAccBufs * kAccCols + kABufs * kACols <= kTmemCols, "TMEM budget");
+static_assert(kNarrowAccBufs * kNarrowAccCols + kABufs * kACols <= kTmemCols, "TMEM budget (narrow)");
 constexpr unsigned long long kWaitNs = 1000000000ull;
 
 struct Ctrl {
-    uint64_t full[kStages];        // TMA bytes landed (1 arrival + tx)
-    uint64_t empty[kStages];       // MMAs of the stage done (tcgen05.commit)
-    uint64_t a_full[kNarrowABufs];   // x_hi/x_lo of a stage in TMEM (kSplitThreads arrivals)
-    uint64_t a_empty[kNarrowABufs];  // MMAs reading that A buffer done (tcgen05.commit)
-    uint64_t acc_full[kAccBufs];   // chunk accumulator complete (tcgen05.commit)
-    uint64_t acc_empty[kAccBufs];  // chunk accumulator read out (kEpiThreads arrivals)
-    uint64_t drain;                // MMAs in flight on abort
+    uint64_t full[kMaxStages];       // TMA bytes landed (1 arrival + tx)
+    uint64_t empty[kMaxStages];      // MMAs of the stage done (tcgen05.commit): its shared memory and its A buffer
+    uint64_t a_full[kABufs];         // x_hi/x_lo of a stage in TMEM (kSplitThreads arrivals)
+    uint64_t acc_full[kMaxAccBufs];  // chunk accumulator complete (tcgen05.commit)
+    uint64_t acc_empty[kMaxAccBufs]; // chunk accumulator read out (kEpiThreads arrivals)
+    uint64_t drain;                  // MMAs in flight on abort
     uint32_t tmem_base;
     int32_t abort;
 };
@@ -391,7 +404,7 @@ __device__ __forceinline__ void finish_values(const WideArgs& g, int64_t row, in
 // at most 64 columns), sums the chunks in FP32 (from zeros, as the reference starts from a zero
 // accumulator), finishes the values and stores them (32 x 32 TMA boxes staged in shared memory, or
 // direct row stores).
-template <int PIECES>
+template <int PIECES, int ACC_BUFS>
 __device__ __forceinline__ void epilogue_role(const WideArgs& g, const CUtensorMap* tmap_y, Ctrl& ctl,
                                               volatile int32_t* abort, uint32_t tmem, unsigned char* epi_smem,
                                               int warp, int lane, int tiles, int n_tiles, int chunks,
@@ -425,7 +438,7 @@ __device__ __forceinline__ void epilogue_role(const WideArgs& g, const CUtensorM
             }
             tc_fence_before();
             mbar_arrive(&ctl.acc_empty[cb]);
-            advance(cb, cph, kAccBufs);
+            advance(cb, cph, ACC_BUFS);
         }
         if (!ok) break;
         if (g.tma_y) {
@@ -479,6 +492,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ unsigned char smem_raw[];
     unsigned char* ring = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                            ~uintptr_t(1023));
+    constexpr int stages = NARROW ? kNarrowStages : kStages;
+    constexpr uint32_t stage_bytes = NARROW ? kNarrowStageBytes : kStageBytes;
+    // a stage: [x box 0][x box 1][w_hi box 0][w_hi box 1][w_lo box 0][w_lo box 1]
+    constexpr uint32_t w_box = NARROW ? kNarrowWBytes : kTileBytes;
+    constexpr uint32_t wh_off = 2 * kTileBytes, wl_off = 2 * kTileBytes + 2 * w_box;
     unsigned char* epi_smem = ring + kStages * kStageBytes;
     Ctrl& ctl = *reinterpret_cast<Ctrl*>(epi_smem + kEpiBytes);
     volatile int32_t* abort = &ctl.abort;
@@ -486,23 +504,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int m_tiles = int((g.m + kBM - 1) / kBM);
     const int n_tiles = (g.n + kBN - 1) / kBN;
     const int tiles = m_tiles * n_tiles;
-    const int k_stages = (g.k + kBK - 1) / kBK;
-    const int chunks = (g.k + kChunkK - 1) / kChunkK;
-    constexpr int kStagesPerChunk = kChunkK / kBK;
-    constexpr int a_bufs = NARROW ? kNarrowABufs : kABufs;
+    const int k_stages = (g.k + kStageK - 1) / kStageK;
+    const int chunks = k_stages;  // a chunk accumulator per stage
+    constexpr int acc_bufs = NARROW ? kNarrowAccBufs : kAccBufs;
     constexpr uint32_t acc_cols = NARROW ? kNarrowAccCols : kAccCols;
-    constexpr uint32_t a_base = kAccBufs * acc_cols;
+    constexpr uint32_t a_base = acc_bufs * acc_cols;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < stages; ++s) {
             mbar_init(&ctl.full[s], 1);
             mbar_init(&ctl.empty[s], 1);
         }
-        for (int b = 0; b < kNarrowABufs; ++b) {
-            mbar_init(&ctl.a_full[b], kSplitThreads);
-            mbar_init(&ctl.a_empty[b], 1);
-        }
-        for (int b = 0; b < kAccBufs; ++b) {
+        for (int b = 0; b < kABufs; ++b) mbar_init(&ctl.a_full[b], kSplitThreads);
+        for (int b = 0; b < acc_bufs; ++b) {
             mbar_init(&ctl.acc_full[b], 1);
             mbar_init(&ctl.acc_empty[b], kEpiThreads);
         }
@@ -535,21 +549,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ok = false;
                         break;
                     }
-                    unsigned char* st = ring + s * kStageBytes;
-                    mbar_expect_tx(&ctl.full[s], kTileBytes + 2 * g.w_box_bytes);
-                    tma_load_2d(st, &tmap_x, &ctl.full[s], ks * kBK, m0);
-                    tma_load_2d(st + kTileBytes, &tmap_wh, &ctl.full[s], ks * kBK, n0);
-                    tma_load_2d(st + 2 * kTileBytes, &tmap_wl, &ctl.full[s], ks * kBK, n0);
+                    unsigned char* st = ring + s * stage_bytes;
+                    const int k0 = ks * kStageK;
+                    const bool two = k0 + kBK < g.k;  // the second box holds part of K
+                    mbar_expect_tx(&ctl.full[s], (two ? 2u : 1u) * (kTileBytes + 2 * g.w_box_bytes));
+                    tma_load_2d(st, &tmap_x, &ctl.full[s], k0, m0);
+                    tma_load_2d(st + wh_off, &tmap_wh, &ctl.full[s], k0, n0);
+                    tma_load_2d(st + wl_off, &tmap_wl, &ctl.full[s], k0, n0);
+                    if (two) {
+                        tma_load_2d(st + kTileBytes, &tmap_x, &ctl.full[s], k0 + kBK, m0);
+                        tma_load_2d(st + wh_off + w_box, &tmap_wh, &ctl.full[s], k0 + kBK, n0);
+                        tma_load_2d(st + wl_off + w_box, &tmap_wl, &ctl.full[s], k0 + kBK, n0);
+                    }
                     armed |= 1u << s;
                     armed_ph = (armed_ph & ~(1u << s)) | (ph << s);
-                    advance(s, ph, kStages);
+                    advance(s, ph, stages);
                 }
             }
             if (!ok) {  // let the copies in flight land before the CTA exits
-                for (int i = 0; i < kStages; ++i)
+                for (int i = 0; i < stages; ++i)
                     if ((armed >> i) & 1u) mbar_wait(&ctl.full[i], (armed_ph >> i) & 1u, abort, true);
             } else {  // tail: the last stages' release arrivals land before the CTA exits
-                for (int i = 0; i < kStages && mbar_wait(&ctl.empty[s], ph ^ 1u, abort); ++i) advance(s, ph, kStages);
+                for (int i = 0; i < stages && mbar_wait(&ctl.empty[s], ph ^ 1u, abort); ++i) advance(s, ph, stages);
             }
         }
     } else if (warp == 1) {
@@ -563,42 +584,34 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int n0 = (t % n_tiles) * kBN;
                 const int nw = min(kBN, g.n - n0);
                 const uint32_t idesc = tf32_idesc(kBM, (nw + 15) & ~15);
-                int ks = 0;
-                for (int ch = 0; ch < chunks && ok; ++ch) {
-                    if (!mbar_wait(&ctl.acc_empty[cb], cph ^ 1u, abort)) {
+                for (int ks = 0; ks < k_stages; ++ks) {
+                    // a stage is one chunk: its own accumulator, summed by the epilogue in FP32
+                    if (!mbar_wait(&ctl.acc_empty[cb], cph ^ 1u, abort) || !mbar_wait(&ctl.full[s], ph, abort) ||
+                        !mbar_wait(&ctl.a_full[sa], aph, abort)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     const uint32_t d = tmem + uint32_t(cb) * acc_cols;
-                    const int ks_end = min(ks + kStagesPerChunk, k_stages);
-                    uint32_t acc = 0;
-                    for (; ks < ks_end; ++ks) {
-                        if (!mbar_wait(&ctl.full[s], ph, abort) || !mbar_wait(&ctl.a_full[sa], aph, abort)) {
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
-                        const uint32_t base = ring_addr + uint32_t(s) * kStageBytes;
-                        const uint64_t wh = sw128_desc(base + kTileBytes), wl = sw128_desc(base + 2 * kTileBytes);
-                        const uint32_t xh = tmem + a_base + uint32_t(sa) * kACols, xl = xh + kBK;
-                        // the small cross terms first: x_lo w_hi, x_hi w_lo, then x_hi w_hi
-                        if (acc)
-                            tc_mma_k32_ts<1>(d, xl, wh, idesc);
-                        else
-                            tc_mma_k32_ts<0>(d, xl, wh, idesc);
-                        acc = 1;
-                        tc_mma_k32_ts<1>(d, xh, wl, idesc);
-                        tc_mma_k32_ts<1>(d, xh, wh, idesc);
-                        issued = true;
-                        tc_commit(&ctl.empty[s]);     // the stage's shared memory is free once these are done
-                        tc_commit(&ctl.a_empty[sa]);  // and so is its A buffer
-                        advance(s, ph, kStages);
-                        advance(sa, aph, a_bufs);
+                    const uint32_t base = ring_addr + uint32_t(s) * stage_bytes;
+                    const uint64_t wh = sw128_desc(base + wh_off), wl = sw128_desc(base + wl_off);
+                    const uint32_t xh = tmem + a_base + uint32_t(sa) * kACols, xl = xh + kStageK;
+                    // per box: the small cross terms first (x_lo w_hi, x_hi w_lo), then x_hi w_hi
+                    tc_mma_k32_ts<0>(d, xl, wh, idesc);
+                    tc_mma_k32_ts<1>(d, xh, wl, idesc);
+                    tc_mma_k32_ts<1>(d, xh, wh, idesc);
+                    if (ks * kStageK + kBK < g.k) {  // the second box (a descriptor step of w_box bytes)
+                        constexpr uint64_t kBoxStep = w_box >> 4;
+                        tc_mma_k32_ts<1>(d, xl + kBK, wh + kBoxStep, idesc);
+                        tc_mma_k32_ts<1>(d, xh + kBK, wl + kBoxStep, idesc);
+                        tc_mma_k32_ts<1>(d, xh + kBK, wh + kBoxStep, idesc);
                     }
-                    if (!ok) break;
+                    issued = true;
+                    tc_commit(&ctl.empty[s]);  // the stage's shared memory and its A buffer are free once done
                     tc_commit(&ctl.acc_full[cb]);
-                    advance(cb, cph, kAccBufs);
+                    advance(s, ph, stages);
+                    advance(sa, aph, kABufs);
+                    advance(cb, cph, acc_bufs);
                 }
             }
             if (!ok && issued) {  // the MMAs in flight finish before TMEM is freed
@@ -608,21 +621,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp >= 4 && warp < 8) {
         // ------------------------------------------------------- x splitter
-        // thread = row r of the tile = TMEM lane r; the row's 32 floats sit in
-        // 8 16-byte chunks, chunk c at position c ^ (r % 8) (128-byte swizzle)
+        // thread = row r of the tile = TMEM lane r; a box row's 32 floats sit in
+        // 8 16-byte chunks, chunk c at position c ^ (r % 8) (128-byte swizzle).
+        // The A buffer of stage j (j % 2) is free once stage j - 2's MMAs are done: the completion of
+        // that stage's `empty` phase (use (j - 2) / stages of its ring slot). With two ring slots the
+        // slot is this stage's own, whose reload already waited for it.
         const int q = warp & 3, r = q * 32 + lane;
         const uint32_t lane_addr = uint32_t(q * 32) << 16;
-        int s = 0, sa = 0;
-        uint32_t ph = 0, aph = 0;
+        int s = 0, sa = 0, j = 0;
+        uint32_t ph = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-            for (int ks = 0; ks < k_stages; ++ks) {
-                // the split is computed while the A buffer's previous MMAs may still run; only the
-                // TMEM stores wait for them
+            for (int ks = 0; ks < k_stages; ++ks, ++j) {
                 bool got = mbar_wait(&ctl.full[s], ph, abort);
-                float h[32], v[32];
-                if (got) {
-                    const float4* row = reinterpret_cast<const float4*>(ring + s * kStageBytes + r * 128);
+                if (got && stages != kABufs && j >= kABufs) {
+                    const int jp = j - kABufs;
+                    got = mbar_wait(&ctl.empty[jp % stages], uint32_t(jp / stages) & 1u, abort);
+                }
+                if (!__all_sync(0xffffffffu, got)) {  // warp-uniform: tcgen05.st is .sync.aligned
+                    *abort = 1;
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t ta = tmem + lane_addr + a_base + uint32_t(sa) * kACols;
+                const int boxes = ks * kStageK + kBK < g.k ? 2 : 1;
+                for (int b = 0; b < boxes; ++b) {
+                    float h[32], v[32];
+                    const float4* row = reinterpret_cast<const float4*>(ring + s * stage_bytes + b * kTileBytes + r * 128);
 #pragma unroll
                     for (int c = 0; c < 8; ++c) {
                         const float4 f = row[c ^ (r & 7)];
@@ -633,34 +659,27 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     if (g.in_silu) {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) v[j] = silu(v[j]);
+                        for (int jj = 0; jj < 32; ++jj) v[jj] = silu(v[jj]);
                     }
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        h[j] = rna_tf32(v[j]);
-                        v[j] -= h[j];
+                    for (int jj = 0; jj < 32; ++jj) {
+                        h[jj] = rna_tf32(v[jj]);
+                        v[jj] -= h[jj];
                     }
-                    got = mbar_wait(&ctl.a_empty[sa], aph ^ 1u, abort);
+                    tmem_st32(ta + uint32_t(b * kBK), h, false);
+                    tmem_st32(ta + uint32_t(kStageK + b * kBK), v, false);
                 }
-                if (!__all_sync(0xffffffffu, got)) {  // warp-uniform: tcgen05.st is .sync.aligned
-                    *abort = 1;
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t ta = tmem + lane_addr + a_base + uint32_t(sa) * kACols;
-                tmem_st32(ta, h, false);
-                tmem_st32(ta + kBK, v, true);
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                 tc_fence_before();
                 mbar_arrive(&ctl.a_full[sa]);
-                advance(s, ph, kStages);
-                advance(sa, aph, a_bufs);
+                advance(s, ph, stages);
+                sa ^= 1;
             }
         }
     } else if (warp >= 8) {
         // --------------------------------------------------------- epilogue
-        epilogue_role<NARROW ? 1 : 2>(g, &tmap_y, ctl, abort, tmem, epi_smem, warp, lane, tiles, n_tiles, chunks,
-                                      acc_cols);
+        epilogue_role<NARROW ? 1 : 2, acc_bufs>(g, &tmap_y, ctl, abort, tmem, epi_smem, warp, lane, tiles, n_tiles,
+                                                chunks, acc_cols);
     }
 
     tc_fence_before();

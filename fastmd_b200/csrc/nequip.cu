@@ -434,7 +434,7 @@ constexpr int kBwdBlock = 616 + kMW + kAW + 1 + kWW + kXW + 36;
 
 __global__ void __launch_bounds__(kRecvThreads) nq_conv_bwd_edge_kernel(ConvArgs a, const float* __restrict__ dmsg,
                                                                         float* __restrict__ dW,
-                                                                        float* __restrict__ dY) {
+                                                                        float* __restrict__ dY, int accumulate_dy) {
     extern __shared__ __align__(16) float nq_smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float* cg = nq_smem;
@@ -472,7 +472,10 @@ __global__ void __launch_bounds__(kRecvThreads) nq_conv_bwd_edge_kernel(ConvArgs
 #pragma unroll
                 for (int q = 0; q < 9; ++q) dyw[warp * 9 + q] = dy[q];
             __syncthreads();
-            if (tid < 9) dY[9 * e + tid] = ((dyw[tid] + dyw[9 + tid]) + dyw[18 + tid]) + dyw[27 + tid];
+            if (tid < 9) {
+                const float v = ((dyw[tid] + dyw[9 + tid]) + dyw[18 + tid]) + dyw[27 + tid];
+                dY[9 * e + tid] = accumulate_dy ? dY[9 * e + tid] + v : v;
+            }
         }
     }
 }
@@ -677,6 +680,35 @@ __global__ void __launch_bounds__(256) nq_self_conn_kernel(const float* __restri
     }
 }
 
+// forces[a] = sum of grad_vec over the edges a receives - sum over the edges a sends: a warp per atom,
+// lane l takes the run's entries l, l + 32, ..., then a fixed xor tree over the lanes
+constexpr int kForceWarpsNq = 8;
+__global__ void __launch_bounds__(32 * kForceWarpsNq) nq_edge_forces_kernel(
+    const float* __restrict__ g, const int32_t* __restrict__ edge_index, const int64_t* __restrict__ recv_off,
+    const int64_t* __restrict__ send_off, const int32_t* __restrict__ send_perm, int64_t n_atoms,
+    float* __restrict__ forces) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = int64_t(gridDim.x) * kForceWarpsNq;
+    for (int64_t a = blockIdx.x * int64_t(kForceWarpsNq) + (threadIdx.x >> 5); a < n_atoms; a += warps) {
+        float r[3] = {0.f, 0.f, 0.f}, t[3] = {0.f, 0.f, 0.f};
+        for (int64_t e = recv_off[a] + lane; e < recv_off[a + 1]; e += 32)
+#pragma unroll
+            for (int c = 0; c < 3; ++c) r[c] += g[3 * e + c];
+        for (int64_t k = send_off[a] + lane; k < send_off[a + 1]; k += 32) {
+            const int64_t e = send_perm[k];
+#pragma unroll
+            for (int c = 0; c < 3; ++c) t[c] += g[3 * e + c];
+        }
+#pragma unroll
+        for (int c = 0; c < 3; ++c)
+            for (int d = 16; d > 0; d >>= 1) {
+                r[c] += __shfl_xor_sync(0xffffffffu, r[c], d);
+                t[c] += __shfl_xor_sync(0xffffffffu, t[c], d);
+            }
+        if (lane < 3) forces[3 * a + lane] = r[lane] - t[lane];
+    }
+}
+
 bool make_cell3(const float* host, Cell3& c) {
     if (host == nullptr) return false;
     for (int k = 0; k < 9; ++k) c.c[k] = host[k];
@@ -770,22 +802,37 @@ fmd_status fmd_nequip_conv(const float* x, const float* Y, const float* W, const
 fmd_status fmd_nequip_conv_bwd(const float* x, const float* Y, const float* W, const float* cg,
                                const int32_t* edge_index, const int64_t* recv_off, const int64_t* send_off,
                                const int32_t* send_perm, int64_t n_atoms, float inv_avg, const float* grad_messages,
-                               float* grad_x, float* grad_W, float* grad_Y, void* stream) {
+                               float* grad_x, float* grad_W, float* grad_Y, int32_t accumulate_grad_y, void* stream) {
     ConvArgs a;
     fmd_status st = conv_args(a, x, Y, W, cg, edge_index, recv_off, send_off, send_perm, n_atoms, inv_avg);
     if (st != FMD_OK) return st;
     if (n_atoms == 0) return FMD_OK;
-    if (grad_messages == nullptr || grad_x == nullptr || grad_W == nullptr || grad_Y == nullptr ||
-        send_off == nullptr)
+    if (grad_messages == nullptr || grad_W == nullptr || grad_Y == nullptr || (grad_x != nullptr && send_off == nullptr))
         return FMD_ERR_INVALID_ARGUMENT;
     const size_t smem_e = sizeof(float) * kBwdBlock, smem_x = sizeof(float) * kBxBlock;
     if ((st = grant_dynamic_smem((const void*)nq_conv_bwd_edge_kernel, smem_e)) != FMD_OK) return st;
     if ((st = grant_dynamic_smem((const void*)nq_conv_bwd_x_kernel, smem_x)) != FMD_OK) return st;
     const cudaStream_t s = as_stream(stream);
     nq_conv_bwd_edge_kernel<<<grid_of(n_atoms, 1), kRecvThreads, smem_e, s>>>(a, grad_messages, grad_W,
-                                                                                       grad_Y);
+                                                                                       grad_Y, accumulate_grad_y != 0);
     if ((st = check_launch()) != FMD_OK) return st;
+    if (grad_x == nullptr) return FMD_OK;  // the input needs no gradient (the first block's embedding)
     nq_conv_bwd_x_kernel<<<grid_of(n_atoms, 1), kRecvThreads, smem_x, s>>>(a, grad_messages, grad_x);
+    return check_launch();
+}
+
+fmd_status fmd_edge_forces(const float* grad_vec, const int32_t* edge_index, const int64_t* recv_off,
+                           const int64_t* send_off, const int32_t* send_perm, int64_t n_atoms, float* forces,
+                           void* stream) {
+    if (n_atoms < 0) return FMD_ERR_INVALID_ARGUMENT;
+    if (n_atoms == 0) return FMD_OK;
+    if (grad_vec == nullptr || recv_off == nullptr || send_off == nullptr || send_perm == nullptr ||
+        forces == nullptr)
+        return FMD_ERR_INVALID_ARGUMENT;
+    (void)edge_index;  // the runs name the edges; kept for the callers' symmetry with the gradient's layout
+    const int64_t blocks = (n_atoms + kForceWarpsNq - 1) / kForceWarpsNq;
+    nq_edge_forces_kernel<<<int(blocks < 148 * 16 ? blocks : 148 * 16), 32 * kForceWarpsNq, 0, as_stream(stream)>>>(
+        grad_vec, edge_index, recv_off, send_off, send_perm, n_atoms, forces);
     return check_launch();
 }
 

@@ -9,10 +9,11 @@ envelope -> 64 -> 64 -> 960 path weights, SiLU, no bias) over the 15 couplings l
 spherical harmonics up to l = 2, normalised by the average neighbour count, a second linear per l
 and a gated nonlinearity (SiLU on the scalars, sigmoid gates on l = 1, 2), plus the self-connection;
 then a scalar readout 128 -> 64 -> 1, scaled and shifted, summed per system in FP64. Forces are minus
-the position gradient, through the autograd graph of this build's kernels: the edge basis and its
-backward (``fmd_nequip_edge_basis``), the convolution and its backward (``fmd_nequip_conv``), the
-linears on the tcgen05 wide GEMM (``precision="tf32x3"``) or its IEEE path (``"ieee"``), the position
-gradient summed over the receiver and sender CSRs (``fmd_csr_segment_sum``). Element indices are
+the position gradient: autograd over this build's kernels back to the radial basis and the harmonics
+(the convolution and its backward, ``fmd_nequip_conv``; the linears on the tcgen05 wide GEMM,
+``precision="tf32x3"``, or its IEEE path, ``"ieee"``), then the edge basis backward
+(``fmd_nequip_edge_basis_bwd``) and the forces summed over the receiver and sender CSRs
+(``fmd_edge_forces``). Element indices are
 atomic number - 1 (89 elements). The padded rows of an exact-rc build (``PaddingRule("exact_rc_loops")``,
 fastmd/models/sevennet.py:16-22) read the override vector, which the envelope maps to zero.
 """
@@ -82,44 +83,34 @@ def coupling_table() -> np.ndarray:
     return np.concatenate([clebsch_gordan(*p).reshape(-1) for p in PATHS]).astype(np.float32)
 
 
-class _EdgeBasis(Function):
-    """(Y [E, 9], B [E, n_basis]) of the edges; the backward returns the position gradient."""
+_ACT_INPUT_SILU, _ACT_SILU_GRAD = 16, 2  # fmd_gemm_tf32x3: SiLU on the operand / times silu'(c)
 
-    @staticmethod
-    def forward(ctx, pos, model, batch):
-        E = int(batch.edge_index.shape[0])
-        dev = pos.device
-        c = model.config
-        Y = torch.empty(E, 9, device=dev)
-        B = torch.empty(E, c.num_bessel, device=dev)
-        geo = torch.empty(E, 4, device=dev)
-        cell_ptr = model.cell_ptr(batch)
-        override = getattr(batch, "edge_vec_override", None)
-        call("fmd_nequip_edge_basis", ptr(pos), cell_ptr, ptr(batch.edge_index), ptr(batch.edge_image), ptr(override),
-             ptr(batch.n_edges) if override is not None else None, E, c.r_max, c.num_bessel, c.poly_p, ptr(Y), ptr(B),
-             ptr(geo), stream(dev))
-        ctx.model, ctx.batch = model, batch
-        ctx.save_for_backward(geo)
-        return Y, B
 
-    @staticmethod
-    def backward(ctx, dY, dB):
-        (geo,) = ctx.saved_tensors
-        batch, c = ctx.batch, ctx.model.config
-        E, N = int(geo.shape[0]), batch.n_real
-        g = torch.empty(E, 3, device=geo.device)
-        override = getattr(batch, "edge_vec_override", None)
-        call("fmd_nequip_edge_basis_bwd", ptr(geo), ptr(dY.contiguous()), ptr(dB.contiguous()), ptr(override),
-             ptr(batch.n_edges) if override is not None else None, E, c.r_max, c.num_bessel, c.poly_p, ptr(g),
-             stream(geo.device))
-        # dE/dpos_a = sum over sent edges (a = neighbour) - sum over received edges (a = centre)
-        n_pos = batch.positions.shape[0]
-        recv = ops.csr_segment_sum(g, batch.edge_index[:, 0].long(), N, None, batch.recv_off[:N + 1], True)
-        send = ops.csr_segment_sum(g, batch.edge_index[:, 1].long(), N, batch.send_perm.long(),
-                                   batch.send_off[:N + 1])
-        grad = torch.zeros(n_pos, 3, device=geo.device)
-        grad[:N] = send - recv
-        return grad, None, None
+def _zero(t: Tensor) -> Tensor:
+    """``t`` set to zeros by a stream-ordered memset (``fmd_zero``; no kernel)."""
+    call("fmd_zero", ptr(t), t.numel() * t.element_size(), stream(t.device))
+    return t
+
+
+def _gemm(model, a: Tensor, w: Tensor, transposed: bool = False, out=None, accumulate: bool = False, act: int = 0,
+          c=None, a_pre=None, y_pre=None) -> Tensor:
+    """``y (+)= a @ B`` with ``B = w^T`` (or ``w`` when ``transposed``) in the model's precision: the tcgen05
+    3xTF32 GEMM (``act``/``c`` its fused SiLU modes; ``accumulate`` adds to ``out``) or the IEEE SIMT GEMM
+    (``act = 1`` SiLU output with the pre-activation into ``y_pre``; ``a_pre``: the operand times
+    silu'(a_pre) as it is loaded)."""
+    m, k = a.shape
+    n = w.shape[1] if transposed else w.shape[0]
+    y = torch.empty((m, n), device=a.device) if out is None else out
+    if m == 0:
+        return y
+    if model.precision == "tf32x3":
+        if accumulate:
+            c = y
+        return wide_gemm._launch(a, w, transposed, "tf32x3", c=c, out=y, act=act)
+    call("fmd_gemm_f32", ptr(a), a.stride(0), ptr(a_pre), a_pre.stride(0) if a_pre is not None else 0, ptr(w),
+         w.stride(0), int(not transposed), None, ptr(y), y.stride(0), ptr(y_pre),
+         y_pre.stride(0) if y_pre is not None else 0, m, n, k, act, int(accumulate), stream(a.device))
+    return y
 
 
 def _planes(flat: Tensor, n: int, mults) -> tuple[Tensor, ...]:
@@ -131,57 +122,203 @@ def _planes(flat: Tensor, n: int, mults) -> tuple[Tensor, ...]:
     return tuple(out)
 
 
-class _Conv(Function):
-    """Messages (three planes [N, 224], [3N, 384], [5N, 352]) of the node features x (the planar buffer
-    of 480 N floats); the backward returns the gradients of x, Y and W."""
+class _RadialNet(Function):
+    """The path weights W_L [E, 960] of every block from the radial basis B [E, n_basis]: the blocks' first
+    layers as one GEMM (p1 = B W1^T, their weights stacked), then per block W_L = silu(silu(p1_L) W2^T) W3^T
+    with each SiLU applied to the next GEMM's operand; the backward forms every silu' product in a GEMM
+    epilogue and writes each block's first-layer gradient into its column block, so dB is one GEMM."""
 
     @staticmethod
-    def forward(ctx, x, Y, W, model, batch):
-        N = batch.n_real
-        m = torch.empty(N * sum(M_MULT[l] * DIM[l] for l in range(3)), device=x.device)
-        call("fmd_nequip_conv", ptr(x), ptr(Y), ptr(W), ptr(model.cg), ptr(batch.edge_index), ptr(batch.recv_off), N,
-             1.0 / model.config.avg_num_neighbors, ptr(m), stream(x.device))
-        ctx.save_for_backward(x, Y, W)
-        ctx.model, ctx.batch = model, batch
-        return _planes(m, N, M_MULT)
+    def forward(ctx, B, model):
+        c, H = model.config, model.config.radial_hidden
+        E = B.shape[0]
+        ws = model.w
+        p2s, Ws = [], []
+        if model.precision == "tf32x3":
+            p1 = _gemm(model, B, model.rad1_all)
+            for L in range(c.num_layers):
+                p2 = _gemm(model, p1[:, L * H:(L + 1) * H], ws[f"L{L}.rad2"], act=_ACT_INPUT_SILU)
+                Ws.append(_gemm(model, p2, ws[f"L{L}.rad3"], act=_ACT_INPUT_SILU))
+                p2s.append(p2)
+        else:
+            p1 = torch.empty((E, c.num_layers * H), device=B.device)
+            a1 = _gemm(model, B, model.rad1_all, act=1, y_pre=p1)
+            for L in range(c.num_layers):
+                p2 = torch.empty((E, H), device=B.device)
+                a2 = _gemm(model, a1[:, L * H:(L + 1) * H], ws[f"L{L}.rad2"], act=1, y_pre=p2)
+                Ws.append(_gemm(model, a2, ws[f"L{L}.rad3"]))
+                p2s.append(p2)
+        ctx.save_for_backward(p1, *p2s)
+        ctx.model = model
+        ctx.set_materialize_grads(False)
+        return tuple(Ws)
 
     @staticmethod
-    def backward(ctx, *dm):
-        x, Y, W = ctx.saved_tensors
-        model, batch = ctx.model, ctx.batch
-        N = batch.n_real
-        dm = torch.cat([(g if g is not None else torch.zeros(N * M_MULT[l] * DIM[l], device=x.device)).reshape(-1)
-                        for l, g in enumerate(dm)])
-        gx, gW, gY = torch.empty_like(x), torch.empty_like(W), torch.empty_like(Y)
-        call("fmd_nequip_conv_bwd", ptr(x), ptr(Y), ptr(W), ptr(model.cg), ptr(batch.edge_index), ptr(batch.recv_off),
-             ptr(batch.send_off), ptr(batch.send_perm), N, 1.0 / model.config.avg_num_neighbors, ptr(dm), ptr(gx),
-             ptr(gW), ptr(gY), stream(x.device))
-        return gx, gY, gW, None, None
+    def backward(ctx, *dWs):
+        p1, *p2s = ctx.saved_tensors
+        model = ctx.model
+        H, ws = model.config.radial_hidden, model.w
+        g1 = torch.empty_like(p1)
+        if any(d is None for d in dWs):
+            _zero(g1)
+        for L, dW in enumerate(dWs):
+            if dW is None:
+                continue
+            blk = slice(L * H, (L + 1) * H)
+            if model.precision == "tf32x3":
+                g2 = _gemm(model, dW.contiguous(), ws[f"L{L}.rad3"], True, act=_ACT_SILU_GRAD, c=p2s[L])
+                _gemm(model, g2, ws[f"L{L}.rad2"], True, out=g1[:, blk], act=_ACT_SILU_GRAD, c=p1[:, blk])
+            else:
+                da2 = _gemm(model, dW.contiguous(), ws[f"L{L}.rad3"], True)
+                _gemm(model, da2, ws[f"L{L}.rad2"], True, out=g1[:, blk], a_pre=p2s[L])
+        if model.precision == "tf32x3":
+            dB = _gemm(model, g1, model.rad1_all, True)
+        else:
+            dB = _gemm(model, g1, model.rad1_all, True, a_pre=p1)
+        return dB, None
 
 
-class _SelfConnection(Function):
-    """The element-dependent linear of the three feature planes (``fmd_nequip_self_connection``); its
-    input gradient is the same kernel on the transposed weights ``t0, t1, t2`` (frozen; kept as copies
-    so that both directions read a weight row across the warp's consecutive output channels)."""
+class _NodeIn(Function):
+    """A block's inputs from the node features (planes x0 [N, 128], x1 [3N, 64], x2 [5N, 32]; x1 and x2
+    None in the first block, exact zeros): the first linear of each plane written into one planar buffer
+    h (the convolution's input) and the element-dependent self-connection planes sc0, sc1, sc2
+    (``fmd_nequip_self_connection``). The backward adds the linears' input gradients to the
+    self-connection's (the GEMM accumulating into it)."""
 
     @staticmethod
-    def forward(ctx, x0, x1, x2, elem, w0, w1, w2, t0, t1, t2):
-        n = x0.shape[0]
-        xs = [x0.contiguous(), x1.contiguous(), x2.contiguous()]
-        out = [torch.empty_like(t) for t in xs]
-        call("fmd_nequip_self_connection", ptr(xs[0]), ptr(xs[1]), ptr(xs[2]), ptr(elem), ptr(w0), ptr(w1), ptr(w2), n,
-             0, ptr(out[0]), ptr(out[1]), ptr(out[2]), stream(x0.device))
-        ctx.save_for_backward(elem, t0, t1, t2)
-        return tuple(out)
+    def forward(ctx, x0, x1, x2, model, L):
+        N, dev = x0.shape[0], x0.device
+        first = x1 is None
+        if first:
+            zeros = _zero(torch.empty(N * (3 * 64 + 5 * 32), device=dev))
+            x1, x2 = zeros[:N * 192].view(3 * N, 64), zeros[N * 192:].view(5 * N, 32)
+        h = torch.empty(N * X_WIDTH, device=dev)
+        hp = _planes(h, N, MULT)
+        xs = (x0.contiguous(), x1.contiguous(), x2.contiguous())
+        if first:
+            _zero(h[N * MULT[0]:])  # a linear map of an exact zero plane is an exact zero plane
+        for l in range(1 if first else 3):
+            _gemm(model, xs[l], model.lin[f"L{L}.lin1_{l}"], out=hp[l])
+        sc = [torch.empty_like(t) for t in xs]
+        call("fmd_nequip_self_connection", ptr(xs[0]), ptr(xs[1]), ptr(xs[2]), ptr(model._elem),
+             *[ptr(model.w[f"L{L}.sc{l}"]) for l in range(3)], N, 0, ptr(sc[0]), ptr(sc[1]), ptr(sc[2]),
+             stream(dev))
+        ctx.model, ctx.L, ctx.first, ctx.n = model, L, first, N
+        ctx.set_materialize_grads(False)
+        return h, sc[0], sc[1], sc[2]
 
     @staticmethod
-    def backward(ctx, g0, g1, g2):
-        elem, t0, t1, t2 = ctx.saved_tensors
-        gs = [g.contiguous() for g in (g0, g1, g2)]
+    def backward(ctx, dh, d0, d1, d2):
+        model, L, N = ctx.model, ctx.L, ctx.n
+        dev = model.device
+        gs = [g.contiguous() if g is not None else None for g in (d0, d1, d2)]
+        shapes = ((N, 128), (3 * N, 64), (5 * N, 32))
+        for l in range(3):
+            if gs[l] is None:
+                gs[l] = _zero(torch.empty(shapes[l], device=dev))
         dx = [torch.empty_like(g) for g in gs]
-        call("fmd_nequip_self_connection", ptr(gs[0]), ptr(gs[1]), ptr(gs[2]), ptr(elem), ptr(t0), ptr(t1), ptr(t2),
-             gs[0].shape[0], 0, ptr(dx[0]), ptr(dx[1]), ptr(dx[2]), stream(gs[0].device))
-        return dx[0], dx[1], dx[2], None, None, None, None, None, None, None
+        call("fmd_nequip_self_connection", ptr(gs[0]), ptr(gs[1]), ptr(gs[2]), ptr(model._elem),
+             *[ptr(model.sc_t[f"L{L}.sc{l}"]) for l in range(3)], N, 0, ptr(dx[0]), ptr(dx[1]), ptr(dx[2]),
+             stream(dev))
+        if dh is not None:
+            dhp = _planes(dh.contiguous(), N, MULT)
+            for l in range(1 if ctx.first else 3):
+                _gemm(model, dhp[l], model.lin[f"L{L}.lin1_{l}"], True, out=dx[l], accumulate=True)
+        if ctx.first:
+            return dx[0], None, None, None, None
+        return dx[0], dx[1], dx[2], None, None
+
+
+class _Conv(Function):
+    """Messages (the planar buffer of 3136 N floats: [N, 224] | [N, 3, 384] | [N, 5, 352]) of the block's
+    planar input h; the backward returns the gradients of h and W and adds the harmonics' gradient into
+    the model's per-evaluation dY buffer (the last block's backward, which runs first, writes it)."""
+
+    @staticmethod
+    def forward(ctx, h, W, model, batch, L):
+        N = batch.n_real
+        m = torch.empty(N * sum(M_MULT[l] * DIM[l] for l in range(3)), device=h.device)
+        call("fmd_nequip_conv", ptr(h), ptr(model._Y), ptr(W), ptr(model.cg), ptr(batch.edge_index),
+             ptr(batch.recv_off), N, 1.0 / model.config.avg_num_neighbors, ptr(m), stream(h.device))
+        ctx.save_for_backward(h, W)
+        ctx.model, ctx.batch, ctx.L = model, batch, L
+        ctx.set_materialize_grads(False)
+        return m
+
+    @staticmethod
+    def backward(ctx, dm):
+        h, W = ctx.saved_tensors
+        model, batch, L = ctx.model, ctx.batch, ctx.L
+        last = L == model.config.num_layers - 1
+        if dm is None:
+            if last:
+                _zero(model._dY)
+            return None, None, None, None, None
+        N = batch.n_real
+        # the first block's input (the embedding and exact-zero planes) needs no gradient: dx not formed
+        gx = torch.empty_like(h) if ctx.needs_input_grad[0] else None
+        gW = torch.empty_like(W)
+        call("fmd_nequip_conv_bwd", ptr(h), ptr(model._Y), ptr(W), ptr(model.cg), ptr(batch.edge_index),
+             ptr(batch.recv_off), ptr(batch.send_off), ptr(batch.send_perm), N,
+             1.0 / model.config.avg_num_neighbors, ptr(dm.contiguous()), ptr(gx), ptr(gW), ptr(model._dY),
+             int(not last), stream(h.device))
+        return gx, gW, None, None, None
+
+
+class _PlanarOut(Function):
+    """The second linear of each message plane (o0 [N, 224], o1 [3N, 64], o2 [5N, 32]); the backward
+    writes the three input gradients into the planes of one buffer (the convolution's gradient input)."""
+
+    @staticmethod
+    def forward(ctx, m, model, L):
+        N = model._n
+        mp = _planes(m, N, M_MULT)
+        ctx.model, ctx.L = model, L
+        ctx.set_materialize_grads(False)
+        return tuple(_gemm(model, mp[l], model.lin[f"L{L}.lin2_{l}"]) for l in range(3))
+
+    @staticmethod
+    def backward(ctx, d0, d1, d2):
+        model, L = ctx.model, ctx.L
+        N = model._n
+        dm = torch.empty(N * sum(M_MULT[l] * DIM[l] for l in range(3)), device=model.device)
+        dmp = _planes(dm, N, M_MULT)
+        for l, g in enumerate((d0, d1, d2)):
+            if g is None:
+                _zero(dmp[l])
+            else:
+                _gemm(model, g.contiguous(), model.lin[f"L{L}.lin2_{l}"], True, out=dmp[l])
+        return dm, None, None
+
+
+class _Readout(Function):
+    """The system energy (FP64 [1]): e_i = (x0_i W1^T) W2^T scaled and shifted, summed in FP64
+    (``fmd_mace_node_energy``: fixed-order block tree). The readout is linear, so the backward is the
+    outer product of dE/de_i (``fmd_mace_node_energy_bwd``) with the row v = W2 W1."""
+
+    @staticmethod
+    def forward(ctx, x0, model):
+        N, c = x0.shape[0], model.config
+        hid = _gemm(model, x0.contiguous(), model.w["readout1"])
+        out = _gemm(model, hid, model.w["readout2"])
+        node = torch.empty(N, dtype=torch.float64, device=x0.device)
+        total = torch.empty(1, dtype=torch.float64, device=x0.device)
+        call("fmd_mace_node_energy", ptr(out), 1, N, ptr(model._elem32), ptr(model._e0), float(c.scale),
+             float(c.shift), N, 1, ptr(node), ptr(total), stream(x0.device))
+        ctx.model, ctx.n = model, N
+        return total
+
+    @staticmethod
+    def backward(ctx, d_total):
+        model, N = ctx.model, ctx.n
+        dev = model.device
+        d_term = torch.empty((N, 1), device=dev)
+        call("fmd_mace_node_energy_bwd", ptr(d_total.contiguous()), float(model.config.scale), N, 1, ptr(d_term),
+             stream(dev))
+        dx0 = torch.empty((N, MULT[0]), device=dev)
+        call("fmd_gemm_f32", ptr(d_term), 1, None, 0, ptr(model._readout_row), 1, 1, None, ptr(dx0), MULT[0], None,
+             0, N, MULT[0], 1, 0, 0, stream(dev))
+        return dx0, None
 
 
 class _Gate(Function):
@@ -196,13 +333,14 @@ class _Gate(Function):
         call("fmd_nequip_gate", ptr(o0), ptr(o1), ptr(o2), ptr(sc0.contiguous()), ptr(sc1.contiguous()),
              ptr(sc2.contiguous()), n, ptr(x[0]), ptr(x[1]), ptr(x[2]), stream(o0.device))
         ctx.save_for_backward(o0, o1, o2)
+        ctx.set_materialize_grads(False)  # the last block's x1, x2 feed nothing: zeros by memset below
         return tuple(x)
 
     @staticmethod
     def backward(ctx, dx0, dx1, dx2):
         o0, o1, o2 = ctx.saved_tensors
         n = o0.shape[0]
-        dx = [g.contiguous() if g is not None else torch.zeros(n * DIM[l], MULT[l], device=o0.device)
+        dx = [g.contiguous() if g is not None else _zero(torch.empty(n * DIM[l], MULT[l], device=o0.device))
               for l, g in enumerate((dx0, dx1, dx2))]
         do = [torch.empty_like(o0), torch.empty_like(o1), torch.empty_like(o2)]
         call("fmd_nequip_gate_bwd", ptr(o0), ptr(o1), ptr(o2), ptr(dx[0]), ptr(dx[1]), ptr(dx[2]), n, ptr(do[0]),
@@ -236,6 +374,11 @@ class NequIPModel:
         self.sc_t = {k: v.transpose(1, 2).contiguous() for k, v in self.w.items() if ".sc" in k}
         self.precision = precision
         self.cg = torch.as_tensor(coupling_table(), device=self.device)
+        # the linear readout folded to one row for its backward: d e_i / d x0_i = W2 W1 (FP64 product)
+        row = host["readout2"].astype(np.float64) @ host["readout1"].astype(np.float64)
+        self._readout_row = torch.as_tensor(row.reshape(-1, 1), dtype=torch.float32, device=self.device)
+        self._e0 = torch.zeros(self.config.n_elements, dtype=torch.float64, device=self.device)
+        self._one = torch.ones(1, dtype=torch.float64, device=self.device)  # dE/dE, made once
 
     # ------------------------------------------------------------ per-system state (no host work per call)
     def prepare(self, batch):
@@ -246,6 +389,7 @@ class NequIPModel:
         if int(elem.min()) < 0 or int(elem.max()) >= self.config.n_elements:
             raise ValueError(f"atomic numbers outside 1..{self.config.n_elements}")
         self._elem = elem.contiguous()
+        self._elem32 = elem.to(torch.int32).contiguous()
         self._cell_host, self._cell_ptr = _host_cell(batch.cell)
         self._prepared = (batch.species.data_ptr(), batch.cell.data_ptr())
         return batch
@@ -253,43 +397,51 @@ class NequIPModel:
     def cell_ptr(self, batch):
         return self._cell_ptr
 
-    def _linear(self, x, weight):
-        return wide_gemm.linear(x, weight, precision=self.precision)
-
     def energy_forces(self, batch, n_systems: int = 1) -> tuple[Tensor, Tensor]:
         """(energy [1] fp64, forces [N, 3]) of one system; capturable in a CUDA graph once ``prepare``
-        ran for the system (no host synchronisation)."""
+        ran for the system (no host synchronisation). Every launch is one of this library's kernels (or a
+        memset): the edge basis, the radial network, per block the node inputs, the convolution, the
+        second linears and the gate, the FP64 readout; autograd back to the radial basis (the
+        convolutions add the harmonics' gradient into one buffer), the basis backward, and the forces
+        summed over the receiver and sender CSRs (``fmd_edge_forces``)."""
         if n_systems != 1:
             raise ValueError("the NequIP model evaluates one system per batch")
         if getattr(self, "_prepared", None) != (batch.species.data_ptr(), batch.cell.data_ptr()):
             self.prepare(batch)
         c = self.config
         N = batch.n_real
-        elem = self._elem
+        dev = self.device
+        E = int(batch.edge_index.shape[0])
+        self._n = N
+        Y = torch.empty(E, 9, device=dev)
+        B = torch.empty(E, c.num_bessel, device=dev)
+        geo = torch.empty(E, 4, device=dev)
+        override = getattr(batch, "edge_vec_override", None)
+        n_real_edges = ptr(batch.n_edges) if override is not None else None
+        call("fmd_nequip_edge_basis", ptr(batch.positions), self._cell_ptr, ptr(batch.edge_index),
+             ptr(batch.edge_image), ptr(override), n_real_edges, E, c.r_max, c.num_bessel, c.poly_p, ptr(Y), ptr(B),
+             ptr(geo), stream(dev))
+        self._Y = Y
+        self._dY = torch.empty(E, 9, device=dev)
         with torch.enable_grad():
-            pos = batch.positions.detach().requires_grad_(True)
-            Y, B = _EdgeBasis.apply(pos, self, batch)
-            # node features as planes [N (2l + 1), mult]; l = 1, 2 start at exact zeros
-            x = [self.w["embed"][elem], None, None]
-            # the radial networks' first layers of every block in one GEMM (column views, no copies)
-            r1 = torch.split(torch.nn.functional.silu(self._linear(B, self.rad1_all)), c.radial_hidden, dim=1)
+            Bl = B.requires_grad_(True)
+            Ws = _RadialNet.apply(Bl, self)
+            # node features as planes [N (2l + 1), mult]; l = 1, 2 start at exact zeros (None)
+            x = [ops.gather_cat([(self.w["embed"], self._elem)]), None, None]
             for L in range(c.num_layers):
-                zero = lambda l: torch.zeros(N * DIM[l], MULT[l], device=self.device)  # noqa: E731
-                # a linear map of an exact zero plane is an exact zero plane: not launched
-                h = [self._linear(x[l], self.lin[f"L{L}.lin1_{l}"]) if x[l] is not None else zero(l) for l in range(3)]
-                sc = _SelfConnection.apply(*[x[l] if x[l] is not None else zero(l) for l in range(3)], elem,
-                                           *[self.w[f"L{L}.sc{l}"] for l in range(3)],
-                                           *[self.sc_t[f"L{L}.sc{l}"] for l in range(3)])
-                r = torch.nn.functional.silu(self._linear(r1[L], self.w[f"L{L}.rad2"]))
-                W = self._linear(r, self.w[f"L{L}.rad3"])
-                m = _Conv.apply(torch.cat([p.reshape(-1) for p in h]), Y, W.contiguous(), self, batch)
-                o = [self._linear(m[l], self.lin[f"L{L}.lin2_{l}"]) for l in range(3)]
-                x = list(_Gate.apply(*o, *sc))
-            hid = self._linear(x[0].contiguous(), self.w["readout1"])
-            e_atom = self._linear(hid, self.w["readout2"])[:, 0] * c.scale + c.shift
-            energy = e_atom.double().sum()
-            (grad,) = torch.autograd.grad(energy, pos)
-        return energy.detach().reshape(1), (-grad[:N]).detach()
+                h, sc0, sc1, sc2 = _NodeIn.apply(x[0], x[1], x[2], self, L)
+                m = _Conv.apply(h, Ws[L], self, batch, L)
+                o = _PlanarOut.apply(m, self, L)
+                x = list(_Gate.apply(*o, sc0, sc1, sc2))
+            energy = _Readout.apply(x[0], self)
+            (dB,) = torch.autograd.grad(energy, Bl, grad_outputs=self._one)
+        g = torch.empty(E, 3, device=dev)
+        call("fmd_nequip_edge_basis_bwd", ptr(geo), ptr(self._dY), ptr(dB.contiguous()), ptr(override), n_real_edges,
+             E, c.r_max, c.num_bessel, c.poly_p, ptr(g), stream(dev))
+        forces = torch.empty(N, 3, device=dev)
+        call("fmd_edge_forces", ptr(g), ptr(batch.edge_index), ptr(batch.recv_off), ptr(batch.send_off),
+             ptr(batch.send_perm), N, ptr(forces), stream(dev))
+        return energy.detach().reshape(1), forces
 
     energy_forces_fused = energy_forces
 

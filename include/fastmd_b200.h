@@ -117,6 +117,10 @@ FMD_API fmd_status fmd_gather_rows_bwd_long(const float* gout, int64_t ldgo, int
 /* Strided row copy dst[r, :w] = src[r, :w] (the aligned block's gradient). */
 FMD_API fmd_status fmd_copy_rows(const float* src, int64_t lds, float* dst, int64_t ldd, int64_t rows,
                          int32_t width, void* stream);
+/* bytes zero bytes at dst, stream-ordered (a memset, no kernel): the zero
+ * planes and gradient buffers a model evaluation starts from (the torch
+ * zeros / zero_ calls around the reference's model code). */
+FMD_API fmd_status fmd_zero(void* dst, int64_t bytes, void* stream);
 
 /* ------------------------------------------- CSR segment metadata (C1) */
 
@@ -802,13 +806,25 @@ FMD_API fmd_status fmd_nequip_conv(const float* x, const float* Y, const float* 
                                    const int32_t* edge_index, const int64_t* recv_off, int64_t n_atoms, float inv_avg,
                                    float* messages, void* stream);
 /* Its backward from grad_messages (the messages' planar layout): grad_W
- * [E, 960] and grad_Y [E, 9] per receiver, grad_x (x's planar layout) per
- * sender (send_off / send_perm). */
+ * [E, 960] and grad_Y [E, 9] per receiver (grad_Y added to its contents
+ * when accumulate_grad_y: the layers of a model share the harmonics), grad_x
+ * (x's planar layout) per sender (send_off / send_perm; grad_x null: not
+ * formed, for an input that needs no gradient). */
 FMD_API fmd_status fmd_nequip_conv_bwd(const float* x, const float* Y, const float* W, const float* cg,
                                        const int32_t* edge_index, const int64_t* recv_off, const int64_t* send_off,
                                        const int32_t* send_perm, int64_t n_atoms, float inv_avg,
                                        const float* grad_messages, float* grad_x, float* grad_W, float* grad_Y,
-                                       void* stream);
+                                       int32_t accumulate_grad_y, void* stream);
+/* Forces of an edge-gradient model: forces[a] = sum over the edges a
+ * receives (centre a, recv_off runs) of grad_vec[e] - sum over the edges a
+ * sends (neighbour a, send_off runs of send_perm) of grad_vec[e], with
+ * grad_vec [E, 3] = dE/d(edge vector r_j - r_i + image). A warp per atom, its
+ * lanes over the two runs and a fixed xor tree: deterministic. Replaces the
+ * position gradient autograd forms from the edge vectors (the reference's
+ * -dE/dpos through torch.autograd.grad, fastmd/models/sevennet.py). */
+FMD_API fmd_status fmd_edge_forces(const float* grad_vec, const int32_t* edge_index, const int64_t* recv_off,
+                                   const int64_t* send_off, const int32_t* send_perm, int64_t n_atoms,
+                                   float* forces, void* stream);
 
 /* The self-connection of the three feature planes (x0 [N, 128], x1
  * [N, 3, 64], x2 [N, 5, 32]): out_l[n, m, c] = sum_u x_l[n, m, u]
