@@ -1099,12 +1099,14 @@ __global__ void __launch_bounds__(kBT) edge_bwd_kernel(EdgeArgs a, FusedWeights 
 
 // ------------------------------------------------ tensor-core radial MLP path
 
-constexpr int kTG = 16;  // edges per tile of the geometry kernels
+constexpr int kTG = 64;  // edges per tile of the geometry kernels (256 threads: geometry per edge, basis
+                         // functions and the first-layer products spread over the CTA)
 
 // geometry, radial features and the first radial layer's pre-activation p1 = phi W1^T of every layer
 // for every edge row (padding rows after the real count: p1 = 0, so the GEMM chain yields R = 0 there)
 __global__ void __launch_bounds__(256) edge_geom_tc_kernel(EdgeArgs a, FusedWeights w, FusedState st) {
-    __shared__ float phi[kTG][16];
+    __shared__ float phi[kTG][17];
+    __shared__ float geo[kTG][3];  // d, 1 / d, cutoff envelope f
     __shared__ float w1t[kMaxLayers][16][kH];
     const int t = threadIdx.x;
     const float pref = sqrtf(2.0f / w.r_max);
@@ -1132,11 +1134,16 @@ __global__ void __launch_bounds__(256) edge_geom_tc_kernel(EdgeArgs a, FusedWeig
             }
             float f, df;
             cutoff_poly(d, w.r_max, w.poly_p, f, df);
-            const float inv = d > 0.f ? 1.0f / d : 0.f;
-            for (int n = 0; n < w.n_basis; ++n) {
-                const float k = float(n + 1) * 3.14159265358979323846f / w.r_max;
-                phi[t][n] = d > 0.f ? pref * sinf(k * d) * inv * f : 0.f;
-            }
+            geo[t][0] = d;
+            geo[t][1] = d > 0.f ? 1.0f / d : 0.f;
+            geo[t][2] = f;
+        }
+        __syncthreads();
+        for (int idx = t; idx < kTG * w.n_basis; idx += 256) {
+            const int e = idx / w.n_basis, n = idx % w.n_basis;
+            const float d = geo[e][0];
+            const float k = float(n + 1) * 3.14159265358979323846f / w.r_max;
+            phi[e][n] = d > 0.f ? pref * sinf(k * d) * geo[e][1] * geo[e][2] : 0.f;
         }
         __syncthreads();
         for (int L = 0; L < w.n_layers; ++L) {
@@ -1167,14 +1174,14 @@ __global__ void __launch_bounds__(256) edge_geom_bwd_tc_kernel(EdgeArgs a, Fused
         const int64_t e0 = tile * kTG;
         const int ne = int(n_edges - e0 < kTG ? n_edges - e0 : kTG);
         __syncthreads();
-        if (t < kTG * 16) dphi[t / 16][t % 16] = 0.f;
+        for (int idx = t; idx < kTG * 16; idx += 256) dphi[idx / 16][idx % 16] = 0.f;
         for (int L = 0; L < w.n_layers; ++L) {
             const float* g1 = st.pre[0][L];
             __syncthreads();
             for (int idx = t; idx < ne * kH; idx += 256) g[idx / kH][idx % kH] = g1[(e0 + idx / kH) * kH + idx % kH];
             __syncthreads();
-            if (t < ne * nb) {
-                const int e = t / nb, n = t % nb;
+            for (int idx = t; idx < ne * nb; idx += 256) {
+                const int e = idx / nb, n = idx % nb;
                 float acc = 0.f;
 #pragma unroll 16
                 for (int c = 0; c < kH; ++c) acc = fmaf(g[e][c], w1[L][c][n], acc);
