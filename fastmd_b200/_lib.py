@@ -24,6 +24,13 @@ class FmdCatPart(ctypes.Structure):
                 ("width", c_int32), ("_pad", c_int32)]
 
 
+class FmdGemmProblem(ctypes.Structure):
+    """One problem of fmd_gemm_tf32x3_grouped (the arguments of fmd_gemm_tf32x3)."""
+    _fields_ = [("x", c_void_p), ("ldx", c_int64), ("w_hi", c_void_p), ("w_lo", c_void_p), ("ldw", c_int64),
+                ("bias", c_void_p), ("c", c_void_p), ("ldc", c_int64), ("y", c_void_p), ("ldy", c_int64),
+                ("m", c_int64), ("n", c_int32), ("k", c_int32), ("act", c_int32), ("accumulate", c_int32)]
+
+
 _P = c_void_p  # every device pointer and the stream travel as void*
 _I64, _I32 = c_int64, c_int32
 
@@ -78,6 +85,7 @@ _SIGNATURES: dict[str, list] = {
     "fmd_wait_probe": [_I32, _P, _P],
     "fmd_tf32_split": [_P, _I64, _I64, _I64, _I32, _P, _P, _I64, _P],
     "fmd_gemm_tf32x3": [_P, _I64, _P, _P, _I64, _P, _P, _I64, _P, _I64, _I64, _I32, _I32, _I32, _I32, _P, _P],
+    "fmd_gemm_tf32x3_grouped": [POINTER(FmdGemmProblem), _I32, _P, _P],
     "fmd_matris_geometry": [_P, _P, _P, _P, _I64, _I64, _P, _P, _P, _P],
     "fmd_matris_bessel": [_P, _P, _I64, _I64, _P, _P, _I32, c_float, c_float, c_float, _P, _P, _I64, _P],
     "fmd_matris_bessel_bwd": [_P, _P, _I64, _I64, _P, _P, _I32, c_float, c_float, c_float, _P, _P, _I64, _P, _P],

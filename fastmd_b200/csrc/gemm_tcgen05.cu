@@ -123,6 +123,32 @@ struct WideArgs {
     uint32_t w_box_bytes;  // bytes of one w_hi / w_lo box (128 B per row of the box)
 };
 
+// Up to kMaxGroup independent problems in one launch (fmd_gemm_tf32x3_grouped): their tiles concatenated
+// in problem order; every role finds a tile's problem from the running tile counts.
+constexpr int kMaxGroup = 4;
+struct Group {
+    WideArgs p[kMaxGroup];
+    int32_t n_problems;
+    int32_t tile_end[kMaxGroup];  // tiles of problems 0 .. p
+};
+struct GroupMaps {
+    CUtensorMap x[kMaxGroup], wh[kMaxGroup], wl[kMaxGroup], y[kMaxGroup];
+};
+
+// the problem of tile t and the tile's index inside it (one problem: index 0 at compile time, so every
+// argument is read at a static parameter offset)
+template <bool GROUPED>
+__device__ __forceinline__ int problem_of(const Group& G, int t, int& local) {
+    if constexpr (!GROUPED) {
+        local = t;
+        return 0;
+    }
+    int p = 0;
+    while (p + 1 < G.n_problems && t >= G.tile_end[p]) ++p;
+    local = t - (p > 0 ? G.tile_end[p - 1] : 0);
+    return p;
+}
+
 // ------------------------------------------------------------- PTX wrappers
 
 __device__ __forceinline__ uint32_t su32(const void* p) {
@@ -404,18 +430,22 @@ __device__ __forceinline__ void finish_values(const WideArgs& g, int64_t row, in
 // at most 64 columns), sums the chunks in FP32 (from zeros, as the reference starts from a zero
 // accumulator), finishes the values and stores them (32 x 32 TMA boxes staged in shared memory, or
 // direct row stores).
-template <int PIECES, int ACC_BUFS>
-__device__ __forceinline__ void epilogue_role(const WideArgs& g, const CUtensorMap* tmap_y, Ctrl& ctl,
+template <int PIECES, int ACC_BUFS, bool GROUPED>
+__device__ __forceinline__ void epilogue_role(const Group& G, const GroupMaps& maps, Ctrl& ctl,
                                               volatile int32_t* abort, uint32_t tmem, unsigned char* epi_smem,
-                                              int warp, int lane, int tiles, int n_tiles, int chunks,
-                                              uint32_t acc_cols) {
+                                              int warp, int lane, int tiles, uint32_t acc_cols) {
     constexpr int W = 32 * PIECES;
     const int q = warp & 3, half = (warp - 8) >> 2;
     int cb = 0;
     uint32_t cph = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-        const int64_t row = int64_t(t / n_tiles) * kBM + q * 32 + lane;
-        const int col0 = (t % n_tiles) * kBN + half * W;
+        int local;
+        const int pi = problem_of<GROUPED>(G, t, local);
+        const WideArgs& g = G.p[pi];
+        const int n_tiles = (g.n + kBN - 1) / kBN;
+        const int chunks = (g.k + kStageK - 1) / kStageK;
+        const int64_t row = int64_t(local / n_tiles) * kBM + q * 32 + lane;
+        const int col0 = (local % n_tiles) * kBN + half * W;
         float acc[W];
 #pragma unroll
         for (int j = 0; j < W; ++j) acc[j] = 0.0f;
@@ -459,7 +489,7 @@ __device__ __forceinline__ void epilogue_role(const WideArgs& g, const CUtensorM
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
                 if (lane == 0 && row0 < g.m && col0 + piece * 32 < g.n)  // boxes with no element in y skipped
-                    tma_store_2d(tmap_y, box, col0 + piece * 32, row0);
+                    tma_store_2d(&maps.y[pi], box, col0 + piece * 32, row0);
             }
         } else if (row < g.m) {
             float* yr = g.y + row * g.ldy;
@@ -481,14 +511,12 @@ __device__ __forceinline__ void epilogue_role(const WideArgs& g, const CUtensorM
             }
         }
     }
-    if (g.tma_y && lane == 0) bulk_wait_all();  // stores complete before the CTA exits
+    if (lane == 0) bulk_wait_all();  // stores complete before the CTA exits
 }
 
-template <bool NARROW>
+template <bool NARROW, bool GROUPED>
 __global__ void __launch_bounds__(kThreads, 1)
-    wide_gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_wh,
-                            const __grid_constant__ CUtensorMap tmap_wl, const __grid_constant__ CUtensorMap tmap_y,
-                            WideArgs g) {
+    wide_gemm_tf32x3_kernel(const __grid_constant__ GroupMaps maps, const __grid_constant__ Group G) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char* ring = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                            ~uintptr_t(1023));
@@ -501,11 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     Ctrl& ctl = *reinterpret_cast<Ctrl*>(epi_smem + kEpiBytes);
     volatile int32_t* abort = &ctl.abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m_tiles = int((g.m + kBM - 1) / kBM);
-    const int n_tiles = (g.n + kBN - 1) / kBN;
-    const int tiles = m_tiles * n_tiles;
-    const int k_stages = (g.k + kStageK - 1) / kStageK;
-    const int chunks = k_stages;  // a chunk accumulator per stage
+    const int tiles = G.tile_end[G.n_problems - 1];  // a chunk accumulator per 64-wide K stage
     constexpr int acc_bufs = NARROW ? kNarrowAccBufs : kAccBufs;
     constexpr uint32_t acc_cols = NARROW ? kNarrowAccCols : kAccCols;
     constexpr uint32_t a_base = acc_bufs * acc_cols;
@@ -543,7 +567,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t ph = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-                const int m0 = (t / n_tiles) * kBM, n0 = (t % n_tiles) * kBN;
+                int local;
+                const int pi = problem_of<GROUPED>(G, t, local);
+                const WideArgs& g = G.p[pi];
+                const int n_tiles = (g.n + kBN - 1) / kBN;
+                const int k_stages = (g.k + kStageK - 1) / kStageK;
+                const int m0 = (local / n_tiles) * kBM, n0 = (local % n_tiles) * kBN;
                 for (int ks = 0; ks < k_stages; ++ks) {
                     if (!mbar_wait(&ctl.empty[s], ph ^ 1u, abort)) {
                         ok = false;
@@ -553,13 +582,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int k0 = ks * kStageK;
                     const bool two = k0 + kBK < g.k;  // the second box holds part of K
                     mbar_expect_tx(&ctl.full[s], (two ? 2u : 1u) * (kTileBytes + 2 * g.w_box_bytes));
-                    tma_load_2d(st, &tmap_x, &ctl.full[s], k0, m0);
-                    tma_load_2d(st + wh_off, &tmap_wh, &ctl.full[s], k0, n0);
-                    tma_load_2d(st + wl_off, &tmap_wl, &ctl.full[s], k0, n0);
+                    tma_load_2d(st, &maps.x[pi], &ctl.full[s], k0, m0);
+                    tma_load_2d(st + wh_off, &maps.wh[pi], &ctl.full[s], k0, n0);
+                    tma_load_2d(st + wl_off, &maps.wl[pi], &ctl.full[s], k0, n0);
                     if (two) {
-                        tma_load_2d(st + kTileBytes, &tmap_x, &ctl.full[s], k0 + kBK, m0);
-                        tma_load_2d(st + wh_off + w_box, &tmap_wh, &ctl.full[s], k0 + kBK, n0);
-                        tma_load_2d(st + wl_off + w_box, &tmap_wl, &ctl.full[s], k0 + kBK, n0);
+                        tma_load_2d(st + kTileBytes, &maps.x[pi], &ctl.full[s], k0 + kBK, m0);
+                        tma_load_2d(st + wh_off + w_box, &maps.wh[pi], &ctl.full[s], k0 + kBK, n0);
+                        tma_load_2d(st + wl_off + w_box, &maps.wl[pi], &ctl.full[s], k0 + kBK, n0);
                     }
                     armed |= 1u << s;
                     armed_ph = (armed_ph & ~(1u << s)) | (ph << s);
@@ -581,7 +610,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t ph = 0, aph = 0, cph = 0;
             bool ok = true, issued = false;
             for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-                const int n0 = (t % n_tiles) * kBN;
+                int local;
+                const WideArgs& g = G.p[problem_of<GROUPED>(G, t, local)];
+                const int n_tiles = (g.n + kBN - 1) / kBN;
+                const int k_stages = (g.k + kStageK - 1) / kStageK;
+                const int n0 = (local % n_tiles) * kBN;
                 const int nw = min(kBN, g.n - n0);
                 const uint32_t idesc = tf32_idesc(kBM, (nw + 15) & ~15);
                 for (int ks = 0; ks < k_stages; ++ks) {
@@ -632,6 +665,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t ph = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+            int local;
+            const WideArgs& g = G.p[problem_of<GROUPED>(G, t, local)];
+            const int k_stages = (g.k + kStageK - 1) / kStageK;
             for (int ks = 0; ks < k_stages; ++ks, ++j) {
                 bool got = mbar_wait(&ctl.full[s], ph, abort);
                 if (got && stages != kABufs && j >= kABufs) {
@@ -678,8 +714,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp >= 8) {
         // --------------------------------------------------------- epilogue
-        epilogue_role<NARROW ? 1 : 2, acc_bufs>(g, &tmap_y, ctl, abort, tmem, epi_smem, warp, lane, tiles, n_tiles,
-                                                chunks, acc_cols);
+        epilogue_role<NARROW ? 1 : 2, acc_bufs, GROUPED>(G, maps, ctl, abort, tmem, epi_smem, warp, lane, tiles, acc_cols);
     }
 
     tc_fence_before();
@@ -690,7 +725,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
                      : "memory");
     }
-    if (threadIdx.x == 0 && ctl.abort) raise_flag(g.flags, FMD_FLAG_WAIT_TIMEOUT);
+    if (threadIdx.x == 0 && ctl.abort) raise_flag(G.p[0].flags, FMD_FLAG_WAIT_TIMEOUT);
 }
 
 // hi = rna_tf32(w), lo = w - hi, row-major [rows, cols] or, with transpose,
@@ -851,17 +886,127 @@ fmd_status device_info(DeviceInfo* out) {
         d.sm100 = major == 10;
         d.sms = sms;
         if (d.sm100) {
-            err = cudaFuncSetAttribute(wide_gemm_tf32x3_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       int(kSmemBytes));
-            if (err == cudaSuccess)
-                err = cudaFuncSetAttribute(wide_gemm_tf32x3_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           int(kSmemBytes));
+            const void* kernels[4] = {(const void*)wide_gemm_tf32x3_kernel<false, false>,
+                                      (const void*)wide_gemm_tf32x3_kernel<true, false>,
+                                      (const void*)wide_gemm_tf32x3_kernel<false, true>,
+                                      (const void*)wide_gemm_tf32x3_kernel<true, true>};
+            for (int i = 0; i < 4 && err == cudaSuccess; ++i)
+                err = cudaFuncSetAttribute(kernels[i], cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes));
             if (err != cudaSuccess) return record_cuda_error(err);
         }
         d.ready = true;
     }
     *out = d;
     return FMD_OK;
+}
+
+// Checks one problem and fills its kernel arguments and tensor maps (narrow: the w boxes hold n rows,
+// rounded up to 16, instead of 128).
+fmd_status check_problem(const fmd_gemm_problem& q) {
+    const int32_t act = q.act;
+    if (q.m == 0 && q.n >= 1 && q.k >= 1) return FMD_OK;  // skipped: nothing is read or written
+    if (q.m < 0 || q.n < 1 || q.k < 1 || q.m > (int64_t(1) << 31) - kBM || q.x == nullptr || q.w_hi == nullptr ||
+        q.w_lo == nullptr || q.y == nullptr || q.ldx < q.k || q.ldw < q.k || q.ldy < q.n ||
+        (q.c != nullptr && q.ldc < q.n) || (act & ~(FMD_ACT_MASK | FMD_ACT_INPUT_SILU)) ||
+        (act & FMD_ACT_MASK) > FMD_ACT_SILU_GRAD || ((act & FMD_ACT_MASK) == FMD_ACT_SILU_GRAD && q.c == nullptr))
+        return FMD_ERR_INVALID_ARGUMENT;
+    // TMA: 16-byte aligned bases and row strides
+    if (!aligned16(q.x) || !aligned16(q.w_hi) || !aligned16(q.w_lo) || (q.ldx & 3) || (q.ldw & 3))
+        return FMD_ERR_UNSUPPORTED;
+    if (((q.m + kBM - 1) / kBM) * ((q.n + kBN - 1) / kBN) > INT32_MAX) return FMD_ERR_UNSUPPORTED;
+    return FMD_OK;
+}
+
+fmd_status prepare_problem(const fmd_gemm_problem& q, bool narrow, EncodeTiled enc, WideArgs& g, CUtensorMap& tx,
+                           CUtensorMap& twh, CUtensorMap& twl, CUtensorMap& ty, int64_t& tiles) {
+    const int32_t act = q.act;
+    tiles = ((q.m + kBM - 1) / kBM) * ((q.n + kBN - 1) / kBN);
+    const uint32_t w_rows = narrow ? uint32_t((q.n + 15) & ~15) : uint32_t(kBN);
+    CUresult r = encode_operand(enc, &tx, q.x, q.m, q.k, q.ldx);
+    if (r == CUDA_SUCCESS) r = encode_operand(enc, &twh, q.w_hi, q.n, q.k, q.ldw, w_rows);
+    if (r == CUDA_SUCCESS) r = encode_operand(enc, &twl, q.w_lo, q.n, q.k, q.ldw, w_rows);
+    if (r != CUDA_SUCCESS) return record_error_text(FMD_ERR_CUDA, "cuTensorMapEncodeTiled failed, CUresult", r);
+    // y through TMA stores (32 x 32 boxes) when its base and row stride allow it
+    memset(&ty, 0, sizeof(ty));
+    const bool tma_y = aligned16(q.y) && (q.ldy & 3) == 0 &&
+                       encode_operand(enc, &ty, q.y, q.m, q.n, q.ldy, 32) == CUDA_SUCCESS;
+    g.bias = q.bias;
+    g.c = q.c;
+    g.ldc = q.ldc;
+    g.y = q.y;
+    g.ldy = q.ldy;
+    g.m = q.m;
+    g.n = q.n;
+    g.k = q.k;
+    g.act = act & FMD_ACT_MASK;
+    g.in_silu = (act & FMD_ACT_INPUT_SILU) != 0;
+    g.accumulate = q.accumulate != 0;
+    g.vec_c = q.c != nullptr && aligned16(q.c) && (q.ldc & 3) == 0;
+    g.vec_y = aligned16(q.y) && (q.ldy & 3) == 0;
+    g.tma_y = tma_y;
+    g.w_box_bytes = w_rows * uint32_t(kBK * sizeof(float));
+    return FMD_OK;
+}
+
+// The launch of up to kMaxGroup problems: narrow (64-column accumulators) when every n <= 64.
+fmd_status launch_group(const fmd_gemm_problem* problems, int32_t n_problems, int32_t* flags, void* stream) {
+    if (problems == nullptr || n_problems < 1 || n_problems > kMaxGroup) return FMD_ERR_INVALID_ARGUMENT;
+    bool any = false;
+    for (int i = 0; i < n_problems; ++i) {
+        const fmd_status bad = check_problem(problems[i]);
+        if (bad != FMD_OK) return bad;
+        any = any || problems[i].m > 0;
+    }
+    DeviceInfo dev;
+    fmd_status st = device_info(&dev);
+    if (st != FMD_OK) return st;
+    if (!dev.sm100) return FMD_ERR_UNSUPPORTED;
+    if (!any) return FMD_OK;
+    const DriverCalls& drv = driver_calls();
+    if (drv.encode == nullptr || drv.ctx_get_current == nullptr)
+        return record_error_text(FMD_ERR_CUDA, "driver entry point cuTensorMapEncodeTiled unavailable", 0);
+    // The tensor-map encoder is a driver call: a host thread on which the runtime has not yet made the
+    // primary context current (a fresh autograd worker, say) gets it bound first.
+    CUcontext current = nullptr;
+    if (drv.ctx_get_current(&current) != CUDA_SUCCESS || current == nullptr) {
+        int dev_index = 0;
+        cudaError_t err = cudaGetDevice(&dev_index);
+        if (err == cudaSuccess) err = cudaSetDevice(dev_index);
+        if (err != cudaSuccess) return record_cuda_error(err);
+    }
+    bool narrow = true;
+    for (int i = 0; i < n_problems; ++i) narrow = narrow && problems[i].n <= int32_t(kNarrowAccCols);
+    GroupMaps maps;
+    Group G;
+    memset(&maps, 0, sizeof(maps));
+    memset(&G, 0, sizeof(G));
+    int64_t total = 0;
+    for (int i = 0; i < n_problems; ++i) {
+        if (problems[i].m == 0) continue;  // nothing to compute
+        int64_t tiles = 0;
+        WideArgs g;
+        memset(&g, 0, sizeof(g));
+        st = prepare_problem(problems[i], narrow, drv.encode, g, maps.x[G.n_problems], maps.wh[G.n_problems],
+                             maps.wl[G.n_problems], maps.y[G.n_problems], tiles);
+        if (st != FMD_OK) return st;
+        g.flags = flags;
+        total += tiles;
+        if (total > INT32_MAX) return FMD_ERR_UNSUPPORTED;
+        G.p[G.n_problems] = g;
+        G.tile_end[G.n_problems] = int32_t(total);
+        ++G.n_problems;
+    }
+    if (G.n_problems == 0) return FMD_OK;
+    const int grid = int(total < dev.sms ? total : dev.sms);
+    const cudaStream_t s = as_stream(stream);
+    if (G.n_problems == 1) {
+        if (narrow) wide_gemm_tf32x3_kernel<true, false><<<grid, kThreads, kSmemBytes, s>>>(maps, G);
+        else wide_gemm_tf32x3_kernel<false, false><<<grid, kThreads, kSmemBytes, s>>>(maps, G);
+    } else {
+        if (narrow) wide_gemm_tf32x3_kernel<true, true><<<grid, kThreads, kSmemBytes, s>>>(maps, G);
+        else wide_gemm_tf32x3_kernel<false, true><<<grid, kThreads, kSmemBytes, s>>>(maps, G);
+    }
+    return check_launch();
 }
 
 }  // namespace
@@ -902,69 +1047,13 @@ fmd_status fmd_tf32_mma_rate(int32_t iters, int32_t* flags, void* stream) {
 fmd_status fmd_gemm_tf32x3(const float* x, int64_t ldx, const float* w_hi, const float* w_lo, int64_t ldw,
                            const float* bias, const float* c, int64_t ldc, float* y, int64_t ldy, int64_t m,
                            int32_t n, int32_t k, int32_t act, int32_t accumulate, int32_t* flags, void* stream) {
-    if (m < 0 || n < 1 || k < 1 || m > (int64_t(1) << 31) - kBM || x == nullptr || w_hi == nullptr ||
-        w_lo == nullptr || y == nullptr || ldx < k || ldw < k || ldy < n || (c != nullptr && ldc < n) ||
-        (act & ~(FMD_ACT_MASK | FMD_ACT_INPUT_SILU)) || (act & FMD_ACT_MASK) > FMD_ACT_SILU_GRAD ||
-        ((act & FMD_ACT_MASK) == FMD_ACT_SILU_GRAD && c == nullptr))
-        return FMD_ERR_INVALID_ARGUMENT;
-    // TMA: 16-byte aligned bases and row strides
-    if (!aligned16(x) || !aligned16(w_hi) || !aligned16(w_lo) || (ldx & 3) || (ldw & 3))
-        return FMD_ERR_UNSUPPORTED;
-    const int64_t tiles = ((m + kBM - 1) / kBM) * ((n + kBN - 1) / kBN);
-    if (tiles > INT32_MAX) return FMD_ERR_UNSUPPORTED;
-    DeviceInfo dev;
-    fmd_status st = device_info(&dev);
-    if (st != FMD_OK) return st;
-    if (!dev.sm100) return FMD_ERR_UNSUPPORTED;
-    if (m == 0) return FMD_OK;
-    const DriverCalls& drv = driver_calls();
-    if (drv.encode == nullptr || drv.ctx_get_current == nullptr)
-        return record_error_text(FMD_ERR_CUDA, "driver entry point cuTensorMapEncodeTiled unavailable", 0);
-    // The tensor-map encoder is a driver call: a host thread on which the runtime has not yet made the
-    // primary context current (a fresh autograd worker, say) gets it bound first.
-    CUcontext current = nullptr;
-    if (drv.ctx_get_current(&current) != CUDA_SUCCESS || current == nullptr) {
-        int dev_index = 0;
-        cudaError_t err = cudaGetDevice(&dev_index);
-        if (err == cudaSuccess) err = cudaSetDevice(dev_index);
-        if (err != cudaSuccess) return record_cuda_error(err);
-    }
-    // n <= 64: one narrow column tile; the w boxes hold its rows rounded up to 16 (the MMA's N)
-    const bool narrow = n <= int32_t(kNarrowAccCols);
-    const uint32_t w_rows = narrow ? uint32_t((n + 15) & ~15) : uint32_t(kBN);
-    CUtensorMap tx, twh, twl;
-    CUresult r = encode_operand(drv.encode, &tx, x, m, k, ldx);
-    if (r == CUDA_SUCCESS) r = encode_operand(drv.encode, &twh, w_hi, n, k, ldw, w_rows);
-    if (r == CUDA_SUCCESS) r = encode_operand(drv.encode, &twl, w_lo, n, k, ldw, w_rows);
-    if (r != CUDA_SUCCESS) return record_error_text(FMD_ERR_CUDA, "cuTensorMapEncodeTiled failed, CUresult", r);
-    // y through TMA stores (32 x 32 boxes) when its base and row stride allow it
-    CUtensorMap ty;
-    memset(&ty, 0, sizeof(ty));
-    const bool tma_y = aligned16(y) && (ldy & 3) == 0 &&
-                       encode_operand(drv.encode, &ty, y, m, n, ldy, 32) == CUDA_SUCCESS;
-    WideArgs g;
-    g.bias = bias;
-    g.c = c;
-    g.ldc = ldc;
-    g.y = y;
-    g.ldy = ldy;
-    g.flags = flags;
-    g.m = m;
-    g.n = n;
-    g.k = k;
-    g.act = act & FMD_ACT_MASK;
-    g.in_silu = (act & FMD_ACT_INPUT_SILU) != 0;
-    g.accumulate = accumulate != 0;
-    g.vec_c = c != nullptr && aligned16(c) && (ldc & 3) == 0;
-    g.vec_y = aligned16(y) && (ldy & 3) == 0;
-    g.tma_y = tma_y;
-    g.w_box_bytes = w_rows * uint32_t(kBK * sizeof(float));
-    const int grid = int(tiles < dev.sms ? tiles : dev.sms);
-    if (narrow)
-        wide_gemm_tf32x3_kernel<true><<<grid, kThreads, kSmemBytes, as_stream(stream)>>>(tx, twh, twl, ty, g);
-    else
-        wide_gemm_tf32x3_kernel<false><<<grid, kThreads, kSmemBytes, as_stream(stream)>>>(tx, twh, twl, ty, g);
-    return check_launch();
+    const fmd_gemm_problem q{x, ldx, w_hi, w_lo, ldw, bias, c, ldc, y, ldy, m, n, k, act, accumulate};
+    return launch_group(&q, 1, flags, stream);
+}
+
+fmd_status fmd_gemm_tf32x3_grouped(const fmd_gemm_problem* problems, int32_t n_problems, int32_t* flags,
+                                   void* stream) {
+    return launch_group(problems, n_problems, flags, stream);
 }
 
 }  // extern "C"

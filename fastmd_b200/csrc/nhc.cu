@@ -5,12 +5,21 @@
 // half step; the thermostat scalars (eta, p_eta, Q) are thread-redundant
 // registers; the only cross-thread work is the block reduction of
 // sum(p^2/m), done 1 + 3*tloop times per half step with a fixed tree
-// (deterministic). This file is compiled with --fmad=false so every
+// (deterministic). A replica of more than 4,096 degrees of freedom runs on a
+// thread-block cluster of CL CTAs of 512 threads (one CTA of 1,024 would hold
+// 16 and more elements per thread in local memory): element
+// (k CL + rank) THREADS + thread,
+// the CTA totals combined through distributed shared memory in rank order,
+// so every CTA of the cluster computes the same thermostat. This file is compiled with --fmad=false so every
 // elementwise operation rounds exactly as the NumPy expressions of ASE do;
 // exp is CUDA's double exp. The chain length is a template parameter so the
 // chain arrays are registers, not local memory.
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace fmd {
 
@@ -57,23 +66,37 @@ __device__ __forceinline__ void p_eta_j(Chain<M>& c, int J, double ke2, double k
     c.pe[J] = pj;
 }
 
-template <int EPT, int THREADS>
+// sum(p^2/m) over the replica: the CTA's block tree, then (CL > 1) the CTA totals of the cluster in rank
+// order; smem[32], smem[33] alternate as the published CTA total (a CTA is never two sums ahead of
+// another: each sum ends with a cluster barrier)
+template <int EPT, int THREADS, int CL>
 __device__ __forceinline__ double ke2_sum(const double (&p)[EPT], const double (&m)[EPT],
-                                          const bool (&live)[EPT], double* smem) {
+                                          const bool (&live)[EPT], double* smem, int& slot) {
     double acc = 0.0;
 #pragma unroll
     for (int k = 0; k < EPT; ++k)
         if (live[k]) acc += (p[k] * p[k]) / m[k];
-    return block_sum<THREADS>(acc, smem);
+    double t = block_sum<THREADS>(acc, smem);
+    if constexpr (CL > 1) {
+        cg::cluster_group cluster = cg::this_cluster();
+        double* pub = smem + 32 + slot;
+        if (threadIdx.x == 0) *pub = t;
+        cluster.sync();
+        t = 0.0;
+#pragma unroll
+        for (int r = 0; r < CL; ++r) t += *cluster.map_shared_rank(pub, r);
+        slot ^= 1;
+    }
+    return t;
 }
 
 // ASE integrate_nhc(p, dt/2) with the Suzuki-Yoshida 4th order sub-steps
-template <int M, int EPT, int THREADS>
+template <int M, int EPT, int THREADS, int CL>
 __device__ void nhc_half(double (&p)[EPT], const double (&m)[EPT], const bool (&live)[EPT],
-                         Chain<M>& c, const double* __restrict__ consts, int tloop, double* smem) {
+                         Chain<M>& c, const double* __restrict__ consts, int tloop, double* smem, int& slot) {
     const double kT = consts[2];
     const double ndof_kT = consts[3];
-    double ke2 = ke2_sum<EPT, THREADS>(p, m, live, smem);
+    double ke2 = ke2_sum<EPT, THREADS, CL>(p, m, live, smem, slot);
     for (int t = 0; t < tloop; ++t) {
 #pragma unroll
         for (int k = 0; k < 3; ++k) {
@@ -88,7 +111,7 @@ __device__ void nhc_half(double (&p)[EPT], const double (&m)[EPT], const bool (&
             const double scale = exp((neg_delta * c.pe[0]) / c.Q[0]);
 #pragma unroll
             for (int e = 0; e < EPT; ++e) p[e] = p[e] * scale;
-            ke2 = ke2_sum<EPT, THREADS>(p, m, live, smem);
+            ke2 = ke2_sum<EPT, THREADS, CL>(p, m, live, smem, slot);
 #pragma unroll
             for (int j = 0; j < M; ++j) p_eta_j<M>(c, j, ke2, kT, ndof_kT, delta2, neg_delta4);
         }
@@ -122,8 +145,8 @@ __device__ __forceinline__ void load_chain(Chain<M>& c, const NhcArgs& a, int64_
 }
 
 template <int M>
-__device__ __forceinline__ void store_chain(const Chain<M>& c, const NhcArgs& a, int64_t n3R, int r) {
-    if (threadIdx.x != 0) return;
+__device__ __forceinline__ void store_chain(const Chain<M>& c, const NhcArgs& a, int64_t n3R, int r, bool writer) {
+    if (!writer) return;
     double* eta = a.state + 3 * n3R + int64_t(r) * M;
     double* pe = a.state + 3 * n3R + int64_t(a.n_replicas) * M + int64_t(r) * M;
 #pragma unroll
@@ -138,10 +161,12 @@ __device__ __forceinline__ double kick_of(double dt2, double f, int f32_kick) {
     return dt2 * f;
 }
 
-template <int M, int EPT, int THREADS>
+template <int M, int EPT, int THREADS, int CL>
 __global__ void __launch_bounds__(THREADS) nhc_pre_force_kernel(NhcArgs a) {
-    __shared__ double smem[32];
-    const int r = blockIdx.x;
+    __shared__ double smem[34];
+    const int r = blockIdx.x / CL, rank = blockIdx.x % CL;
+    const bool writer = rank == 0 && threadIdx.x == 0;
+    int slot = 0;
     const int64_t n3 = 3 * a.n_atoms;
     const int64_t n3R = n3 * a.n_replicas;
     double* q_ptr = a.state + int64_t(r) * n3;
@@ -152,7 +177,7 @@ __global__ void __launch_bounds__(THREADS) nhc_pre_force_kernel(NhcArgs a) {
     bool live[EPT];
 #pragma unroll
     for (int k = 0; k < EPT; ++k) {
-        const int64_t i = threadIdx.x + int64_t(k) * THREADS;
+        const int64_t i = threadIdx.x + (int64_t(k) * CL + rank) * THREADS;
         live[k] = i < n3;
         p[k] = live[k] ? p_ptr[i] : 0.0;
         m[k] = live[k] ? m_ptr[i / 3] : 1.0;
@@ -160,13 +185,13 @@ __global__ void __launch_bounds__(THREADS) nhc_pre_force_kernel(NhcArgs a) {
     Chain<M> c;
     load_chain<M>(c, a, n3R, r);
     // (1) p = integrate_nhc(p, dt/2)
-    nhc_half<M, EPT, THREADS>(p, m, live, c, a.consts, a.tloop, smem);
+    nhc_half<M, EPT, THREADS, CL>(p, m, live, c, a.consts, a.tloop, smem, slot);
     const double dt = a.consts[0];
     const double dt2 = a.consts[1];
 #pragma unroll
     for (int k = 0; k < EPT; ++k) {
         if (!live[k]) continue;
-        const int64_t i = threadIdx.x + int64_t(k) * THREADS;
+        const int64_t i = threadIdx.x + (int64_t(k) * CL + rank) * THREADS;
         // (2) p += dt/2 F(q_n), the cached forces
         const double pk = p[k] + kick_of(dt2, f_ptr[i], a.f32_kick);
         // (3) q += dt p / m
@@ -175,13 +200,16 @@ __global__ void __launch_bounds__(THREADS) nhc_pre_force_kernel(NhcArgs a) {
         p_ptr[i] = pk;
         if (a.positions32) a.positions32[int64_t(r) * n3 + i] = float(q);
     }
-    store_chain<M>(c, a, n3R, r);
+    store_chain<M>(c, a, n3R, r, writer);
+    if constexpr (CL > 1) cg::this_cluster().sync();  // no CTA leaves while another reads its total
 }
 
-template <int M, int EPT, int THREADS>
+template <int M, int EPT, int THREADS, int CL>
 __global__ void __launch_bounds__(THREADS) nhc_post_force_kernel(NhcArgs a) {
-    __shared__ double smem[32];
-    const int r = blockIdx.x;
+    __shared__ double smem[34];
+    const int r = blockIdx.x / CL, rank = blockIdx.x % CL;
+    const bool writer = rank == 0 && threadIdx.x == 0;
+    int slot = 0;
     const int64_t n3 = 3 * a.n_atoms;
     const int64_t n3R = n3 * a.n_replicas;
     double* p_ptr = a.state + n3R + int64_t(r) * n3;
@@ -192,7 +220,7 @@ __global__ void __launch_bounds__(THREADS) nhc_post_force_kernel(NhcArgs a) {
     bool live[EPT];
 #pragma unroll
     for (int k = 0; k < EPT; ++k) {
-        const int64_t i = threadIdx.x + int64_t(k) * THREADS;
+        const int64_t i = threadIdx.x + (int64_t(k) * CL + rank) * THREADS;
         live[k] = i < n3;
         m[k] = live[k] ? m_ptr[i / 3] : 1.0;
         p[k] = 0.0;
@@ -207,26 +235,27 @@ __global__ void __launch_bounds__(THREADS) nhc_post_force_kernel(NhcArgs a) {
     Chain<M> c;
     load_chain<M>(c, a, n3R, r);
     // (5) p = integrate_nhc(p, dt/2)
-    nhc_half<M, EPT, THREADS>(p, m, live, c, a.consts, a.tloop, smem);
+    nhc_half<M, EPT, THREADS, CL>(p, m, live, c, a.consts, a.tloop, smem, slot);
 #pragma unroll
     for (int k = 0; k < EPT; ++k) {
-        const int64_t i = threadIdx.x + int64_t(k) * THREADS;
+        const int64_t i = threadIdx.x + (int64_t(k) * CL + rank) * THREADS;
         if (live[k]) p_ptr[i] = p[k];
     }
-    store_chain<M>(c, a, n3R, r);
-    if (a.energy && threadIdx.x == 0) {
-        a.state[3 * n3R + 2 * int64_t(a.n_replicas) * M + r] = a.energy[r];
-    }
+    store_chain<M>(c, a, n3R, r, writer);
+    if constexpr (CL > 1) cg::this_cluster().sync();  // no CTA leaves while another reads its total
+    if (a.energy && writer) a.state[3 * n3R + 2 * int64_t(a.n_replicas) * M + r] = a.energy[r];
 }
 
 // Step n's second half and step n+1's first half in one launch: p += dt/2 F(q_{n+1}); NHC(dt/2); F, E
 // cached; NHC(dt/2); p += dt/2 F(q_{n+1}); q += dt p / m. The momenta, forces and chain stay in registers
 // between the halves; every operation is the one of the two separate kernels in the same order, so the
 // state is bitwise that of nhc_post_force_kernel followed by nhc_pre_force_kernel.
-template <int M, int EPT, int THREADS>
+template <int M, int EPT, int THREADS, int CL>
 __global__ void __launch_bounds__(THREADS) nhc_post_pre_kernel(NhcArgs a) {
-    __shared__ double smem[32];
-    const int r = blockIdx.x;
+    __shared__ double smem[34];
+    const int r = blockIdx.x / CL, rank = blockIdx.x % CL;
+    const bool writer = rank == 0 && threadIdx.x == 0;
+    int slot = 0;
     const int64_t n3 = 3 * a.n_atoms;
     const int64_t n3R = n3 * a.n_replicas;
     double* q_ptr = a.state + int64_t(r) * n3;
@@ -239,7 +268,7 @@ __global__ void __launch_bounds__(THREADS) nhc_post_pre_kernel(NhcArgs a) {
     bool live[EPT];
 #pragma unroll
     for (int k = 0; k < EPT; ++k) {
-        const int64_t i = threadIdx.x + int64_t(k) * THREADS;
+        const int64_t i = threadIdx.x + (int64_t(k) * CL + rank) * THREADS;
         live[k] = i < n3;
         m[k] = live[k] ? m_ptr[i / 3] : 1.0;
         p[k] = 0.0;
@@ -253,28 +282,48 @@ __global__ void __launch_bounds__(THREADS) nhc_post_pre_kernel(NhcArgs a) {
     }
     Chain<M> c;
     load_chain<M>(c, a, n3R, r);
-    nhc_half<M, EPT, THREADS>(p, m, live, c, a.consts, a.tloop, smem);  // (5) of step n
-    if (a.energy && threadIdx.x == 0) a.state[3 * n3R + 2 * int64_t(a.n_replicas) * M + r] = a.energy[r];
-    nhc_half<M, EPT, THREADS>(p, m, live, c, a.consts, a.tloop, smem);  // (1) of step n+1
+    nhc_half<M, EPT, THREADS, CL>(p, m, live, c, a.consts, a.tloop, smem, slot);  // (5) of step n
+    if (a.energy && writer) a.state[3 * n3R + 2 * int64_t(a.n_replicas) * M + r] = a.energy[r];
+    nhc_half<M, EPT, THREADS, CL>(p, m, live, c, a.consts, a.tloop, smem, slot);  // (1) of step n+1
 #pragma unroll
     for (int k = 0; k < EPT; ++k) {
         if (!live[k]) continue;
-        const int64_t i = threadIdx.x + int64_t(k) * THREADS;
+        const int64_t i = threadIdx.x + (int64_t(k) * CL + rank) * THREADS;
         const double pk = p[k] + kick_of(dt2, f[k], a.f32_kick);  // (2)
         const double q = q_ptr[i] + (dt * pk) / m[k];              // (3)
         q_ptr[i] = q;
         p_ptr[i] = pk;
         if (a.positions32) a.positions32[int64_t(r) * n3 + i] = float(q);
     }
-    store_chain<M>(c, a, n3R, r);
+    store_chain<M>(c, a, n3R, r, writer);
+    if constexpr (CL > 1) cg::this_cluster().sync();  // no CTA leaves while another reads its total
 }
 
-// KIND 0: pre-force half, 1: post-force half, 2: post-force half then the next pre-force half
-template <int KIND, int M, int EPT, int THREADS>
-inline void launch_nhc(const NhcArgs& a, cudaStream_t s) {
-    if (KIND == 0) nhc_pre_force_kernel<M, EPT, THREADS><<<a.n_replicas, THREADS, 0, s>>>(a);
-    else if (KIND == 1) nhc_post_force_kernel<M, EPT, THREADS><<<a.n_replicas, THREADS, 0, s>>>(a);
-    else nhc_post_pre_kernel<M, EPT, THREADS><<<a.n_replicas, THREADS, 0, s>>>(a);
+// KIND 0: pre-force half, 1: post-force half, 2: post-force half then the next pre-force half; CL CTAs
+// (a thread-block cluster) per replica
+template <int KIND, int M, int EPT, int THREADS, int CL = 1>
+inline fmd_status launch_nhc(const NhcArgs& a, cudaStream_t s) {
+    auto kernel = KIND == 0 ? nhc_pre_force_kernel<M, EPT, THREADS, CL>
+                            : (KIND == 1 ? nhc_post_force_kernel<M, EPT, THREADS, CL> : nhc_post_pre_kernel<M, EPT, THREADS, CL>);
+    if constexpr (CL == 1) {
+        kernel<<<a.n_replicas, THREADS, 0, s>>>(a);
+        return check_launch();
+    } else {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(unsigned(a.n_replicas) * CL, 1, 1);
+        cfg.blockDim = dim3(THREADS, 1, 1);
+        cfg.dynamicSmemBytes = 0;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = CL;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, a);
+        return err == cudaSuccess ? check_launch() : record_cuda_error(err);
+    }
 }
 
 // threads and elements per thread from 3n: the fewest threads (multiple of
@@ -282,16 +331,16 @@ inline void launch_nhc(const NhcArgs& a, cudaStream_t s) {
 template <int KIND, int M>
 inline fmd_status dispatch_ept(const NhcArgs& a, cudaStream_t s) {
     const int64_t n3 = 3 * a.n_atoms;
-    if (n3 <= 128) launch_nhc<KIND, M, 1, 128>(a, s);
-    else if (n3 <= 512) launch_nhc<KIND, M, 1, 512>(a, s);
-    else if (n3 <= 1024) launch_nhc<KIND, M, 1, 1024>(a, s);
-    else if (n3 <= 2048) launch_nhc<KIND, M, 2, 1024>(a, s);
-    else if (n3 <= 4096) launch_nhc<KIND, M, 4, 1024>(a, s);
-    else if (n3 <= 8192) launch_nhc<KIND, M, 8, 1024>(a, s);
-    else if (n3 <= 16384) launch_nhc<KIND, M, 16, 1024>(a, s);
-    else if (n3 <= 32768) launch_nhc<KIND, M, 32, 1024>(a, s);
-    else return FMD_ERR_UNSUPPORTED;
-    return check_launch();
+    if (n3 <= 128) return launch_nhc<KIND, M, 1, 128>(a, s);
+    if (n3 <= 512) return launch_nhc<KIND, M, 1, 512>(a, s);
+    if (n3 <= 1024) return launch_nhc<KIND, M, 1, 1024>(a, s);
+    if (n3 <= 2048) return launch_nhc<KIND, M, 2, 1024>(a, s);
+    if (n3 <= 4096) return launch_nhc<KIND, M, 4, 1024>(a, s);
+    // larger replicas: a cluster of 4 or 8 CTAs of 512 threads (registers for the elements and the chain)
+    if (n3 <= 8192) return launch_nhc<KIND, M, 4, 512, 4>(a, s);
+    if (n3 <= 16384) return launch_nhc<KIND, M, 4, 512, 8>(a, s);
+    if (n3 <= 32768) return launch_nhc<KIND, M, 8, 512, 8>(a, s);
+    return FMD_ERR_UNSUPPORTED;
 }
 
 template <int KIND>

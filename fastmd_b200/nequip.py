@@ -113,6 +113,26 @@ def _gemm(model, a: Tensor, w: Tensor, transposed: bool = False, out=None, accum
     return y
 
 
+def _gemms(model, specs) -> list[Tensor]:
+    """Several independent ``_gemm`` calls: on the tensor cores up to four per launch
+    (``fmd_gemm_tf32x3_grouped``, each result bitwise that of its own launch); on the IEEE path one by one.
+    A spec is a dict with keys a, w and optionally transposed, out, accumulate, act, c."""
+    if model.precision != "tf32x3":
+        return [_gemm(model, q["a"], q["w"], q.get("transposed", False), out=q.get("out"),
+                      accumulate=q.get("accumulate", False), act=q.get("act", 0), c=q.get("c")) for q in specs]
+    outs = []
+    for i in range(0, len(specs), 4):
+        group = []
+        for q in specs[i:i + 4]:
+            c = q.get("c")
+            if q.get("accumulate", False):
+                c = q["out"]
+            group.append({"a": q["a"], "weight": q["w"], "transposed": q.get("transposed", False), "c": c,
+                          "out": q.get("out"), "act": q.get("act", 0)})
+        outs.extend(wide_gemm.grouped(group))
+    return outs
+
+
 def _planes(flat: Tensor, n: int, mults) -> tuple[Tensor, ...]:
     """The l planes of a planar buffer as [n (2l + 1), mult] matrices (views)."""
     out, off = [], 0
@@ -136,10 +156,10 @@ class _RadialNet(Function):
         p2s, Ws = [], []
         if model.precision == "tf32x3":
             p1 = _gemm(model, B, model.rad1_all)
-            for L in range(c.num_layers):
-                p2 = _gemm(model, p1[:, L * H:(L + 1) * H], ws[f"L{L}.rad2"], act=_ACT_INPUT_SILU)
-                Ws.append(_gemm(model, p2, ws[f"L{L}.rad3"], act=_ACT_INPUT_SILU))
-                p2s.append(p2)
+            layers = range(c.num_layers)
+            p2s = _gemms(model, [{"a": p1[:, L * H:(L + 1) * H], "w": ws[f"L{L}.rad2"], "act": _ACT_INPUT_SILU}
+                                 for L in layers])
+            Ws = _gemms(model, [{"a": p2s[L], "w": ws[f"L{L}.rad3"], "act": _ACT_INPUT_SILU} for L in layers])
         else:
             p1 = torch.empty((E, c.num_layers * H), device=B.device)
             a1 = _gemm(model, B, model.rad1_all, act=1, y_pre=p1)
@@ -161,16 +181,17 @@ class _RadialNet(Function):
         g1 = torch.empty_like(p1)
         if any(d is None for d in dWs):
             _zero(g1)
-        for L, dW in enumerate(dWs):
-            if dW is None:
-                continue
-            blk = slice(L * H, (L + 1) * H)
-            if model.precision == "tf32x3":
-                g2 = _gemm(model, dW.contiguous(), ws[f"L{L}.rad3"], True, act=_ACT_SILU_GRAD, c=p2s[L])
-                _gemm(model, g2, ws[f"L{L}.rad2"], True, out=g1[:, blk], act=_ACT_SILU_GRAD, c=p1[:, blk])
-            else:
-                da2 = _gemm(model, dW.contiguous(), ws[f"L{L}.rad3"], True)
-                _gemm(model, da2, ws[f"L{L}.rad2"], True, out=g1[:, blk], a_pre=p2s[L])
+        live = [L for L, dW in enumerate(dWs) if dW is not None]
+        blk = lambda L: slice(L * H, (L + 1) * H)  # noqa: E731
+        if model.precision == "tf32x3":
+            g2s = _gemms(model, [{"a": dWs[L].contiguous(), "w": ws[f"L{L}.rad3"], "transposed": True,
+                                  "act": _ACT_SILU_GRAD, "c": p2s[L]} for L in live])
+            _gemms(model, [{"a": g2, "w": ws[f"L{L}.rad2"], "transposed": True, "out": g1[:, blk(L)],
+                            "act": _ACT_SILU_GRAD, "c": p1[:, blk(L)]} for L, g2 in zip(live, g2s)])
+        else:
+            for L in live:
+                da2 = _gemm(model, dWs[L].contiguous(), ws[f"L{L}.rad3"], True)
+                _gemm(model, da2, ws[f"L{L}.rad2"], True, out=g1[:, blk(L)], a_pre=p2s[L])
         if model.precision == "tf32x3":
             dB = _gemm(model, g1, model.rad1_all, True)
         else:
@@ -197,8 +218,7 @@ class _NodeIn(Function):
         xs = (x0.contiguous(), x1.contiguous(), x2.contiguous())
         if first:
             _zero(h[N * MULT[0]:])  # a linear map of an exact zero plane is an exact zero plane
-        for l in range(1 if first else 3):
-            _gemm(model, xs[l], model.lin[f"L{L}.lin1_{l}"], out=hp[l])
+        _gemms(model, [{"a": xs[l], "w": model.lin[f"L{L}.lin1_{l}"], "out": hp[l]} for l in range(1 if first else 3)])
         sc = [torch.empty_like(t) for t in xs]
         call("fmd_nequip_self_connection", ptr(xs[0]), ptr(xs[1]), ptr(xs[2]), ptr(model._elem),
              *[ptr(model.w[f"L{L}.sc{l}"]) for l in range(3)], N, 0, ptr(sc[0]), ptr(sc[1]), ptr(sc[2]),
@@ -222,8 +242,8 @@ class _NodeIn(Function):
              stream(dev))
         if dh is not None:
             dhp = _planes(dh.contiguous(), N, MULT)
-            for l in range(1 if ctx.first else 3):
-                _gemm(model, dhp[l], model.lin[f"L{L}.lin1_{l}"], True, out=dx[l], accumulate=True)
+            _gemms(model, [{"a": dhp[l], "w": model.lin[f"L{L}.lin1_{l}"], "transposed": True, "out": dx[l],
+                            "accumulate": True} for l in range(1 if ctx.first else 3)])
         if ctx.first:
             return dx[0], None, None, None, None
         return dx[0], dx[1], dx[2], None, None
@@ -275,7 +295,7 @@ class _PlanarOut(Function):
         mp = _planes(m, N, M_MULT)
         ctx.model, ctx.L = model, L
         ctx.set_materialize_grads(False)
-        return tuple(_gemm(model, mp[l], model.lin[f"L{L}.lin2_{l}"]) for l in range(3))
+        return tuple(_gemms(model, [{"a": mp[l], "w": model.lin[f"L{L}.lin2_{l}"]} for l in range(3)]))
 
     @staticmethod
     def backward(ctx, d0, d1, d2):
@@ -283,11 +303,13 @@ class _PlanarOut(Function):
         N = model._n
         dm = torch.empty(N * sum(M_MULT[l] * DIM[l] for l in range(3)), device=model.device)
         dmp = _planes(dm, N, M_MULT)
+        specs = []
         for l, g in enumerate((d0, d1, d2)):
             if g is None:
                 _zero(dmp[l])
             else:
-                _gemm(model, g.contiguous(), model.lin[f"L{L}.lin2_{l}"], True, out=dmp[l])
+                specs.append({"a": g.contiguous(), "w": model.lin[f"L{L}.lin2_{l}"], "transposed": True, "out": dmp[l]})
+        _gemms(model, specs)
         return dm, None, None
 
 

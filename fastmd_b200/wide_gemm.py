@@ -118,6 +118,34 @@ def _launch(a: torch.Tensor, weight: torch.Tensor, transposed: bool, precision: 
     return y
 
 
+def grouped(problems) -> list[torch.Tensor]:
+    """Up to 4 independent ``_launch(a, weight, transposed, "tf32x3", bias, c, out, act)`` problems in one
+    ``fmd_gemm_tf32x3_grouped`` launch (each result bitwise that of its own call); ``problems`` are dicts
+    with keys a, weight and optionally transposed, bias, c, out, act. Returns the outputs."""
+    from ._lib import FmdGemmProblem
+
+    if not 1 <= len(problems) <= 4:
+        raise ValueError("one to four problems per grouped launch")
+    arr = (FmdGemmProblem * len(problems))()
+    outs, keep = [], []
+    for i, q in enumerate(problems):
+        a, weight = q["a"], q["weight"]
+        transposed = q.get("transposed", False)
+        m, k = a.shape
+        n = weight.shape[1] if transposed else weight.shape[0]
+        out = q.get("out")
+        y = torch.empty((m, n), device=a.device, dtype=torch.float32) if out is None else out
+        split = _split(weight, transposed)
+        c, bias = q.get("c"), q.get("bias")
+        arr[i] = FmdGemmProblem(ptr(a), a.stride(0), ptr(split.hi), ptr(split.lo), split.hi.stride(0), ptr(bias),
+                                ptr(c), c.stride(0) if c is not None else 0, ptr(y), y.stride(0), m, n, k,
+                                int(q.get("act", 0)), 0)
+        outs.append(y)
+        keep.append(split)
+    call("fmd_gemm_tf32x3_grouped", arr, len(problems), None, stream(problems[0]["a"].device))
+    return outs
+
+
 def _check(a, weight, transposed, bias=None, c=None, out=None, precision="tf32x3") -> torch.Tensor:
     """``a`` in a layout the kernel takes (a copy fixes a row stride or base the TMA cannot use: a row's
     result does not depend on it), after the checks of ``wide_gemm_decline``."""

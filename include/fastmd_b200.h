@@ -557,6 +557,30 @@ FMD_API fmd_status fmd_gemm_tf32x3(const float* x, int64_t ldx, const float* w_h
                                    int32_t n, int32_t k, int32_t act, int32_t accumulate, int32_t* flags,
                                    void* stream);
 
+/* One problem of fmd_gemm_tf32x3_grouped: the arguments of fmd_gemm_tf32x3. */
+typedef struct fmd_gemm_problem {
+    const float* x;
+    int64_t ldx;
+    const float* w_hi;
+    const float* w_lo;
+    int64_t ldw;
+    const float* bias;
+    const float* c;
+    int64_t ldc;
+    float* y;
+    int64_t ldy;
+    int64_t m;
+    int32_t n, k, act, accumulate;
+} fmd_gemm_problem;
+
+/* Up to 4 independent fmd_gemm_tf32x3 problems in one launch (their tiles
+ * concatenated over one persistent grid; each problem's results are those of
+ * its own fmd_gemm_tf32x3 call, bit for bit). For a layer's per-l linears of
+ * the NequIP/SevenNet planes (three small GEMMs whose launches would each cost
+ * the fixed pipeline latency). Problems with m = 0 are skipped. */
+FMD_API fmd_status fmd_gemm_tf32x3_grouped(const fmd_gemm_problem* problems, int32_t n_problems, int32_t* flags,
+                                           void* stream);
+
 /* ------------------------- MACE-architecture message passing (D1, D3, E2) */
 
 /* The message-passing backbone of the MACE-architecture potential behind

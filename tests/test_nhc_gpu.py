@@ -151,3 +151,79 @@ def test_fused_post_pre_half_equals_the_two_halves(cuda, tag, replicas):
         torch.cuda.synchronize()
         assert torch.equal(a.state.flat, b.state.flat), step
         assert torch.equal(a.positions32, b.positions32), step
+
+
+@pytest.mark.parametrize("n", [1500, 5000, 10000])
+def test_large_replica_clusters_match_the_oracle(cuda, n):
+    """A replica of more than 4,096 degrees of freedom runs on a thread-block cluster (4 or 8 CTAs, the
+    kinetic-energy sums combined across the cluster in rank order): 10 steps under harmonic forces
+    against the FP64 oracle NHC (1e-12 of each block's scale), two replicas as a union bitwise equal to
+    each run alone, and the fused post/pre half bitwise equal to the two halves."""
+    from fastmd_b200.gpu_nhc import GPUNoseHooverChainNVT, ReplicaNoseHooverChainNVT
+    from oracle.nhc import NHC
+
+    rng = np.random.default_rng(n)
+    masses = rng.uniform(100.0, 140.0, n)
+    q0 = rng.uniform(0.0, 40.0, (n, 3))
+    p0 = rng.normal(0.0, 2.0, (n, 3))
+    k = 0.7
+    kw = dict(temperature_K=500.0, timestep=0.0245, tdamp=2.45, tchain=3, tloop=1)
+
+    def forces(x, ref):
+        d = x - ref
+        return -k * d, 0.5 * k * float((d * d).sum())
+
+    ref = NHC(masses, q0, p0, np.zeros((n, 3)), **kw)
+    gpu = GPUNoseHooverChainNVT(masses, q0, p0, force_dtype=torch.float64, device=cuda, **kw)
+    q0d = torch.from_numpy(q0).to(cuda)
+    gpu.set_forces(torch.zeros((n, 3), dtype=torch.float64, device=cuda),
+                   torch.zeros(1, dtype=torch.float64, device=cuda))
+    for _ in range(10):
+        x = ref.pre_force()
+        f, e = forces(x, q0)
+        ref.post_force(f, e)
+        xg = gpu.step_pre_force()
+        fg = -k * (xg - q0d)
+        gpu.step_post_force(fg, (0.5 * k * ((xg - q0d) ** 2).sum()).reshape(1))
+    flat = gpu.state.flat.cpu().numpy()
+    want = ref.flat()
+    n3 = 3 * n
+    for lo, hi in ((0, n3), (n3, 2 * n3), (2 * n3, 3 * n3), (3 * n3, 3 * n3 + 6)):
+        scale = max(np.abs(want[lo:hi]).max(), 1e-30)
+        assert np.abs(flat[lo:hi] - want[lo:hi]).max() <= 1e-12 * scale, (lo, hi)
+
+    # two replicas as one union: each bitwise equal to its run alone
+    p1 = rng.normal(0.0, 2.0, (n, 3))
+    union = ReplicaNoseHooverChainNVT(masses, np.concatenate([q0, q0]), np.concatenate([p0, p1]), replicas=2,
+                                      force_dtype=torch.float64, device=cuda, **kw)
+    alone = [GPUNoseHooverChainNVT(masses, q0, pp, force_dtype=torch.float64, device=cuda, **kw) for pp in (p0, p1)]
+    fz = torch.zeros((n, 3), dtype=torch.float64, device=cuda)
+    ez = torch.zeros(1, dtype=torch.float64, device=cuda)
+    union.set_forces(torch.cat([fz, fz]), torch.zeros(2, dtype=torch.float64, device=cuda))
+    for a in alone:
+        a.set_forces(fz, ez)
+    for step in range(3):
+        fu = torch.from_numpy(rng.normal(0.0, 1.0, (2 * n, 3))).to(cuda)
+        union.step_pre_force()
+        union.step_post_force(fu, torch.ones(2, dtype=torch.float64, device=cuda))
+        for r, a in enumerate(alone):
+            a.step_pre_force()
+            a.step_post_force(fu[r * n:(r + 1) * n].contiguous(), torch.ones(1, dtype=torch.float64, device=cuda))
+    torch.cuda.synchronize()
+    uq = union.state.q.reshape(-1)
+    for r, a in enumerate(alone):
+        assert torch.equal(uq[r * n3:(r + 1) * n3], a.state.q.reshape(-1))
+
+    # the fused post/pre half
+    b = GPUNoseHooverChainNVT(masses, q0, p0, force_dtype=torch.float64, device=cuda, **kw)
+    c = GPUNoseHooverChainNVT(masses, q0, p0, force_dtype=torch.float64, device=cuda, **kw)
+    for s_ in (b, c):
+        s_.set_forces(fz, ez)
+        s_.step_pre_force()
+    for step in range(3):
+        f = torch.from_numpy(rng.normal(0.0, 1.0, (n, 3))).to(cuda)
+        b.step_post_force(f, ez)
+        b.step_pre_force()
+        c.step_post_pre_force(f, ez)
+        torch.cuda.synchronize()
+        assert torch.equal(b.state.flat, c.state.flat), step

@@ -196,3 +196,29 @@ def test_input_silu_and_silu_grad_modes(m, n, k):
     lib = _lib.lib()
     assert lib.fmd_gemm_tf32x3(ptr(xd), ldx, ptr(sp.hi), ptr(sp.lo), ldw, None, None, 0, ptr(y), n, m, n, k, 2, 0,
                                None, s) == 1
+
+
+@pytest.mark.parametrize("shapes", [
+    [(5000, 128, 128, 0), (15000, 64, 64, 0), (25000, 32, 32, 0)],        # a NequIP block's per-l linears
+    [(5000, 224, 128, 0), (15000, 64, 384, 0), (25000, 32, 352, 0)],      # their input gradients
+    [(3000, 64, 64, 16), (3000, 64, 64, 16), (777, 48, 100, 0), (129, 8, 320, 0)],  # narrow only, 4 problems
+    [(0, 64, 64, 0), (1000, 256, 264, 1)],                                # an empty problem skipped
+])
+def test_grouped_problems_equal_single_calls(shapes):
+    """fmd_gemm_tf32x3_grouped: each problem's output equals its own fmd_gemm_tf32x3 call bit for bit,
+    whether the group runs as narrow (every n <= 64) or wide tiles."""
+    from fastmd_b200 import wide_gemm
+
+    g = torch.Generator(device="cuda").manual_seed(len(shapes))
+    problems, singles = [], []
+    for m, n, k, act in shapes:
+        ld = (k + 3) // 4 * 4
+        a = torch.randn(m, ld, device="cuda", generator=g)[:, :k]
+        w = torch.randn(n, k, device="cuda", generator=g) / k ** 0.5
+        b = torch.randn(n, device="cuda", generator=g)
+        problems.append({"a": a, "weight": w, "bias": b, "act": act})
+        singles.append(wide_gemm._launch(a, w, False, "tf32x3", b, act=act))
+    outs = wide_gemm.grouped(problems)
+    torch.cuda.synchronize()
+    for y, ref in zip(outs, singles):
+        assert torch.equal(y, ref)
