@@ -83,6 +83,10 @@ struct FusedWeights {
     const float* tc_t_hi[3][kMaxLayers];
     const float* tc_t_lo[3][kMaxLayers];
     int64_t tc_min_edges;             // 0: never
+    // the node path's channel mixings on the tensor cores: TF32 splits of lin0, lin1, out0, out1, up0,
+    // up1 as [out][in] (m = 0..5, the forward mixings) and as [in][out] (m = 6..11, their backward)
+    const float* ntc_hi[12][kMaxLayers];
+    const float* ntc_lo[12][kMaxLayers];
 };
 
 // per-layer activations
@@ -907,6 +911,280 @@ __global__ void __launch_bounds__(kQ * C, 2) sender_node_kernel(GraphArgs gr, Fu
     }
 }
 
+// ------------------------------------------------- node path on the tensor cores
+//
+// For the large replica unions (the tensor-core radial path) of a 2-layer model, every
+// element-independent channel mixing of the node kernels (lin, out and up, forward and backward: a
+// [rows x C] x [C x C] product over all atoms, the scalar rows and the 3 vector rows of each atom as the
+// two problems of one fmd_gemm_tf32x3_grouped launch) runs on the tensor cores; the per-element work
+// stays on the CUDA cores in these kernels: the symmetric contraction and its backward (thread per atom
+// and channel), and, per group of same-element atoms, the skip mixings, the readout and the sender
+// gather. Each kernel's arithmetic is its node kernel's.
+
+// b[i][k] (and bv[i][c][k] = cc v[i][c][k] when bv is given) of the symmetric contraction of layer L
+template <int C>
+__global__ void __launch_bounds__(256) tcn_contract_kernel(FusedWeights w, FusedState st, int L,
+                                                           const float* __restrict__ a0l,
+                                                           const float* __restrict__ a1l, float* __restrict__ b,
+                                                           float* __restrict__ bv, int64_t n) {
+    for (int64_t idx = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; idx < n * C;
+         idx += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t i = idx / C;
+        const int k = int(idx % C);
+        const int64_t z = st.elem[i];
+        const float aa = a0l[i * C + k];
+        const float vx = a1l[i * 3 * C + k], vy = a1l[i * 3 * C + C + k], vz = a1l[i * 3 * C + 2 * C + k];
+        const float* p0 = w.prod0[L] + z * 5 * C + k;
+        const float q = (vx * vx + vy * vy) + vz * vz;
+        const float b0 = (((p0[0] * aa + p0[C] * aa * aa) + p0[2 * C] * q) + p0[3 * C] * aa * aa * aa) + p0[4 * C] * aa * q;
+        b[i * C + k] = b0;
+        if (bv != nullptr) {
+            const float* p1 = w.prod1[L] + z * 4 * C + k;
+            const float cc = ((p1[0] + p1[C] * aa) + p1[2 * C] * aa * aa) + p1[3 * C] * q;
+            bv[i * 3 * C + k] = cc * vx;
+            bv[i * 3 * C + C + k] = cc * vy;
+            bv[i * 3 * C + 2 * C + k] = cc * vz;
+        }
+    }
+}
+
+// last layer, before its output mixing: t = the skip mixing of s_out[L - 1] (per element) into t_out, the
+// layer-0 readout term e_term0 = s_out[0] . r0 (L = 1), and the scalar contraction b0 into b
+template <int C, int G>
+__global__ void __launch_bounds__(kQ * C, 2) tcn_last_pre_kernel(FusedWeights w, FusedState st, int L,
+                                                                 float* __restrict__ t_out, float* __restrict__ b) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    NodeSmem<C>& m = *reinterpret_cast<NodeSmem<C>*>(smem_raw);
+    const int k = threadIdx.x % C, g = threadIdx.x / C;
+    for (int64_t grp = blockIdx.x; grp < node_units<G>(st); grp += gridDim.x) {
+        int atoms[kG];
+        group_atoms<G>(st, grp, atoms);
+        if (atoms[0] < 0) continue;
+        const int64_t z = st.elem[atoms[0]];
+        const int my = atoms[g];
+        const int64_t i = my < 0 ? atoms[0] : my;
+        __syncthreads();
+        m.t[g][k] = st.s_out[L - 1][i * C + k];
+        __syncthreads();
+        if (L - 1 == 0) {  // layer 0's readout, from its output (node_fwd's atom_sum)
+            const float e = atom_sum<C>(m.t[g][k] * w.r0[k], m.sc);
+            if (k == 0 && my >= 0) st.e_term0[my] = e;
+        }
+        mix_rows<C, G, 0>(m.t, w.skip0[L] + z * C * C, nullptr, nullptr, m.t, nullptr, m.red);
+        const float aa = st.A0l[L][i * C + k];
+        const float vx = st.A1l[L][i * 3 * C + k], vy = st.A1l[L][i * 3 * C + C + k],
+                    vz = st.A1l[L][i * 3 * C + 2 * C + k];
+        const float q = (vx * vx + vy * vy) + vz * vz;
+        const float* p0 = w.prod0[L] + z * 5 * C + k;
+        const float b0 = (((p0[0] * aa + p0[C] * aa * aa) + p0[2 * C] * q) + p0[3 * C] * aa * aa * aa) + p0[4 * C] * aa * q;
+        if (my >= 0) {
+            t_out[my * int64_t(C) + k] = m.t[g][k];
+            b[my * int64_t(C) + k] = b0;
+        }
+    }
+}
+
+// last layer, after its output mixing (so = s_out[L], the skip added by the GEMM): the readout MLP, the
+// node energies, ds = dE/d so into ds_out and the skip backward into ds_skip[L]
+template <int C, int G>
+__global__ void __launch_bounds__(kQ * C, 2) tcn_last_post_kernel(FusedWeights w, FusedState st, int L,
+                                                                  float* __restrict__ ds_out) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    NodeSmem<C>& m = *reinterpret_cast<NodeSmem<C>*>(smem_raw);
+    const int k = threadIdx.x % C, g = threadIdx.x / C;
+    const int RH = w.readout_hidden;
+    for (int idx = threadIdx.x; idx < RH * C; idx += kQ * C) m.ra[idx / C][idx % C] = w.ra[idx];
+    for (int64_t grp = blockIdx.x; grp < node_units<G>(st); grp += gridDim.x) {
+        int atoms[kG];
+        group_atoms<G>(st, grp, atoms);
+        if (atoms[0] < 0) continue;
+        const int64_t z = st.elem[atoms[0]];
+        const int my = atoms[g];
+        const int64_t i = my < 0 ? atoms[0] : my;
+        __syncthreads();
+        m.s[g][k] = st.s_out[L][i * C + k];
+        __syncthreads();
+        for (int idx = threadIdx.x; idx < G * RH; idx += kQ * C) {
+            const int gg = idx / RH, j = idx % RH;
+            float acc = 0.f;
+            for (int c = 0; c < C; ++c) acc = fmaf(m.s[gg][c], m.ra[j][c], acc);
+            m.pre[gg][j] = acc;
+        }
+        __syncthreads();
+        if (k == 0 && my >= 0) {
+            float e1 = 0.f;
+            for (int j = 0; j < RH; ++j) e1 = fmaf(w.rb[j], silu_f(m.pre[g][j]), e1);
+            st.node_energy[my] = w.e0[z] + w.scale * (double(st.e_term0[my]) + double(e1)) + w.shift;
+        }
+        const float sc = float(w.scale);
+        float acc = 0.f;
+        for (int j = 0; j < RH; ++j) acc = fmaf(w.rb[j] * silu_g(m.pre[g][j]), m.ra[j][k], acc);
+        const float ds = sc * acc;
+        __syncthreads();
+        m.t[g][k] = ds;
+        __syncthreads();
+        mix_rows<C, G, 0>(m.t, w.skip0t[L] + z * C * C, nullptr, nullptr, m.v, nullptr, m.red);
+        if (my >= 0) {
+            st.ds_skip[L][my * int64_t(C) + k] = m.v[g][k];
+            ds_out[my * int64_t(C) + k] = ds;
+        }
+    }
+}
+
+// last layer, the contraction backward: from db0 (the output mixing's backward) to the lin mixing's
+// input gradients (s: da, v: 2 gq v), in place over db0 / into gv
+template <int C>
+__global__ void __launch_bounds__(256) tcn_last_bwd_kernel(FusedWeights w, FusedState st, int L,
+                                                           float* __restrict__ db, float* __restrict__ gv,
+                                                           int64_t n) {
+    for (int64_t idx = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; idx < n * C;
+         idx += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t i = idx / C;
+        const int k = int(idx % C);
+        const int64_t z = st.elem[i];
+        const float aa = st.A0l[L][i * C + k];
+        const float vx = st.A1l[L][i * 3 * C + k], vy = st.A1l[L][i * 3 * C + C + k],
+                    vz = st.A1l[L][i * 3 * C + 2 * C + k];
+        const float q = (vx * vx + vy * vy) + vz * vz;
+        const float* p0 = w.prod0[L] + z * 5 * C + k;
+        const float db0 = db[i * C + k];
+        const float gq = db0 * (p0[2 * C] + p0[4 * C] * aa);
+        const float da = db0 * (((p0[0] + 2.f * p0[C] * aa) + 3.f * p0[3 * C] * aa * aa) + p0[4 * C] * q);
+        db[i * C + k] = da;
+        gv[i * 3 * C + k] = 2.f * gq * vx;
+        gv[i * 3 * C + C + k] = 2.f * gq * vy;
+        gv[i * 3 * C + 2 * C + k] = 2.f * gq * vz;
+    }
+}
+
+// the sender side of layer L: each atom's gathered edge gradient (the first phase of sender_node) into
+// gs [N][C] and gv [N][3][C]
+template <int C, int G>
+__global__ void __launch_bounds__(kQ * C, 2) tcn_sender_gather_kernel(GraphArgs gr, FusedWeights w, FusedState st,
+                                                                      int L, float* __restrict__ gs,
+                                                                      float* __restrict__ gv) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    NodeSmem<C>& m = *reinterpret_cast<NodeSmem<C>*>(smem_raw);
+    constexpr int CPL = C / 32, NW = C / 32;
+    const int k = threadIdx.x % C, g = threadIdx.x / C;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int ga = warp / NW, wa = warp % NW;
+    float (*redf)[C] = reinterpret_cast<float (*)[C]>(&m.red[0][0][0]);
+    const int P = 4;
+    const float* R = st.R[L];
+    for (int64_t grp = blockIdx.x; grp < node_units<G>(st); grp += gridDim.x) {
+        int atoms[kG];
+        group_atoms<G>(st, grp, atoms);
+        if (atoms[0] < 0) continue;
+        const int my = atoms[g];
+        const int mw = atoms[ga];
+        const int64_t jw = mw < 0 ? atoms[0] : mw;
+        float ds[CPL], dx[CPL], dy[CPL], dz[CPL];
+#pragma unroll
+        for (int qq = 0; qq < CPL; ++qq) ds[qq] = dx[qq] = dy[qq] = dz[qq] = 0.f;
+        for (int64_t t = gr.send_off[jw] + wa; ga < G && t < gr.send_off[jw + 1]; t += NW) {
+            const int64_t e = gr.send_perm[t];
+            const int64_t i = gr.edge_index[2 * e];
+            const float4 y = st.ysh[e];
+            const float* Re = R + e * (P * C) + lane * CPL;
+            const float* a0 = st.dA0[L] + i * C + lane * CPL;
+            const float* a1 = st.dA1[L] + i * 3 * C + lane * CPL;
+            float r0[CPL], r1[CPL], r2v[CPL], r3v[CPL], d0[CPL], dxv[CPL], dyv[CPL], dzv[CPL];
+            ldv<CPL>(Re, r0);
+            ldv<CPL>(Re + C, r1);
+            ldv<CPL>(Re + 2 * C, r2v);
+            ldv<CPL>(Re + 3 * C, r3v);
+            ldv<CPL>(a0, d0);
+            ldv<CPL>(a1, dxv);
+            ldv<CPL>(a1 + C, dyv);
+            ldv<CPL>(a1 + 2 * C, dzv);
+#pragma unroll
+            for (int qq = 0; qq < CPL; ++qq) {
+                const float g0 = d0[qq] * w.inv_avg;
+                const float gx = dxv[qq] * w.inv_avg;
+                const float gy = dyv[qq] * w.inv_avg;
+                const float gz = dzv[qq] * w.inv_avg;
+                ds[qq] = fmaf(r0[qq], g0, ds[qq]);
+                ds[qq] = fmaf(r1[qq], (gx * y.x + gy * y.y) + gz * y.z, ds[qq]);
+                const float r2 = r2v[qq], r3 = r3v[qq] * g0 * kIS3;
+                dx[qq] = fmaf(r2, gx, fmaf(r3, y.x, dx[qq]));
+                dy[qq] = fmaf(r2, gy, fmaf(r3, y.y, dy[qq]));
+                dz[qq] = fmaf(r2, gz, fmaf(r3, y.z, dz[qq]));
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int qq = 0; qq < CPL; ++qq) {
+            const int kk = lane * CPL + qq;
+            redf[(ga * NW + wa) * 4 + 0][kk] = ds[qq];
+            redf[(ga * NW + wa) * 4 + 1][kk] = dx[qq];
+            redf[(ga * NW + wa) * 4 + 2][kk] = dy[qq];
+            redf[(ga * NW + wa) * 4 + 3][kk] = dz[qq];
+        }
+        __syncthreads();
+        float sum[4] = {0.f, 0.f, 0.f, 0.f};
+        if (g < G)
+            for (int wv = 0; wv < NW; ++wv)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) sum[c] += redf[(g * NW + wv) * 4 + c][k];
+        if (my >= 0) {
+            gs[my * int64_t(C) + k] = sum[0];
+#pragma unroll
+            for (int c = 0; c < 3; ++c) gv[my * int64_t(3 * C) + c * C + k] = sum[1 + c];
+        }
+    }
+}
+
+// between the up-mixing backward and the output mixing backward of layer Lp = L - 1 (in place): the skip
+// connection's gradient and the layer-0 readout
+template <int C>
+__global__ void __launch_bounds__(256) tcn_sender_mid_kernel(FusedWeights w, FusedState st, int L,
+                                                             float* __restrict__ s, float* __restrict__ v, int64_t n) {
+    for (int64_t idx = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; idx < n * C;
+         idx += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t i = idx / C;
+        const int k = int(idx % C);
+        float dsi = s[i * C + k];
+        if (st.ds_skip[L]) dsi += st.ds_skip[L][i * C + k];
+        if (L - 1 == 0) dsi = fmaf(float(w.scale), w.r0[k], dsi);
+        s[i * C + k] = dsi;
+        if (st.dv_skip[L])
+#pragma unroll
+            for (int c = 0; c < 3; ++c) v[i * 3 * C + c * C + k] += st.dv_skip[L][i * 3 * C + c * C + k];
+    }
+}
+
+// the product backward of layer Lp (in place): from (db0, b) to (ga, cc b + 2 gq v)
+template <int C>
+__global__ void __launch_bounds__(256) tcn_sender_prod_kernel(FusedWeights w, FusedState st, int Lp,
+                                                              float* __restrict__ s, float* __restrict__ v,
+                                                              int64_t n) {
+    for (int64_t idx = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; idx < n * C;
+         idx += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t i = idx / C;
+        const int k = int(idx % C);
+        const int64_t z = st.elem[i];
+        const float* p0 = w.prod0[Lp] + z * 5 * C + k;
+        const float* p1 = w.prod1[Lp] + z * 4 * C + k;
+        const float aa = st.A0l[Lp][i * C + k];
+        const float vx = st.A1l[Lp][i * 3 * C + k], vy = st.A1l[Lp][i * 3 * C + C + k],
+                    vz = st.A1l[Lp][i * 3 * C + 2 * C + k];
+        const float q = (vx * vx + vy * vy) + vz * vz;
+        const float db0 = s[i * C + k];
+        const float bx = v[i * 3 * C + k], by = v[i * 3 * C + C + k], bz = v[i * 3 * C + 2 * C + k];
+        float ga = db0 * (((p0[0] + 2.f * p0[C] * aa) + 3.f * p0[3 * C] * aa * aa) + p0[4 * C] * q);
+        float gq = db0 * (p0[2 * C] + p0[4 * C] * aa);
+        const float cc = ((p1[0] + p1[C] * aa) + p1[2 * C] * aa * aa) + p1[3 * C] * q;
+        const float bv = (bx * vx + by * vy) + bz * vz;
+        ga += bv * (p1[C] + 2.f * p1[2 * C] * aa);
+        gq += bv * p1[3 * C];
+        s[i * C + k] = ga;
+        v[i * 3 * C + k] = cc * bx + 2.f * gq * vx;
+        v[i * 3 * C + C + k] = cc * by + 2.f * gq * vy;
+        v[i * 3 * C + 2 * C + k] = cc * bz + 2.f * gq * vz;
+    }
+}
+
 // ---------------------------------------------------------------- edge backward
 
 constexpr int kBT = 512;        // threads of the backward edge kernel
@@ -1292,6 +1570,84 @@ __global__ void __launch_bounds__(32 * kForceWarps) forces_kernel(GraphArgs g, c
     }
 }
 
+// the node path's channel mixings on the tensor cores: a 2-layer model with every split present
+bool use_node_tc(const FusedWeights& w, bool radial_tc) {
+    if (!radial_tc || w.n_layers != 2) return false;
+    // layer 0: lin, out (both directions); layer 1 (the last): lin, out0, up (both directions)
+    const int need0[8] = {0, 1, 2, 3, 6, 7, 8, 9};
+    const int need1[10] = {0, 1, 2, 4, 5, 6, 7, 8, 10, 11};
+    for (int m : need0)
+        if (!w.ntc_hi[m][0] || !w.ntc_lo[m][0]) return false;
+    for (int m : need1)
+        if (!w.ntc_hi[m][1] || !w.ntc_lo[m][1]) return false;
+    return true;
+}
+
+// ys = xs W_ms^T (+ cs) over the N scalar rows and yv = xv W_mv^T (+ cv) over the 3N vector rows of layer L's
+// mixing m (one grouped launch; xv null: the scalar rows alone)
+template <int C>
+fmd_status node_mix(const FusedWeights& w, const FusedState& st, int64_t n, int L, int ms, int mv, const float* xs,
+                    float* ys, const float* cs, const float* xv, float* yv, const float* cv, cudaStream_t s) {
+    fmd_gemm_problem q[2] = {
+        {xs, C, w.ntc_hi[ms][L], w.ntc_lo[ms][L], C, nullptr, cs, C, ys, C, n, C, C, 0, 0},
+        {xv, C, w.ntc_hi[mv][L], w.ntc_lo[mv][L], C, nullptr, cv, C, yv, C, 3 * n, C, C, 0, 0}};
+    return fmd_gemm_tf32x3_grouped(q, xv != nullptr ? 2 : 1, st.flags, s);
+}
+
+// node_fwd (L = 0), node_last (L = 1) and sender_node (L = 1) of a 2-layer model on the tensor-core path;
+// the state buffers that are free at each point hold the intermediates
+template <int C>
+fmd_status node_tc_forward(const FusedWeights& w, const FusedState& st, int64_t n, int group_grid, bool single,
+                           size_t node_smem, int L, cudaStream_t s) {
+    const int eg = int((n * C + 255) / 256 < int64_t(kNumSMs) * 8 ? (n * C + 255) / 256 : int64_t(kNumSMs) * 8);
+    fmd_status r = node_mix<C>(w, st, n, L, 0, 1, st.A0[L], st.A0l[L], nullptr, st.A1[L], st.A1l[L], nullptr, s);
+    if (r != FMD_OK) return r;
+    if (L == 0) {  // node_fwd: contraction, output mixing, the next layer's up-mixing
+        tcn_contract_kernel<C><<<eg, 256, 0, s>>>(w, st, L, st.A0l[L], st.A1l[L], st.dA0[L], st.dA1[L], n);
+        if ((r = check_launch()) != FMD_OK) return r;
+        r = node_mix<C>(w, st, n, L, 2, 3, st.dA0[L], st.s_out[L], nullptr, st.dA1[L], st.v_out[L], nullptr, s);
+        if (r != FMD_OK) return r;
+        return node_mix<C>(w, st, n, L + 1, 4, 5, st.s_out[L], st.s_t[L + 1], nullptr, st.v_out[L], st.v_t[L + 1],
+                           nullptr, s);
+    }
+    // node_last: skip and contraction (per element), output mixing + skip, readout and its backward, the
+    // output mixing's backward, the contraction's backward, the lin mixing's backward
+    float* t = st.A0[L];     // the skip term, then db0 and da
+    float* b = st.dA0[L];    // b0
+    float* dsb = st.v_out[L];  // ds (the first N C floats)
+    if (single) tcn_last_pre_kernel<C, 1><<<group_grid, kQ * C, node_smem, s>>>(w, st, L, t, b);
+    else tcn_last_pre_kernel<C, kG><<<group_grid, kQ * C, node_smem, s>>>(w, st, L, t, b);
+    if ((r = check_launch()) != FMD_OK) return r;
+    if ((r = node_mix<C>(w, st, n, L, 2, 3, b, st.s_out[L], t, nullptr, nullptr, nullptr, s)) != FMD_OK) return r;
+    if (single) tcn_last_post_kernel<C, 1><<<group_grid, kQ * C, node_smem, s>>>(w, st, L, dsb);
+    else tcn_last_post_kernel<C, kG><<<group_grid, kQ * C, node_smem, s>>>(w, st, L, dsb);
+    if ((r = check_launch()) != FMD_OK) return r;
+    if ((r = node_mix<C>(w, st, n, L, 8, 9, dsb, t, nullptr, nullptr, nullptr, nullptr, s)) != FMD_OK) return r;
+    tcn_last_bwd_kernel<C><<<eg, 256, 0, s>>>(w, st, L, t, st.A1[L], n);
+    if ((r = check_launch()) != FMD_OK) return r;
+    return node_mix<C>(w, st, n, L, 6, 7, t, st.dA0[L], nullptr, st.A1[L], st.dA1[L], nullptr, s);
+}
+
+template <int C>
+fmd_status node_tc_sender(const GraphArgs& ga, const FusedWeights& w, const FusedState& st, int64_t n,
+                          int group_grid, bool single, size_t node_smem, int L, cudaStream_t s) {
+    const int eg = int((n * C + 255) / 256 < int64_t(kNumSMs) * 8 ? (n * C + 255) / 256 : int64_t(kNumSMs) * 8);
+    const int Lp = L - 1;
+    if (single) tcn_sender_gather_kernel<C, 1><<<group_grid, kQ * C, node_smem, s>>>(ga, w, st, L, st.A0[L], st.A1[L]);
+    else tcn_sender_gather_kernel<C, kG><<<group_grid, kQ * C, node_smem, s>>>(ga, w, st, L, st.A0[L], st.A1[L]);
+    fmd_status r = check_launch();
+    if (r != FMD_OK) return r;
+    r = node_mix<C>(w, st, n, L, 10, 11, st.A0[L], st.s_t[L], nullptr, st.A1[L], st.v_t[L], nullptr, s);
+    if (r != FMD_OK) return r;
+    tcn_sender_mid_kernel<C><<<eg, 256, 0, s>>>(w, st, L, st.s_t[L], st.v_t[L], n);
+    if ((r = check_launch()) != FMD_OK) return r;
+    r = node_mix<C>(w, st, n, Lp, 8, 9, st.s_t[L], st.s_out[Lp], nullptr, st.v_t[L], st.v_out[Lp], nullptr, s);
+    if (r != FMD_OK) return r;
+    tcn_sender_prod_kernel<C><<<eg, 256, 0, s>>>(w, st, Lp, st.s_out[Lp], st.v_out[Lp], n);
+    if ((r = check_launch()) != FMD_OK) return r;
+    return node_mix<C>(w, st, n, Lp, 6, 7, st.s_out[Lp], st.dA0[Lp], nullptr, st.v_out[Lp], st.dA1[Lp], nullptr, s);
+}
+
 template <int C>
 fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeights& w, const FusedState& st,
                        int64_t atoms_per_system, int32_t n_systems, float* forces, double* total, int32_t stages,
@@ -1313,15 +1669,20 @@ fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeigh
     if ((stt = grant_dynamic_smem((const void*)edge_bwd_kernel<C>, sizeof(EdgeBwdSmem))) != FMD_OK) return stt;
     // the six node kernels (three, for 4 and 1 atoms per CTA) share one NodeSmem size: grant each once
     {
-        const void* kernels[6] = {(const void*)node_fwd_kernel<C, kG>,    (const void*)node_fwd_kernel<C, 1>,
-                                  (const void*)node_last_kernel<C, kG>,   (const void*)node_last_kernel<C, 1>,
-                                  (const void*)sender_node_kernel<C, kG>, (const void*)sender_node_kernel<C, 1>};
+        const void* kernels[12] = {(const void*)node_fwd_kernel<C, kG>,    (const void*)node_fwd_kernel<C, 1>,
+                                   (const void*)node_last_kernel<C, kG>,   (const void*)node_last_kernel<C, 1>,
+                                   (const void*)sender_node_kernel<C, kG>, (const void*)sender_node_kernel<C, 1>,
+                                   (const void*)tcn_last_pre_kernel<C, kG>, (const void*)tcn_last_pre_kernel<C, 1>,
+                                   (const void*)tcn_last_post_kernel<C, kG>, (const void*)tcn_last_post_kernel<C, 1>,
+                                   (const void*)tcn_sender_gather_kernel<C, kG>,
+                                   (const void*)tcn_sender_gather_kernel<C, 1>};
         // the largest shared-memory carveout: two CTAs of a node kernel per SM
         for (const void* kernel : kernels)
             if ((stt = grant_dynamic_smem(kernel, node_smem, true)) != FMD_OK) return stt;
     }
     const int L = w.n_layers;
     const bool tc = use_radial_tc(w, st, ea.n_edges);
+    const bool ntc = use_node_tc(w, tc);
     const int geom_grid = int((ea.n_edges + kTG - 1) / kTG < int64_t(kNumSMs) * 8 ? (ea.n_edges + kTG - 1) / kTG
                                                                                   : int64_t(kNumSMs) * 8);
     if (tc && n_tiles > 0 && on(0)) {
@@ -1337,18 +1698,30 @@ fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeigh
             else message_fused_kernel<C, 4><<<atom_grid, 32 * kMsgWarps, 0, s>>>(ga, w, st, l);
         }
         if (l < L - 1 && on(2)) {
-            if (single) node_fwd_kernel<C, 1><<<group_grid, kQ * C, node_smem, s>>>(w, st, l);
+            if (ntc) {
+                if ((stt = check_launch()) != FMD_OK) return stt;
+                if ((stt = node_tc_forward<C>(w, st, ga.n_atoms, group_grid, single, node_smem, l, s)) != FMD_OK)
+                    return stt;
+            } else if (single) node_fwd_kernel<C, 1><<<group_grid, kQ * C, node_smem, s>>>(w, st, l);
             else node_fwd_kernel<C, kG><<<group_grid, kQ * C, node_smem, s>>>(w, st, l);
         }
     }
     if (on(3)) {
-        if (single) node_last_kernel<C, 1><<<group_grid, kQ * C, node_smem, s>>>(w, st, L - 1);
+        if (ntc) {
+            if ((stt = check_launch()) != FMD_OK) return stt;
+            if ((stt = node_tc_forward<C>(w, st, ga.n_atoms, group_grid, single, node_smem, L - 1, s)) != FMD_OK)
+                return stt;
+        } else if (single) node_last_kernel<C, 1><<<group_grid, kQ * C, node_smem, s>>>(w, st, L - 1);
         else node_last_kernel<C, kG><<<group_grid, kQ * C, node_smem, s>>>(w, st, L - 1);
     }
     for (int l = L - 1; l >= 1; --l) {
         if (on(4)) msg_bwd_edge_kernel<C, 4><<<atom_grid, 32 * kMsgBwdWarps, 0, s>>>(ga, w, st, l, l != L - 1);
         if (on(5)) {
-            if (single) sender_node_kernel<C, 1><<<group_grid, kQ * C, node_smem, s>>>(ga, w, st, l);
+            if (ntc) {
+                if ((stt = check_launch()) != FMD_OK) return stt;
+                if ((stt = node_tc_sender<C>(ga, w, st, ga.n_atoms, group_grid, single, node_smem, l, s)) != FMD_OK)
+                    return stt;
+            } else if (single) sender_node_kernel<C, 1><<<group_grid, kQ * C, node_smem, s>>>(ga, w, st, l);
             else sender_node_kernel<C, kG><<<group_grid, kQ * C, node_smem, s>>>(ga, w, st, l);
         }
     }
@@ -1411,6 +1784,11 @@ fmd_status fmd_mace_fused_step(const fmd_mace_fused_weights* weights, const fmd_
     w.scale = h.scale; w.shift = h.shift; w.n_layers = h.n_layers; w.n_basis = h.n_basis; w.poly_p = h.poly_p;
     w.readout_hidden = h.readout_hidden; w.r_max = h.r_max; w.inv_avg = h.inv_avg;
     w.tc_min_edges = h.radial_tc_min_edges;
+    for (int m = 0; m < 12; ++m)
+        for (int l = 0; l < h.n_layers; ++l) {
+            w.ntc_hi[m][l] = h.node_tc_hi[m][l];
+            w.ntc_lo[m][l] = h.node_tc_lo[m][l];
+        }
     for (int k = 0; k < 3; ++k)
         for (int l = 0; l < h.n_layers; ++l) {
             w.tc_hi[k][l] = h.radial_tc_hi[k][l]; w.tc_lo[k][l] = h.radial_tc_lo[k][l];

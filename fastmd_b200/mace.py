@@ -421,7 +421,7 @@ def _struct_types():
             ("poly_p", ctypes.c_int32), ("readout_hidden", ctypes.c_int32), ("radial_hidden", ctypes.c_int32),
             ("r_max", ctypes.c_float), ("inv_avg", ctypes.c_float), ("_pad", ctypes.c_int32)] + [
             (name, arr * 3) for name in ("radial_tc_hi", "radial_tc_lo", "radial_tc_t_hi", "radial_tc_t_lo")] + [
-            ("radial_tc_min_edges", ctypes.c_int64)]
+            ("radial_tc_min_edges", ctypes.c_int64), ("node_tc_hi", arr * 12), ("node_tc_lo", arr * 12)]
 
     class FusedState(ctypes.Structure):
         _fields_ = [(name, arr) for name in (
@@ -511,6 +511,24 @@ def _fused_weights(model: "MACEModel"):
                     keep[f"{L}.{hi_name}{k}"], keep[f"{L}.{lo_name}{k}"] = hi, lo
                     getattr(fw, hi_name)[k][L] = ptr(hi)
                     getattr(fw, lo_name)[k][L] = ptr(lo)
+        # the node kernels' channel mixings on the tensor cores (a 2-layer model): [out][in] splits for the
+        # forward mixings (index m) and [in][out] splits for their backward (6 + m)
+        if c.num_interactions == 2:
+            for L in range(c.num_interactions):
+                for m, name in enumerate(("lin0", "lin1", "out0", "out1", "up0", "up1")):
+                    key = f"{L}.{name}"
+                    if key not in w or (L == 0 and name in ("up0", "up1")):
+                        continue  # layer 0's up-mixing is the embedding table
+                    wk = w[key].contiguous()
+                    for transposed in (0, 1):
+                        hi = torch.empty_like(wk)
+                        lo = torch.empty_like(wk)
+                        call("fmd_tf32_split", ptr(wk), wk.shape[0], wk.shape[1], wk.shape[1], transposed, ptr(hi),
+                             ptr(lo), wk.shape[1], s)
+                        idx = m + 6 * transposed
+                        keep[f"{key}.ntc_hi{transposed}"], keep[f"{key}.ntc_lo{transposed}"] = hi, lo
+                        fw.node_tc_hi[idx][L] = ptr(hi)
+                        fw.node_tc_lo[idx][L] = ptr(lo)
     return fw, keep
 
 
@@ -563,6 +581,7 @@ class _FusedBuffers:
                     st.radial_pre[k][L] = ptr(self.t[f"{L}.pre{k}"])
         st.flags = ptr(_lib.flags_word(dev))
         self.tensor_core_radial = False  # whether the last step took the tensor-core radial path
+        self.tensor_core_nodes = False   # and the node mixings on the tensor cores
         self.state = st
         self.energy: dict[int, Tensor] = {}
 
@@ -585,6 +604,8 @@ def _energy_forces_fused(self: "MACEModel", batch, n_systems: int = 1, stages: i
         buf = _FusedBuffers(self, N, cap, batch.element)
         self._fused_bufs[key] = buf
     buf.tensor_core_radial = 0 < self.radial_tc_min_edges <= E
+    # the node kernels' channel mixings on the tensor cores as well (2-layer models)
+    buf.tensor_core_nodes = buf.tensor_core_radial and self.config.num_interactions == 2
     if n_systems not in buf.energy:
         buf.energy[n_systems] = torch.zeros(n_systems, dtype=torch.float64, device=self.device)
     energy, forces = buf.energy[n_systems], buf.t["forces"]

@@ -736,6 +736,12 @@ typedef struct fmd_mace_fused_weights {
     const float* radial_tc_t_hi[3][FMD_MACE_MAX_LAYERS];
     const float* radial_tc_t_lo[3][FMD_MACE_MAX_LAYERS];
     int64_t radial_tc_min_edges;
+    /* the node kernels' channel mixings on the tensor cores (with the radial path,
+     * 2-layer models): TF32 hi / lo splits (fmd_tf32_split) of lin0, lin1, out0,
+     * out1, up0, up1 as [out][in] (index 0..5) and as [in][out] (6..11); NULL:
+     * the mixings stay in the node kernels on the CUDA cores */
+    const float* node_tc_hi[12][FMD_MACE_MAX_LAYERS];
+    const float* node_tc_lo[12][FMD_MACE_MAX_LAYERS];
 } fmd_mace_fused_weights;
 
 /* Persistent activations of the fused step (caller-owned device buffers,

@@ -205,8 +205,9 @@ def test_fused_replica_union_equals_single_systems(cuda, R):
 
 
 def test_fused_tensor_core_radial_matches_oracle(cuda):
-    """The radial MLPs and their backward as the tcgen05 3xTF32 GEMM chain (forced on the 135-atom
-    graph) against the FP64 oracle and the IEEE edge kernels, to the benchmark's 1e-5."""
+    """The radial MLPs and their backward as the tcgen05 3xTF32 GEMM chain, and the node kernels' channel
+    mixings as grouped tcgen05 GEMMs (forced on the 135-atom graph), against the FP64 oracle and the IEEE
+    CUDA-core kernels, to the benchmark's 1e-5."""
     from fastmd_b200.mace import MACEModel
     from fastmd_b200.ops import read_flags
 
@@ -216,6 +217,7 @@ def test_fused_tensor_core_radial_matches_oracle(cuda):
     tc = MACEModel(device=cuda, radial_precision="tf32x3")
     energy, forces = (x.clone() for x in tc.energy_forces_fused(batch))
     assert next(iter(tc._fused_bufs.values())).tensor_core_radial
+    assert next(iter(tc._fused_bufs.values())).tensor_core_nodes
     E, F, _ = _oracle(tc, batch, numbers)
     _close(energy.cpu().numpy(), E)
     _close(forces.cpu().numpy(), F)
@@ -243,6 +245,7 @@ def test_fused_tensor_core_radial_on_a_large_union(cuda):
     auto = MACEModel(device=cuda)
     energy, forces = (x.clone() for x in auto.energy_forces_fused(batch, n_systems=R))
     assert next(iter(auto._fused_bufs.values())).tensor_core_radial
+    assert next(iter(auto._fused_bufs.values())).tensor_core_nodes
     ieee = MACEModel(device=cuda, radial_precision="ieee")
     ei, fi = ieee.energy_forces_fused(batch, n_systems=R)
     for r in range(R):
