@@ -533,15 +533,22 @@ def _roofline(md, device):
     hbm, _, kind = _peaks()
     names = dict(STAGES)
     E_rows = int(md.builder.batch.edge_index.shape[0])
+    c = md.model.config
+    layers = c.num_interactions
     if 0 < md.model.radial_tc_min_edges <= E_rows:
         # a large union: the radial MLPs run as chained tcgen05 GEMMs (several kernels per stage)
         names[0] = ("radial MLP forward (edge_geom_tc + 6 tcgen05 3xTF32 GEMMs)", 7)
         names[6] = ("radial MLP backward (6 tcgen05 3xTF32 GEMMs + edge_geom_bwd_tc)", 7)
+        if layers == 2:  # and the node kernels' channel mixings as grouped tcgen05 GEMMs
+            names[2] = ("node_fwd on the tensor cores (3 grouped tcgen05 GEMMs + the contraction kernel)", 4)
+            names[3] = ("node_last on the tensor cores (4 grouped tcgen05 GEMMs + 3 CUDA-core kernels)", 7)
+            names[5] = ("sender side on the tensor cores (3 grouped tcgen05 GEMMs + 3 CUDA-core kernels)", 6)
     stages = {names[bit][0]: round(_time_stage(md, device, bit), 3) for bit in names}
-    single = {bit: stages[names[bit][0]] for bit in names if names[bit][1] == 1}
-    bit = max(single, key=single.get)
-    us = single[bit]
-    c = md.model.config
+    # the single-kernel launches: a stage of one kernel, or of one kernel per layer (per-launch average)
+    per_launch = {bit: stages[names[bit][0]] / (layers if names[bit][1] == 2 else 1)
+                  for bit in names if names[bit][1] in (1, 2)}
+    bit = max(per_launch, key=per_launch.get)
+    us = per_launch[bit]
     N = md.builder.n_real
     E = int(md.builder.batch.n_edges.item())
     pc = sum(c.paths(L) * c.channels for L in range(c.num_interactions))
@@ -554,10 +561,22 @@ def _roofline(md, device):
             6: (E * (16 + 12 + 12 + 4 * pc) + weights,
                 2.0 * E * sum(2 * (c.num_bessel * 64 + 2 * 64 * 64) + 64 * c.paths(L) * c.channels
                               for L in range(c.num_interactions)))}
+    # the per-layer edge kernels (average per launch over the layers): message_fused reads the R row (P_L C
+    # floats), 16 B of harmonics and the sender index per edge and the sender rows and writes the A rows once
+    # per atom; msg_bwd_edge reads half the R row and writes the dR row per edge, plus dY, and reads the dA
+    # and sender rows once per atom
+    C = c.channels
+    P = [c.paths(L) for L in range(layers)]
+    sender = [4 * (C + (3 * C if P[L] == 4 else 0)) for L in range(layers)]
+    algo[1] = (sum(E * (4 * P[L] * C + 20) + N * (sender[L] + 16 * C + 8) for L in range(layers)) / layers,
+               sum(2.0 * E * C * (2 + 6 * (P[L] == 4)) for L in range(layers)) / layers)
+    algo[4] = (sum(E * (2 * P[L] * C + 4 * P[L] * C + 20 + 12 * (1 + (L != layers - 1))) + N * (16 * C + sender[L])
+                   for L in range(layers)) / layers,
+               sum(2.0 * E * C * (4 + 8 * (P[L] == 4)) for L in range(layers)) / layers)
     # the node-side stages (2-layer model: node_fwd at layer 0, node_last and sender_node at layer 1); rows of
     # C floats per atom read or written once, R rows of P_L C floats and 16 B of harmonics per edge, the
     # C x C mixings once from HBM (per-element skip and product weights included)
-    C, Lz = c.channels, c.num_interactions - 1
+    Lz = c.num_interactions - 1
     mix = 4 * C * C
     per_elem = 4 * c.num_elements * (2 * C * C + 9 * C)
     if c.num_interactions == 2:
@@ -583,7 +602,8 @@ def _roofline(md, device):
            "peak_source": f"{kind} (MEASURED_PEAKS.json hbm_gbs)" if kind == "measured" else "fallback 6650 GB/s",
            "avg_launch_us": us, "stages_us": stages, "traffic": traffic, "edges": E, "atoms": N,
            "note": ("135 atoms / 2,054 edges: every stage is latency-bound" if N <= 135 else
-                    "node stages: gathers of edge rows and C x C channel mixings on the CUDA cores")}
+                    "the dominant launch of a single kernel (per-layer stages: the average launch); the multi-kernel "
+                    "stages (radial chains, the node sequences of grouped tcgen05 GEMMs) are timed in stages_us")}
     if bytes_ is not None:
         achieved = bytes_ / (us * 1e-6) / 1e9
         out.update({"achieved": achieved, "frac": achieved / hbm, "algorithmic_bytes_per_launch": bytes_,
