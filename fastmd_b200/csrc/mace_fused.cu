@@ -989,6 +989,7 @@ __global__ void __launch_bounds__(kQ * C, 2) tcn_last_pre_kernel(FusedWeights w,
 template <int C, int G>
 __global__ void __launch_bounds__(kQ * C, 2) tcn_last_post_kernel(FusedWeights w, FusedState st, int L,
                                                                   float* __restrict__ ds_out) {
+    static_assert((C & (C - 1)) == 0, "the readout's channel rotation wraps with a mask");
     extern __shared__ __align__(16) unsigned char smem_raw[];
     NodeSmem<C>& m = *reinterpret_cast<NodeSmem<C>*>(smem_raw);
     const int k = threadIdx.x % C, g = threadIdx.x / C;
@@ -1004,10 +1005,15 @@ __global__ void __launch_bounds__(kQ * C, 2) tcn_last_post_kernel(FusedWeights w
         __syncthreads();
         m.s[g][k] = st.s_out[L][i * C + k];
         __syncthreads();
+        // pre_j = s . ra_j: thread (atom, j) walks the channels from c = j on (rows of ra are C floats apart,
+        // one bank: starting each j on its own channel keeps the 16 threads' reads on different banks)
         for (int idx = threadIdx.x; idx < G * RH; idx += kQ * C) {
             const int gg = idx / RH, j = idx % RH;
             float acc = 0.f;
-            for (int c = 0; c < C; ++c) acc = fmaf(m.s[gg][c], m.ra[j][c], acc);
+            for (int cc = 0; cc < C; ++cc) {
+                const int c = (cc + j) & (C - 1);
+                acc = fmaf(m.s[gg][c], m.ra[j][c], acc);
+            }
             m.pre[gg][j] = acc;
         }
         __syncthreads();
