@@ -1391,7 +1391,7 @@ constexpr int kTG = 64;  // edges per tile of the geometry kernels (256 threads:
 __global__ void __launch_bounds__(256) edge_geom_tc_kernel(EdgeArgs a, FusedWeights w, FusedState st) {
     __shared__ float phi[kTG][17];
     __shared__ float geo[kTG][3];  // d, 1 / d, cutoff envelope f
-    __shared__ float w1t[kMaxLayers][16][kH];
+    __shared__ __align__(16) float w1t[kMaxLayers][16][kH];
     const int t = threadIdx.x;
     const float pref = sqrtf(2.0f / w.r_max);
     const int64_t n_real = real_edges(a);
@@ -1430,13 +1430,22 @@ __global__ void __launch_bounds__(256) edge_geom_tc_kernel(EdgeArgs a, FusedWeig
             phi[e][n] = d > 0.f ? pref * sinf(k * d) * geo[e][1] * geo[e][2] : 0.f;
         }
         __syncthreads();
+        // p1[e][k] = sum_n phi[e][n] W1^T[n][k] in n order: thread (edge, 4 channels) holds the edge's basis in
+        // registers and reads W1^T four channels per 16-byte broadcast, stores four channels per float4
         for (int L = 0; L < w.n_layers; ++L) {
             float* p1 = st.pre[0][L];
-            for (int idx = t; idx < ne * kH; idx += 256) {
-                const int e = idx / kH, k = idx % kH;
-                float acc = 0.f;
-                for (int n = 0; n < w.n_basis; ++n) acc = fmaf(phi[e][n], w1t[L][n][k], acc);
-                p1[(e0 + e) * kH + k] = acc;
+            for (int idx = t; idx < ne * (kH / 4); idx += 256) {
+                const int e = idx / (kH / 4), k = (idx % (kH / 4)) * 4;
+                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int n = 0; n < w.n_basis; ++n) {
+                    const float ph = phi[e][n];
+                    const float4 wv = *reinterpret_cast<const float4*>(&w1t[L][n][k]);
+                    acc.x = fmaf(ph, wv.x, acc.x);
+                    acc.y = fmaf(ph, wv.y, acc.y);
+                    acc.z = fmaf(ph, wv.z, acc.z);
+                    acc.w = fmaf(ph, wv.w, acc.w);
+                }
+                *reinterpret_cast<float4*>(p1 + (e0 + e) * kH + k) = acc;
             }
         }
     }
@@ -1445,13 +1454,16 @@ __global__ void __launch_bounds__(256) edge_geom_tc_kernel(EdgeArgs a, FusedWeig
 // dphi = sum over layers of g1 W1 (g1 = dE/dp1, left in the p1 buffer by the GEMM chain), then the
 // geometry backward of every real edge
 __global__ void __launch_bounds__(256) edge_geom_bwd_tc_kernel(EdgeArgs a, FusedWeights w, FusedState st) {
-    __shared__ float w1[kMaxLayers][kH][17];  // W1 [hidden][basis] (padded rows)
+    __shared__ __align__(16) float w1[kMaxLayers][kH][16];  // W1 [hidden][basis]
     __shared__ float g[kTG][kH + 1];
     __shared__ float dphi[kTG][16];
     const int t = threadIdx.x;
     const int nb = w.n_basis;
     for (int L = 0; L < w.n_layers; ++L)
-        for (int idx = t; idx < kH * nb; idx += 256) w1[L][idx / nb][idx % nb] = w.w1[L][idx];
+        for (int idx = t; idx < kH * 16; idx += 256) {
+            const int c = idx / 16, n = idx % 16;
+            w1[L][c][n] = n < nb ? w.w1[L][c * nb + n] : 0.f;
+        }
     const int64_t n_edges = real_edges(a);
     const int64_t n_tiles = (n_edges + kTG - 1) / kTG;
     for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
@@ -1464,12 +1476,25 @@ __global__ void __launch_bounds__(256) edge_geom_bwd_tc_kernel(EdgeArgs a, Fused
             __syncthreads();
             for (int idx = t; idx < ne * kH; idx += 256) g[idx / kH][idx % kH] = g1[(e0 + idx / kH) * kH + idx % kH];
             __syncthreads();
-            for (int idx = t; idx < ne * nb; idx += 256) {
-                const int e = idx / nb, n = idx % nb;
-                float acc = 0.f;
+            // dphi[e][n] += sum_c g[e][c] W1[c][n] in c order: thread (edge, 4 basis functions), the W1 row read
+            // four basis functions per 16-byte broadcast
+            for (int idx = t; idx < ne * 4; idx += 256) {
+                const int e = idx >> 2, n0 = (idx & 3) * 4;
+                if (n0 >= nb) continue;
+                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 16
-                for (int c = 0; c < kH; ++c) acc = fmaf(g[e][c], w1[L][c][n], acc);
-                dphi[e][n] += acc;
+                for (int c = 0; c < kH; ++c) {
+                    const float gv = g[e][c];
+                    const float4 wv = *reinterpret_cast<const float4*>(&w1[L][c][n0]);
+                    acc.x = fmaf(gv, wv.x, acc.x);
+                    acc.y = fmaf(gv, wv.y, acc.y);
+                    acc.z = fmaf(gv, wv.z, acc.z);
+                    acc.w = fmaf(gv, wv.w, acc.w);
+                }
+                dphi[e][n0] += acc.x;
+                if (n0 + 1 < nb) dphi[e][n0 + 1] += acc.y;
+                if (n0 + 2 < nb) dphi[e][n0 + 2] += acc.z;
+                if (n0 + 3 < nb) dphi[e][n0 + 3] += acc.w;
             }
         }
         __syncthreads();
