@@ -989,7 +989,7 @@ __global__ void __launch_bounds__(kQ * C, 2) tcn_last_pre_kernel(FusedWeights w,
 template <int C, int G>
 __global__ void __launch_bounds__(kQ * C, 2) tcn_last_post_kernel(FusedWeights w, FusedState st, int L,
                                                                   float* __restrict__ ds_out) {
-    static_assert((C & (C - 1)) == 0, "the readout's channel rotation wraps with a mask");
+    static_assert((C & (C - 1)) == 0 && C >= 32, "the readout's channel rotation wraps with a mask");
     extern __shared__ __align__(16) unsigned char smem_raw[];
     NodeSmem<C>& m = *reinterpret_cast<NodeSmem<C>*>(smem_raw);
     const int k = threadIdx.x % C, g = threadIdx.x / C;
@@ -1005,26 +1005,47 @@ __global__ void __launch_bounds__(kQ * C, 2) tcn_last_post_kernel(FusedWeights w
         __syncthreads();
         m.s[g][k] = st.s_out[L][i * C + k];
         __syncthreads();
-        // pre_j = s . ra_j: thread (atom, j) walks the channels from c = j on (rows of ra are C floats apart,
-        // one bank: starting each j on its own channel keeps the 16 threads' reads on different banks)
-        for (int idx = threadIdx.x; idx < G * RH; idx += kQ * C) {
-            const int gg = idx / RH, j = idx % RH;
+        // pre_j = s . ra_j: with RH = 16, thread (atom, j, eighth of the channels) sums C / 8 channels (walked
+        // from a start that keeps a warp's reads on distinct banks), then a 3-step shuffle over the eighths;
+        // otherwise thread (atom, j) walks all channels from c = j on
+        if (RH == 16 && kQ * C >= kG * 16 * 8) {
+            constexpr int CE = C / 8;
+            const int gg = threadIdx.x / 128, j = (threadIdx.x >> 3) & 15, part = threadIdx.x & 7;
             float acc = 0.f;
-            for (int cc = 0; cc < C; ++cc) {
-                const int c = (cc + j) & (C - 1);
-                acc = fmaf(m.s[gg][c], m.ra[j][c], acc);
+            if (gg < G) {
+                for (int cc = 0; cc < CE; ++cc) {
+                    const int c = part * CE + ((cc + j + 4 * (part >> 1)) & (CE - 1));
+                    acc = fmaf(m.s[gg][c], m.ra[j][c], acc);
+                }
             }
-            m.pre[gg][j] = acc;
+            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+            acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+            if (part == 0 && gg < G) m.pre[gg][j] = acc;
+        } else {
+            for (int idx = threadIdx.x; idx < G * RH; idx += kQ * C) {
+                const int gg = idx / RH, j = idx % RH;
+                float acc = 0.f;
+                for (int cc = 0; cc < C; ++cc) {
+                    const int c = (cc + j) & (C - 1);
+                    acc = fmaf(m.s[gg][c], m.ra[j][c], acc);
+                }
+                m.pre[gg][j] = acc;
+            }
         }
         __syncthreads();
+        // the energy (thread (atom, 0)) and the readout backward's coefficients rb_j silu'(pre_j), once per
+        // (atom, j)
         if (k == 0 && my >= 0) {
             float e1 = 0.f;
             for (int j = 0; j < RH; ++j) e1 = fmaf(w.rb[j], silu_f(m.pre[g][j]), e1);
             st.node_energy[my] = w.e0[z] + w.scale * (double(st.e_term0[my]) + double(e1)) + w.shift;
         }
+        if (k < RH) m.sc[g][k] = w.rb[k] * silu_g(m.pre[g][k]);
+        __syncthreads();
         const float sc = float(w.scale);
         float acc = 0.f;
-        for (int j = 0; j < RH; ++j) acc = fmaf(w.rb[j] * silu_g(m.pre[g][j]), m.ra[j][k], acc);
+        for (int j = 0; j < RH; ++j) acc = fmaf(m.sc[g][j], m.ra[j][k], acc);
         const float ds = sc * acc;
         __syncthreads();
         m.t[g][k] = ds;
