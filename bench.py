@@ -541,7 +541,7 @@ def _roofline(md, device):
         names[6] = ("radial MLP backward (6 tcgen05 3xTF32 GEMMs + edge_geom_bwd_tc)", 7)
         if layers == 2:  # and the node kernels' channel mixings as grouped tcgen05 GEMMs
             names[2] = ("node_fwd on the tensor cores (3 grouped tcgen05 GEMMs + the contraction kernel)", 4)
-            names[3] = ("node_last on the tensor cores (4 grouped tcgen05 GEMMs + 3 CUDA-core kernels)", 7)
+            names[3] = ("node_last on the tensor cores (6 grouped tcgen05 GEMMs + 4 CUDA-core kernels)", 10)
             names[5] = ("sender side on the tensor cores (3 grouped tcgen05 GEMMs + 3 CUDA-core kernels)", 6)
     stages = {names[bit][0]: round(_time_stage(md, device, bit), 3) for bit in names}
     # the single-kernel launches: a stage of one kernel, or of one kernel per layer (per-launch average)

@@ -87,6 +87,9 @@ struct FusedWeights {
     // up1 as [out][in] (m = 0..5, the forward mixings) and as [in][out] (m = 6..11, their backward)
     const float* ntc_hi[12][kMaxLayers];
     const float* ntc_lo[12][kMaxLayers];
+    // and the per-element skip mixings: splits of skip0t (0, the forward) and skip0 (1, the backward)
+    const float* skip_hi[2][kMaxLayers];
+    const float* skip_lo[2][kMaxLayers];
 };
 
 // per-layer activations
@@ -115,6 +118,10 @@ struct FusedState {
     int64_t n_groups;
     float* pre[3][kMaxLayers];  // [E][kH] radial pre-activations p1..p3 (tensor-core path; gradients in place)
     int32_t* flags;
+    const int32_t* elem_order;  // [N] atoms sorted by element (the tensor-core skip mixings)
+    const int32_t* elem_rank;   // [N] its inverse
+    int64_t n_runs;             // element runs (element, first, count) over elem_order, on the host
+    const int64_t* runs_host;
 };
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
@@ -948,11 +955,27 @@ __global__ void __launch_bounds__(256) tcn_contract_kernel(FusedWeights w, Fused
     }
 }
 
+// dst[r] = src[order[r]] (rows of C floats): the rows in element order for the per-element GEMMs
+template <int C>
+__global__ void __launch_bounds__(256) tcn_gather_rows_kernel(const float* __restrict__ src,
+                                                              const int32_t* __restrict__ order, int64_t n,
+                                                              float* __restrict__ dst) {
+    constexpr int V = C / 4;
+    for (int64_t idx = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; idx < n * V;
+         idx += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t r = idx / V;
+        const int q = int(idx % V);
+        reinterpret_cast<float4*>(dst + r * C)[q] = reinterpret_cast<const float4*>(src + int64_t(order[r]) * C)[q];
+    }
+}
+
 // last layer, before its output mixing: t = the skip mixing of s_out[L - 1] (per element) into t_out, the
-// layer-0 readout term e_term0 = s_out[0] . r0 (L = 1), and the scalar contraction b0 into b
+// layer-0 readout term e_term0 = s_out[0] . r0 (L = 1), and the scalar contraction b0 into b; with tp, the
+// skip mixing was done by the per-element GEMMs in element order (row elem_rank[i] of tp) and is copied
 template <int C, int G>
 __global__ void __launch_bounds__(kQ * C, 2) tcn_last_pre_kernel(FusedWeights w, FusedState st, int L,
-                                                                 float* __restrict__ t_out, float* __restrict__ b) {
+                                                                 float* __restrict__ t_out, float* __restrict__ b,
+                                                                 const float* __restrict__ tp) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     NodeSmem<C>& m = *reinterpret_cast<NodeSmem<C>*>(smem_raw);
     const int k = threadIdx.x % C, g = threadIdx.x / C;
@@ -970,7 +993,7 @@ __global__ void __launch_bounds__(kQ * C, 2) tcn_last_pre_kernel(FusedWeights w,
             const float e = atom_sum<C>(m.t[g][k] * w.r0[k], m.sc);
             if (k == 0 && my >= 0) st.e_term0[my] = e;
         }
-        mix_rows<C, G, 0>(m.t, w.skip0[L] + z * C * C, nullptr, nullptr, m.t, nullptr, m.red);
+        if (tp == nullptr) mix_rows<C, G, 0>(m.t, w.skip0[L] + z * C * C, nullptr, nullptr, m.t, nullptr, m.red);
         const float aa = st.A0l[L][i * C + k];
         const float vx = st.A1l[L][i * 3 * C + k], vy = st.A1l[L][i * 3 * C + C + k],
                     vz = st.A1l[L][i * 3 * C + 2 * C + k];
@@ -978,17 +1001,19 @@ __global__ void __launch_bounds__(kQ * C, 2) tcn_last_pre_kernel(FusedWeights w,
         const float* p0 = w.prod0[L] + z * 5 * C + k;
         const float b0 = (((p0[0] * aa + p0[C] * aa * aa) + p0[2 * C] * q) + p0[3 * C] * aa * aa * aa) + p0[4 * C] * aa * q;
         if (my >= 0) {
-            t_out[my * int64_t(C) + k] = m.t[g][k];
+            t_out[my * int64_t(C) + k] = tp != nullptr ? tp[int64_t(st.elem_rank[my]) * C + k] : m.t[g][k];
             b[my * int64_t(C) + k] = b0;
         }
     }
 }
 
 // last layer, after its output mixing (so = s_out[L], the skip added by the GEMM): the readout MLP, the
-// node energies, ds = dE/d so into ds_out and the skip backward into ds_skip[L]
+// node energies, ds = dE/d so into ds_out and the skip backward into ds_skip[L]; with dsp, ds also into
+// row elem_rank[i] of dsp for the per-element GEMMs, which do the skip backward instead
 template <int C, int G>
 __global__ void __launch_bounds__(kQ * C, 2) tcn_last_post_kernel(FusedWeights w, FusedState st, int L,
-                                                                  float* __restrict__ ds_out) {
+                                                                  float* __restrict__ ds_out,
+                                                                  float* __restrict__ dsp) {
     static_assert((C & (C - 1)) == 0 && C >= 32, "the readout's channel rotation wraps with a mask");
     extern __shared__ __align__(16) unsigned char smem_raw[];
     NodeSmem<C>& m = *reinterpret_cast<NodeSmem<C>*>(smem_raw);
@@ -1048,6 +1073,13 @@ __global__ void __launch_bounds__(kQ * C, 2) tcn_last_post_kernel(FusedWeights w
         for (int j = 0; j < RH; ++j) acc = fmaf(m.sc[g][j], m.ra[j][k], acc);
         const float ds = sc * acc;
         __syncthreads();
+        if (dsp != nullptr) {
+            if (my >= 0) {
+                dsp[int64_t(st.elem_rank[my]) * C + k] = ds;
+                ds_out[my * int64_t(C) + k] = ds;
+            }
+            continue;
+        }
         m.t[g][k] = ds;
         __syncthreads();
         mix_rows<C, G, 0>(m.t, w.skip0t[L] + z * C * C, nullptr, nullptr, m.v, nullptr, m.red);
@@ -1063,7 +1095,7 @@ __global__ void __launch_bounds__(kQ * C, 2) tcn_last_post_kernel(FusedWeights w
 template <int C>
 __global__ void __launch_bounds__(256) tcn_last_bwd_kernel(FusedWeights w, FusedState st, int L,
                                                            float* __restrict__ db, float* __restrict__ gv,
-                                                           int64_t n) {
+                                                           const float* __restrict__ dskp, int64_t n) {
     for (int64_t idx = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; idx < n * C;
          idx += int64_t(gridDim.x) * blockDim.x) {
         const int64_t i = idx / C;
@@ -1078,6 +1110,7 @@ __global__ void __launch_bounds__(256) tcn_last_bwd_kernel(FusedWeights w, Fused
         const float gq = db0 * (p0[2 * C] + p0[4 * C] * aa);
         const float da = db0 * (((p0[0] + 2.f * p0[C] * aa) + 3.f * p0[3 * C] * aa * aa) + p0[4 * C] * q);
         db[i * C + k] = da;
+        if (dskp != nullptr) st.ds_skip[L][i * C + k] = dskp[int64_t(st.elem_rank[i]) * C + k];
         gv[i * 3 * C + k] = 2.f * gq * vx;
         gv[i * 3 * C + C + k] = 2.f * gq * vy;
         gv[i * 3 * C + 2 * C + k] = 2.f * gq * vz;
@@ -1646,6 +1679,25 @@ fmd_status node_mix(const FusedWeights& w, const FusedState& st, int64_t n, int 
     return fmd_gemm_tf32x3_grouped(q, xv != nullptr ? 2 : 1, st.flags, s);
 }
 
+// y rows (element order) = the per-element skip mixing of x rows (element order) of layer L: direction d = 0
+// the forward (skip0t), 1 the backward (skip0); one problem per element run, up to four per launch
+template <int C>
+fmd_status skip_mix(const FusedWeights& w, const FusedState& st, int L, int d, const float* x, float* y,
+                    cudaStream_t s) {
+    for (int64_t r0 = 0; r0 < st.n_runs; r0 += 4) {
+        fmd_gemm_problem q[4];
+        int np = 0;
+        for (int64_t r = r0; r < st.n_runs && r < r0 + 4; ++r) {
+            const int64_t z = st.runs_host[3 * r], first = st.runs_host[3 * r + 1], count = st.runs_host[3 * r + 2];
+            q[np++] = {x + first * C, C, w.skip_hi[d][L] + z * C * C, w.skip_lo[d][L] + z * C * C, C, nullptr,
+                       nullptr, 0, y + first * C, C, count, C, C, 0, 0};
+        }
+        const fmd_status r = fmd_gemm_tf32x3_grouped(q, np, st.flags, s);
+        if (r != FMD_OK) return r;
+    }
+    return FMD_OK;
+}
+
 // node_fwd (L = 0), node_last (L = 1) and sender_node (L = 1) of a 2-layer model on the tensor-core path;
 // the state buffers that are free at each point hold the intermediates
 template <int C>
@@ -1667,15 +1719,29 @@ fmd_status node_tc_forward(const FusedWeights& w, const FusedState& st, int64_t 
     float* t = st.A0[L];     // the skip term, then db0 and da
     float* b = st.dA0[L];    // b0
     float* dsb = st.v_out[L];  // ds (the first N C floats)
-    if (single) tcn_last_pre_kernel<C, 1><<<group_grid, kQ * C, node_smem, s>>>(w, st, L, t, b);
-    else tcn_last_pre_kernel<C, kG><<<group_grid, kQ * C, node_smem, s>>>(w, st, L, t, b);
+    // the skip mixings on the tensor cores when the atoms' element runs and the splits are given: rows in
+    // element order in dA1[L] (free until the lin backward writes it), x / ds in its first N C floats, the
+    // mixings' outputs in the next
+    const bool tskip = w.skip_hi[0][L] && w.skip_lo[0][L] && w.skip_hi[1][L] && w.skip_lo[1][L] &&
+                       st.elem_order && st.elem_rank && st.n_runs > 0 && st.runs_host;
+    float* xp = st.dA1[L];
+    float* yp = st.dA1[L] + n * C;
+    if (tskip) {
+        const int gg = int((n * C / 4 + 255) / 256 < int64_t(kNumSMs) * 8 ? (n * C / 4 + 255) / 256 : int64_t(kNumSMs) * 8);
+        tcn_gather_rows_kernel<C><<<gg, 256, 0, s>>>(st.s_out[L - 1], st.elem_order, n, xp);
+        if ((r = check_launch()) != FMD_OK) return r;
+        if ((r = skip_mix<C>(w, st, L, 0, xp, yp, s)) != FMD_OK) return r;
+    }
+    if (single) tcn_last_pre_kernel<C, 1><<<group_grid, kQ * C, node_smem, s>>>(w, st, L, t, b, tskip ? yp : nullptr);
+    else tcn_last_pre_kernel<C, kG><<<group_grid, kQ * C, node_smem, s>>>(w, st, L, t, b, tskip ? yp : nullptr);
     if ((r = check_launch()) != FMD_OK) return r;
     if ((r = node_mix<C>(w, st, n, L, 2, 3, b, st.s_out[L], t, nullptr, nullptr, nullptr, s)) != FMD_OK) return r;
-    if (single) tcn_last_post_kernel<C, 1><<<group_grid, kQ * C, node_smem, s>>>(w, st, L, dsb);
-    else tcn_last_post_kernel<C, kG><<<group_grid, kQ * C, node_smem, s>>>(w, st, L, dsb);
+    if (single) tcn_last_post_kernel<C, 1><<<group_grid, kQ * C, node_smem, s>>>(w, st, L, dsb, tskip ? xp : nullptr);
+    else tcn_last_post_kernel<C, kG><<<group_grid, kQ * C, node_smem, s>>>(w, st, L, dsb, tskip ? xp : nullptr);
     if ((r = check_launch()) != FMD_OK) return r;
+    if (tskip && (r = skip_mix<C>(w, st, L, 1, xp, yp, s)) != FMD_OK) return r;
     if ((r = node_mix<C>(w, st, n, L, 8, 9, dsb, t, nullptr, nullptr, nullptr, nullptr, s)) != FMD_OK) return r;
-    tcn_last_bwd_kernel<C><<<eg, 256, 0, s>>>(w, st, L, t, st.A1[L], n);
+    tcn_last_bwd_kernel<C><<<eg, 256, 0, s>>>(w, st, L, t, st.A1[L], tskip ? yp : nullptr, n);
     if ((r = check_launch()) != FMD_OK) return r;
     return node_mix<C>(w, st, n, L, 6, 7, t, st.dA0[L], nullptr, st.A1[L], st.dA1[L], nullptr, s);
 }
@@ -1841,6 +1907,15 @@ fmd_status fmd_mace_fused_step(const fmd_mace_fused_weights* weights, const fmd_
             w.ntc_hi[m][l] = h.node_tc_hi[m][l];
             w.ntc_lo[m][l] = h.node_tc_lo[m][l];
         }
+    for (int d = 0; d < 2; ++d)
+        for (int l = 0; l < h.n_layers; ++l) {
+            w.skip_hi[d][l] = h.skip_tc_hi[d][l];
+            w.skip_lo[d][l] = h.skip_tc_lo[d][l];
+        }
+    st.elem_order = state->elem_order;
+    st.elem_rank = state->elem_rank;
+    st.n_runs = state->n_elem_runs;
+    st.runs_host = state->elem_runs_host;
     for (int k = 0; k < 3; ++k)
         for (int l = 0; l < h.n_layers; ++l) {
             w.tc_hi[k][l] = h.radial_tc_hi[k][l]; w.tc_lo[k][l] = h.radial_tc_lo[k][l];

@@ -421,14 +421,16 @@ def _struct_types():
             ("poly_p", ctypes.c_int32), ("readout_hidden", ctypes.c_int32), ("radial_hidden", ctypes.c_int32),
             ("r_max", ctypes.c_float), ("inv_avg", ctypes.c_float), ("_pad", ctypes.c_int32)] + [
             (name, arr * 3) for name in ("radial_tc_hi", "radial_tc_lo", "radial_tc_t_hi", "radial_tc_t_lo")] + [
-            ("radial_tc_min_edges", ctypes.c_int64), ("node_tc_hi", arr * 12), ("node_tc_lo", arr * 12)]
+            ("radial_tc_min_edges", ctypes.c_int64), ("node_tc_hi", arr * 12), ("node_tc_lo", arr * 12),
+            ("skip_tc_hi", arr * 2), ("skip_tc_lo", arr * 2)]
 
     class FusedState(ctypes.Structure):
         _fields_ = [(name, arr) for name in (
             "R", "dR", "s_t", "v_t", "A0", "A1", "A0l", "A1l", "s_out", "v_out", "dA0", "dA1", "ds_skip",
             "dv_skip")] + [
             ("ysh", P), ("dY", P), ("g_r", P), ("e_term0", P), ("node_energy", P), ("elem", P), ("groups", P),
-            ("n_groups", ctypes.c_int64), ("radial_pre", arr * 3), ("flags", P)]
+            ("n_groups", ctypes.c_int64), ("radial_pre", arr * 3), ("flags", P), ("elem_order", P),
+            ("elem_rank", P), ("n_elem_runs", ctypes.c_int64), ("elem_runs_host", P)]
 
     return FusedWeights, FusedState
 
@@ -529,6 +531,16 @@ def _fused_weights(model: "MACEModel"):
                         keep[f"{key}.ntc_hi{transposed}"], keep[f"{key}.ntc_lo{transposed}"] = hi, lo
                         fw.node_tc_hi[idx][L] = ptr(hi)
                         fw.node_tc_lo[idx][L] = ptr(lo)
+                # the per-element skip mixings: skip0t [Z][out][in] (forward) and skip0 [Z][in][out] (backward)
+                if f"{L}.skip0" in w:
+                    for d, src in enumerate((w[f"{L}.skip0"].transpose(1, 2).contiguous(), w[f"{L}.skip0"].contiguous())):
+                        flat = src.reshape(-1, src.shape[-1])
+                        hi, lo = torch.empty_like(flat), torch.empty_like(flat)
+                        call("fmd_tf32_split", ptr(flat), flat.shape[0], flat.shape[1], flat.shape[1], 0, ptr(hi),
+                             ptr(lo), flat.shape[1], s)
+                        keep[f"{L}.skip_tc_hi{d}"], keep[f"{L}.skip_tc_lo{d}"] = hi, lo
+                        fw.skip_tc_hi[d][L] = ptr(hi)
+                        fw.skip_tc_lo[d][L] = ptr(lo)
     return fw, keep
 
 
@@ -574,6 +586,18 @@ class _FusedBuffers:
         st.ysh, st.dY, st.g_r = ptr(self.t["ysh"]), ptr(self.t["dY"]), ptr(self.t["g_r"])
         st.e_term0, st.node_energy = ptr(self.t["e_term0"]), ptr(self.t["node_energy"])
         st.elem, st.groups, st.n_groups = ptr(elem), ptr(groups), int(groups.shape[0])
+        # the atoms by element for the skip mixings on the tensor cores: order, rank and the element runs
+        elem_np = elem.cpu().numpy()
+        order = np.argsort(elem_np, kind="stable").astype(np.int32)
+        rank = np.empty_like(order)
+        rank[order] = np.arange(order.size, dtype=np.int32)
+        zs, first, counts = np.unique(elem_np[order], return_index=True, return_counts=True)
+        self.elem_runs_host = np.ascontiguousarray(np.stack([zs, first, counts], axis=1).astype(np.int64))
+        self.t["elem_order"] = torch.from_numpy(order).to(dev)
+        self.t["elem_rank"] = torch.from_numpy(rank).to(dev)
+        st.elem_order, st.elem_rank = ptr(self.t["elem_order"]), ptr(self.t["elem_rank"])
+        st.n_elem_runs = int(self.elem_runs_host.shape[0])
+        st.elem_runs_host = self.elem_runs_host.ctypes.data
         if 0 < model.radial_tc_min_edges <= E:  # the radial pre-activations of the tensor-core path
             for L in range(c.num_interactions):
                 for k in range(3):

@@ -742,6 +742,10 @@ typedef struct fmd_mace_fused_weights {
      * the mixings stay in the node kernels on the CUDA cores */
     const float* node_tc_hi[12][FMD_MACE_MAX_LAYERS];
     const float* node_tc_lo[12][FMD_MACE_MAX_LAYERS];
+    /* and the per-element skip mixings: splits of skip0t ([Z][out][in], the forward) and of skip0 (the
+     * backward), index 0 / 1 */
+    const float* skip_tc_hi[2][FMD_MACE_MAX_LAYERS];
+    const float* skip_tc_lo[2][FMD_MACE_MAX_LAYERS];
 } fmd_mace_fused_weights;
 
 /* Persistent activations of the fused step (caller-owned device buffers,
@@ -778,6 +782,14 @@ typedef struct fmd_mace_fused_state {
     int64_t n_groups;
     float* radial_pre[3][FMD_MACE_MAX_LAYERS];
     int32_t* flags;
+    /* the skip mixings of the tensor-core node path (per element, one GEMM problem per element present):
+     * elem_order [N] the atoms sorted by element, elem_rank [N] its inverse (device), and n_elem_runs
+     * host triples elem_runs_host [n][3] = (element row, first, count) over elem_order; NULL / 0: the skip
+     * mixings stay on the CUDA cores */
+    const int32_t* elem_order;
+    const int32_t* elem_rank;
+    int64_t n_elem_runs;
+    const int64_t* elem_runs_host;
 } fmd_mace_fused_state;
 
 /* Energies and forces of one step: geometry, radial MLPs, messages, node
