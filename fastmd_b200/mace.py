@@ -39,7 +39,10 @@ from fastmd_b200._lib import call, ptr, stream
 ELEMENTS = 89  # one-hot over Z = 1..89 (the benchmark's "89 element embeddings")
 RADIAL_PRECISIONS = ("auto", "tf32x3", "ieee")
 # the captured-mode row threshold of the reference's 3xTF32 wide GEMMs (fastmd/config.py:153)
-RADIAL_TC_MIN_EDGES = 65536
+# the whole-step crossover measured on a B200 (us per MD step, SIMT edge kernels / tensor-core radial path):
+# 1 replica (2.2k edge rows) 151 / 305, 2 replicas 216 / 312, 4 replicas (8.8k rows) 370 / 355,
+# 8 replicas 604 / 418, 32 replicas 2160 / 810
+RADIAL_TC_MIN_EDGES = 8192
 
 
 @dataclass(frozen=True)
@@ -144,7 +147,7 @@ class MACEModel:
         if radial_precision not in RADIAL_PRECISIONS:
             raise ValueError(f"radial_precision must be one of {RADIAL_PRECISIONS}")
         # the fused step's radial MLPs: tcgen05 3xTF32 GEMMs from this many edge rows on, else the
-        # IEEE FP32 edge kernels ("auto": the reference's 65,536-row wide-GEMM threshold)
+        # IEEE FP32 edge kernels ("auto": from the measured crossover of the two paths, 8,192 rows)
         self.radial_tc_min_edges = {"auto": RADIAL_TC_MIN_EDGES, "tf32x3": 1, "ieee": 0}[radial_precision]
         if self.config.l_max != 1 or self.config.correlation != 3:
             raise ValueError("this build implements l_max = 1 and correlation = 3")

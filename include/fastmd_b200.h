@@ -687,7 +687,9 @@ FMD_API fmd_status fmd_mace_node_energy_bwd(const double* d_total, double scale,
  * pre-activations p1..p3 (3xTF32, FP32 accuracy) instead of the SIMT edge
  * kernels (IEEE FP32). The reference's own wide-GEMM rule takes the 3xTF32
  * path from 65,536 rows in a capture (fastmd/config.py:153,
- * fastmd/engine/kernels/triton_wide_gemm.py:339 _decide). */
+ * fastmd/engine/kernels/triton_wide_gemm.py:339 _decide); the fused step's
+ * whole-step crossover on a B200 lies near 8,192 edge rows (4 replicas of
+ * 135 atoms), the host's default for radial_tc_min_edges. */
 #define FMD_MACE_MAX_LAYERS 4
 typedef struct fmd_mace_fused_weights {
     const float* radial_w1t[FMD_MACE_MAX_LAYERS];
