@@ -32,6 +32,8 @@
 
 #include <cub/device/device_scan.cuh>
 
+#include <algorithm>
+#include <cmath>
 #include <mutex>
 
 #include <cooperative_groups.h>
@@ -819,74 +821,399 @@ __global__ void __cluster_dims__(kRefCluster, 1, 1) __launch_bounds__(kRefThread
 }
 
 // ------------------------------------------------------------- ragged list
+//
+// Two passes and no candidate matrix of (neighbour, shift) rows:
+//   collect: one sweep of the cell list; per centre it counts the pairs the
+//            eager path keeps and stores its candidates' keys
+//            (neighbour << 12 | image, 32-bit below 2^20 atoms) unsorted in a
+//            scratch row;
+//   scan:    the kept counts give the row offsets;
+//   emit:    a warp per centre sorts its keys by (neighbour, image) with a
+//            bitonic network in registers and writes the kept pairs into its
+//            output row (consecutive lanes, consecutive edges).
+//
+// A pair is kept when it is a candidate (dist2 < (rc + 1e-6)^2 in the
+// staged arithmetic of the candidate build, gpu_graph_builder.py:161) and
+// |(q - p) + image @ cell| < rc (gpu_graph_builder.py:186-192). The two
+// distances differ only by float32 rounding, bounded on the host by delta: a
+// candidate with dist2 < (rc - delta)^2 passes the second test, so the
+// collect sweep evaluates that test only in the thin shell between the two
+// radii.
 
-// edges per centre with the ragged path's predicate (|diff| < rc)
-__global__ void ragged_count_kernel(const float4* __restrict__ wrapped, int64_t rows, Cell9 cell,
-                                    const int32_t* __restrict__ nbr, const int32_t* __restrict__ shift,
-                                    const int32_t* __restrict__ count, int32_t bmax, float cutoff,
-                                    int64_t* __restrict__ counts_out) {
-    const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    const int nwarps = (gridDim.x * blockDim.x) >> 5;
-    for (int64_t i = warp_global; i < rows; i += nwarps) {
-        const int cnt = min(count[i], bmax);
-        const float4 p4 = wrapped[i];
-        const float3 p = make_float3(p4.x, p4.y, p4.z);
-        int edges = 0;
-        for (int k0 = 0; k0 < cnt; k0 += 32) {
-            const int k = k0 + lane;
-            bool hit = false;
-            if (k < cnt) {
-                const int32_t j = nbr[i * bmax + k];
-                const float4 q4 = wrapped[j];
-                hit = ragged_dist(p, make_float3(q4.x, q4.y, q4.z), ld3i(shift, i * bmax + k), cell.c) < cutoff;
+constexpr int kRagWarps = 8;
+constexpr int kRagStage = 1024;   // staged (atom, image) entries per chunk
+constexpr int kRagHome = 512;     // home atoms per pass of the collect sweep
+constexpr int kRagMaxList = 2048; // largest candidate row (bmax + 1)
+
+struct RaggedArgs {
+    const int32_t* cell_start;   // [ncells + 1]
+    const int32_t* cell_atoms;   // atoms grouped by cell
+    const float4* cell_pos;      // wrapped positions grouped by cell
+    const float4* wrapped;       // wrapped positions by atom
+    Cell9 cell;
+    Grid grid;
+    float cand_cut;              // rc + 1e-6: candidate iff dist2 < cand_cut^2
+    float cutoff;                // rc: kept iff |diff| < rc
+    float lo2;                   // a candidate below it passes |diff| < rc
+    int32_t bmax;                // more candidates of a centre raise FMD_FLAG_CANDIDATE_OVERFLOW
+    int32_t row_cap;             // keys per scratch row: bmax + 1 (the centre itself included)
+    int32_t sort_cap;            // emit pass: per-warp shared list for rows over 128 keys (0: none)
+    int32_t off_cap;             // (cell, image) offsets of a neighbourhood
+    void* keys;                  // [n, row_cap] candidate keys (KeyT)
+    int32_t* n_keys;             // [n] candidates per centre (the centre itself included)
+    int64_t* counts;             // kept pairs per centre
+    const int64_t* offsets;      // row offsets [n + 1]
+    int64_t n_atoms;
+    int64_t e_cap;
+    int64_t* center;
+    int64_t* neighbor;
+    int32_t* images;
+    float* dist;
+    int32_t* flags;
+};
+
+// an image in 12 bits, 4 per axis offset by 8, ordered as (x, y, z) (|image| <= the search reach <= 5)
+__device__ __forceinline__ int32_t pack_image4(int ix, int iy, int iz) {
+    return ((ix + 8) << 8) | ((iy + 8) << 4) | (iz + 8);
+}
+
+__device__ __forceinline__ int3 unpack_image4(uint32_t v) {
+    return make_int3(int((v >> 8) & 15u) - 8, int((v >> 4) & 15u) - 8, int(v & 15u) - 8);
+}
+
+struct Hood {
+    int32_t* begin;   // [off_cap] first cell-grouped row of the offset's cell
+    int32_t* pref;    // [off_cap + 1] exclusive prefix of the offsets' atom counts
+    int32_t* img;     // [off_cap] packed image (pack_image4)
+    float* shift;     // [off_cap * 3] image @ cell
+};
+
+// (cell, image) of offset k of home cell `home`: the offset's atom count, with its row start,
+// packed image and image @ cell stored
+__device__ __forceinline__ int hood_entry(const Hood& o, const int32_t* __restrict__ cell_start, int home, int k,
+                                          const Grid& g, const Cell9& cell) {
+    const int w1 = 2 * g.s[1] + 1, w2 = 2 * g.s[2] + 1;
+    const int hx = home / (g.n[1] * g.n[2]), hy = (home / g.n[2]) % g.n[1], hz = home % g.n[2];
+    const int gx = hx + k / (w1 * w2) - g.s[0], gy = hy + (k / w2) % w1 - g.s[1], gz = hz + k % w2 - g.s[2];
+    const int ix = floor_div(gx, g.n[0]), iy = floor_div(gy, g.n[1]), iz = floor_div(gz, g.n[2]);
+    const int cx = gx - ix * g.n[0], cy = gy - iy * g.n[1], cz = gz - iz * g.n[2];
+    const int c = (cx * g.n[1] + cy) * g.n[2] + cz;
+    const int b = cell_start[c];
+    o.begin[k] = b;
+    o.img[k] = pack_image4(ix, iy, iz);
+    const float fx = float(ix), fy = float(iy), fz = float(iz);
+    o.shift[3 * k] = (fx * cell.c[0] + fy * cell.c[3]) + fz * cell.c[6];
+    o.shift[3 * k + 1] = (fx * cell.c[1] + fy * cell.c[4]) + fz * cell.c[7];
+    o.shift[3 * k + 2] = (fx * cell.c[2] + fy * cell.c[5]) + fz * cell.c[8];
+    return cell_start[c + 1] - b;
+}
+
+// The (cell, image) offsets around home cell `home` and the prefix of their atom counts; returns
+// the number of staged entries, with the block synchronised. Up to 32 offsets (a search reach of
+// one cell) one warp builds it.
+__device__ int load_hood(const Hood& o, const int32_t* __restrict__ cell_start, int home, const Grid& g,
+                         const Cell9& cell, int* s_scan) {
+    const int n_off = (2 * g.s[0] + 1) * (2 * g.s[1] + 1) * (2 * g.s[2] + 1);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = int(blockDim.x >> 5);
+    __syncthreads();  // the previous home cell's readers are done
+    if (n_off <= 32) {
+        if (warp == 0) {
+            const int cnt = lane < n_off ? hood_entry(o, cell_start, home, lane, g, cell) : 0;
+            int x = cnt;
+            for (int d = 1; d < 32; d <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, x, d);
+                if (lane >= d) x += y;
             }
-            edges += __popc(__ballot_sync(0xffffffffu, hit));
+            if (lane < n_off) o.pref[lane] = x - cnt;
+            if (lane == 31) o.pref[n_off] = x;
         }
-        if (lane == 0) counts_out[i] = edges;
+        __syncthreads();
+        return o.pref[n_off];
+    }
+    int running = 0;
+    for (int o0 = 0; o0 < n_off; o0 += blockDim.x) {
+        const int k = o0 + threadIdx.x;
+        const int cnt = k < n_off ? hood_entry(o, cell_start, home, k, g, cell) : 0;
+        int x = cnt;
+        for (int d = 1; d < 32; d <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, d);
+            if (lane >= d) x += y;
+        }
+        if (lane == 31) s_scan[warp] = x;
+        __syncthreads();
+        int before = 0, total = 0;
+        for (int w = 0; w < nw; ++w) {
+            if (w < warp) before += s_scan[w];
+            total += s_scan[w];
+        }
+        if (k < n_off) o.pref[k] = running + before + x - cnt;
+        running += total;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) o.pref[n_off] = running;
+    __syncthreads();
+    return running;
+}
+
+// the offset of staged entry t: the last o with pref[o] <= t
+__device__ __forceinline__ int hood_offset(const int32_t* pref, int n_off, int t) {
+    int lo = 0, hi = n_off;
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (pref[mid] <= t) lo = mid; else hi = mid;
+    }
+    return lo;
+}
+
+// fn(e, src, k) for every staged entry t in [c0, c0 + ns) (e = t - c0, src its cell-grouped row, k
+// its offset): a warp per offset, its lanes over the offset cell's atoms
+template <class F>
+__device__ __forceinline__ void for_staged(const Hood& o, int n_off, int c0, int ns, F&& fn) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = int(blockDim.x >> 5);
+    for (int k = warp; k < n_off; k += nw) {
+        const int p0 = o.pref[k];
+        const int lo = max(p0, c0), hi = min(o.pref[k + 1], c0 + ns);
+        for (int t = lo + lane; t < hi; t += 32) fn(t - c0, o.begin[k] + (t - p0), k);
     }
 }
 
-__global__ void ragged_write_kernel(const float4* __restrict__ wrapped, int64_t rows, Cell9 cell,
-                                    const int32_t* __restrict__ nbr, const int32_t* __restrict__ shift,
-                                    const int32_t* __restrict__ count, int32_t bmax, float cutoff,
-                                    const int64_t* __restrict__ offsets, int64_t e_cap,
-                                    int64_t* __restrict__ center, int64_t* __restrict__ neighbor,
-                                    int32_t* __restrict__ images, float* __restrict__ dist) {
-    const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    const int nwarps = (gridDim.x * blockDim.x) >> 5;
-    for (int64_t i = warp_global; i < rows; i += nwarps) {
-        const int cnt = min(count[i], bmax);
-        const float4 p4 = wrapped[i];
-        const float3 p = make_float3(p4.x, p4.y, p4.z);
-        int64_t out = offsets[i];
-        for (int k0 = 0; k0 < cnt; k0 += 32) {
-            const int k = k0 + lane;
-            bool hit = false;
-            float d = 0.f;
-            int32_t j = 0;
-            int3 s = make_int3(0, 0, 0);
-            if (k < cnt) {
-                j = nbr[i * bmax + k];
-                s = ld3i(shift, i * bmax + k);
-                const float4 q4 = wrapped[j];
-                d = ragged_dist(p, make_float3(q4.x, q4.y, q4.z), s, cell.c);
-                hit = d < cutoff;
-            }
-            const unsigned mask = __ballot_sync(0xffffffffu, hit);
-            if (hit) {
-                const int64_t e = out + __popc(mask & ((1u << lane) - 1u));
-                if (e < e_cap) {
-                    center[e] = i;
-                    neighbor[e] = j;
-                    images[3 * e] = s.x;
-                    images[3 * e + 1] = s.y;
-                    images[3 * e + 2] = s.z;
-                    dist[e] = d;
+// the eager path's distance |(q - p) + sh| (gpu_graph_builder.py:186-192) for sh = image @ cell
+__device__ __forceinline__ float eager_dist(float4 p, float4 q, float sx, float sy, float sz) {
+    const float dx = (q.x - p.x) + sx, dy = (q.y - p.y) + sy, dz = (q.z - p.z) + sz;
+    return sqrtf((dx * dx + dy * dy) + dz * dz);
+}
+
+__device__ __forceinline__ int warp_sum_int(int v) {
+    for (int d = 16; d > 0; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
+    return v;
+}
+
+// KeyT: uint32_t when every atom index is below 2^20, else uint64_t
+template <class KeyT>
+__global__ void __launch_bounds__(kRagWarps * 32) ragged_nbr_collect_kernel(RaggedArgs a) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    float4* spos = reinterpret_cast<float4*>(smem_raw);      // [kRagStage] staged position + image shift
+    KeyT* skey = reinterpret_cast<KeyT*>(spos + kRagStage);  // [kRagStage] (atom << 12) | image
+    Hood o;
+    o.begin = reinterpret_cast<int32_t*>(skey + kRagStage);
+    o.pref = o.begin + a.off_cap;
+    o.img = o.pref + a.off_cap + 1;
+    int32_t* kept_n = o.img + a.off_cap;   // [kRagHome] kept pairs (the centre itself included)
+    int32_t* cand_n = kept_n + kRagHome;   // [kRagHome] candidates (the centre itself included)
+    o.shift = reinterpret_cast<float*>(cand_n + kRagHome);
+    __shared__ int s_scan[32];
+    KeyT* keys = static_cast<KeyT*>(a.keys);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const unsigned below = (1u << lane) - 1u;
+    const Grid& g = a.grid;
+    const float cut2 = a.cand_cut * a.cand_cut;
+    const int n_off = (2 * g.s[0] + 1) * (2 * g.s[1] + 1) * (2 * g.s[2] + 1);
+    for (int home = blockIdx.x; home < g.ncells; home += gridDim.x) {
+        const int h_begin = a.cell_start[home], h_end = a.cell_start[home + 1];
+        if (h_begin == h_end) continue;  // uniform per CTA
+        const int staged = load_hood(o, a.cell_start, home, g, a.cell, s_scan);
+        for (int hb = h_begin; hb < h_end; hb += kRagHome) {
+            const int n_home = min(kRagHome, h_end - hb);
+            for (int h = threadIdx.x; h < n_home; h += blockDim.x) kept_n[h] = cand_n[h] = 0;
+            for (int c0 = 0; c0 < staged; c0 += kRagStage) {
+                const int ns = min(kRagStage, staged - c0);
+                __syncthreads();
+                for_staged(o, n_off, c0, ns, [&](int e, int src, int k) {
+                    const float4 q = a.cell_pos[src];
+                    spos[e] = make_float4(q.x + o.shift[3 * k], q.y + o.shift[3 * k + 1], q.z + o.shift[3 * k + 2], 0.f);
+                    skey[e] = (KeyT(uint32_t(a.cell_atoms[src])) << 12) | KeyT(uint32_t(o.img[k]));
+                });
+                __syncthreads();
+                for (int h = warp; h < n_home; h += kRagWarps) {
+                    const float4 hp = a.cell_pos[hb + h];
+                    KeyT* row = keys + size_t(a.cell_atoms[hb + h]) * a.row_cap;
+                    int n = cand_n[h], kept = 0;
+                    for (int base = 0; base < ns; base += 32) {
+                        const int k = base + lane;
+                        float d2 = cut2;
+                        if (k < ns) {
+                            const float4 s = spos[k];
+                            const float dx = s.x - hp.x, dy = s.y - hp.y, dz = s.z - hp.z;
+                            d2 = (dx * dx + dy * dy) + dz * dz;
+                        }
+                        const bool hit = d2 < cut2;
+                        const unsigned mask = __ballot_sync(0xffffffffu, hit);
+                        if (hit) {
+                            const int pos = n + __popc(mask & below);
+                            if (pos < a.row_cap) row[pos] = skey[k];
+                            kept += d2 < a.lo2 ? 1 : 0;
+                        }
+                        n += __popc(mask);
+                        const bool shell = hit && !(d2 < a.lo2);
+                        if (__any_sync(0xffffffffu, shell) && shell) {  // the eager path's own distance decides
+                            const int lo = hood_offset(o.pref, n_off, c0 + k);
+                            const float4 q = a.cell_pos[o.begin[lo] + (c0 + k - o.pref[lo])];
+                            kept += eager_dist(hp, q, o.shift[3 * lo], o.shift[3 * lo + 1], o.shift[3 * lo + 2]) <
+                                            a.cutoff
+                                        ? 1
+                                        : 0;
+                        }
+                    }
+                    kept = warp_sum_int(kept);
+                    if (lane == 0) {
+                        kept_n[h] += kept;
+                        cand_n[h] = n;
+                    }
                 }
             }
-            out += __popc(mask);
+            __syncthreads();
+            for (int h = threadIdx.x; h < n_home; h += blockDim.x) {
+                // the centre meets itself once (zero image, distance 0) when its position is finite
+                const float4 hp = a.cell_pos[hb + h];
+                const int self = (isfinite(hp.x) && isfinite(hp.y) && isfinite(hp.z)) ? 1 : 0;
+                const int32_t row = a.cell_atoms[hb + h];
+                a.counts[row] = kept_n[h] - self;
+                a.n_keys[row] = cand_n[h];
+                if (cand_n[h] - self > a.bmax) raise_flag(a.flags, FMD_FLAG_CANDIDATE_OVERFLOW);
+            }
+        }
+    }
+}
+
+// ascending bitonic sort of list[0, n) (n a power of two) by one warp, in shared memory
+template <class KeyT>
+__device__ __forceinline__ void warp_bitonic_sort(KeyT* list, int n, int lane) {
+    for (int size = 2; size <= n; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int t = lane; t < (n >> 1); t += 32) {
+                const int i = 2 * t - (t & (stride - 1));
+                const int j = i + stride;
+                const KeyT x = list[i], y = list[j];
+                if ((x > y) == ((i & size) == 0)) {
+                    list[i] = y;
+                    list[j] = x;
+                }
+            }
+            __syncwarp();
+        }
+    }
+}
+
+// ascending bitonic sort of 32 * EPL keys held by one warp, element j * 32 + lane in v[j]
+template <int EPL, class KeyT>
+__device__ __forceinline__ void warp_bitonic_regs(KeyT (&v)[EPL], int lane) {
+    constexpr int kN = 32 * EPL;
+#pragma unroll
+    for (int size = 2; size <= kN; size <<= 1) {
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            if (stride >= 32) {  // partners in the same lane
+                const int js = stride >> 5;
+#pragma unroll
+                for (int j = 0; j < EPL; ++j) {
+                    if ((j & js) == 0) {
+                        const bool up = ((j * 32) & size) == 0;
+                        const KeyT x = v[j], y = v[j + js];
+                        const bool swap = (x > y) == up;
+                        v[j] = swap ? y : x;
+                        v[j + js] = swap ? x : y;
+                    }
+                }
+            } else {
+                const bool lower = (lane & stride) == 0;
+#pragma unroll
+                for (int j = 0; j < EPL; ++j) {
+                    const KeyT p = __shfl_xor_sync(0xffffffffu, v[j], stride);
+                    const bool up = ((j * 32 + lane) & size) == 0;
+                    const bool take_min = lower == up;
+                    v[j] = (take_min == (p < v[j])) ? p : v[j];
+                }
+            }
+        }
+    }
+}
+
+template <class KeyT>
+struct RowWriter {
+    float4 hp;          // the centre's wrapped position
+    int32_t row;        // the centre
+    KeyT self;          // its own key (zero image)
+    int64_t out, end;   // next output edge, end of its row (clipped to e_cap)
+};
+
+// one warp: the kept pairs among 32 sorted keys (one per lane, `valid` below the row's key count),
+// written at the row's next edges in key order
+template <class KeyT>
+__device__ __forceinline__ void emit_sorted(const RaggedArgs& a, RowWriter<KeyT>& r, KeyT v, bool valid, int lane) {
+    bool keep = false;
+    float d = 0.f;
+    int32_t j = 0;
+    int3 s3 = make_int3(0, 0, 0);
+    if (valid) {
+        j = int32_t(v >> 12);
+        s3 = unpack_image4(uint32_t(v & KeyT(0xFFFu)));
+        const float4 q = a.wrapped[j];
+        const float3 sh = row_times(make_float3(float(s3.x), float(s3.y), float(s3.z)), a.cell.c);
+        // the candidate's staged distance (as the collect sweep computed it) and the eager distance
+        const float ex = (q.x + sh.x) - r.hp.x, ey = (q.y + sh.y) - r.hp.y, ez = (q.z + sh.z) - r.hp.z;
+        const float d2 = (ex * ex + ey * ey) + ez * ez;
+        d = eager_dist(r.hp, q, sh.x, sh.y, sh.z);
+        keep = v != r.self && (d2 < a.lo2 || d < a.cutoff);
+    }
+    const unsigned mask = __ballot_sync(0xffffffffu, keep);
+    if (keep) {
+        const int64_t e = r.out + __popc(mask & ((1u << lane) - 1u));
+        if (e < r.end) {
+            a.center[e] = r.row;
+            a.neighbor[e] = j;
+            a.images[3 * e] = s3.x;
+            a.images[3 * e + 1] = s3.y;
+            a.images[3 * e + 2] = s3.z;
+            a.dist[e] = d;
+        }
+    }
+    r.out += __popc(mask);
+}
+
+template <int EPL, class KeyT>
+__device__ __forceinline__ void sort_and_emit(const RaggedArgs& a, RowWriter<KeyT>& r, const KeyT* keys, int k,
+                                              int lane) {
+    KeyT v[EPL];
+#pragma unroll
+    for (int j = 0; j < EPL; ++j) v[j] = j * 32 + lane < k ? keys[j * 32 + lane] : ~KeyT(0);
+    warp_bitonic_regs<EPL, KeyT>(v, lane);
+#pragma unroll
+    for (int j = 0; j < EPL; ++j)
+        if (j * 32 < k) emit_sorted(a, r, v[j], j * 32 + lane < k, lane);
+}
+
+// a warp per centre: its candidate keys sorted, its kept pairs written into its output row
+template <class KeyT>
+__global__ void __launch_bounds__(kRagWarps * 32) ragged_nbr_emit_kernel(RaggedArgs a) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];  // [warps][sort_cap] keys of long rows
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    KeyT* list = reinterpret_cast<KeyT*>(smem_raw) + size_t(warp) * a.sort_cap;
+    const KeyT* keys = static_cast<const KeyT*>(a.keys);
+    const int64_t n_warps = int64_t(gridDim.x) * kRagWarps;
+    for (int64_t row = int64_t(blockIdx.x) * kRagWarps + warp; row < a.n_atoms; row += n_warps) {
+        const int k = min(a.n_keys[row], a.row_cap);
+        const KeyT* src = keys + size_t(row) * a.row_cap;
+        RowWriter<KeyT> r;
+        r.hp = a.wrapped[row];
+        r.row = int32_t(row);
+        r.self = (KeyT(uint32_t(row)) << 12) | KeyT(uint32_t(pack_image4(0, 0, 0)));
+        r.out = a.offsets[row];
+        r.end = min(a.offsets[row + 1], a.e_cap);
+        if (k <= 32) {
+            sort_and_emit<1, KeyT>(a, r, src, k, lane);
+        } else if (k <= 64) {
+            sort_and_emit<2, KeyT>(a, r, src, k, lane);
+        } else if (k <= 128) {
+            sort_and_emit<4, KeyT>(a, r, src, k, lane);
+        } else {  // a long row: sorted in shared memory
+            int n = 256;
+            while (n < k) n <<= 1;
+            for (int i = lane; i < n; i += 32) list[i] = i < k ? src[i] : ~KeyT(0);
+            __syncwarp();
+            warp_bitonic_sort(list, n, lane);
+            for (int base = 0; base < k; base += 32)
+                emit_sorted(a, r, list[min(base + lane, k - 1)], base + lane < k, lane);
+            __syncwarp();
         }
     }
 }
@@ -1028,11 +1355,9 @@ inline CellWorkspace carve(void* ws, int64_t atoms, int64_t cells) {
 
 inline int list_cap_for(int32_t bmax) { return bmax < 32 ? 32 : (bmax > 1024 ? 1024 : bmax); }
 
-// bin + scan + scatter + query into a candidate matrix
-inline fmd_status run_cell_list(const float* positions, int64_t n_atoms, int32_t n_systems, const Cell9& cell,
-                                const Grid& grid, float cutoff, int32_t bmax, int32_t* nbr, int32_t* shift,
-                                int32_t* count, const CellWorkspace& w, int32_t* flags, cudaStream_t s,
-                                bool fill_unused = true) {
+// bin + scan + scatter: the atoms grouped by cell
+inline fmd_status build_cells(const float* positions, int64_t n_atoms, int32_t n_systems, const Cell9& cell,
+                              const Grid& grid, const CellWorkspace& w, int32_t* flags, cudaStream_t s) {
     const int64_t atoms = n_atoms * n_systems;
     const int64_t cells = int64_t(grid.ncells) * n_systems;
     cudaError_t err = cudaMemsetAsync(w.cell_count, 0, sizeof(int32_t) * (cells + 1), s);
@@ -1048,7 +1373,18 @@ inline fmd_status run_cell_list(const float* positions, int64_t n_atoms, int32_t
     if (err != cudaSuccess) return record_cuda_error(err);
     cell_scatter_kernel<<<grid_for(atoms, threads), threads, 0, s>>>(atoms, w.wrapped, w.atom_cell, w.atom_slot,
                                                                       w.cell_start, w.cell_atoms, w.cell_pos);
-    if ((st = check_launch()) != FMD_OK) return st;
+    return check_launch();
+}
+
+// bin + scan + scatter + query into a candidate matrix
+inline fmd_status run_cell_list(const float* positions, int64_t n_atoms, int32_t n_systems, const Cell9& cell,
+                                const Grid& grid, float cutoff, int32_t bmax, int32_t* nbr, int32_t* shift,
+                                int32_t* count, const CellWorkspace& w, int32_t* flags, cudaStream_t s) {
+    const int64_t atoms = n_atoms * n_systems;
+    const int64_t cells = int64_t(grid.ncells) * n_systems;
+    const int threads = 256;
+    fmd_status st = build_cells(positions, n_atoms, n_systems, cell, grid, w, flags, s);
+    if (st != FMD_OK) return st;
     QueryArgs q{};
     q.cell_start = w.cell_start;
     q.cell_atoms = w.cell_atoms;
@@ -1071,7 +1407,6 @@ inline fmd_status run_cell_list(const float* positions, int64_t n_atoms, int32_t
     const int qgrid = int(cells < int64_t(kNumSMs) * 16 ? cells : int64_t(kNumSMs) * 16);
     cell_query_kernel<<<qgrid, kQueryWarps * 32, smem, s>>>(q);
     if ((st = check_launch()) != FMD_OK) return st;
-    if (!fill_unused) return FMD_OK;  // a consumer that reads only the first count slots of a row
     cand_fill_kernel<<<grid_for(atoms * bmax, threads), threads, 0, s>>>(atoms, bmax, int32_t(atoms), nbr, shift,
                                                                          count);
     return check_launch();
@@ -1250,16 +1585,34 @@ static size_t ragged_scan_bytes(int64_t n_atoms) {
     return cub_bytes;
 }
 
+// candidate keys of the ragged list: 32-bit (atom << 12 | image) below 2^20 atoms, else 64-bit
+static size_t ragged_key_bytes(int64_t n_atoms) { return n_atoms <= (int64_t(1) << 20) ? 4 : 8; }
+
 fmd_status fmd_neighbor_list_workspace_bytes(const float* cell_host, float cutoff, int64_t n_atoms,
                                              int32_t bmax, size_t* bytes) {
     Grid g{};
     if (cell_host == nullptr || bytes == nullptr || n_atoms < 1 || bmax < 1 ||
         !make_grid(cell_host, cutoff + 1e-6f, g))
         return FMD_ERR_INVALID_ARGUMENT;
-    *bytes = cell_workspace_bytes(n_atoms, g.ncells) + align_up(sizeof(int32_t) * size_t(n_atoms) * bmax) +
-             align_up(sizeof(int32_t) * size_t(n_atoms) * bmax * 3) + align_up(sizeof(int32_t) * n_atoms) +
-             align_up(sizeof(int64_t) * (n_atoms + 1)) + align_up(ragged_scan_bytes(n_atoms));
+    *bytes = cell_workspace_bytes(n_atoms, g.ncells) + align_up(sizeof(int64_t) * (n_atoms + 1)) +
+             align_up(sizeof(int32_t) * n_atoms) + align_up(ragged_key_bytes(n_atoms) * size_t(n_atoms) * (bmax + 1)) +
+             align_up(ragged_scan_bytes(n_atoms));
     return FMD_OK;
+}
+
+// A candidate closer than rc - delta passes the eager path's |(q - p) + image @ cell| < rc. Both
+// distances round each difference component at most twice, on magnitudes of at most
+// (3 + reach) C + 2 rc (C: the largest coordinate of a wrapped position, the image shift at most
+// reach C), so they differ by less than 2^-23 ((3 + reach) C + 5 rc); delta is 8 times that.
+static float eager_shell_lo2(const float* cell_host, const Grid& g, float cutoff) {
+    double c_max = 0.0;
+    for (int c = 0; c < 3; ++c)
+        c_max = fmax(c_max, fabs(double(cell_host[c])) + fabs(double(cell_host[3 + c])) + fabs(double(cell_host[6 + c])));
+    const int reach = std::max(g.s[0], std::max(g.s[1], g.s[2]));
+    const double delta = ldexp((3.0 + reach) * c_max + 5.0 * double(cutoff), -20);
+    const double lo = double(cutoff) - delta;
+    if (!(lo > 0.0)) return 0.f;
+    return nextafterf(float(lo * lo), 0.f);
 }
 
 fmd_status fmd_neighbor_list(const float* positions, const float* cell_host, int64_t n_atoms, float cutoff,
@@ -1273,6 +1626,7 @@ fmd_status fmd_neighbor_list(const float* positions, const float* cell_host, int
         dist == nullptr || offsets == nullptr || n_atoms < 1 || bmax < 1 || e_capacity < 0 ||
         !make_cell(cell_host, cell) || !make_grid(cell_host, cand_cut, grid) || n_atoms >= (int64_t(1) << 31))
         return FMD_ERR_INVALID_ARGUMENT;
+    if (bmax >= kRagMaxList) return FMD_ERR_UNSUPPORTED;  // more than 2047 candidates per centre
     size_t need = 0;
     if (fmd_neighbor_list_workspace_bytes(cell_host, cutoff, n_atoms, bmax, &need) != FMD_OK)
         return FMD_ERR_INVALID_ARGUMENT;
@@ -1281,29 +1635,72 @@ fmd_status fmd_neighbor_list(const float* positions, const float* cell_host, int
     char* p = static_cast<char*>(workspace);
     const CellWorkspace w = carve(p, n_atoms, grid.ncells);
     p += cell_workspace_bytes(n_atoms, grid.ncells);
-    int32_t* nbr = reinterpret_cast<int32_t*>(p); p += align_up(sizeof(int32_t) * size_t(n_atoms) * bmax);
-    int32_t* shift = reinterpret_cast<int32_t*>(p); p += align_up(sizeof(int32_t) * size_t(n_atoms) * bmax * 3);
-    int32_t* count = reinterpret_cast<int32_t*>(p); p += align_up(sizeof(int32_t) * n_atoms);
     int64_t* counts64 = reinterpret_cast<int64_t*>(p); p += align_up(sizeof(int64_t) * (n_atoms + 1));
+    int32_t* n_keys = reinterpret_cast<int32_t*>(p); p += align_up(sizeof(int32_t) * n_atoms);
+    const bool narrow_keys = ragged_key_bytes(n_atoms) == 4;
+    void* keys = p; p += align_up(ragged_key_bytes(n_atoms) * size_t(n_atoms) * (bmax + 1));
     void* cub_temp = p;
     size_t cub_bytes = ragged_scan_bytes(n_atoms);
-    // the ragged kernels read only the first count slots of a candidate row: no fill of the rest
-    fmd_status st = run_cell_list(positions, n_atoms, 1, cell, grid, cand_cut, bmax, nbr, shift, count, w,
-                                  flags, s, false);
+    fmd_status st = build_cells(positions, n_atoms, 1, cell, grid, w, flags, s);
     if (st != FMD_OK) return st;
-    const int threads = 256;
-    ragged_count_kernel<<<grid_for(n_atoms * 32, threads), threads, 0, s>>>(w.wrapped, n_atoms, cell, nbr, shift,
-                                                                            count, bmax, cutoff, counts64);
+    RaggedArgs a{};
+    a.cell_start = w.cell_start;
+    a.cell_atoms = w.cell_atoms;
+    a.cell_pos = w.cell_pos;
+    a.wrapped = w.wrapped;
+    a.cell = cell;
+    a.grid = grid;
+    a.cand_cut = cand_cut;
+    a.cutoff = cutoff;
+    a.lo2 = eager_shell_lo2(cell_host, grid, cutoff);
+    a.bmax = bmax;
+    a.row_cap = bmax + 1;
+    a.sort_cap = 0;
+    if (a.row_cap > 128) {
+        a.sort_cap = 256;
+        while (a.sort_cap < a.row_cap) a.sort_cap <<= 1;
+    }
+    a.off_cap = (2 * grid.s[0] + 1) * (2 * grid.s[1] + 1) * (2 * grid.s[2] + 1);
+    a.keys = keys;
+    a.n_keys = n_keys;
+    a.counts = counts64;
+    a.offsets = offsets;
+    a.n_atoms = n_atoms;
+    a.e_cap = e_capacity;
+    a.center = center;
+    a.neighbor = neighbor;
+    a.images = images;
+    a.dist = dist;
+    a.flags = flags;
+    const size_t key_bytes = ragged_key_bytes(n_atoms);
+    const size_t hood = sizeof(int32_t) * (3 * size_t(a.off_cap) + 1) + sizeof(float) * 3 * size_t(a.off_cap);
+    const size_t collect_smem = (sizeof(float4) + key_bytes) * kRagStage + 2 * sizeof(int32_t) * kRagHome + hood + 16;
+    const size_t emit_smem = key_bytes * size_t(kRagWarps) * a.sort_cap;
+    const void* collect = narrow_keys ? reinterpret_cast<const void*>(ragged_nbr_collect_kernel<uint32_t>)
+                                      : reinterpret_cast<const void*>(ragged_nbr_collect_kernel<uint64_t>);
+    const void* emit = narrow_keys ? reinterpret_cast<const void*>(ragged_nbr_emit_kernel<uint32_t>)
+                                   : reinterpret_cast<const void*>(ragged_nbr_emit_kernel<uint64_t>);
+    if ((st = grant_dynamic_smem(collect, collect_smem)) != FMD_OK || (st = grant_dynamic_smem(emit, emit_smem)) != FMD_OK)
+        return st;
+    const int qgrid = grid.ncells < kNumSMs * 16 ? grid.ncells : kNumSMs * 16;
+    if (narrow_keys)
+        ragged_nbr_collect_kernel<uint32_t><<<qgrid, kRagWarps * 32, collect_smem, s>>>(a);
+    else
+        ragged_nbr_collect_kernel<uint64_t><<<qgrid, kRagWarps * 32, collect_smem, s>>>(a);
     if ((st = check_launch()) != FMD_OK) return st;
     cudaError_t err = cudaMemsetAsync(counts64 + n_atoms, 0, sizeof(int64_t), s);
     if (err != cudaSuccess) return record_cuda_error(err);
     err = cub::DeviceScan::ExclusiveSum(cub_temp, cub_bytes, counts64, offsets, int(n_atoms + 1), s);
     if (err != cudaSuccess) return record_cuda_error(err);
-    ragged_write_kernel<<<grid_for(n_atoms * 32, threads), threads, 0, s>>>(
-        w.wrapped, n_atoms, cell, nbr, shift, count, bmax, cutoff, offsets, e_capacity, center, neighbor, images,
-        dist);
+    const int64_t egrid64 = (n_atoms + kRagWarps - 1) / kRagWarps;
+    const int egrid = int(egrid64 < int64_t(kNumSMs) * 64 ? egrid64 : int64_t(kNumSMs) * 64);
+    if (narrow_keys)
+        ragged_nbr_emit_kernel<uint32_t><<<egrid, kRagWarps * 32, emit_smem, s>>>(a);
+    else
+        ragged_nbr_emit_kernel<uint64_t><<<egrid, kRagWarps * 32, emit_smem, s>>>(a);
     if ((st = check_launch()) != FMD_OK) return st;
     if (wrapped != nullptr) {
+        const int threads = 256;
         copy_wrapped_kernel<<<grid_for(n_atoms, threads), threads, 0, s>>>(w.wrapped, n_atoms, wrapped);
         if ((st = check_launch()) != FMD_OK) return st;
     }

@@ -261,8 +261,12 @@ FMD_API fmd_status fmd_neighbor_list_workspace_bytes(const float* cell_host, flo
  * offsets int64 [n + 1] (edges per centre; offsets[n] = edge count, rows past
  * e_capacity are not written). wrapped (optional) receives the wrapped
  * positions. More than bmax candidates of an atom raises
- * FMD_FLAG_CANDIDATE_OVERFLOW (grow bmax and rerun). Replaces
- * neighbor_list_nvidia (fastmd/graph/gpu_graph_builder.py:108). */
+ * FMD_FLAG_CANDIDATE_OVERFLOW (grow bmax and rerun); bmax of 2048 or more
+ * returns FMD_ERR_UNSUPPORTED. One sweep of the cell list counts the kept
+ * pairs and stores each centre's candidate keys (4 bytes each below 2^20
+ * atoms, else 8; bmax + 1 per centre in the workspace); a second pass sorts
+ * each centre's keys and writes its row. Replaces neighbor_list_nvidia
+ * (fastmd/graph/gpu_graph_builder.py:108). */
 FMD_API fmd_status fmd_neighbor_list(const float* positions, const float* cell_host, int64_t n_atoms,
                                      float cutoff, int32_t bmax, int64_t e_capacity, float* wrapped,
                                      int64_t* center, int64_t* neighbor, int32_t* images, float* dist,

@@ -179,6 +179,73 @@ def test_ragged_neighbor_list_equals_oracle(cuda):
     assert np.array_equal(off.cpu().numpy(), np.searchsorted(c, np.arange(pos.shape[0] + 1)))
 
 
+def _candidates_then_eager_filter(pos32, cell32, rc, bmax, cuda):
+    """The eager path as the composition the reference runs: this library's cell-list candidates at
+    rc + 1e-6 (fmd_candidates_build: the candidate test in the staged float32 arithmetic), then the
+    oracle's eager re-filter (gpu_graph_builder.py:186-192) and the canonical order."""
+    import ctypes
+
+    from fastmd_b200._lib import call, ptr, stream
+    from fastmd_b200.graph import _host_cell
+
+    n = pos32.shape[0]
+    _, cell_ptr = _host_cell(torch.from_numpy(cell32))
+    cand_cut = float(np.float32(rc) + np.float32(1e-6))
+    nbytes = ctypes.c_size_t(0)
+    call("fmd_cell_list_workspace_bytes", cell_ptr, cand_cut, n, 1, ctypes.byref(nbytes))
+    ws = torch.empty(max(int(nbytes.value), 1), dtype=torch.uint8, device=cuda)
+    nbr = torch.empty(n, bmax, dtype=torch.int32, device=cuda)
+    shift = torch.empty(n, bmax, 3, dtype=torch.int32, device=cuda)
+    count = torch.empty(n, dtype=torch.int32, device=cuda)
+    flags = torch.zeros(1, dtype=torch.int32, device=cuda)
+    call("fmd_candidates_build", ptr(torch.from_numpy(pos32).to(cuda)), cell_ptr, n, 1, cand_cut, bmax, ptr(nbr),
+         ptr(shift), ptr(count), None, None, None, ptr(ws), ws.numel(), ptr(flags), stream(cuda))
+    count = count.cpu().numpy()
+    assert int(flags.item()) == 0 and count.max() <= bmax
+    rows = np.repeat(np.arange(n), count)
+    slots = np.concatenate([np.arange(c) for c in count])
+    nb, im = nbr.cpu().numpy()[rows, slots].astype(np.int64), shift.cpu().numpy()[rows, slots].astype(np.int64)
+    wrapped, _, _ = onb.wrap(pos32, cell32, inv_cell=onb.inverse_cell(cell32))
+    keep, dist = onb.ragged_filter(wrapped, cell32, rows, nb, im, rc)
+    return onb.canonical(rows[keep], nb[keep], im[keep], n, dist[keep])
+
+
+def _assert_ragged_equals(pos32, cell32, rc, bmax, cuda, **kw):
+    from fastmd_b200.graph import neighbor_list
+
+    oc, onb_, oim, odist = _candidates_then_eager_filter(pos32, cell32, rc, bmax, cuda)
+    c, nb, im, d, _, off = neighbor_list(torch.from_numpy(pos32).to(cuda), torch.from_numpy(cell32), rc,
+                                         return_wrapped=True, **kw)
+    assert np.array_equal(c.cpu().numpy(), oc) and np.array_equal(nb.cpu().numpy(), onb_)
+    assert np.array_equal(im.cpu().numpy(), oim) and np.array_equal(d.cpu().numpy(), odist)
+    assert np.array_equal(off.cpu().numpy(), np.searchsorted(oc, np.arange(pos32.shape[0] + 1)))
+    return odist
+
+
+def test_ragged_list_at_the_cutoff_equals_candidates_then_the_eager_filter(cuda):
+    """A simple cubic lattice of spacing rc / 2 jittered by a few float32 ulps: thousands of pairs lie
+    within 1e-5 A of rc, where the candidate test (rc + 1e-6) and the eager distance (< rc) decide
+    differently, so the count sweep's shell test runs; bitwise the candidate build followed by the
+    eager filter, also when a too small max_neighbors makes the host grow the candidate rows."""
+    rng = np.random.default_rng(4)
+    g = np.arange(8, dtype=np.float64) * 3.0
+    pos = np.stack(np.meshgrid(g, g, g, indexing="ij"), -1).reshape(-1, 3) + rng.uniform(-3e-6, 3e-6, (512, 3))
+    pos32, cell32 = pos.astype(np.float32), (np.eye(3) * 24.0).astype(np.float32)
+    odist = _assert_ragged_equals(pos32, cell32, 6.0, 256, cuda)
+    assert int((np.abs(odist - 6.0) < 1e-5).sum()) > 1000
+    _assert_ragged_equals(pos32, cell32, 6.0, 256, cuda, max_neighbors=4)
+
+
+def test_ragged_list_of_dense_neighbourhoods_equals_candidates_then_the_eager_filter(cuda):
+    """1,500 atoms at 0.3 / A^3 in a triclinic cell (about 270 neighbours within 6 A, 2 x 2 x 2 cells):
+    every neighbourhood stages about 5,000 (atom, image) entries, five chunks of the write sweep."""
+    rng = np.random.default_rng(5)
+    length = (1500 / 0.3) ** (1.0 / 3.0)
+    cell = np.array([[1.0, 0.0, 0.0], [0.3, 1.0, 0.0], [0.2, 0.1, 1.0]]) * length
+    pos = rng.uniform(0.0, 1.0, (1500, 3)) @ cell
+    _assert_ragged_equals(pos.astype(np.float32), cell.astype(np.float32), 6.0, 600, cuda)
+
+
 def test_ragged_c2_scale_properties(cuda):
     """The op-microbenchmark system (100k atoms, 0.06 / A^3, rc 6): about 54 neighbours per atom,
     canonical order, and every edge's reverse present (up to float32 ties)."""
