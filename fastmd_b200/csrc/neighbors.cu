@@ -1171,11 +1171,11 @@ __device__ __forceinline__ void emit_sorted(const RaggedArgs& a, RowWriter<KeyT>
 }
 
 template <int EPL, class KeyT>
-__device__ __forceinline__ void sort_and_emit(const RaggedArgs& a, RowWriter<KeyT>& r, const KeyT* keys, int k,
+__device__ __forceinline__ void sort_and_emit(const RaggedArgs& a, RowWriter<KeyT>& r, const KeyT (&pre)[4], int k,
                                               int lane) {
     KeyT v[EPL];
 #pragma unroll
-    for (int j = 0; j < EPL; ++j) v[j] = j * 32 + lane < k ? keys[j * 32 + lane] : ~KeyT(0);
+    for (int j = 0; j < EPL; ++j) v[j] = j * 32 + lane < k ? pre[j] : ~KeyT(0);
     warp_bitonic_regs<EPL, KeyT>(v, lane);
 #pragma unroll
     for (int j = 0; j < EPL; ++j)
@@ -1191,8 +1191,11 @@ __global__ void __launch_bounds__(kRagWarps * 32) ragged_nbr_emit_kernel(RaggedA
     const KeyT* keys = static_cast<const KeyT*>(a.keys);
     const int64_t n_warps = int64_t(gridDim.x) * kRagWarps;
     for (int64_t row = int64_t(blockIdx.x) * kRagWarps + warp; row < a.n_atoms; row += n_warps) {
-        const int k = min(a.n_keys[row], a.row_cap);
         const KeyT* src = keys + size_t(row) * a.row_cap;
+        KeyT pre[4];  // the row's first 128 key slots, loaded with its count
+#pragma unroll
+        for (int j = 0; j < 4; ++j) pre[j] = j * 32 + lane < a.row_cap ? src[j * 32 + lane] : ~KeyT(0);
+        const int k = min(a.n_keys[row], a.row_cap);
         RowWriter<KeyT> r;
         r.hp = a.wrapped[row];
         r.row = int32_t(row);
@@ -1200,11 +1203,11 @@ __global__ void __launch_bounds__(kRagWarps * 32) ragged_nbr_emit_kernel(RaggedA
         r.out = a.offsets[row];
         r.end = min(a.offsets[row + 1], a.e_cap);
         if (k <= 32) {
-            sort_and_emit<1, KeyT>(a, r, src, k, lane);
+            sort_and_emit<1, KeyT>(a, r, pre, k, lane);
         } else if (k <= 64) {
-            sort_and_emit<2, KeyT>(a, r, src, k, lane);
+            sort_and_emit<2, KeyT>(a, r, pre, k, lane);
         } else if (k <= 128) {
-            sort_and_emit<4, KeyT>(a, r, src, k, lane);
+            sort_and_emit<4, KeyT>(a, r, pre, k, lane);
         } else {  // a long row: sorted in shared memory
             int n = 256;
             while (n < k) n <<= 1;
