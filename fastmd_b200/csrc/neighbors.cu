@@ -988,6 +988,12 @@ __device__ __forceinline__ int warp_sum_int(int v) {
     return v;
 }
 
+// a staged entry's candidate distance: (q + image @ cell) - p, squared in the candidate build's order
+__device__ __forceinline__ float staged_dist2(float4 s, float4 p) {
+    const float dx = s.x - p.x, dy = s.y - p.y, dz = s.z - p.z;
+    return (dx * dx + dy * dy) + dz * dz;
+}
+
 // KeyT: uint32_t when every atom index is below 2^20, else uint64_t
 template <class KeyT>
 __global__ void __launch_bounds__(kRagWarps * 32) ragged_nbr_collect_kernel(RaggedArgs a) {
@@ -1028,32 +1034,49 @@ __global__ void __launch_bounds__(kRagWarps * 32) ragged_nbr_collect_kernel(Ragg
                     const float4 hp = a.cell_pos[hb + h];
                     KeyT* row = keys + size_t(a.cell_atoms[hb + h]) * a.row_cap;
                     int n = cand_n[h], kept = 0;
+                    // the test: lane i keeps the hit mask of staged entries [32 i, 32 i + 32) (ns <= 1024)
+                    unsigned mine = 0u;
                     for (int base = 0; base < ns; base += 32) {
                         const int k = base + lane;
-                        float d2 = cut2;
-                        if (k < ns) {
-                            const float4 s = spos[k];
-                            const float dx = s.x - hp.x, dy = s.y - hp.y, dz = s.z - hp.z;
-                            d2 = (dx * dx + dy * dy) + dz * dz;
-                        }
-                        const bool hit = d2 < cut2;
-                        const unsigned mask = __ballot_sync(0xffffffffu, hit);
-                        if (hit) {
-                            const int pos = n + __popc(mask & below);
+                        const bool hit = k < ns && staged_dist2(spos[k], hp) < cut2;
+                        const unsigned m = __ballot_sync(0xffffffffu, hit);
+                        if (lane == (base >> 5)) mine = m;
+                    }
+                    // the hits, one per lane: the owning 32-entry group by a search over the groups'
+                    // inclusive hit counts, the entry by the rank of the hit inside the group's mask
+                    const int c = __popc(mine);
+                    int incl = c;
+                    for (int d = 1; d < 32; d <<= 1) {
+                        const int y = __shfl_up_sync(0xffffffffu, incl, d);
+                        if (lane >= d) incl += y;
+                    }
+                    const int excl = incl - c, total = __shfl_sync(0xffffffffu, incl, 31);
+                    for (int j0 = 0; j0 < total; j0 += 32) {
+                        const int jj = j0 + lane;
+                        int grp = 0;
+#pragma unroll
+                        for (int step = 16; step >= 1; step >>= 1)
+                            if (__shfl_sync(0xffffffffu, incl, grp + step - 1) <= jj) grp += step;
+                        const unsigned m = __shfl_sync(0xffffffffu, mine, grp);
+                        const int r = jj - __shfl_sync(0xffffffffu, excl, grp);
+                        if (jj < total) {
+                            const int k = grp * 32 + int(__fns(m, 0, r + 1));
+                            const float d2 = staged_dist2(spos[k], hp);
+                            const int pos = n + jj;
                             if (pos < a.row_cap) row[pos] = skey[k];
-                            kept += d2 < a.lo2 ? 1 : 0;
-                        }
-                        n += __popc(mask);
-                        const bool shell = hit && !(d2 < a.lo2);
-                        if (__any_sync(0xffffffffu, shell) && shell) {  // the eager path's own distance decides
-                            const int lo = hood_offset(o.pref, n_off, c0 + k);
-                            const float4 q = a.cell_pos[o.begin[lo] + (c0 + k - o.pref[lo])];
-                            kept += eager_dist(hp, q, o.shift[3 * lo], o.shift[3 * lo + 1], o.shift[3 * lo + 2]) <
-                                            a.cutoff
-                                        ? 1
-                                        : 0;
+                            if (d2 < a.lo2) {
+                                ++kept;
+                            } else {  // the shell: the eager path's own distance decides
+                                const int lo = hood_offset(o.pref, n_off, c0 + k);
+                                const float4 q = a.cell_pos[o.begin[lo] + (c0 + k - o.pref[lo])];
+                                kept += eager_dist(hp, q, o.shift[3 * lo], o.shift[3 * lo + 1], o.shift[3 * lo + 2]) <
+                                                a.cutoff
+                                            ? 1
+                                            : 0;
+                            }
                         }
                     }
+                    n += total;
                     kept = warp_sum_int(kept);
                     if (lane == 0) {
                         kept_n[h] += kept;
