@@ -699,16 +699,103 @@ __global__ void __launch_bounds__(kQ * C, 2) node_last_kernel(FusedWeights w, Fu
 }
 
 // per receiver run: dR(l) and dY (warp per edge, lane channels; dY accumulated over layers); every
-// output is one edge's, so the kMsgBwdWarps warps of a receiver give the same bits in any number
+// output is one edge's, so the warps of a receiver give the same bits in any number or order
 constexpr int kMsgBwdWarps = 8;
-template <int C, int P>
-__global__ void __launch_bounds__(32 * kMsgBwdWarps) msg_bwd_edge_kernel(GraphArgs g, FusedWeights w, FusedState st,
-                                                                        int L, int accumulate_dy) {
+
+// one warp: U edges e0, e0 + stride, ... (those below end) of receiver gradient rows g0, gx, gy, gz,
+// their loads issued together
+template <int C, int P, int U>
+__device__ __forceinline__ void msg_bwd_edges(const GraphArgs& g, const FusedWeights& w, const FusedState& st, int L,
+                                              int accumulate_dy, const float* g0, const float* gx, const float* gy,
+                                              const float* gz, int64_t e0, int64_t stride, int64_t end, int lane) {
     constexpr int CPL = C / 32;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float* R = st.R[L];
     float* dR = st.dR[L];
-    for (int64_t i = blockIdx.x; i < g.n_atoms; i += gridDim.x) {
+    int64_t ee[U];
+    bool valid[U];
+    float4 y[U];
+    float sv[U][CPL], r1[U][CPL], r3[U][CPL], vx[U][CPL], vy[U][CPL], vz[U][CPL];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        valid[u] = e0 + u * stride < end;
+        ee[u] = valid[u] ? e0 + u * stride : e0;
+        const int64_t j = g.edge_index[2 * ee[u] + 1];
+        y[u] = st.ysh[ee[u]];
+        const float* Re = R + ee[u] * (P * C) + lane * CPL;
+        const float* srow = ((L == 0) ? w.s_t0 + int64_t(st.elem[j]) * C : st.s_t[L] + j * C) + lane * CPL;
+        ldv<CPL>(srow, sv[u]);
+        ldv<CPL>(Re + C, r1[u]);
+        if constexpr (P == 4) {
+            const float* vrow = st.v_t[L] + j * 3 * C + lane * CPL;
+            ldv<CPL>(Re + 3 * C, r3[u]);
+            ldv<CPL>(vrow, vx[u]);
+            ldv<CPL>(vrow + C, vy[u]);
+            ldv<CPL>(vrow + 2 * C, vz[u]);
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        if (!valid[u]) continue;
+        const int64_t e = ee[u];
+        float* dRe = dR + e * (P * C) + lane * CPL;
+        float o0[CPL], o1[CPL], o2[CPL], o3[CPL];
+        float px = 0.f, py = 0.f, pz = 0.f;
+#pragma unroll
+        for (int q = 0; q < CPL; ++q) {
+            const float s = sv[u][q];
+            const float gdy = (gx[q] * y[u].x + gy[q] * y[u].y) + gz[q] * y[u].z;
+            o0[q] = g0[q] * s;
+            o1[q] = s * gdy;
+            const float c1 = r1[u][q] * s;
+            px = fmaf(c1, gx[q], px);
+            py = fmaf(c1, gy[q], py);
+            pz = fmaf(c1, gz[q], pz);
+            if constexpr (P == 4) {
+                o2[q] = (gx[q] * vx[u][q] + gy[q] * vy[u][q]) + gz[q] * vz[u][q];
+                o3[q] = g0[q] * ((vx[u][q] * y[u].x + vy[u][q] * y[u].y) + vz[u][q] * y[u].z) * kIS3;
+                const float c3 = r3[u][q] * g0[q] * kIS3;
+                px = fmaf(c3, vx[u][q], px);
+                py = fmaf(c3, vy[u][q], py);
+                pz = fmaf(c3, vz[u][q], pz);
+            }
+        }
+        stv<CPL>(dRe, o0);
+        stv<CPL>(dRe + C, o1);
+        if constexpr (P == 4) {
+            stv<CPL>(dRe + 2 * C, o2);
+            stv<CPL>(dRe + 3 * C, o3);
+        }
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) {
+            px += __shfl_xor_sync(0xffffffffu, px, d);
+            py += __shfl_xor_sync(0xffffffffu, py, d);
+            pz += __shfl_xor_sync(0xffffffffu, pz, d);
+        }
+        if (lane == 0) {
+            float* out = st.dY + 3 * e;
+            if (accumulate_dy) {
+                out[0] += px;
+                out[1] += py;
+                out[2] += pz;
+            } else {
+                out[0] = px;
+                out[1] = py;
+                out[2] = pz;
+            }
+        }
+    }
+}
+
+// per_warp: each warp owns whole receiver runs (grid-stride over warps), two edges in flight; else a
+// CTA per receiver with its warps over the run (few atoms: every SM busy)
+template <int C, int P>
+__global__ void __launch_bounds__(32 * kMsgBwdWarps) msg_bwd_edge_kernel(GraphArgs g, FusedWeights w, FusedState st,
+                                                                        int L, int accumulate_dy, int per_warp) {
+    constexpr int CPL = C / 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t first = per_warp ? int64_t(blockIdx.x) * kMsgBwdWarps + warp : blockIdx.x;
+    const int64_t step = per_warp ? int64_t(gridDim.x) * kMsgBwdWarps : gridDim.x;
+    for (int64_t i = first; i < g.n_atoms; i += step) {
         float g0[CPL], gx[CPL], gy[CPL], gz[CPL];
 #pragma unroll
         for (int q = 0; q < CPL; ++q) {
@@ -719,66 +806,12 @@ __global__ void __launch_bounds__(32 * kMsgBwdWarps) msg_bwd_edge_kernel(GraphAr
             gz[q] = st.dA1[L][i * 3 * C + 2 * C + k] * w.inv_avg;
         }
         const int64_t beg = g.recv_off[i], end = g.recv_off[i + 1];
-        for (int64_t e = beg + warp; e < end; e += kMsgBwdWarps) {
-            const int64_t j = g.edge_index[2 * e + 1];
-            const float4 y = st.ysh[e];
-            const float* Re = R + e * (P * C) + lane * CPL;
-            float* dRe = dR + e * (P * C) + lane * CPL;
-            const float* srow = ((L == 0) ? w.s_t0 + int64_t(st.elem[j]) * C : st.s_t[L] + j * C) + lane * CPL;
-            float sv[CPL], r1[CPL], r3[CPL], vx[CPL], vy[CPL], vz[CPL], o0[CPL], o1[CPL], o2[CPL], o3[CPL];
-            ldv<CPL>(srow, sv);
-            ldv<CPL>(Re + C, r1);
-            if constexpr (P == 4) {
-                const float* vrow = st.v_t[L] + j * 3 * C + lane * CPL;
-                ldv<CPL>(Re + 3 * C, r3);
-                ldv<CPL>(vrow, vx);
-                ldv<CPL>(vrow + C, vy);
-                ldv<CPL>(vrow + 2 * C, vz);
-            }
-            float px = 0.f, py = 0.f, pz = 0.f;
-#pragma unroll
-            for (int q = 0; q < CPL; ++q) {
-                const float s = sv[q];
-                const float gdy = (gx[q] * y.x + gy[q] * y.y) + gz[q] * y.z;
-                o0[q] = g0[q] * s;
-                o1[q] = s * gdy;
-                const float c1 = r1[q] * s;
-                px = fmaf(c1, gx[q], px);
-                py = fmaf(c1, gy[q], py);
-                pz = fmaf(c1, gz[q], pz);
-                if constexpr (P == 4) {
-                    o2[q] = (gx[q] * vx[q] + gy[q] * vy[q]) + gz[q] * vz[q];
-                    o3[q] = g0[q] * ((vx[q] * y.x + vy[q] * y.y) + vz[q] * y.z) * kIS3;
-                    const float c3 = r3[q] * g0[q] * kIS3;
-                    px = fmaf(c3, vx[q], px);
-                    py = fmaf(c3, vy[q], py);
-                    pz = fmaf(c3, vz[q], pz);
-                }
-            }
-            stv<CPL>(dRe, o0);
-            stv<CPL>(dRe + C, o1);
-            if constexpr (P == 4) {
-                stv<CPL>(dRe + 2 * C, o2);
-                stv<CPL>(dRe + 3 * C, o3);
-            }
-#pragma unroll
-            for (int d = 16; d > 0; d >>= 1) {
-                px += __shfl_xor_sync(0xffffffffu, px, d);
-                py += __shfl_xor_sync(0xffffffffu, py, d);
-                pz += __shfl_xor_sync(0xffffffffu, pz, d);
-            }
-            if (lane == 0) {
-                float* out = st.dY + 3 * e;
-                if (accumulate_dy) {
-                    out[0] += px;
-                    out[1] += py;
-                    out[2] += pz;
-                } else {
-                    out[0] = px;
-                    out[1] = py;
-                    out[2] = pz;
-                }
-            }
+        if (per_warp) {
+            for (int64_t e = beg; e < end; e += 2)
+                msg_bwd_edges<C, P, 2>(g, w, st, L, accumulate_dy, g0, gx, gy, gz, e, 1, end, lane);
+        } else {
+            for (int64_t e = beg + warp; e < end; e += kMsgBwdWarps)
+                msg_bwd_edges<C, P, 1>(g, w, st, L, accumulate_dy, g0, gx, gy, gz, e, kMsgBwdWarps, end, lane);
         }
     }
 }
@@ -1774,6 +1807,9 @@ fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeigh
     const int64_t n_tiles = (ea.n_edges + kTF - 1) / kTF;
     const int edge_grid = int(n_tiles < int64_t(kNumSMs) * 8 ? n_tiles : int64_t(kNumSMs) * 8);
     const int atom_grid = int(ga.n_atoms < int64_t(kNumSMs) * 16 ? ga.n_atoms : int64_t(kNumSMs) * 16);
+    // the per-edge backward: a warp per receiver run once every SM has several CTAs of such warps
+    const int bwd_per_warp = ga.n_atoms >= int64_t(kNumSMs) * 16 ? 1 : 0;
+    const int msg_bwd_grid = bwd_per_warp ? int((ga.n_atoms + kMsgBwdWarps - 1) / kMsgBwdWarps) : atom_grid;
     // fewer groups than SMs: one CTA per entry of the group table (4x the CTAs, the same results)
     const bool single = st.n_groups < kNumSMs;
     const int64_t units = single ? st.n_groups * kG : st.n_groups;
@@ -1833,7 +1869,7 @@ fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeigh
         else node_last_kernel<C, kG><<<group_grid, kQ * C, node_smem, s>>>(w, st, L - 1);
     }
     for (int l = L - 1; l >= 1; --l) {
-        if (on(4)) msg_bwd_edge_kernel<C, 4><<<atom_grid, 32 * kMsgBwdWarps, 0, s>>>(ga, w, st, l, l != L - 1);
+        if (on(4)) msg_bwd_edge_kernel<C, 4><<<msg_bwd_grid, 32 * kMsgBwdWarps, 0, s>>>(ga, w, st, l, l != L - 1, bwd_per_warp);
         if (on(5)) {
             if (ntc) {
                 if ((stt = check_launch()) != FMD_OK) return stt;
@@ -1843,7 +1879,7 @@ fmd_status launch_step(const EdgeArgs& ea, const GraphArgs& ga, const FusedWeigh
             else sender_node_kernel<C, kG><<<group_grid, kQ * C, node_smem, s>>>(ga, w, st, l);
         }
     }
-    if (on(4)) msg_bwd_edge_kernel<C, 2><<<atom_grid, 32 * kMsgBwdWarps, 0, s>>>(ga, w, st, 0, L != 1);
+    if (on(4)) msg_bwd_edge_kernel<C, 2><<<msg_bwd_grid, 32 * kMsgBwdWarps, 0, s>>>(ga, w, st, 0, L != 1, bwd_per_warp);
     if (tc && b_tiles > 0 && on(6)) {
         if ((stt = check_launch()) != FMD_OK) return stt;
         if ((stt = radial_tc_backward(w, st, ea.n_edges, C, s)) != FMD_OK) return stt;
