@@ -13,8 +13,10 @@ model energy and forces -> NHC half. ``--replicas R`` runs R independent
 config 4's shard (64/128/256/512 replicas on 1/2/4/8 GPUs), so ``value`` is
 config 4's whole-job atom-steps/s at every N. At N = 1 the line also carries
 ``config1`` (one 135-atom replica alone: its ms/step, roofline and the three
-execution modes) and ``config0_matris`` (the same system under MatRIS-10M,
-whole_step, beside the CPU port of the reference's config-0 path).
+execution modes), ``config0_matris`` (the same system under MatRIS-10M,
+whole_step, beside the CPU port of the reference's config-0 path) and
+``sevennet_s01`` (the same system under the SevenNet-0-architecture NequIP
+potential, beside the reference's published 7net-0 step on H100).
 
 Under torchrun (N > 1) every rank integrates its own replicas (seeds
 rank*R .. rank*R+R-1), no collective on the step path; the per-replica
@@ -318,6 +320,16 @@ def _ours(args):
             matris = _config0_matris(args, device, flush)
         except Exception as error:  # noqa: BLE001 - the line still reports the measured step
             matris = {"error": f"{type(error).__name__}: {error}"}
+    sevennet = None
+    if rank == 0 and world == 1 and not args.no_matris:
+        try:  # the reference's S01 system under the SevenNet-0-architecture potential (README.md:82)
+            sevennet = _op_nequip(argparse.Namespace(reps=3, steps=1000, warmup=100))
+            sevennet.update({"workload": "S01: the 135-atom CsSnI3 cell (config 1's system) under the "
+                                         "SevenNet-0-architecture NequIP potential (seeded weights), NVT-NHC "
+                                         "whole_step", "reference_published_h100_ms_per_step": 2.5952,
+                             "reference_source": "README.md:82 (7net-0 on S01, H100, incl. trajectory output)"})
+        except Exception as error:  # noqa: BLE001 - the line still reports the measured step
+            sevennet = {"error": f"{type(error).__name__}: {error}"}
     ops = None
     if rank == 0 and world == 1 and not args.no_ops:
         try:
@@ -345,7 +357,7 @@ def _ours(args):
                     f"{S} steps"},
             "gpu_launches": launches_per_window * windows, "launches_per_step": launches_per_window / S,
             "roofline": roofline, "cpu_baseline": cpu, "clocks": clk, "ops_config2": ops,
-            "execution_modes": modes, "config1": config1, "config0_matris": matris,
+            "execution_modes": modes, "config1": config1, "config0_matris": matris, "sevennet_s01": sevennet,
             "fallbacks": md.runner.fallbacks, "candidate_refreshes": md.runner.refreshes,
             "final_temperature_K": float(thermo_now["temperature"][0]),
             "final_conserved_eV": float(thermo_now["conserved_energy"][0])}
