@@ -10,9 +10,12 @@ Restates fastmd/engine/kernels/triton_wide_gemm.py:
 The products of TF32 parts are exact in float64 and every sum here is float64, so ``gemm_3xtf32``
 returns the exact value of the 3xTF32 formula with ``lo`` kept exact; a tensor-core implementation
 differs from it by the FP32 rounding of its accumulations (bounded per 64-wide chunk) and by reading
-``lo`` at TF32 precision (at most 2^-22 of a product's magnitude). Parity unpinned: the reference
-kernel needs TMA descriptors on a GPU and cannot run in this container, so only the TF32 rounding is
-pinned (by known answers from the PTX definition of ``cvt.rna.tf32.f32``), not the reference's outputs.
+``lo`` at TF32 precision (at most 2^-22 of a product's magnitude). Pinned to the reference's own kernels:
+``tests/golden/make_golden.py`` runs ``_split_kernel`` and ``_wide_gemm_persistent`` / ``_wide_gemm_tiles``
+under the Triton interpreter (their one PTX instruction, ``cvt.rna.tf32.f32``, replaced by its bit
+definition, which the known answers of the CPU tests pin), and this restatement equals those outputs: the
+split bitwise, the products within 2e-7 of ``sum |x||w|`` (the interpreter's FP32 dots) on five shapes
+(K 64 to 448, a partial last chunk, bias, accumulate, the input-gradient orientation).
 """
 from __future__ import annotations
 

@@ -40,6 +40,9 @@ used) and runs, on CPU:
   legacy CPU graph (``matris_cases``; pymatgen placeholders, the graph fed by a dense search);
 * the line-graph envelope product ``_line_envelope_fwd/_bwd``
   (fastmd/models/matris/op/triton_line_envelope.py:50/:87) under the interpreter;
+* the 3xTF32 wide GEMM ``_split_kernel`` + ``_wide_gemm_persistent`` / ``_wide_gemm_tiles``
+  (fastmd/engine/kernels/triton_wide_gemm.py:132/:103/:120) under the interpreter, its one inline
+  PTX instruction (``cvt.rna.tf32.f32``) replaced by that instruction's definition in bit operations;
 * the torch backend of ``GPUNoseHooverChainNVT`` (fastmd/execution/gpu_nhc.py:709,
   ``backend="torch"``) with harmonic forces, and ``maxwell_boltzmann_momenta``
   (gpu_nhc.py:199).
@@ -166,6 +169,54 @@ def line_envelope_cases(torch, le):
         le._line_envelope_bwd[grid](tg, tb, ts, tt, grad, T, D=D, S0=D, GS0=D, BM=BM, BD=BD)
         out.update({f"env_{tag}_base": base, f"env_{tag}_source": source, f"env_{tag}_target": target,
                     f"env_{tag}_gout": gout, f"env_{tag}_out": env.numpy(), f"env_{tag}_grad": grad.numpy()})
+    return out
+
+
+def wide_gemm_cases(torch, wg):
+    """The reference's 3xTF32 wide GEMM (fastmd/engine/kernels/triton_wide_gemm.py): ``_split_kernel`` (:132)
+    for the K-major weight pairs, then ``_wide_gemm_persistent`` (:103, K <= 256) or ``_wide_gemm_tiles`` (:120,
+    K >= 384) on tensor descriptors, with the launch geometry of ``_launch`` (:297: 128-row tiles, BN = min(128, N),
+    BK 64), under the interpreter. The interpreter cannot execute the kernel's one inline PTX instruction
+    (``cvt.rna.tf32.f32`` in ``_rna_tf32``, :63), so that function is replaced by the instruction's definition in
+    bit operations (round to nearest, ties away from zero, the low 13 bits cleared); everything else is the
+    reference's code. The interpreter's dots are FP32 products of the given operands (the TF32 parts exact), so
+    these outputs are the reference's algorithm (term set and order, 64-wide chunks on fresh accumulators summed in
+    FP32, bias then c) at FP32 rounding."""
+    import triton
+    from triton.tools.tensor_descriptor import TensorDescriptor
+
+    from _rna_tf32_definition import rna_tf32 as _rna_tf32_definition
+    from inputs import WIDE_GEMM_CASES, wide_gemm_inputs
+
+    wg._rna_tf32 = _rna_tf32_definition
+    out = {}
+    # the inputs are counter streams (tests/golden/inputs.py), regenerated by the tests: only outputs are stored
+    for i, (tag, (m, k, n, transposed, has_bias, has_c)) in enumerate(WIDE_GEMM_CASES.items()):
+        a, w, bias, c = wide_gemm_inputs(i, m, k, n, transposed, has_bias, has_c)
+        tw = torch.from_numpy(w)
+        src = tw.t() if transposed else tw  # the K-major [N, K] operand
+        hi = torch.empty(src.shape)
+        lo = torch.empty(src.shape)
+        total = n * k
+        wg._split_kernel[(triton.cdiv(total, 1024),)](src, hi, lo, total, COLS=k, S_ROW=src.stride(0),
+                                                       S_COL=src.stride(1), BLOCK=1024)
+        ta = torch.from_numpy(a)
+        y = torch.empty((m, n))
+        bm, bn = 128, min(128, n)
+        args = (TensorDescriptor.from_tensor(ta, [bm, wg._BK]), TensorDescriptor.from_tensor(hi, [bn, wg._BK]),
+                TensorDescriptor.from_tensor(lo, [bn, wg._BK]), torch.from_numpy(c) if has_c else y,
+                TensorDescriptor.from_tensor(y, [bm, bn]), torch.from_numpy(bias) if has_bias else hi, m)
+        consts = dict(K=k, NT_N=n // bn, BM=bm, BN=bn, BK=wg._BK, PREC="tf32x3", HAS_BIAS=has_bias, HAS_C=has_c)
+        tiles = triton.cdiv(m, bm) * (n // bn)
+        if k >= 384:
+            wg._wide_gemm_tiles[(tiles,)](*args, **consts)
+        else:  # persistent programs: min(tiles, SMs) of a 148-SM device
+            wg._wide_gemm_persistent[(min(tiles, 148),)](*args, **consts)
+        out[f"wg_{tag}_y"] = y.numpy()
+        out[f"wg_{tag}_shape"] = np.array([m, k, n, transposed, has_bias, has_c], dtype=np.int64)
+        if tag == "k64_n64_bias":  # the reference's K-major split of one weight, for the bitwise split check
+            out[f"wg_{tag}_hi"] = hi.numpy()
+            out[f"wg_{tag}_lo"] = lo.numpy()
     return out
 
 
@@ -866,6 +917,7 @@ def radial_cases(torch):
 
 def main(reference: str, only: list[str]) -> None:
     os.environ["TRITON_INTERPRET"] = "1"
+    sys.path.insert(0, str(HERE))
     _install_stubs()
     sys.path.insert(0, reference)
     import torch
@@ -886,6 +938,7 @@ def main(reference: str, only: list[str]) -> None:
     import fastmd.models.matris.op.triton_directed_pair_aggregate as pa
     import fastmd.models.matris.op.triton_residual_add as ra
     import fastmd.models.matris.op.triton_line_envelope as le
+    import fastmd.engine.kernels.triton_wide_gemm as wg
 
     fixtures = {
         "gather_cat": lambda: gather_cat_cases(torch, gc),
@@ -904,6 +957,7 @@ def main(reference: str, only: list[str]) -> None:
         "padding": lambda: padding_cases(torch, fcb),
         "matris": lambda: matris_cases(torch),
         "line_envelope": lambda: line_envelope_cases(torch, le),
+        "wide_gemm": lambda: wide_gemm_cases(torch, wg),
     }
     for name, make in fixtures.items():
         if not only or name in only:

@@ -222,3 +222,37 @@ def test_grouped_problems_equal_single_calls(shapes):
     torch.cuda.synchronize()
     for y, ref in zip(outs, singles):
         assert torch.equal(y, ref)
+
+
+def test_matches_the_reference_kernel_outputs():
+    """fmd_gemm_tf32x3 against the outputs of the reference's own 3xTF32 kernels on the same inputs (the
+    golden fixture: fastmd/engine/kernels/triton_wide_gemm.py under the Triton interpreter, FP32 dots): the
+    forward with bias, the accumulate form (+ c), the input-gradient orientation (dX = dY W into c), a
+    64-wide tile and K = 448. Bar: the kernel's own bound against the exact 3xTF32 value plus the
+    fixture's FP32 rounding (below 2e-7 of the same scale)."""
+    import sys
+    from pathlib import Path
+
+    from fastmd_b200 import _lib, wide_gemm
+    from fastmd_b200._lib import call, ptr
+
+    here = Path(__file__).resolve().parent / "golden"
+    sys.path.insert(0, str(here))
+    from inputs import WIDE_GEMM_CASES, wide_gemm_inputs
+
+    golden = np.load(here / "wide_gemm.npz")
+    s = _lib.stream()
+    for i, (tag, (m, k, n, transposed, has_bias, has_c)) in enumerate(WIDE_GEMM_CASES.items()):
+        a, w, bias, c = wide_gemm_inputs(i, m, k, n, transposed, has_bias, has_c)
+        ad, wd = torch.from_numpy(a).cuda(), torch.from_numpy(w).cuda()
+        bd = torch.from_numpy(bias).cuda() if has_bias else None
+        cd = torch.from_numpy(c).cuda() if has_c else None
+        sp = wide_gemm._split(wd, transposed)  # the K-major [n, k] pair of B
+        y = torch.empty(m, n, device="cuda")
+        call("fmd_gemm_tf32x3", ptr(ad), k, ptr(sp.hi), ptr(sp.lo), k, ptr(bd) if has_bias else None,
+             ptr(cd) if has_c else None, n if has_c else 0, ptr(y), n, m, n, k, 0, 0, None, s)
+        torch.cuda.synchronize()
+        wk = np.ascontiguousarray(w.T if transposed else w)
+        scale = ow.error_scale(a, wk, bias=bias, c=c)
+        err = np.abs(y.cpu().double().numpy() - golden[f"wg_{tag}_y"].astype(np.float64)) / scale
+        assert err.max() < TOL + 2e-7, (tag, err.max())

@@ -52,3 +52,34 @@ def test_3xtf32_formula_is_fp32_accurate():
     # one TF32 product alone is far coarser: the lo terms carry the FP32 accuracy
     one = ow.rna_tf32(x).astype(np.float64) @ ow.rna_tf32(w).astype(np.float64).T + b
     assert np.max(np.abs(one - exact) / scale) > 2.0**-14
+
+
+def _golden_cases():
+    import sys
+    from pathlib import Path
+
+    here = Path(__file__).resolve().parent / "golden"
+    sys.path.insert(0, str(here))
+    from inputs import WIDE_GEMM_CASES, wide_gemm_inputs
+
+    return np.load(here / "wide_gemm.npz"), WIDE_GEMM_CASES, wide_gemm_inputs
+
+
+def test_oracle_matches_the_reference_kernel():
+    """The reference's own 3xTF32 kernels (_split_kernel, _wide_gemm_persistent / _wide_gemm_tiles of
+    fastmd/engine/kernels/triton_wide_gemm.py, run by the Triton interpreter with cvt.rna.tf32.f32 as its
+    bit definition; tests/golden/make_golden.py) against the oracle: the split bitwise, the products within
+    FP32 rounding of the chunk sums (the interpreter's dots are FP32; the oracle's sums are exact)."""
+    golden, cases, inputs = _golden_cases()
+    for i, (tag, (m, k, n, transposed, has_bias, has_c)) in enumerate(cases.items()):
+        a, w, bias, c = inputs(i, m, k, n, transposed, has_bias, has_c)
+        assert list(golden[f"wg_{tag}_shape"]) == [m, k, n, transposed, has_bias, has_c]
+        wk = np.ascontiguousarray(w.T if transposed else w)  # the [N, K] operand: y = a wk^T
+        ref = ow.gemm_3xtf32(a, wk, bias=bias, c=c)
+        scale = ow.error_scale(a, wk, bias=bias, c=c)
+        err = np.abs(golden[f"wg_{tag}_y"].astype(np.float64) - ref) / scale
+        assert err.max() < 5e-7, (tag, err.max())
+        if f"wg_{tag}_hi" in golden:
+            hi, lo = ow.split(wk)
+            np.testing.assert_array_equal(golden[f"wg_{tag}_hi"], hi)
+            np.testing.assert_array_equal(golden[f"wg_{tag}_lo"], lo)
