@@ -9,7 +9,8 @@
 //   act = identity or SiLU (the pre-activation optionally stored)
 //
 // 64x64 output tile per 256-thread CTA, 16-deep K slices staged in shared
-// memory, 4x4 outputs per thread; every output is one sequential FP32 FMA
+// memory (double-buffered: the next slice's loads overlap the current slice's
+// products), 4x4 outputs per thread; every output is one sequential FP32 FMA
 // chain over K (deterministic, independent of the tiling of M and N).
 
 #include "common.cuh"
@@ -44,58 +45,82 @@ struct GemmArgs {
     int accumulate;
 };
 
+// the operand values of one K slice that thread t stages: A rows (t + 256 q) / 16, k (t + 256 q) % 16;
+// W: columns (t + 256 q) / 16 and k % 16 (W [N, K]), or k (t + 256 q) / 64 and columns % 64 (W [K, N])
+__device__ __forceinline__ void load_slice(const GemmArgs& g, int64_t row0, int col0, int k0, float (&pa)[4],
+                                           float (&pw)[4]) {
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        const int idx = threadIdx.x + t * 256;
+        const int r = idx / BK, kk = idx % BK;
+        const int64_t gr = row0 + r;
+        const int gk = k0 + kk;
+        float v = 0.f;
+        if (gr < g.m && gk < g.k) {
+            v = g.a[gr * g.lda + gk];
+            if (g.a_pre) v *= silu_grad(g.a_pre[gr * g.lda_pre + gk]);
+        }
+        pa[t] = v;
+    }
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        const int idx = threadIdx.x + t * 256;
+        float v = 0.f;
+        if (g.trans_w) {
+            const int c = idx / BK, kk = idx % BK;
+            const int gc = col0 + c, gk = k0 + kk;
+            if (gc < g.n && gk < g.k) v = g.w[int64_t(gc) * g.ldw + gk];
+        } else {
+            const int kk = idx / BN, c = idx % BN;
+            const int gc = col0 + c, gk = k0 + kk;
+            if (gc < g.n && gk < g.k) v = g.w[int64_t(gk) * g.ldw + gc];
+        }
+        pw[t] = v;
+    }
+}
+
+__device__ __forceinline__ void store_slice(const GemmArgs& g, float (*As)[BM + 4], float (*Ws)[BN + 4],
+                                            const float (&pa)[4], const float (&pw)[4]) {
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        const int idx = threadIdx.x + t * 256;
+        As[idx % BK][idx / BK] = pa[t];
+        if (g.trans_w) Ws[idx % BK][idx / BK] = pw[t];
+        else Ws[idx / BN][idx % BN] = pw[t];
+    }
+}
+
+// K slices double-buffered: the next slice's global loads are in flight (registers) while the current
+// slice's products run from shared memory; one barrier per slice
 __global__ void __launch_bounds__(256) sgemm_kernel(GemmArgs g) {
-    __shared__ float As[BK][BM + 4];
-    __shared__ float Ws[BK][BN + 4];
+    __shared__ float As[2][BK][BM + 4];
+    __shared__ float Ws[2][BK][BN + 4];
     const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
     const int64_t row0 = int64_t(blockIdx.x) * BM;
     const int col0 = blockIdx.y * BN;
     float acc[4][4] = {};
-    for (int k0 = 0; k0 < g.k; k0 += BK) {
-        // A tile: 64 rows x 16 k, 4 loads per thread
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-            const int idx = threadIdx.x + t * 256;
-            const int r = idx / BK, kk = idx % BK;
-            const int64_t gr = row0 + r;
-            const int gk = k0 + kk;
-            float v = 0.f;
-            if (gr < g.m && gk < g.k) {
-                v = g.a[gr * g.lda + gk];
-                if (g.a_pre) v *= silu_grad(g.a_pre[gr * g.lda_pre + gk]);
-            }
-            As[kk][r] = v;
-        }
-        // W tile: 16 k x 64 n
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-            const int idx = threadIdx.x + t * 256;
-            float v = 0.f;
-            if (g.trans_w) {
-                const int c = idx / BK, kk = idx % BK;
-                const int gc = col0 + c, gk = k0 + kk;
-                if (gc < g.n && gk < g.k) v = g.w[int64_t(gc) * g.ldw + gk];
-                Ws[kk][c] = v;
-            } else {
-                const int kk = idx / BN, c = idx % BN;
-                const int gc = col0 + c, gk = k0 + kk;
-                if (gc < g.n && gk < g.k) v = g.w[int64_t(gk) * g.ldw + gc];
-                Ws[kk][c] = v;
-            }
-        }
-        __syncthreads();
+    float pa[4], pw[4];
+    load_slice(g, row0, col0, 0, pa, pw);
+    store_slice(g, As[0], Ws[0], pa, pw);
+    __syncthreads();
+    const int slices = (g.k + BK - 1) / BK;
+    for (int sl = 0; sl < slices; ++sl) {
+        const int buf = sl & 1;
+        if (sl + 1 < slices) load_slice(g, row0, col0, (sl + 1) * BK, pa, pw);
 #pragma unroll
         for (int kk = 0; kk < BK; ++kk) {
             float av[4], wv[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) av[i] = As[kk][ty + 16 * i];
+            for (int i = 0; i < 4; ++i) av[i] = As[buf][kk][ty + 16 * i];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) wv[j] = Ws[kk][tx + 16 * j];
+            for (int j = 0; j < 4; ++j) wv[j] = Ws[buf][kk][tx + 16 * j];
 #pragma unroll
             for (int i = 0; i < 4; ++i)
 #pragma unroll
                 for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], wv[j], acc[i][j]);
         }
+        // the other buffer was last read before the previous barrier
+        if (sl + 1 < slices) store_slice(g, As[buf ^ 1], Ws[buf ^ 1], pa, pw);
         __syncthreads();
     }
 #pragma unroll
