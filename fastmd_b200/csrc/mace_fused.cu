@@ -1592,17 +1592,18 @@ __global__ void __launch_bounds__(256) edge_geom_bwd_tc_kernel(EdgeArgs a, Fused
 // the radial MLPs of every layer as GEMMs on the tensor cores:
 //   p2 = silu(p1) W2^T, p3 = silu(p2) W3^T, R = silu(p3) W4^T
 fmd_status radial_tc_forward(const FusedWeights& w, const FusedState& st, int64_t E, int C, cudaStream_t s) {
-    for (int L = 0; L < w.n_layers; ++L) {
-        const int PC = (L == 0 ? 2 : 4) * C;
-        const int act = FMD_ACT_NONE | FMD_ACT_INPUT_SILU;
-        fmd_status r = fmd_gemm_tf32x3(st.pre[0][L], kH, w.tc_hi[0][L], w.tc_lo[0][L], kH, nullptr, nullptr, 0,
-                                       st.pre[1][L], kH, E, kH, kH, act, 0, st.flags, s);
-        if (r == FMD_OK)
-            r = fmd_gemm_tf32x3(st.pre[1][L], kH, w.tc_hi[1][L], w.tc_lo[1][L], kH, nullptr, nullptr, 0,
-                                st.pre[2][L], kH, E, kH, kH, act, 0, st.flags, s);
-        if (r == FMD_OK)
-            r = fmd_gemm_tf32x3(st.pre[2][L], kH, w.tc_hi[2][L], w.tc_lo[2][L], kH, nullptr, nullptr, 0, st.R[L],
-                                PC, E, PC, kH, act, 0, st.flags, s);
+    // the layers' chains are independent: GEMM k of every layer in one grouped launch (bitwise the
+    // single calls), 3 launches instead of 3 per layer
+    for (int k = 0; k < 3; ++k) {
+        fmd_gemm_problem pr[kMaxLayers];
+        for (int L = 0; L < w.n_layers; ++L) {
+            const int PC = (L == 0 ? 2 : 4) * C;
+            const int n = k < 2 ? kH : PC;
+            pr[L] = fmd_gemm_problem{st.pre[k][L], kH, w.tc_hi[k][L], w.tc_lo[k][L], kH, nullptr, nullptr, 0,
+                                     k < 2 ? st.pre[k + 1][L] : st.R[L], n, E, n, kH,
+                                     FMD_ACT_NONE | FMD_ACT_INPUT_SILU, 0};
+        }
+        const fmd_status r = fmd_gemm_tf32x3_grouped(pr, w.n_layers, st.flags, s);
         if (r != FMD_OK) return r;
     }
     return FMD_OK;
@@ -1610,17 +1611,18 @@ fmd_status radial_tc_forward(const FusedWeights& w, const FusedState& st, int64_
 
 // their backward, each gradient written over its pre-activation:
 //   g3 = (dR W4) silu'(p3), g2 = (g3 W3) silu'(p2), g1 = (g2 W2) silu'(p1)
+// (GEMM k of every layer in one grouped launch, as the forward)
 fmd_status radial_tc_backward(const FusedWeights& w, const FusedState& st, int64_t E, int C, cudaStream_t s) {
-    for (int L = 0; L < w.n_layers; ++L) {
-        const int PC = (L == 0 ? 2 : 4) * C;
-        fmd_status r = fmd_gemm_tf32x3(st.dR[L], PC, w.tc_t_hi[2][L], w.tc_t_lo[2][L], PC, nullptr, st.pre[2][L],
-                                       kH, st.pre[2][L], kH, E, kH, PC, FMD_ACT_SILU_GRAD, 0, st.flags, s);
-        if (r == FMD_OK)
-            r = fmd_gemm_tf32x3(st.pre[2][L], kH, w.tc_t_hi[1][L], w.tc_t_lo[1][L], kH, nullptr, st.pre[1][L], kH,
-                                st.pre[1][L], kH, E, kH, kH, FMD_ACT_SILU_GRAD, 0, st.flags, s);
-        if (r == FMD_OK)
-            r = fmd_gemm_tf32x3(st.pre[1][L], kH, w.tc_t_hi[0][L], w.tc_t_lo[0][L], kH, nullptr, st.pre[0][L], kH,
-                                st.pre[0][L], kH, E, kH, kH, FMD_ACT_SILU_GRAD, 0, st.flags, s);
+    for (int k = 2; k >= 0; --k) {
+        fmd_gemm_problem pr[kMaxLayers];
+        for (int L = 0; L < w.n_layers; ++L) {
+            const int PC = (L == 0 ? 2 : 4) * C;
+            const float* x = k == 2 ? st.dR[L] : st.pre[k + 1][L];
+            const int K = k == 2 ? PC : kH;
+            pr[L] = fmd_gemm_problem{x, K, w.tc_t_hi[k][L], w.tc_t_lo[k][L], K, nullptr, st.pre[k][L], kH,
+                                     st.pre[k][L], kH, E, kH, K, FMD_ACT_SILU_GRAD, 0};
+        }
+        const fmd_status r = fmd_gemm_tf32x3_grouped(pr, w.n_layers, st.flags, s);
         if (r != FMD_OK) return r;
     }
     return FMD_OK;
